@@ -1,0 +1,34 @@
+// Host-side helpers shared by the C-ABI entry points: status codes, the
+// thread-local record of the last CUDA error, and TMA descriptor creation
+// through the driver entry point (so the library does not link libcuda).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/da_b200.h"
+
+namespace da {
+
+// Records the pending CUDA runtime error (clearing it) and returns DA_ERR_CUDA.
+int record_cuda_error();
+// Records an explicit CUDA error code and returns DA_ERR_CUDA.
+int record_cuda_error_code(int code);
+
+// Encodes a 2-D tiled tensor map over a row-major matrix [outer, inner]
+// with the given row stride, a box of [box_outer, box_inner] elements and
+// 128-byte swizzling (box_inner * elem_bytes must be 128) unless
+// `swizzle128` is false.  Returns DA_OK or a DA_ERR_* status.
+int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes,
+                 uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
+                 uint32_t box_outer, bool swizzle128 = true);
+
+// Optional debug progress buffer (pinned host memory) set by
+// da_set_debug_trace; kernels that support it write per-CTA markers there.
+int* debug_trace();
+
+// Number of SMs of the current device (cached per device).
+int sm_count();
+
+}  // namespace da

@@ -1,0 +1,37 @@
+// Shared declarations of the dictionary-route kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace da {
+namespace route {
+
+struct RouteFwdArgs {
+  const void* q;            // route input rows: [rows, q_cols] with row stride q_row_stride (elements)
+  int64_t rows;             // rows per group
+  int64_t q_cols;           // columns of the q matrix
+  int64_t q_row_stride;     // elements between consecutive rows
+  int groups;               // groups of R columns routed independently (module: 2*H)
+  int64_t group_col_stride; // column offset between groups (elements)
+  int64_t R, M;
+  int dtype;                // DA_F16 / DA_BF16 of q, z and dict_key_t
+  const void* dk_t;         // [M, R] normalised keys (dtype)
+  const void* dv;           // [R, M] normalised values (bf16)
+  const float* beta;        // device scalar
+  const float* dk_max;      // device scalar
+  float eps;
+  int normalize_input, normalize_output;
+  void* z;                  // [groups, rows, R]
+  float* lse;               // [groups, rows]
+  float* out_norm;          // [groups, rows]
+  int* argmax;              // [groups, rows] optional
+  int* work;                // [2 + repair_cap] persistent, zero-initialised once
+  int repair_cap;
+  int* status;
+};
+
+int route_fwd(const RouteFwdArgs& a, cudaStream_t st);
+
+}  // namespace route
+}  // namespace da

@@ -1,0 +1,327 @@
+"""Op layer: autograd Functions over the sm_100a C ABI.
+
+Public op-level API mirroring the reference's Triton seam
+(src/double_attention/triton_kernels.py:1984-2019 and :2290-2305):
+
+* :func:`dictionary_route` -- same arguments, meaning and errors as
+  ``dictionary_route_triton``;
+* :func:`routed_attention` -- same as ``routed_attention_triton``;
+
+plus the module-path helpers used by ``SharedDictionaryAttention``.
+Every numeric step runs in the B200 kernels of ``libda_b200.so``; there is
+no CPU or PyTorch fallback -- unsupported inputs raise.
+"""
+
+from __future__ import annotations
+
+import math
+import threading
+from dataclasses import dataclass
+
+import torch
+from torch import Tensor
+
+from . import _lib
+from ._lib import call, dtype_code, ptr, stream_ptr
+
+REPAIR_CAP = 4096
+_HALF = (torch.float16, torch.bfloat16)
+
+
+# ----------------------------------------------------------------------------- dispatch
+def compute_dtype(x: Tensor) -> torch.dtype:
+    """The fp16/bf16 dtype the kernels compute in for input ``x``."""
+    if x.is_cuda and torch.is_autocast_enabled("cuda"):
+        return torch.get_autocast_dtype("cuda")
+    return x.dtype
+
+
+def resolve_backend(backend: str, x: Tensor, dtype: torch.dtype | None = None) -> str:
+    """Counterpart of ops.py:142-157.  Only the B200 kernels exist here:
+    ``"auto"``/``"triton"``/``"b200"`` select them and fail loudly when they
+    cannot run; ``"torch"`` is rejected (no CPU implementation ships)."""
+    if backend == "torch":
+        raise NotImplementedError(
+            "backend='torch' is not provided by double_attention_b200; it ships only the B200 kernels"
+        )
+    dtype = dtype or x.dtype
+    if not x.is_cuda or dtype not in _HALF:
+        raise RuntimeError("B200 backend requested but unavailable: CUDA fp16/bf16 tensors are required")
+    major, minor = torch.cuda.get_device_capability(x.device)
+    if (major, minor) != (10, 0):
+        raise RuntimeError(f"B200 backend requested but unavailable: sm_100 GPU required, found sm_{major}{minor}")
+    return "b200"
+
+
+def score_scale_from_log(log_scale: Tensor) -> Tensor:
+    """ops.py:160-161."""
+    return log_scale.clamp(math.log(0.25), math.log(1024.0)).exp()
+
+
+def assemble_score_maps(query: Tensor, key: Tensor, outer_maps: int) -> tuple[Tensor, Tensor]:
+    """Index mapping of ops.py:96-139 (used for the aux outputs; the
+    attention kernel applies the same mapping through its addressing)."""
+    if query.ndim != 4 or query.shape != key.shape:
+        raise ValueError("query and key must have matching [B, H, T, R] shapes")
+    branches = query.shape[1]
+    if branches == outer_maps:
+        return query, key
+    if branches > outer_maps:
+        if branches % outer_maps:
+            raise ValueError("qk_branches must be divisible by outer_maps")
+        group = branches // outer_maps
+        s = group ** -0.25
+        b, _, t, r = query.shape
+
+        def fold(z: Tensor) -> Tensor:
+            return z.reshape(b, outer_maps, group, t, r).permute(0, 1, 3, 2, 4).reshape(b, outer_maps, t, group * r) * s
+
+        return fold(query), fold(key)
+    if outer_maps % branches:
+        raise ValueError("outer_maps must be divisible by qk_branches")
+    rep = outer_maps // branches
+    return query.repeat_interleave(rep, dim=1), key.repeat_interleave(rep, dim=1)
+
+
+# ----------------------------------------------------------------------------- workspaces
+class _Workspace:
+    """Per-(device, stream) scratch the kernels keep between calls: the route
+    kernel's CTA ticket / repair list (zero-initialised once, reset by the
+    kernel itself) and a device status word."""
+
+    def __init__(self, device: torch.device) -> None:
+        self.route_work = torch.zeros(2 + REPAIR_CAP, dtype=torch.int32, device=device)
+        self.status = torch.zeros(2, dtype=torch.int32, device=device)
+
+
+_ws_lock = threading.Lock()
+_workspaces: dict[tuple[int, int], _Workspace] = {}
+
+
+def workspace(device: torch.device) -> _Workspace:
+    key = (device.index if device.index is not None else torch.cuda.current_device(), stream_ptr(device))
+    ws = _workspaces.get(key)
+    if ws is None:
+        with _ws_lock:
+            ws = _workspaces.get(key)
+            if ws is None:
+                ws = _Workspace(device)
+                _workspaces[key] = ws
+    return ws
+
+
+def device_status(device: torch.device | None = None, reset: bool = True) -> int:
+    """OR of all status bits kernels on this device/stream reported (syncs).
+
+    Raises when a kernel reported a device-side wait that gave up, naming
+    the wait site (a logic error in a kernel, never expected)."""
+    device = device or torch.device("cuda", torch.cuda.current_device())
+    ws = workspace(device)
+    flags, site = (int(v) for v in ws.status.tolist())
+    if reset:
+        ws.status.zero_()
+    if flags & 1:
+        raise _lib.DAError("device status", _lib.DA_ERR_DEVICE_TIMEOUT, f"bounded wait gave up at site {site}")
+    return flags
+
+
+def _check_half_cuda(name: str, *tensors: Tensor) -> None:
+    for t in tensors:
+        if not t.is_cuda:
+            raise ValueError(f"{name} requires CUDA tensors")
+    dt = tensors[0].dtype
+    if dt not in _HALF or any(t.dtype != dt for t in tensors):
+        raise ValueError(f"{name} requires fp16 or bf16 inputs of one matching dtype")
+
+
+# ----------------------------------------------------------------------------- dictionaries
+@dataclass
+class DictionaryViews:
+    """Kernel operands of one normalised dictionary bank in one dtype.
+
+    key   [R, M], key_t [M, R] in the compute dtype (q . Dk operands)
+    value [R, M], value_t [M, R] in bf16 (probability . Dv operands)
+    key_max: max column norm of ``key`` as rounded (softmax offset bound).
+    """
+
+    key: Tensor
+    key_t: Tensor
+    value: Tensor
+    value_t: Tensor
+    key_max: Tensor
+
+    @property
+    def routing_dim(self) -> int:
+        return self.key.shape[0]
+
+    @property
+    def size(self) -> int:
+        return self.key.shape[1]
+
+
+class _DictNorm(torch.autograd.Function):
+    """Column normalisation + cast of a bank (modules.py:45-48, :229-231)."""
+
+    @staticmethod
+    def forward(ctx, raw: Tensor, eps: float, dtype: torch.dtype):  # type: ignore[override]
+        raw = raw.detach().contiguous().float()
+        r, m = raw.shape
+        out = torch.empty(r, m, dtype=dtype, device=raw.device)
+        out_t = torch.empty(m, r, dtype=dtype, device=raw.device)
+        denom = torch.empty(m, dtype=torch.float32, device=raw.device)
+        mx = torch.empty(1, dtype=torch.float32, device=raw.device)
+        call("da_dict_norm_fwd", raw.data_ptr(), r, m, eps, dtype_code(dtype), out.data_ptr(), out_t.data_ptr(),
+             denom.data_ptr(), mx.data_ptr(), stream_ptr(raw.device))
+        ctx.save_for_backward(raw, denom)
+        ctx.eps = eps
+        ctx.mark_non_differentiable(mx)
+        return out, out_t, mx
+
+    @staticmethod
+    def backward(ctx, g_out: Tensor | None, g_out_t: Tensor | None, _g_mx):  # type: ignore[override]
+        raw, denom = ctx.saved_tensors
+        if g_out is None and g_out_t is None:
+            return None, None, None
+        r, m = raw.shape
+        ga = None if g_out is None else g_out.float().contiguous()
+        gb = None if g_out_t is None else g_out_t.float().contiguous()
+        grad = torch.empty_like(raw)
+        call("da_dict_norm_bwd", raw.data_ptr(), denom.data_ptr(), ptr(ga), ptr(gb), r, m, ctx.eps,
+             grad.data_ptr(), 0, stream_ptr(raw.device))
+        return grad, None, None
+
+
+def dictionary_views(raw_key: Tensor, raw_value: Tensor | None, eps: float, dtype: torch.dtype) -> DictionaryViews:
+    """Normalise a bank's raw parameters into kernel operands (autograd-aware)."""
+    if not raw_key.is_cuda:
+        raise RuntimeError("B200 backend requested but unavailable: CUDA fp16/bf16 tensors are required")
+    key, key_t, key_max = _DictNorm.apply(raw_key, eps, dtype)
+    if raw_value is None:  # tied dictionary (untied_dictionary=False)
+        if dtype == torch.bfloat16:
+            value, value_t = key, key_t
+        else:
+            value, value_t, _ = _DictNorm.apply(raw_key, eps, torch.bfloat16)
+    else:
+        value, value_t, _ = _DictNorm.apply(raw_value, eps, torch.bfloat16)
+    return DictionaryViews(key, key_t, value, value_t, key_max)
+
+
+def _col_norm_max(d: Tensor) -> Tensor:
+    out = torch.empty(1, dtype=torch.float32, device=d.device)
+    call("da_col_norm_max", d.data_ptr(), d.shape[0], d.shape[1], dtype_code(d.dtype), out.data_ptr(),
+         stream_ptr(d.device))
+    return out
+
+
+def dictionary_views_from_normalized(key: Tensor, value: Tensor, dtype: torch.dtype) -> DictionaryViews:
+    """Kernel operands from caller-normalised dictionaries (cast + transpose)."""
+    k = key.to(dtype).contiguous()
+    v = value.to(torch.bfloat16).contiguous()
+    return DictionaryViews(k, k.t().contiguous(), v, v.t().contiguous(), _col_norm_max(k))
+
+
+# ----------------------------------------------------------------------------- route
+def _route_supported(r: int, m: int) -> None:
+    if r not in (64, 128, 256, 512):
+        raise NotImplementedError(f"dictionary route kernels support routing widths 64/128/256/512, got {r}")
+    if m % 64:
+        raise NotImplementedError(f"dictionary route kernels need a dictionary size divisible by 64, got {m}")
+
+
+def _route_forward(q: Tensor, rows: int, groups: int, col_stride: int, views: DictionaryViews, beta: Tensor,
+                   eps: float, normalize_input: bool, normalize_output: bool,
+                   argmax: Tensor | None = None) -> tuple[Tensor, Tensor, Tensor]:
+    r, m = views.routing_dim, views.size
+    _route_supported(r, m)
+    dev = q.device
+    z = torch.empty(groups, rows, r, dtype=q.dtype, device=dev)
+    lse = torch.empty(groups, rows, dtype=torch.float32, device=dev)
+    onorm = torch.empty(groups, rows, dtype=torch.float32, device=dev)
+    ws = workspace(dev)
+    beta32 = beta.detach().float().reshape(1).contiguous()
+    call("da_route_fwd", q.data_ptr(), rows, q.shape[1], q.stride(0), groups, col_stride, r, m, dtype_code(q.dtype),
+         views.key_t.data_ptr(), views.value.data_ptr(), beta32.data_ptr(), views.key_max.data_ptr(), eps,
+         int(normalize_input), int(normalize_output), z.data_ptr(), lse.data_ptr(), onorm.data_ptr(), ptr(argmax),
+         ws.route_work.data_ptr(), REPAIR_CAP, ws.status.data_ptr(), stream_ptr(dev))
+    return z, lse, onorm
+
+
+class _Route(torch.autograd.Function):
+    """Dictionary route over ``groups`` column blocks of a [rows, cols] matrix."""
+
+    @staticmethod
+    def forward(ctx, q: Tensor, key: Tensor, key_t: Tensor, value: Tensor, value_t: Tensor, key_max: Tensor,  # type: ignore[override]
+                beta: Tensor, rows: int, groups: int, col_stride: int, eps: float, normalize_input: bool,
+                normalize_output: bool):
+        views = DictionaryViews(key, key_t, value, value_t, key_max)
+        z, lse, onorm = _route_forward(q, rows, groups, col_stride, views, beta, eps, normalize_input,
+                                       normalize_output)
+        ctx.save_for_backward(q, key, key_t, value, value_t, key_max, beta, z, lse, onorm)
+        ctx.meta = (rows, groups, col_stride, eps, normalize_input, normalize_output)
+        return z
+
+    @staticmethod
+    def backward(ctx, dz: Tensor):  # type: ignore[override]
+        return _route_backward(ctx, dz)
+
+
+def _route_backward(ctx, dz: Tensor):
+    raise NotImplementedError("dictionary route backward kernel is not available in this build")
+
+
+def route_projected(projected: Tensor, views: DictionaryViews, beta: Tensor, cfg, batch: int, length: int) -> Tensor:
+    """Route the Q and K branches of a fused projection ``[B*T, 2*H*R]``.
+
+    Returns ``[2, H, B, T, R]`` (index 0: routed queries, 1: routed keys);
+    the concatenation of modules.py:239 is only an index mapping here.
+    """
+    _check_variant(cfg)
+    h, r = cfg.qk_branches, cfg.routing_dim
+    z = _Route.apply(projected, views.key, views.key_t, views.value, views.value_t, views.key_max, beta,
+                     batch * length, 2 * h, r, cfg.eps, cfg.normalize_routing_input, cfg.normalize_routing_output)
+    return z.view(2, h, batch, length, r)
+
+
+def _check_variant(cfg) -> None:
+    if cfg.dictionary_activation != "identity" or cfg.dictionary_assignment != "softmax" \
+            or cfg.standardize_dictionary_logits:
+        raise NotImplementedError(
+            "the B200 route kernels implement identity logits with softmax assignment; "
+            f"got activation={cfg.dictionary_activation!r}, assignment={cfg.dictionary_assignment!r}, "
+            f"standardize_logits={cfg.standardize_dictionary_logits}"
+        )
+
+
+def dictionary_route(
+    input: Tensor,
+    dictionary_key: Tensor,
+    dictionary_value: Tensor,
+    beta: Tensor,
+    eps: float = 1e-6,
+    silu_logits: bool = False,
+    direct_silu: bool = False,
+    silu_gain: float = 1.0,
+    standardize_logits: bool = False,
+    standardized_logit_scale: float | None = None,
+    normalize_input: bool = True,
+    normalize_output: bool = True,
+) -> Tensor:
+    """B200 counterpart of ``dictionary_route_triton`` (triton_kernels.py:1984-2019).
+
+    ``input`` [..., R]; ``dictionary_key``/``dictionary_value`` [R, M]
+    (already column-normalised, same fp16/bf16 dtype as ``input``).
+    """
+    _check_half_cuda("dictionary route", input, dictionary_key, dictionary_value)
+    if silu_logits or direct_silu or standardize_logits:
+        raise NotImplementedError("the B200 route kernels implement identity logits with softmax assignment")
+    r = input.shape[-1]
+    if dictionary_key.shape[0] != r or dictionary_value.shape != dictionary_key.shape:
+        raise ValueError("dictionaries must be [routing_dim, M] matching the input")
+    shape = input.shape
+    flat = input.contiguous().view(-1, r)
+    views = dictionary_views_from_normalized(dictionary_key, dictionary_value, input.dtype)
+    if not torch.is_tensor(beta):
+        beta = torch.tensor(float(beta), device=input.device)
+    z = _Route.apply(flat, views.key, views.key_t, views.value, views.value_t, views.key_max, beta, flat.shape[0], 1,
+                     r, eps, normalize_input, normalize_output)
+    return z.view(shape)

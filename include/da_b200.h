@@ -1,0 +1,108 @@
+/*
+ * C ABI of the B200 (sm_100a) routed-attention library.
+ *
+ * Every entry point takes raw device pointers, 64-bit sizes, a dtype code,
+ * scalar parameters and a CUDA stream (as void*), and returns an int status
+ * (DA_OK = 0).  Calls are stream-ordered and never synchronise the host.
+ * The caller allocates every output and workspace; outputs are fully
+ * overwritten unless an `accumulate` flag says otherwise.
+ *
+ * Each declaration names the reference interface it replaces, by
+ * file:line inside the Ahnd6474/double-attention package
+ * (src/double_attention/...).
+ */
+#ifndef DA_B200_H_
+#define DA_B200_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define DA_API __attribute__((visibility("default")))
+#else
+#define DA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes --------------------------------------------------- */
+enum {
+  DA_OK = 0,
+  DA_ERR_NULL = 1,             /* a required pointer is null */
+  DA_ERR_SHAPE = 2,            /* unsupported or inconsistent shape */
+  DA_ERR_DTYPE = 3,            /* unsupported dtype code */
+  DA_ERR_ALIGN = 4,            /* pointer or row stride not 16-byte aligned */
+  DA_ERR_UNSUPPORTED = 5,      /* variant not implemented by the kernels */
+  DA_ERR_DEVICE_TIMEOUT = 6,   /* a device-side bounded wait gave up */
+  DA_ERR_CUDA = 7,             /* CUDA runtime/driver error: da_last_cuda_error() */
+  DA_ERR_WORKSPACE = 8         /* workspace smaller than the *_workspace_size query */
+};
+
+/* ---- dtype codes ---------------------------------------------------- */
+enum { DA_F16 = 0, DA_BF16 = 1, DA_F32 = 2 };
+
+DA_API const char* da_version(void);
+DA_API const char* da_status_string(int status);
+/* Last CUDA error code recorded by a call on this host thread. */
+DA_API int da_last_cuda_error(void);
+
+/* Debug aid with no reference counterpart: pinned, device-accessible host
+ * memory (8 ints per CTA) into which kernels write progress markers, or
+ * null to disable.  Lets a host thread see where a kernel stands. */
+DA_API int da_set_debug_trace(int* host_mapped);
+
+/* ---- dictionary bank normalisation ----------------------------------
+ * Replaces SharedDictionaryBank.normalized (modules.py:45-48: F.normalize
+ * over dim 0) and the AMP cast of the normalised views (modules.py:229-231).
+ * raw: [R, M] fp32 row-major.  Writes (each optional):
+ *   out   [R, M] and out_t [M, R] in out_dtype (DA_F16 / DA_BF16),
+ *   denom [M] fp32 = max(||raw[:, j]||, eps),
+ *   max_col_norm [1] fp32 = largest 2-norm of the rounded output columns. */
+DA_API int da_dict_norm_fwd(const float* raw, int64_t R, int64_t M, float eps, int out_dtype, void* out, void* out_t,
+                     float* denom, float* max_col_norm, void* stream);
+
+/* Backward of da_dict_norm_fwd (autograd of F.normalize, modules.py:46-47).
+ * grad: [R, M] fp32 and/or grad_t: [M, R] fp32 (summed when both are given).
+ * grad_raw: [R, M] fp32, overwritten (accumulate = 0) or added to. */
+DA_API int da_dict_norm_bwd(const float* raw, const float* denom, const float* grad, const float* grad_t, int64_t R,
+                     int64_t M, float eps, float* grad_raw, int accumulate, void* stream);
+
+/* Largest column 2-norm of a [R, M] fp16/bf16 dictionary, into out[0]. */
+DA_API int da_col_norm_max(const void* dict, int64_t R, int64_t M, int dtype, float* out, void* stream);
+
+/* ---- dictionary route, forward ---------------------------------------
+ * Replaces dictionary_route_triton / _DictionaryRouteFunction.forward
+ * (triton_kernels.py:1984-2019, :1806-1870; math of ops.py:16-62) for the
+ * identity-logit softmax route.  Input rows come from a [rows, q_cols] matrix
+ * (row stride q_row_stride elements); `groups` blocks of R columns starting
+ * every group_col_stride columns are routed independently (the module path
+ * routes the Q and K branches of the fused projection in one call,
+ * modules.py:239-241).  R in {64,128,256,512}; M a multiple of 64.
+ *   dict_key_t  [M, R] normalised keys, dtype of q;
+ *   dict_value  [R, M] normalised values, bf16;
+ *   beta, dk_max: device fp32 scalars (dk_max = max column norm of the keys).
+ * Outputs: z [groups, rows, R] (dtype of q); lse, out_norm [groups, rows] fp32
+ * (log-sum-exp of the beta-scaled logits, ||softmax . Dv^T||); argmax
+ * [groups, rows] int32 (optional, may be null).
+ * work: int32 [2 + repair_cap], zero-filled before first use and left zeroed
+ * by every call; one work buffer must not be shared by calls that run
+ * concurrently. */
+DA_API int da_route_fwd(const void* q, int64_t rows, int64_t q_cols, int64_t q_row_stride, int groups,
+                        int64_t group_col_stride, int64_t R, int64_t M, int dtype, const void* dict_key_t,
+                        const void* dict_value, const float* beta, const float* dk_max, float eps,
+                        int normalize_input, int normalize_output, void* z, float* lse, float* out_norm,
+                        int* argmax, int* work, int repair_cap, int* status, void* stream);
+
+/* ---- building-block check -------------------------------------------
+ * No reference counterpart: D[128, n] = A[128, k] * B^T computed by one
+ * tcgen05 tile (cta_group 1 or 2) for testing the descriptor layouts.
+ * A: [128, k] bf16; B: [n, k] bf16 (b_mn_major = 0) or [k, n] (= 1). */
+DA_API int da_selftest_mma(int cta_group, int n, int b_mn_major, int k, const void* A, const void* B, float* D,
+                    int* status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DA_B200_H_ */

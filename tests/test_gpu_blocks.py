@@ -1,0 +1,82 @@
+"""Tensor-core building blocks and the dictionary normalisation kernel on a B200.
+
+The MMA self-test computes one 128 x N tile with the same TMA layouts,
+shared-memory descriptors and TMEM read-back the routing kernels use, and
+compares it element by element with an fp32 matmul of the same bf16 inputs.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from double_attention_b200 import _lib
+
+pytestmark = pytest.mark.gpu
+
+CASES = [
+    (1, 64, False),
+    (1, 128, False),
+    (1, 256, False),
+    (1, 128, True),
+    (1, 256, True),
+    (2, 64, False),
+    (2, 128, False),
+    (2, 256, False),
+    (2, 128, True),
+    (2, 256, True),
+]
+
+
+@pytest.mark.parametrize("k", [64, 256])
+@pytest.mark.parametrize(("cta_group", "n", "b_mn"), CASES)
+def test_selftest_mma_tile(cta_group: int, n: int, b_mn: bool, k: int) -> None:
+    torch.manual_seed(1000 + 7 * n + k + cta_group)
+    dev = torch.device("cuda")
+    a = torch.randn(128, k, device=dev).to(torch.bfloat16)
+    b = torch.randn(n, k, device=dev).to(torch.bfloat16)
+    b_arg = b.t().contiguous() if b_mn else b
+    d = torch.full((128, n), float("nan"), device=dev)
+    status = torch.zeros(2, dtype=torch.int32, device=dev)
+    _lib.call(
+        "da_selftest_mma", cta_group, n, int(b_mn), k, a.data_ptr(), b_arg.data_ptr(), d.data_ptr(),
+        status.data_ptr(), _lib.stream_ptr(),
+    )
+    torch.cuda.synchronize()
+    assert status.tolist() == [0, 0]
+    expected = a.float() @ b.float().t()
+    torch.testing.assert_close(d, expected, atol=1e-3, rtol=1e-4)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize(("r", "m"), [(256, 512), (128, 512), (512, 1536), (8, 16)])
+def test_dict_norm_forward_backward(dtype: torch.dtype, r: int, m: int) -> None:
+    torch.manual_seed(r + m)
+    dev = torch.device("cuda")
+    raw = (torch.randn(r, m, device=dev) * r**-0.5).requires_grad_()
+    raw.data[:, 3] = 0.0  # a column below eps takes the clamped branch
+    out = torch.empty(r, m, device=dev, dtype=dtype)
+    out_t = torch.empty(m, r, device=dev, dtype=dtype)
+    denom = torch.empty(m, device=dev)
+    max_norm = torch.empty(1, device=dev)
+    eps = 1e-6
+    _lib.call(
+        "da_dict_norm_fwd", raw.data_ptr(), r, m, eps, _lib.dtype_code(dtype), out.data_ptr(), out_t.data_ptr(),
+        denom.data_ptr(), max_norm.data_ptr(), _lib.stream_ptr(),
+    )
+    expected = torch.nn.functional.normalize(raw, dim=0, eps=eps)
+    # the column norm's summation order differs from torch's: allow 1 ulp
+    torch.testing.assert_close(out, expected.detach().to(dtype))
+    torch.testing.assert_close(out_t.float(), out.float().t(), atol=0, rtol=0)
+    torch.testing.assert_close(denom, raw.detach().norm(dim=0).clamp_min(eps), atol=1e-6, rtol=1e-5)
+    torch.testing.assert_close(max_norm[0], out.float().norm(dim=0).max(), atol=1e-6, rtol=1e-5)
+
+    grad = torch.randn(r, m, device=dev)
+    grad_t = torch.randn(m, r, device=dev)
+    expected.backward(grad + grad_t.t())
+    grad_raw = torch.empty(r, m, device=dev)
+    _lib.call(
+        "da_dict_norm_bwd", raw.data_ptr(), denom.data_ptr(), grad.data_ptr(), grad_t.data_ptr(), r, m, eps,
+        grad_raw.data_ptr(), 0, _lib.stream_ptr(),
+    )
+    torch.testing.assert_close(grad_raw, raw.grad, atol=1e-4, rtol=1e-4)
