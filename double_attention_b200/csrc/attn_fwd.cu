@@ -1,0 +1,562 @@
+// Outer routed attention with the alpha map mix fused, forward.
+//
+// Reference: routed_attention_reference (src/double_attention/ops.py:65-93),
+// the map mix of SharedDictionaryAttention.forward (modules.py:265-272) and
+// the Triton kernel it replaces (triton_kernels.py:674-811, :2022-2090):
+//
+//   A_s = softmax_causal(gamma_s Q_s K_s^T),   Y = sum_s alpha_s A_s V,
+//
+// with Q_s/K_s the routed vectors of map s (a group of concatenated branches
+// scaled by group^-1/4 each, ops.py:113-131, i.e. gamma_s / sqrt(group) on
+// the dot product) and V [B, T, D] the dense value shared by every map.
+//
+// One CTA pair (2-CTA cluster, cta_group::2 MMAs) owns 128 query rows of one
+// sequence, 64 per CTA.  Per key tile of 64:
+//   * S_s = Q_s K_s^T for every map lands folded in TMEM (32 columns each);
+//   * the softmax warpgroup forms one probability tile P (bf16, shared mem);
+//   * O += P V with V read straight from [B, T, D] as an MN-major operand;
+//     D = 512 costs 256 TMEM columns per CTA thanks to the folded layout,
+//     so the whole dense value is accumulated without splitting D.
+// Scores are bounded by gamma_s ||q|| max||k||, which serves as a fixed
+// softmax offset: no running-max rescaling of O.  With one map the row sum
+// normalises O at the end.  With several maps a first sweep over the keys
+// (Q K^T only) produces each map's exact log-sum-exp, and the second sweep
+// builds the already-normalised mixture P = sum_s alpha_s exp(S_s - lse_s),
+// so Y = P V needs a single P.V product for all maps.
+#include <math.h>
+
+#include "attn_common.h"
+#include "common.cuh"
+#include "host_util.h"
+
+namespace da {
+namespace attn {
+
+constexpr int kThreads = 192;   // warp0 TMA, warp1 MMA, warps2-5 softmax/epilogue
+constexpr int kRows = 64;       // query rows per CTA
+constexpr int kNK = 64;         // keys per tile
+constexpr int kMaxStages = 4;
+
+struct Layout {
+  int kw;          // total Q/K width over maps and branches
+  int nqb;         // 64-column boxes per Q/K row block
+  int nc, npv;     // N of one P.V instruction, instructions per tile
+  int q_bytes, k_bytes, v_bytes;
+  int stages;
+  int off_q, off_k, off_v, off_p, off_red, smem;
+  int tmem_s, tmem_cols;
+};
+
+__host__ __device__ inline Layout make_layout(int maps, int group, int R, int D) {
+  Layout L;
+  L.kw = maps * group * R;
+  L.nqb = L.kw / 64;
+  L.nc = D < 256 ? D : 256;
+  L.npv = D / L.nc;
+  L.q_bytes = kRows * L.kw * 2;
+  L.k_bytes = (kNK / 2) * L.kw * 2;
+  L.v_bytes = (D / 2) * kNK * 2;
+  const int fixed = L.q_bytes + 2 * kRows * kNK * 2 + 128 * 8 * 4;
+  int st = (225 * 1024 - fixed) / (L.k_bytes + L.v_bytes);
+  L.stages = st > kMaxStages ? kMaxStages : st;
+  L.off_q = 0;
+  L.off_k = L.off_q + L.q_bytes;
+  L.off_v = L.off_k + L.stages * L.k_bytes;
+  L.off_p = L.off_v + L.stages * L.v_bytes;
+  L.off_red = L.off_p + 2 * kRows * kNK * 2;
+  const int used = L.off_red + 128 * 8 * 4;
+  L.smem = used < 120 * 1024 ? 120 * 1024 : used;  // one CTA per SM
+  L.tmem_s = D / 2;
+  const int cols = D / 2 + 2 * maps * 32;
+  L.tmem_cols = cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : cols <= 256 ? 256 : 512;
+  return L;
+}
+
+struct FwdParams {
+  int64_t q_rows, q_base, q_sb, q_sbr;
+  int64_t k_rows, k_base, k_sb, k_sbr;
+  int B, T, R, D, maps, group, causal;
+  int branch0[kMaxMaps];
+  const float* scales;
+  const float* weights;
+  const float* key_norm_max;
+  float key_norm_bound;
+  void* y;
+  float* lse;
+  int* status;
+  int* trace;
+};
+
+template <typename T, bool kMix>
+__global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_constant__ CUtensorMap tq,
+                                                               const __grid_constant__ CUtensorMap tk,
+                                                               const __grid_constant__ CUtensorMap tv,
+                                                               const FwdParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t q_full, o_full;
+  __shared__ uint64_t k_full[kMaxStages], k_empty[kMaxStages], v_full[kMaxStages], v_empty[kMaxStages];
+  __shared__ uint64_t s_full[2], p_full[2], p_empty[2];
+  __shared__ uint32_t tmem_base;
+  __shared__ int abort_flag;
+
+  const Layout L = make_layout(p.maps, p.group, p.R, p.D);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_ctarank() & 1u;
+  const int tiles = (p.T + 127) / 128;
+  const int pair = blockIdx.x / 2;
+  const int b = pair / tiles;
+  const int t0 = (tiles - 1 - pair % tiles) * 128;  // heaviest (latest) query tiles first
+  const int nk_all = (p.T + kNK - 1) / kNK;
+  const int nj = p.causal ? min(nk_all, t0 / kNK + 2) : nk_all;
+  const int U = kMix ? 2 * nj : nj;       // key-tile visits (two sweeps when mixing maps)
+  const int rpb = p.R / 64;               // boxes per branch
+  Abort ab{&abort_flag, p.status};
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    mbar_init(&q_full, 1);
+    mbar_init(&o_full, 1);
+    for (int s = 0; s < kMaxStages; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 2);
+      mbar_init(&p_empty[i], 1);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc<2>(&tmem_base, L.tmem_cols);
+    tmem_relinquish<2>();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer (both CTAs)
+    if (lane == 0) {
+      prefetch_tmap(&tq);
+      prefetch_tmap(&tk);
+      prefetch_tmap(&tv);
+      if (rank == 0) mbar_arrive_expect_tx(&q_full, 2 * L.q_bytes);
+      const uint32_t qf = mapa_shared(smem_u32(&q_full), 0);
+      for (int s = 0; s < p.maps; ++s)
+        for (int gi = 0; gi < p.group; ++gi) {
+          const int64_t row = p.q_base + b * p.q_sb + (p.branch0[s] + gi) * p.q_sbr + t0 + 64 * (int)rank;
+          const int y = (int)min(row, p.q_rows - 1);  // boxes never start outside the matrix
+          for (int kb = 0; kb < rpb; ++kb) {
+            const int qb = (s * p.group + gi) * rpb + kb;
+            tma_load_2d_pair(&tq, qf, smem + L.off_q + qb * (kRows * 128), kb * 64, y);
+          }
+        }
+      int k_issued = 0, v_issued = 0;
+      for (int u = 0; u < U; ++u) {
+        const int j = u % nj;
+        const int ks = u % L.stages;
+        if (!mbar_wait(&k_empty[ks], ((u / L.stages) & 1u) ^ 1u, ab, 11)) break;
+        if (rank == 0) mbar_arrive_expect_tx(&k_full[ks], 2 * L.k_bytes);
+        const uint32_t kf = mapa_shared(smem_u32(&k_full[ks]), 0);
+        for (int s = 0; s < p.maps; ++s)
+          for (int gi = 0; gi < p.group; ++gi) {
+            const int64_t row = p.k_base + b * p.k_sb + (p.branch0[s] + gi) * p.k_sbr + j * kNK + 32 * (int)rank;
+            const int y = (int)min(row, p.k_rows - 1);
+            for (int kb = 0; kb < rpb; ++kb) {
+              const int qb = (s * p.group + gi) * rpb + kb;
+              tma_load_2d_pair(&tk, kf, smem + L.off_k + ks * L.k_bytes + qb * ((kNK / 2) * 128), kb * 64, y);
+            }
+          }
+        k_issued = u + 1;
+        if (kMix && u < nj) continue;  // first sweep: keys only
+        const int v = kMix ? u - nj : u;
+        const int vs = v % L.stages;
+        if (!mbar_wait(&v_empty[vs], ((v / L.stages) & 1u) ^ 1u, ab, 12)) break;
+        if (rank == 0) mbar_arrive_expect_tx(&v_full[vs], 2 * L.v_bytes);
+        const uint32_t vf = mapa_shared(smem_u32(&v_full[vs]), 0);
+        const int per = (L.nc / 2) / 64;  // 64-column boxes per CTA per instruction
+        for (int i = 0; i < L.npv; ++i)
+          for (int bx = 0; bx < per; ++bx)
+            tma_load_2d_pair(&tv, vf, smem + L.off_v + vs * L.v_bytes + (i * per + bx) * (kNK * 128),
+                             i * L.nc + (int)rank * (L.nc / 2) + bx * 64, b * p.T + j * kNK);
+        v_issued = v + 1;
+      }
+      if (rank == 0) {  // drain: no TMA may be in flight at teardown
+        mbar_wait_drain(&q_full, 0);
+        for (int u = (k_issued > L.stages ? k_issued - L.stages : 0); u < k_issued; ++u)
+          mbar_wait_drain(&k_full[u % L.stages], (u / L.stages) & 1u);
+        for (int v = (v_issued > L.stages ? v_issued - L.stages : 0); v < v_issued; ++v)
+          mbar_wait_drain(&v_full[v % L.stages], (v / L.stages) & 1u);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer (leader)
+    if (rank == 0 && lane == 0) {
+      const uint32_t idesc_s = idesc_f16(128, kNK, std::is_same<T, __nv_bfloat16>::value, false, false);
+      const uint32_t idesc_o = idesc_f16(128, L.nc, true, false, true);  // B = V, MN-major
+      auto commit_both = [&](uint64_t* bar) {
+        mma_commit<2>(smem_u32(bar));
+        mma_commit<2>(mapa_shared(smem_u32(bar), 1));
+      };
+      auto issue_s = [&](int u) -> bool {
+        const int sb = u & 1, ks = u % L.stages;
+        if (u >= 2 && !mbar_wait(&p_full[sb], ((u - 2) >> 1) & 1u, ab, 22)) return false;
+        if (!mbar_wait(&k_full[ks], (u / L.stages) & 1u, ab, 23)) return false;
+        tc_fence_after();
+        const uint32_t qa = smem_u32(smem + L.off_q);
+        const uint32_t ka = smem_u32(smem + L.off_k + ks * L.k_bytes);
+        for (int s = 0; s < p.maps; ++s) {
+          const uint32_t d = tmem + L.tmem_s + (uint32_t)(sb * p.maps + s) * 32;
+          const int nk16 = p.group * p.R / 16;
+          for (int k = 0; k < nk16; ++k) {
+            const int qb = s * p.group * rpb + (k >> 2), kin = k & 3;
+            const uint64_t ad = sdesc_sw128(qa + qb * (kRows * 128) + kin * 32, 16, 1024);
+            const uint64_t bd = sdesc_sw128(ka + qb * ((kNK / 2) * 128) + kin * 32, 16, 1024);
+            mma_f16_ss<2>(d, ad, bd, idesc_s, k > 0 ? 1u : 0u);
+          }
+        }
+        commit_both(&s_full[sb]);
+        commit_both(&k_empty[ks]);
+        return true;
+      };
+      auto issue_pv = [&](int v) -> bool {
+        const int u = kMix ? v + nj : v;
+        const int pb = v & 1, vs = v % L.stages;
+        if (!mbar_wait(&p_full[u & 1], (u >> 1) & 1u, ab, 24)) return false;
+        if (!mbar_wait(&v_full[vs], (v / L.stages) & 1u, ab, 25)) return false;
+        tc_fence_after();
+        const uint32_t pa = smem_u32(smem + L.off_p + pb * (kRows * kNK * 2));
+        const uint32_t va = smem_u32(smem + L.off_v + vs * L.v_bytes);
+        const int per = (L.nc / 2) / 64;
+        for (int i = 0; i < L.npv; ++i) {
+          for (int kk = 0; kk < kNK / 16; ++kk) {
+            const uint64_t ad = sdesc_sw128(pa + kk * 32, 16, 1024);
+            // MN-major V: rows are keys (K), 128 B = 64 value columns (N);
+            // LBO = distance between 64-column boxes, SBO = 8 key rows.
+            const uint64_t bd = sdesc_sw128(va + i * per * (kNK * 128) + kk * 16 * 128, kNK * 128, 1024);
+            mma_f16_ss<2>(tmem + (uint32_t)(i * (L.nc / 2)), ad, bd, idesc_o, (v > 0 || kk > 0) ? 1u : 0u);
+          }
+        }
+        commit_both(&p_empty[pb]);
+        commit_both(&v_empty[vs]);
+        return true;
+      };
+      bool ok = mbar_wait(&q_full, 0, ab, 21);
+      tc_fence_after();
+      for (int u = 0; ok && u < U; ++u) {
+        ok = issue_s(u);
+        const int v = kMix ? u - nj : u;
+        if (ok && v >= 1) ok = issue_pv(v - 1);
+      }
+      if (ok) ok = issue_pv(nj - 1);
+      commit_both(&o_full);
+      mbar_wait_drain(&o_full, 0);
+    }
+  } else {
+    // ---------------------------------------------------------------- softmax + epilogue
+    const int quad = warp & 3;
+    const int l = quad * 32 + lane;
+    const int r = l & 63, half = l >> 6;
+    const int t = t0 + 64 * (int)rank + r;  // query position of this thread's row
+    const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+    float* red = reinterpret_cast<float*>(smem + L.off_red);
+    const uint32_t pf_leader = mapa_shared(smem_u32(&p_full[0]), 0);
+    const bool arriver = (warp == 2 && lane == 0);
+    const float kLog2e = 1.4426950408889634f;
+
+    bool ok = mbar_wait(&s_full[0], 0, ab, 31);
+    float scale2[kMaxMaps], bound2[kMaxMaps], off2[kMaxMaps], sum[kMaxMaps], mx[kMaxMaps];
+    const float gsc = rsqrtf((float)p.group);
+#pragma unroll
+    for (int s = 0; s < kMaxMaps; ++s) {
+      scale2[s] = bound2[s] = off2[s] = sum[s] = 0.f;
+      mx[s] = -INFINITY;
+      if (s < p.maps) {
+        float qn2 = 0.f;
+        if (ok) {
+          const uint32_t qa = smem_u32(smem + L.off_q);
+          for (int qb = s * p.group * rpb; qb < (s + 1) * p.group * rpb; ++qb)
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              const uint4 w = ld_shared_v4(qa + qb * (kRows * 128) + sw128_offset(r, c));
+              const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float2 f = unpack2<T>(ws[e]);
+                qn2 = fmaf(f.x, f.x, fmaf(f.y, f.y, qn2));
+              }
+            }
+        }
+        const float gamma = p.scales[s] * gsc;
+        const float kmax = p.key_norm_max ? p.key_norm_max[b * p.maps + s] : p.key_norm_bound;
+        scale2[s] = gamma * kLog2e;
+        bound2[s] = gamma * sqrtf(qn2) * kmax * kLog2e;
+      }
+    }
+
+    // Valid keys of key tile j for this thread: 32 columns starting at
+    // j*64 + 32*half; index i is valid iff i < lim.
+    auto key_limit = [&](int j) -> int {
+      const int k0 = j * kNK + 32 * half;
+      int lim = p.T - k0;
+      if (p.causal) lim = min(lim, t - k0 + 1);
+      return max(0, min(32, lim));
+    };
+
+    // ---- sweep 1 (several maps): exact per-map log-sum-exp
+    if (kMix) {
+      for (int u = 0; u < nj; ++u) {
+        const int sb = u & 1;
+        if (ok && u > 0) ok = mbar_wait(&s_full[sb], (u >> 1) & 1u, ab, 32);
+        ok = __all_sync(0xffffffffu, ok);
+        if (ok) {
+          tc_fence_after();
+          const int lim = key_limit(u);
+          for (int s = 0; s < p.maps; ++s) {
+            float v[32];
+            tmem_ld32(tmem + lane_base + L.tmem_s + (uint32_t)(sb * p.maps + s) * 32, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              if (i < lim) {
+                const float a = v[i] * scale2[s];
+                mx[s] = fmaxf(mx[s], a);
+                sum[s] += ex2(a - bound2[s]);
+              }
+            }
+          }
+        }
+        tc_fence_before();
+        named_bar_sync(1, 128);
+        if (arriver) mbar_arrive_cluster(pf_leader + sb * 8);
+      }
+      // combine the two column halves of every row
+      for (int s = 0; s < p.maps; ++s) {
+        red[s * 128 + l] = sum[s];
+        red[(4 + s) * 128 + l] = mx[s];
+      }
+      named_bar_sync(1, 128);
+      for (int s = 0; s < p.maps; ++s) {
+        sum[s] += red[s * 128 + (l ^ 64)];
+        mx[s] = fmaxf(mx[s], red[(4 + s) * 128 + (l ^ 64)]);
+        const float alpha = p.weights ? p.weights[s] : 1.f;
+        const float lse2 = bound2[s] + log2f(sum[s]);
+        off2[s] = lse2 - log2f(alpha);   // P term = 2^(S*scale2 - off2) = alpha * softmax
+        bound2[s] = lse2;                // reported log-sum-exp (log2 units)
+      }
+      named_bar_sync(1, 128);
+    }
+
+    // ---- probability tiles for P.V
+    float psum = 0.f, pmx = -INFINITY;
+    for (int v = 0; v < nj; ++v) {
+      const int u = kMix ? v + nj : v;
+      const int sb = u & 1, pb = v & 1;
+      if (ok && u > 0) ok = mbar_wait(&s_full[sb], (u >> 1) & 1u, ab, 32);
+      if (ok && v >= 2) ok = mbar_wait(&p_empty[pb], ((v - 2) >> 1) & 1u, ab, 33);
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok) {
+        tc_fence_after();
+        const int lim = key_limit(v);
+        float pm[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) pm[i] = 0.f;
+        for (int s = 0; s < p.maps; ++s) {
+          float sv[32];
+          tmem_ld32(tmem + lane_base + L.tmem_s + (uint32_t)(sb * p.maps + s) * 32, sv);
+          tmem_wait_ld();
+          if (kMix) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (i < lim) pm[i] += ex2(sv[i] * scale2[s] - off2[s]);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (i < lim) {
+                const float a = sv[i] * scale2[0];
+                pmx = fmaxf(pmx, a);
+                pm[i] = ex2(a - bound2[0]);
+                psum += pm[i];
+              }
+          }
+        }
+        uint32_t packed[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) packed[i] = pack_bf16x2(pm[2 * i], pm[2 * i + 1]);
+        const uint32_t pa = smem_u32(smem + L.off_p + pb * (kRows * kNK * 2));
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          st_shared_v4(pa + sw128_offset(r, half * 4 + c), packed[4 * c], packed[4 * c + 1], packed[4 * c + 2],
+                       packed[4 * c + 3]);
+        fence_proxy_async();
+      }
+      tc_fence_before();
+      named_bar_sync(1, 128);
+      if (arriver) mbar_arrive_cluster(pf_leader + sb * 8);
+    }
+
+    // ---- epilogue
+    if (ok) ok = mbar_wait(&o_full, 0, ab, 34);
+    ok = __all_sync(0xffffffffu, ok);
+    float inv_l = 1.f;
+    if (!kMix) {
+      red[l] = psum;
+      red[128 + l] = pmx;
+      named_bar_sync(1, 128);
+      psum += red[l ^ 64];
+      pmx = fmaxf(pmx, red[128 + (l ^ 64)]);
+      named_bar_sync(1, 128);
+      inv_l = 1.f / psum;
+      mx[0] = pmx;
+      bound2[0] = bound2[0] + log2f(psum);  // log-sum-exp in log2 units
+    }
+    tc_fence_after();
+    const bool live = t < p.T;
+    if (ok) {
+      T* yrow = reinterpret_cast<T*>(p.y) + ((size_t)b * p.T + (live ? t : 0)) * p.D;
+      for (int i = 0; i < L.npv; ++i) {
+        const int col0 = i * L.nc + half * (L.nc / 2);
+        for (int c = 0; c < L.nc / 2; c += 32) {
+          float o[32];
+          tmem_ld32(tmem + lane_base + (uint32_t)(i * (L.nc / 2) + c), o);
+          tmem_wait_ld();
+          if (live) {
+            uint32_t w[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) w[e] = pack2<T>(o[2 * e] * inv_l, o[2 * e + 1] * inv_l);
+            uint4* dst = reinterpret_cast<uint4*>(yrow + col0 + c);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) dst[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
+          }
+        }
+      }
+      if (live && half == 0) {
+        const float kLn2 = 0.6931471805599453f;
+        for (int s = 0; s < p.maps; ++s) {
+          p.lse[((size_t)b * p.maps + s) * p.T + t] = bound2[s] * kLn2;
+          // the largest term of a row must stay far above the fp32 range floor
+          const float top = kMix ? mx[s] - (bound2[s] - log2f(sum[s])) : mx[0] - (bound2[0] - log2f(psum));
+          if (top < -100.f) atomicOr(p.status, DA_DEV_LOW_MASS);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  if (warp == 1) tmem_dealloc<2>(tmem, L.tmem_cols);
+}
+
+template <typename T, bool kMix>
+int launch(const AttnFwdArgs& a, cudaStream_t st) {
+  const Layout L = make_layout(a.maps, a.group, a.R, a.D);
+  const CUtensorMapDataType qdt =
+      std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap tq, tk, tv;
+  int rc = make_tmap_2d(&tq, a.q.ptr, qdt, 2, a.R, a.q.rows, (uint64_t)a.R * 2, 64, kRows);
+  if (rc) return rc;
+  rc = make_tmap_2d(&tk, a.k.ptr, qdt, 2, a.R, a.k.rows, (uint64_t)a.R * 2, 64, kNK / 2);
+  if (rc) return rc;
+  rc = make_tmap_2d(&tv, a.v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.D, (uint64_t)a.B * a.T, (uint64_t)a.D * 2, 64,
+                    kNK);
+  if (rc) return rc;
+  FwdParams p;
+  p.q_rows = a.q.rows;
+  p.q_base = a.q.base;
+  p.q_sb = a.q.sb;
+  p.q_sbr = a.q.sbr;
+  p.k_rows = a.k.rows;
+  p.k_base = a.k.base;
+  p.k_sb = a.k.sb;
+  p.k_sbr = a.k.sbr;
+  p.B = a.B;
+  p.T = a.T;
+  p.R = a.R;
+  p.D = a.D;
+  p.maps = a.maps;
+  p.group = a.group;
+  p.causal = a.causal;
+  for (int s = 0; s < kMaxMaps; ++s) p.branch0[s] = a.branch0[s];
+  p.scales = a.scales;
+  p.weights = a.weights;
+  p.key_norm_max = a.key_norm_max;
+  p.key_norm_bound = a.key_norm_bound;
+  p.y = a.y;
+  p.lse = a.lse;
+  p.status = a.status;
+  p.trace = debug_trace();
+  auto kern = attn_fwd_kernel<T, kMix>;
+  const int smem = L.smem + 1024;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return record_cuda_error();
+  const long pairs = (long)a.B * ((a.T + 127) / 128);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, tq, tk, tv, p) != cudaSuccess) return record_cuda_error();
+  return DA_OK;
+}
+
+int attn_fwd(const AttnFwdArgs& a, cudaStream_t st) {
+  const bool bf16 = a.dtype == DA_BF16;
+  if (a.maps > 1) return bf16 ? launch<__nv_bfloat16, true>(a, st) : launch<__half, true>(a, st);
+  return bf16 ? launch<__nv_bfloat16, false>(a, st) : launch<__half, false>(a, st);
+}
+
+}  // namespace attn
+}  // namespace da
+
+extern "C" int da_attn_fwd(const void* q, int64_t q_rows, int64_t q_base, int64_t q_sb, int64_t q_sbr,
+                           const void* k, int64_t k_rows, int64_t k_base, int64_t k_sb, int64_t k_sbr,
+                           const void* v, int B, int T, int R, int D, int maps, int group, const int* branch0,
+                           int causal, int dtype, const float* scales, const float* weights,
+                           const float* key_norm_max, float key_norm_bound, void* y, float* lse, int* status,
+                           void* stream) {
+  using namespace da;
+  if (!q || !k || !v || !branch0 || !scales || !y || !lse || !status) return DA_ERR_NULL;
+  if (dtype != DA_BF16 && dtype != DA_F16) return DA_ERR_DTYPE;
+  if (B <= 0 || T <= 0 || maps < 1 || maps > attn::kMaxMaps || group < 1) return DA_ERR_SHAPE;
+  if (R % 64 || R <= 0) return DA_ERR_UNSUPPORTED;
+  if (maps * group * R > 512) return DA_ERR_UNSUPPORTED;  // Q/K width per pair of rows
+  if (D != 128 && D != 256 && D != 512) return DA_ERR_UNSUPPORTED;
+  if (maps > 1 && !weights) return DA_ERR_NULL;
+  if ((2 * maps * 32 + D / 2) > 512) return DA_ERR_UNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(y) & 15) || (reinterpret_cast<uintptr_t>(v) & 15)) return DA_ERR_ALIGN;
+  attn::AttnFwdArgs a;
+  a.q = {q, q_rows, q_base, q_sb, q_sbr};
+  a.k = {k, k_rows, k_base, k_sb, k_sbr};
+  a.v = v;
+  a.B = B;
+  a.T = T;
+  a.R = R;
+  a.D = D;
+  a.maps = maps;
+  a.group = group;
+  for (int s = 0; s < attn::kMaxMaps; ++s) a.branch0[s] = s < maps ? branch0[s] : 0;
+  a.causal = causal;
+  a.dtype = dtype;
+  a.scales = scales;
+  a.weights = weights;
+  a.key_norm_max = key_norm_max;
+  a.key_norm_bound = key_norm_bound;
+  a.y = y;
+  a.lse = lse;
+  a.status = status;
+  return attn::attn_fwd(a, static_cast<cudaStream_t>(stream));
+}

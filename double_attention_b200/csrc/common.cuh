@@ -26,6 +26,7 @@ namespace da {
 enum : int {
   DA_DEV_TIMEOUT = 1,        // a bounded wait ran out
   DA_DEV_ROW_OVERFLOW = 2,   // more low-mass rows than the repair list holds
+  DA_DEV_LOW_MASS = 4,       // a softmax row's largest term fell below 2^-100
 };
 
 constexpr unsigned long long kWaitTimeoutNs = 2000000000ull;  // 2 s per wait

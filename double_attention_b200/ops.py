@@ -325,3 +325,170 @@ def dictionary_route(
     z = _Route.apply(flat, views.key, views.key_t, views.value, views.value_t, views.key_max, beta, flat.shape[0], 1,
                      r, eps, normalize_input, normalize_output)
     return z.view(shape)
+
+
+# ----------------------------------------------------------------------------- outer attention
+MAX_MAPS = 4
+
+
+@dataclass
+class RowMap:
+    """Rows of a [rows, R] matrix: row(b, branch, t) = base + b*sb + branch*sbr + t."""
+
+    tensor: Tensor
+    base: int
+    sb: int
+    sbr: int
+
+    @property
+    def rows(self) -> int:
+        return self.tensor.shape[0]
+
+
+def _attention_supported(r: int, d: int, maps: int, group: int) -> None:
+    if r % 64:
+        raise NotImplementedError(f"outer attention kernels need a routing width divisible by 64, got {r}")
+    if d not in (128, 256, 512):
+        raise NotImplementedError(f"outer attention kernels support value widths 128/256/512, got {d}")
+    if maps > MAX_MAPS or maps * group * r > 512:
+        raise NotImplementedError(
+            f"outer attention kernels support up to {MAX_MAPS} maps and maps*group*R <= 512 "
+            f"(got maps={maps}, group={group}, R={r})"
+        )
+
+
+def _attention_forward(q: RowMap, k: RowMap, v: Tensor, batch: int, length: int, r: int, maps: int, group: int,
+                       branch0: list[int], causal: bool, scales: Tensor, weights: Tensor | None,
+                       key_norm_max: Tensor | None, key_norm_bound: float, out_dtype: torch.dtype):
+    d = v.shape[-1]
+    _attention_supported(r, d, maps, group)
+    dev = v.device
+    v16 = v.contiguous() if v.dtype == torch.bfloat16 else v.to(torch.bfloat16).contiguous()
+    y = torch.empty(batch, length, d, dtype=out_dtype, device=dev)
+    lse = torch.empty(batch, maps, length, dtype=torch.float32, device=dev)
+    ws = workspace(dev)
+    sc = scales.detach().float().contiguous()
+    wt = None if weights is None else weights.detach().float().contiguous()
+    kn = None if key_norm_max is None else key_norm_max.detach().float().contiguous()
+    b0 = (ctypes_int_array(MAX_MAPS))(*(branch0 + [0] * (MAX_MAPS - len(branch0))))
+    b0_addr = ctypes_addressof(b0)
+    call("da_attn_fwd", q.tensor.data_ptr(), q.rows, q.base, q.sb, q.sbr, k.tensor.data_ptr(), k.rows, k.base, k.sb,
+         k.sbr, v16.data_ptr(), batch, length, r, d, maps, group, b0_addr, int(causal), dtype_code(q.tensor.dtype),
+         sc.data_ptr(), ptr(wt), ptr(kn), float(key_norm_bound), y.data_ptr(), lse.data_ptr(), ws.status.data_ptr(),
+         stream_ptr(dev))
+    return y, lse
+
+
+def ctypes_int_array(n: int):
+    import ctypes
+
+    return ctypes.c_int * n
+
+
+def ctypes_addressof(obj) -> int:
+    import ctypes
+
+    return ctypes.addressof(obj)
+
+
+def _map_layout(h: int, s: int) -> tuple[int, list[int]]:
+    """Branches per map and first branch of each map (ops.py:96-139)."""
+    if h >= s:
+        group = h // s
+        return group, [i * group for i in range(s)]
+    rep = s // h
+    return 1, [i // rep for i in range(s)]
+
+
+class _MixedAttention(torch.autograd.Function):
+    """Y = sum_s alpha_s softmax_causal(gamma_s Q_s K_s^T) V for routed [2,H,B,T,R]."""
+
+    @staticmethod
+    def forward(ctx, routed: Tensor, value: Tensor, scales: Tensor, weights: Tensor | None, maps: int,  # type: ignore[override]
+                causal: bool, key_norm_bound: float):
+        _two, h, batch, length, r = routed.shape
+        flat = routed.view(-1, r)
+        group, branch0 = _map_layout(h, maps)
+        qmap = RowMap(flat, 0, length, batch * length)
+        kmap = RowMap(flat, h * batch * length, length, batch * length)
+        y, lse = _attention_forward(qmap, kmap, value, batch, length, r, maps, group, branch0, causal, scales,
+                                    weights if maps > 1 else None, None, key_norm_bound, routed.dtype)
+        ctx.save_for_backward(routed, value, scales, weights if weights is not None else scales, y, lse)
+        ctx.meta = (maps, causal, key_norm_bound, weights is not None)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy: Tensor):  # type: ignore[override]
+        raise NotImplementedError("outer attention backward kernel is not available in this build")
+
+
+def routed_attention_mixed(routed: Tensor, value: Tensor, scales: Tensor, map_weights: Tensor | None, cfg) -> Tensor:
+    """Module path: mixed outer attention over the routed [2, H, B, T, R] tensor."""
+    maps = cfg.outer_maps
+    # Routed vectors have norm <= 1 (normalised outputs, or convex combinations
+    # of unit dictionary atoms), which bounds every score by gamma_s.
+    return _MixedAttention.apply(routed, value, scales, map_weights, maps, cfg.causal, 1.0)
+
+
+def routed_attention_maps(routed: Tensor, value: Tensor, scales: Tensor, cfg) -> Tensor:
+    """Per-map outputs [B, S, T, D] (map_combine='concat'): one launch per map."""
+    outs = []
+    for s in range(cfg.outer_maps):
+        outs.append(_SingleMapAttention.apply(routed, value, scales, s, cfg.outer_maps, cfg.causal))
+    return torch.stack(outs, dim=1)
+
+
+class _SingleMapAttention(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, routed: Tensor, value: Tensor, scales: Tensor, s: int, maps: int, causal: bool):  # type: ignore[override]
+        _two, h, batch, length, r = routed.shape
+        flat = routed.view(-1, r)
+        group, branch0 = _map_layout(h, maps)
+        qmap = RowMap(flat, 0, length, batch * length)
+        kmap = RowMap(flat, h * batch * length, length, batch * length)
+        y, _ = _attention_forward(qmap, kmap, value, batch, length, r, 1, group, [branch0[s]], causal,
+                                  scales[s:s + 1], None, None, 1.0, routed.dtype)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy: Tensor):  # type: ignore[override]
+        raise NotImplementedError("outer attention backward kernel is not available in this build")
+
+
+class _PerMapAttention(torch.autograd.Function):
+    """Op-level routed attention: [B, S, T, R] query/key -> [B, S, T, D]."""
+
+    @staticmethod
+    def forward(ctx, query: Tensor, key: Tensor, value: Tensor, scales: Tensor, causal: bool):  # type: ignore[override]
+        batch, maps, length, r = query.shape
+        qf = query.contiguous().view(-1, r)
+        kf = key.contiguous().view(-1, r)
+        kmax = key.detach().float().norm(dim=-1).amax(dim=-1).contiguous()  # [B, S] score bound
+        outs = []
+        for s in range(maps):
+            qmap = RowMap(qf, 0, maps * length, length)
+            kmap = RowMap(kf, 0, maps * length, length)
+            y, _ = _attention_forward(qmap, kmap, value, batch, length, r, 1, 1, [s], causal, scales[s:s + 1], None,
+                                      kmax[:, s].contiguous(), 1.0, query.dtype)
+            outs.append(y)
+        return torch.stack(outs, dim=1)
+
+    @staticmethod
+    def backward(ctx, dy: Tensor):  # type: ignore[override]
+        raise NotImplementedError("outer attention backward kernel is not available in this build")
+
+
+def routed_attention(query: Tensor, key: Tensor, value: Tensor, scales: Tensor, causal: bool = True) -> Tensor:
+    """B200 counterpart of ``routed_attention_triton`` (triton_kernels.py:2290-2305).
+
+    ``query``/``key`` [B, S, T, R], ``value`` [B, T, D] (one fp16/bf16 dtype),
+    ``scales`` [S]; returns [B, S, T, D].
+    """
+    if query.ndim != 4 or key.shape != query.shape:
+        raise ValueError("query and key must have matching [B, S, T, R] shapes")
+    if value.ndim != 3 or value.shape[:2] != (query.shape[0], query.shape[2]):
+        raise ValueError("value must have shape [B, T, D] matching query")
+    if scales.shape != (query.shape[1],):
+        raise ValueError(f"scales must have shape [{query.shape[1]}]")
+    _check_half_cuda("routed attention", query, key, value)
+    return _PerMapAttention.apply(query, key, value, scales, causal)

@@ -94,6 +94,25 @@ DA_API int da_route_fwd(const void* q, int64_t rows, int64_t q_cols, int64_t q_r
                         int normalize_input, int normalize_output, void* z, float* lse, float* out_norm,
                         int* argmax, int* work, int repair_cap, int* status, void* stream);
 
+/* ---- outer routed attention with the map mix, forward -------------------
+ * Replaces routed_attention_triton / _routed_attention_triton_forward
+ * (triton_kernels.py:2290-2305, :2022-2090; math of ops.py:65-93) together
+ * with score-map assembly (ops.py:96-139, as addressing) and the alpha mix
+ * (modules.py:265-272):  Y = sum_s alpha_s softmax(gamma_s Q_s K_s^T) V.
+ * Q/K rows: row(b, branch, t) = base + b*sb + branch*sbr + t inside [rows, R]
+ * matrices of dtype `dtype`; map s concatenates `group` branches starting at
+ * branch0[s] (host array of `maps` ints) and scales the dot product by
+ * gamma_s / sqrt(group).  v: [B, T, D] bf16, D in {128, 256, 512};
+ * maps <= 4 and maps*group*R <= 512.  weights: [maps] alpha (may be null when
+ * maps == 1).  key_norm_max: [B*maps] upper bounds of ||k|| per (b, map), or
+ * null to use key_norm_bound for all.  Outputs y [B, T, D] (dtype) and lse
+ * [B, maps, T] fp32 (natural-log normaliser of every map's softmax). */
+DA_API int da_attn_fwd(const void* q, int64_t q_rows, int64_t q_base, int64_t q_sb, int64_t q_sbr, const void* k,
+                       int64_t k_rows, int64_t k_base, int64_t k_sb, int64_t k_sbr, const void* v, int B, int T,
+                       int R, int D, int maps, int group, const int* branch0, int causal, int dtype,
+                       const float* scales, const float* weights, const float* key_norm_max, float key_norm_bound,
+                       void* y, float* lse, int* status, void* stream);
+
 /* ---- building-block check -------------------------------------------
  * No reference counterpart: D[128, n] = A[128, k] * B^T computed by one
  * tcgen05 tile (cta_group 1 or 2) for testing the descriptor layouts.
