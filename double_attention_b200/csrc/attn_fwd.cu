@@ -530,6 +530,7 @@ extern "C" int da_attn_fwd(const void* q, int64_t q_rows, int64_t q_base, int64_
                            void* stream) {
   using namespace da;
   if (!q || !k || !v || !branch0 || !scales || !y || !lse || !status) return DA_ERR_NULL;
+  if (int rc = bind_device(q)) return rc;
   if (dtype != DA_BF16 && dtype != DA_F16) return DA_ERR_DTYPE;
   if (B <= 0 || T <= 0 || maps < 1 || maps > attn::kMaxMaps || group < 1) return DA_ERR_SHAPE;
   if (R % 64 || R <= 0) return DA_ERR_UNSUPPORTED;

@@ -88,6 +88,7 @@ extern "C" int da_dict_norm_fwd(const float* raw, int64_t R, int64_t M, float ep
                                 void* out_t, float* denom, float* max_col_norm, void* stream) {
   using namespace da;
   if (!raw) return DA_ERR_NULL;
+  if (int rc = bind_device(raw)) return rc;
   if (R <= 0 || M <= 0 || R > (1 << 16) || M > (1 << 24)) return DA_ERR_SHAPE;
   if (out_dtype != DA_BF16 && out_dtype != DA_F16) return DA_ERR_DTYPE;
   if (out_t && (reinterpret_cast<uintptr_t>(out_t) & 15)) return DA_ERR_ALIGN;
@@ -108,6 +109,7 @@ extern "C" int da_dict_norm_bwd(const float* raw, const float* denom, const floa
                                 int64_t R, int64_t M, float eps, float* grad_raw, int accumulate, void* stream) {
   using namespace da;
   if (!raw || !denom || !grad_raw || (!grad && !grad_t)) return DA_ERR_NULL;
+  if (int rc = bind_device(raw)) return rc;
   if (R <= 0 || M <= 0 || R > (1 << 16) || M > (1 << 24)) return DA_ERR_SHAPE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   dict_norm_bwd_kernel<<<dim3((unsigned)((M + 127) / 128)), dim3(128), 0, st>>>(raw, denom, grad, grad_t, (int)R,
@@ -137,6 +139,7 @@ __global__ void col_norm_max_kernel(const T* __restrict__ d, int R, int M, float
 extern "C" int da_col_norm_max(const void* dict, int64_t R, int64_t M, int dtype, float* out, void* stream) {
   using namespace da;
   if (!dict || !out) return DA_ERR_NULL;
+  if (int rc = bind_device(dict)) return rc;
   if (R <= 0 || M <= 0) return DA_ERR_SHAPE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(out, 0, sizeof(float), st) != cudaSuccess) return record_cuda_error();

@@ -1,0 +1,219 @@
+// Dense GEMM on tcgen05: C[M, N] (+)= sum_k A(m, k) B(n, k).
+//
+// Used for the fused Q/K projection of SharedDictionaryAttention
+// (modules.py:143-157: x . cat(W_q, W_k)^T) and for its backward (dX = dC W,
+// dW = dC^T X).  A and B are each either K-major (row-major [M, K] /
+// [N, K]) or MN-major (row-major [K, M] / [K, N]); both layouts are staged
+// by TMA into 128-byte swizzled tiles that the tensor core reads directly.
+// One CTA computes a 128 x kN tile, streaming K in 64-wide stages through a
+// kStages-deep TMA -> MMA pipeline, accumulating in TMEM; four epilogue
+// warps read the accumulator back (one row per thread) and store it.
+#include "common.cuh"
+#include "host_util.h"
+
+namespace da {
+namespace gemm {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kThreads = 192;  // warp0 TMA, warp1 MMA, warps2-5 epilogue
+
+template <int kN>
+struct Cfg {
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = kN * kBK * 2;
+  static constexpr int kStages = kN == 256 ? 4 : 6;
+  static constexpr int kSmem = kStages * (kABytes + kBBytes);
+};
+
+struct Params {
+  int M, N, K;
+  void* c;
+  int64_t ldc;
+  int out_f32;     // C is fp32 (else the input dtype)
+  int accumulate;  // C += A.B (else C = A.B)
+  int* status;
+};
+
+template <typename T, int kN, bool kAmn, bool kBmn>
+__global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap ta,
+                                                           const __grid_constant__ CUtensorMap tb, const Params p) {
+  using C = Cfg<kN>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t full[C::kStages], empty[C::kStages], done;
+  __shared__ uint32_t tmem_base;
+  __shared__ int abort_flag;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int m0 = blockIdx.x * kBM, n0 = blockIdx.y * kN;
+  const int nk = (p.K + kBK - 1) / kBK;  // TMA zero-fills the ragged last K stage
+  Abort ab{&abort_flag, p.status};
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc<1>(&tmem_base, kN);
+    tmem_relinquish<1>();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&ta);
+      prefetch_tmap(&tb);
+      int issued = 0;
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % C::kStages;
+        if (!mbar_wait(&empty[s], ((kb / C::kStages) & 1u) ^ 1u, ab, 41)) break;
+        mbar_arrive_expect_tx(&full[s], C::kABytes + C::kBBytes);
+        uint8_t* sa = smem + s * (C::kABytes + C::kBBytes);
+        uint8_t* sb = sa + C::kABytes;
+        if (!kAmn) {
+          tma_load_2d(&ta, &full[s], sa, kb * kBK, m0);
+        } else {
+          tma_load_2d(&ta, &full[s], sa, m0, kb * kBK);
+          tma_load_2d(&ta, &full[s], sa + kBK * 128, m0 + 64, kb * kBK);
+        }
+        if (!kBmn) {
+          tma_load_2d(&tb, &full[s], sb, kb * kBK, n0);
+        } else {
+          for (int i = 0; i < kN / 64; ++i) tma_load_2d(&tb, &full[s], sb + i * kBK * 128, n0 + i * 64, kb * kBK);
+        }
+        issued = kb + 1;
+      }
+      for (int kb = (issued > C::kStages ? issued - C::kStages : 0); kb < issued; ++kb)
+        mbar_wait_drain(&full[kb % C::kStages], (kb / C::kStages) & 1u);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16(kBM, kN, std::is_same<T, __nv_bfloat16>::value, kAmn, kBmn);
+      bool ok = true;
+      for (int kb = 0; ok && kb < nk; ++kb) {
+        const int s = kb % C::kStages;
+        ok = mbar_wait(&full[s], (kb / C::kStages) & 1u, ab, 42);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t sa = smem_u32(smem + s * (C::kABytes + C::kBBytes));
+        const uint32_t sb = sa + C::kABytes;
+#pragma unroll
+        for (int k = 0; k < kBK / 16; ++k) {
+          const uint64_t ad = kAmn ? sdesc_sw128(sa + k * 16 * 128, kBK * 128, 1024)
+                                   : sdesc_sw128(sa + k * 32, 16, 1024);
+          const uint64_t bd = kBmn ? sdesc_sw128(sb + k * 16 * 128, kBK * 128, 1024)
+                                   : sdesc_sw128(sb + k * 32, 16, 1024);
+          mma_f16_ss<1>(tmem, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+        }
+        mma_commit<1>(smem_u32(&empty[s]));
+      }
+      mma_commit<1>(smem_u32(&done));
+      mbar_wait_drain(&done, 0);
+    }
+  } else {
+    const int quad = warp & 3;
+    const int row = m0 + quad * 32 + lane;
+    bool ok = mbar_wait(&done, 0, ab, 43);
+    ok = __all_sync(0xffffffffu, ok);
+    tc_fence_after();
+    if (ok) {
+      const bool live = row < p.M;
+      for (int c = 0; c < kN; c += 32) {
+        float v[32];
+        tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + c, v);
+        tmem_wait_ld();
+        if (!live || n0 + c >= p.N) continue;
+        if (p.out_f32) {
+          float* dst = reinterpret_cast<float*>(p.c) + (size_t)row * p.ldc + n0 + c;
+#pragma unroll
+          for (int e = 0; e < 32; e += 4) {
+            float4 w = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+            if (p.accumulate) {
+              const float4 o = *reinterpret_cast<float4*>(dst + e);
+              w.x += o.x; w.y += o.y; w.z += o.z; w.w += o.w;
+            }
+            *reinterpret_cast<float4*>(dst + e) = w;
+          }
+        } else {
+          T* dst = reinterpret_cast<T*>(p.c) + (size_t)row * p.ldc + n0 + c;
+          uint32_t w[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) w[e] = pack2<T>(v[2 * e], v[2 * e + 1]);
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            reinterpret_cast<uint4*>(dst)[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc<1>(tmem, kN);
+}
+
+template <typename T, int kN, bool kAmn, bool kBmn>
+int launch(const void* A, int64_t lda, const void* B, int64_t ldb, const Params& p, cudaStream_t st) {
+  using C = Cfg<kN>;
+  const CUtensorMapDataType dt =
+      std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap ta, tb;
+  int rc = kAmn ? make_tmap_2d(&ta, A, dt, 2, p.M, p.K, (uint64_t)lda * 2, 64, kBK)
+                : make_tmap_2d(&ta, A, dt, 2, p.K, p.M, (uint64_t)lda * 2, 64, kBM);
+  if (rc) return rc;
+  rc = kBmn ? make_tmap_2d(&tb, B, dt, 2, p.N, p.K, (uint64_t)ldb * 2, 64, kBK)
+            : make_tmap_2d(&tb, B, dt, 2, p.K, p.N, (uint64_t)ldb * 2, 64, kN);
+  if (rc) return rc;
+  auto kern = gemm_kernel<T, kN, kAmn, kBmn>;
+  const int smem = C::kSmem + 1024;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return record_cuda_error();
+  dim3 grid((unsigned)((p.M + kBM - 1) / kBM), (unsigned)((p.N + kN - 1) / kN));
+  kern<<<grid, kThreads, smem, st>>>(ta, tb, p);
+  if (cudaPeekAtLastError() != cudaSuccess) return record_cuda_error();
+  return DA_OK;
+}
+
+template <typename T>
+int dispatch(int a_mn, int b_mn, int n_tile, const void* A, int64_t lda, const void* B, int64_t ldb, const Params& p,
+             cudaStream_t st) {
+#define DA_GEMM_CASE(NT, AMN, BMN) \
+  if (n_tile == NT && a_mn == AMN && b_mn == BMN) return launch<T, NT, AMN, BMN>(A, lda, B, ldb, p, st);
+  DA_GEMM_CASE(128, 0, 0)
+  DA_GEMM_CASE(256, 0, 0)
+  DA_GEMM_CASE(128, 0, 1)
+  DA_GEMM_CASE(256, 0, 1)
+  DA_GEMM_CASE(128, 1, 1)
+  DA_GEMM_CASE(256, 1, 1)
+#undef DA_GEMM_CASE
+  return DA_ERR_UNSUPPORTED;
+}
+
+}  // namespace gemm
+}  // namespace da
+
+extern "C" int da_gemm(const void* A, int64_t lda, int a_mn_major, const void* B, int64_t ldb, int b_mn_major,
+                       void* C, int64_t ldc, int64_t M, int64_t N, int64_t K, int dtype, int out_f32, int accumulate,
+                       int* status, void* stream) {
+  using namespace da;
+  if (!A || !B || !C || !status) return DA_ERR_NULL;
+  if (int rc = bind_device(A)) return rc;
+  if (dtype != DA_BF16 && dtype != DA_F16) return DA_ERR_DTYPE;
+  if (M <= 0 || N <= 0 || K <= 0 || N % 128) return DA_ERR_SHAPE;
+  if ((lda % 8) || (ldb % 8)) return DA_ERR_ALIGN;  // 16-byte row strides for TMA
+  if (a_mn_major && M % 128) return DA_ERR_SHAPE;   // every A box starts inside the matrix
+  if (accumulate && !out_f32) return DA_ERR_UNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(C) & 15) || (ldc % 8)) return DA_ERR_ALIGN;
+  gemm::Params p{(int)M, (int)N, (int)K, C, ldc, out_f32, accumulate, status};
+  const int n_tile = (N % 256 == 0 && (M / 128) * (N / 256) >= 120) ? 256 : 128;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == DA_BF16) return gemm::dispatch<__nv_bfloat16>(a_mn_major, b_mn_major, n_tile, A, lda, B, ldb, p, st);
+  return gemm::dispatch<__half>(a_mn_major, b_mn_major, n_tile, A, lda, B, ldb, p, st);
+}

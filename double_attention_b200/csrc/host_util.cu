@@ -56,6 +56,25 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, 
   return DA_OK;
 }
 
+int bind_device(const void* ptr) {
+  // One device per host thread (one process per GPU; autograd keeps one
+  // worker thread per device), so the binding is done once per thread.
+  static thread_local int bound = -1;
+  if (bound >= 0) return DA_OK;
+  cudaPointerAttributes attr;
+  if (cudaPointerGetAttributes(&attr, ptr) != cudaSuccess) return record_cuda_error();
+  if (attr.type != cudaMemoryTypeDevice && attr.type != cudaMemoryTypeManaged) return DA_OK;
+  int cur = -1;
+  if (cudaGetDevice(&cur) != cudaSuccess || cur != attr.device) {
+    cudaGetLastError();
+    if (cudaSetDevice(attr.device) != cudaSuccess) return record_cuda_error();
+  }
+  // cudaSetDevice is lazy about making the context current; touch it.
+  if (cudaFree(nullptr) != cudaSuccess) return record_cuda_error();
+  bound = attr.device;
+  return DA_OK;
+}
+
 static int* g_debug_trace = nullptr;
 int* debug_trace() { return g_debug_trace; }
 void set_debug_trace(int* p) { g_debug_trace = p; }

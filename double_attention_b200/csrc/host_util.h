@@ -28,6 +28,12 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, 
 // da_set_debug_trace; kernels that support it write per-CTA markers there.
 int* debug_trace();
 
+// Makes the primary context of the device owning `ptr` current on the
+// calling thread (autograd runs backward on its own threads, where the
+// runtime this library links may not have a context yet).  Returns DA_OK
+// or DA_ERR_CUDA.
+int bind_device(const void* ptr);
+
 // Number of SMs of the current device (cached per device).
 int sm_count();
 

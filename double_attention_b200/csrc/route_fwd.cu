@@ -583,6 +583,7 @@ extern "C" int da_route_fwd(const void* q, int64_t rows, int64_t q_cols, int64_t
   using namespace da;
   if (!q || !dict_key_t || !dict_value || !beta || !dk_max || !z || !lse || !out_norm || !work || !status)
     return DA_ERR_NULL;
+  if (int rc = bind_device(q)) return rc;
   if (dtype != DA_BF16 && dtype != DA_F16) return DA_ERR_DTYPE;
   if (rows <= 0 || groups <= 0 || M <= 0 || M % 64 || rows > (1ll << 30)) return DA_ERR_SHAPE;
   if (R != 64 && R != 128 && R != 256 && R != 512) return DA_ERR_UNSUPPORTED;

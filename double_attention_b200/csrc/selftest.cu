@@ -155,6 +155,7 @@ extern "C" int da_selftest_mma(int cta_group, int n, int b_mn_major, int k, cons
                                float* D, int* status, void* stream) {
   using namespace da;
   if (!A || !B || !D) return DA_ERR_NULL;
+  if (int rc = bind_device(A)) return rc;
   if (k <= 0 || k % 64 || k > 256) return DA_ERR_SHAPE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 #define DA_SELFTEST_CASE(CG, N, MN) \

@@ -492,3 +492,55 @@ def routed_attention(query: Tensor, key: Tensor, value: Tensor, scales: Tensor, 
         raise ValueError(f"scales must have shape [{query.shape[1]}]")
     _check_half_cuda("routed attention", query, key, value)
     return _PerMapAttention.apply(query, key, value, scales, causal)
+
+
+# ----------------------------------------------------------------------------- projection GEMM
+def gemm(a: Tensor, a_mn: bool, b: Tensor, b_mn: bool, m: int, n: int, k: int, out: Tensor,
+         accumulate: bool = False) -> Tensor:
+    """out[m, n] (+)= sum_k A(m, k) B(n, k) on the tcgen05 GEMM (see da_gemm)."""
+    if a.dtype != b.dtype or a.dtype not in _HALF:
+        raise ValueError("gemm operands must share one fp16/bf16 dtype")
+    if a.stride(-1) != 1 or b.stride(-1) != 1 or out.stride(-1) != 1:
+        raise ValueError("gemm operands must be row-major")
+    ws = workspace(a.device)
+    call("da_gemm", a.data_ptr(), a.stride(0), int(a_mn), b.data_ptr(), b.stride(0), int(b_mn), out.data_ptr(),
+         out.stride(0), m, n, k, dtype_code(a.dtype), int(out.dtype == torch.float32), int(accumulate),
+         ws.status.data_ptr(), stream_ptr(a.device))
+    return out
+
+
+class _Projection(torch.autograd.Function):
+    """[B*T, N] = x [B*T, K] . W[N, K]^T  (the fused Q/K projection)."""
+
+    @staticmethod
+    def forward(ctx, x2d: Tensor, weight: Tensor):  # type: ignore[override]
+        m, k = x2d.shape
+        n = weight.shape[0]
+        out = torch.empty(m, n, dtype=x2d.dtype, device=x2d.device)
+        gemm(x2d, False, weight, False, m, n, k, out)
+        ctx.save_for_backward(x2d, weight)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout: Tensor):  # type: ignore[override]
+        x2d, weight = ctx.saved_tensors
+        dout = dout.contiguous()
+        m, k = x2d.shape
+        n = weight.shape[0]
+        dx = dw = None
+        if ctx.needs_input_grad[0]:
+            dx = torch.empty(m, k, dtype=x2d.dtype, device=x2d.device)
+            gemm(dout, False, weight, True, m, k, n, dx)          # dX = dC . W
+        if ctx.needs_input_grad[1]:
+            dw = torch.empty(n, k, dtype=torch.float32, device=x2d.device)
+            gemm(dout, True, x2d, True, n, k, m, dw)              # dW = dC^T . X (fp32)
+            dw = dw.to(weight.dtype)
+        return dx, dw
+
+
+def qk_projection(x: Tensor, fused_weight: Tensor) -> Tensor:
+    """Fused Q/K projection ``x [B, T, D] -> [B*T, 2*H*R]`` (modules.py:143-157)."""
+    x2d = x.reshape(-1, x.shape[-1])
+    if not x2d.is_contiguous():
+        x2d = x2d.contiguous()
+    return _Projection.apply(x2d, fused_weight.contiguous())

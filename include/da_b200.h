@@ -113,6 +113,19 @@ DA_API int da_attn_fwd(const void* q, int64_t q_rows, int64_t q_base, int64_t q_
                        const float* scales, const float* weights, const float* key_norm_max, float key_norm_bound,
                        void* y, float* lse, int* status, void* stream);
 
+/* ---- dense GEMM (fused Q/K projection and its backward) -----------------
+ * Replaces the cuBLAS GEMM of _project_query_key (modules.py:143-157,
+ * F.linear(x, cat(W_q, W_k))) and its autograd backward.
+ * C[M, N] (+)= sum_k A(m, k) B(n, k), fp16/bf16 operands, fp32 accumulation.
+ * A is [M, K] row-major (a_mn_major = 0) or [K, M] (= 1), leading dimension
+ * lda; B is [N, K] (b_mn_major = 0) or [K, N] (= 1).  C is [M, N] with
+ * leading dimension ldc, in the operand dtype or fp32 (out_f32); accumulate
+ * (fp32 only) adds to C.  N must be a multiple of 128; lda/ldb/ldc multiples
+ * of 8 elements. */
+DA_API int da_gemm(const void* A, int64_t lda, int a_mn_major, const void* B, int64_t ldb, int b_mn_major, void* C,
+                   int64_t ldc, int64_t M, int64_t N, int64_t K, int dtype, int out_f32, int accumulate, int* status,
+                   void* stream);
+
 /* ---- building-block check -------------------------------------------
  * No reference counterpart: D[128, n] = A[128, k] * B^T computed by one
  * tcgen05 tile (cta_group 1 or 2) for testing the descriptor layouts.

@@ -1,0 +1,52 @@
+"""tcgen05 GEMM (fused Q/K projection and its backward) against fp32 matmul."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from double_attention_b200 import ops
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize(("a_mn", "b_mn"), [(False, False), (False, True), (True, True)])
+@pytest.mark.parametrize(("m", "n", "k"), [(4096, 512, 512), (300, 1024, 512), (512, 512, 4104), (256, 256, 96)])
+def test_gemm_layouts(m, n, k, a_mn, b_mn, dtype) -> None:
+    if a_mn and m % 128:
+        pytest.skip("MN-major A needs M % 128 == 0")
+    torch.manual_seed(m + n + k)
+    dev = torch.device("cuda")
+    a = torch.randn(m, k, device=dev).to(dtype)
+    b = torch.randn(n, k, device=dev).to(dtype)
+    a_arg = a.t().contiguous() if a_mn else a
+    b_arg = b.t().contiguous() if b_mn else b
+    out = torch.empty(m, n, device=dev, dtype=torch.float32)
+    ops.gemm(a_arg, a_mn, b_arg, b_mn, m, n, k, out)
+    torch.cuda.synchronize()
+    assert ops.device_status(dev) == 0
+    expected = a.float() @ b.float().t()
+    torch.testing.assert_close(out, expected, atol=2e-3 * k**0.5, rtol=1e-3)
+    # dtype output and fp32 accumulation
+    out16 = torch.empty(m, n, device=dev, dtype=dtype)
+    ops.gemm(a_arg, a_mn, b_arg, b_mn, m, n, k, out16)
+    torch.testing.assert_close(out16.float(), expected, atol=2e-3 * k**0.5, rtol=1e-2)
+    ops.gemm(a_arg, a_mn, b_arg, b_mn, m, n, k, out, accumulate=True)
+    torch.testing.assert_close(out, 2 * expected, atol=4e-3 * k**0.5, rtol=1e-3)
+
+
+def test_projection_autograd() -> None:
+    torch.manual_seed(3)
+    dev = torch.device("cuda")
+    x = torch.randn(2, 300, 512, device=dev).to(torch.bfloat16).requires_grad_()
+    w = (torch.randn(1024, 512, device=dev) * 0.04).to(torch.bfloat16).requires_grad_()
+    y = ops.qk_projection(x, w)
+    dy = torch.randn_like(y)
+    y.backward(dy)
+    xr, wr = x.detach().float().requires_grad_(), w.detach().float().requires_grad_()
+    yr = xr.reshape(-1, 512) @ wr.t()
+    yr.backward(dy.float())
+    torch.testing.assert_close(y.float(), yr, atol=2e-2, rtol=1e-2)
+    torch.testing.assert_close(x.grad.float(), xr.grad, atol=5e-2, rtol=2e-2)
+    torch.testing.assert_close(w.grad.float(), wr.grad, atol=1e-1, rtol=2e-2)
