@@ -18,66 +18,119 @@
 namespace da {
 namespace {
 
+// One CTA per 32 columns: the [R, 32] tile is staged in shared memory with
+// coalesced row reads, column norms are reduced across 8 row groups, and both
+// the [R, M] and the transposed [M, R] outputs are written coalesced.
 template <typename T>
-__global__ void dict_norm_fwd_kernel(const float* __restrict__ raw, int R, int M, float eps, T* __restrict__ out,
-                                     T* __restrict__ out_t, float* __restrict__ denom_out,
-                                     float* __restrict__ max_norm) {
-  const int j = blockIdx.x * blockDim.x + threadIdx.x;
-  if (j >= M) return;
+__global__ void __launch_bounds__(256) dict_norm_fwd_kernel(const float* __restrict__ raw, int R, int M, float eps,
+                                                            T* __restrict__ out, T* __restrict__ out_t,
+                                                            float* __restrict__ denom_out,
+                                                            float* __restrict__ max_norm) {
+  extern __shared__ float tile[];          // [R][33] (padded)
+  __shared__ float part[8][33], part2[8][33], inv[32];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int j0 = blockIdx.x * 32, j = j0 + tx;
   float ss = 0.f;
-  for (int r = 0; r < R; ++r) {
-    const float v = raw[(size_t)r * M + j];
+  for (int r = ty; r < R; r += 8) {
+    const float v = j < M ? raw[(size_t)r * M + j] : 0.f;
+    tile[r * 33 + tx] = v;
     ss = fmaf(v, v, ss);
   }
-  const float denom = fmaxf(sqrtf(ss), eps);
-  if (denom_out) denom_out[j] = denom;
-  float rounded_ss = 0.f;
-  for (int r0 = 0; r0 < R; r0 += 8) {
-    T vals[8];
+  part[ty][tx] = ss;
+  __syncthreads();
+  if (ty == 0) {
+    float t = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int r = r0 + i;
-      const float y = r < R ? raw[(size_t)r * M + j] / denom : 0.f;
-      vals[i] = from_f32<T>(y);
-      const float yr = static_cast<float>(vals[i]);
-      rounded_ss = fmaf(yr, yr, rounded_ss);
-      if (out && r < R) out[(size_t)r * M + j] = vals[i];
-    }
-    if (out_t) {
-      T* dst = out_t + (size_t)j * R + r0;
-      if (r0 + 8 <= R && (R % 8) == 0) {
-        *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<uint4*>(vals);
-      } else {
-        for (int i = 0; i < 8 && r0 + i < R; ++i) dst[i] = vals[i];
-      }
+    for (int i = 0; i < 8; ++i) t += part[i][tx];
+    const float denom = fmaxf(sqrtf(t), eps);
+    inv[tx] = denom;
+    if (denom_out && j < M) denom_out[j] = denom;
+  }
+  __syncthreads();
+  const float denom = inv[tx];
+  float rs = 0.f;
+  for (int r = ty; r < R; r += 8) {
+    const T y = from_f32<T>(tile[r * 33 + tx] / denom);
+    const float yr = static_cast<float>(y);
+    rs = fmaf(yr, yr, rs);
+    tile[r * 33 + tx] = yr;
+    if (out && j < M) out[(size_t)r * M + j] = y;
+  }
+  part2[ty][tx] = rs;
+  __syncthreads();
+  if (max_norm && ty == 0 && j < M) {
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) t += part2[i][tx];
+    atomicMax(reinterpret_cast<int*>(max_norm), __float_as_int(sqrtf(t)));
+  }
+  if (out_t) {
+    // column c of the tile becomes row (j0 + c) of out_t: consecutive threads
+    // write consecutive elements of that row.
+    for (int c = ty; c < 32; c += 8) {
+      if (j0 + c >= M) break;
+      T* dst = out_t + (size_t)(j0 + c) * R;
+      for (int r = tx; r < R; r += 32) dst[r] = from_f32<T>(tile[r * 33 + c]);
     }
   }
-  if (max_norm) atomicMax(reinterpret_cast<int*>(max_norm), __float_as_int(sqrtf(rounded_ss)));
 }
 
 // grad (and grad_t, the same gradient given in [M, R] layout) are summed.
-__global__ void dict_norm_bwd_kernel(const float* __restrict__ raw, const float* __restrict__ denom, const float* __restrict__ grad,
-                                     const float* __restrict__ grad_t, int R, int M, float eps,
-                                     float* __restrict__ grad_raw, int accumulate) {
-  const int j = blockIdx.x * blockDim.x + threadIdx.x;
-  if (j >= M) return;
-  const float d = denom[j];
+// One CTA per 32 columns, both operands staged in shared memory.
+__global__ void __launch_bounds__(256) dict_norm_bwd_kernel(const float* __restrict__ raw,
+                                                            const float* __restrict__ denom,
+                                                            const float* __restrict__ grad,
+                                                            const float* __restrict__ grad_t, int R, int M, float eps,
+                                                            float* __restrict__ grad_raw, int accumulate) {
+  extern __shared__ float smem_f[];
+  float* tx_ = smem_f;              // [R][33] raw
+  float* tg = smem_f + R * 33;      // [R][33] gradient
+  __shared__ float part_ss[8][33], part_dot[8][33], colv[2][32];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int j0 = blockIdx.x * 32, j = j0 + tx;
+  for (int r = ty; r < R; r += 8) {
+    tx_[r * 33 + tx] = j < M ? raw[(size_t)r * M + j] : 0.f;
+    tg[r * 33 + tx] = (grad && j < M) ? grad[(size_t)r * M + j] : 0.f;
+  }
+  __syncthreads();
+  if (grad_t) {
+    for (int c = ty; c < 32; c += 8) {
+      if (j0 + c >= M) break;
+      const float* src = grad_t + (size_t)(j0 + c) * R;
+      for (int r = tx; r < R; r += 32) tg[r * 33 + c] += src[r];
+    }
+    __syncthreads();
+  }
+  const float d = j < M ? denom[j] : 1.f;
   float ss = 0.f, dot = 0.f;
-  for (int r = 0; r < R; ++r) {
-    const float x = raw[(size_t)r * M + j];
-    float g = grad ? grad[(size_t)r * M + j] : 0.f;
-    if (grad_t) g += grad_t[(size_t)j * R + r];
+  for (int r = ty; r < R; r += 8) {
+    const float x = tx_[r * 33 + tx], g = tg[r * 33 + tx];
     ss = fmaf(x, x, ss);
     dot = fmaf(g, x / d, dot);
   }
-  const bool clamped = !(sqrtf(ss) > eps);
-  for (int r = 0; r < R; ++r) {
-    const float x = raw[(size_t)r * M + j];
-    float g = grad ? grad[(size_t)r * M + j] : 0.f;
-    if (grad_t) g += grad_t[(size_t)j * R + r];
-    const float dx = clamped ? g / eps : (g - (x / d) * dot) / d;
-    float* dst = grad_raw + (size_t)r * M + j;
-    *dst = accumulate ? *dst + dx : dx;
+  part_ss[ty][tx] = ss;
+  part_dot[ty][tx] = dot;
+  __syncthreads();
+  if (ty == 0) {
+    float a = 0.f, b = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      a += part_ss[i][tx];
+      b += part_dot[i][tx];
+    }
+    colv[0][tx] = a;
+    colv[1][tx] = b;
+  }
+  __syncthreads();
+  const bool clamped = !(sqrtf(colv[0][tx]) > eps);
+  const float cdot = colv[1][tx];
+  if (j < M) {
+    for (int r = ty; r < R; r += 8) {
+      const float x = tx_[r * 33 + tx], g = tg[r * 33 + tx];
+      const float dx = clamped ? g / eps : (g - (x / d) * cdot) / d;
+      float* dst = grad_raw + (size_t)r * M + j;
+      *dst = accumulate ? *dst + dx : dx;
+    }
   }
 }
 
@@ -89,18 +142,26 @@ extern "C" int da_dict_norm_fwd(const float* raw, int64_t R, int64_t M, float ep
   using namespace da;
   if (!raw) return DA_ERR_NULL;
   if (int rc = bind_device(raw)) return rc;
-  if (R <= 0 || M <= 0 || R > (1 << 16) || M > (1 << 24)) return DA_ERR_SHAPE;
+  if (R <= 0 || M <= 0 || R > 1536 || M > (1 << 24)) return DA_ERR_SHAPE;
   if (out_dtype != DA_BF16 && out_dtype != DA_F16) return DA_ERR_DTYPE;
   if (out_t && (reinterpret_cast<uintptr_t>(out_t) & 15)) return DA_ERR_ALIGN;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (max_col_norm && cudaMemsetAsync(max_col_norm, 0, sizeof(float), st) != cudaSuccess) return record_cuda_error();
-  const dim3 grid((unsigned)((M + 127) / 128)), block(128);
-  if (out_dtype == DA_BF16)
-    dict_norm_fwd_kernel<__nv_bfloat16><<<grid, block, 0, st>>>(raw, (int)R, (int)M, eps, (__nv_bfloat16*)out,
-                                                                (__nv_bfloat16*)out_t, denom, max_col_norm);
-  else
-    dict_norm_fwd_kernel<__half><<<grid, block, 0, st>>>(raw, (int)R, (int)M, eps, (__half*)out, (__half*)out_t,
-                                                         denom, max_col_norm);
+  const dim3 grid((unsigned)((M + 31) / 32)), block(256);
+  const size_t smem = (size_t)R * 33 * sizeof(float);
+  if (smem > 200 * 1024) return DA_ERR_SHAPE;
+  if (out_dtype == DA_BF16) {
+    auto k = dict_norm_fwd_kernel<__nv_bfloat16>;
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return record_cuda_error();
+    k<<<grid, block, smem, st>>>(raw, (int)R, (int)M, eps, (__nv_bfloat16*)out, (__nv_bfloat16*)out_t, denom,
+                                 max_col_norm);
+  } else {
+    auto k = dict_norm_fwd_kernel<__half>;
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return record_cuda_error();
+    k<<<grid, block, smem, st>>>(raw, (int)R, (int)M, eps, (__half*)out, (__half*)out_t, denom, max_col_norm);
+  }
   if (cudaPeekAtLastError() != cudaSuccess) return record_cuda_error();
   return DA_OK;
 }
@@ -112,8 +173,13 @@ extern "C" int da_dict_norm_bwd(const float* raw, const float* denom, const floa
   if (int rc = bind_device(raw)) return rc;
   if (R <= 0 || M <= 0 || R > (1 << 16) || M > (1 << 24)) return DA_ERR_SHAPE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  dict_norm_bwd_kernel<<<dim3((unsigned)((M + 127) / 128)), dim3(128), 0, st>>>(raw, denom, grad, grad_t, (int)R,
-                                                                                 (int)M, eps, grad_raw, accumulate);
+  const size_t smem = 2 * (size_t)R * 33 * sizeof(float);
+  if (smem > 200 * 1024) return DA_ERR_SHAPE;
+  if (cudaFuncSetAttribute(dict_norm_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+      cudaSuccess)
+    return record_cuda_error();
+  dict_norm_bwd_kernel<<<dim3((unsigned)((M + 31) / 32)), dim3(256), smem, st>>>(raw, denom, grad, grad_t, (int)R,
+                                                                                  (int)M, eps, grad_raw, accumulate);
   if (cudaPeekAtLastError() != cudaSuccess) return record_cuda_error();
   return DA_OK;
 }
