@@ -43,6 +43,7 @@ struct Layout {
   int nc, npv;     // N of one P.V instruction, instructions per tile
   int q_bytes, k_bytes, v_bytes;
   int stages;
+  int nb;          // S (TMEM) and P (smem) buffers in flight
   int off_q, off_k, off_v, off_p, off_red, smem;
   int tmem_s, tmem_cols;
 };
@@ -56,18 +57,23 @@ __host__ __device__ inline Layout make_layout(int maps, int group, int R, int D)
   L.q_bytes = kRows * L.kw * 2;
   L.k_bytes = (kNK / 2) * L.kw * 2;
   L.v_bytes = (D / 2) * kNK * 2;
-  const int fixed = L.q_bytes + 2 * kRows * kNK * 2 + 128 * 8 * 4;
-  int st = (225 * 1024 - fixed) / (L.k_bytes + L.v_bytes);
-  L.stages = st > kMaxStages ? kMaxStages : st;
+  L.nb = (D / 2 + 4 * maps * 32) <= 512 ? 4 : 2;
+  auto stages_for = [&](int nb) {
+    const int fixed = L.q_bytes + nb * kRows * kNK * 2 + 128 * 8 * 4;
+    const int st = (225 * 1024 - fixed) / (L.k_bytes + L.v_bytes);
+    return st > kMaxStages ? kMaxStages : st;
+  };
+  if (L.nb == 4 && stages_for(4) < 2) L.nb = 2;
+  L.stages = stages_for(L.nb);
   L.off_q = 0;
   L.off_k = L.off_q + L.q_bytes;
   L.off_v = L.off_k + L.stages * L.k_bytes;
   L.off_p = L.off_v + L.stages * L.v_bytes;
-  L.off_red = L.off_p + 2 * kRows * kNK * 2;
+  L.off_red = L.off_p + L.nb * kRows * kNK * 2;
   const int used = L.off_red + 128 * 8 * 4;
   L.smem = used < 120 * 1024 ? 120 * 1024 : used;  // one CTA per SM
   L.tmem_s = D / 2;
-  const int cols = D / 2 + 2 * maps * 32;
+  const int cols = D / 2 + L.nb * maps * 32;
   L.tmem_cols = cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : cols <= 256 ? 256 : 512;
   return L;
 }
@@ -96,7 +102,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ uint64_t q_full, o_full;
   __shared__ uint64_t k_full[kMaxStages], k_empty[kMaxStages], v_full[kMaxStages], v_empty[kMaxStages];
-  __shared__ uint64_t s_full[2], p_full[2], p_empty[2];
+  __shared__ uint64_t s_full[4], p_full[4], p_empty[4];
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
 
@@ -123,7 +129,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < 4; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 2);
       mbar_init(&p_empty[i], 1);
@@ -141,11 +147,12 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   const uint32_t tmem = tmem_base;
 
   if (warp == 0) {
-    // ---------------------------------------------------------------- TMA producer (both CTAs)
+    // ---------------------------------------------------------------- TMA producers (both CTAs)
+    // Lane 0 streams Q and the key tiles, lane 1 the value tiles: the two
+    // rings advance independently, so scores can run ahead of P.V products.
     if (lane == 0) {
       prefetch_tmap(&tq);
       prefetch_tmap(&tk);
-      prefetch_tmap(&tv);
       if (rank == 0) mbar_arrive_expect_tx(&q_full, 2 * L.q_bytes);
       const uint32_t qf = mapa_shared(smem_u32(&q_full), 0);
       for (int s = 0; s < p.maps; ++s)
@@ -157,7 +164,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
             tma_load_2d_pair(&tq, qf, smem + L.off_q + qb * (kRows * 128), kb * 64, y);
           }
         }
-      int k_issued = 0, v_issued = 0;
+      int k_issued = 0;
       for (int u = 0; u < U; ++u) {
         const int j = u % nj;
         const int ks = u % L.stages;
@@ -174,26 +181,30 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
             }
           }
         k_issued = u + 1;
-        if (kMix && u < nj) continue;  // first sweep: keys only
-        const int v = kMix ? u - nj : u;
-        const int vs = v % L.stages;
-        if (!mbar_wait(&v_empty[vs], ((v / L.stages) & 1u) ^ 1u, ab, 12)) break;
-        if (rank == 0) mbar_arrive_expect_tx(&v_full[vs], 2 * L.v_bytes);
-        const uint32_t vf = mapa_shared(smem_u32(&v_full[vs]), 0);
-        const int per = (L.nc / 2) / 64;  // 64-column boxes per CTA per instruction
-        for (int i = 0; i < L.npv; ++i)
-          for (int bx = 0; bx < per; ++bx)
-            tma_load_2d_pair(&tv, vf, smem + L.off_v + vs * L.v_bytes + (i * per + bx) * (kNK * 128),
-                             i * L.nc + (int)rank * (L.nc / 2) + bx * 64, b * p.T + j * kNK);
-        v_issued = v + 1;
       }
       if (rank == 0) {  // drain: no TMA may be in flight at teardown
         mbar_wait_drain(&q_full, 0);
         for (int u = (k_issued > L.stages ? k_issued - L.stages : 0); u < k_issued; ++u)
           mbar_wait_drain(&k_full[u % L.stages], (u / L.stages) & 1u);
+      }
+    } else if (lane == 1) {
+      prefetch_tmap(&tv);
+      int v_issued = 0;
+      const int per = (L.nc / 2) / 64;  // 64-column boxes per CTA per instruction
+      for (int v = 0; v < nj; ++v) {
+        const int vs = v % L.stages;
+        if (!mbar_wait(&v_empty[vs], ((v / L.stages) & 1u) ^ 1u, ab, 12)) break;
+        if (rank == 0) mbar_arrive_expect_tx(&v_full[vs], 2 * L.v_bytes);
+        const uint32_t vf = mapa_shared(smem_u32(&v_full[vs]), 0);
+        for (int i = 0; i < L.npv; ++i)
+          for (int bx = 0; bx < per; ++bx)
+            tma_load_2d_pair(&tv, vf, smem + L.off_v + vs * L.v_bytes + (i * per + bx) * (kNK * 128),
+                             i * L.nc + (int)rank * (L.nc / 2) + bx * 64, b * p.T + v * kNK);
+        v_issued = v + 1;
+      }
+      if (rank == 0)
         for (int v = (v_issued > L.stages ? v_issued - L.stages : 0); v < v_issued; ++v)
           mbar_wait_drain(&v_full[v % L.stages], (v / L.stages) & 1u);
-      }
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer (leader)
@@ -205,8 +216,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         mma_commit<2>(mapa_shared(smem_u32(bar), 1));
       };
       auto issue_s = [&](int u) -> bool {
-        const int sb = u & 1, ks = u % L.stages;
-        if (u >= 2 && !mbar_wait(&p_full[sb], ((u - 2) >> 1) & 1u, ab, 22)) return false;
+        const int sb = u % L.nb, ks = u % L.stages;
+        if (u >= L.nb && !mbar_wait(&p_full[sb], ((u - L.nb) / L.nb) & 1u, ab, 22)) return false;
         if (!mbar_wait(&k_full[ks], (u / L.stages) & 1u, ab, 23)) return false;
         tc_fence_after();
         const uint32_t qa = smem_u32(smem + L.off_q);
@@ -227,8 +238,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       };
       auto issue_pv = [&](int v) -> bool {
         const int u = kMix ? v + nj : v;
-        const int pb = v & 1, vs = v % L.stages;
-        if (!mbar_wait(&p_full[u & 1], (u >> 1) & 1u, ab, 24)) return false;
+        const int pb = v % L.nb, vs = v % L.stages;
+        if (!mbar_wait(&p_full[u % L.nb], (u / L.nb) & 1u, ab, 24)) return false;
         if (!mbar_wait(&v_full[vs], (v / L.stages) & 1u, ab, 25)) return false;
         tc_fence_after();
         const uint32_t pa = smem_u32(smem + L.off_p + pb * (kRows * kNK * 2));
@@ -249,12 +260,13 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       };
       bool ok = mbar_wait(&q_full, 0, ab, 21);
       tc_fence_after();
-      for (int u = 0; ok && u < U; ++u) {
-        ok = issue_s(u);
-        const int v = kMix ? u - nj : u;
-        if (ok && v >= 1) ok = issue_pv(v - 1);
+      // Scores run up to nb tiles ahead of the probability products.
+      int next_u = 0;
+      for (int v = 0; ok && v < nj; ++v) {
+        const int uv = kMix ? v + nj : v;
+        while (ok && next_u < U && next_u < uv + L.nb) ok = issue_s(next_u++);
+        if (ok) ok = issue_pv(v);
       }
-      if (ok) ok = issue_pv(nj - 1);
       commit_both(&o_full);
       mbar_wait_drain(&o_full, 0);
     }
@@ -312,8 +324,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     // ---- sweep 1 (several maps): exact per-map log-sum-exp
     if (kMix) {
       for (int u = 0; u < nj; ++u) {
-        const int sb = u & 1;
-        if (ok && u > 0) ok = mbar_wait(&s_full[sb], (u >> 1) & 1u, ab, 32);
+        const int sb = u % L.nb;
+        if (ok && u > 0) ok = mbar_wait(&s_full[sb], (u / L.nb) & 1u, ab, 32);
         ok = __all_sync(0xffffffffu, ok);
         if (ok) {
           tc_fence_after();
@@ -357,9 +369,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     float psum = 0.f, pmx = -INFINITY;
     for (int v = 0; v < nj; ++v) {
       const int u = kMix ? v + nj : v;
-      const int sb = u & 1, pb = v & 1;
-      if (ok && u > 0) ok = mbar_wait(&s_full[sb], (u >> 1) & 1u, ab, 32);
-      if (ok && v >= 2) ok = mbar_wait(&p_empty[pb], ((v - 2) >> 1) & 1u, ab, 33);
+      const int sb = u % L.nb, pb = v % L.nb;
+      if (ok && u > 0) ok = mbar_wait(&s_full[sb], (u / L.nb) & 1u, ab, 32);
+      if (ok && v >= L.nb) ok = mbar_wait(&p_empty[pb], ((v - L.nb) / L.nb) & 1u, ab, 33);
       ok = __all_sync(0xffffffffu, ok);
       if (ok) {
         tc_fence_after();

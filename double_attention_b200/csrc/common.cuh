@@ -150,6 +150,20 @@ DA_DEV void trace_mark(int* trace, int slot, int value) {
   }
 }
 
+// Post-mortem timestamp (no fence; read after the kernel completed):
+// trace[index] = low 31 bits of %globaltimer in ns.
+DA_DEV void trace_at(int* trace, int index) {
+  if (trace) {
+    const int v = static_cast<int>(globaltimer() & 0x7fffffffull);
+    asm volatile("st.global.s32 [%0], %1;" :: "l"(trace + index), "r"(v) : "memory");
+  }
+}
+
+// Records the low 32 bits of %globaltimer (ns) in the trace slot.
+DA_DEV void trace_time(int* trace, int slot) {
+  if (trace) trace_mark(trace, slot, static_cast<int>(globaltimer() & 0x7fffffffull));
+}
+
 // ---------------------------------------------------------------- TMA
 DA_DEV void prefetch_tmap(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" :: "l"(tmap) : "memory");

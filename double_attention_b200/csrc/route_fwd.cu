@@ -40,6 +40,7 @@ struct FwdCfg {
   static constexpr int kNc = kR < 256 ? kR : 256;  // N of one P.Dv^T instruction
   static constexpr int kPV = kR / kNc;             // P.Dv^T instructions per tile
   static constexpr int kStages = kR == 512 ? 2 : (kR == 256 ? 4 : 8);
+  static constexpr int kB = 4;                     // S (TMEM) and P (smem) buffers in flight
   static constexpr int kQBytes = kRows * kR * 2;         // this CTA's q rows
   static constexpr int kDkBytes = (kNA / 2) * kR * 2;    // this CTA's half of a Dk tile
   static constexpr int kDvBytes = (kR / 2) * kNA * 2;    // this CTA's half of a Dv tile
@@ -48,13 +49,14 @@ struct FwdCfg {
   static constexpr int kOffDk = kOffQ + kQBytes;
   static constexpr int kOffDv = kOffDk + kStages * kDkBytes;
   static constexpr int kOffP = kOffDv + kStages * kDvBytes;
-  static constexpr int kOffRed = kOffP + 2 * kPBytes;     // 2 x 128 floats for row reductions
+  static constexpr int kOffRed = kOffP + kB * kPBytes;     // 2 x 128 floats for row reductions
   // At least 120 KB so that exactly one CTA of a pair lives on each SM.
   static constexpr int kSmemUsed = kOffRed + 2 * 128 * 4;
+  static_assert(kSmemUsed + 1024 + 512 <= 232448, "route tile does not fit in shared memory");
   static constexpr int kSmem = kSmemUsed < 120 * 1024 ? 120 * 1024 : kSmemUsed;
   static constexpr int kTmemO = 0;
   static constexpr int kTmemS = kR / 2;
-  static constexpr int kTmemCols = (kR / 2 + 64) <= 128 ? 128 : ((kR / 2 + 64) <= 256 ? 256 : 512);
+  static constexpr int kTmemCols = (kR / 2 + 32 * kB) <= 128 ? 128 : ((kR / 2 + 32 * kB) <= 256 ? 256 : 512);
   static constexpr int kThreads = 192;             // warp0 TMA, warp1 MMA, warps2-5 softmax
 };
 
@@ -176,7 +178,7 @@ __global__ void __launch_bounds__(192, 1) route_fwd_kernel(const __grid_constant
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ uint64_t q_full, o_full;
   __shared__ uint64_t dk_full[C::kStages], dk_empty[C::kStages], dv_full[C::kStages], dv_empty[C::kStages];
-  __shared__ uint64_t s_full[2], p_full[2], p_empty[2];
+  __shared__ uint64_t s_full[C::kB], p_full[C::kB], p_empty[C::kB];
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag, is_last;
 
@@ -188,7 +190,9 @@ __global__ void __launch_bounds__(192, 1) route_fwd_kernel(const __grid_constant
   const int row0 = (pair % tiles_per_group) * 128;  // first row of the pair inside the group
   const int NJ = p.M / C::kNA;
   Abort ab{&abort_flag, p.status};
-  if (threadIdx.x == 0) trace_mark(p.trace, 7, 1);
+  if (threadIdx.x == 0) trace_time(p.trace, 0);
+  // fine post-mortem timeline of the first pair: 1024 ints per CTA after the 8-int slots
+  int* ft = (p.trace && blockIdx.x < 2) ? p.trace + 8 * gridDim.x + blockIdx.x * 1024 : nullptr;
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
@@ -200,7 +204,7 @@ __global__ void __launch_bounds__(192, 1) route_fwd_kernel(const __grid_constant
       mbar_init(&dv_full[s], 1);
       mbar_init(&dv_empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < C::kB; ++b) {
       mbar_init(&s_full[b], 1);
       mbar_init(&p_full[b], 2);  // one arrival per CTA of the pair
       mbar_init(&p_empty[b], 1);
@@ -211,20 +215,20 @@ __global__ void __launch_bounds__(192, 1) route_fwd_kernel(const __grid_constant
     tmem_alloc<2>(&tmem_base, C::kTmemCols);
     tmem_relinquish<2>();
   }
-  if (threadIdx.x == 32) trace_mark(p.trace, 7, 2);
   tc_fence_before();
   __syncthreads();
   cluster_sync();
   tc_fence_after();
   const uint32_t tmem = tmem_base;
-  if (threadIdx.x == 0) trace_mark(p.trace, 7, 3);
+  if (threadIdx.x == 0) trace_time(p.trace, 1);
 
   if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer (both CTAs)
+    // ------------------------------------------------------------ TMA producers (both CTAs)
+    // Lane 0 streams q and the key tiles, lane 1 the value tiles; the rings
+    // advance independently so scores can run ahead of the P.Dv^T products.
     if (lane == 0) {
       prefetch_tmap(&tq);
       prefetch_tmap(&tdk);
-      prefetch_tmap(&tdv);
       if (rank == 0) mbar_arrive_expect_tx(&q_full, 2 * C::kQBytes);
       const uint32_t qf = mapa_shared(smem_u32(&q_full), 0);
       const int qcol = g * p.col_stride;
@@ -233,7 +237,7 @@ __global__ void __launch_bounds__(192, 1) route_fwd_kernel(const __grid_constant
       const int qrow = min(row0 + 64 * (int)rank, p.rows - 1);
       for (int kb = 0; kb < kR / 64; ++kb)
         tma_load_2d_pair(&tq, qf, smem + C::kOffQ + kb * (C::kRows * 128), qcol + kb * 64, qrow);
-      int dk_issued = 0, dv_issued = 0;
+      int dk_issued = 0;
       for (int j = 0; j < NJ; ++j) {
         const int s = j % C::kStages;
         const uint32_t ph = (j / C::kStages) & 1u;
@@ -244,6 +248,18 @@ __global__ void __launch_bounds__(192, 1) route_fwd_kernel(const __grid_constant
           tma_load_2d_pair(&tdk, kf, smem + C::kOffDk + s * C::kDkBytes + kb * ((C::kNA / 2) * 128), kb * 64,
                            j * C::kNA + (C::kNA / 2) * (int)rank);
         dk_issued = j + 1;
+      }
+      if (rank == 0) {  // drain: the leader's barriers count both CTAs' bytes
+        mbar_wait_drain(&q_full, 0);
+        for (int j = (dk_issued > C::kStages ? dk_issued - C::kStages : 0); j < dk_issued; ++j)
+          mbar_wait_drain(&dk_full[j % C::kStages], (j / C::kStages) & 1u);
+      }
+    } else if (lane == 1) {
+      prefetch_tmap(&tdv);
+      int dv_issued = 0;
+      for (int j = 0; j < NJ; ++j) {
+        const int s = j % C::kStages;
+        const uint32_t ph = (j / C::kStages) & 1u;
         if (!mbar_wait(&dv_empty[s], ph ^ 1u, ab, 12)) break;
         if (rank == 0) mbar_arrive_expect_tx(&dv_full[s], 2 * C::kDvBytes);
         const uint32_t vf = mapa_shared(smem_u32(&dv_full[s]), 0);
@@ -251,19 +267,10 @@ __global__ void __launch_bounds__(192, 1) route_fwd_kernel(const __grid_constant
           tma_load_2d_pair(&tdv, vf, smem + C::kOffDv + s * C::kDvBytes + i * ((C::kNc / 2) * 128), j * C::kNA,
                            i * C::kNc + (C::kNc / 2) * (int)rank);
         dv_issued = j + 1;
-        trace_mark(p.trace, 0, 100 + j);
       }
-      trace_mark(p.trace, 0, 200);
-      // Drain: the leader's full barriers count both CTAs' bytes, so once the
-      // last issued phase of each stage completed, no load is in flight.
-      if (rank == 0) {
-        mbar_wait_drain(&q_full, 0);
-        for (int j = (dk_issued > C::kStages ? dk_issued - C::kStages : 0); j < dk_issued; ++j)
-          mbar_wait_drain(&dk_full[j % C::kStages], (j / C::kStages) & 1u);
+      if (rank == 0)
         for (int j = (dv_issued > C::kStages ? dv_issued - C::kStages : 0); j < dv_issued; ++j)
           mbar_wait_drain(&dv_full[j % C::kStages], (j / C::kStages) & 1u);
-      }
-      trace_mark(p.trace, 0, 300);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (leader CTA)
@@ -277,8 +284,9 @@ __global__ void __launch_bounds__(192, 1) route_fwd_kernel(const __grid_constant
         mma_commit<2>(mapa_shared(smem_u32(bar), 1));
       };
       auto issue_s = [&](int j) -> bool {
-        const int sb = j & 1, s = j % C::kStages;
-        if (j >= 2 && !mbar_wait(&p_full[sb], ((j - 2) >> 1) & 1u, ab, 22)) return false;
+        const int sb = j % C::kB, s = j % C::kStages;
+        trace_at(ft, 100 + 2 * j);
+        if (j >= C::kB && !mbar_wait(&p_full[sb], ((j - C::kB) / C::kB) & 1u, ab, 22)) return false;
         if (!mbar_wait(&dk_full[s], (j / C::kStages) & 1u, ab, 23)) return false;
         tc_fence_after();
         const uint32_t qa = smem_u32(smem + C::kOffQ), ka = smem_u32(smem + C::kOffDk + s * C::kDkBytes);
@@ -287,15 +295,18 @@ __global__ void __launch_bounds__(192, 1) route_fwd_kernel(const __grid_constant
           const int kb = k >> 2, kin = k & 3;
           const uint64_t ad = sdesc_sw128(qa + kb * (C::kRows * 128) + kin * 32, 16, 1024);
           const uint64_t bd = sdesc_sw128(ka + kb * ((C::kNA / 2) * 128) + kin * 32, 16, 1024);
-          mma_f16_ss<2>(tmem + C::kTmemS + sb * 32, ad, bd, idesc_s, k > 0 ? 1u : 0u);
+          mma_f16_ss<2>(tmem + C::kTmemS + (uint32_t)sb * 32, ad, bd, idesc_s, k > 0 ? 1u : 0u);
         }
         commit_both(&s_full[sb]);
         commit_both(&dk_empty[s]);
+        trace_at(ft, 101 + 2 * j);
         return true;
       };
       auto issue_pv = [&](int j) -> bool {
-        const int pb = j & 1, s = j % C::kStages;
-        if (!mbar_wait(&p_full[pb], (j >> 1) & 1u, ab, 24)) return false;
+        const int pb = j % C::kB, s = j % C::kStages;
+        trace_at(ft, 200 + 4 * j);
+        if (!mbar_wait(&p_full[pb], (j / C::kB) & 1u, ab, 24)) return false;
+        trace_at(ft, 201 + 4 * j);
         if (!mbar_wait(&dv_full[s], (j / C::kStages) & 1u, ab, 25)) return false;
         tc_fence_after();
         const uint32_t pa = smem_u32(smem + C::kOffP + pb * C::kPBytes);
@@ -311,20 +322,19 @@ __global__ void __launch_bounds__(192, 1) route_fwd_kernel(const __grid_constant
         }
         commit_both(&p_empty[pb]);
         commit_both(&dv_empty[s]);
+        trace_at(ft, 202 + 4 * j);
         return true;
       };
-      trace_mark(p.trace, 1, ok ? 100 : 99);
-      if (ok) ok = issue_s(0);
-      for (int j = 1; ok && j < NJ; ++j) {
-        ok = issue_s(j);
-        if (ok) ok = issue_pv(j - 1);
-        trace_mark(p.trace, 1, 100 + j);
+      trace_time(p.trace, 2);
+      // Scores run up to kB tiles ahead of the probability products.
+      int next_s = 0;
+      for (int j = 0; ok && j < NJ; ++j) {
+        while (ok && next_s < NJ && next_s < j + C::kB) ok = issue_s(next_s++);
+        if (ok) ok = issue_pv(j);
       }
-      if (ok) ok = issue_pv(NJ - 1);
       commit_both(&o_full);
-      trace_mark(p.trace, 1, ok ? 200 : 199);
+      trace_time(p.trace, 3);
       mbar_wait_drain(&o_full, 0);  // every issued MMA has completed
-      trace_mark(p.trace, 1, 300);
     }
   } else {
     // ------------------------------------------------------------ softmax + epilogue (warps 2..5)
@@ -339,6 +349,7 @@ __global__ void __launch_bounds__(192, 1) route_fwd_kernel(const __grid_constant
 
     // q row norm from the staged q tile (S_0 complete implies q landed).
     bool ok = mbar_wait(&s_full[0], 0, ab, 31);
+    if (arriver) trace_time(p.trace, 4);
     float qn2 = 0.f;
     if (ok) {
       const uint32_t qa = smem_u32(smem + C::kOffQ);
@@ -368,16 +379,19 @@ __global__ void __launch_bounds__(192, 1) route_fwd_kernel(const __grid_constant
     // Every thread runs every iteration (named barriers need all 128), even
     // after a failed wait; failed threads just skip the work.
     for (int j = 0; j < NJ; ++j) {
-      const int sb = j & 1;
-      if (ok && j > 0) ok = mbar_wait(&s_full[sb], (j >> 1) & 1u, ab, 32);
-      if (ok && j >= 2) ok = mbar_wait(&p_empty[sb], ((j - 2) >> 1) & 1u, ab, 33);
+      const int sb = j % C::kB;
+      if (arriver) trace_at(ft, 400 + 8 * j);
+      if (ok && j > 0) ok = mbar_wait(&s_full[sb], (j / C::kB) & 1u, ab, 32);
+      if (arriver) trace_at(ft, 401 + 8 * j);
+      if (ok && j >= C::kB) ok = mbar_wait(&p_empty[sb], ((j - C::kB) / C::kB) & 1u, ab, 33);
       // tcgen05.ld is warp-collective: the whole warp loads or none of it.
       ok = __all_sync(0xffffffffu, ok);
       if (ok) {
         tc_fence_after();
         float v[32];
-        tmem_ld32(tmem + lane_base + C::kTmemS + sb * 32, v);
+        tmem_ld32(tmem + lane_base + C::kTmemS + (uint32_t)sb * 32, v);
         tmem_wait_ld();
+        if (arriver) trace_at(ft, 402 + 8 * j);
         uint32_t packed[16];
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
@@ -397,20 +411,24 @@ __global__ void __launch_bounds__(192, 1) route_fwd_kernel(const __grid_constant
         for (int c = 0; c < 4; ++c)
           st_shared_v4(pa + sw128_offset(r, half * 4 + c), packed[4 * c], packed[4 * c + 1], packed[4 * c + 2],
                        packed[4 * c + 3]);
+        if (arriver) trace_at(ft, 403 + 8 * j);
         fence_proxy_async();
+        if (arriver) trace_at(ft, 404 + 8 * j);
       }
       tc_fence_before();
       named_bar_sync(1, 128);
       if (arriver) {
+        trace_at(ft, 405 + 8 * j);
         mbar_arrive_cluster(pf_leader + sb * 8);
-        trace_mark(p.trace, 2, (ok ? 100 : 1000) + j);
+        trace_at(ft, 406 + 8 * j);
       }
     }
 
+    if (arriver) trace_time(p.trace, 5);
     // ---- epilogue: combine the two column halves of each row, normalise, store.
     if (ok) ok = mbar_wait(&o_full, 0, ab, 34);
     ok = __all_sync(0xffffffffu, ok);
-    if (arriver) trace_mark(p.trace, 2, ok ? 200 : 199);
+    if (arriver) trace_time(p.trace, 6);
     red[l] = sum;
     red[128 + l] = mx;
     named_bar_sync(1, 128);
@@ -479,15 +497,11 @@ __global__ void __launch_bounds__(192, 1) route_fwd_kernel(const __grid_constant
     }
   }
 
-  if (threadIdx.x == 64) trace_mark(p.trace, 2, 400);
   tc_fence_before();
   __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) trace_mark(p.trace, 7, 4);
   cluster_sync();
-  if (threadIdx.x == 0) trace_mark(p.trace, 7, 5);
   if (warp == 1) tmem_dealloc<2>(tmem, C::kTmemCols);
-  if (threadIdx.x == 32) trace_mark(p.trace, 7, 6);
 
   // The last CTA to finish repairs the listed rows and resets the counters.
   if (threadIdx.x == 0) is_last = atomicAdd(&p.work[0], 1) == (int)gridDim.x - 1;
@@ -502,7 +516,7 @@ __global__ void __launch_bounds__(192, 1) route_fwd_kernel(const __grid_constant
       __threadfence();
     }
   }
-  if (threadIdx.x == 0) trace_mark(p.trace, 7, 9);
+  if (threadIdx.x == 0) trace_time(p.trace, 7);
 }
 
 template <int kR, typename T>

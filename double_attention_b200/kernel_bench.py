@@ -1,0 +1,133 @@
+"""Single-kernel driver: runs one sm_100a kernel on a BASELINE workload shape.
+
+Used for per-kernel timing and for focused profiler captures, e.g.
+
+    python -m double_attention_b200.kernel_bench --kernel route --config 2 --reps 3
+    ncu --set full --clock-control none -k regex:route_fwd -c 1 \\
+        python -m double_attention_b200.kernel_bench --kernel route --config 2 --reps 3
+
+Inputs are synthetic (seeded N(0,1) activations, normalised random
+dictionaries / routed vectors) with the shapes of the named config.  With
+``--time`` the kernel is timed with CUDA events (L2 flushed between
+launches) and one JSON line with the algorithmic FLOPs and achieved
+TFLOP/s is printed.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import statistics
+
+import torch
+import torch.nn.functional as F
+
+from . import ops
+
+# (preset, batch, seq, dtype) per BASELINE.json config (per GPU)
+SHAPES = {
+    2: ("a1", 8, 512, torch.float16),
+    3: ("qk4-s4", 16, 2048, torch.bfloat16),
+    4: ("a1-r512-d1536", 4, 8192, torch.bfloat16),
+    5: ("a1", 32, 1024, torch.bfloat16),
+}
+
+
+class _Cfg:
+    def __init__(self, maps: int) -> None:
+        self.outer_maps = maps
+        self.causal = True
+
+
+def make_case(kernel: str, config: int, device: torch.device):
+    from .config import experiment_config
+
+    preset, batch, seq, dtype = SHAPES[config]
+    cfg = experiment_config(preset)
+    h, r, m, d = cfg.qk_branches, cfg.routing_dim, cfg.dictionary_size, cfg.model_dim
+    g = torch.Generator().manual_seed(config)
+    if kernel == "route":
+        proj = torch.randn(batch * seq, 2 * h * r, generator=g).to(dtype).to(device)
+        dk = F.normalize(torch.randn(r, m, generator=g), dim=0).to(dtype).to(device)
+        dv = F.normalize(torch.randn(r, m, generator=g), dim=0).to(dtype).to(device)
+        views = ops.dictionary_views_from_normalized(dk, dv, dtype)
+        beta = torch.tensor(cfg.beta, device=device)
+        rows = 2 * batch * seq * h
+
+        def run():
+            ops._route_forward(proj, batch * seq, 2 * h, r, views, beta, cfg.eps, True, True)
+
+        return run, 4.0 * r * m * rows
+    if kernel == "attention":
+        routed = F.normalize(torch.randn(2, h, batch, seq, r, generator=g), dim=-1).to(dtype).to(device)
+        value = torch.randn(batch, seq, d, generator=g).to(torch.bfloat16).to(device)
+        scales = torch.full((cfg.outer_maps,), cfg.initial_score_scale, device=device)
+        mix = torch.full((cfg.outer_maps,), 1.0 / cfg.outer_maps, device=device) if cfg.outer_maps > 1 else None
+        c = _Cfg(cfg.outer_maps)
+
+        def run():
+            ops.routed_attention_mixed(routed, value, scales, mix, c)
+
+        return run, float(batch) * seq * seq * (cfg.outer_maps * r + d)
+    if kernel == "projection":
+        x = torch.randn(batch * seq, d, generator=g).to(dtype).to(device)
+        w = (torch.randn(2 * h * r, d, generator=g) * d**-0.5).to(dtype).to(device)
+        out = torch.empty(batch * seq, 2 * h * r, dtype=dtype, device=device)
+
+        def run():
+            ops.gemm(x, False, w, False, batch * seq, 2 * h * r, d, out)
+
+        return run, 2.0 * batch * seq * d * 2 * h * r
+    raise ValueError(f"unknown kernel {kernel!r}")
+
+
+def time_kernel(run, reps: int, device: torch.device) -> float:
+    """Mean device time (ms) of `run`, L2 flushed before each launch."""
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+    for _ in range(3):
+        run()
+    # capture the launch in a CUDA graph so host overhead cannot leak into the timing
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream(device)
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        run()
+    stream.wait_stream(side)
+    with torch.cuda.graph(graph):
+        run()
+    events = []
+    for _ in range(reps):
+        flush.zero_()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        graph.replay()
+        e.record(stream)
+        events.append((s, e))
+    torch.cuda.synchronize()
+    return statistics.mean(s.elapsed_time(e) for s, e in events)
+
+
+def main(argv=None) -> int:
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--kernel", choices=("route", "attention", "projection"), required=True)
+    p.add_argument("--config", type=int, choices=sorted(SHAPES), default=2)
+    p.add_argument("--reps", type=int, default=3)
+    p.add_argument("--time", action="store_true")
+    args = p.parse_args(argv)
+    device = torch.device("cuda", 0)
+    run, flops = make_case(args.kernel, args.config, device)
+    if args.time:
+        ms = time_kernel(run, args.reps, device)
+        print(json.dumps({"kernel": args.kernel, "config": args.config, "ms": ms, "flops": flops,
+                          "tflops": flops / (ms / 1e3) / 1e12}))
+    else:
+        for _ in range(args.reps):
+            run()
+        torch.cuda.synchronize()
+    ops.device_status(device)
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -1,0 +1,53 @@
+"""The C-ABI library loads on a CPU-only host and exports every entry point
+declared in include/*.h; no compute is called here."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from double_attention_b200 import _lib
+
+REPO = Path(__file__).resolve().parent.parent
+
+
+def declared_symbols() -> list[str]:
+    names = []
+    for header in sorted((REPO / "include").glob("*.h")):
+        names += re.findall(r"^DA_API\s+[\w\s\*]+?\b(da_\w+)\s*\(", header.read_text(), flags=re.M)
+    return names
+
+
+def test_header_declares_entry_points() -> None:
+    names = declared_symbols()
+    for required in ("da_dict_norm_fwd", "da_route_fwd", "da_attn_fwd", "da_gemm", "da_status_string"):
+        assert required in names
+
+
+def test_library_loads_and_exports_every_declared_symbol() -> None:
+    handle = _lib.lib()
+    for name in declared_symbols():
+        assert hasattr(handle, name), name
+    assert b"sm_100a" in handle.da_version()
+    assert handle.da_status_string(_lib.DA_ERR_SHAPE) == b"unsupported or inconsistent shape"
+
+
+def test_bound_signatures_cover_compute_entry_points() -> None:
+    for name in declared_symbols():
+        if name in ("da_version", "da_status_string", "da_last_cuda_error"):
+            continue
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+
+
+def test_argument_validation_happens_before_any_device_work() -> None:
+    handle = _lib.lib()
+    # null pointers are rejected on the host (no CUDA call is made)
+    assert handle.da_route_fwd(*([None] * 1), *([0] * 8), *([None] * 4), ctypes.c_float(1e-6), 1, 1,
+                               *([None] * 5), 0, None, None) == _lib.DA_ERR_NULL
+    with pytest.raises(ValueError):
+        _lib.check("da_gemm", _lib.DA_ERR_SHAPE)
+    with pytest.raises(NotImplementedError):
+        _lib.check("da_attn_fwd", _lib.DA_ERR_UNSUPPORTED)
