@@ -94,6 +94,22 @@ DA_API int da_route_fwd(const void* q, int64_t rows, int64_t q_cols, int64_t q_r
                         int normalize_input, int normalize_output, void* z, float* lse, float* out_norm,
                         int* argmax, int* work, int repair_cap, int* status, void* stream);
 
+/* No counterpart in the reference.  Same computation and arguments as
+ * da_route_fwd, for callers that cannot allocate device memory when they run
+ * the route (for example code running under CUDA stream capture, or engines
+ * that give a plugin only its inputs and outputs): the work area lives in a
+ * __device__ array inside this library, so no `work` buffer is passed and
+ * nothing is allocated.  At most 65536 route rows (groups * rows) per call,
+ * else DA_ERR_WORKSPACE.  Every GPU that loads the library holds the array
+ * (about 256 KiB) until exit; all calls on a device share it, so calls that
+ * can overlap on the GPU race.  The first call on each device looks the
+ * array's address up and should come before any stream capture. */
+DA_API int da_route_fwd_static(const void* q, int64_t rows, int64_t q_cols, int64_t q_row_stride, int groups,
+                               int64_t group_col_stride, int64_t R, int64_t M, int dtype, const void* dict_key_t,
+                               const void* dict_value, const float* beta, const float* dk_max, float eps,
+                               int normalize_input, int normalize_output, void* z, float* lse, float* out_norm,
+                               int* argmax, int* status, void* stream);
+
 /* ---- outer routed attention with the map mix, forward -------------------
  * Replaces routed_attention_triton / _routed_attention_triton_forward
  * (triton_kernels.py:2290-2305, :2022-2090; math of ops.py:65-93) together
