@@ -32,48 +32,71 @@
 namespace da {
 namespace attn {
 
-constexpr int kThreads = 192;   // warp0 TMA, warp1 MMA, warps2-5 softmax/epilogue
+constexpr int kThreads = 192;   // warp0 TMA (lane 0 keys, lane 1 values), warp1 MMA, warps2-5 softmax/epilogue
 constexpr int kRows = 64;       // query rows per CTA
-constexpr int kNK = 64;         // keys per tile
-constexpr int kMaxStages = 4;
+constexpr int kMaxK = 8, kMaxV = 4, kMaxSB = 4, kMaxPB = 2;
 
+// Tile plan.  The paired MMA reaches full rate only with N = 256 (its issue
+// cost is ~46 cycles regardless of N), so a single map scores 256 keys per
+// tile; mixed maps use 128-key tiles processed map by map through rotating
+// TMEM score buffers.  Keys and values stream as 64-wide chunks through
+// independent stage rings; everything is sized to fit 225 KB of shared
+// memory and 512 TMEM columns.
 struct Layout {
-  int kw;          // total Q/K width over maps and branches
-  int nqb;         // 64-column boxes per Q/K row block
-  int nc, npv;     // N of one P.V instruction, instructions per tile
-  int q_bytes, k_bytes, v_bytes;
-  int stages;
-  int nb;          // S (TMEM) and P (smem) buffers in flight
+  int kw, nk, kchunks, rpb;
+  int nc, npv, per;
+  int q_bytes, k_stage, v_stage, p_bytes;
+  int nks, nvs, nsb, npb;
   int off_q, off_k, off_v, off_p, off_red, smem;
-  int tmem_s, tmem_cols;
+  int tmem_s, s_cols, tmem_cols;
 };
 
-__host__ __device__ inline Layout make_layout(int maps, int group, int R, int D) {
+__host__ __device__ inline Layout make_layout(int maps, int group, int R, int D, bool mix) {
   Layout L;
   L.kw = maps * group * R;
-  L.nqb = L.kw / 64;
+  L.rpb = R / 64;
+  L.kchunks = group * L.rpb;
   L.nc = D < 256 ? D : 256;
   L.npv = D / L.nc;
+  L.per = (L.nc / 2) / 64;
   L.q_bytes = kRows * L.kw * 2;
-  L.k_bytes = (kNK / 2) * L.kw * 2;
-  L.v_bytes = (D / 2) * kNK * 2;
-  L.nb = (D / 2 + 4 * maps * 32) <= 512 ? 4 : 2;
-  auto stages_for = [&](int nb) {
-    const int fixed = L.q_bytes + nb * kRows * kNK * 2 + 128 * 8 * 4;
-    const int st = (225 * 1024 - fixed) / (L.k_bytes + L.v_bytes);
-    return st > kMaxStages ? kMaxStages : st;
-  };
-  if (L.nb == 4 && stages_for(4) < 2) L.nb = 2;
-  L.stages = stages_for(L.nb);
+  L.v_stage = 64 * D;  // 64 keys x D/2 columns (bf16) per CTA
+  const int red = 128 * 8 * 4;
+  const int avail = 225 * 1024;
+  L.nk = 0;
+  for (int nk = mix ? 128 : 256; nk >= 128 && L.nk == 0; nk -= 128) {
+    const int k_stage = (nk / 2) * 128, p_bytes = kRows * nk * 2;
+    const int rest = avail - L.q_bytes - 2 * p_bytes - 2 * L.v_stage - red;
+    if (rest >= 2 * k_stage) {
+      L.nk = nk;
+      L.k_stage = k_stage;
+      L.p_bytes = p_bytes;
+      L.npb = 2;
+      L.nvs = 2;
+      L.nks = rest / k_stage > kMaxK ? kMaxK : rest / k_stage;
+    }
+  }
+  if (L.nk == 0) {  // last resort: single-buffered probabilities
+    L.nk = 128;
+    L.k_stage = 64 * 128;
+    L.p_bytes = kRows * 128 * 2;
+    L.npb = 1;
+    L.nvs = 2;
+    const int rest = avail - L.q_bytes - L.p_bytes - 2 * L.v_stage - red;
+    L.nks = rest / L.k_stage > kMaxK ? kMaxK : rest / L.k_stage;
+  }
+  L.s_cols = L.nk / 2;
+  L.tmem_s = D / 2;
+  const int nsb = (512 - D / 2) / L.s_cols;
+  L.nsb = nsb > kMaxSB ? kMaxSB : nsb;
   L.off_q = 0;
   L.off_k = L.off_q + L.q_bytes;
-  L.off_v = L.off_k + L.stages * L.k_bytes;
-  L.off_p = L.off_v + L.stages * L.v_bytes;
-  L.off_red = L.off_p + L.nb * kRows * kNK * 2;
-  const int used = L.off_red + 128 * 8 * 4;
+  L.off_v = L.off_k + L.nks * L.k_stage;
+  L.off_p = L.off_v + L.nvs * L.v_stage;
+  L.off_red = L.off_p + L.npb * L.p_bytes;
+  const int used = L.off_red + red;
   L.smem = used < 120 * 1024 ? 120 * 1024 : used;  // one CTA per SM
-  L.tmem_s = D / 2;
-  const int cols = D / 2 + L.nb * maps * 32;
+  const int cols = D / 2 + L.nsb * L.s_cols;
   L.tmem_cols = cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : cols <= 256 ? 256 : 512;
   return L;
 }
@@ -101,39 +124,46 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ uint64_t q_full, o_full;
-  __shared__ uint64_t k_full[kMaxStages], k_empty[kMaxStages], v_full[kMaxStages], v_empty[kMaxStages];
-  __shared__ uint64_t s_full[4], p_full[4], p_empty[4];
+  __shared__ uint64_t k_full[kMaxK], k_empty[kMaxK], v_full[kMaxV], v_empty[kMaxV];
+  __shared__ uint64_t s_full[kMaxSB], p_full[kMaxSB], p_empty[kMaxPB];
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
 
-  const Layout L = make_layout(p.maps, p.group, p.R, p.D);
+  const Layout L = make_layout(p.maps, p.group, p.R, p.D, kMix);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const uint32_t rank = cluster_ctarank() & 1u;
   const int tiles = (p.T + 127) / 128;
   const int pair = blockIdx.x / 2;
   const int b = pair / tiles;
   const int t0 = (tiles - 1 - pair % tiles) * 128;  // heaviest (latest) query tiles first
-  const int nk_all = (p.T + kNK - 1) / kNK;
-  const int nj = p.causal ? min(nk_all, t0 / kNK + 2) : nk_all;
-  const int U = kMix ? 2 * nj : nj;       // key-tile visits (two sweeps when mixing maps)
-  const int rpb = p.R / 64;               // boxes per branch
+  const int nk = L.nk;
+  const int nk_all = (p.T + nk - 1) / nk;
+  const int nj = p.causal ? min(nk_all, (t0 + 127) / nk + 1) : nk_all;
+  const int maps = kMix ? p.maps : 1;
+  const int sweep_units = nj * maps;
+  const int U = kMix ? 2 * sweep_units : sweep_units;  // S units: (sweep, key tile, map)
+  const int u2 = kMix ? sweep_units : 0;               // first unit of the P.V sweep
   Abort ab{&abort_flag, p.status};
+  // post-mortem per-unit timeline of the first pair (debug trace only)
+  int* ft = (p.trace && blockIdx.x < 2) ? p.trace + blockIdx.x * 4096 : nullptr;
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
     mbar_init(&q_full, 1);
     mbar_init(&o_full, 1);
-    for (int s = 0; s < kMaxStages; ++s) {
-      mbar_init(&k_full[s], 1);
-      mbar_init(&k_empty[s], 1);
-      mbar_init(&v_full[s], 1);
-      mbar_init(&v_empty[s], 1);
+    for (int i = 0; i < kMaxK; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
     }
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < kMaxV; ++i) {
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
+    for (int i = 0; i < kMaxSB; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 2);
-      mbar_init(&p_empty[i], 1);
     }
+    for (int i = 0; i < kMaxPB; ++i) mbar_init(&p_empty[i], 1);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -148,123 +178,131 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producers (both CTAs)
-    // Lane 0 streams Q and the key tiles, lane 1 the value tiles: the two
-    // rings advance independently, so scores can run ahead of P.V products.
     if (lane == 0) {
       prefetch_tmap(&tq);
       prefetch_tmap(&tk);
       if (rank == 0) mbar_arrive_expect_tx(&q_full, 2 * L.q_bytes);
       const uint32_t qf = mapa_shared(smem_u32(&q_full), 0);
-      for (int s = 0; s < p.maps; ++s)
+      for (int s = 0; s < maps; ++s)
         for (int gi = 0; gi < p.group; ++gi) {
           const int64_t row = p.q_base + b * p.q_sb + (p.branch0[s] + gi) * p.q_sbr + t0 + 64 * (int)rank;
           const int y = (int)min(row, p.q_rows - 1);  // boxes never start outside the matrix
-          for (int kb = 0; kb < rpb; ++kb) {
-            const int qb = (s * p.group + gi) * rpb + kb;
-            tma_load_2d_pair(&tq, qf, smem + L.off_q + qb * (kRows * 128), kb * 64, y);
-          }
+          for (int kb = 0; kb < L.rpb; ++kb)
+            tma_load_2d_pair(&tq, qf, smem + L.off_q + ((s * p.group + gi) * L.rpb + kb) * (kRows * 128), kb * 64, y);
         }
-      int k_issued = 0;
+      int kc = 0;
       for (int u = 0; u < U; ++u) {
-        const int j = u % nj;
-        const int ks = u % L.stages;
-        if (!mbar_wait(&k_empty[ks], ((u / L.stages) & 1u) ^ 1u, ab, 11)) break;
-        if (rank == 0) mbar_arrive_expect_tx(&k_full[ks], 2 * L.k_bytes);
-        const uint32_t kf = mapa_shared(smem_u32(&k_full[ks]), 0);
-        for (int s = 0; s < p.maps; ++s)
-          for (int gi = 0; gi < p.group; ++gi) {
-            const int64_t row = p.k_base + b * p.k_sb + (p.branch0[s] + gi) * p.k_sbr + j * kNK + 32 * (int)rank;
-            const int y = (int)min(row, p.k_rows - 1);
-            for (int kb = 0; kb < rpb; ++kb) {
-              const int qb = (s * p.group + gi) * rpb + kb;
-              tma_load_2d_pair(&tk, kf, smem + L.off_k + ks * L.k_bytes + qb * ((kNK / 2) * 128), kb * 64, y);
-            }
-          }
-        k_issued = u + 1;
+        const int rem = u % sweep_units, j = rem / maps, s = rem % maps;
+        bool ok = true;
+        for (int c = 0; c < L.kchunks; ++c, ++kc) {
+          const int st = kc % L.nks;
+          if (!mbar_wait(&k_empty[st], ((kc / L.nks) & 1u) ^ 1u, ab, 11)) { ok = false; break; }
+          if (rank == 0) mbar_arrive_expect_tx(&k_full[st], 2 * L.k_stage);
+          const int gi = c / L.rpb, kb = c % L.rpb;
+          const int64_t row = p.k_base + b * p.k_sb + (p.branch0[s] + gi) * p.k_sbr + j * nk + (int)rank * (nk / 2);
+          tma_load_2d_pair(&tk, mapa_shared(smem_u32(&k_full[st]), 0), smem + L.off_k + st * L.k_stage, kb * 64,
+                           (int)min(row, p.k_rows - 1));
+        }
+        if (!ok) break;
       }
       if (rank == 0) {  // drain: no TMA may be in flight at teardown
         mbar_wait_drain(&q_full, 0);
-        for (int u = (k_issued > L.stages ? k_issued - L.stages : 0); u < k_issued; ++u)
-          mbar_wait_drain(&k_full[u % L.stages], (u / L.stages) & 1u);
+        for (int c = (kc > L.nks ? kc - L.nks : 0); c < kc; ++c)
+          mbar_wait_drain(&k_full[c % L.nks], (c / L.nks) & 1u);
       }
     } else if (lane == 1) {
       prefetch_tmap(&tv);
-      int v_issued = 0;
-      const int per = (L.nc / 2) / 64;  // 64-column boxes per CTA per instruction
+      int vc = 0;
+      const int64_t vrows = (int64_t)p.B * p.T;
       for (int v = 0; v < nj; ++v) {
-        const int vs = v % L.stages;
-        if (!mbar_wait(&v_empty[vs], ((v / L.stages) & 1u) ^ 1u, ab, 12)) break;
-        if (rank == 0) mbar_arrive_expect_tx(&v_full[vs], 2 * L.v_bytes);
-        const uint32_t vf = mapa_shared(smem_u32(&v_full[vs]), 0);
-        for (int i = 0; i < L.npv; ++i)
-          for (int bx = 0; bx < per; ++bx)
-            tma_load_2d_pair(&tv, vf, smem + L.off_v + vs * L.v_bytes + (i * per + bx) * (kNK * 128),
-                             i * L.nc + (int)rank * (L.nc / 2) + bx * 64, b * p.T + v * kNK);
-        v_issued = v + 1;
+        bool ok = true;
+        for (int c = 0; c < nk / 64; ++c, ++vc) {
+          const int st = vc % L.nvs;
+          if (!mbar_wait(&v_empty[st], ((vc / L.nvs) & 1u) ^ 1u, ab, 12)) { ok = false; break; }
+          if (rank == 0) mbar_arrive_expect_tx(&v_full[st], 2 * L.v_stage);
+          const uint32_t vf = mapa_shared(smem_u32(&v_full[st]), 0);
+          const int y = (int)min((int64_t)b * p.T + v * nk + c * 64, vrows - 1);
+          for (int i = 0; i < L.npv; ++i)
+            for (int bx = 0; bx < L.per; ++bx)
+              tma_load_2d_pair(&tv, vf, smem + L.off_v + st * L.v_stage + (i * L.per + bx) * (64 * 128),
+                               i * L.nc + (int)rank * (L.nc / 2) + bx * 64, y);
+        }
+        if (!ok) break;
       }
       if (rank == 0)
-        for (int v = (v_issued > L.stages ? v_issued - L.stages : 0); v < v_issued; ++v)
-          mbar_wait_drain(&v_full[v % L.stages], (v / L.stages) & 1u);
+        for (int c = (vc > L.nvs ? vc - L.nvs : 0); c < vc; ++c)
+          mbar_wait_drain(&v_full[c % L.nvs], (c / L.nvs) & 1u);
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer (leader)
     if (rank == 0 && lane == 0) {
-      const uint32_t idesc_s = idesc_f16(128, kNK, std::is_same<T, __nv_bfloat16>::value, false, false);
+      const uint32_t idesc_s = idesc_f16(128, nk, std::is_same<T, __nv_bfloat16>::value, false, false);
       const uint32_t idesc_o = idesc_f16(128, L.nc, true, false, true);  // B = V, MN-major
       auto commit_both = [&](uint64_t* bar) {
         mma_commit<2>(smem_u32(bar));
         mma_commit<2>(mapa_shared(smem_u32(bar), 1));
       };
+      const uint32_t qa = smem_u32(smem + L.off_q);
+      int kc = 0, vc = 0;
       auto issue_s = [&](int u) -> bool {
-        const int sb = u % L.nb, ks = u % L.stages;
-        if (u >= L.nb && !mbar_wait(&p_full[sb], ((u - L.nb) / L.nb) & 1u, ab, 22)) return false;
-        if (!mbar_wait(&k_full[ks], (u / L.stages) & 1u, ab, 23)) return false;
-        tc_fence_after();
-        const uint32_t qa = smem_u32(smem + L.off_q);
-        const uint32_t ka = smem_u32(smem + L.off_k + ks * L.k_bytes);
-        for (int s = 0; s < p.maps; ++s) {
-          const uint32_t d = tmem + L.tmem_s + (uint32_t)(sb * p.maps + s) * 32;
-          const int nk16 = p.group * p.R / 16;
-          for (int k = 0; k < nk16; ++k) {
-            const int qb = s * p.group * rpb + (k >> 2), kin = k & 3;
-            const uint64_t ad = sdesc_sw128(qa + qb * (kRows * 128) + kin * 32, 16, 1024);
-            const uint64_t bd = sdesc_sw128(ka + qb * ((kNK / 2) * 128) + kin * 32, 16, 1024);
-            mma_f16_ss<2>(d, ad, bd, idesc_s, k > 0 ? 1u : 0u);
-          }
+        const int sb = u % L.nsb;
+        const int s = (u % sweep_units) % maps;
+        if (u < 256) trace_at(ft, 1024 + 4 * u);
+        if (u >= L.nsb && !mbar_wait(&p_full[sb], ((u - L.nsb) / L.nsb) & 1u, ab, 22)) return false;
+        if (u < 256) trace_at(ft, 1025 + 4 * u);
+        const uint32_t d = tmem + L.tmem_s + (uint32_t)(sb * L.s_cols);
+        for (int c = 0; c < L.kchunks; ++c, ++kc) {
+          const int st = kc % L.nks;
+          if (!mbar_wait(&k_full[st], (kc / L.nks) & 1u, ab, 23)) return false;
+          tc_fence_after();
+          const uint64_t ad0 = sdesc_sw128(qa + (s * L.kchunks + c) * (kRows * 128), 16, 1024);
+          const uint64_t bd0 = sdesc_sw128(smem_u32(smem + L.off_k + st * L.k_stage), 16, 1024);
+#pragma unroll
+          for (int kin = 0; kin < 4; ++kin)  // +32 B per K step of 16 = +2 in the encoded address
+            mma_f16_ss<2>(d, ad0 + 2 * kin, bd0 + 2 * kin, idesc_s, (c | kin) ? 1u : 0u);
+          commit_both(&k_empty[st]);
         }
         commit_both(&s_full[sb]);
-        commit_both(&k_empty[ks]);
+        if (u < 256) trace_at(ft, 1026 + 4 * u);
         return true;
       };
       auto issue_pv = [&](int v) -> bool {
-        const int u = kMix ? v + nj : v;
-        const int pb = v % L.nb, vs = v % L.stages;
-        if (!mbar_wait(&p_full[u % L.nb], (u / L.nb) & 1u, ab, 24)) return false;
-        if (!mbar_wait(&v_full[vs], (v / L.stages) & 1u, ab, 25)) return false;
-        tc_fence_after();
-        const uint32_t pa = smem_u32(smem + L.off_p + pb * (kRows * kNK * 2));
-        const uint32_t va = smem_u32(smem + L.off_v + vs * L.v_bytes);
-        const int per = (L.nc / 2) / 64;
-        for (int i = 0; i < L.npv; ++i) {
-          for (int kk = 0; kk < kNK / 16; ++kk) {
-            const uint64_t ad = sdesc_sw128(pa + kk * 32, 16, 1024);
+        const int ulast = u2 + v * maps + maps - 1;
+        const int pb = v % L.npb;
+        if (v < 256) trace_at(ft, 2048 + 4 * v);
+        if (!mbar_wait(&p_full[ulast % L.nsb], (ulast / L.nsb) & 1u, ab, 24)) return false;
+        if (v < 256) trace_at(ft, 2049 + 4 * v);
+        const uint32_t pa = smem_u32(smem + L.off_p + pb * L.p_bytes);
+        for (int c = 0; c < nk / 64; ++c, ++vc) {
+          const int st = vc % L.nvs;
+          if (!mbar_wait(&v_full[st], (vc / L.nvs) & 1u, ab, 25)) return false;
+          tc_fence_after();
+          const uint32_t va = smem_u32(smem + L.off_v + st * L.v_stage);
+          for (int i = 0; i < L.npv; ++i) {
             // MN-major V: rows are keys (K), 128 B = 64 value columns (N);
             // LBO = distance between 64-column boxes, SBO = 8 key rows.
-            const uint64_t bd = sdesc_sw128(va + i * per * (kNK * 128) + kk * 16 * 128, kNK * 128, 1024);
-            mma_f16_ss<2>(tmem + (uint32_t)(i * (L.nc / 2)), ad, bd, idesc_o, (v > 0 || kk > 0) ? 1u : 0u);
+            const uint64_t bd0 = sdesc_sw128(va + i * L.per * (64 * 128), 64 * 128, 1024);
+            const uint64_t ad0 = sdesc_sw128(pa + c * (kRows * 128), 16, 1024);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)  // K step of 16 keys: A +32 B (+2), B +16 rows x 128 B (+128)
+              mma_f16_ss<2>(tmem + (uint32_t)(i * (L.nc / 2)), ad0 + 2 * kk, bd0 + 128 * kk, idesc_o,
+                            (v | c | kk) ? 1u : 0u);
           }
+          commit_both(&v_empty[st]);
         }
         commit_both(&p_empty[pb]);
-        commit_both(&v_empty[vs]);
+        if (v < 256) trace_at(ft, 2050 + 4 * v);
         return true;
       };
+      trace_at(ft, 0);
       bool ok = mbar_wait(&q_full, 0, ab, 21);
+      trace_at(ft, 1);
       tc_fence_after();
-      // Scores run up to nb tiles ahead of the probability products.
+      // Scores run up to nsb units ahead of the probability products.
       int next_u = 0;
       for (int v = 0; ok && v < nj; ++v) {
-        const int uv = kMix ? v + nj : v;
-        while (ok && next_u < U && next_u < uv + L.nb) ok = issue_s(next_u++);
+        const int ulast = u2 + v * maps + maps - 1;
+        while (ok && next_u < U && next_u < ulast + L.nsb) ok = issue_s(next_u++);
         if (ok) ok = issue_pv(v);
       }
       commit_both(&o_full);
@@ -281,6 +319,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     const uint32_t pf_leader = mapa_shared(smem_u32(&p_full[0]), 0);
     const bool arriver = (warp == 2 && lane == 0);
     const float kLog2e = 1.4426950408889634f;
+    const int hc = nk / 2;  // key columns per thread per tile
 
     bool ok = mbar_wait(&s_full[0], 0, ab, 31);
     float scale2[kMaxMaps], bound2[kMaxMaps], off2[kMaxMaps], sum[kMaxMaps], mx[kMaxMaps];
@@ -289,11 +328,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     for (int s = 0; s < kMaxMaps; ++s) {
       scale2[s] = bound2[s] = off2[s] = sum[s] = 0.f;
       mx[s] = -INFINITY;
-      if (s < p.maps) {
+      if (s < maps) {
         float qn2 = 0.f;
         if (ok) {
           const uint32_t qa = smem_u32(smem + L.off_q);
-          for (int qb = s * p.group * rpb; qb < (s + 1) * p.group * rpb; ++qb)
+          for (int qb = s * L.kchunks; qb < (s + 1) * L.kchunks; ++qb)
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
               const uint4 w = ld_shared_v4(qa + qb * (kRows * 128) + sw128_offset(r, c));
@@ -312,49 +351,51 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       }
     }
 
-    // Valid keys of key tile j for this thread: 32 columns starting at
-    // j*64 + 32*half; index i is valid iff i < lim.
-    auto key_limit = [&](int j) -> int {
-      const int k0 = j * kNK + 32 * half;
+    // Number of valid keys among the 32 columns starting at key k0.
+    auto key_limit = [&](int k0) -> int {
       int lim = p.T - k0;
       if (p.causal) lim = min(lim, t - k0 + 1);
       return max(0, min(32, lim));
     };
+    auto finish_unit = [&](int u, bool wrote_p) {
+      if (wrote_p) fence_proxy_async();
+      tc_fence_before();
+      if (arriver && u < 256) trace_at(ft, 3074 + 4 * u);
+      named_bar_sync(1, 128);
+      if (arriver) mbar_arrive_cluster(pf_leader + (u % L.nsb) * 8);
+      if (arriver && u < 256) trace_at(ft, 3075 + 4 * u);
+    };
 
     // ---- sweep 1 (several maps): exact per-map log-sum-exp
     if (kMix) {
-      for (int u = 0; u < nj; ++u) {
-        const int sb = u % L.nb;
-        if (ok && u > 0) ok = mbar_wait(&s_full[sb], (u / L.nb) & 1u, ab, 32);
+      for (int u = 0; u < sweep_units; ++u) {
+        const int j = u / maps, s = u % maps, sb = u % L.nsb;
+        if (ok && u > 0) ok = mbar_wait(&s_full[sb], (u / L.nsb) & 1u, ab, 32);
         ok = __all_sync(0xffffffffu, ok);
         if (ok) {
           tc_fence_after();
-          const int lim = key_limit(u);
-          for (int s = 0; s < p.maps; ++s) {
+          for (int ch = 0; ch < hc / 32; ++ch) {
             float v[32];
-            tmem_ld32(tmem + lane_base + L.tmem_s + (uint32_t)(sb * p.maps + s) * 32, v);
+            tmem_ld32(tmem + lane_base + L.tmem_s + (uint32_t)(sb * L.s_cols + ch * 32), v);
             tmem_wait_ld();
+            const int lim = key_limit(j * nk + half * hc + ch * 32);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
+            for (int i = 0; i < 32; ++i)
               if (i < lim) {
                 const float a = v[i] * scale2[s];
                 mx[s] = fmaxf(mx[s], a);
                 sum[s] += ex2(a - bound2[s]);
               }
-            }
           }
         }
-        tc_fence_before();
-        named_bar_sync(1, 128);
-        if (arriver) mbar_arrive_cluster(pf_leader + sb * 8);
+        finish_unit(u, false);
       }
-      // combine the two column halves of every row
-      for (int s = 0; s < p.maps; ++s) {
+      for (int s = 0; s < maps; ++s) {
         red[s * 128 + l] = sum[s];
         red[(4 + s) * 128 + l] = mx[s];
       }
       named_bar_sync(1, 128);
-      for (int s = 0; s < p.maps; ++s) {
+      for (int s = 0; s < maps; ++s) {
         sum[s] += red[s * 128 + (l ^ 64)];
         mx[s] = fmaxf(mx[s], red[(4 + s) * 128 + (l ^ 64)]);
         const float alpha = p.weights ? p.weights[s] : 1.f;
@@ -367,50 +408,77 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
 
     // ---- probability tiles for P.V
     float psum = 0.f, pmx = -INFINITY;
+    float pm[kMix ? 64 : 1];
     for (int v = 0; v < nj; ++v) {
-      const int u = kMix ? v + nj : v;
-      const int sb = u % L.nb, pb = v % L.nb;
-      if (ok && u > 0) ok = mbar_wait(&s_full[sb], (u / L.nb) & 1u, ab, 32);
-      if (ok && v >= L.nb) ok = mbar_wait(&p_empty[pb], ((v - L.nb) / L.nb) & 1u, ab, 33);
-      ok = __all_sync(0xffffffffu, ok);
-      if (ok) {
-        tc_fence_after();
-        const int lim = key_limit(v);
-        float pm[32];
+      const int pb = v % L.npb;
+      const uint32_t pa = smem_u32(smem + L.off_p + pb * L.p_bytes);
+      for (int s = 0; s < maps; ++s) {
+        const int u = u2 + v * maps + s, sb = u % L.nsb;
+        if (arriver && u < 256) trace_at(ft, 3072 + 4 * u);
+        if (ok && u > 0) ok = mbar_wait(&s_full[sb], (u / L.nsb) & 1u, ab, 32);
+        if (arriver && u < 256) trace_at(ft, 3073 + 4 * u);
+        if (ok && s == 0 && v >= L.npb) ok = mbar_wait(&p_empty[pb], ((v - L.npb) / L.npb) & 1u, ab, 33);
+        ok = __all_sync(0xffffffffu, ok);
+        if (ok) {
+          tc_fence_after();
+          for (int ch = 0; ch < hc / 32; ++ch) {
+            float sv[32];
+            tmem_ld32(tmem + lane_base + L.tmem_s + (uint32_t)(sb * L.s_cols + ch * 32), sv);
+            tmem_wait_ld();
+            const int k0 = v * nk + half * hc + ch * 32;
+            const int lim = key_limit(k0);
+            if constexpr (kMix) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) pm[i] = 0.f;
-        for (int s = 0; s < p.maps; ++s) {
-          float sv[32];
-          tmem_ld32(tmem + lane_base + L.tmem_s + (uint32_t)(sb * p.maps + s) * 32, sv);
-          tmem_wait_ld();
-          if (kMix) {
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (i < lim) pm[i] += ex2(sv[i] * scale2[s] - off2[s]);
-          } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (i < lim) {
-                const float a = sv[i] * scale2[0];
-                pmx = fmaxf(pmx, a);
-                pm[i] = ex2(a - bound2[0]);
-                psum += pm[i];
+              for (int i = 0; i < 32; ++i) {
+                const float e = i < lim ? ex2(sv[i] * scale2[s] - off2[s]) : 0.f;
+                pm[ch * 32 + i] = s == 0 ? e : pm[ch * 32 + i] + e;
               }
+            } else {
+              uint32_t packed[16];
+#pragma unroll
+              for (int i = 0; i < 32; i += 2) {
+                float e0 = 0.f, e1 = 0.f;
+                if (i < lim) {
+                  const float a = sv[i] * scale2[0];
+                  pmx = fmaxf(pmx, a);
+                  e0 = ex2(a - bound2[0]);
+                }
+                if (i + 1 < lim) {
+                  const float a = sv[i + 1] * scale2[0];
+                  pmx = fmaxf(pmx, a);
+                  e1 = ex2(a - bound2[0]);
+                }
+                psum += e0 + e1;
+                packed[i / 2] = pack_bf16x2(e0, e1);
+              }
+              const int kc = half * hc + ch * 32;  // key column inside the tile
+              const uint32_t box = pa + (kc >> 6) * (kRows * 128);
+              const int cb = (kc & 63) >> 3;
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                st_shared_v4(box + sw128_offset(r, cb + e), packed[4 * e], packed[4 * e + 1], packed[4 * e + 2],
+                             packed[4 * e + 3]);
+            }
+          }
+          if constexpr (kMix) {
+            if (s == maps - 1) {
+              for (int ch = 0; ch < hc / 32; ++ch) {
+                const int kc = half * hc + ch * 32;
+                const uint32_t box = pa + (kc >> 6) * (kRows * 128);
+                const int cb = (kc & 63) >> 3;
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                  st_shared_v4(box + sw128_offset(r, cb + e),
+                               pack_bf16x2(pm[ch * 32 + 8 * e], pm[ch * 32 + 8 * e + 1]),
+                               pack_bf16x2(pm[ch * 32 + 8 * e + 2], pm[ch * 32 + 8 * e + 3]),
+                               pack_bf16x2(pm[ch * 32 + 8 * e + 4], pm[ch * 32 + 8 * e + 5]),
+                               pack_bf16x2(pm[ch * 32 + 8 * e + 6], pm[ch * 32 + 8 * e + 7]));
+              }
+            }
           }
         }
-        uint32_t packed[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) packed[i] = pack_bf16x2(pm[2 * i], pm[2 * i + 1]);
-        const uint32_t pa = smem_u32(smem + L.off_p + pb * (kRows * kNK * 2));
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-          st_shared_v4(pa + sw128_offset(r, half * 4 + c), packed[4 * c], packed[4 * c + 1], packed[4 * c + 2],
-                       packed[4 * c + 3]);
-        fence_proxy_async();
+        finish_unit(u, !kMix || s == maps - 1);
       }
-      tc_fence_before();
-      named_bar_sync(1, 128);
-      if (arriver) mbar_arrive_cluster(pf_leader + sb * 8);
     }
 
     // ---- epilogue
@@ -450,7 +518,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       }
       if (live && half == 0) {
         const float kLn2 = 0.6931471805599453f;
-        for (int s = 0; s < p.maps; ++s) {
+        for (int s = 0; s < maps; ++s) {
           p.lse[((size_t)b * p.maps + s) * p.T + t] = bound2[s] * kLn2;
           // the largest term of a row must stay far above the fp32 range floor
           const float top = kMix ? mx[s] - (bound2[s] - log2f(sum[s])) : mx[0] - (bound2[0] - log2f(psum));
@@ -468,16 +536,16 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
 
 template <typename T, bool kMix>
 int launch(const AttnFwdArgs& a, cudaStream_t st) {
-  const Layout L = make_layout(a.maps, a.group, a.R, a.D);
+  const Layout L = make_layout(a.maps, a.group, a.R, a.D, kMix);
   const CUtensorMapDataType qdt =
       std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap tq, tk, tv;
   int rc = make_tmap_2d(&tq, a.q.ptr, qdt, 2, a.R, a.q.rows, (uint64_t)a.R * 2, 64, kRows);
   if (rc) return rc;
-  rc = make_tmap_2d(&tk, a.k.ptr, qdt, 2, a.R, a.k.rows, (uint64_t)a.R * 2, 64, kNK / 2);
+  rc = make_tmap_2d(&tk, a.k.ptr, qdt, 2, a.R, a.k.rows, (uint64_t)a.R * 2, 64, L.nk / 2);
   if (rc) return rc;
   rc = make_tmap_2d(&tv, a.v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.D, (uint64_t)a.B * a.T, (uint64_t)a.D * 2, 64,
-                    kNK);
+                    64);
   if (rc) return rc;
   FwdParams p;
   p.q_rows = a.q.rows;
@@ -549,7 +617,10 @@ extern "C" int da_attn_fwd(const void* q, int64_t q_rows, int64_t q_base, int64_
   if (maps * group * R > 512) return DA_ERR_UNSUPPORTED;  // Q/K width per pair of rows
   if (D != 128 && D != 256 && D != 512) return DA_ERR_UNSUPPORTED;
   if (maps > 1 && !weights) return DA_ERR_NULL;
-  if ((2 * maps * 32 + D / 2) > 512) return DA_ERR_UNSUPPORTED;
+  {
+    const attn::Layout L = attn::make_layout(maps, group, R, D, maps > 1);
+    if (L.nks < 2 || L.nsb < 2) return DA_ERR_UNSUPPORTED;  // tile plan does not fit
+  }
   if ((reinterpret_cast<uintptr_t>(y) & 15) || (reinterpret_cast<uintptr_t>(v) & 15)) return DA_ERR_ALIGN;
   attn::AttnFwdArgs a;
   a.q = {q, q_rows, q_base, q_sb, q_sbr};
