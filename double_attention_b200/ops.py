@@ -379,6 +379,54 @@ def _attention_forward(q: RowMap, k: RowMap, v: Tensor, batch: int, length: int,
     return y, lse
 
 
+def _attention_bwd_supported(r: int, d: int, group: int) -> None:
+    if d not in (256, 512) or group * r not in (128, 256, 512):
+        raise NotImplementedError(
+            "outer attention backward kernels support value widths 256/512 and group*R in 128/256/512 "
+            f"(got D={d}, group={group}, R={r})"
+        )
+
+
+def _attention_delta(dy: Tensor, y: Tensor) -> Tensor:
+    """delta[b*T + t] = <dY, Y> per row (fp32), Y the output of one map alone."""
+    rows, d = dy.numel() // dy.shape[-1], dy.shape[-1]
+    delta = torch.empty(rows, dtype=torch.float32, device=dy.device)
+    call("da_attn_bwd_delta", dy.data_ptr(), y.data_ptr(), rows, d, dtype_code(dy.dtype), delta.data_ptr(),
+         stream_ptr(dy.device))
+    return delta
+
+
+def _attention_forward_delta(q: RowMap, k: RowMap, v: Tensor, dy: Tensor, batch: int, length: int, r: int,
+                             group: int, branch0: int, causal: bool, scale: Tensor,
+                             key_norm_bound: float) -> tuple[Tensor, Tensor]:
+    """One map's log-sum-exp [B, T] and delta = <dY, Y_map> [B*T] (Y_map in fp32), no output rows."""
+    d = v.shape[-1]
+    dev = v.device
+    lse = torch.empty(batch, length, dtype=torch.float32, device=dev)
+    delta = torch.empty(batch * length, dtype=torch.float32, device=dev)
+    ws = workspace(dev)
+    call("da_attn_fwd_delta", q.tensor.data_ptr(), q.rows, q.base, q.sb, q.sbr, k.tensor.data_ptr(), k.rows, k.base,
+         k.sb, k.sbr, v.data_ptr(), dy.data_ptr(), batch, length, r, d, group, branch0, int(causal),
+         dtype_code(q.tensor.dtype), scale.data_ptr(), None, float(key_norm_bound), lse.data_ptr(), delta.data_ptr(),
+         ws.status.data_ptr(), stream_ptr(dev))
+    return lse, delta
+
+
+def _attention_backward_map(q: RowMap, k: RowMap, v: Tensor, dy: Tensor, batch: int, length: int, r: int,
+                            group: int, branch0: int, causal: bool, scale: Tensor, weight: Tensor | None,
+                            lse: Tensor, delta: Tensor, dq: Tensor | None, dk: Tensor | None, dv: Tensor | None,
+                            dscale: Tensor | None) -> None:
+    """Accumulate one map's gradients into fp32 dq / dk (at the Q / K rows), dv and dscale."""
+    d = v.shape[-1]
+    _attention_bwd_supported(r, d, group)
+    dev = v.device
+    ws = workspace(dev)
+    call("da_attn_bwd", q.tensor.data_ptr(), q.rows, q.base, q.sb, q.sbr, k.tensor.data_ptr(), k.rows, k.base, k.sb,
+         k.sbr, v.data_ptr(), dy.data_ptr(), batch, length, r, d, group, branch0, int(causal),
+         dtype_code(q.tensor.dtype), scale.data_ptr(), ptr(weight), lse.data_ptr(), delta.data_ptr(), ptr(dq),
+         ptr(dk), ptr(dv), ptr(dscale), ws.status.data_ptr(), stream_ptr(dev))
+
+
 def ctypes_int_array(n: int):
     import ctypes
 
@@ -419,7 +467,40 @@ class _MixedAttention(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, dy: Tensor):  # type: ignore[override]
-        raise NotImplementedError("outer attention backward kernel is not available in this build")
+        routed, value, scales, weights, y, lse = ctx.saved_tensors
+        maps, causal, key_norm_bound, has_weights = ctx.meta
+        _two, h, batch, length, r = routed.shape
+        dtype, d = routed.dtype, value.shape[-1]
+        flat = routed.view(-1, r)
+        group, branch0 = _map_layout(h, maps)
+        qmap = RowMap(flat, 0, length, batch * length)
+        kmap = RowMap(flat, h * batch * length, length, batch * length)
+        v16 = value.detach().to(dtype).contiguous()
+        dy16 = dy.to(dtype).contiguous()
+        need = ctx.needs_input_grad
+        droute = torch.zeros(flat.shape, dtype=torch.float32, device=flat.device) if need[0] else None
+        dv = torch.zeros(batch * length, d, dtype=torch.float32, device=flat.device) if need[1] else None
+        dscale = torch.zeros(maps, dtype=torch.float32, device=flat.device)
+        sc = scales.detach().float().contiguous()
+        wt = weights.detach().float().contiguous() if has_weights and maps > 1 else None
+        dweight = torch.zeros(maps, dtype=torch.float32, device=flat.device) if wt is not None else None
+        v_fwd = value.detach().to(torch.bfloat16).contiguous() if maps > 1 else None
+        for s in range(maps):
+            if maps == 1:
+                lse_s, delta = lse[:, 0].contiguous(), _attention_delta(dy16, y)
+            else:  # delta needs the map's own output: recomputed in fp32, never stored
+                lse_s, delta = _attention_forward_delta(qmap, kmap, v_fwd, dy16, batch, length, r, group,
+                                                        branch0[s], causal, sc[s:s + 1], key_norm_bound)
+            if dweight is not None:
+                dweight[s] = delta.sum()
+            _attention_backward_map(qmap, kmap, v16, dy16, batch, length, r, group, branch0[s], causal,
+                                    sc[s:s + 1], None if wt is None else wt[s:s + 1], lse_s, delta, droute, droute,
+                                    dv, dscale[s:s + 1] if need[2] else None)
+        g_routed = droute.view(routed.shape).to(dtype) if droute is not None else None
+        g_value = dv.view(value.shape).to(value.dtype) if dv is not None else None
+        g_scales = dscale.to(scales.dtype) if need[2] else None
+        g_weights = dweight.to(weights.dtype) if (dweight is not None and need[3]) else None
+        return g_routed, g_value, g_scales, g_weights, None, None, None
 
 
 def routed_attention_mixed(routed: Tensor, value: Tensor, scales: Tensor, map_weights: Tensor | None, cfg) -> Tensor:
@@ -446,13 +527,35 @@ class _SingleMapAttention(torch.autograd.Function):
         group, branch0 = _map_layout(h, maps)
         qmap = RowMap(flat, 0, length, batch * length)
         kmap = RowMap(flat, h * batch * length, length, batch * length)
-        y, _ = _attention_forward(qmap, kmap, value, batch, length, r, 1, group, [branch0[s]], causal,
-                                  scales[s:s + 1], None, None, 1.0, routed.dtype)
+        y, lse = _attention_forward(qmap, kmap, value, batch, length, r, 1, group, [branch0[s]], causal,
+                                    scales[s:s + 1], None, None, 1.0, routed.dtype)
+        ctx.save_for_backward(routed, value, scales, y, lse)
+        ctx.meta = (s, maps, causal)
         return y
 
     @staticmethod
     def backward(ctx, dy: Tensor):  # type: ignore[override]
-        raise NotImplementedError("outer attention backward kernel is not available in this build")
+        routed, value, scales, y, lse = ctx.saved_tensors
+        s, maps, causal = ctx.meta
+        _two, h, batch, length, r = routed.shape
+        dtype, d = routed.dtype, value.shape[-1]
+        flat = routed.view(-1, r)
+        group, branch0 = _map_layout(h, maps)
+        qmap = RowMap(flat, 0, length, batch * length)
+        kmap = RowMap(flat, h * batch * length, length, batch * length)
+        v16 = value.detach().to(dtype).contiguous()
+        dy16 = dy.to(dtype).contiguous()
+        need = ctx.needs_input_grad
+        droute = torch.zeros(flat.shape, dtype=torch.float32, device=flat.device) if need[0] else None
+        dv = torch.zeros(batch * length, d, dtype=torch.float32, device=flat.device) if need[1] else None
+        dscale = torch.zeros(scales.shape[0], dtype=torch.float32, device=flat.device)
+        delta = _attention_delta(dy16, y)
+        _attention_backward_map(qmap, kmap, v16, dy16, batch, length, r, group, branch0[s], causal,
+                                scales.detach().float()[s:s + 1].contiguous(), None, lse[:, 0].contiguous(), delta,
+                                droute, droute, dv, dscale[s:s + 1] if need[2] else None)
+        return (droute.view(routed.shape).to(dtype) if droute is not None else None,
+                dv.view(value.shape).to(value.dtype) if dv is not None else None,
+                dscale.to(scales.dtype) if need[2] else None, None, None, None)
 
 
 class _PerMapAttention(torch.autograd.Function):
@@ -464,18 +567,43 @@ class _PerMapAttention(torch.autograd.Function):
         qf = query.contiguous().view(-1, r)
         kf = key.contiguous().view(-1, r)
         kmax = key.detach().float().norm(dim=-1).amax(dim=-1).contiguous()  # [B, S] score bound
-        outs = []
+        outs, lses = [], []
+        qmap = RowMap(qf, 0, maps * length, length)
+        kmap = RowMap(kf, 0, maps * length, length)
         for s in range(maps):
-            qmap = RowMap(qf, 0, maps * length, length)
-            kmap = RowMap(kf, 0, maps * length, length)
-            y, _ = _attention_forward(qmap, kmap, value, batch, length, r, 1, 1, [s], causal, scales[s:s + 1], None,
-                                      kmax[:, s].contiguous(), 1.0, query.dtype)
+            y, lse = _attention_forward(qmap, kmap, value, batch, length, r, 1, 1, [s], causal, scales[s:s + 1],
+                                        None, kmax[:, s].contiguous(), 1.0, query.dtype)
             outs.append(y)
-        return torch.stack(outs, dim=1)
+            lses.append(lse[:, 0])
+        out = torch.stack(outs, dim=1)
+        ctx.save_for_backward(qf, kf, value, scales, out, torch.stack(lses, dim=0))
+        ctx.meta = (batch, maps, length, r, causal)
+        return out
 
     @staticmethod
     def backward(ctx, dy: Tensor):  # type: ignore[override]
-        raise NotImplementedError("outer attention backward kernel is not available in this build")
+        qf, kf, value, scales, out, lses = ctx.saved_tensors
+        batch, maps, length, r, causal = ctx.meta
+        dtype, d = qf.dtype, value.shape[-1]
+        qmap = RowMap(qf, 0, maps * length, length)
+        kmap = RowMap(kf, 0, maps * length, length)
+        v16 = value.detach().to(dtype).contiguous()
+        need = ctx.needs_input_grad
+        dq = torch.zeros(qf.shape, dtype=torch.float32, device=qf.device) if need[0] else None
+        dk = torch.zeros(kf.shape, dtype=torch.float32, device=qf.device) if need[1] else None
+        dv = torch.zeros(batch * length, d, dtype=torch.float32, device=qf.device) if need[2] else None
+        dscale = torch.zeros(maps, dtype=torch.float32, device=qf.device)
+        sc = scales.detach().float().contiguous()
+        for s in range(maps):
+            dy_s = dy[:, s].to(dtype).contiguous()
+            delta = _attention_delta(dy_s, out[:, s].contiguous())
+            _attention_backward_map(qmap, kmap, v16, dy_s, batch, length, r, 1, s, causal, sc[s:s + 1], None,
+                                    lses[s].contiguous(), delta, dq, dk, dv, dscale[s:s + 1] if need[3] else None)
+        shape = (batch, maps, length, r)
+        return (dq.view(shape).to(dtype) if dq is not None else None,
+                dk.view(shape).to(dtype) if dk is not None else None,
+                dv.view(value.shape).to(value.dtype) if dv is not None else None,
+                dscale.to(scales.dtype) if need[3] else None, None)
 
 
 def routed_attention(query: Tensor, key: Tensor, value: Tensor, scales: Tensor, causal: bool = True) -> Tensor:
