@@ -51,6 +51,7 @@ struct Params {
   float* dv;                // fp32 [B*T, D] (accumulated), or null
   float* dscale;            // fp32 scalar (accumulated d gamma_s), or null
   int* status;
+  int do_dv, do_dk;         // key-parallel kernel: which of dV / dK this launch accumulates
 };
 
 // Shared plumbing of both kernels.
@@ -307,7 +308,10 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
     const float scale2 = gamma * kLog2e;
     const float lse2 = live ? p.lse[(int64_t)b * p.T + t] * kLog2e : 0.f;
     const float delta = live ? p.delta[(int64_t)b * p.T + t] : 0.f;
-    float dg = 0.f;
+    // d gamma from this row's own sums: with A = sum P dP S, B = sum P S,
+    // C = sum P dP (the exact delta), sum_k dS_k S_k = alpha (A - C B); this
+    // does not inherit the rounding of the delta taken from the stored output.
+    float sA = 0.f, sB = 0.f, sC = 0.f;
     bool ok = true;
     for (int j = 0; j < nj; ++j) {
       const int sb = j & 1;
@@ -333,12 +337,18 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
             if (i < lim) {
               const float pr = ex2(sv[i] * scale2 - lse2);
               d0 = alpha * pr * (pv[i] - delta);
-              dg = fmaf(d0, sv[i], dg);
+              const float pp = pr * pv[i];
+              sA = fmaf(pp, sv[i], sA);
+              sB = fmaf(pr, sv[i], sB);
+              sC += pp;
             }
             if (i + 1 < lim) {
               const float pr = ex2(sv[i + 1] * scale2 - lse2);
               d1 = alpha * pr * (pv[i + 1] - delta);
-              dg = fmaf(d1, sv[i + 1], dg);
+              const float pp = pr * pv[i + 1];
+              sA = fmaf(pp, sv[i + 1], sA);
+              sB = fmaf(pr, sv[i + 1], sB);
+              sC += pp;
             }
             packed[i / 2] = pack2<T>(d0, d1);
           }
@@ -353,6 +363,18 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
       tc_fence_before();
       named_bar_sync(1, 128);
       if (arriver) mbar_arrive_cluster(pf_leader + sb * 8);
+    }
+    if (p.dscale) {  // combine the two halves of each row (every softmax thread takes part)
+      float* red = reinterpret_cast<float*>(smem + L.off_red);
+      red[l] = sA;
+      red[128 + l] = sB;
+      red[256 + l] = sC;
+      named_bar_sync(1, 128);
+      float dg = 0.f;
+      if (half == 0 && live && ok)
+        dg = alpha * ((sA + red[l ^ 64]) - (sC + red[256 + (l ^ 64)]) * (sB + red[128 + (l ^ 64)]));
+      for (int o = 16; o; o >>= 1) dg += __shfl_xor_sync(0xffffffffu, dg, o);
+      if (lane == 0 && dg != 0.f) atomicAdd(p.dscale, dg * gsc);
     }
     if (ok) ok = mbar_wait(&o_full, 0, ab, 34);
     ok = __all_sync(0xffffffffu, ok);
@@ -379,10 +401,6 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
             }
           }
         }
-      if (p.dscale) {
-        for (int o = 16; o; o >>= 1) dg += __shfl_xor_sync(0xffffffffu, dg, o);
-        if (lane == 0) atomicAdd(p.dscale, dg * gsc);
-      }
     }
   }
   tc_fence_before();
@@ -398,7 +416,10 @@ struct KvLayout {
   int tmem_dv, tmem_dk, tmem_s, tmem_p, tmem_cols;
 };
 
-__host__ __device__ inline KvLayout kv_layout(int group, int R, int D) {
+// dV and dK accumulate side by side in TMEM when they fit (D/2 + group*R/2
+// columns next to S^T and dP^T); otherwise the host runs a dV launch and a dK
+// launch, each holding one accumulator.
+__host__ __device__ inline KvLayout kv_layout(int group, int R, int D, bool do_dv, bool do_dk) {
   KvLayout L;
   L.kw = group * R;
   L.rpb = R / 64;
@@ -417,11 +438,11 @@ __host__ __device__ inline KvLayout kv_layout(int group, int R, int D) {
   L.nst = avail / kStage > kMaxStages ? kMaxStages : avail / kStage;
   L.smem = L.off_ring + L.nst * kStage;
   L.tmem_dv = 0;
-  L.tmem_dk = D / 2;
-  L.tmem_s = L.tmem_dk + L.kw / 2;
+  L.tmem_dk = do_dv ? D / 2 : 0;
+  L.tmem_s = L.tmem_dk + (do_dk ? L.kw / 2 : 0);
   L.tmem_p = L.tmem_s + kTile / 2;
-  const int cols = L.tmem_p + kTile / 2;
-  L.tmem_cols = cols <= 256 ? 256 : 512;
+  const int cols = L.tmem_p + (do_dk ? kTile / 2 : 0);
+  L.tmem_cols = cols <= 256 ? 256 : (cols <= 512 ? 512 : 1024);  // 1024: does not fit
   return L;
 }
 
@@ -437,7 +458,8 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
 
-  const KvLayout L = kv_layout(p.group, p.R, p.D);
+  const bool do_dv = p.do_dv != 0, do_dk = p.do_dk != 0;
+  const KvLayout L = kv_layout(p.group, p.R, p.D, do_dv, do_dk);
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const uint32_t rank = cluster_ctarank() & 1u;
@@ -481,7 +503,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
     prefetch_tmap(&tv);
     prefetch_tmap(&tdy);
     const uint32_t inf = mapa_shared(smem_u32(&in_full), 0);
-    if (rank == 0) mbar_arrive_expect_tx(&in_full, 2 * (kRows * L.kw * 2 + kRows * p.D * 2));
+    if (rank == 0) mbar_arrive_expect_tx(&in_full, 2 * (kRows * L.kw * 2 + (do_dk ? kRows * p.D * 2 : 0)));
     const int krow = k0 + 64 * (int)rank;
     for (int cb = 0; cb < L.kw / 64; ++cb) {
       const int gi = cb / L.rpb, x = (cb % L.rpb) * 64;
@@ -489,7 +511,9 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
       tma_load_2d_pair(&tk, inf, smem + L.off_k + cb * (kRows * 128), x, (int)min(row, p.k_rows - 1));
     }
     const int vy = (int)min((int64_t)b * p.T + krow, rowsBT - 1);
-    for (int cb = 0; cb < p.D / 64; ++cb) tma_load_2d_pair(&tv, inf, smem + L.off_v + cb * (kRows * 128), cb * 64, vy);
+    if (do_dk)  // V rows feed dP^T, needed only for dS
+      for (int cb = 0; cb < p.D / 64; ++cb)
+        tma_load_2d_pair(&tv, inf, smem + L.off_v + cb * (kRows * 128), cb * 64, vy);
     int it = 0;
     bool ok = true;
     auto stage = [&](int bytes) -> uint8_t* {
@@ -513,7 +537,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
         }
       }
       const int y = (int)min((int64_t)b * p.T + q, rowsBT - 1);
-      for (int cc = 0; ok && cc < L.d_chunks; ++cc, ++it) {
+      for (int cc = 0; ok && do_dk && cc < L.d_chunks; ++cc, ++it) {
         uint8_t* dst = stage(2 * kRows * 128);
         if (!ok) return;
         const uint32_t bar = stage_bar();
@@ -522,7 +546,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
     };
     auto items_dkv = [&](int i) {  // dY (MN-major) for dV, then Q (MN-major) for dK: all 128 queries
       const int dper = (dn / 2) / 64;
-      for (int qc = 0; ok && qc < kTile / 64; ++qc) {
+      for (int qc = 0; ok && do_dv && qc < kTile / 64; ++qc) {
         const int q = i * kTile + qc * 64;
         const int y = (int)min((int64_t)b * p.T + q, rowsBT - 1);
         for (int ins = 0; ok && ins < L.dins; ++ins, ++it) {
@@ -534,7 +558,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
         }
       }
       const int per = (L.ncol / 2) / 64;
-      for (int qc = 0; ok && qc < kTile / 64; ++qc)
+      for (int qc = 0; ok && do_dk && qc < kTile / 64; ++qc)
         for (int ins = 0; ok && ins < L.nins; ++ins, ++it) {
           uint8_t* dst = stage(per * 64 * 128);
           if (!ok) return;
@@ -591,7 +615,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
         }
         give();
       }
-      for (int cc = 0; ok && cc < L.d_chunks; ++cc) {
+      for (int cc = 0; ok && do_dk && cc < L.d_chunks; ++cc) {
         uint32_t st;
         if (!(ok = take(&st))) break;
         for (int k = 0; k < 8; ++k) {
@@ -606,7 +630,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
       // dV += P^T dY and dK += dS^T Q once the softmax wrote this tile's P^T / dS^T
       if (!(ok = mbar_wait(&p_full, i & 1u, ab, 24))) break;
       tc_fence_after();
-      for (int qc = 0; ok && qc < kTile / 64; ++qc)
+      for (int qc = 0; ok && do_dv && qc < kTile / 64; ++qc)
         for (int ins = 0; ok && ins < L.dins; ++ins) {
           uint32_t st;
           if (!(ok = take(&st))) break;
@@ -617,7 +641,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
           }
           give();
         }
-      for (int qc = 0; ok && qc < kTile / 64; ++qc)
+      for (int qc = 0; ok && do_dk && qc < kTile / 64; ++qc)
         for (int ins = 0; ok && ins < L.nins; ++ins) {
           uint32_t st;
           if (!(ok = take(&st))) break;
@@ -666,7 +690,12 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
         for (int ch = 0; ch < 2; ++ch) {
           float sv[32], dpv[32];
           tmem_ld32(tmem + lane_base + L.tmem_s + ch * 32, sv);
-          tmem_ld32(tmem + lane_base + L.tmem_p + ch * 32, dpv);
+          if (do_dk) {
+            tmem_ld32(tmem + lane_base + L.tmem_p + ch * 32, dpv);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) dpv[e] = 0.f;
+          }
           tmem_wait_ld();
           const int qc0 = half * 64 + ch * 32;  // query column inside the tile
           uint32_t pk[16], dk[16];
@@ -704,7 +733,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
     ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
     if (ok) {
-      for (int ins = 0; ins < L.dins; ++ins)
+      for (int ins = 0; do_dv && ins < L.dins; ++ins)
         for (int c = 0; c < dn / 2; c += 32) {
           float v[32];
           tmem_ld32(tmem + lane_base + L.tmem_dv + ins * (dn / 2) + c, v);
@@ -722,7 +751,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
             }
           }
         }
-      for (int ins = 0; ins < L.nins; ++ins)
+      for (int ins = 0; do_dk && ins < L.nins; ++ins)
         for (int c = 0; c < L.ncol / 2; c += 32) {
           float v[32];
           tmem_ld32(tmem + lane_base + L.tmem_dk + ins * (L.ncol / 2) + c, v);
@@ -836,8 +865,11 @@ extern "C" int da_attn_bwd(const void* q, int64_t q_rows, int64_t q_base, int64_
   const int kw = group * R;
   if (kw != 128 && kw != 256 && kw != 512) return DA_ERR_UNSUPPORTED;
   const DqLayout LQ = dq_layout(group, R, D);
-  const KvLayout LK = kv_layout(group, R, D);
-  if (LQ.nst < 2 || LK.nst < 2 || LQ.tmem_p + 2 * (kTile / 2) > 512 || LK.tmem_p + kTile / 2 > 512)
+  // one key-parallel launch for dV and dK when both accumulators fit in TMEM, else one each
+  const bool split = kv_layout(group, R, D, true, true).tmem_cols > 512;
+  if (LQ.nst < 2 || LQ.tmem_p + 2 * (kTile / 2) > 512) return DA_ERR_UNSUPPORTED;
+  if (kv_layout(group, R, D, true, false).tmem_cols > 512 || kv_layout(group, R, D, false, true).tmem_cols > 512 ||
+      kv_layout(group, R, D, true, true).nst < 2)
     return DA_ERR_UNSUPPORTED;
   if ((reinterpret_cast<uintptr_t>(dq) | reinterpret_cast<uintptr_t>(dk) | reinterpret_cast<uintptr_t>(dv)) & 15)
     return DA_ERR_ALIGN;
@@ -862,6 +894,8 @@ extern "C" int da_attn_bwd(const void* q, int64_t q_rows, int64_t q_base, int64_
   p.B = B; p.T = T; p.R = R; p.D = D; p.group = group; p.branch0 = branch0; p.causal = causal;
   p.scale = scale; p.weight = weight; p.lse = lse; p.delta = delta;
   p.dq = dq; p.dk = dk; p.dv = dv; p.dscale = dscale; p.status = status;
+  p.do_dv = dv != nullptr;
+  p.do_dk = dk != nullptr;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int pairs = (int)(B * tiles);
   const bool bf16 = dtype == DA_BF16;
@@ -870,8 +904,20 @@ extern "C" int da_attn_bwd(const void* q, int64_t q_rows, int64_t q_base, int64_
               : launch_pair(dq_kernel<__half>, LQ, pairs, tq, tk, tv, tdy, p, st);
     if (rc) return rc;
   }
-  if (dk || dv)
-    rc = bf16 ? launch_pair(dkv_kernel<__nv_bfloat16>, LK, pairs, tq, tk, tv, tdy, p, st)
-              : launch_pair(dkv_kernel<__half>, LK, pairs, tq, tk, tv, tdy, p, st);
+  auto launch_kv = [&](bool with_dv, bool with_dk) -> int {
+    Params pk = p;
+    pk.do_dv = with_dv;
+    pk.do_dk = with_dk;
+    const KvLayout LK = kv_layout(group, R, D, with_dv, with_dk);
+    return bf16 ? launch_pair(dkv_kernel<__nv_bfloat16>, LK, pairs, tq, tk, tv, tdy, pk, st)
+                : launch_pair(dkv_kernel<__half>, LK, pairs, tq, tk, tv, tdy, pk, st);
+  };
+  if (dv && dk && split) {
+    rc = launch_kv(true, false);
+    if (rc) return rc;
+    rc = launch_kv(false, true);
+  } else if (dv || dk) {
+    rc = launch_kv(dv != nullptr, dk != nullptr);
+  }
   return rc;
 }

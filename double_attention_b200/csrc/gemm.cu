@@ -33,6 +33,7 @@ struct Params {
   int out_f32;     // C is fp32 (else the input dtype)
   int accumulate;  // C += A.B (else C = A.B)
   int* status;
+  int kps;         // K stages per split (split-K when gridDim.z > 1), 0 = all
 };
 
 template <typename T, int kN, bool kAmn, bool kBmn>
@@ -46,7 +47,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   __shared__ int abort_flag;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int m0 = blockIdx.x * kBM, n0 = blockIdx.y * kN;
-  const int nk = (p.K + kBK - 1) / kBK;  // TMA zero-fills the ragged last K stage
+  const int nk_all = (p.K + kBK - 1) / kBK;  // TMA zero-fills the ragged last K stage
+  // split-K: this CTA reduces K stages [kb0, kb0 + nk) and adds its partial sum atomically
+  const bool split = gridDim.z > 1;
+  const int kb0 = split ? (int)blockIdx.z * p.kps : 0;
+  const int nk = split ? min(p.kps, nk_all - kb0) : nk_all;  // >= 1 (the host sizes the splits)
   Abort ab{&abort_flag, p.status};
 
   if (threadIdx.x == 0) {
@@ -79,15 +84,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         uint8_t* sa = smem + s * (C::kABytes + C::kBBytes);
         uint8_t* sb = sa + C::kABytes;
         if (!kAmn) {
-          tma_load_2d(&ta, &full[s], sa, kb * kBK, m0);
+          tma_load_2d(&ta, &full[s], sa, (kb0 + kb) * kBK, m0);
         } else {
-          tma_load_2d(&ta, &full[s], sa, m0, kb * kBK);
-          tma_load_2d(&ta, &full[s], sa + kBK * 128, m0 + 64, kb * kBK);
+          tma_load_2d(&ta, &full[s], sa, m0, (kb0 + kb) * kBK);
+          tma_load_2d(&ta, &full[s], sa + kBK * 128, m0 + 64, (kb0 + kb) * kBK);
         }
         if (!kBmn) {
-          tma_load_2d(&tb, &full[s], sb, kb * kBK, n0);
+          tma_load_2d(&tb, &full[s], sb, (kb0 + kb) * kBK, n0);
         } else {
-          for (int i = 0; i < kN / 64; ++i) tma_load_2d(&tb, &full[s], sb + i * kBK * 128, n0 + i * 64, kb * kBK);
+          for (int i = 0; i < kN / 64; ++i)
+            tma_load_2d(&tb, &full[s], sb + i * kBK * 128, n0 + i * 64, (kb0 + kb) * kBK);
         }
         issued = kb + 1;
       }
@@ -131,7 +137,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + c, v);
         tmem_wait_ld();
         if (!live || n0 + c >= p.N) continue;
-        if (p.out_f32) {
+        if (split) {
+          float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.c) + (size_t)row * p.ldc + n0 + c);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) atomicAdd(dst + e, make_float4(v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3]));
+        } else if (p.out_f32) {
           float* dst = reinterpret_cast<float*>(p.c) + (size_t)row * p.ldc + n0 + c;
 #pragma unroll
           for (int e = 0; e < 32; e += 4) {
@@ -160,7 +170,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
 }
 
 template <typename T, int kN, bool kAmn, bool kBmn>
-int launch(const void* A, int64_t lda, const void* B, int64_t ldb, const Params& p, cudaStream_t st) {
+int launch(const void* A, int64_t lda, const void* B, int64_t ldb, const Params& p, int splits, cudaStream_t st) {
   using C = Cfg<kN>;
   const CUtensorMapDataType dt =
       std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -175,7 +185,7 @@ int launch(const void* A, int64_t lda, const void* B, int64_t ldb, const Params&
   const int smem = C::kSmem + 1024;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return record_cuda_error();
-  dim3 grid((unsigned)((p.M + kBM - 1) / kBM), (unsigned)((p.N + kN - 1) / kN));
+  dim3 grid((unsigned)((p.M + kBM - 1) / kBM), (unsigned)((p.N + kN - 1) / kN), (unsigned)splits);
   kern<<<grid, kThreads, smem, st>>>(ta, tb, p);
   if (cudaPeekAtLastError() != cudaSuccess) return record_cuda_error();
   return DA_OK;
@@ -183,9 +193,9 @@ int launch(const void* A, int64_t lda, const void* B, int64_t ldb, const Params&
 
 template <typename T>
 int dispatch(int a_mn, int b_mn, int n_tile, const void* A, int64_t lda, const void* B, int64_t ldb, const Params& p,
-             cudaStream_t st) {
+             int splits, cudaStream_t st) {
 #define DA_GEMM_CASE(NT, AMN, BMN) \
-  if (n_tile == NT && a_mn == AMN && b_mn == BMN) return launch<T, NT, AMN, BMN>(A, lda, B, ldb, p, st);
+  if (n_tile == NT && a_mn == AMN && b_mn == BMN) return launch<T, NT, AMN, BMN>(A, lda, B, ldb, p, splits, st);
   DA_GEMM_CASE(128, 0, 0)
   DA_GEMM_CASE(256, 0, 0)
   DA_GEMM_CASE(128, 0, 1)
@@ -211,9 +221,36 @@ extern "C" int da_gemm(const void* A, int64_t lda, int a_mn_major, const void* B
   if (a_mn_major && M % 128) return DA_ERR_SHAPE;   // every A box starts inside the matrix
   if (accumulate && !out_f32) return DA_ERR_UNSUPPORTED;
   if ((reinterpret_cast<uintptr_t>(C) & 15) || (ldc % 8)) return DA_ERR_ALIGN;
-  gemm::Params p{(int)M, (int)N, (int)K, C, ldc, out_f32, accumulate, status};
+  gemm::Params p{(int)M, (int)N, (int)K, C, ldc, out_f32, accumulate, status, 0};
   const int n_tile = (N % 256 == 0 && (M / 128) * (N / 256) >= 120) ? 256 : 128;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (dtype == DA_BF16) return gemm::dispatch<__nv_bfloat16>(a_mn_major, b_mn_major, n_tile, A, lda, B, ldb, p, st);
-  return gemm::dispatch<__half>(a_mn_major, b_mn_major, n_tile, A, lda, B, ldb, p, st);
+  if (dtype == DA_BF16)
+    return gemm::dispatch<__nv_bfloat16>(a_mn_major, b_mn_major, n_tile, A, lda, B, ldb, p, 1, st);
+  return gemm::dispatch<__half>(a_mn_major, b_mn_major, n_tile, A, lda, B, ldb, p, 1, st);
+}
+
+extern "C" int da_gemm_splitk(const void* A, int64_t lda, int a_mn_major, const void* B, int64_t ldb, int b_mn_major,
+                              float* C, int64_t ldc, int64_t M, int64_t N, int64_t K, int dtype, int splits,
+                              int* status, void* stream) {
+  using namespace da;
+  if (!A || !B || !C || !status) return DA_ERR_NULL;
+  if (int rc = bind_device(A)) return rc;
+  if (dtype != DA_BF16 && dtype != DA_F16) return DA_ERR_DTYPE;
+  if (M <= 0 || N <= 0 || K <= 0 || N % 128 || M % 128) return DA_ERR_SHAPE;
+  if ((lda % 8) || (ldb % 8)) return DA_ERR_ALIGN;
+  if ((reinterpret_cast<uintptr_t>(C) & 15) || (ldc % 4)) return DA_ERR_ALIGN;
+  const int nk = (int)((K + gemm::kBK - 1) / gemm::kBK);
+  const int n_tile = 128;
+  if (splits <= 0) {  // about two CTAs per SM-sized wave of output tiles
+    const int tiles = (int)((M / 128) * (N / n_tile));
+    splits = (2 * sm_count() + tiles - 1) / tiles;
+  }
+  int kps = (nk + splits - 1) / splits;
+  if (kps < 1) kps = 1;
+  splits = (nk + kps - 1) / kps;  // every split gets at least one K stage
+  gemm::Params p{(int)M, (int)N, (int)K, C, ldc, 1, 1, status, kps};
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == DA_BF16)
+    return gemm::dispatch<__nv_bfloat16>(a_mn_major, b_mn_major, n_tile, A, lda, B, ldb, p, splits, st);
+  return gemm::dispatch<__half>(a_mn_major, b_mn_major, n_tile, A, lda, B, ldb, p, splits, st);
 }

@@ -33,5 +33,31 @@ struct RouteFwdArgs {
 
 int route_fwd(const RouteFwdArgs& a, cudaStream_t st);
 
+struct RouteBwdArgs {
+  const void* q;            // forward input rows (same addressing as RouteFwdArgs)
+  int64_t rows, q_cols, q_row_stride;
+  int groups;
+  int64_t group_col_stride;
+  int64_t R, M;
+  int dtype;
+  const void* dk_t;         // [M, R] normalised keys (dtype)
+  const void* dv_t;         // [M, R] normalised values (bf16)
+  const float* beta;
+  float eps;
+  int normalize_input, normalize_output;
+  const void* z;            // [groups, rows, R] forward output (dtype)
+  const void* dz;           // [groups, rows, R] its gradient (dtype)
+  const float* lse;         // [groups, rows] from the forward
+  const float* out_norm;    // [groups, rows] from the forward
+  void* dq;                 // gradient of q, layout of q (dtype)
+  void* p_out;              // [groups, rows, M] bf16 assignment weights
+  void* dl_out;             // [groups, rows, M] dtype: invn * beta * dLs
+  void* g_out;              // [groups, rows, R] bf16 gradient of the reconstruction
+  float* dbeta;             // accumulated, may be null
+  int* status;
+};
+
+int route_bwd(const RouteBwdArgs& a, cudaStream_t st);
+
 }  // namespace route
 }  // namespace da

@@ -142,6 +142,10 @@ class DictionaryViews:
     key   [R, M], key_t [M, R] in the compute dtype (q . Dk operands)
     value [R, M], value_t [M, R] in bf16 (probability . Dv operands)
     key_max: max column norm of ``key`` as rounded (softmax offset bound).
+    key_anchor / value_anchor: [R, M] tensors through which the route
+    backward returns the dictionary gradients in fp32 (their contents are
+    never read), so gradients from every block sharing a bank accumulate in
+    fp32 before one normalisation backward.
     """
 
     key: Tensor
@@ -149,6 +153,8 @@ class DictionaryViews:
     value: Tensor
     value_t: Tensor
     key_max: Tensor
+    key_anchor: Tensor
+    value_anchor: Tensor
 
     @property
     def routing_dim(self) -> int:
@@ -175,11 +181,14 @@ class _DictNorm(torch.autograd.Function):
         ctx.save_for_backward(raw, denom)
         ctx.eps = eps
         ctx.mark_non_differentiable(mx)
-        return out, out_t, mx
+        anchor = torch.empty(r, m, dtype=torch.float32, device=raw.device)  # fp32 gradient entry, never read
+        return out, out_t, mx, anchor
 
     @staticmethod
-    def backward(ctx, g_out: Tensor | None, g_out_t: Tensor | None, _g_mx):  # type: ignore[override]
+    def backward(ctx, g_out: Tensor | None, g_out_t: Tensor | None, _g_mx, g_anchor: Tensor | None):  # type: ignore[override]
         raw, denom = ctx.saved_tensors
+        if g_anchor is not None:
+            g_out = g_anchor if g_out is None else g_anchor + g_out.float()
         if g_out is None and g_out_t is None:
             return None, None, None
         r, m = raw.shape
@@ -195,15 +204,15 @@ def dictionary_views(raw_key: Tensor, raw_value: Tensor | None, eps: float, dtyp
     """Normalise a bank's raw parameters into kernel operands (autograd-aware)."""
     if not raw_key.is_cuda:
         raise RuntimeError("B200 backend requested but unavailable: CUDA fp16/bf16 tensors are required")
-    key, key_t, key_max = _DictNorm.apply(raw_key, eps, dtype)
+    key, key_t, key_max, key_anchor = _DictNorm.apply(raw_key, eps, dtype)
     if raw_value is None:  # tied dictionary (untied_dictionary=False)
         if dtype == torch.bfloat16:
-            value, value_t = key, key_t
+            value, value_t, value_anchor = key, key_t, key_anchor
         else:
-            value, value_t, _ = _DictNorm.apply(raw_key, eps, torch.bfloat16)
+            value, value_t, _, value_anchor = _DictNorm.apply(raw_key, eps, torch.bfloat16)
     else:
-        value, value_t, _ = _DictNorm.apply(raw_value, eps, torch.bfloat16)
-    return DictionaryViews(key, key_t, value, value_t, key_max)
+        value, value_t, _, value_anchor = _DictNorm.apply(raw_value, eps, torch.bfloat16)
+    return DictionaryViews(key, key_t, value, value_t, key_max, key_anchor, value_anchor)
 
 
 def _col_norm_max(d: Tensor) -> Tensor:
@@ -214,10 +223,13 @@ def _col_norm_max(d: Tensor) -> Tensor:
 
 
 def dictionary_views_from_normalized(key: Tensor, value: Tensor, dtype: torch.dtype) -> DictionaryViews:
-    """Kernel operands from caller-normalised dictionaries (cast + transpose)."""
-    k = key.to(dtype).contiguous()
-    v = value.to(torch.bfloat16).contiguous()
-    return DictionaryViews(k, k.t().contiguous(), v, v.t().contiguous(), _col_norm_max(k))
+    """Kernel operands from caller-normalised dictionaries (cast + transpose).
+
+    The caller's tensors themselves are the gradient anchors: the route
+    backward returns the dictionary gradients to them."""
+    k = key.detach().to(dtype).contiguous()
+    v = value.detach().to(torch.bfloat16).contiguous()
+    return DictionaryViews(k, k.t().contiguous(), v, v.t().contiguous(), _col_norm_max(k), key, value)
 
 
 # ----------------------------------------------------------------------------- route
@@ -251,13 +263,14 @@ class _Route(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, q: Tensor, key: Tensor, key_t: Tensor, value: Tensor, value_t: Tensor, key_max: Tensor,  # type: ignore[override]
-                beta: Tensor, rows: int, groups: int, col_stride: int, eps: float, normalize_input: bool,
-                normalize_output: bool):
-        views = DictionaryViews(key, key_t, value, value_t, key_max)
+                key_anchor: Tensor, value_anchor: Tensor, beta: Tensor, rows: int, groups: int, col_stride: int,
+                eps: float, normalize_input: bool, normalize_output: bool):
+        views = DictionaryViews(key, key_t, value, value_t, key_max, key_anchor, value_anchor)
         z, lse, onorm = _route_forward(q, rows, groups, col_stride, views, beta, eps, normalize_input,
                                        normalize_output)
-        ctx.save_for_backward(q, key, key_t, value, value_t, key_max, beta, z, lse, onorm)
-        ctx.meta = (rows, groups, col_stride, eps, normalize_input, normalize_output)
+        ctx.save_for_backward(q, key_t, value_t, beta, z, lse, onorm)
+        ctx.meta = (rows, groups, col_stride, eps, normalize_input, normalize_output,
+                    key_anchor.dtype, value_anchor.dtype)
         return z
 
     @staticmethod
@@ -265,8 +278,48 @@ class _Route(torch.autograd.Function):
         return _route_backward(ctx, dz)
 
 
+def gemm_splitk(a: Tensor, lda: int, a_mn: bool, b: Tensor, ldb: int, b_mn: bool, m: int, n: int, k: int,
+                out: Tensor, splits: int = 0) -> Tensor:
+    """out[m, n] += sum_k A(m, k) B(n, k) in fp32, K split over CTAs (see da_gemm_splitk)."""
+    ws = workspace(out.device)
+    call("da_gemm_splitk", a.data_ptr(), lda, int(a_mn), b.data_ptr(), ldb, int(b_mn), out.data_ptr(), out.stride(0),
+         m, n, k, dtype_code(a.dtype), splits, ws.status.data_ptr(), stream_ptr(out.device))
+    return out
+
+
 def _route_backward(ctx, dz: Tensor):
-    raise NotImplementedError("dictionary route backward kernel is not available in this build")
+    """dq, fp32 dDk / dDv (into the anchors) and dbeta of one route call."""
+    q, key_t, value_t, beta, z, lse, onorm = ctx.saved_tensors
+    rows, groups, col_stride, eps, ni, no, key_dtype, value_dtype = ctx.meta
+    need = ctx.needs_input_grad
+    m, r = key_t.shape
+    dev = q.device
+    dz = dz.to(z.dtype).contiguous()
+    full = groups * col_stride == q.shape[1] and col_stride == r and q.stride(0) == q.shape[1]
+    dq = torch.empty_like(q) if full else torch.zeros_like(q)
+    p_out = torch.empty(groups, rows, m, dtype=torch.bfloat16, device=dev)
+    dl_out = torch.empty(groups, rows, m, dtype=q.dtype, device=dev)
+    g_out = torch.empty(groups, rows, r, dtype=torch.bfloat16, device=dev)
+    dbeta = torch.zeros(1, dtype=torch.float32, device=dev) if need[8] else None
+    ws = workspace(dev)
+    beta32 = beta.detach().float().reshape(1).contiguous()
+    call("da_route_bwd", q.data_ptr(), rows, q.shape[1], q.stride(0), groups, col_stride, r, m, dtype_code(q.dtype),
+         key_t.data_ptr(), value_t.data_ptr(), beta32.data_ptr(), eps, int(ni), int(no), z.data_ptr(), dz.data_ptr(),
+         lse.data_ptr(), onorm.data_ptr(), dq.data_ptr(), p_out.data_ptr(), dl_out.data_ptr(), g_out.data_ptr(),
+         ptr(dbeta), ws.status.data_ptr(), stream_ptr(dev))
+    d_key = d_value = None
+    if need[6]:  # dDk = sum_groups q_g^T dL'_g  (dL' already carries 1 / ||q||)
+        d_key = torch.zeros(r, m, dtype=torch.float32, device=dev)
+        for g in range(groups):
+            gemm_splitk(q[:, g * col_stride:], q.stride(0), True, dl_out[g], m, True, r, m, rows, d_key)
+    if need[7]:  # dDv = G^T P over every routed row
+        d_value = torch.zeros(r, m, dtype=torch.float32, device=dev)
+        gemm_splitk(g_out.view(-1, r), r, True, p_out.view(-1, m), m, True, r, m, groups * rows, d_value)
+    return (dq if need[0] else None, None, None, None, None, None,
+            None if d_key is None else d_key.to(key_dtype),
+            None if d_value is None else d_value.to(value_dtype),
+            None if dbeta is None else dbeta.view(beta.shape).to(beta.dtype),
+            None, None, None, None, None, None)
 
 
 def route_projected(projected: Tensor, views: DictionaryViews, beta: Tensor, cfg, batch: int, length: int) -> Tensor:
@@ -277,8 +330,9 @@ def route_projected(projected: Tensor, views: DictionaryViews, beta: Tensor, cfg
     """
     _check_variant(cfg)
     h, r = cfg.qk_branches, cfg.routing_dim
-    z = _Route.apply(projected, views.key, views.key_t, views.value, views.value_t, views.key_max, beta,
-                     batch * length, 2 * h, r, cfg.eps, cfg.normalize_routing_input, cfg.normalize_routing_output)
+    z = _Route.apply(projected, views.key, views.key_t, views.value, views.value_t, views.key_max, views.key_anchor,
+                     views.value_anchor, beta, batch * length, 2 * h, r, cfg.eps, cfg.normalize_routing_input,
+                     cfg.normalize_routing_output)
     return z.view(2, h, batch, length, r)
 
 
@@ -322,8 +376,8 @@ def dictionary_route(
     views = dictionary_views_from_normalized(dictionary_key, dictionary_value, input.dtype)
     if not torch.is_tensor(beta):
         beta = torch.tensor(float(beta), device=input.device)
-    z = _Route.apply(flat, views.key, views.key_t, views.value, views.value_t, views.key_max, beta, flat.shape[0], 1,
-                     r, eps, normalize_input, normalize_output)
+    z = _Route.apply(flat, views.key, views.key_t, views.value, views.value_t, views.key_max, views.key_anchor,
+                     views.value_anchor, beta, flat.shape[0], 1, r, eps, normalize_input, normalize_output)
     return z.view(shape)
 
 

@@ -110,6 +110,27 @@ DA_API int da_route_fwd_static(const void* q, int64_t rows, int64_t q_cols, int6
                                int normalize_input, int normalize_output, void* z, float* lse, float* out_norm,
                                int* argmax, int* status, void* stream);
 
+/* ---- dictionary route, backward --------------------------------------
+ * Replaces _DictionaryRouteFunction.backward (triton_kernels.py:1873-1981)
+ * with its row-normalisation and scaled-softmax backward kernels
+ * (:1410-1501) for the identity-logit softmax route; the two
+ * dictionary-gradient GEMMs it leaves to cuBLAS (:1939, :1961) run on
+ * da_gemm_splitk over the rows this call stores.  Same q addressing, R, M,
+ * dtype, eps and flags as the forward call; R in {128, 256, 512}, M a
+ * multiple of 128.  dict_key_t [M, R] (dtype), dict_value_t [M, R] bf16;
+ * z / dz [groups, rows, R] (forward output and its gradient, dtype); lse /
+ * out_norm from the forward.  Outputs: dq in the layout of q (dtype,
+ * overwritten at the routed columns); p_out [groups, rows, M] bf16 = the
+ * assignment weights; dl_out [groups, rows, M] dtype = the logit gradient
+ * divided by the input norm (dDk = sum_groups q_g^T dl_out_g); g_out
+ * [groups, rows, R] bf16 = gradient of the reconstruction (dDv = g_out^T
+ * p_out); dbeta (may be null) is accumulated (+=). */
+DA_API int da_route_bwd(const void* q, int64_t rows, int64_t q_cols, int64_t q_row_stride, int groups,
+                        int64_t group_col_stride, int64_t R, int64_t M, int dtype, const void* dict_key_t,
+                        const void* dict_value_t, const float* beta, float eps, int normalize_input,
+                        int normalize_output, const void* z, const void* dz, const float* lse, const float* out_norm,
+                        void* dq, void* p_out, void* dl_out, void* g_out, float* dbeta, int* status, void* stream);
+
 /* ---- outer routed attention with the map mix, forward -------------------
  * Replaces routed_attention_triton / _routed_attention_triton_forward
  * (triton_kernels.py:2290-2305, :2022-2090; math of ops.py:65-93) together
@@ -176,6 +197,16 @@ DA_API int da_attn_bwd(const void* q, int64_t q_rows, int64_t q_base, int64_t q_
 DA_API int da_gemm(const void* A, int64_t lda, int a_mn_major, const void* B, int64_t ldb, int b_mn_major, void* C,
                    int64_t ldc, int64_t M, int64_t N, int64_t K, int dtype, int out_f32, int accumulate, int* status,
                    void* stream);
+
+/* Split-K variant for reductions over many rows (the dictionary gradients
+ * dDk = q^T dL and dDv = g^T P, triton_kernels.py:1939, :1961):
+ * C[M, N] += sum_k A(m, k) B(n, k) in fp32, the K range split over `splits`
+ * CTAs per output tile (0 = pick from the SM count) whose partial sums are
+ * added atomically, so C must hold its initial value (e.g. zeros).  M and N
+ * multiples of 128. */
+DA_API int da_gemm_splitk(const void* A, int64_t lda, int a_mn_major, const void* B, int64_t ldb, int b_mn_major,
+                          float* C, int64_t ldc, int64_t M, int64_t N, int64_t K, int dtype, int splits, int* status,
+                          void* stream);
 
 /* ---- building-block check -------------------------------------------
  * No reference counterpart: D[128, n] = A[128, k] * B^T computed by one
