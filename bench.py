@@ -2,19 +2,26 @@
 """Routed-attention throughput on B200 (the BASELINE.json metric).
 
 Default workload: preset ``a1``
-SharedDictionaryAttention forward in fp16, batch 8 x seq 512 per GPU
-(x ~ N(0,1) from a seeded generator, weights from torch.manual_seed(0)).
-A "step" is one module forward over one batch; ``value`` is routed tokens/s
-summed over all ranks with inputs resident in HBM, ``e2e`` is the same
-through the public module call with pinned host input/output copied inside
-the timed region.  One JSON line is printed by rank 0.
+SharedDictionaryAttention forward in fp16, batch 8 x seq 512 per GPU.
+Other workloads (``--config``):
+  3  qk4-s4 SharedDictionaryAttention forward+backward, bf16, global batch 16 x 2048 (dY ~ N(0,1))
+  4  a1-r512-d1536 forward, bf16, batch 4 x 8192 per GPU
+  5  DoubleAttentionLM training step (a1, 6 layers, one bank, FFN 1536, vocab 2048, T 1024),
+     bf16 autocast, AdamW, global batch 256 data-parallel with NCCL gradient averaging
+Inputs are synthetic: x ~ N(0,1) and dY ~ N(0,1) from seeded generators,
+token ids uniform in [0, 2048), weights from torch.manual_seed(0).
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2|4]
+A "step" is one pass of the workload over one batch; ``value`` is routed
+tokens/s summed over all ranks with inputs resident in HBM, ``e2e`` is the
+same through the public module call with pinned host inputs copied in and
+the result copied out inside the timed region.  One JSON line is printed
+by rank 0.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2|3|4|5]
   python bench.py --impl reference ...   # the reference algorithm on host cores
 
-Multi-GPU runs are launched with torchrun (one rank per GPU, NCCL); each
-rank processes its own batch (weak scaling) and the slowest rank's device
-time is reported.
+Multi-GPU runs are launched with torchrun (one rank per GPU, NCCL); the
+slowest rank's device time is reported.
 """
 
 from __future__ import annotations
@@ -23,7 +30,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -35,30 +41,49 @@ REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO))
 
 METRIC = "routed-attention tokens/sec"
-# Larger than the 126 MB L2; its ~80 us of device time also keeps the GPU
-# busy while the host enqueues the timed step after it.
+# Larger than the 126 MB L2; its device time also keeps the GPU busy while
+# the host enqueues the timed step after it.
 L2_FLUSH_BYTES = 512 << 20
 
 CONFIGS = {
-    # a1 forward, fp16, B8 T512
-    2: dict(preset="a1", dtype=torch.float16, batch=8, seq=512, mode="fwd",
+    # a1 forward, fp16, B8 T512 per GPU
+    2: dict(kind="module", preset="a1", dtype=torch.float16, batch=8, seq=512, mode="fwd", scaling="weak",
             workload="a1 SharedDictionaryAttention forward, fp16, B8 T512 per GPU"),
+    # qk4-s4 forward+backward, bf16, B16 T2048 split over the GPUs
+    3: dict(kind="module", preset="qk4-s4", dtype=torch.bfloat16, batch=16, seq=2048, mode="fwdbwd",
+            scaling="strong",
+            workload="qk4-s4 SharedDictionaryAttention forward+backward, bf16, global B16 T2048, dY ~ N(0,1)"),
     # a1-r512-d1536 forward, bf16, 4 x 8192 per GPU
-    4: dict(preset="a1-r512-d1536", dtype=torch.bfloat16, batch=4, seq=8192, mode="fwd",
-            workload="a1-r512-d1536 SharedDictionaryAttention forward, bf16, B4 T8192 per GPU"),
+    4: dict(kind="module", preset="a1-r512-d1536", dtype=torch.bfloat16, batch=4, seq=8192, mode="fwd",
+            scaling="weak", workload="a1-r512-d1536 SharedDictionaryAttention forward, bf16, B4 T8192 per GPU"),
+    # LM training step, global batch 256 split over the GPUs
+    5: dict(kind="lm", preset="a1", dtype=torch.bfloat16, batch=256, seq=1024, mode="train", scaling="strong",
+            layers=6, ffn=1536, vocab=2048,
+            workload="DoubleAttentionLM a1 6 layers train step (AdamW), bf16 autocast, global B256 T1024"),
+}
+
+# kernels whose live duration is measured for the roofline, per mode
+ROOFLINE_KERNELS = {
+    "fwd": ("route", "attention"),
+    "fwdbwd": ("route", "attention", "route_bwd", "dict_grads", "attention_bwd"),
+    "train": ("route", "attention", "route_bwd", "dict_grads", "attention_bwd"),
 }
 
 
 def parse_args(argv=None):
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--steps", type=int, default=None, help="timed steps (default per config)")
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS))
     p.add_argument("--impl", choices=("b200", "reference"), default="b200")
     p.add_argument("--no-graph", action="store_true", help="time eager launches instead of a CUDA graph")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
-    return p.parse_args(argv)
+    args = p.parse_args(argv)
+    if args.steps is None:
+        args.steps = {2: 200, 3: 20, 4: 20, 5: 10}[args.config]
+    args.warmup = max(3, args.warmup) if args.impl == "b200" else args.warmup
+    return args
 
 
 # ----------------------------------------------------------------------------- distributed
@@ -153,20 +178,123 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(self.samples)}
 
 
-# ----------------------------------------------------------------------------- workload
-def build_module(cfg, device):
-    from double_attention_b200 import SharedDictionaryAttention, experiment_config
+# ----------------------------------------------------------------------------- workloads
+def per_rank_batch(cfg, world: int) -> int:
+    if cfg["scaling"] == "weak":
+        return cfg["batch"]
+    if cfg["batch"] % world:
+        raise SystemExit(f"global batch {cfg['batch']} does not split over {world} GPUs")
+    return cfg["batch"] // world
 
-    torch.manual_seed(0)
-    module = SharedDictionaryAttention(experiment_config(cfg["preset"]))
-    return module.to(device=device, dtype=cfg["dtype"]).eval()
 
-
-def make_input(cfg, seed: int) -> torch.Tensor:
+def _seeded_normal(shape, seed: int, dtype) -> torch.Tensor:
     g = torch.Generator().manual_seed(seed)
-    return torch.randn(cfg["batch"], cfg["seq"], 512, generator=g).to(cfg["dtype"])
+    return torch.randn(*shape, generator=g).to(dtype)
 
 
+def _token_ids(batch: int, seq: int, vocab: int, seed: int) -> torch.Tensor:
+    g = torch.Generator().manual_seed(seed)
+    return torch.randint(0, vocab, (batch, seq + 1), generator=g)
+
+
+class ModuleWorkload:
+    """SharedDictionaryAttention forward (or forward+backward) on one rank's batch."""
+
+    def __init__(self, cfg, device, rank: int, world: int) -> None:
+        from double_attention_b200 import SharedDictionaryAttention, experiment_config
+
+        self.cfg, self.device = cfg, device
+        self.batch = per_rank_batch(cfg, world)
+        self.train = cfg["mode"] == "fwdbwd"
+        torch.manual_seed(0)
+        module = SharedDictionaryAttention(experiment_config(cfg["preset"])).to(device=device, dtype=cfg["dtype"])
+        self.module = module.train(self.train)
+        shape = (self.batch, cfg["seq"], 512)
+        self.x_host = _seeded_normal(shape, 1 + rank, cfg["dtype"]).pin_memory()
+        self.x = self.x_host.to(device)
+        self.out_host = torch.empty(shape, dtype=cfg["dtype"]).pin_memory()
+        if self.train:
+            self.dy_host = _seeded_normal(shape, 1000 + rank, cfg["dtype"]).pin_memory()
+            self.dy = self.dy_host.to(device)
+            self.x.requires_grad_(True)
+        self.tokens = self.batch * cfg["seq"]
+        self.h2d = self.x_host.numel() * self.x_host.element_size() * (2 if self.train else 1)
+        self.d2h = self.out_host.numel() * self.out_host.element_size()
+        self.capturable = True
+
+    def step(self) -> None:
+        if not self.train:
+            with torch.no_grad():
+                self.module(self.x)
+            return
+        for p in self.module.parameters():
+            p.grad = None
+        self.x.grad = None
+        self.module(self.x).backward(self.dy)
+
+    def e2e_step(self) -> None:
+        if not self.train:
+            with torch.no_grad():
+                xd = self.x_host.to(self.device, non_blocking=True)
+                self.out_host.copy_(self.module(xd), non_blocking=True)
+            return
+        for p in self.module.parameters():
+            p.grad = None
+        xd = self.x_host.to(self.device, non_blocking=True).requires_grad_(True)
+        dyd = self.dy_host.to(self.device, non_blocking=True)
+        self.module(xd).backward(dyd)
+        self.out_host.copy_(xd.grad, non_blocking=True)  # the input gradient is the step's result
+
+
+class LMWorkload:
+    """One DoubleAttentionLM training step (forward, backward, gradient average, AdamW)."""
+
+    def __init__(self, cfg, device, rank: int, world: int) -> None:
+        from double_attention_b200 import DoubleAttentionLM, experiment_config
+        from double_attention_b200.data_parallel import GradientAllReduce
+
+        self.cfg, self.device = cfg, device
+        self.batch = per_rank_batch(cfg, world)
+        torch.manual_seed(0)
+        model = DoubleAttentionLM(cfg["vocab"], cfg["seq"], experiment_config(cfg["preset"]), cfg["layers"],
+                                  dictionary_group_size=cfg["layers"], feedforward_dim=cfg["ffn"])
+        self.model = model.to(device).train()
+        self.opt = torch.optim.AdamW(self.model.parameters(), lr=3e-4, fused=True)
+        banks = [p for bank in self.model.stack.banks for p in bank.parameters()]
+        self.reducer = GradientAllReduce(self.model.parameters(), last=banks)
+        ids = _token_ids(self.batch, cfg["seq"], cfg["vocab"], seed=2 + rank)
+        self.ids_host = ids[:, :-1].contiguous().pin_memory()
+        self.tgt_host = ids[:, 1:].contiguous().pin_memory()
+        self.ids, self.tgt = self.ids_host.to(device), self.tgt_host.to(device)
+        self.loss_host = torch.empty((), dtype=torch.float32).pin_memory()
+        self.tokens = self.batch * cfg["seq"]
+        self.h2d = 2 * self.ids_host.numel() * self.ids_host.element_size()
+        self.d2h = 4
+        self.capturable = False  # NCCL collectives and the optimiser run eagerly
+
+    def _train(self, ids, tgt):
+        self.opt.zero_grad(set_to_none=True)
+        with torch.autocast("cuda", dtype=self.cfg["dtype"]):
+            _, loss = self.model(ids, tgt)
+        loss.backward()
+        self.reducer.finish()
+        self.opt.step()
+        return loss
+
+    def step(self) -> None:
+        self._train(self.ids, self.tgt)
+
+    def e2e_step(self) -> None:
+        ids = self.ids_host.to(self.device, non_blocking=True)
+        tgt = self.tgt_host.to(self.device, non_blocking=True)
+        self.loss_host.copy_(self._train(ids, tgt).detach().float(), non_blocking=True)
+
+
+def make_workload(cfg, device, rank, world):
+    return (LMWorkload if cfg["kind"] == "lm" else ModuleWorkload)(cfg, device, rank, world)
+
+
+# ----------------------------------------------------------------------------- timing
 def time_steps(fn, steps: int, flush: torch.Tensor, stream) -> list[float]:
     """Per-step device time (ms) with CUDA events on `stream`, L2 flushed before each step."""
     times = []
@@ -181,41 +309,38 @@ def time_steps(fn, steps: int, flush: torch.Tensor, stream) -> list[float]:
     return [s.elapsed_time(e) for s, e in times]
 
 
-def kernel_rooflines(module, cfg, x, flush, stream, reps: int = 20):
-    """Live duration of the route and attention kernels at this workload."""
-    from double_attention_b200 import ops
+def capture(fn, device, stream):
+    """CUDA graph of `fn` (None if it cannot be captured)."""
+    try:
+        side = torch.cuda.Stream(device)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            fn()
+        stream.wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fn()
+        graph.replay()
+        torch.cuda.synchronize()
+        return graph
+    except Exception as exc:  # graph capture is an optimisation only
+        print(f"[bench] CUDA graph capture failed ({exc}); timing eager launches", file=sys.stderr)
+        torch.cuda.synchronize()
+        return None
 
-    c = module.config
-    b, t = cfg["batch"], cfg["seq"]
-    with torch.no_grad():
-        views = ops.dictionary_views(module.bank.raw_key, module.bank.raw_value, c.eps, cfg["dtype"])
-        w = torch.cat((module.query.weight, module.key.weight), 0)
-        proj = ops.qk_projection(x, w)
-        beta = module.beta
-        value = module.value(x).to(torch.bfloat16)
-        routed = ops.route_projected(proj, views, beta, c, b, t)
-        scales = ops.score_scale_from_log(module.log_score_scales)
 
-        def route():
-            ops._route_forward(proj, b * t, 2 * c.qk_branches, c.routing_dim, views, beta, c.eps,
-                               c.normalize_routing_input, c.normalize_routing_output)
+def kernel_rooflines(cfg, config: int, device):
+    """Live per-launch duration and algorithmic FLOPs of the main kernels at this workload's shapes."""
+    from double_attention_b200 import kernel_bench
 
-        def attention():
-            ops.routed_attention_mixed(routed, value, scales, None, c)
-
-        out = {}
-        for name, fn in (("route_fwd", route), ("attention_fwd", attention)):
-            for _ in range(3):
-                fn()
-            ms = statistics.mean(time_steps(fn, reps, flush, stream))
-            out[name] = ms
-    rows = 2 * b * t * c.qk_branches
-    flops = {
-        "route_fwd": 4.0 * c.routing_dim * c.dictionary_size * rows,
-        # causal: T^2/2 key pairs, 2 flop per MAC, R-wide scores + D-wide values
-        "attention_fwd": b * t * t * (c.outer_maps * c.routing_dim + c.model_dim),
-    }
-    return out, flops
+    out = {}
+    for name in ROOFLINE_KERNELS[cfg["mode"]]:
+        run, flops = kernel_bench.make_case(name, config, device)
+        ms = kernel_bench.time_kernel(run, 20, device)
+        out[name] = (ms, flops)
+        del run
+    torch.cuda.empty_cache()
+    return out
 
 
 def load_peaks():
@@ -236,59 +361,70 @@ def load_traffic(kernel: str, workload_key: str):
         return None
 
 
-def count_kernel_launches(module, x) -> int:
-    from double_attention_b200 import _lib
-
-    counted = {"da_dict_norm_fwd", "da_route_fwd", "da_attn_fwd", "da_gemm", "da_col_norm_max"}
-    n = 0
-    orig = _lib.call
-
-    def counting(name, *args):
-        nonlocal n
-        if name in counted:
-            n += 1
-        return orig(name, *args)
-
-    import double_attention_b200.ops as ops_mod
-
-    ops_mod.call = counting
-    try:
-        with torch.no_grad():
-            module(x)
-        torch.cuda.synchronize()
-    finally:
-        ops_mod.call = orig
-    return n
-
-
+# ----------------------------------------------------------------------------- CPU reference
 def cpu_reference(cfg, seconds: float, steps: int | None = None, warmup: int = 0):
-    """The reference algorithm (the CPU oracle restatement) on host cores."""
-    import oracle
-    from double_attention_b200 import SharedDictionaryAttention, experiment_config
+    """The reference algorithm (the fp32 CPU oracle restatement) on host cores, on a bounded sample.
 
-    torch.manual_seed(0)
-    module = SharedDictionaryAttention(experiment_config(cfg["preset"]))
-    params = {k: v.detach().float() for k, v in module.state_dict().items()}
-    x = make_input(cfg, seed=1).float()
+    Returns (tokens/s, threads, samples, sample batch, median seconds)."""
+    import oracle
+    from double_attention_b200 import experiment_config
+
     threads = torch.get_num_threads()
-    sample_batch = cfg["batch"]
-    if cfg["seq"] > 2048:  # bound the sample: one sequence, scaled by tokens
-        sample_batch = 1
-    xs = x[:sample_batch]
-    with torch.no_grad():
-        for _ in range(max(1, warmup)):
-            oracle.attention_forward(params, xs, module.config)
-        times = []
-        t_end = time.perf_counter() + seconds
-        while (steps is None and time.perf_counter() < t_end) or (steps is not None and len(times) < steps):
-            t0 = time.perf_counter()
-            oracle.attention_forward(params, xs, module.config)
-            times.append(time.perf_counter() - t0)
-            if steps is None and len(times) >= 1000:
-                break
+    seq = cfg["seq"]
+    sample_batch = 1 if (cfg["mode"] != "fwd" or seq > 2048) else cfg["batch"]
+    if cfg["kind"] == "lm":
+        from double_attention_b200 import DoubleAttentionLM
+
+        torch.manual_seed(0)
+        model = DoubleAttentionLM(cfg["vocab"], seq, experiment_config(cfg["preset"]), cfg["layers"],
+                                  dictionary_group_size=cfg["layers"], feedforward_dim=cfg["ffn"])
+        params = {k: v.detach().float().clone().requires_grad_() for k, v in model.named_parameters()}
+        state = {k: v.detach().float() for k, v in model.state_dict().items()}
+        opt = torch.optim.AdamW(params.values(), lr=3e-4)
+        ids = _token_ids(sample_batch, seq, cfg["vocab"], seed=2)
+
+        def one():
+            opt.zero_grad(set_to_none=True)
+            full = dict(state)
+            full.update(params)
+            full["lm_head.weight"] = full["token_embedding.weight"]
+            _, loss = oracle.lm_forward(full, ids[:, :-1], ids[:, 1:], model.stack.config, cfg["layers"],
+                                        cfg["layers"])
+            loss.backward()
+            opt.step()
+    else:
+        from double_attention_b200 import SharedDictionaryAttention
+
+        torch.manual_seed(0)
+        module = SharedDictionaryAttention(experiment_config(cfg["preset"]))
+        train = cfg["mode"] == "fwdbwd"
+        params = {k: v.detach().float().clone().requires_grad_(train) for k, v in module.state_dict().items()}
+        x = _seeded_normal((sample_batch, seq, 512), 1, torch.float32)
+        dy = _seeded_normal((sample_batch, seq, 512), 1000, torch.float32)
+
+        def one():
+            if train:
+                xr = x.clone().requires_grad_()
+                oracle.attention_forward(params, xr, module.config).backward(dy)
+            else:
+                with torch.no_grad():
+                    oracle.attention_forward(params, x, module.config)
+    for _ in range(max(1, warmup)):
+        one()
+    times = []
+    t_end = time.perf_counter() + seconds
+    while (steps is None and time.perf_counter() < t_end) or (steps is not None and len(times) < steps):
+        t0 = time.perf_counter()
+        one()
+        times.append(time.perf_counter() - t0)
+        if steps is None and len(times) >= 1000:
+            break
     sec = statistics.median(times)
-    tokens = sample_batch * cfg["seq"]
-    return tokens / sec, threads, len(times), sample_batch, sec
+    return sample_batch * seq / sec, threads, len(times), sample_batch, sec
+
+
+def _mode_words(cfg) -> str:
+    return {"fwd": "forward", "fwdbwd": "forward+backward", "train": "LM training step (fwd, bwd, AdamW)"}[cfg["mode"]]
 
 
 # ----------------------------------------------------------------------------- arms
@@ -296,7 +432,7 @@ def run_reference(args, cfg, world, rank):
     if rank != 0:
         return
     tps, threads, n, sb, sec = cpu_reference(cfg, args.cpu_seconds, steps=args.steps, warmup=args.warmup)
-    sample = (f"{n} steps of the fp32 CPU oracle forward on {sb}x{cfg['seq']} tokens "
+    sample = (f"{n} steps of the fp32 CPU oracle {_mode_words(cfg)} on {sb}x{cfg['seq']} tokens "
               f"(median {sec * 1e3:.1f} ms/step), tokens/s of that sample")
     line = {
         "impl": "reference",
@@ -308,12 +444,12 @@ def run_reference(args, cfg, world, rank):
         "warmup": args.warmup,
         "ms_per_step": sec * 1e3,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": cfg["scaling"],
         "vs_baseline": None,
         "dtype": "fp32",
         "data": "synthetic",
-        "config": {"workload": cfg["workload"], "preset": cfg["preset"], "batch_per_gpu": cfg["batch"],
-                   "seq_len": cfg["seq"], "parallelism": f"dp{args.gpus}", "device": "host cpu"},
+        "config": {"workload": cfg["workload"], "preset": cfg["preset"], "seq_len": cfg["seq"],
+                   "mode": cfg["mode"], "parallelism": f"dp{args.gpus}", "device": "host cpu"},
         "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -321,95 +457,72 @@ def run_reference(args, cfg, world, rank):
 
 
 def run_b200(args, cfg, world, rank, local):
+    from double_attention_b200 import _lib
+
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    module = build_module(cfg, device)
-    x_host = make_input(cfg, seed=1 + rank).pin_memory()
-    x = x_host.to(device)
-    y_host = torch.empty(cfg["batch"], cfg["seq"], 512, dtype=cfg["dtype"]).pin_memory()
+    work = make_workload(cfg, device, rank, world)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     stream = torch.cuda.current_stream(device)
-    tokens = cfg["batch"] * cfg["seq"]
 
     # --- device-resident step, captured in a CUDA graph when possible
+    for _ in range(args.warmup):
+        work.step()
+    torch.cuda.synchronize()
+    launches0 = _lib.kernel_launches()
+    work.step()
+    torch.cuda.synchronize()
+    launches_per_step = _lib.kernel_launches() - launches0
     graph = None
-    with torch.no_grad():
-        for _ in range(max(3, args.warmup)):
-            y = module(x)
-        torch.cuda.synchronize()
-        if not args.no_graph:
-            try:
-                side = torch.cuda.Stream(device)
-                side.wait_stream(stream)
-                with torch.cuda.stream(side):
-                    module(x)
-                stream.wait_stream(side)
-                graph = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(graph):
-                    y_graph = module(x)
-                graph.replay()
-                torch.cuda.synchronize()
-            except Exception as exc:  # graph capture is an optimisation only
-                print(f"[bench] CUDA graph capture failed ({exc}); timing eager launches", file=sys.stderr)
-                graph = None
-
-        def step():
-            if graph is not None:
-                graph.replay()
-            else:
-                module(x)
-
-        for _ in range(args.warmup):
-            step()
-        barrier(world)
-        torch.cuda.synchronize()
-        with ClockSampler(local) as clocks:
-            time.sleep(0.05)  # let the sampler take its first readings
-            times = time_steps(step, args.steps, flush, stream)
-        barrier(world)
-        torch.cuda.synchronize()
+    if work.capturable and not args.no_graph:
+        graph = capture(work.step, device, stream)
+    used_graph = graph is not None
+    step = graph.replay if used_graph else work.step
+    for _ in range(3):
+        step()
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        time.sleep(0.05)  # let the sampler take its first readings
+        times = time_steps(step, args.steps, flush, stream)
+    barrier(world)
+    torch.cuda.synchronize()
     ms = max_over_ranks(sum(times) / len(times), world)
-    value = tokens * world / (ms / 1e3)
+    value = work.tokens * world / (ms / 1e3)
 
-    # --- end to end through the public API: pinned host in, pinned host out
-    with torch.no_grad():
-        def e2e_step():
-            xd = x_host.to(device, non_blocking=True)
-            yd = module(xd)
-            y_host.copy_(yd, non_blocking=True)
-
-        for _ in range(args.warmup):
-            e2e_step()
-        barrier(world)
-        torch.cuda.synchronize()
-        e2e_times = time_steps(e2e_step, args.steps, flush, stream)
-        barrier(world)
+    # --- end to end through the public API: pinned host in, result back to pinned host
+    for _ in range(3):
+        work.e2e_step()
+    barrier(world)
+    torch.cuda.synchronize()
+    e2e_times = time_steps(work.e2e_step, args.steps, flush, stream)
+    barrier(world)
     e2e_ms = max_over_ranks(sum(e2e_times) / len(e2e_times), world)
-    e2e_value = tokens * world / (e2e_ms / 1e3)
-    h2d = x_host.numel() * x_host.element_size()
-    d2h = y_host.numel() * y_host.element_size()
+    e2e_value = work.tokens * world / (e2e_ms / 1e3)
+    h2d, d2h = work.h2d, work.d2h
 
-    launches = count_kernel_launches(module, x)
-
-    # --- roofline of the dominant kernel (rank 0 only; timed alone, L2 flushed)
+    # --- roofline of the dominant kernel (rank 0 only; each kernel timed alone, L2 flushed)
     roofline = cpu_base = None
     if rank == 0:
-        durations, flops = kernel_rooflines(module, cfg, x, flush, stream)
-        top = max(durations, key=durations.get)
+        del work, step, graph
+        torch.cuda.empty_cache()
+        kernels = kernel_rooflines(cfg, args.config, device)
+        top = max(kernels, key=lambda k: kernels[k][0])
         peak_tf, _hbm, peak_kind = load_peaks()
-        achieved = flops[top] / (durations[top] / 1e3) / 1e12
+        ms_top, flops_top = kernels[top]
+        achieved = flops_top / (ms_top / 1e3) / 1e12
         roofline = {
             "kernel": top, "bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
             "frac": achieved / peak_tf, "peak_source": f"{peak_kind} bf16 dense (burst)",
-            "flops_per_launch": flops[top], "ms_per_launch": durations[top],
+            "flops_per_launch": flops_top, "ms_per_launch": ms_top,
             "traffic": load_traffic(top, f"config{args.config}"),
-            "other_kernels": {k: {"ms": v, "tflops": flops[k] / (v / 1e3) / 1e12} for k, v in durations.items()
+            "other_kernels": {k: {"ms": v[0], "tflops": v[1] / (v[0] / 1e3) / 1e12} for k, v in kernels.items()
                               if k != top},
         }
         if world == 1:
             tps, threads, n, sb, sec = cpu_reference(cfg, args.cpu_seconds)
             cpu_base = {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port",
-                        "sample": f"{n} fp32 CPU oracle forwards of {sb}x{cfg['seq']} tokens in "
+                        "sample": f"{n} fp32 CPU oracle {_mode_words(cfg)} steps on {sb}x{cfg['seq']} tokens in "
                                   f"~{args.cpu_seconds:.0f} s (median {sec * 1e3:.1f} ms)"}
 
     clock_summary = clocks.summary()
@@ -423,22 +536,22 @@ def run_b200(args, cfg, world, rank, local):
             "warmup": args.warmup,
             "ms_per_step": ms,
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": cfg["scaling"],
             "vs_baseline": None,
             "dtype": "fp16" if cfg["dtype"] == torch.float16 else "bf16",
             "data": "synthetic",
             "config": {
-                "workload": cfg["workload"], "preset": cfg["preset"], "batch_per_gpu": cfg["batch"],
-                "global_batch": cfg["batch"] * world, "seq_len": cfg["seq"], "mode": cfg["mode"],
-                "parallelism": f"dp{world}", "l2": "flushed before every timed step (512 MiB write)",
-                "cuda_graph": graph is not None,
+                "workload": cfg["workload"], "preset": cfg["preset"],
+                "batch_per_gpu": per_rank_batch(cfg, world), "global_batch": per_rank_batch(cfg, world) * world,
+                "seq_len": cfg["seq"], "mode": cfg["mode"], "parallelism": f"dp{world}",
+                "l2": "flushed before every timed step (512 MiB write)", "cuda_graph": used_graph,
             },
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_ms},
             "roofline": roofline,
             "cpu_baseline": cpu_base,
             "clocks": clock_summary,
-            "gpu_launches": launches * args.steps,
+            "gpu_launches": launches_per_step * args.steps,
         }
         print(json.dumps(line), flush=True)
 

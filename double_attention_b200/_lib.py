@@ -94,6 +94,8 @@ def lib() -> ctypes.CDLL:
             handle.da_version.restype = ctypes.c_char_p
             handle.da_last_cuda_error.argtypes = []
             handle.da_last_cuda_error.restype = ctypes.c_int
+            handle.da_kernel_launches.argtypes = []
+            handle.da_kernel_launches.restype = ctypes.c_uint64
             _lib = handle
     return _lib
 
@@ -115,6 +117,11 @@ def check(name: str, status: int) -> None:
 
 def call(name: str, *args) -> None:
     check(name, getattr(lib(), name)(*args))
+
+
+def kernel_launches() -> int:
+    """Kernels launched by the library so far in this process."""
+    return int(lib().da_kernel_launches())
 
 
 def ptr(t: torch.Tensor | None) -> int | None:

@@ -822,6 +822,7 @@ int launch_pair(Kern kern, const Layout& L, int pairs, const CUtensorMap& tq, co
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   if (cudaLaunchKernelEx(&cfg, kern, tq, tk, tv, tdy, p) != cudaSuccess) return record_cuda_error();
+  note_launch();
   return DA_OK;
 }
 
@@ -847,6 +848,7 @@ extern "C" int da_attn_bwd_delta(const void* dy, const void* y, int64_t rows, in
     attn::bwd::delta_kernel<__half><<<grid, 32 * per_block, 0, st>>>(
         static_cast<const __half*>(dy), static_cast<const __half*>(y), rows, D, delta);
   if (cudaPeekAtLastError() != cudaSuccess) return record_cuda_error();
+  note_launch();
   return DA_OK;
 }
 

@@ -613,6 +613,7 @@ int launch(const AttnFwdArgs& a, cudaStream_t st) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   if (cudaLaunchKernelEx(&cfg, kern, tq, tk, tv, p) != cudaSuccess) return record_cuda_error();
+  note_launch();
   return DA_OK;
 }
 

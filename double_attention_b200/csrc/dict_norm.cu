@@ -163,6 +163,7 @@ extern "C" int da_dict_norm_fwd(const float* raw, int64_t R, int64_t M, float ep
     k<<<grid, block, smem, st>>>(raw, (int)R, (int)M, eps, (__half*)out, (__half*)out_t, denom, max_col_norm);
   }
   if (cudaPeekAtLastError() != cudaSuccess) return record_cuda_error();
+  note_launch();
   return DA_OK;
 }
 
@@ -181,6 +182,7 @@ extern "C" int da_dict_norm_bwd(const float* raw, const float* denom, const floa
   dict_norm_bwd_kernel<<<dim3((unsigned)((M + 31) / 32)), dim3(256), smem, st>>>(raw, denom, grad, grad_t, (int)R,
                                                                                   (int)M, eps, grad_raw, accumulate);
   if (cudaPeekAtLastError() != cudaSuccess) return record_cuda_error();
+  note_launch();
   return DA_OK;
 }
 
@@ -217,5 +219,6 @@ extern "C" int da_col_norm_max(const void* dict, int64_t R, int64_t M, int dtype
   else
     return DA_ERR_DTYPE;
   if (cudaPeekAtLastError() != cudaSuccess) return record_cuda_error();
+  note_launch();
   return DA_OK;
 }

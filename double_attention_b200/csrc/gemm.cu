@@ -188,6 +188,7 @@ int launch(const void* A, int64_t lda, const void* B, int64_t ldb, const Params&
   dim3 grid((unsigned)((p.M + kBM - 1) / kBM), (unsigned)((p.N + kN - 1) / kN), (unsigned)splits);
   kern<<<grid, kThreads, smem, st>>>(ta, tb, p);
   if (cudaPeekAtLastError() != cudaSuccess) return record_cuda_error();
+  note_launch();
   return DA_OK;
 }
 

@@ -1,6 +1,7 @@
 // Host helpers: error bookkeeping, tensor-map encoding, device attributes.
 #include "host_util.h"
 
+#include <atomic>
 #include <mutex>
 
 namespace da {
@@ -98,6 +99,15 @@ int sm_count() {
 }  // namespace da
 
 extern "C" int da_last_cuda_error(void) { return da::g_last_cuda_error; }
+
+namespace da {
+namespace {
+std::atomic<unsigned long long> g_kernel_launches{0};
+}  // namespace
+void note_launch() { g_kernel_launches.fetch_add(1, std::memory_order_relaxed); }
+}  // namespace da
+
+extern "C" uint64_t da_kernel_launches(void) { return da::g_kernel_launches.load(std::memory_order_relaxed); }
 
 extern "C" int da_set_debug_trace(int* host_mapped) {
   da::set_debug_trace(host_mapped);

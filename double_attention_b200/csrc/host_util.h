@@ -37,4 +37,7 @@ int bind_device(const void* ptr);
 // Number of SMs of the current device (cached per device).
 int sm_count();
 
+// Count one kernel launched by this library (process-wide counter).
+void note_launch();
+
 }  // namespace da

@@ -540,6 +540,7 @@ int launch(const RouteBwdArgs& a, cudaStream_t st) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   if (cudaLaunchKernelEx(&cfg, kern, tq, tdk, tdv, p) != cudaSuccess) return record_cuda_error();
+  note_launch();
   return DA_OK;
 }
 

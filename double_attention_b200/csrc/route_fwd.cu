@@ -572,6 +572,7 @@ int launch_fwd(const RouteFwdArgs& a, cudaStream_t st) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   if (cudaLaunchKernelEx(&cfg, kern, tq, tdk, tdv, p) != cudaSuccess) return record_cuda_error();
+  note_launch();
   return DA_OK;
 }
 

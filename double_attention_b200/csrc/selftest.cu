@@ -145,6 +145,7 @@ int launch_selftest(const void* A, const void* B, int K, float* D, int* status, 
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   if (cudaLaunchKernelEx(&cfg, kern, ta, tb, K, D, status) != cudaSuccess) return record_cuda_error();
+  note_launch();
   return DA_OK;
 }
 

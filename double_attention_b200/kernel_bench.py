@@ -33,6 +33,9 @@ SHAPES = {
 }
 
 
+KERNELS = ("route", "attention", "route_bwd", "dict_grads", "attention_bwd", "projection")
+
+
 class _Cfg:
     def __init__(self, maps: int) -> None:
         self.outer_maps = maps
@@ -69,6 +72,62 @@ def make_case(kernel: str, config: int, device: torch.device):
             ops.routed_attention_mixed(routed, value, scales, mix, c)
 
         return run, float(batch) * seq * seq * (cfg.outer_maps * r + d)
+    if kernel == "route_bwd":  # the fused route backward kernel alone (da_route_bwd)
+        proj = torch.randn(batch * seq, 2 * h * r, generator=g).to(dtype).to(device)
+        dk = F.normalize(torch.randn(r, m, generator=g), dim=0).to(dtype).to(device)
+        dv = F.normalize(torch.randn(r, m, generator=g), dim=0).to(dtype).to(device)
+        views = ops.dictionary_views_from_normalized(dk, dv, dtype)
+        beta = torch.tensor(cfg.beta, device=device)
+        rows, groups = batch * seq, 2 * h
+        z, lse, onorm = ops._route_forward(proj, rows, groups, r, views, beta, cfg.eps, True, True)
+        dz = torch.randn(groups, rows, r, generator=g).to(dtype).to(device)
+        dq = torch.empty_like(proj)
+        p_out = torch.empty(groups, rows, m, dtype=torch.bfloat16, device=device)
+        dl_out = torch.empty(groups, rows, m, dtype=dtype, device=device)
+        g_out = torch.empty(groups, rows, r, dtype=torch.bfloat16, device=device)
+        dbeta = torch.zeros(1, device=device)
+        ws = ops.workspace(device)
+        beta32 = beta.float().reshape(1)
+
+        def run():
+            ops.call("da_route_bwd", proj.data_ptr(), rows, proj.shape[1], proj.stride(0), groups, r, r, m,
+                     ops.dtype_code(dtype), views.key_t.data_ptr(), views.value_t.data_ptr(), beta32.data_ptr(),
+                     cfg.eps, 1, 1, z.data_ptr(), dz.data_ptr(), lse.data_ptr(), onorm.data_ptr(), dq.data_ptr(),
+                     p_out.data_ptr(), dl_out.data_ptr(), g_out.data_ptr(), dbeta.data_ptr(),
+                     ws.status.data_ptr(), ops.stream_ptr(device))
+
+        # dP and dq_hat (the dictionary-gradient GEMMs are timed as "dict_grads")
+        return run, 4.0 * r * m * groups * rows
+    if kernel == "dict_grads":  # dDk and dDv split-K GEMMs over all route rows
+        rows, groups = batch * seq, 2 * h
+        proj = torch.randn(rows, 2 * h * r, generator=g).to(dtype).to(device)
+        dl_out = (torch.randn(groups, rows, m, generator=g) * 1e-2).to(dtype).to(device)
+        p_out = torch.rand(groups, rows, m, generator=g).to(torch.bfloat16).to(device)
+        g_out = torch.randn(groups, rows, r, generator=g).to(torch.bfloat16).to(device)
+        d_key = torch.zeros(r, m, device=device)
+        d_value = torch.zeros(r, m, device=device)
+
+        def run():
+            for gi in range(groups):
+                ops.gemm_splitk(proj[:, gi * r:], proj.stride(0), True, dl_out[gi], m, True, r, m, rows, d_key)
+            ops.gemm_splitk(g_out.view(-1, r), r, True, p_out.view(-1, m), m, True, r, m, groups * rows, d_value)
+
+        return run, 4.0 * r * m * groups * rows
+    if kernel == "attention_bwd":  # the whole attention backward op (delta passes, dQ, dK/dV launches)
+        routed = F.normalize(torch.randn(2, h, batch, seq, r, generator=g), dim=-1).to(dtype).to(device)
+        routed.requires_grad_()
+        value = torch.randn(batch, seq, d, generator=g).to(dtype).to(device).requires_grad_()
+        scales = torch.full((cfg.outer_maps,), cfg.initial_score_scale, device=device, requires_grad=True)
+        mix = (torch.full((cfg.outer_maps,), 1.0 / cfg.outer_maps, device=device, requires_grad=True)
+               if cfg.outer_maps > 1 else None)
+        dy = torch.randn(batch, seq, d, generator=g).to(dtype).to(device)
+        y = ops.routed_attention_mixed(routed, value, scales, mix, _Cfg(cfg.outer_maps))
+        inputs = [t for t in (routed, value, scales, mix) if t is not None]
+
+        def run():
+            torch.autograd.grad(y, inputs, dy, retain_graph=True)
+
+        return run, float(batch) * seq * seq * (2 * cfg.outer_maps * r + 2 * d)
     if kernel == "projection":
         x = torch.randn(batch * seq, d, generator=g).to(dtype).to(device)
         w = (torch.randn(2 * h * r, d, generator=g) * d**-0.5).to(dtype).to(device)
@@ -89,19 +148,24 @@ def time_kernel(run, reps: int, device: torch.device) -> float:
         run()
     # capture the launch in a CUDA graph so host overhead cannot leak into the timing
     graph = torch.cuda.CUDAGraph()
-    side = torch.cuda.Stream(device)
-    side.wait_stream(stream)
-    with torch.cuda.stream(side):
-        run()
-    stream.wait_stream(side)
-    with torch.cuda.graph(graph):
-        run()
+    try:
+        side = torch.cuda.Stream(device)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            run()
+        stream.wait_stream(side)
+        with torch.cuda.graph(graph):
+            run()
+        launch = graph.replay
+    except RuntimeError:  # not capturable: time eager launches (host overhead included)
+        torch.cuda.synchronize()
+        launch = run
     events = []
     for _ in range(reps):
         flush.zero_()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record(stream)
-        graph.replay()
+        launch()
         e.record(stream)
         events.append((s, e))
     torch.cuda.synchronize()
@@ -110,7 +174,7 @@ def time_kernel(run, reps: int, device: torch.device) -> float:
 
 def main(argv=None) -> int:
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    p.add_argument("--kernel", choices=("route", "attention", "projection"), required=True)
+    p.add_argument("--kernel", choices=KERNELS, required=True)
     p.add_argument("--config", type=int, choices=sorted(SHAPES), default=2)
     p.add_argument("--reps", type=int, default=3)
     p.add_argument("--time", action="store_true")

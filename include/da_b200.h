@@ -46,6 +46,9 @@ DA_API const char* da_version(void);
 DA_API const char* da_status_string(int status);
 /* Last CUDA error code recorded by a call on this host thread. */
 DA_API int da_last_cuda_error(void);
+/* Number of kernels this library has launched in this process (all devices,
+ * all threads); a diagnostic for counting launches around a region. */
+DA_API uint64_t da_kernel_launches(void);
 
 /* Debug aid with no reference counterpart: pinned, device-accessible host
  * memory (8 ints per CTA) into which kernels write progress markers, or

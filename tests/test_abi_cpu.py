@@ -33,11 +33,12 @@ def test_library_loads_and_exports_every_declared_symbol() -> None:
         assert hasattr(handle, name), name
     assert b"sm_100a" in handle.da_version()
     assert handle.da_status_string(_lib.DA_ERR_SHAPE) == b"unsupported or inconsistent shape"
+    assert _lib.kernel_launches() >= 0
 
 
 def test_bound_signatures_cover_compute_entry_points() -> None:
     for name in declared_symbols():
-        if name in ("da_version", "da_status_string", "da_last_cuda_error"):
+        if name in ("da_version", "da_status_string", "da_last_cuda_error", "da_kernel_launches"):
             continue
         assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
 
