@@ -159,9 +159,10 @@ DA_DEV void trace_at(int* trace, int index) {
   }
 }
 
-// Records the low 32 bits of %globaltimer (ns) in the trace slot.
+// Records the low 31 bits of %globaltimer (ns) in the trace slot (plain
+// store, read after the kernel completed).
 DA_DEV void trace_time(int* trace, int slot) {
-  if (trace) trace_mark(trace, slot, static_cast<int>(globaltimer() & 0x7fffffffull));
+  if (trace) trace_at(trace, blockIdx.x * 8 + slot);
 }
 
 // ---------------------------------------------------------------- TMA

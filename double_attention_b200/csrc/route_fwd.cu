@@ -189,6 +189,9 @@ __global__ void __launch_bounds__(192, 1) route_fwd_kernel(const __grid_constant
   const int g = pair / tiles_per_group;
   const int row0 = (pair % tiles_per_group) * 128;  // first row of the pair inside the group
   const int NJ = p.M / C::kNA;
+  // Pairs start at different atom tiles (and wrap around), so the CTAs of a
+  // wave do not all read the same dictionary lines from L2 at once.
+  const int rot = pair % NJ;
   Abort ab{&abort_flag, p.status};
   if (threadIdx.x == 0) trace_time(p.trace, 0);
   // fine post-mortem timeline of the first pair: 1024 ints per CTA after the 8-int slots
@@ -242,11 +245,12 @@ __global__ void __launch_bounds__(192, 1) route_fwd_kernel(const __grid_constant
         const int s = j % C::kStages;
         const uint32_t ph = (j / C::kStages) & 1u;
         if (!mbar_wait(&dk_empty[s], ph ^ 1u, ab, 11)) break;
+        trace_at(ft, 700 + j);
         if (rank == 0) mbar_arrive_expect_tx(&dk_full[s], 2 * C::kDkBytes);
         const uint32_t kf = mapa_shared(smem_u32(&dk_full[s]), 0);
         for (int kb = 0; kb < kR / 64; ++kb)
           tma_load_2d_pair(&tdk, kf, smem + C::kOffDk + s * C::kDkBytes + kb * ((C::kNA / 2) * 128), kb * 64,
-                           j * C::kNA + (C::kNA / 2) * (int)rank);
+                           ((j + rot) % NJ) * C::kNA + (C::kNA / 2) * (int)rank);
         dk_issued = j + 1;
       }
       if (rank == 0) {  // drain: the leader's barriers count both CTAs' bytes
@@ -264,7 +268,7 @@ __global__ void __launch_bounds__(192, 1) route_fwd_kernel(const __grid_constant
         if (rank == 0) mbar_arrive_expect_tx(&dv_full[s], 2 * C::kDvBytes);
         const uint32_t vf = mapa_shared(smem_u32(&dv_full[s]), 0);
         for (int i = 0; i < C::kPV; ++i)
-          tma_load_2d_pair(&tdv, vf, smem + C::kOffDv + s * C::kDvBytes + i * ((C::kNc / 2) * 128), j * C::kNA,
+          tma_load_2d_pair(&tdv, vf, smem + C::kOffDv + s * C::kDvBytes + i * ((C::kNc / 2) * 128), ((j + rot) % NJ) * C::kNA,
                            i * C::kNc + (C::kNc / 2) * (int)rank);
         dv_issued = j + 1;
       }
@@ -288,6 +292,7 @@ __global__ void __launch_bounds__(192, 1) route_fwd_kernel(const __grid_constant
         trace_at(ft, 100 + 2 * j);
         if (j >= C::kB && !mbar_wait(&p_full[sb], ((j - C::kB) / C::kB) & 1u, ab, 22)) return false;
         if (!mbar_wait(&dk_full[s], (j / C::kStages) & 1u, ab, 23)) return false;
+        trace_at(ft, 600 + j);
         tc_fence_after();
         const uint32_t qa = smem_u32(smem + C::kOffQ), ka = smem_u32(smem + C::kOffDk + s * C::kDkBytes);
 #pragma unroll 4
@@ -397,9 +402,11 @@ __global__ void __launch_bounds__(192, 1) route_fwd_kernel(const __grid_constant
         for (int i = 0; i < 32; i += 2) {
           const float a = v[i] * scale, b = v[i + 1] * scale;
           if (want_argmax) {
-            const int base = j * C::kNA + half * 32 + i;
-            if (a > mx) amax = base;
-            if (b > fmaxf(mx, a)) amax = base + 1;
+            // first index of the maximum, whatever order the tiles were visited in
+            const int base = ((j + rot) % NJ) * C::kNA + half * 32 + i;
+            if (a > mx || (a == mx && base < amax)) amax = base;
+            const float ma = fmaxf(mx, a);
+            if (b > ma || (b == ma && base + 1 < amax)) amax = base + 1;
           }
           mx = fmaxf(mx, fmaxf(a, b));
           const float ea = ex2(a - bound), eb = ex2(b - bound);
@@ -436,12 +443,12 @@ __global__ void __launch_bounds__(192, 1) route_fwd_kernel(const __grid_constant
     const float mx_other = red[128 + (l ^ 64)];
     const float mx_all = fmaxf(mx, mx_other);
     named_bar_sync(1, 128);
-    // argmax: the half holding the larger maximum wins (ties: lower index = half 0)
+    // argmax: the half holding the larger maximum wins (ties: the lower index)
     int* ired = reinterpret_cast<int*>(red);
     ired[l] = amax;
     named_bar_sync(1, 128);
     const int amax_other = ired[l ^ 64];
-    const int amax_all = (mx > mx_other || (mx == mx_other && half == 0)) ? amax : amax_other;
+    const int amax_all = mx > mx_other ? amax : (mx < mx_other ? amax_other : min(amax, amax_other));
     named_bar_sync(1, 128);
     tc_fence_after();
     float ss = 0.f;
@@ -519,6 +526,416 @@ __global__ void __launch_bounds__(192, 1) route_fwd_kernel(const __grid_constant
   if (threadIdx.x == 0) trace_time(p.trace, 7);
 }
 
+// ============================================================================
+// Wide-tile variant (R = 128 / 256 / 512, M a multiple of 128).
+//
+// The paired MMA only reaches full rate with N = 256 (each instruction costs
+// ~46 cycles to issue whatever its N), and the 64-atom tiles above issue 16
+// small score instructions per tile.  Here a pair scores 128 or 256 atoms per
+// tile (N = nk) with the key rows streamed as 64-column K chunks through one
+// ring and the value rows as 64-atom K chunks through another, exactly like
+// the outer attention's single-map kernel; the epilogue (statistics, output
+// normalisation, exact repair of low-mass rows) is the one above.
+struct WideLayout {
+  int nk, kchunks, nc, npv;
+  int q_bytes, k_stage, v_stage, p_bytes;
+  int nks, nvs, nsb, npb;
+  int off_q, off_k, off_v, off_p, off_red, smem;
+  int tmem_s, s_cols, tmem_cols;
+};
+
+constexpr int kWideMaxK = 8, kWideMaxV = 4, kWideMaxSB = 4, kWideMaxPB = 2;
+
+__host__ __device__ inline WideLayout wide_layout(int R, int M) {
+  WideLayout L;
+  L.kchunks = R / 64;
+  L.nc = R < 256 ? R : 256;
+  L.npv = R / L.nc;
+  L.q_bytes = 64 * R * 2;
+  L.v_stage = (R / 2) * 128;  // this CTA's R/2 value rows x 64 atoms
+  const int red = 2 * 128 * 4;
+  const int avail = 225 * 1024;
+  L.nk = 0;
+  for (int nk = (M % 256 == 0) ? 256 : 128; nk >= 128 && L.nk == 0; nk -= 128) {
+    if (M % nk) continue;
+    for (int npb = 2; npb >= 1 && L.nk == 0; --npb) {
+      const int k_stage = (nk / 2) * 128, p_bytes = 64 * nk * 2;
+      const int rest = avail - L.q_bytes - npb * p_bytes - 2 * L.v_stage - red;
+      if (rest >= 3 * k_stage) {
+        L.nk = nk;
+        L.k_stage = k_stage;
+        L.p_bytes = p_bytes;
+        L.npb = npb;
+        L.nvs = 2;
+        L.nks = rest / k_stage > kWideMaxK ? kWideMaxK : rest / k_stage;
+      }
+    }
+  }
+  if (L.nk == 0) {
+    L.nk = 0;  // caller falls back to the 64-atom kernel
+    L.nks = 0;
+    L.smem = 0;
+    return L;
+  }
+  L.s_cols = L.nk / 2;
+  L.tmem_s = R / 2;
+  const int nsb = (512 - R / 2) / L.s_cols;
+  L.nsb = nsb > kWideMaxSB ? kWideMaxSB : nsb;
+  L.off_q = 0;
+  L.off_k = L.off_q + L.q_bytes;
+  L.off_v = L.off_k + L.nks * L.k_stage;
+  L.off_p = L.off_v + L.nvs * L.v_stage;
+  L.off_red = L.off_p + L.npb * L.p_bytes;
+  const int used = L.off_red + red;
+  L.smem = used < 120 * 1024 ? 120 * 1024 : used;  // one CTA per SM
+  const int cols = R / 2 + L.nsb * L.s_cols;
+  L.tmem_cols = cols <= 128 ? 128 : (cols <= 256 ? 256 : 512);
+  return L;
+}
+
+template <int kR, typename T>
+__global__ void __launch_bounds__(192, 1) route_fwd_wide_kernel(const __grid_constant__ CUtensorMap tq,
+                                                                const __grid_constant__ CUtensorMap tdk,
+                                                                const __grid_constant__ CUtensorMap tdv,
+                                                                const FwdParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t q_full, o_full;
+  __shared__ uint64_t k_full[kWideMaxK], k_empty[kWideMaxK], v_full[kWideMaxV], v_empty[kWideMaxV];
+  __shared__ uint64_t s_full[kWideMaxSB], p_full[kWideMaxSB], p_empty[kWideMaxPB];
+  __shared__ uint32_t tmem_base;
+  __shared__ int abort_flag, is_last;
+
+  const WideLayout L = wide_layout(kR, p.M);
+  constexpr int kRows = 64;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_ctarank() & 1u;
+  const int pair = blockIdx.x / 2;
+  const int tiles_per_group = (p.rows + 127) / 128;
+  const int g = pair / tiles_per_group;
+  const int row0 = (pair % tiles_per_group) * 128;
+  const int nk = L.nk;
+  const int NJ = p.M / nk;
+  const int rot = pair % NJ;  // pairs start at different atom tiles
+  Abort ab{&abort_flag, p.status};
+  if (threadIdx.x == 0) trace_time(p.trace, 0);
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    mbar_init(&q_full, 1);
+    mbar_init(&o_full, 1);
+    for (int i = 0; i < kWideMaxK; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < kWideMaxV; ++i) {
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
+    for (int i = 0; i < kWideMaxSB; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 2);
+    }
+    for (int i = 0; i < kWideMaxPB; ++i) mbar_init(&p_empty[i], 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc<2>(&tmem_base, L.tmem_cols);
+    tmem_relinquish<2>();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+  if (threadIdx.x == 0) trace_time(p.trace, 1);
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producers (both CTAs)
+    if (lane == 0) {  // q rows, then key rows in 64-column K chunks
+      prefetch_tmap(&tq);
+      prefetch_tmap(&tdk);
+      if (rank == 0) mbar_arrive_expect_tx(&q_full, 2 * L.q_bytes);
+      const uint32_t qf = mapa_shared(smem_u32(&q_full), 0);
+      const int qrow = min(row0 + 64 * (int)rank, p.rows - 1);  // boxes never start outside the matrix
+      for (int kb = 0; kb < kR / 64; ++kb)
+        tma_load_2d_pair(&tq, qf, smem + L.off_q + kb * (kRows * 128), g * p.col_stride + kb * 64, qrow);
+      int kc = 0;
+      bool ok = true;
+      for (int j = 0; ok && j < NJ; ++j) {
+        const int jj = (j + rot) % NJ;
+        for (int c = 0; c < L.kchunks; ++c, ++kc) {
+          const int st = kc % L.nks;
+          if (!mbar_wait(&k_empty[st], ((kc / L.nks) & 1u) ^ 1u, ab, 11)) { ok = false; break; }
+          if (rank == 0) mbar_arrive_expect_tx(&k_full[st], 2 * L.k_stage);
+          tma_load_2d_pair(&tdk, mapa_shared(smem_u32(&k_full[st]), 0), smem + L.off_k + st * L.k_stage, c * 64,
+                           jj * nk + (int)rank * (nk / 2));
+        }
+      }
+      if (rank == 0) {  // drain: no TMA may be in flight at teardown
+        mbar_wait_drain(&q_full, 0);
+        for (int c = (kc > L.nks ? kc - L.nks : 0); c < kc; ++c)
+          mbar_wait_drain(&k_full[c % L.nks], (c / L.nks) & 1u);
+      }
+    } else if (lane == 1) {  // value rows (this CTA's R/2 slice of every N block) in 64-atom K chunks
+      prefetch_tmap(&tdv);
+      int vc = 0;
+      bool ok = true;
+      for (int j = 0; ok && j < NJ; ++j) {
+        const int jj = (j + rot) % NJ;
+        for (int c = 0; c < nk / 64; ++c, ++vc) {
+          const int st = vc % L.nvs;
+          if (!mbar_wait(&v_empty[st], ((vc / L.nvs) & 1u) ^ 1u, ab, 12)) { ok = false; break; }
+          if (rank == 0) mbar_arrive_expect_tx(&v_full[st], 2 * L.v_stage);
+          const uint32_t vf = mapa_shared(smem_u32(&v_full[st]), 0);
+          for (int i = 0; i < L.npv; ++i)
+            tma_load_2d_pair(&tdv, vf, smem + L.off_v + st * L.v_stage + i * ((L.nc / 2) * 128), jj * nk + c * 64,
+                             i * L.nc + (int)rank * (L.nc / 2));
+        }
+      }
+      if (rank == 0)
+        for (int c = (vc > L.nvs ? vc - L.nvs : 0); c < vc; ++c)
+          mbar_wait_drain(&v_full[c % L.nvs], (c / L.nvs) & 1u);
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer (leader)
+    if (rank == 0 && lane == 0) {
+      const uint32_t idesc_s = idesc_f16(128, nk, std::is_same<T, __nv_bfloat16>::value, false, false);
+      const uint32_t idesc_o = idesc_f16(128, L.nc, true, false, false);  // Dv rows are K-major (atoms contiguous)
+      auto commit_both = [&](uint64_t* bar) {
+        mma_commit<2>(smem_u32(bar));
+        mma_commit<2>(mapa_shared(smem_u32(bar), 1));
+      };
+      const uint32_t qa = smem_u32(smem + L.off_q);
+      int kc = 0, vc = 0;
+      auto issue_s = [&](int j) -> bool {
+        const int sb = j % L.nsb;
+        if (j >= L.nsb && !mbar_wait(&p_full[sb], ((j - L.nsb) / L.nsb) & 1u, ab, 22)) return false;
+        const uint32_t d = tmem + L.tmem_s + (uint32_t)(sb * L.s_cols);
+        for (int c = 0; c < L.kchunks; ++c, ++kc) {
+          const int st = kc % L.nks;
+          if (!mbar_wait(&k_full[st], (kc / L.nks) & 1u, ab, 23)) return false;
+          tc_fence_after();
+          const uint64_t ad0 = sdesc_sw128(qa + c * (kRows * 128), 16, 1024);
+          const uint64_t bd0 = sdesc_sw128(smem_u32(smem + L.off_k + st * L.k_stage), 16, 1024);
+#pragma unroll
+          for (int kin = 0; kin < 4; ++kin)  // +32 B per K step of 16 = +2 in the encoded address
+            mma_f16_ss<2>(d, ad0 + 2 * kin, bd0 + 2 * kin, idesc_s, (c | kin) ? 1u : 0u);
+          commit_both(&k_empty[st]);
+        }
+        commit_both(&s_full[sb]);
+        return true;
+      };
+      auto issue_pv = [&](int j) -> bool {
+        const int pb = j % L.npb;
+        if (!mbar_wait(&p_full[j % L.nsb], (j / L.nsb) & 1u, ab, 24)) return false;
+        const uint32_t pa = smem_u32(smem + L.off_p + pb * L.p_bytes);
+        for (int c = 0; c < nk / 64; ++c, ++vc) {
+          const int st = vc % L.nvs;
+          if (!mbar_wait(&v_full[st], (vc / L.nvs) & 1u, ab, 25)) return false;
+          tc_fence_after();
+          const uint32_t va = smem_u32(smem + L.off_v + st * L.v_stage);
+          const uint64_t ad0 = sdesc_sw128(pa + c * (kRows * 128), 16, 1024);
+          for (int i = 0; i < L.npv; ++i) {
+            const uint64_t bd0 = sdesc_sw128(va + i * ((L.nc / 2) * 128), 16, 1024);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              mma_f16_ss<2>(tmem + (uint32_t)(i * (L.nc / 2)), ad0 + 2 * kk, bd0 + 2 * kk, idesc_o,
+                            (j | c | kk) ? 1u : 0u);
+          }
+          commit_both(&v_empty[st]);
+        }
+        commit_both(&p_empty[pb]);
+        return true;
+      };
+      bool ok = mbar_wait(&q_full, 0, ab, 21);
+      trace_time(p.trace, 2);
+      tc_fence_after();
+      int next_s = 0;  // scores run up to nsb tiles ahead of the probability products
+      for (int j = 0; ok && j < NJ; ++j) {
+        while (ok && next_s < NJ && next_s < j + L.nsb) ok = issue_s(next_s++);
+        if (ok) ok = issue_pv(j);
+      }
+      commit_both(&o_full);
+      trace_time(p.trace, 3);
+      mbar_wait_drain(&o_full, 0);
+    }
+  } else {
+    // ---------------------------------------------------------------- softmax + epilogue (warps 2..5)
+    const int quad = warp & 3;
+    const int l = quad * 32 + lane;
+    const int r = l & 63, half = l >> 6;
+    const int grow = row0 + 64 * (int)rank + r;
+    const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+    float* red = reinterpret_cast<float*>(smem + L.off_red);
+    const uint32_t pf_leader = mapa_shared(smem_u32(&p_full[0]), 0);
+    const bool arriver = (warp == 2 && lane == 0);
+    const int hc = nk / 2;  // atoms of a tile per thread
+
+    bool ok = mbar_wait(&s_full[0], 0, ab, 31);  // S_0 complete: the q tile has landed
+    if (arriver) trace_time(p.trace, 4);
+    float qn2 = 0.f;
+    if (ok) {
+      const uint32_t qa = smem_u32(smem + L.off_q);
+      for (int kb = 0; kb < kR / 64; ++kb)
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const uint4 v = ld_shared_v4(qa + kb * (kRows * 128) + sw128_offset(r, c));
+          const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = unpack2<T>(w[e]);
+            qn2 = fmaf(f.x, f.x, fmaf(f.y, f.y, qn2));
+          }
+        }
+    }
+    const float beta = *p.beta;
+    const float qn = sqrtf(qn2);
+    const float invn = p.normalize_input ? 1.f / fmaxf(qn, p.eps) : 1.f;
+    const float kLog2e = 1.4426950408889634f;
+    const float scale = beta * invn * kLog2e;
+    const float bound = beta * qn * invn * (*p.dk_max) * kLog2e;
+    float sum = 0.f, mx = -INFINITY;
+    int amax = 0;
+    const bool want_argmax = p.argmax != nullptr;
+
+    for (int j = 0; j < NJ; ++j) {
+      const int sb = j % L.nsb, pb = j % L.npb;
+      const int jj = (j + rot) % NJ;
+      if (ok && j > 0) ok = mbar_wait(&s_full[sb], (j / L.nsb) & 1u, ab, 32);
+      if (ok && j >= L.npb) ok = mbar_wait(&p_empty[pb], ((j - L.npb) / L.npb) & 1u, ab, 33);
+      ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-collective
+      if (ok) {
+        tc_fence_after();
+        const uint32_t pa = smem_u32(smem + L.off_p + pb * L.p_bytes);
+        for (int ch = 0; ch < hc / 32; ++ch) {
+          float v[32];
+          tmem_ld32(tmem + lane_base + L.tmem_s + (uint32_t)(sb * L.s_cols + ch * 32), v);
+          tmem_wait_ld();
+          const int kc = half * hc + ch * 32;  // atom column inside the tile
+          uint32_t packed[16];
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            const float a = v[i] * scale, b = v[i + 1] * scale;
+            if (want_argmax) {  // first index of the maximum, whatever the visiting order
+              const int base = jj * nk + kc + i;
+              if (a > mx || (a == mx && base < amax)) amax = base;
+              const float ma = fmaxf(mx, a);
+              if (b > ma || (b == ma && base + 1 < amax)) amax = base + 1;
+            }
+            mx = fmaxf(mx, fmaxf(a, b));
+            const float ea = ex2(a - bound), eb = ex2(b - bound);
+            sum += ea + eb;
+            packed[i / 2] = pack_bf16x2(ea, eb);
+          }
+          const uint32_t box = pa + (kc >> 6) * (kRows * 128);
+          const int cb = (kc & 63) >> 3;
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            st_shared_v4(box + sw128_offset(r, cb + e), packed[4 * e], packed[4 * e + 1], packed[4 * e + 2],
+                         packed[4 * e + 3]);
+        }
+        fence_proxy_async();
+      }
+      tc_fence_before();
+      named_bar_sync(1, 128);
+      if (arriver) mbar_arrive_cluster(pf_leader + sb * 8);
+    }
+
+    // ---- epilogue: combine the two column halves of each row, normalise, store.
+    if (arriver) trace_time(p.trace, 5);
+    if (ok) ok = mbar_wait(&o_full, 0, ab, 34);
+    if (arriver) trace_time(p.trace, 6);
+    ok = __all_sync(0xffffffffu, ok);
+    red[l] = sum;
+    red[128 + l] = mx;
+    named_bar_sync(1, 128);
+    const float sum_all = sum + red[l ^ 64];
+    const float mx_other = red[128 + (l ^ 64)];
+    const float mx_all = fmaxf(mx, mx_other);
+    named_bar_sync(1, 128);
+    int* ired = reinterpret_cast<int*>(red);
+    ired[l] = amax;
+    named_bar_sync(1, 128);
+    const int amax_other = ired[l ^ 64];
+    const int amax_all = mx > mx_other ? amax : (mx < mx_other ? amax_other : min(amax, amax_other));
+    named_bar_sync(1, 128);
+    tc_fence_after();
+    float ss = 0.f;
+    if (ok) {
+      for (int i = 0; i < L.npv; ++i)
+        for (int c = 0; c < L.nc / 2; c += 32) {
+          float v[32];
+          tmem_ld32(tmem + lane_base + (uint32_t)(i * (L.nc / 2) + c), v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) ss = fmaf(v[e], v[e], ss);
+        }
+    }
+    red[l] = ss;
+    named_bar_sync(1, 128);
+    const float ss_all = ss + red[l ^ 64];
+    const float onorm = sqrtf(ss_all);  // ||o|| where o = sum_all * r
+    const float factor = p.normalize_output ? 1.f / fmaxf(onorm, p.eps * sum_all) : 1.f / sum_all;
+    const bool live = grow < p.rows;
+    if (ok) {  // warp-uniform: every lane loads, only rows that exist are stored
+      T* zrow = reinterpret_cast<T*>(p.z) + ((size_t)g * p.rows + (live ? grow : 0)) * kR;
+      for (int i = 0; i < L.npv; ++i) {
+        const int col0 = i * L.nc + half * (L.nc / 2);
+        for (int c = 0; c < L.nc / 2; c += 32) {
+          float v[32];
+          tmem_ld32(tmem + lane_base + (uint32_t)(i * (L.nc / 2) + c), v);
+          tmem_wait_ld();
+          if (live) {
+            uint32_t w[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) w[e] = pack2<T>(v[2 * e] * factor, v[2 * e + 1] * factor);
+            uint4* dst = reinterpret_cast<uint4*>(zrow + col0 + c);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) dst[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
+          }
+        }
+      }
+    }
+    if (ok && live && half == 0) {
+      const size_t idx = (size_t)g * p.rows + grow;
+      const float kLn2 = 0.6931471805599453f;
+      p.lse[idx] = (bound + log2f(sum_all)) * kLn2;
+      p.out_norm[idx] = onorm / sum_all;
+      if (want_argmax) p.argmax[idx] = amax_all;
+      if (mx_all - bound < -100.f || !(sum_all > 0.f)) {
+        const int slot = atomicAdd(&p.work[1], 1);
+        if (slot < p.repair_cap) p.work[2 + slot] = (int)idx;
+        else atomicOr(p.status, DA_DEV_ROW_OVERFLOW);
+        __threadfence();  // the listed row is visible before this CTA takes its ticket
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  if (warp == 1) tmem_dealloc<2>(tmem, L.tmem_cols);
+
+  // The last CTA to finish repairs the listed rows and resets the counters.
+  if (threadIdx.x == 0) {
+    __threadfence();
+    is_last = atomicAdd(&p.work[0], 1) == (int)gridDim.x - 1;
+  }
+  __syncthreads();
+  if (is_last) {
+    __threadfence();
+    repair_listed_rows<kR, T>(p, reinterpret_cast<float*>(smem));
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      p.work[1] = 0;
+      p.work[0] = 0;
+      __threadfence();
+    }
+  }
+  if (threadIdx.x == 0) trace_time(p.trace, 7);
+}
+
 template <int kR, typename T>
 int launch_fwd(const RouteFwdArgs& a, cudaStream_t st) {
   using C = FwdCfg<kR>;
@@ -554,8 +971,17 @@ int launch_fwd(const RouteFwdArgs& a, cudaStream_t st) {
   p.repair_cap = a.repair_cap;
   p.status = a.status;
   p.trace = debug_trace();
-  auto kern = route_fwd_kernel<kR, T>;
-  const int smem = C::kSmem + 1024;
+  const WideLayout W = wide_layout(kR, (int)a.M);
+  const bool wide = kR >= 128 && W.nk != 0 && W.nks >= 3 && W.nsb >= 2;
+  if (wide) {  // re-encode the key / value maps with the wide tile's boxes
+    rc = make_tmap_2d(&tdk, a.dk_t, qdt, 2, kR, a.M, (uint64_t)kR * 2, 64, W.nk / 2);
+    if (rc) return rc;
+    rc = make_tmap_2d(&tdv, a.dv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.M, kR, (uint64_t)a.M * 2, 64, W.nc / 2);
+    if (rc) return rc;
+    if ((a.M + kR + 64) * 4 > W.smem) return DA_ERR_SHAPE;  // repair scratch must fit
+  }
+  auto kern = wide ? route_fwd_wide_kernel<kR, T> : route_fwd_kernel<kR, T>;
+  const int smem = (wide ? W.smem : C::kSmem) + 1024;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return record_cuda_error();
   const long pairs = (long)a.groups * ((a.rows + 127) / 128);
