@@ -75,6 +75,85 @@ __global__ void __launch_bounds__(256) dict_norm_fwd_kernel(const float* __restr
   }
 }
 
+// Key and value banks in one launch (grid.y = 0: key in the compute dtype,
+// 1: value in bf16), eight columns per CTA so that even a 512-atom bank
+// spreads over 128 CTAs.  Each thread keeps its column's rows in shared
+// memory between the norm and the write passes.
+template <typename TK>
+__global__ void __launch_bounds__(256) dict_norm_pair_kernel(const float* __restrict__ raw_key,
+                                                             const float* __restrict__ raw_value, int R, int M,
+                                                             float eps, TK* __restrict__ key, TK* __restrict__ key_t,
+                                                             float* __restrict__ key_denom,
+                                                             float* __restrict__ key_max,
+                                                             __nv_bfloat16* __restrict__ value,
+                                                             __nv_bfloat16* __restrict__ value_t,
+                                                             float* __restrict__ value_denom) {
+  extern __shared__ float tile8[];  // [R][9]
+  __shared__ float part[32][9], colden[8];
+  const bool is_key = blockIdx.y == 0;
+  const float* raw = is_key ? raw_key : raw_value;
+  const int tx = threadIdx.x & 7, ty = threadIdx.x >> 3;
+  const int j0 = blockIdx.x * 8, j = j0 + tx;
+  const bool col = j < M;
+  float ss = 0.f;
+#pragma unroll 8
+  for (int r = ty; r < R; r += 32) {
+    const float v = col ? raw[(size_t)r * M + j] : 0.f;
+    tile8[r * 9 + tx] = v;
+    ss = fmaf(v, v, ss);
+  }
+  part[ty][tx] = ss;
+  __syncthreads();
+  if (ty == 0) {
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) t += part[i][tx];
+    const float d = fmaxf(sqrtf(t), eps);
+    colden[tx] = d;
+    float* dout = is_key ? key_denom : value_denom;
+    if (dout && col) dout[j] = d;
+  }
+  __syncthreads();
+  const float inv = 1.f / colden[tx];
+  float rs = 0.f;
+#pragma unroll 8
+  for (int r = ty; r < R; r += 32) {
+    const float x = tile8[r * 9 + tx] * inv;
+    float yr;
+    if (is_key) {
+      const TK y = from_f32<TK>(x);
+      yr = static_cast<float>(y);
+      if (key && col) key[(size_t)r * M + j] = y;
+    } else {
+      const __nv_bfloat16 y = __float2bfloat16_rn(x);
+      yr = __bfloat162float(y);
+      if (value && col) value[(size_t)r * M + j] = y;
+    }
+    rs = fmaf(yr, yr, rs);
+    tile8[r * 9 + tx] = yr;
+  }
+  part[ty][tx] = rs;
+  __syncthreads();
+  if (is_key && key_max && ty == 0 && col) {
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) t += part[i][tx];
+    atomicMax(reinterpret_cast<int*>(key_max), __float_as_int(sqrtf(t)));
+  }
+  // transposed rows j0 .. j0+7, R elements each, written by all 256 threads
+  for (int c = 0; c < 8 && j0 + c < M; ++c) {
+    if (is_key) {
+      if (!key_t) break;
+      TK* dst = key_t + (size_t)(j0 + c) * R;
+      for (int r = threadIdx.x; r < R; r += 256) dst[r] = from_f32<TK>(tile8[r * 9 + c]);
+    } else {
+      if (!value_t) break;
+      __nv_bfloat16* dst = value_t + (size_t)(j0 + c) * R;
+      for (int r = threadIdx.x; r < R; r += 256) dst[r] = __float2bfloat16_rn(tile8[r * 9 + c]);
+    }
+  }
+}
+
 // grad (and grad_t, the same gradient given in [M, R] layout) are summed.
 // One CTA per 32 columns, both operands staged in shared memory.
 __global__ void __launch_bounds__(256) dict_norm_bwd_kernel(const float* __restrict__ raw,
@@ -218,6 +297,37 @@ extern "C" int da_col_norm_max(const void* dict, int64_t R, int64_t M, int dtype
     col_norm_max_kernel<__half><<<grid, block, 0, st>>>((const __half*)dict, (int)R, (int)M, out);
   else
     return DA_ERR_DTYPE;
+  if (cudaPeekAtLastError() != cudaSuccess) return record_cuda_error();
+  note_launch();
+  return DA_OK;
+}
+
+extern "C" int da_dict_norm_pair_fwd(const float* raw_key, const float* raw_value, int64_t R, int64_t M, float eps,
+                                     int key_dtype, void* key, void* key_t, float* key_denom, float* key_max,
+                                     void* value, void* value_t, float* value_denom, void* stream) {
+  using namespace da;
+  if (!raw_key) return DA_ERR_NULL;
+  if (int rc = bind_device(raw_key)) return rc;
+  if (R <= 0 || M <= 0 || R > 1536 || M > (1 << 24)) return DA_ERR_SHAPE;
+  if (key_dtype != DA_BF16 && key_dtype != DA_F16) return DA_ERR_DTYPE;
+  const bool with_value = raw_value && (value || value_t || value_denom);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (key_max && cudaMemsetAsync(key_max, 0, sizeof(float), st) != cudaSuccess) return record_cuda_error();
+  const dim3 grid((unsigned)((M + 7) / 8), with_value ? 2u : 1u), block(256);
+  const size_t smem = (size_t)R * 9 * sizeof(float);
+  if (key_dtype == DA_BF16) {
+    auto k = dict_norm_pair_kernel<__nv_bfloat16>;
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return record_cuda_error();
+    k<<<grid, block, smem, st>>>(raw_key, raw_value, (int)R, (int)M, eps, (__nv_bfloat16*)key, (__nv_bfloat16*)key_t,
+                                 key_denom, key_max, (__nv_bfloat16*)value, (__nv_bfloat16*)value_t, value_denom);
+  } else {
+    auto k = dict_norm_pair_kernel<__half>;
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return record_cuda_error();
+    k<<<grid, block, smem, st>>>(raw_key, raw_value, (int)R, (int)M, eps, (__half*)key, (__half*)key_t, key_denom,
+                                 key_max, (__nv_bfloat16*)value, (__nv_bfloat16*)value_t, value_denom);
+  }
   if (cudaPeekAtLastError() != cudaSuccess) return record_cuda_error();
   note_launch();
   return DA_OK;

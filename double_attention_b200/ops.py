@@ -200,18 +200,77 @@ class _DictNorm(torch.autograd.Function):
         return grad, None, None
 
 
+class _DictNormPair(torch.autograd.Function):
+    """Key bank (compute dtype) and value bank (bf16) normalised in one launch.
+
+    ``raw_value`` None means a tied dictionary whose value views are a bf16
+    normalisation of ``raw_key`` (the compute dtype is not bf16)."""
+
+    @staticmethod
+    def forward(ctx, raw_key: Tensor, raw_value: Tensor | None, eps: float, dtype: torch.dtype):  # type: ignore[override]
+        rk = raw_key.detach().contiguous().float()
+        rv = rk if raw_value is None else raw_value.detach().contiguous().float()
+        r, m = rk.shape
+        dev = rk.device
+        key = torch.empty(r, m, dtype=dtype, device=dev)
+        key_t = torch.empty(m, r, dtype=dtype, device=dev)
+        value = torch.empty(r, m, dtype=torch.bfloat16, device=dev)
+        value_t = torch.empty(m, r, dtype=torch.bfloat16, device=dev)
+        kden = torch.empty(m, dtype=torch.float32, device=dev)
+        vden = torch.empty(m, dtype=torch.float32, device=dev)
+        kmax = torch.empty(1, dtype=torch.float32, device=dev)
+        call("da_dict_norm_pair_fwd", rk.data_ptr(), rv.data_ptr(), r, m, eps, dtype_code(dtype), key.data_ptr(),
+             key_t.data_ptr(), kden.data_ptr(), kmax.data_ptr(), value.data_ptr(), value_t.data_ptr(),
+             vden.data_ptr(), stream_ptr(dev))
+        ctx.save_for_backward(rk, rv, kden, vden)
+        ctx.eps = eps
+        ctx.tied = raw_value is None
+        ctx.mark_non_differentiable(kmax)
+        key_anchor = torch.empty(r, m, dtype=torch.float32, device=dev)  # fp32 gradient entries, never read
+        value_anchor = torch.empty(r, m, dtype=torch.float32, device=dev)
+        return key, key_t, kmax, key_anchor, value, value_t, value_anchor
+
+    @staticmethod
+    def backward(ctx, g_key, g_key_t, _g_kmax, g_key_anchor, g_value, g_value_t, g_value_anchor):  # type: ignore[override]
+        rk, rv, kden, vden = ctx.saved_tensors
+        r, m = rk.shape
+        dev = rk.device
+
+        def merged(g, anchor):
+            if anchor is None:
+                return None if g is None else g.float().contiguous()
+            return anchor.contiguous() if g is None else (anchor + g.float()).contiguous()
+
+        gk, gv = merged(g_key, g_key_anchor), merged(g_value, g_value_anchor)
+        gkt = None if g_key_t is None else g_key_t.float().contiguous()
+        gvt = None if g_value_t is None else g_value_t.float().contiguous()
+        grad_key = grad_value = None
+        if gk is not None or gkt is not None:
+            grad_key = torch.empty_like(rk)
+            call("da_dict_norm_bwd", rk.data_ptr(), kden.data_ptr(), ptr(gk), ptr(gkt), r, m, ctx.eps,
+                 grad_key.data_ptr(), 0, stream_ptr(dev))
+        if gv is not None or gvt is not None:
+            if ctx.tied:  # the value bank is the key bank: both gradients land on raw_key
+                if grad_key is None:
+                    grad_key = torch.zeros_like(rk)
+                call("da_dict_norm_bwd", rk.data_ptr(), vden.data_ptr(), ptr(gv), ptr(gvt), r, m, ctx.eps,
+                     grad_key.data_ptr(), 1, stream_ptr(dev))
+            else:
+                grad_value = torch.empty_like(rv)
+                call("da_dict_norm_bwd", rv.data_ptr(), vden.data_ptr(), ptr(gv), ptr(gvt), r, m, ctx.eps,
+                     grad_value.data_ptr(), 0, stream_ptr(dev))
+        return grad_key, grad_value, None, None
+
+
 def dictionary_views(raw_key: Tensor, raw_value: Tensor | None, eps: float, dtype: torch.dtype) -> DictionaryViews:
     """Normalise a bank's raw parameters into kernel operands (autograd-aware)."""
     if not raw_key.is_cuda:
         raise RuntimeError("B200 backend requested but unavailable: CUDA fp16/bf16 tensors are required")
-    key, key_t, key_max, key_anchor = _DictNorm.apply(raw_key, eps, dtype)
-    if raw_value is None:  # tied dictionary (untied_dictionary=False)
-        if dtype == torch.bfloat16:
-            value, value_t, value_anchor = key, key_t, key_anchor
-        else:
-            value, value_t, _, value_anchor = _DictNorm.apply(raw_key, eps, torch.bfloat16)
-    else:
-        value, value_t, _, value_anchor = _DictNorm.apply(raw_value, eps, torch.bfloat16)
+    if raw_value is None and dtype == torch.bfloat16:  # tied dictionary: one set of bf16 views serves both
+        key, key_t, key_max, key_anchor = _DictNorm.apply(raw_key, eps, dtype)
+        return DictionaryViews(key, key_t, key, key_t, key_max, key_anchor, key_anchor)
+    key, key_t, key_max, key_anchor, value, value_t, value_anchor = _DictNormPair.apply(raw_key, raw_value, eps,
+                                                                                      dtype)
     return DictionaryViews(key, key_t, value, value_t, key_max, key_anchor, value_anchor)
 
 

@@ -65,6 +65,16 @@ DA_API int da_set_debug_trace(int* host_mapped);
 DA_API int da_dict_norm_fwd(const float* raw, int64_t R, int64_t M, float eps, int out_dtype, void* out, void* out_t,
                      float* denom, float* max_col_norm, void* stream);
 
+/* Both banks of a dictionary in one launch (the module path normalises the
+ * key and value banks every forward, modules.py:45-48, :229-231): the key
+ * bank as da_dict_norm_fwd in key_dtype (key, key_t, key_denom, key_max),
+ * the value bank in bf16 (value, value_t, value_denom).  raw_value may equal
+ * raw_key (tied dictionary in a dtype other than bf16) or be null (key only).
+ * Every output pointer may be null. */
+DA_API int da_dict_norm_pair_fwd(const float* raw_key, const float* raw_value, int64_t R, int64_t M, float eps,
+                                 int key_dtype, void* key, void* key_t, float* key_denom, float* key_max,
+                                 void* value, void* value_t, float* value_denom, void* stream);
+
 /* Backward of da_dict_norm_fwd (autograd of F.normalize, modules.py:46-47).
  * grad: [R, M] fp32 and/or grad_t: [M, R] fp32 (summed when both are given).
  * grad_raw: [R, M] fp32, overwritten (accumulate = 0) or added to. */

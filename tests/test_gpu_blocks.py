@@ -80,3 +80,28 @@ def test_dict_norm_forward_backward(dtype: torch.dtype, r: int, m: int) -> None:
         grad_raw.data_ptr(), 0, _lib.stream_ptr(),
     )
     torch.testing.assert_close(grad_raw, raw.grad, atol=1e-4, rtol=1e-4)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize(("r", "m"), [(256, 512), (128, 512), (512, 1536), (8, 20)])
+def test_dict_norm_pair_matches_single_bank_calls(dtype: torch.dtype, r: int, m: int) -> None:
+    """One launch for the key bank (compute dtype) and the value bank (bf16)."""
+    torch.manual_seed(r * m)
+    dev = torch.device("cuda")
+    raw_k = torch.randn(r, m, device=dev) * r**-0.5
+    raw_v = torch.randn(r, m, device=dev) * r**-0.5
+    raw_k[:, 1] = 0.0
+    eps = 1e-6
+    key, key_t = torch.empty(r, m, device=dev, dtype=dtype), torch.empty(m, r, device=dev, dtype=dtype)
+    val, val_t = (torch.empty(r, m, device=dev, dtype=torch.bfloat16),
+                  torch.empty(m, r, device=dev, dtype=torch.bfloat16))
+    kden, vden, kmax = torch.empty(m, device=dev), torch.empty(m, device=dev), torch.empty(1, device=dev)
+    _lib.call("da_dict_norm_pair_fwd", raw_k.data_ptr(), raw_v.data_ptr(), r, m, eps, _lib.dtype_code(dtype),
+              key.data_ptr(), key_t.data_ptr(), kden.data_ptr(), kmax.data_ptr(), val.data_ptr(), val_t.data_ptr(),
+              vden.data_ptr(), _lib.stream_ptr())
+    torch.testing.assert_close(key, torch.nn.functional.normalize(raw_k, dim=0, eps=eps).to(dtype))
+    torch.testing.assert_close(val, torch.nn.functional.normalize(raw_v, dim=0, eps=eps).to(torch.bfloat16))
+    assert torch.equal(key_t, key.t()) and torch.equal(val_t, val.t())
+    torch.testing.assert_close(kden, raw_k.norm(dim=0).clamp_min(eps), atol=1e-6, rtol=1e-5)
+    torch.testing.assert_close(vden, raw_v.norm(dim=0).clamp_min(eps), atol=1e-6, rtol=1e-5)
+    torch.testing.assert_close(kmax[0], key.float().norm(dim=0).max(), atol=1e-6, rtol=1e-5)
