@@ -174,22 +174,26 @@ def time_kernel(run, reps: int, device: torch.device) -> float:
 
 def main(argv=None) -> int:
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    p.add_argument("--kernel", choices=KERNELS, required=True)
+    p.add_argument("--kernel", required=True, help=f"comma-separated list of {', '.join(KERNELS)}")
     p.add_argument("--config", type=int, choices=sorted(SHAPES), default=2)
     p.add_argument("--reps", type=int, default=3)
     p.add_argument("--time", action="store_true")
     args = p.parse_args(argv)
     device = torch.device("cuda", 0)
-    run, flops = make_case(args.kernel, args.config, device)
-    if args.time:
-        ms = time_kernel(run, args.reps, device)
-        print(json.dumps({"kernel": args.kernel, "config": args.config, "ms": ms, "flops": flops,
-                          "tflops": flops / (ms / 1e3) / 1e12}))
-    else:
-        for _ in range(args.reps):
-            run()
-        torch.cuda.synchronize()
-    ops.device_status(device)
+    for kernel in args.kernel.split(","):
+        if kernel not in KERNELS:
+            raise SystemExit(f"unknown kernel {kernel!r}")
+        run, flops = make_case(kernel, args.config, device)
+        if args.time:
+            ms = time_kernel(run, args.reps, device)
+            print(json.dumps({"kernel": kernel, "config": args.config, "ms": ms, "flops": flops,
+                              "tflops": flops / (ms / 1e3) / 1e12}))
+        else:
+            for _ in range(args.reps):
+                run()
+            torch.cuda.synchronize()
+        del run
+        ops.device_status(device)
     return 0
 
 
