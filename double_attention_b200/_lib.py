@@ -55,6 +55,8 @@ SIGNATURES: dict[str, list] = {
     "da_gemm_splitk": [_p, _i64, _i32, _p, _i64, _i32, _p, _i64, _i64, _i64, _i64, _i32, _i32, _p, _p],
     "da_route_bwd": [_p, _i64, _i64, _i64, _i32, _i64, _i64, _i64, _i32, _p, _p, _p, _f32, _i32, _i32, _p, _p, _p,
                      _p, _p, _p, _p, _p, _p, _p, _p],
+    "da_attn_bwd_mixed": [_p, _i64, _i64, _i64, _i64, _p, _i64, _i64, _i64, _i64, _p, _p, _i32, _i32, _i32, _i32,
+                          _i32, _i32, _p, _i32, _i32, _p, _p, _p, _p, _i32, _p, _p, _p, _p, _p, _p, _p],
     "da_selftest_mma": [_i32, _i32, _i32, _i32, _p, _p, _p, _p, _p],
     "da_route_fwd": [_p, _i64, _i64, _i64, _i32, _i64, _i64, _i64, _i32, _p, _p, _p, _p, _f32, _i32, _i32,
                      _p, _p, _p, _p, _p, _i32, _p, _p],

@@ -1,0 +1,1002 @@
+// Outer routed attention, backward, all maps of a mixed attention at once.
+//
+// Reference: _routed_attention_triton_backward (triton_kernels.py:2093-2263)
+// plus the gradient of the alpha mix (modules.py:265-272).  With maps s,
+// S_s = gamma_s/sqrt(group) Q_s K_s^T, P_s = exp(S_s - lse_s) (causal) and
+// Y = sum_s alpha_s P_s V:
+//   dP      = dY V^T                       (the same for every map)
+//   delta_s = sum_k P_s dP = <dY, P_s V>   (row sums)
+//   dS_s    = alpha_s P_s (dP - delta_s)
+//   dQ_s    = gamma_eff,s dS_s K_s,  dK_s = gamma_eff,s dS_s^T Q_s
+//   dV      = (sum_s alpha_s P_s)^T dY     (one product for all maps)
+//   dgamma_s = alpha_s sum (P dP S - (sum P dP)(sum P S)) / sqrt(group) per row
+//   dalpha_s = sum_rows delta_s
+// Three paired-CTA kernels (2-CTA clusters, cta_group::2 MMAs, folded TMEM):
+//   * query-parallel (dQ): per key tile, dP once, then S_s map by map; with
+//     no delta given, a first sweep over the keys computes delta_s exactly
+//     (fp32 P and dP) and the second forms dS_s and accumulates dQ_s;
+//   * key-parallel (dK): per query tile, dP^T once, then S_s^T, dS_s^T and dK_s
+//     map by map;
+//   * key-parallel (dV): per query tile, S_s^T map by map into the mixed
+//     probabilities, then one dV product.
+// Score and dP tiles are double-buffered in TMEM, so the tensor core works on
+// the next unit while the softmax warpgroup handles the current one.
+// Operands stream through one ring of 16 KB stages filled in exactly the
+// order the MMA warp consumes them.
+#include <math.h>
+
+#include "attn_common.h"
+#include "common.cuh"
+#include "host_util.h"
+
+namespace da {
+namespace attn {
+namespace bwdm {
+
+constexpr int kThreads = 192;
+constexpr int kRows = 64;      // rows (queries or keys) per CTA
+constexpr int kTile = 128;     // columns (keys or queries) per tile and pair
+constexpr int kStage = 16384;  // ring stage bytes
+constexpr int kMaxStages = 8;
+constexpr int kBox = kRows * 128;  // one 64-row x 128-byte swizzled box
+
+struct Params {
+  int64_t q_rows, q_base, q_sb, q_sbr;
+  int64_t k_rows, k_base, k_sb, k_sbr;
+  int B, T, R, D, maps, group, causal;
+  int branch0[kMaxMaps];
+  const float* scales;   // [maps] gamma_s
+  const float* weights;  // [maps] alpha_s, or null for 1
+  const float* lse;      // [B, maps, T] natural log
+  float* delta;          // [B, maps, T]: read, or written by the dQ kernel's first sweep
+  int delta_given;
+  float* dq;             // fp32 [q_rows, R], +=
+  float* dk;             // fp32 [k_rows, R], +=
+  float* dv;             // fp32 [B*T, D], +=
+  float* dscale;         // [maps] d gamma_s, += (may be null)
+  float* dweight;        // [maps] d alpha_s, += (dQ kernel with the first sweep; may be null)
+  int* status;
+  int* trace;            // optional post-mortem timeline (debug)
+};
+
+DA_DEV int64_t row_of(int64_t base, int64_t sb, int64_t sbr, int b, int branch, int t) {
+  return base + (int64_t)b * sb + (int64_t)branch * sbr + t;
+}
+
+struct Layout {
+  int kw, W, rpb, ncol, nins;
+  int off_a, off_b, off_t, off_red, off_ring, nst, smem;
+  int tmem_acc, tmem_s, tmem_p, tmem_cols;
+};
+
+// kind 0: dQ (A = Q of all maps, B = dY), 1: dK (A = K of all maps, B = V), 2: dV (A = K of all maps)
+__host__ __device__ inline Layout make_layout(int kind, int maps, int group, int R, int D) {
+  Layout L;
+  L.kw = group * R;
+  L.W = maps * L.kw;
+  L.rpb = R / 64;
+  L.ncol = L.kw < 256 ? L.kw : 256;
+  L.nins = L.kw / L.ncol;
+  L.off_a = 0;
+  L.off_b = L.off_a + kRows * L.W * 2;
+  const int b_bytes = kind == 2 ? 0 : kRows * D * 2;
+  L.off_t = L.off_b + b_bytes;                 // two dS / P tiles
+  L.off_red = L.off_t + 2 * kRows * kTile * 2;
+  L.off_ring = L.off_red + 8192;
+  const int avail = 225 * 1024 - L.off_ring;
+  L.nst = avail / kStage > kMaxStages ? kMaxStages : avail / kStage;
+  L.smem = L.off_ring + L.nst * kStage;
+  L.tmem_acc = 0;
+  const int acc = kind == 2 ? D / 2 : L.W / 2;
+  L.tmem_s = acc;
+  L.tmem_p = L.tmem_s + 2 * (kTile / 2);
+  const int cols = L.tmem_p + (kind == 2 ? 0 : 2 * (kTile / 2));
+  L.tmem_cols = cols <= 256 ? 256 : (cols <= 512 ? 512 : 1024);
+  return L;
+}
+
+// Loads one 64-row K-major chunk of 128 map-local columns of a row-mapped [rows, R] matrix
+// (map s, `nb` boxes) for rows starting at `t` of batch `b`.
+struct MapRows {
+  int64_t rows, base, sb, sbr;
+};
+
+DA_DEV void load_map_chunk(const CUtensorMap* tm, const MapRows& m, const Params& p, uint32_t bar, uint8_t* dst,
+                           int b, int s, int cc, int nb, int t) {
+  for (int bx = 0; bx < nb; ++bx) {
+    const int mb = cc * 2 + bx, gi = mb / (p.R / 64), x = (mb % (p.R / 64)) * 64;
+    const int64_t row = row_of(m.base, m.sb, m.sbr, b, p.branch0[s] + gi, t);
+    tma_load_2d_pair(tm, bar, dst + bx * kBox, x, (int)min(row, m.rows - 1));
+  }
+}
+
+// =============================================================================== dQ kernel
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_constant__ CUtensorMap tq,
+                                                               const __grid_constant__ CUtensorMap tk,
+                                                               const __grid_constant__ CUtensorMap tv,
+                                                               const __grid_constant__ CUtensorMap tdy,
+                                                               const Params p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t in_full, o_full, r_full[kMaxStages], r_empty[kMaxStages];
+  __shared__ uint64_t s_full[2], p_full[2], dp_full[2], dp_free[2], ds_empty[2];
+  __shared__ uint32_t tmem_base;
+  __shared__ int abort_flag;
+
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  const Layout L = make_layout(0, p.maps, p.group, p.R, p.D);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_ctarank() & 1u;
+  const int tiles = (p.T + kTile - 1) / kTile;
+  const int pair = blockIdx.x / 2;
+  const int b = pair / tiles;
+  const int t0 = (tiles - 1 - pair % tiles) * kTile;
+  const int nj = p.causal ? t0 / kTile + 1 : tiles;
+  const int maps = p.maps;
+  const int sweeps = p.delta_given ? 1 : 2;
+  const int per_sweep = nj * maps;
+  const int U = sweeps * per_sweep;
+  const int u_dq = (sweeps - 1) * per_sweep;  // first unit that forms dS and accumulates dQ
+  const MapRows qm{p.q_rows, p.q_base, p.q_sb, p.q_sbr}, km{p.k_rows, p.k_base, p.k_sb, p.k_sbr};
+  const int64_t rowsBT = (int64_t)p.B * p.T;
+  Abort ab{&abort_flag, p.status};
+  // post-mortem per-unit timeline of the first pair (debug trace only)
+  int* ft = (p.trace && blockIdx.x < 2) ? p.trace + blockIdx.x * 4096 : nullptr;
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    mbar_init(&in_full, 1);
+    mbar_init(&o_full, 1);
+    for (int i = 0; i < kMaxStages; ++i) {
+      mbar_init(&r_full[i], 1);
+      mbar_init(&r_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 2);
+      mbar_init(&dp_full[i], 1);
+      mbar_init(&dp_free[i], 2);
+      mbar_init(&ds_empty[i], 1);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc<2>(&tmem_base, L.tmem_cols);
+    tmem_relinquish<2>();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+
+  // unit u -> (sweep tile g, tile j within the sweep, map s)
+  auto unit_j = [&](int u) { return (u % per_sweep) / maps; };
+  auto unit_s = [&](int u) { return u % maps; };
+  auto unit_g = [&](int u) { return u / maps; };  // sweep-major tile counter (dP products)
+
+  if (warp == 0 && lane == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    prefetch_tmap(&tq);
+    prefetch_tmap(&tk);
+    prefetch_tmap(&tv);
+    prefetch_tmap(&tdy);
+    const uint32_t inf = mapa_shared(smem_u32(&in_full), 0);
+    if (rank == 0) mbar_arrive_expect_tx(&in_full, 2 * (kRows * L.W * 2 + kRows * p.D * 2));
+    const int tq_row = t0 + 64 * (int)rank;
+    for (int s = 0; s < maps; ++s)
+      for (int cc = 0; cc < L.kw / 128; ++cc)
+        load_map_chunk(&tq, qm, p, inf, smem + L.off_a + (s * (L.kw / 64) + cc * 2) * kBox, b, s, cc, 2, tq_row);
+    const int dy_row = (int)min((int64_t)b * p.T + tq_row, rowsBT - 1);
+    for (int cb = 0; cb < p.D / 64; ++cb) tma_load_2d_pair(&tdy, inf, smem + L.off_b + cb * kBox, cb * 64, dy_row);
+    int it = 0;
+    bool ok = true;
+    auto stage = [&](int bytes) -> uint8_t* {
+      const int st = it % L.nst;
+      if (!mbar_wait(&r_empty[st], ((it / L.nst) & 1u) ^ 1u, ab, 11)) { ok = false; return nullptr; }
+      if (rank == 0) mbar_arrive_expect_tx(&r_full[st], 2 * bytes);
+      return smem + L.off_ring + st * kStage;
+    };
+    auto stage_bar = [&]() { return mapa_shared(smem_u32(&r_full[it % L.nst]), 0); };
+    auto emit_dp = [&](int u) {  // value rows of this CTA's 64 keys, 128 columns per stage
+      const int krow0 = unit_j(u) * kTile + 64 * (int)rank;
+      const int y = (int)min((int64_t)b * p.T + krow0, rowsBT - 1);
+      for (int cc = 0; ok && cc < p.D / 128; ++cc, ++it) {
+        uint8_t* dst = stage(2 * kBox);
+        if (!ok) return;
+        const uint32_t bar = stage_bar();
+        for (int bx = 0; bx < 2; ++bx) tma_load_2d_pair(&tv, bar, dst + bx * kBox, cc * 128 + bx * 64, y);
+      }
+    };
+    auto emit_s = [&](int u) {  // key rows of map s for this CTA's 64 keys
+      const int krow0 = unit_j(u) * kTile + 64 * (int)rank;
+      for (int cc = 0; ok && cc < L.kw / 128; ++cc, ++it) {
+        uint8_t* dst = stage(2 * kBox);
+        if (!ok) return;
+        load_map_chunk(&tk, km, p, stage_bar(), dst, b, unit_s(u), cc, 2, krow0);
+      }
+    };
+    auto emit_dq = [&](int u) {  // key rows of all 128 keys, MN-major, this CTA's half of each N block
+      const int per = (L.ncol / 2) / 64, s = unit_s(u), j = unit_j(u);
+      for (int kc = 0; ok && kc < kTile / 64; ++kc)
+        for (int ins = 0; ok && ins < L.nins; ++ins, ++it) {
+          uint8_t* dst = stage(per * kBox);
+          if (!ok) return;
+          const uint32_t bar = stage_bar();
+          for (int bx = 0; bx < per; ++bx) {
+            const int mb = (ins * L.ncol + (int)rank * (L.ncol / 2)) / 64 + bx;
+            const int gi = mb / L.rpb, x = (mb % L.rpb) * 64;
+            const int64_t row = row_of(km.base, km.sb, km.sbr, b, p.branch0[s] + gi, j * kTile + kc * 64);
+            tma_load_2d_pair(&tk, bar, dst + bx * kBox, x, (int)min(row, km.rows - 1));
+          }
+        }
+    };
+    emit_dp(0);
+    emit_s(0);
+    for (int u = 0; ok && u < U; ++u) {
+      if (u + 1 < U) {
+        if (unit_s(u + 1) == 0) emit_dp(u + 1);
+        emit_s(u + 1);
+      }
+      if (u >= u_dq) emit_dq(u);
+    }
+    if (rank == 0) {
+      mbar_wait_drain(&in_full, 0);
+      for (int i = (it > L.nst ? it - L.nst : 0); i < it; ++i) mbar_wait_drain(&r_full[i % L.nst], (i / L.nst) & 1u);
+    }
+  } else if (warp == 1 && lane == 0 && rank == 0) {
+    // ---------------------------------------------------------------- MMA issuer (leader)
+    const uint32_t idesc_s = idesc_f16(128, kTile, kBf16, false, false);
+    const uint32_t idesc_q = idesc_f16(128, L.ncol, kBf16, false, true);  // B = K rows, MN-major
+    auto commit_both = [&](uint64_t* bar) {
+      mma_commit<2>(smem_u32(bar));
+      mma_commit<2>(mapa_shared(smem_u32(bar), 1));
+    };
+    int it = 0;
+    auto take = [&](uint32_t* addr) -> bool {
+      const int st = it % L.nst;
+      if (!mbar_wait(&r_full[st], (it / L.nst) & 1u, ab, 23)) return false;
+      tc_fence_after();
+      *addr = smem_u32(smem + L.off_ring + st * kStage);
+      return true;
+    };
+    auto give = [&]() { commit_both(&r_empty[it % L.nst]); ++it; };
+    const uint32_t qa = smem_u32(smem + L.off_a), dya = smem_u32(smem + L.off_b);
+    auto issue_dp = [&](int u) -> bool {
+      const int g = unit_g(u), db = g & 1;
+      if (g < 200) trace_at(ft, 1024 + 4 * g);
+      if (g >= 2 && !mbar_wait(&dp_free[db], ((g - 2) >> 1) & 1u, ab, 27)) return false;
+      for (int cc = 0; cc < p.D / 128; ++cc) {
+        uint32_t st;
+        if (!take(&st)) return false;
+        for (int k = 0; k < 8; ++k) {
+          const uint64_t ad = sdesc_sw128(dya + (cc * 2 + (k >> 2)) * kBox + (k & 3) * 32, 16, 1024);
+          const uint64_t bd = sdesc_sw128(st + (k >> 2) * kBox + (k & 3) * 32, 16, 1024);
+          mma_f16_ss<2>(tmem + L.tmem_p + db * (kTile / 2), ad, bd, idesc_s, (cc | k) ? 1u : 0u);
+        }
+        give();
+      }
+      commit_both(&dp_full[db]);
+      if (g < 200) trace_at(ft, 1025 + 4 * g);
+      return true;
+    };
+    auto issue_s = [&](int u) -> bool {
+      const int sb = u & 1, s = unit_s(u);
+      if (u < 300) trace_at(ft, 2048 + 4 * u);
+      if (u >= 2 && !mbar_wait(&p_full[sb], ((u - 2) >> 1) & 1u, ab, 22)) return false;
+      for (int cc = 0; cc < L.kw / 128; ++cc) {
+        uint32_t st;
+        if (!take(&st)) return false;
+        for (int k = 0; k < 8; ++k) {
+          const uint64_t ad =
+              sdesc_sw128(qa + (s * (L.kw / 64) + cc * 2 + (k >> 2)) * kBox + (k & 3) * 32, 16, 1024);
+          const uint64_t bd = sdesc_sw128(st + (k >> 2) * kBox + (k & 3) * 32, 16, 1024);
+          mma_f16_ss<2>(tmem + L.tmem_s + sb * (kTile / 2), ad, bd, idesc_s, (cc | k) ? 1u : 0u);
+        }
+        give();
+      }
+      commit_both(&s_full[sb]);
+      if (u < 300) trace_at(ft, 2049 + 4 * u);
+      return true;
+    };
+    auto issue_dq = [&](int u) -> bool {
+      const int v = u - u_dq, s = unit_s(u), j = unit_j(u);
+      if (u < 300) trace_at(ft, 2050 + 4 * u);
+      if (!mbar_wait(&p_full[u & 1], (u >> 1) & 1u, ab, 24)) return false;
+      if (u < 300) trace_at(ft, 2051 + 4 * u);
+      tc_fence_after();
+      const uint32_t dsa = smem_u32(smem + L.off_t + (v & 1) * (kRows * kTile * 2));
+      for (int kc = 0; kc < kTile / 64; ++kc)
+        for (int ins = 0; ins < L.nins; ++ins) {
+          uint32_t st;
+          if (!take(&st)) return false;
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t ad = sdesc_sw128(dsa + kc * kBox + kk * 32, 16, 1024);
+            const uint64_t bd = sdesc_sw128(st + kk * 16 * 128, 64 * 128, 1024);
+            mma_f16_ss<2>(tmem + L.tmem_acc + s * (L.kw / 2) + ins * (L.ncol / 2), ad, bd, idesc_q,
+                          (j | kc | kk) ? 1u : 0u);
+          }
+          give();
+        }
+      commit_both(&ds_empty[v & 1]);
+      return true;
+    };
+    bool ok = mbar_wait(&in_full, 0, ab, 21);
+    tc_fence_after();
+    if (ok) ok = issue_dp(0);
+    if (ok) ok = issue_s(0);
+    for (int u = 0; ok && u < U; ++u) {
+      if (u + 1 < U) {
+        if (unit_s(u + 1) == 0) ok = issue_dp(u + 1);
+        if (ok) ok = issue_s(u + 1);
+      }
+      if (ok && u >= u_dq) ok = issue_dq(u);
+    }
+    commit_both(&o_full);
+    mbar_wait_drain(&o_full, 0);
+  } else if (warp >= 2) {
+    // ---------------------------------------------------------------- softmax + epilogue
+    const int quad = warp & 3;
+    const int l = quad * 32 + lane;
+    const int r = l & 63, half = l >> 6;
+    const int t = t0 + 64 * (int)rank + r;
+    const bool live = t < p.T;
+    const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+    const uint32_t pf_leader = mapa_shared(smem_u32(&p_full[0]), 0);
+    const uint32_t df_leader = mapa_shared(smem_u32(&dp_free[0]), 0);
+    const bool arriver = (warp == 2 && lane == 0);
+    float* red = reinterpret_cast<float*>(smem + L.off_red);
+    const float kLog2e = 1.4426950408889634f;
+    const float gsc = rsqrtf((float)p.group);
+    float scale2[kMaxMaps], lse2[kMaxMaps], delta[kMaxMaps], alpha[kMaxMaps];
+    float sA[kMaxMaps], sB[kMaxMaps], sC[kMaxMaps];
+#pragma unroll
+    for (int s = 0; s < kMaxMaps; ++s) {
+      scale2[s] = lse2[s] = delta[s] = sA[s] = sB[s] = sC[s] = 0.f;
+      alpha[s] = 1.f;
+      if (s < maps) {
+        scale2[s] = p.scales[s] * gsc * kLog2e;
+        alpha[s] = p.weights ? p.weights[s] : 1.f;
+        if (live) {
+          lse2[s] = p.lse[((int64_t)b * maps + s) * p.T + t] * kLog2e;
+          if (p.delta_given) delta[s] = p.delta[((int64_t)b * maps + s) * p.T + t];
+        }
+      }
+    }
+    bool ok = true;
+    for (int u = 0; u < U; ++u) {
+      const int sb = u & 1, s = unit_s(u), j = unit_j(u), g = unit_g(u);
+      const bool form_ds = u >= u_dq;
+      const int v = u - u_dq;
+      if (arriver && u < 300) trace_at(ft, 3072 + 4 * u);
+      if (ok) ok = mbar_wait(&s_full[sb], (u >> 1) & 1u, ab, 32);
+      if (ok && s == 0) ok = mbar_wait(&dp_full[g & 1], (g >> 1) & 1u, ab, 35);
+      if (arriver && u < 300) trace_at(ft, 3073 + 4 * u);
+      if (ok && form_ds && v >= 2) ok = mbar_wait(&ds_empty[v & 1], ((v - 2) >> 1) & 1u, ab, 33);
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok) {
+        tc_fence_after();
+        const uint32_t dsa = smem_u32(smem + L.off_t + (v & 1) * (kRows * kTile * 2));
+        // this map's row constants in registers (the per-map arrays live in local memory)
+        const float sc2 = scale2[s], ls2 = lse2[s], dl = delta[s], al = alpha[s];
+        float dsum = 0.f, a_acc = 0.f, b_acc = 0.f, c_acc = 0.f;
+#pragma unroll
+        for (int ch = 0; ch < 2; ++ch) {
+          float sv[32], pv[32];
+          tmem_ld32(tmem + lane_base + L.tmem_s + sb * (kTile / 2) + ch * 32, sv);
+          tmem_ld32(tmem + lane_base + L.tmem_p + (g & 1) * (kTile / 2) + ch * 32, pv);
+          tmem_wait_ld();
+          const int k0 = j * kTile + half * 64 + ch * 32;
+          int lim = p.T - k0;
+          if (p.causal) lim = min(lim, t - k0 + 1);
+          if (!live) lim = 0;
+          uint32_t packed[16];
+          // branch-free: masked columns get probability 0 (a select, so any value the
+          // exponential takes there is discarded); two partial sums shorten the chains
+          if (form_ds) {
+            float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f, c0 = 0.f, c1 = 0.f;
+#pragma unroll
+            for (int i = 0; i < 32; i += 2) {
+              const float e0 = ex2(sv[i] * sc2 - ls2), e1 = ex2(sv[i + 1] * sc2 - ls2);
+              const float p0 = i < lim ? e0 : 0.f, p1 = i + 1 < lim ? e1 : 0.f;
+              const float q0 = p0 * pv[i], q1 = p1 * pv[i + 1];
+              a0 = fmaf(q0, sv[i], a0);
+              a1 = fmaf(q1, sv[i + 1], a1);
+              b0 = fmaf(p0, sv[i], b0);
+              b1 = fmaf(p1, sv[i + 1], b1);
+              c0 += q0;
+              c1 += q1;
+              packed[i / 2] = pack2<T>(al * (q0 - p0 * dl), al * (q1 - p1 * dl));
+            }
+            a_acc += a0 + a1;
+            b_acc += b0 + b1;
+            c_acc += c0 + c1;
+          } else {
+            float d0 = 0.f, d1 = 0.f;
+#pragma unroll
+            for (int i = 0; i < 32; i += 2) {
+              const float e0 = ex2(sv[i] * sc2 - ls2), e1 = ex2(sv[i + 1] * sc2 - ls2);
+              d0 = fmaf(i < lim ? e0 : 0.f, pv[i], d0);
+              d1 = fmaf(i + 1 < lim ? e1 : 0.f, pv[i + 1], d1);
+            }
+            dsum += d0 + d1;
+          }
+          if (form_ds) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              st_shared_v4(dsa + half * kBox + sw128_offset(r, ch * 4 + e), packed[4 * e], packed[4 * e + 1],
+                           packed[4 * e + 2], packed[4 * e + 3]);
+          }
+        }
+        if (form_ds) {
+          sA[s] += a_acc;
+          sB[s] += b_acc;
+          sC[s] += c_acc;
+          fence_proxy_async();
+        } else {
+          delta[s] += dsum;
+        }
+      }
+      if (arriver && u < 300) trace_at(ft, 3074 + 4 * u);
+      tc_fence_before();
+      named_bar_sync(1, 128);
+      if (arriver) {
+        if (u < 300) trace_at(ft, 3075 + 4 * u);
+        mbar_arrive_cluster(pf_leader + sb * 8);
+        if (s == maps - 1) mbar_arrive_cluster(df_leader + (g & 1) * 8);
+      }
+      if (!p.delta_given && u == per_sweep - 1) {
+        // end of the first sweep: whole-row delta_s (two halves), stored for the key-parallel kernels
+        for (int m = 0; m < maps; ++m) red[m * 128 + l] = delta[m];
+        named_bar_sync(1, 128);
+        for (int m = 0; m < maps; ++m) delta[m] += red[m * 128 + (l ^ 64)];
+        named_bar_sync(1, 128);
+        for (int m = 0; m < maps; ++m) {
+          if (ok && live && half == 0) p.delta[((int64_t)b * maps + m) * p.T + t] = delta[m];
+          if (p.dweight) {
+            float w = (ok && live && half == 0) ? delta[m] : 0.f;
+            for (int o = 16; o; o >>= 1) w += __shfl_xor_sync(0xffffffffu, w, o);
+            if (lane == 0 && w != 0.f) atomicAdd(p.dweight + m, w);
+          }
+        }
+      }
+    }
+    // ---- d gamma_s from each row's own sums (both halves), then the dQ epilogue
+    if (p.dscale) {
+      for (int m = 0; m < maps; ++m) {
+        red[(3 * m) * 128 + l] = sA[m];
+        red[(3 * m + 1) * 128 + l] = sB[m];
+        red[(3 * m + 2) * 128 + l] = sC[m];
+      }
+      named_bar_sync(1, 128);
+      for (int m = 0; m < maps; ++m) {
+        float dg = 0.f;
+        if (half == 0 && live && ok) {
+          const float A = sA[m] + red[(3 * m) * 128 + (l ^ 64)];
+          const float Bs = sB[m] + red[(3 * m + 1) * 128 + (l ^ 64)];
+          const float C = sC[m] + red[(3 * m + 2) * 128 + (l ^ 64)];
+          dg = alpha[m] * (A - C * Bs);
+        }
+        for (int o = 16; o; o >>= 1) dg += __shfl_xor_sync(0xffffffffu, dg, o);
+        if (lane == 0 && dg != 0.f) atomicAdd(p.dscale + m, dg * gsc);
+      }
+    }
+    if (ok) ok = mbar_wait(&o_full, 0, ab, 34);
+    ok = __all_sync(0xffffffffu, ok);
+    tc_fence_after();
+    if (ok && p.dq) {
+      for (int m = 0; m < maps; ++m) {
+        const float gamma = p.scales[m] * gsc;
+        for (int ins = 0; ins < L.nins; ++ins)
+          for (int c = 0; c < L.ncol / 2; c += 32) {
+            float vv[32];
+            tmem_ld32(tmem + lane_base + L.tmem_acc + m * (L.kw / 2) + ins * (L.ncol / 2) + c, vv);
+            tmem_wait_ld();
+            if (live) {
+              const int col = ins * L.ncol + half * (L.ncol / 2) + c;  // map-local column, one branch
+              const int gi = col / p.R;
+              const int64_t row = row_of(qm.base, qm.sb, qm.sbr, b, p.branch0[m] + gi, t);
+              float* dst = p.dq + row * p.R + (col % p.R);
+#pragma unroll
+              for (int e = 0; e < 32; e += 4) {
+                float4 o = *reinterpret_cast<float4*>(dst + e);
+                o.x += gamma * vv[e];
+                o.y += gamma * vv[e + 1];
+                o.z += gamma * vv[e + 2];
+                o.w += gamma * vv[e + 3];
+                *reinterpret_cast<float4*>(dst + e) = o;
+              }
+            }
+          }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  if (warp == 1) tmem_dealloc<2>(tmem, L.tmem_cols);
+}
+
+// =============================================================================== dK / dV kernels
+// kDK: dK_s += dS_s^T Q_s (per map); else dV += (sum_s alpha_s P_s)^T dY (once per query tile).
+template <typename T, bool kDK>
+__global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_constant__ CUtensorMap tq,
+                                                                const __grid_constant__ CUtensorMap tk,
+                                                                const __grid_constant__ CUtensorMap tv,
+                                                                const __grid_constant__ CUtensorMap tdy,
+                                                                const Params p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t in_full, o_full, r_full[kMaxStages], r_empty[kMaxStages];
+  __shared__ uint64_t s_full[2], p_full[2], dp_full[2], dp_free[2], t_empty[2];
+  __shared__ uint32_t tmem_base;
+  __shared__ int abort_flag;
+
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  const Layout L = make_layout(kDK ? 1 : 2, p.maps, p.group, p.R, p.D);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_ctarank() & 1u;
+  const int tiles = (p.T + kTile - 1) / kTile;
+  const int pair = blockIdx.x / 2;
+  const int b = pair / tiles;
+  const int k0 = (pair % tiles) * kTile;     // first key of this pair (early keys have the most queries)
+  const int i0 = p.causal ? k0 / kTile : 0;  // first query tile
+  const int ni = tiles - i0;
+  const int maps = p.maps;
+  const int U = ni * maps;
+  const int dn = p.D < 256 ? p.D : 256;      // N of one dV instruction
+  const int dins = p.D / dn;
+  const MapRows qm{p.q_rows, p.q_base, p.q_sb, p.q_sbr}, km{p.k_rows, p.k_base, p.k_sb, p.k_sbr};
+  const int64_t rowsBT = (int64_t)p.B * p.T;
+  Abort ab{&abort_flag, p.status};
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    mbar_init(&in_full, 1);
+    mbar_init(&o_full, 1);
+    for (int i = 0; i < kMaxStages; ++i) {
+      mbar_init(&r_full[i], 1);
+      mbar_init(&r_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 2);
+      mbar_init(&dp_full[i], 1);
+      mbar_init(&dp_free[i], 2);
+      mbar_init(&t_empty[i], 1);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc<2>(&tmem_base, L.tmem_cols);
+    tmem_relinquish<2>();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+
+  auto unit_g = [&](int u) { return u / maps; };  // query tile (0 .. ni-1)
+  auto unit_s = [&](int u) { return u % maps; };
+
+  if (warp == 0 && lane == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    prefetch_tmap(&tq);
+    prefetch_tmap(&tk);
+    prefetch_tmap(&tv);
+    prefetch_tmap(&tdy);
+    const uint32_t inf = mapa_shared(smem_u32(&in_full), 0);
+    if (rank == 0) mbar_arrive_expect_tx(&in_full, 2 * (kRows * L.W * 2 + (kDK ? kRows * p.D * 2 : 0)));
+    const int krow = k0 + 64 * (int)rank;
+    for (int s = 0; s < maps; ++s)
+      for (int cc = 0; cc < L.kw / 128; ++cc)
+        load_map_chunk(&tk, km, p, inf, smem + L.off_a + (s * (L.kw / 64) + cc * 2) * kBox, b, s, cc, 2, krow);
+    if (kDK) {
+      const int vy = (int)min((int64_t)b * p.T + krow, rowsBT - 1);
+      for (int cb = 0; cb < p.D / 64; ++cb) tma_load_2d_pair(&tv, inf, smem + L.off_b + cb * kBox, cb * 64, vy);
+    }
+    int it = 0;
+    bool ok = true;
+    auto stage = [&](int bytes) -> uint8_t* {
+      const int st = it % L.nst;
+      if (!mbar_wait(&r_empty[st], ((it / L.nst) & 1u) ^ 1u, ab, 11)) { ok = false; return nullptr; }
+      if (rank == 0) mbar_arrive_expect_tx(&r_full[st], 2 * bytes);
+      return smem + L.off_ring + st * kStage;
+    };
+    auto stage_bar = [&]() { return mapa_shared(smem_u32(&r_full[it % L.nst]), 0); };
+    auto emit_dp = [&](int u) {  // dY rows of this CTA's 64 queries, 128 columns per stage
+      const int q = (i0 + unit_g(u)) * kTile + 64 * (int)rank;
+      const int y = (int)min((int64_t)b * p.T + q, rowsBT - 1);
+      for (int cc = 0; ok && cc < p.D / 128; ++cc, ++it) {
+        uint8_t* dst = stage(2 * kBox);
+        if (!ok) return;
+        const uint32_t bar = stage_bar();
+        for (int bx = 0; bx < 2; ++bx) tma_load_2d_pair(&tdy, bar, dst + bx * kBox, cc * 128 + bx * 64, y);
+      }
+    };
+    auto emit_s = [&](int u) {  // query rows of map s for this CTA's 64 queries
+      const int q = (i0 + unit_g(u)) * kTile + 64 * (int)rank;
+      for (int cc = 0; ok && cc < L.kw / 128; ++cc, ++it) {
+        uint8_t* dst = stage(2 * kBox);
+        if (!ok) return;
+        load_map_chunk(&tq, qm, p, stage_bar(), dst, b, unit_s(u), cc, 2, q);
+      }
+    };
+    auto emit_acc = [&](int u) {  // MN-major operand of the accumulating product, all 128 queries
+      const int i = i0 + unit_g(u), s = unit_s(u);
+      if (kDK) {
+        const int per = (L.ncol / 2) / 64;
+        for (int qc = 0; ok && qc < kTile / 64; ++qc)
+          for (int ins = 0; ok && ins < L.nins; ++ins, ++it) {
+            uint8_t* dst = stage(per * kBox);
+            if (!ok) return;
+            const uint32_t bar = stage_bar();
+            for (int bx = 0; bx < per; ++bx) {
+              const int mb = (ins * L.ncol + (int)rank * (L.ncol / 2)) / 64 + bx;
+              const int gi = mb / L.rpb, x = (mb % L.rpb) * 64;
+              const int64_t row = row_of(qm.base, qm.sb, qm.sbr, b, p.branch0[s] + gi, i * kTile + qc * 64);
+              tma_load_2d_pair(&tq, bar, dst + bx * kBox, x, (int)min(row, qm.rows - 1));
+            }
+          }
+      } else {
+        const int dper = (dn / 2) / 64;
+        for (int qc = 0; ok && qc < kTile / 64; ++qc) {
+          const int y = (int)min((int64_t)b * p.T + i * kTile + qc * 64, rowsBT - 1);
+          for (int ins = 0; ok && ins < dins; ++ins, ++it) {
+            uint8_t* dst = stage(dper * kBox);
+            if (!ok) return;
+            const uint32_t bar = stage_bar();
+            for (int bx = 0; bx < dper; ++bx)
+              tma_load_2d_pair(&tdy, bar, dst + bx * kBox, ins * dn + (int)rank * (dn / 2) + bx * 64, y);
+          }
+        }
+      }
+    };
+    // same order as the MMA warp below
+    if (kDK) emit_dp(0);
+    emit_s(0);
+    for (int u = 0; ok && u < U; ++u) {
+      if (u + 1 < U) {
+        if (kDK && unit_s(u + 1) == 0) emit_dp(u + 1);
+        emit_s(u + 1);
+      }
+      if (kDK || unit_s(u) == maps - 1) emit_acc(u);
+    }
+    if (rank == 0) {
+      mbar_wait_drain(&in_full, 0);
+      for (int i = (it > L.nst ? it - L.nst : 0); i < it; ++i) mbar_wait_drain(&r_full[i % L.nst], (i / L.nst) & 1u);
+    }
+  } else if (warp == 1 && lane == 0 && rank == 0) {
+    // ---------------------------------------------------------------- MMA issuer (leader)
+    const uint32_t idesc_s = idesc_f16(128, kTile, kBf16, false, false);
+    const uint32_t idesc_acc = kDK ? idesc_f16(128, L.ncol, kBf16, false, true)   // B = Q rows, MN-major
+                                   : idesc_f16(128, dn, kBf16, false, true);      // B = dY rows, MN-major
+    auto commit_both = [&](uint64_t* bar) {
+      mma_commit<2>(smem_u32(bar));
+      mma_commit<2>(mapa_shared(smem_u32(bar), 1));
+    };
+    int it = 0;
+    auto take = [&](uint32_t* addr) -> bool {
+      const int st = it % L.nst;
+      if (!mbar_wait(&r_full[st], (it / L.nst) & 1u, ab, 23)) return false;
+      tc_fence_after();
+      *addr = smem_u32(smem + L.off_ring + st * kStage);
+      return true;
+    };
+    auto give = [&]() { commit_both(&r_empty[it % L.nst]); ++it; };
+    const uint32_t ka = smem_u32(smem + L.off_a), va = smem_u32(smem + L.off_b);
+    auto issue_dp = [&](int u) -> bool {  // dP^T = V dY^T
+      const int g = unit_g(u), db = g & 1;
+      if (g >= 2 && !mbar_wait(&dp_free[db], ((g - 2) >> 1) & 1u, ab, 27)) return false;
+      for (int cc = 0; cc < p.D / 128; ++cc) {
+        uint32_t st;
+        if (!take(&st)) return false;
+        for (int k = 0; k < 8; ++k) {
+          const uint64_t ad = sdesc_sw128(va + (cc * 2 + (k >> 2)) * kBox + (k & 3) * 32, 16, 1024);
+          const uint64_t bd = sdesc_sw128(st + (k >> 2) * kBox + (k & 3) * 32, 16, 1024);
+          mma_f16_ss<2>(tmem + L.tmem_p + db * (kTile / 2), ad, bd, idesc_s, (cc | k) ? 1u : 0u);
+        }
+        give();
+      }
+      commit_both(&dp_full[db]);
+      return true;
+    };
+    auto issue_s = [&](int u) -> bool {  // S^T = K_s Q_s^T
+      const int sb = u & 1, s = unit_s(u);
+      if (u >= 2 && !mbar_wait(&p_full[sb], ((u - 2) >> 1) & 1u, ab, 22)) return false;
+      for (int cc = 0; cc < L.kw / 128; ++cc) {
+        uint32_t st;
+        if (!take(&st)) return false;
+        for (int k = 0; k < 8; ++k) {
+          const uint64_t ad =
+              sdesc_sw128(ka + (s * (L.kw / 64) + cc * 2 + (k >> 2)) * kBox + (k & 3) * 32, 16, 1024);
+          const uint64_t bd = sdesc_sw128(st + (k >> 2) * kBox + (k & 3) * 32, 16, 1024);
+          mma_f16_ss<2>(tmem + L.tmem_s + sb * (kTile / 2), ad, bd, idesc_s, (cc | k) ? 1u : 0u);
+        }
+        give();
+      }
+      commit_both(&s_full[sb]);
+      return true;
+    };
+    // dK: after every unit (dS_s^T in tile buffer u&1); dV: after the last map of a query tile
+    // (mixed P^T in tile buffer g&1).
+    auto issue_acc = [&](int u) -> bool {
+      const int g = unit_g(u), s = unit_s(u);
+      const int tb = kDK ? (u & 1) : (g & 1);
+      if (!mbar_wait(&p_full[u & 1], (u >> 1) & 1u, ab, 24)) return false;
+      tc_fence_after();
+      const uint32_t ta = smem_u32(smem + L.off_t + tb * (kRows * kTile * 2));
+      const int nins = kDK ? L.nins : dins;
+      const int ncol = kDK ? L.ncol : dn;
+      for (int qc = 0; qc < kTile / 64; ++qc)
+        for (int ins = 0; ins < nins; ++ins) {
+          uint32_t st;
+          if (!take(&st)) return false;
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t ad = sdesc_sw128(ta + qc * kBox + kk * 32, 16, 1024);
+            const uint64_t bd = sdesc_sw128(st + kk * 16 * 128, 64 * 128, 1024);
+            const uint32_t d = tmem + L.tmem_acc + (kDK ? s * (L.kw / 2) : 0) + ins * (ncol / 2);
+            mma_f16_ss<2>(d, ad, bd, idesc_acc, (g | qc | kk) ? 1u : 0u);
+          }
+          give();
+        }
+      commit_both(&t_empty[tb]);
+      return true;
+    };
+    bool ok = mbar_wait(&in_full, 0, ab, 21);
+    tc_fence_after();
+    if (ok && kDK) ok = issue_dp(0);
+    if (ok) ok = issue_s(0);
+    for (int u = 0; ok && u < U; ++u) {
+      if (u + 1 < U) {
+        if (kDK && unit_s(u + 1) == 0) ok = issue_dp(u + 1);
+        if (ok) ok = issue_s(u + 1);
+      }
+      if (ok && (kDK || unit_s(u) == maps - 1)) ok = issue_acc(u);
+    }
+    commit_both(&o_full);
+    mbar_wait_drain(&o_full, 0);
+  } else if (warp >= 2) {
+    // ---------------------------------------------------------------- softmax + epilogue
+    const int quad = warp & 3;
+    const int l = quad * 32 + lane;
+    const int r = l & 63, half = l >> 6;
+    const int key = k0 + 64 * (int)rank + r;
+    const bool live = key < p.T;
+    const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+    const uint32_t pf_leader = mapa_shared(smem_u32(&p_full[0]), 0);
+    const uint32_t df_leader = mapa_shared(smem_u32(&dp_free[0]), 0);
+    const bool arriver = (warp == 2 && lane == 0);
+    float* red = reinterpret_cast<float*>(smem + L.off_red);  // [tile parity][2][maps][128]: lse2, delta
+    const float kLog2e = 1.4426950408889634f;
+    const float gsc = rsqrtf((float)p.group);
+    float scale2[kMaxMaps], alpha[kMaxMaps];
+#pragma unroll
+    for (int s = 0; s < kMaxMaps; ++s) {
+      scale2[s] = s < maps ? p.scales[s] * gsc * kLog2e : 0.f;
+      alpha[s] = (s < maps && p.weights) ? p.weights[s] : 1.f;
+    }
+    float pm[kDK ? 1 : 64];
+    bool ok = true;
+    for (int u = 0; u < U; ++u) {
+      const int sb = u & 1, s = unit_s(u), g = unit_g(u);
+      const int qt = (i0 + g) * kTile;
+      float* rt = red + (g & 1) * (2 * kMaxMaps * 128);
+      if (s == 0) {  // stage this query tile's log-sum-exp (and delta) of every map
+        for (int m = 0; m < maps; ++m) {
+          const int q = qt + l;
+          const bool qv = q < p.T;
+          rt[m * 128 + l] = qv ? p.lse[((int64_t)b * maps + m) * p.T + q] * kLog2e : 0.f;
+          if (kDK) rt[(kMaxMaps + m) * 128 + l] = qv ? p.delta[((int64_t)b * maps + m) * p.T + q] : 0.f;
+        }
+      }
+      if (ok) ok = mbar_wait(&s_full[sb], (u >> 1) & 1u, ab, 32);
+      if (ok && kDK && s == 0) ok = mbar_wait(&dp_full[g & 1], (g >> 1) & 1u, ab, 35);
+      // the tile buffer written by this unit must have been read by the product two uses ago
+      if (ok && kDK && u >= 2) ok = mbar_wait(&t_empty[u & 1], ((u - 2) >> 1) & 1u, ab, 33);
+      if (ok && !kDK && s == 0 && g >= 2) ok = mbar_wait(&t_empty[g & 1], ((g - 2) >> 1) & 1u, ab, 33);
+      if (s == 0) named_bar_sync(1, 128);  // staged lse / delta visible
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok) {
+        tc_fence_after();
+        const uint32_t ta = smem_u32(smem + L.off_t + (kDK ? (u & 1) : (g & 1)) * (kRows * kTile * 2));
+        const float sc2 = scale2[s], al = alpha[s];
+        const float* lse_row = rt + s * 128;
+        const float* delta_row = rt + (kMaxMaps + s) * 128;
+#pragma unroll
+        for (int ch = 0; ch < 2; ++ch) {
+          float sv[32], dpv[32];
+          tmem_ld32(tmem + lane_base + L.tmem_s + sb * (kTile / 2) + ch * 32, sv);
+          if (kDK) tmem_ld32(tmem + lane_base + L.tmem_p + (g & 1) * (kTile / 2) + ch * 32, dpv);
+          tmem_wait_ld();
+          const int qc0 = half * 64 + ch * 32;  // query column inside the tile
+          // valid query columns e: lo <= e < hi (causal: queries at or after this key)
+          const int hi = live ? p.T - (qt + qc0) : 0;
+          const int lo = p.causal ? key - (qt + qc0) : 0;
+          uint32_t packed[16];
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            const float x0 = ex2(sv[e] * sc2 - lse_row[qc0 + e]), x1 = ex2(sv[e + 1] * sc2 - lse_row[qc0 + e + 1]);
+            const float p0 = (e >= lo && e < hi) ? x0 : 0.f, p1 = (e + 1 >= lo && e + 1 < hi) ? x1 : 0.f;
+            if (kDK) {
+              packed[e / 2] = pack2<T>(al * p0 * (dpv[e] - delta_row[qc0 + e]),
+                                       al * p1 * (dpv[e + 1] - delta_row[qc0 + e + 1]));
+            } else {
+              pm[ch * 32 + e] = s == 0 ? al * p0 : fmaf(al, p0, pm[ch * 32 + e]);
+              pm[ch * 32 + e + 1] = s == 0 ? al * p1 : fmaf(al, p1, pm[ch * 32 + e + 1]);
+              packed[e / 2] = pack2<T>(pm[ch * 32 + e], pm[ch * 32 + e + 1]);
+            }
+          }
+          if (kDK || s == maps - 1) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              st_shared_v4(ta + half * kBox + sw128_offset(r, ch * 4 + e), packed[4 * e], packed[4 * e + 1],
+                           packed[4 * e + 2], packed[4 * e + 3]);
+          }
+        }
+        if (kDK || s == maps - 1) fence_proxy_async();
+      }
+      tc_fence_before();
+      named_bar_sync(1, 128);
+      if (arriver) {
+        mbar_arrive_cluster(pf_leader + sb * 8);
+        if (kDK && s == maps - 1) mbar_arrive_cluster(df_leader + (g & 1) * 8);
+      }
+    }
+    if (ok) ok = mbar_wait(&o_full, 0, ab, 34);
+    ok = __all_sync(0xffffffffu, ok);
+    tc_fence_after();
+    if (ok && kDK && p.dk) {
+      for (int m = 0; m < maps; ++m) {
+        const float gamma = p.scales[m] * gsc;
+        for (int ins = 0; ins < L.nins; ++ins)
+          for (int c = 0; c < L.ncol / 2; c += 32) {
+            float vv[32];
+            tmem_ld32(tmem + lane_base + L.tmem_acc + m * (L.kw / 2) + ins * (L.ncol / 2) + c, vv);
+            tmem_wait_ld();
+            if (live) {
+              const int col = ins * L.ncol + half * (L.ncol / 2) + c;
+              const int gi = col / p.R;
+              const int64_t row = row_of(km.base, km.sb, km.sbr, b, p.branch0[m] + gi, key);
+              float* dst = p.dk + row * p.R + (col % p.R);
+#pragma unroll
+              for (int e = 0; e < 32; e += 4) {
+                float4 o = *reinterpret_cast<float4*>(dst + e);
+                o.x += gamma * vv[e];
+                o.y += gamma * vv[e + 1];
+                o.z += gamma * vv[e + 2];
+                o.w += gamma * vv[e + 3];
+                *reinterpret_cast<float4*>(dst + e) = o;
+              }
+            }
+          }
+      }
+    }
+    if (ok && !kDK && p.dv) {
+      for (int ins = 0; ins < dins; ++ins)
+        for (int c = 0; c < dn / 2; c += 32) {
+          float vv[32];
+          tmem_ld32(tmem + lane_base + L.tmem_acc + ins * (dn / 2) + c, vv);
+          tmem_wait_ld();
+          if (live) {
+            float* dst = p.dv + ((int64_t)b * p.T + key) * p.D + ins * dn + half * (dn / 2) + c;
+#pragma unroll
+            for (int e = 0; e < 32; e += 4) {
+              float4 o = *reinterpret_cast<float4*>(dst + e);
+              o.x += vv[e];
+              o.y += vv[e + 1];
+              o.z += vv[e + 2];
+              o.w += vv[e + 3];
+              *reinterpret_cast<float4*>(dst + e) = o;
+            }
+          }
+        }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  if (warp == 1) tmem_dealloc<2>(tmem, L.tmem_cols);
+}
+
+template <typename Kern>
+int launch_pair(Kern kern, const Layout& L, int pairs, const CUtensorMap& tq, const CUtensorMap& tk,
+                const CUtensorMap& tv, const CUtensorMap& tdy, const Params& p, cudaStream_t st) {
+  const int smem = (L.smem < 120 * 1024 ? 120 * 1024 : L.smem) + 1024;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return record_cuda_error();
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, tq, tk, tv, tdy, p) != cudaSuccess) return record_cuda_error();
+  note_launch();
+  return DA_OK;
+}
+
+}  // namespace bwdm
+}  // namespace attn
+}  // namespace da
+
+extern "C" int da_attn_bwd_mixed(const void* q, int64_t q_rows, int64_t q_base, int64_t q_sb, int64_t q_sbr,
+                                 const void* k, int64_t k_rows, int64_t k_base, int64_t k_sb, int64_t k_sbr,
+                                 const void* v, const void* dy, int B, int T, int R, int D, int maps, int group,
+                                 const int* branch0, int causal, int dtype, const float* scales,
+                                 const float* weights, const float* lse, float* delta, int delta_given, float* dq,
+                                 float* dk, float* dv, float* dscale, float* dweight, int* status, void* stream) {
+  using namespace da;
+  using namespace da::attn::bwdm;
+  if (!q || !k || !v || !dy || !branch0 || !scales || !lse || !delta || !status) return DA_ERR_NULL;
+  if (dtype != DA_BF16 && dtype != DA_F16) return DA_ERR_DTYPE;
+  if (int rc = bind_device(q)) return rc;
+  if (B <= 0 || T <= 0 || group < 1 || R <= 0 || R % 64 || maps < 1 || maps > attn::kMaxMaps) return DA_ERR_SHAPE;
+  if (D != 256 && D != 512) return DA_ERR_UNSUPPORTED;
+  const int kw = group * R;
+  if ((kw != 128 && kw != 256 && kw != 512) || maps * kw > 512) return DA_ERR_UNSUPPORTED;
+  for (int kind = 0; kind < 3; ++kind) {
+    const Layout L = make_layout(kind, maps, group, R, D);
+    if (L.nst < 2 || L.tmem_cols > 512) return DA_ERR_UNSUPPORTED;
+  }
+  if ((reinterpret_cast<uintptr_t>(dq) | reinterpret_cast<uintptr_t>(dk) | reinterpret_cast<uintptr_t>(dv)) & 15)
+    return DA_ERR_ALIGN;
+  Params p;
+  p.q_rows = q_rows; p.q_base = q_base; p.q_sb = q_sb; p.q_sbr = q_sbr;
+  p.k_rows = k_rows; p.k_base = k_base; p.k_sb = k_sb; p.k_sbr = k_sbr;
+  p.B = B; p.T = T; p.R = R; p.D = D; p.maps = maps; p.group = group; p.causal = causal;
+  for (int s = 0; s < attn::kMaxMaps; ++s) {
+    p.branch0[s] = s < maps ? branch0[s] : 0;
+    if (s < maps) {
+      if (p.branch0[s] < 0) return DA_ERR_SHAPE;
+      // every row a launch can address lies inside the row maps
+      const int64_t last_b = (int64_t)(B - 1), last_br = (int64_t)(p.branch0[s] + group - 1);
+      if (q_base + last_b * q_sb + last_br * q_sbr + (T - 1) >= q_rows) return DA_ERR_SHAPE;
+      if (k_base + last_b * k_sb + last_br * k_sbr + (T - 1) >= k_rows) return DA_ERR_SHAPE;
+    }
+  }
+  if (q_base < 0 || k_base < 0) return DA_ERR_SHAPE;
+  p.scales = scales; p.weights = weights; p.lse = lse; p.delta = delta; p.delta_given = delta_given;
+  p.dq = dq; p.dk = dk; p.dv = dv; p.dscale = dscale; p.dweight = dweight; p.status = status;
+  p.trace = debug_trace();
+  const CUtensorMapDataType tdt = dtype == DA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap tq, tk, tv, tdy;
+  int rc = make_tmap_2d(&tq, q, tdt, 2, R, q_rows, (uint64_t)R * 2, 64, 64);
+  if (rc) return rc;
+  rc = make_tmap_2d(&tk, k, tdt, 2, R, k_rows, (uint64_t)R * 2, 64, 64);
+  if (rc) return rc;
+  rc = make_tmap_2d(&tv, v, tdt, 2, D, (uint64_t)B * T, (uint64_t)D * 2, 64, 64);
+  if (rc) return rc;
+  rc = make_tmap_2d(&tdy, dy, tdt, 2, D, (uint64_t)B * T, (uint64_t)D * 2, 64, 64);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int pairs = B * ((T + kTile - 1) / kTile);
+  const bool bf16 = dtype == DA_BF16;
+  // the query-parallel kernel runs first: without a given delta it produces it for the other two
+  if (dq || dscale || !delta_given) {
+    const Layout L = make_layout(0, maps, group, R, D);
+    rc = bf16 ? launch_pair(dq_mixed_kernel<__nv_bfloat16>, L, pairs, tq, tk, tv, tdy, p, st)
+              : launch_pair(dq_mixed_kernel<__half>, L, pairs, tq, tk, tv, tdy, p, st);
+    if (rc) return rc;
+  }
+  if (dk) {
+    const Layout L = make_layout(1, maps, group, R, D);
+    rc = bf16 ? launch_pair(dkv_mixed_kernel<__nv_bfloat16, true>, L, pairs, tq, tk, tv, tdy, p, st)
+              : launch_pair(dkv_mixed_kernel<__half, true>, L, pairs, tq, tk, tv, tdy, p, st);
+    if (rc) return rc;
+  }
+  if (dv) {
+    const Layout L = make_layout(2, maps, group, R, D);
+    rc = bf16 ? launch_pair(dkv_mixed_kernel<__nv_bfloat16, false>, L, pairs, tq, tk, tv, tdy, p, st)
+              : launch_pair(dkv_mixed_kernel<__half, false>, L, pairs, tq, tk, tv, tdy, p, st);
+  }
+  return rc;
+}

@@ -525,6 +525,25 @@ def _attention_forward_delta(q: RowMap, k: RowMap, v: Tensor, dy: Tensor, batch:
     return lse, delta
 
 
+def _attention_backward(q: RowMap, k: RowMap, v: Tensor, dy: Tensor, batch: int, length: int, r: int, maps: int,
+                        group: int, branch0: list[int], causal: bool, scales: Tensor, weights: Tensor | None,
+                        lse: Tensor, delta: Tensor, delta_given: bool, dq: Tensor | None, dk: Tensor | None,
+                        dv: Tensor | None, dscale: Tensor | None, dweight: Tensor | None) -> None:
+    """All maps of one attention in one call (da_attn_bwd_mixed): fp32 gradients accumulated in place."""
+    d = v.shape[-1]
+    _attention_bwd_supported(r, d, group)
+    if maps * group * r > 512:
+        raise NotImplementedError(f"outer attention backward supports maps*group*R <= 512, got {maps * group * r}")
+    dev = v.device
+    ws = workspace(dev)
+    b0 = (ctypes_int_array(MAX_MAPS))(*(branch0 + [0] * (MAX_MAPS - len(branch0))))
+    call("da_attn_bwd_mixed", q.tensor.data_ptr(), q.rows, q.base, q.sb, q.sbr, k.tensor.data_ptr(), k.rows, k.base,
+         k.sb, k.sbr, v.data_ptr(), dy.data_ptr(), batch, length, r, d, maps, group, ctypes_addressof(b0),
+         int(causal), dtype_code(q.tensor.dtype), scales.data_ptr(), ptr(weights), lse.data_ptr(), delta.data_ptr(),
+         int(delta_given), ptr(dq), ptr(dk), ptr(dv), ptr(dscale), ptr(dweight), ws.status.data_ptr(),
+         stream_ptr(dev))
+
+
 def _attention_backward_map(q: RowMap, k: RowMap, v: Tensor, dy: Tensor, batch: int, length: int, r: int,
                             group: int, branch0: int, causal: bool, scale: Tensor, weight: Tensor | None,
                             lse: Tensor, delta: Tensor, dq: Tensor | None, dk: Tensor | None, dv: Tensor | None,
@@ -597,18 +616,12 @@ class _MixedAttention(torch.autograd.Function):
         sc = scales.detach().float().contiguous()
         wt = weights.detach().float().contiguous() if has_weights and maps > 1 else None
         dweight = torch.zeros(maps, dtype=torch.float32, device=flat.device) if wt is not None else None
-        v_fwd = value.detach().to(torch.bfloat16).contiguous() if maps > 1 else None
-        for s in range(maps):
-            if maps == 1:
-                lse_s, delta = lse[:, 0].contiguous(), _attention_delta(dy16, y)
-            else:  # delta needs the map's own output: recomputed in fp32, never stored
-                lse_s, delta = _attention_forward_delta(qmap, kmap, v_fwd, dy16, batch, length, r, group,
-                                                        branch0[s], causal, sc[s:s + 1], key_norm_bound)
-            if dweight is not None:
-                dweight[s] = delta.sum()
-            _attention_backward_map(qmap, kmap, v16, dy16, batch, length, r, group, branch0[s], causal,
-                                    sc[s:s + 1], None if wt is None else wt[s:s + 1], lse_s, delta, droute, droute,
-                                    dv, dscale[s:s + 1] if need[2] else None)
+        if maps == 1:  # delta from the saved output
+            delta, given = _attention_delta(dy16, y).view(batch, 1, length), True
+        else:  # computed exactly by the kernel's first sweep (the per-map outputs are never stored)
+            delta, given = torch.empty(batch, maps, length, dtype=torch.float32, device=flat.device), False
+        _attention_backward(qmap, kmap, v16, dy16, batch, length, r, maps, group, branch0, causal, sc, wt,
+                            lse.contiguous(), delta, given, droute, droute, dv, dscale if need[2] else None, dweight)
         g_routed = droute.view(routed.shape).to(dtype) if droute is not None else None
         g_value = dv.view(value.shape).to(value.dtype) if dv is not None else None
         g_scales = dscale.to(scales.dtype) if need[2] else None
@@ -662,10 +675,10 @@ class _SingleMapAttention(torch.autograd.Function):
         droute = torch.zeros(flat.shape, dtype=torch.float32, device=flat.device) if need[0] else None
         dv = torch.zeros(batch * length, d, dtype=torch.float32, device=flat.device) if need[1] else None
         dscale = torch.zeros(scales.shape[0], dtype=torch.float32, device=flat.device)
-        delta = _attention_delta(dy16, y)
-        _attention_backward_map(qmap, kmap, v16, dy16, batch, length, r, group, branch0[s], causal,
-                                scales.detach().float()[s:s + 1].contiguous(), None, lse[:, 0].contiguous(), delta,
-                                droute, droute, dv, dscale[s:s + 1] if need[2] else None)
+        delta = _attention_delta(dy16, y).view(batch, 1, length)
+        _attention_backward(qmap, kmap, v16, dy16, batch, length, r, 1, group, [branch0[s]], causal,
+                            scales.detach().float()[s:s + 1].contiguous(), None, lse.contiguous(), delta, True,
+                            droute, droute, dv, dscale[s:s + 1] if need[2] else None, None)
         return (droute.view(routed.shape).to(dtype) if droute is not None else None,
                 dv.view(value.shape).to(value.dtype) if dv is not None else None,
                 dscale.to(scales.dtype) if need[2] else None, None, None, None)
@@ -709,9 +722,10 @@ class _PerMapAttention(torch.autograd.Function):
         sc = scales.detach().float().contiguous()
         for s in range(maps):
             dy_s = dy[:, s].to(dtype).contiguous()
-            delta = _attention_delta(dy_s, out[:, s].contiguous())
-            _attention_backward_map(qmap, kmap, v16, dy_s, batch, length, r, 1, s, causal, sc[s:s + 1], None,
-                                    lses[s].contiguous(), delta, dq, dk, dv, dscale[s:s + 1] if need[3] else None)
+            delta = _attention_delta(dy_s, out[:, s].contiguous()).view(batch, 1, length)
+            _attention_backward(qmap, kmap, v16, dy_s, batch, length, r, 1, 1, [s], causal, sc[s:s + 1], None,
+                                lses[s].contiguous().view(batch, 1, length), delta, True, dq, dk, dv,
+                                dscale[s:s + 1] if need[3] else None, None)
         shape = (batch, maps, length, r)
         return (dq.view(shape).to(dtype) if dq is not None else None,
                 dk.view(shape).to(dtype) if dk is not None else None,

@@ -192,6 +192,24 @@ DA_API int da_attn_fwd_delta(const void* q, int64_t q_rows, int64_t q_base, int6
  * output may be null.  D in {256, 512}; group*R in {128, 256, 512}. */
 DA_API int da_attn_bwd_delta(const void* dy, const void* y, int64_t rows, int D, int dtype, float* delta,
                              void* stream);
+
+/* The whole backward of a (mixed) attention in one call, all maps at once
+ * (same reference interfaces as da_attn_bwd, plus the alpha-mix gradient):
+ * dP = dy.V^T is formed once per tile for every map and dV once from the
+ * mixed probabilities.  Arguments as da_attn_fwd (branch0: host array of
+ * `maps` ints), v / dy [B*T, D] in `dtype`, lse [B, maps, T] from the
+ * forward.  delta [B, maps, T]: read when delta_given (one map: from
+ * da_attn_bwd_delta on the saved output), else computed exactly by a first
+ * sweep and written.  Accumulates (+=) into fp32 dq / dk (Q / K rows; may be
+ * one buffer), dv [B*T, D], dscale [maps] (d gamma_s) and, when delta is
+ * computed, dweight [maps] (d alpha_s); any output may be null.
+ * D in {256, 512}; group*R in {128, 256, 512}; maps*group*R <= 512. */
+DA_API int da_attn_bwd_mixed(const void* q, int64_t q_rows, int64_t q_base, int64_t q_sb, int64_t q_sbr,
+                             const void* k, int64_t k_rows, int64_t k_base, int64_t k_sb, int64_t k_sbr,
+                             const void* v, const void* dy, int B, int T, int R, int D, int maps, int group,
+                             const int* branch0, int causal, int dtype, const float* scales, const float* weights,
+                             const float* lse, float* delta, int delta_given, float* dq, float* dk, float* dv,
+                             float* dscale, float* dweight, int* status, void* stream);
 DA_API int da_attn_bwd(const void* q, int64_t q_rows, int64_t q_base, int64_t q_sb, int64_t q_sbr, const void* k,
                        int64_t k_rows, int64_t k_base, int64_t k_sb, int64_t k_sbr, const void* v, const void* dy,
                        int B, int T, int R, int D, int group, int branch0, int causal, int dtype, const float* scale,
