@@ -47,11 +47,7 @@ SIGNATURES: dict[str, list] = {
     "da_gemm": [_p, _i64, _i32, _p, _i64, _i32, _p, _i64, _i64, _i64, _i64, _i32, _i32, _i32, _p, _p],
     "da_attn_fwd": [_p, _i64, _i64, _i64, _i64, _p, _i64, _i64, _i64, _i64, _p, _i32, _i32, _i32, _i32, _i32, _i32,
                     _p, _i32, _i32, _p, _p, _p, _f32, _p, _p, _p, _p],
-    "da_attn_fwd_delta": [_p, _i64, _i64, _i64, _i64, _p, _i64, _i64, _i64, _i64, _p, _p, _i32, _i32, _i32, _i32,
-                          _i32, _i32, _i32, _i32, _p, _p, _f32, _p, _p, _p, _p],
     "da_attn_bwd_delta": [_p, _p, _i64, _i32, _i32, _p, _p],
-    "da_attn_bwd": [_p, _i64, _i64, _i64, _i64, _p, _i64, _i64, _i64, _i64, _p, _p, _i32, _i32, _i32, _i32, _i32,
-                    _i32, _i32, _i32, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p],
     "da_gemm_splitk": [_p, _i64, _i32, _p, _i64, _i32, _p, _i64, _i64, _i64, _i64, _i32, _i32, _p, _p],
     "da_route_bwd": [_p, _i64, _i64, _i64, _i32, _i64, _i64, _i64, _i32, _p, _p, _p, _f32, _i32, _i32, _p, _p, _p,
                      _p, _p, _p, _p, _p, _p, _p, _p],

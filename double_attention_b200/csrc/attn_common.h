@@ -30,9 +30,7 @@ struct AttnFwdArgs {
   const float* weights;      // [maps] alpha_s (device) or null when maps == 1
   const float* key_norm_max; // [B * maps] upper bound of ||k|| per (b, map), or null -> key_norm_bound
   float key_norm_bound;
-  void* y;                   // [B, T, D] output (dtype), or null (delta mode)
-  const void* dy;            // delta mode (maps == 1): [B, T, D] upstream gradient (dtype), else null
-  float* delta;              // delta mode: [B, T] <dY, Y> with Y in fp32, else null
+  void* y;                   // [B, T, D] output (dtype)
   float* lse;                // [B, maps, T] natural-log sum of exp(gamma_s q.k) per map
   int* status;
 };

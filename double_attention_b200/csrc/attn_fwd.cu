@@ -110,9 +110,7 @@ struct FwdParams {
   const float* weights;
   const float* key_norm_max;
   float key_norm_bound;
-  void* y;            // may be null in delta mode
-  const void* dy;     // delta mode: upstream gradient rows
-  float* delta;       // delta mode: <dY, Y> per row
+  void* y;
   float* lse;
   int* status;
   int* trace;
@@ -500,7 +498,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     }
     tc_fence_after();
     const bool live = t < p.T;
-    float dd = 0.f;  // delta mode: this thread's share of <dY, Y>
     if (ok) {
       const size_t row_off = ((size_t)b * p.T + (live ? t : 0)) * p.D;
       for (int i = 0; i < L.npv; ++i) {
@@ -509,26 +506,13 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
           float o[32];
           tmem_ld32(tmem + lane_base + (uint32_t)(i * (L.nc / 2) + c), o);
           tmem_wait_ld();
-          if (live && p.y) {
+          if (live) {
             uint32_t w[16];
 #pragma unroll
             for (int e = 0; e < 16; ++e) w[e] = pack2<T>(o[2 * e] * inv_l, o[2 * e + 1] * inv_l);
             uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.y) + row_off + col0 + c);
 #pragma unroll
             for (int e = 0; e < 4; ++e) dst[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
-          }
-          if (!kMix && live && p.delta) {
-            const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.dy) + row_off + col0 + c);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const uint4 g = src[e];
-              const uint32_t gw[4] = {g.x, g.y, g.z, g.w};
-#pragma unroll
-              for (int h = 0; h < 4; ++h) {
-                const float2 gf = unpack2<T>(gw[h]);
-                dd = fmaf(o[8 * e + 2 * h] * inv_l, gf.x, fmaf(o[8 * e + 2 * h + 1] * inv_l, gf.y, dd));
-              }
-            }
           }
         }
       }
@@ -541,11 +525,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
           if (top < -100.f) atomicOr(p.status, DA_DEV_LOW_MASS);
         }
       }
-    }
-    if (!kMix && p.delta) {  // every softmax thread takes part (no early exit before this barrier)
-      red[l] = dd;
-      named_bar_sync(1, 128);
-      if (ok && live && half == 0) p.delta[(size_t)b * p.T + t] = dd + red[l ^ 64];
     }
   }
 
@@ -590,8 +569,6 @@ int launch(const AttnFwdArgs& a, cudaStream_t st) {
   p.key_norm_max = a.key_norm_max;
   p.key_norm_bound = a.key_norm_bound;
   p.y = a.y;
-  p.dy = a.dy;
-  p.delta = a.delta;
   p.lse = a.lse;
   p.status = a.status;
   p.trace = debug_trace();
@@ -664,50 +641,6 @@ extern "C" int da_attn_fwd(const void* q, int64_t q_rows, int64_t q_base, int64_
   a.key_norm_max = key_norm_max;
   a.key_norm_bound = key_norm_bound;
   a.y = y;
-  a.dy = nullptr;
-  a.delta = nullptr;
-  a.lse = lse;
-  a.status = status;
-  return attn::attn_fwd(a, static_cast<cudaStream_t>(stream));
-}
-
-extern "C" int da_attn_fwd_delta(const void* q, int64_t q_rows, int64_t q_base, int64_t q_sb, int64_t q_sbr,
-                                 const void* k, int64_t k_rows, int64_t k_base, int64_t k_sb, int64_t k_sbr,
-                                 const void* v, const void* dy, int B, int T, int R, int D, int group, int branch0,
-                                 int causal, int dtype, const float* scale, const float* key_norm_max,
-                                 float key_norm_bound, float* lse, float* delta, int* status, void* stream) {
-  using namespace da;
-  if (!q || !k || !v || !dy || !scale || !lse || !delta || !status) return DA_ERR_NULL;
-  if (int rc = bind_device(q)) return rc;
-  if (dtype != DA_BF16 && dtype != DA_F16) return DA_ERR_DTYPE;
-  if (B <= 0 || T <= 0 || group < 1 || branch0 < 0) return DA_ERR_SHAPE;
-  if (R % 64 || R <= 0 || group * R > 512) return DA_ERR_UNSUPPORTED;
-  if (D != 128 && D != 256 && D != 512) return DA_ERR_UNSUPPORTED;
-  {
-    const attn::Layout L = attn::make_layout(1, group, R, D, false);
-    if (L.nks < 2 || L.nsb < 2) return DA_ERR_UNSUPPORTED;
-  }
-  if ((reinterpret_cast<uintptr_t>(dy) & 15) || (reinterpret_cast<uintptr_t>(v) & 15)) return DA_ERR_ALIGN;
-  attn::AttnFwdArgs a;
-  a.q = {q, q_rows, q_base, q_sb, q_sbr};
-  a.k = {k, k_rows, k_base, k_sb, k_sbr};
-  a.v = v;
-  a.B = B;
-  a.T = T;
-  a.R = R;
-  a.D = D;
-  a.maps = 1;
-  a.group = group;
-  for (int s = 0; s < attn::kMaxMaps; ++s) a.branch0[s] = s == 0 ? branch0 : 0;
-  a.causal = causal;
-  a.dtype = dtype;
-  a.scales = scale;
-  a.weights = nullptr;
-  a.key_norm_max = key_norm_max;
-  a.key_norm_bound = key_norm_bound;
-  a.y = nullptr;
-  a.dy = dy;
-  a.delta = delta;
   a.lse = lse;
   a.status = status;
   return attn::attn_fwd(a, static_cast<cudaStream_t>(stream));

@@ -88,14 +88,21 @@ DA_DEV void mbar_arrive_cluster(uint32_t cluster_addr) {
                :: "r"(cluster_addr) : "memory");
 }
 
-// One bounded probe of a barrier phase: suspends for at most ~20 us.
+// Upper bound on how long one probe may suspend the thread (the hardware
+// resumes it earlier when the phase completes).
+#ifndef DA_SUSPEND_HINT_NS
+#define DA_SUSPEND_HINT_NS 20000u
+#endif
+constexpr uint32_t kSuspendHintNs = DA_SUSPEND_HINT_NS;
+
+// One bounded probe of a barrier phase.
 DA_DEV bool mbar_test(uint32_t addr, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok) : "r"(addr), "r"(parity), "r"(20000u) : "memory");
+      : "=r"(ok) : "r"(addr), "r"(parity), "r"(kSuspendHintNs) : "memory");
   return ok != 0;
 }
 
@@ -177,6 +184,14 @@ DA_DEV void tma_load_2d(const void* tmap, uint64_t* bar, void* dst, int x, int y
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4}], [%2];"
       :: "r"(smem_u32(dst)), "l"(tmap), "r"(smem_u32(bar)), "r"(x), "r"(y) : "memory");
+}
+
+// Warms L2 with one 2-D tile of this GPU's global memory (no shared memory,
+// no barrier): issued a few stages ahead of the real loads so that they hit
+// L2 instead of waiting on HBM.
+DA_DEV void tma_prefetch_2d(const void* tmap, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];"
+               :: "l"(tmap), "r"(x), "r"(y) : "memory");
 }
 
 // 2-D tiled load for a CTA pair running paired (cta_group::2) MMAs: the data

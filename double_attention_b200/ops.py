@@ -509,22 +509,6 @@ def _attention_delta(dy: Tensor, y: Tensor) -> Tensor:
     return delta
 
 
-def _attention_forward_delta(q: RowMap, k: RowMap, v: Tensor, dy: Tensor, batch: int, length: int, r: int,
-                             group: int, branch0: int, causal: bool, scale: Tensor,
-                             key_norm_bound: float) -> tuple[Tensor, Tensor]:
-    """One map's log-sum-exp [B, T] and delta = <dY, Y_map> [B*T] (Y_map in fp32), no output rows."""
-    d = v.shape[-1]
-    dev = v.device
-    lse = torch.empty(batch, length, dtype=torch.float32, device=dev)
-    delta = torch.empty(batch * length, dtype=torch.float32, device=dev)
-    ws = workspace(dev)
-    call("da_attn_fwd_delta", q.tensor.data_ptr(), q.rows, q.base, q.sb, q.sbr, k.tensor.data_ptr(), k.rows, k.base,
-         k.sb, k.sbr, v.data_ptr(), dy.data_ptr(), batch, length, r, d, group, branch0, int(causal),
-         dtype_code(q.tensor.dtype), scale.data_ptr(), None, float(key_norm_bound), lse.data_ptr(), delta.data_ptr(),
-         ws.status.data_ptr(), stream_ptr(dev))
-    return lse, delta
-
-
 def _attention_backward(q: RowMap, k: RowMap, v: Tensor, dy: Tensor, batch: int, length: int, r: int, maps: int,
                         group: int, branch0: list[int], causal: bool, scales: Tensor, weights: Tensor | None,
                         lse: Tensor, delta: Tensor, delta_given: bool, dq: Tensor | None, dk: Tensor | None,
@@ -542,21 +526,6 @@ def _attention_backward(q: RowMap, k: RowMap, v: Tensor, dy: Tensor, batch: int,
          int(causal), dtype_code(q.tensor.dtype), scales.data_ptr(), ptr(weights), lse.data_ptr(), delta.data_ptr(),
          int(delta_given), ptr(dq), ptr(dk), ptr(dv), ptr(dscale), ptr(dweight), ws.status.data_ptr(),
          stream_ptr(dev))
-
-
-def _attention_backward_map(q: RowMap, k: RowMap, v: Tensor, dy: Tensor, batch: int, length: int, r: int,
-                            group: int, branch0: int, causal: bool, scale: Tensor, weight: Tensor | None,
-                            lse: Tensor, delta: Tensor, dq: Tensor | None, dk: Tensor | None, dv: Tensor | None,
-                            dscale: Tensor | None) -> None:
-    """Accumulate one map's gradients into fp32 dq / dk (at the Q / K rows), dv and dscale."""
-    d = v.shape[-1]
-    _attention_bwd_supported(r, d, group)
-    dev = v.device
-    ws = workspace(dev)
-    call("da_attn_bwd", q.tensor.data_ptr(), q.rows, q.base, q.sb, q.sbr, k.tensor.data_ptr(), k.rows, k.base, k.sb,
-         k.sbr, v.data_ptr(), dy.data_ptr(), batch, length, r, d, group, branch0, int(causal),
-         dtype_code(q.tensor.dtype), scale.data_ptr(), ptr(weight), lse.data_ptr(), delta.data_ptr(), ptr(dq),
-         ptr(dk), ptr(dv), ptr(dscale), ws.status.data_ptr(), stream_ptr(dev))
 
 
 def ctypes_int_array(n: int):

@@ -163,38 +163,19 @@ DA_API int da_attn_fwd(const void* q, int64_t q_rows, int64_t q_base, int64_t q_
                        const float* scales, const float* weights, const float* key_norm_max, float key_norm_bound,
                        void* y, float* lse, int* status, void* stream);
 
-/* Delta pass for the backward of one map of a mixed attention (no reference
- * counterpart as one call; it stands for the per-map forward outputs the
- * reference keeps, triton_kernels.py:2022-2090, and its backward preprocess,
- * :2093-2160).  Recomputes map `branch0`'s softmax (same addressing and scale
- * as da_attn_fwd with maps = 1) and writes lse [B, T] and
- * delta [B, T] = <dy, Y_map> with Y_map = softmax(gamma Q K^T) V kept in fp32;
- * no output rows are written.  dy [B, T, D] in `dtype`. */
-DA_API int da_attn_fwd_delta(const void* q, int64_t q_rows, int64_t q_base, int64_t q_sb, int64_t q_sbr,
-                             const void* k, int64_t k_rows, int64_t k_base, int64_t k_sb, int64_t k_sbr,
-                             const void* v, const void* dy, int B, int T, int R, int D, int group, int branch0,
-                             int causal, int dtype, const float* scale, const float* key_norm_max,
-                             float key_norm_bound, float* lse, float* delta, int* status, void* stream);
-
 /* ---- outer routed attention, backward -----------------------------------
- * Replaces _routed_attention_triton_backward (triton_kernels.py:2093-2263:
- * the preprocess, dq, dk and dv kernels) for one score map, plus the
- * gradient of the alpha mix (modules.py:265-272) for that map.
- * da_attn_bwd_delta: delta[r] = <dy[r, :], y[r, :]> over `rows` rows of D
- * (D a multiple of 256; dtype bf16 or fp16), where y is the output of the map
- * alone (for one map: the forward output).
- * da_attn_bwd: one map (`group` branches from branch0, same row maps and
- * scale as da_attn_fwd), v / dy [B*T, D] in `dtype` (same as q/k), scale ->
- * gamma_s, weight -> alpha_s (null: 1), lse [B, T] natural-log normaliser of
- * this map, delta [B, T] from da_attn_bwd_delta.  Accumulates (+=) into fp32
- * outputs: dq / dk at the Q / K rows ([rows, R] matrices; may be one buffer
- * when the row maps do not overlap), dv [B*T, D], dscale (d gamma_s); any
- * output may be null.  D in {256, 512}; group*R in {128, 256, 512}. */
+ * Replaces the preprocess kernel of _routed_attention_triton_backward
+ * (triton_kernels.py:2093-2160): delta[r] = <dy[r, :], y[r, :]> over `rows`
+ * rows of D (D a multiple of 256; dtype bf16 or fp16), y the output of one map
+ * (the forward output when there is one map).  The products of the backward
+ * are da_attn_bwd_mixed below. */
 DA_API int da_attn_bwd_delta(const void* dy, const void* y, int64_t rows, int D, int dtype, float* delta,
                              void* stream);
 
 /* The whole backward of a (mixed) attention in one call, all maps at once
- * (same reference interfaces as da_attn_bwd, plus the alpha-mix gradient):
+ * Replaces the dq, dk and dv kernels and the atomic d-scale of
+ * _routed_attention_triton_backward (triton_kernels.py:2093-2263), plus the
+ * gradient of the alpha mix (modules.py:265-272):
  * dP = dy.V^T is formed once per tile for every map and dV once from the
  * mixed probabilities.  Arguments as da_attn_fwd (branch0: host array of
  * `maps` ints), v / dy [B*T, D] in `dtype`, lse [B, maps, T] from the
@@ -210,12 +191,6 @@ DA_API int da_attn_bwd_mixed(const void* q, int64_t q_rows, int64_t q_base, int6
                              const int* branch0, int causal, int dtype, const float* scales, const float* weights,
                              const float* lse, float* delta, int delta_given, float* dq, float* dk, float* dv,
                              float* dscale, float* dweight, int* status, void* stream);
-DA_API int da_attn_bwd(const void* q, int64_t q_rows, int64_t q_base, int64_t q_sb, int64_t q_sbr, const void* k,
-                       int64_t k_rows, int64_t k_base, int64_t k_sb, int64_t k_sbr, const void* v, const void* dy,
-                       int B, int T, int R, int D, int group, int branch0, int causal, int dtype, const float* scale,
-                       const float* weight, const float* lse, const float* delta, float* dq, float* dk, float* dv,
-                       float* dscale, int* status, void* stream);
-
 /* ---- dense GEMM (fused Q/K projection and its backward) -----------------
  * Replaces the cuBLAS GEMM of _project_query_key (modules.py:143-157,
  * F.linear(x, cat(W_q, W_k))) and its autograd backward.
