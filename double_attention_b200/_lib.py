@@ -38,7 +38,9 @@ _f32 = ctypes.c_float
 # name -> argument types; every entry point returns int.
 SIGNATURES: dict[str, list] = {
     "da_dict_norm_fwd": [_p, _i64, _i64, _f32, _i32, _p, _p, _p, _p, _p],
-    "da_dict_norm_pair_fwd": [_p, _p, _i64, _i64, _f32, _i32, _p, _p, _p, _p, _p, _p, _p, _p],
+    "da_dict_norm_pair_fwd": [_p, _p, _i32, _i64, _i64, _f32, _i32, _p, _p, _p, _p, _p, _p, _p, _p],
+    "da_temperatures": [_p, _i32, _f32, _f32, _p, _i32, _i32, _f32, _f32, _p, _p, _p],
+    "da_gemm_segments": [_p, _i64, _i64, _i64, _i32, _i32, _p, _p, _p, _p, _p, _p, _p, _p, _p],
     "da_dict_norm_bwd": [_p, _p, _p, _p, _i64, _i64, _f32, _p, _i32, _p],
     "da_col_norm_max": [_p, _i64, _i64, _i32, _p, _p],
     "da_set_debug_trace": [_p],

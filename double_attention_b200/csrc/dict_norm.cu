@@ -79,9 +79,9 @@ __global__ void __launch_bounds__(256) dict_norm_fwd_kernel(const float* __restr
 // 1: value in bf16), eight columns per CTA so that even a 512-atom bank
 // spreads over 128 CTAs.  Each thread keeps its column's rows in shared
 // memory between the norm and the write passes.
-template <typename TK>
-__global__ void __launch_bounds__(256) dict_norm_pair_kernel(const float* __restrict__ raw_key,
-                                                             const float* __restrict__ raw_value, int R, int M,
+template <typename TR, typename TK>
+__global__ void __launch_bounds__(256) dict_norm_pair_kernel(const TR* __restrict__ raw_key,
+                                                             const TR* __restrict__ raw_value, int R, int M,
                                                              float eps, TK* __restrict__ key, TK* __restrict__ key_t,
                                                              float* __restrict__ key_denom,
                                                              float* __restrict__ key_max,
@@ -91,14 +91,14 @@ __global__ void __launch_bounds__(256) dict_norm_pair_kernel(const float* __rest
   extern __shared__ float tile8[];  // [R][9]
   __shared__ float part[32][9], colden[8];
   const bool is_key = blockIdx.y == 0;
-  const float* raw = is_key ? raw_key : raw_value;
+  const TR* raw = is_key ? raw_key : raw_value;
   const int tx = threadIdx.x & 7, ty = threadIdx.x >> 3;
   const int j0 = blockIdx.x * 8, j = j0 + tx;
   const bool col = j < M;
   float ss = 0.f;
 #pragma unroll 8
   for (int r = ty; r < R; r += 32) {
-    const float v = col ? raw[(size_t)r * M + j] : 0.f;
+    const float v = col ? static_cast<float>(raw[(size_t)r * M + j]) : 0.f;
     tile8[r * 9 + tx] = v;
     ss = fmaf(v, v, ss);
   }
@@ -302,32 +302,79 @@ extern "C" int da_col_norm_max(const void* dict, int64_t R, int64_t M, int dtype
   return DA_OK;
 }
 
-extern "C" int da_dict_norm_pair_fwd(const float* raw_key, const float* raw_value, int64_t R, int64_t M, float eps,
-                                     int key_dtype, void* key, void* key_t, float* key_denom, float* key_max,
-                                     void* value, void* value_t, float* value_denom, void* stream) {
+extern "C" int da_dict_norm_pair_fwd(const void* raw_key, const void* raw_value, int raw_dtype, int64_t R,
+                                     int64_t M, float eps, int key_dtype, void* key, void* key_t, float* key_denom,
+                                     float* key_max, void* value, void* value_t, float* value_denom, void* stream) {
   using namespace da;
   if (!raw_key) return DA_ERR_NULL;
   if (int rc = bind_device(raw_key)) return rc;
   if (R <= 0 || M <= 0 || R > 1536 || M > (1 << 24)) return DA_ERR_SHAPE;
   if (key_dtype != DA_BF16 && key_dtype != DA_F16) return DA_ERR_DTYPE;
+  if (raw_dtype != DA_F32 && raw_dtype != DA_BF16 && raw_dtype != DA_F16) return DA_ERR_DTYPE;
   const bool with_value = raw_value && (value || value_t || value_denom);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (key_max && cudaMemsetAsync(key_max, 0, sizeof(float), st) != cudaSuccess) return record_cuda_error();
   const dim3 grid((unsigned)((M + 7) / 8), with_value ? 2u : 1u), block(256);
   const size_t smem = (size_t)R * 9 * sizeof(float);
-  if (key_dtype == DA_BF16) {
-    auto k = dict_norm_pair_kernel<__nv_bfloat16>;
-    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+  auto run = [&](auto kern, auto raw_tag, auto key_tag) -> int {
+    using TR = decltype(raw_tag);
+    using TK = decltype(key_tag);
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return record_cuda_error();
-    k<<<grid, block, smem, st>>>(raw_key, raw_value, (int)R, (int)M, eps, (__nv_bfloat16*)key, (__nv_bfloat16*)key_t,
-                                 key_denom, key_max, (__nv_bfloat16*)value, (__nv_bfloat16*)value_t, value_denom);
-  } else {
-    auto k = dict_norm_pair_kernel<__half>;
-    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-      return record_cuda_error();
-    k<<<grid, block, smem, st>>>(raw_key, raw_value, (int)R, (int)M, eps, (__half*)key, (__half*)key_t, key_denom,
-                                 key_max, (__nv_bfloat16*)value, (__nv_bfloat16*)value_t, value_denom);
-  }
+    kern<<<grid, block, smem, st>>>(static_cast<const TR*>(raw_key), static_cast<const TR*>(raw_value), (int)R,
+                                    (int)M, eps, static_cast<TK*>(key), static_cast<TK*>(key_t), key_denom, key_max,
+                                    static_cast<__nv_bfloat16*>(value), static_cast<__nv_bfloat16*>(value_t),
+                                    value_denom);
+    if (cudaPeekAtLastError() != cudaSuccess) return record_cuda_error();
+    note_launch();
+    return DA_OK;
+  };
+  const bool kb = key_dtype == DA_BF16;
+  if (raw_dtype == DA_F32)
+    return kb ? run(dict_norm_pair_kernel<float, __nv_bfloat16>, float{}, __nv_bfloat16{})
+              : run(dict_norm_pair_kernel<float, __half>, float{}, __half{});
+  if (raw_dtype == DA_BF16)
+    return kb ? run(dict_norm_pair_kernel<__nv_bfloat16, __nv_bfloat16>, __nv_bfloat16{}, __nv_bfloat16{})
+              : run(dict_norm_pair_kernel<__nv_bfloat16, __half>, __nv_bfloat16{}, __half{});
+  return kb ? run(dict_norm_pair_kernel<__half, __nv_bfloat16>, __half{}, __nv_bfloat16{})
+            : run(dict_norm_pair_kernel<__half, __half>, __half{}, __half{});
+}
+
+// ---- temperatures: beta = exp(clamp(log_beta)), gamma_s = exp(clamp(log_gamma_s)) in fp32
+namespace da {
+namespace {
+template <typename T>
+DA_DEV float load_as_float(const void* p, int i) {
+  return static_cast<float>(static_cast<const T*>(p)[i]);
+}
+DA_DEV float load_any(const void* p, int dtype, int i) {
+  if (dtype == DA_F32) return static_cast<const float*>(p)[i];
+  if (dtype == DA_BF16) return load_as_float<__nv_bfloat16>(p, i);
+  return load_as_float<__half>(p, i);
+}
+__global__ void temperatures_kernel(const void* log_beta, int beta_dtype, float beta_lo, float beta_hi,
+                                    const void* log_scales, int scales_dtype, int maps, float scale_lo,
+                                    float scale_hi, float* beta_out, float* scales_out) {
+  const int i = threadIdx.x;
+  if (i == 0 && log_beta) beta_out[0] = expf(fminf(fmaxf(load_any(log_beta, beta_dtype, 0), beta_lo), beta_hi));
+  if (i < maps && log_scales)
+    scales_out[i] = expf(fminf(fmaxf(load_any(log_scales, scales_dtype, i), scale_lo), scale_hi));
+}
+}  // namespace
+}  // namespace da
+
+extern "C" int da_temperatures(const void* log_beta, int beta_dtype, float beta_lo, float beta_hi,
+                               const void* log_scales, int scales_dtype, int maps, float scale_lo, float scale_hi,
+                               float* beta_out, float* scales_out, void* stream) {
+  using namespace da;
+  if ((log_beta && !beta_out) || (log_scales && !scales_out) || (!log_beta && !log_scales)) return DA_ERR_NULL;
+  if (int rc = bind_device(log_beta ? log_beta : log_scales)) return rc;
+  if (maps < 0 || maps > 32) return DA_ERR_SHAPE;
+  for (int d : {beta_dtype, scales_dtype})
+    if (d != DA_F32 && d != DA_BF16 && d != DA_F16) return DA_ERR_DTYPE;
+  temperatures_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(log_beta, beta_dtype, beta_lo, beta_hi,
+                                                                         log_scales, scales_dtype, maps, scale_lo,
+                                                                         scale_hi, beta_out, scales_out);
   if (cudaPeekAtLastError() != cudaSuccess) return record_cuda_error();
   note_launch();
   return DA_OK;

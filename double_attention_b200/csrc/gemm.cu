@@ -169,6 +169,146 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   if (warp == 1) tmem_dealloc<1>(tmem, kN);
 }
 
+// Several GEMMs that share the A operand, one launch: output columns are
+// split into segments, each with its own weight matrix B_s [N_s, K] (K-major),
+// output C_s (its own leading dimension and dtype) and optional bias.  Used for
+// the Q, K and V projections of one input (modules.py:143-157 and the value
+// projection): x is read once and V is written directly in the bf16 the
+// attention's P.V product reads.  Every segment width is a multiple of kN, so
+// a CTA's tile lies inside one segment.
+constexpr int kMaxSeg = 3;
+
+struct SegParams {
+  int M, K, nseg;
+  int seg_n0[kMaxSeg + 1];  // first global column of each segment; seg_n0[nseg] = total columns
+  void* c[kMaxSeg];
+  int64_t ldc[kMaxSeg];
+  int out_dtype[kMaxSeg];   // DA_F16 / DA_BF16 / DA_F32
+  const void* bias[kMaxSeg];  // [N_s] in the operand dtype, or null
+  int* status;
+};
+
+template <typename T, int kN>
+__global__ void __launch_bounds__(kThreads, 1) gemm_seg_kernel(const __grid_constant__ CUtensorMap ta,
+                                                               const __grid_constant__ CUtensorMap tb0,
+                                                               const __grid_constant__ CUtensorMap tb1,
+                                                               const __grid_constant__ CUtensorMap tb2,
+                                                               const SegParams p) {
+  using C = Cfg<kN>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t full[C::kStages], empty[C::kStages], done;
+  __shared__ uint32_t tmem_base;
+  __shared__ int abort_flag;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int m0 = blockIdx.x * kBM, gn0 = blockIdx.y * kN;
+  int seg = 0;
+  while (seg + 1 < p.nseg && gn0 >= p.seg_n0[seg + 1]) ++seg;
+  const int n0 = gn0 - p.seg_n0[seg];  // column inside the segment
+  const CUtensorMap* tb = seg == 0 ? &tb0 : (seg == 1 ? &tb1 : &tb2);
+  const int nk = (p.K + kBK - 1) / kBK;
+  Abort ab{&abort_flag, p.status};
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc<1>(&tmem_base, kN);
+    tmem_relinquish<1>();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&ta);
+      prefetch_tmap(tb);
+      int issued = 0;
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % C::kStages;
+        if (!mbar_wait(&empty[s], ((kb / C::kStages) & 1u) ^ 1u, ab, 41)) break;
+        mbar_arrive_expect_tx(&full[s], C::kABytes + C::kBBytes);
+        uint8_t* sa = smem + s * (C::kABytes + C::kBBytes);
+        tma_load_2d(&ta, &full[s], sa, kb * kBK, m0);
+        tma_load_2d(tb, &full[s], sa + C::kABytes, kb * kBK, n0);
+        issued = kb + 1;
+      }
+      for (int kb = (issued > C::kStages ? issued - C::kStages : 0); kb < issued; ++kb)
+        mbar_wait_drain(&full[kb % C::kStages], (kb / C::kStages) & 1u);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16(kBM, kN, std::is_same<T, __nv_bfloat16>::value, false, false);
+      bool ok = true;
+      for (int kb = 0; ok && kb < nk; ++kb) {
+        const int s = kb % C::kStages;
+        ok = mbar_wait(&full[s], (kb / C::kStages) & 1u, ab, 42);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t sa = smem_u32(smem + s * (C::kABytes + C::kBBytes));
+        const uint32_t sb = sa + C::kABytes;
+#pragma unroll
+        for (int k = 0; k < kBK / 16; ++k)
+          mma_f16_ss<1>(tmem, sdesc_sw128(sa + k * 32, 16, 1024), sdesc_sw128(sb + k * 32, 16, 1024), idesc,
+                        (kb > 0 || k > 0) ? 1u : 0u);
+        mma_commit<1>(smem_u32(&empty[s]));
+      }
+      mma_commit<1>(smem_u32(&done));
+      mbar_wait_drain(&done, 0);
+    }
+  } else {
+    const int quad = warp & 3;
+    const int row = m0 + quad * 32 + lane;
+    bool ok = mbar_wait(&done, 0, ab, 43);
+    ok = __all_sync(0xffffffffu, ok);
+    tc_fence_after();
+    if (ok) {
+      const bool live = row < p.M;
+      const int od = p.out_dtype[seg];
+      const T* bias = static_cast<const T*>(p.bias[seg]);
+      for (int c = 0; c < kN; c += 32) {
+        float v[32];
+        tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + c, v);
+        tmem_wait_ld();
+        if (!live) continue;
+        if (bias) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) v[e] += static_cast<float>(bias[n0 + c + e]);
+        }
+        char* base = static_cast<char*>(p.c[seg]);
+        if (od == DA_F32) {
+          float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(base) + (size_t)row * p.ldc[seg] + n0 + c);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) dst[e] = make_float4(v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3]);
+        } else {
+          uint32_t w[16];
+          if (od == DA_BF16) {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) w[e] = pack_bf16x2(v[2 * e], v[2 * e + 1]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) w[e] = pack_f16x2(v[2 * e], v[2 * e + 1]);
+          }
+          uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(base) + (size_t)row * p.ldc[seg] + n0 + c);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) dst[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc<1>(tmem, kN);
+}
+
 template <typename T, int kN, bool kAmn, bool kBmn>
 int launch(const void* A, int64_t lda, const void* B, int64_t ldb, const Params& p, int splits, cudaStream_t st) {
   using C = Cfg<kN>;
@@ -254,4 +394,73 @@ extern "C" int da_gemm_splitk(const void* A, int64_t lda, int a_mn_major, const 
   if (dtype == DA_BF16)
     return gemm::dispatch<__nv_bfloat16>(a_mn_major, b_mn_major, n_tile, A, lda, B, ldb, p, splits, st);
   return gemm::dispatch<__half>(a_mn_major, b_mn_major, n_tile, A, lda, B, ldb, p, splits, st);
+}
+
+extern "C" int da_gemm_segments(const void* A, int64_t lda, int64_t M, int64_t K, int dtype, int nseg,
+                                const void* const* B, const int64_t* ldb, const int64_t* N, void* const* C,
+                                const int64_t* ldc, const int* out_dtype, const void* const* bias, int* status,
+                                void* stream) {
+  using namespace da;
+  using namespace da::gemm;
+  if (!A || !B || !N || !C || !ldc || !ldb || !out_dtype || !status) return DA_ERR_NULL;
+  if (int rc = bind_device(A)) return rc;
+  if (dtype != DA_BF16 && dtype != DA_F16) return DA_ERR_DTYPE;
+  if (nseg < 1 || nseg > kMaxSeg || M <= 0 || K <= 0) return DA_ERR_SHAPE;
+  if (lda % 8) return DA_ERR_ALIGN;
+  SegParams p;
+  p.M = (int)M;
+  p.K = (int)K;
+  p.nseg = nseg;
+  p.status = status;
+  int64_t total = 0;
+  bool all256 = true;
+  for (int s = 0; s < nseg; ++s) {
+    if (!B[s] || !C[s]) return DA_ERR_NULL;
+    if (N[s] <= 0 || N[s] % 128) return DA_ERR_SHAPE;
+    if (N[s] % 256) all256 = false;
+    if (ldb[s] % 8) return DA_ERR_ALIGN;
+    const int od = out_dtype[s];
+    if (od != DA_F16 && od != DA_BF16 && od != DA_F32) return DA_ERR_DTYPE;
+    if ((reinterpret_cast<uintptr_t>(C[s]) & 15) || (ldc[s] % 8)) return DA_ERR_ALIGN;
+    p.seg_n0[s] = (int)total;
+    p.c[s] = C[s];
+    p.ldc[s] = ldc[s];
+    p.out_dtype[s] = od;
+    p.bias[s] = bias ? bias[s] : nullptr;
+    total += N[s];
+  }
+  p.seg_n0[nseg] = (int)total;
+  for (int s = nseg; s < kMaxSeg; ++s) {
+    p.seg_n0[s + 1 <= kMaxSeg ? s + 1 : kMaxSeg] = (int)total;
+    p.c[s] = nullptr;
+    p.ldc[s] = 0;
+    p.out_dtype[s] = DA_F32;
+    p.bias[s] = nullptr;
+  }
+  const CUtensorMapDataType dt = dtype == DA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const int n_tile = (all256 && (M / 128) * (total / 256) >= 120) ? 256 : 128;
+  CUtensorMap ta, tb[kMaxSeg];
+  int rc = make_tmap_2d(&ta, A, dt, 2, K, M, (uint64_t)lda * 2, 64, kBM);
+  if (rc) return rc;
+  for (int s = 0; s < kMaxSeg; ++s) {
+    const int si = s < nseg ? s : 0;
+    rc = make_tmap_2d(&tb[s], B[si], dt, 2, K, N[si], (uint64_t)ldb[si] * 2, 64, n_tile);
+    if (rc) return rc;
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  dim3 grid((unsigned)((M + kBM - 1) / kBM), (unsigned)(total / n_tile), 1);
+  auto run = [&](auto kern, int smem_bytes) -> int {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes) != cudaSuccess)
+      return record_cuda_error();
+    kern<<<grid, kThreads, smem_bytes, st>>>(ta, tb[0], tb[1], tb[2], p);
+    if (cudaPeekAtLastError() != cudaSuccess) return record_cuda_error();
+    note_launch();
+    return DA_OK;
+  };
+  const bool bf16 = dtype == DA_BF16;
+  if (n_tile == 256)
+    return bf16 ? run(gemm_seg_kernel<__nv_bfloat16, 256>, Cfg<256>::kSmem + 1024)
+                : run(gemm_seg_kernel<__half, 256>, Cfg<256>::kSmem + 1024);
+  return bf16 ? run(gemm_seg_kernel<__nv_bfloat16, 128>, Cfg<128>::kSmem + 1024)
+              : run(gemm_seg_kernel<__half, 128>, Cfg<128>::kSmem + 1024);
 }

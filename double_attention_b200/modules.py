@@ -171,15 +171,16 @@ class SharedDictionaryAttention(nn.Module):
             views = ops.dictionary_views(active_bank.raw_key, active_bank.raw_value, cfg.eps, compute_dtype)
 
         xc = x.to(compute_dtype)
-        fused_weight = torch.cat((self.query.weight, self.key.weight), dim=0).to(compute_dtype)
-        projected = ops.qk_projection(xc, fused_weight)  # [B*T, 2*H*R]
-        dense_value = self.value(xc) if xc.dtype == self.value.weight.dtype else F.linear(
-            xc, self.value.weight.to(compute_dtype),
-            None if self.value.bias is None else self.value.bias.to(compute_dtype))
+        # Q, K and V projections of x in one launch; V comes out in the bf16 the attention reads
+        projected, dense_value = ops.qkv_projection(
+            xc, self.query.weight.to(compute_dtype), self.key.weight.to(compute_dtype),
+            self.value.weight.to(compute_dtype),
+            None if self.value.bias is None else self.value.bias.to(compute_dtype))  # [B*T, 2*H*R], [B*T, D]
+        dense_value = dense_value.view(x.shape[0], x.shape[1], -1)
+        beta, score_scales = ops.temperatures(self.log_beta, self.log_score_scales)  # fp32, one launch
 
-        routed = ops.route_projected(projected, views, self.beta, cfg, x.shape[0], x.shape[1])  # [2,H,B,T,R]
+        routed = ops.route_projected(projected, views, beta, cfg, x.shape[0], x.shape[1])  # [2,H,B,T,R]
         routed_query, routed_key = routed[0].permute(1, 0, 2, 3), routed[1].permute(1, 0, 2, 3)
-        score_scales = ops.score_scale_from_log(self.log_score_scales)
         if cfg.map_combine == "weighted_sum" and self.map_mix_logits is not None:
             map_weights = torch.softmax(self.map_mix_logits, dim=0)
         else:

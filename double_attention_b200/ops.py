@@ -208,8 +208,8 @@ class _DictNormPair(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, raw_key: Tensor, raw_value: Tensor | None, eps: float, dtype: torch.dtype):  # type: ignore[override]
-        rk = raw_key.detach().contiguous().float()
-        rv = rk if raw_value is None else raw_value.detach().contiguous().float()
+        rk = raw_key.detach().contiguous()  # fp32, or the half type of a cast module (read as is)
+        rv = rk if raw_value is None else raw_value.detach().to(rk.dtype).contiguous()
         r, m = rk.shape
         dev = rk.device
         key = torch.empty(r, m, dtype=dtype, device=dev)
@@ -219,10 +219,12 @@ class _DictNormPair(torch.autograd.Function):
         kden = torch.empty(m, dtype=torch.float32, device=dev)
         vden = torch.empty(m, dtype=torch.float32, device=dev)
         kmax = torch.empty(1, dtype=torch.float32, device=dev)
-        call("da_dict_norm_pair_fwd", rk.data_ptr(), rv.data_ptr(), r, m, eps, dtype_code(dtype), key.data_ptr(),
+        call("da_dict_norm_pair_fwd", rk.data_ptr(), rv.data_ptr(), dtype_code(rk.dtype), r, m, eps, dtype_code(dtype),
+             key.data_ptr(),
              key_t.data_ptr(), kden.data_ptr(), kmax.data_ptr(), value.data_ptr(), value_t.data_ptr(),
              vden.data_ptr(), stream_ptr(dev))
         ctx.save_for_backward(rk, rv, kden, vden)
+        ctx.raw_dtype = raw_key.dtype
         ctx.eps = eps
         ctx.tied = raw_value is None
         ctx.mark_non_differentiable(kmax)
@@ -233,6 +235,7 @@ class _DictNormPair(torch.autograd.Function):
     @staticmethod
     def backward(ctx, g_key, g_key_t, _g_kmax, g_key_anchor, g_value, g_value_t, g_value_anchor):  # type: ignore[override]
         rk, rv, kden, vden = ctx.saved_tensors
+        rk, rv = rk.float(), rv.float()  # the normalisation backward works on fp32 banks
         r, m = rk.shape
         dev = rk.device
 
@@ -259,7 +262,50 @@ class _DictNormPair(torch.autograd.Function):
                 grad_value = torch.empty_like(rv)
                 call("da_dict_norm_bwd", rv.data_ptr(), vden.data_ptr(), ptr(gv), ptr(gvt), r, m, ctx.eps,
                      grad_value.data_ptr(), 0, stream_ptr(dev))
+        if grad_key is not None:
+            grad_key = grad_key.to(ctx.raw_dtype)
+        if grad_value is not None:
+            grad_value = grad_value.to(ctx.raw_dtype)
         return grad_key, grad_value, None, None
+
+
+# ----------------------------------------------------------------------------- temperatures
+BETA_LOG_RANGE = (math.log(0.05), math.log(64.0))     # modules.py:130-132
+SCALE_LOG_RANGE = (math.log(0.25), math.log(1024.0))  # ops.py:160-161
+
+
+class _Temperatures(torch.autograd.Function):
+    """beta and the per-map score scales in fp32 from their logs, one launch."""
+
+    @staticmethod
+    def forward(ctx, log_beta: Tensor, log_scales: Tensor):  # type: ignore[override]
+        dev = log_scales.device
+        beta = torch.empty(1, dtype=torch.float32, device=dev)
+        scales = torch.empty(log_scales.numel(), dtype=torch.float32, device=dev)
+        lb, ls = log_beta.detach().contiguous(), log_scales.detach().contiguous()
+        call("da_temperatures", lb.data_ptr(), dtype_code(lb.dtype), BETA_LOG_RANGE[0], BETA_LOG_RANGE[1],
+             ls.data_ptr(), dtype_code(ls.dtype), ls.numel(), SCALE_LOG_RANGE[0], SCALE_LOG_RANGE[1],
+             beta.data_ptr(), scales.data_ptr(), stream_ptr(dev))
+        ctx.save_for_backward(log_beta, log_scales, beta, scales)
+        return beta, scales
+
+    @staticmethod
+    def backward(ctx, g_beta, g_scales):  # type: ignore[override]
+        log_beta, log_scales, beta, scales = ctx.saved_tensors
+
+        def through_clamp(log_v, value, g, bounds):
+            if g is None:
+                return None
+            inside = (log_v.detach().float() >= bounds[0]) & (log_v.detach().float() <= bounds[1])
+            return (g * value * inside.float().reshape(value.shape)).reshape(log_v.shape).to(log_v.dtype)
+
+        return (through_clamp(log_beta, beta, g_beta, BETA_LOG_RANGE),
+                through_clamp(log_scales, scales, g_scales, SCALE_LOG_RANGE))
+
+
+def temperatures(log_beta: Tensor, log_scales: Tensor) -> tuple[Tensor, Tensor]:
+    """``(beta [1], scales [S])`` in fp32: exp of the clamped logs (modules.py:130-132, ops.py:160-161)."""
+    return _Temperatures.apply(log_beta, log_scales)
 
 
 def dictionary_views(raw_key: Tensor, raw_value: Tensor | None, eps: float, dtype: torch.dtype) -> DictionaryViews:
@@ -760,6 +806,68 @@ class _Projection(torch.autograd.Function):
             gemm(dout, True, x2d, True, n, k, m, dw)              # dW = dC^T . X (fp32)
             dw = dw.to(weight.dtype)
         return dx, dw
+
+
+class _QKVProjection(torch.autograd.Function):
+    """Q/K projection [B*T, 2*H*R] (compute dtype) and value projection [B*T, D] (bf16, + bias) of one
+    input in one launch (modules.py:143-157 and the value Linear)."""
+
+    @staticmethod
+    def forward(ctx, x2d: Tensor, wq: Tensor, wk: Tensor, wv: Tensor, bv: Tensor | None):  # type: ignore[override]
+        m, k = x2d.shape
+        hr, d = wq.shape[0], wv.shape[0]
+        dev = x2d.device
+        proj = torch.empty(m, 2 * hr, dtype=x2d.dtype, device=dev)
+        value = torch.empty(m, d, dtype=torch.bfloat16, device=dev)
+        import ctypes
+
+        ptrs = lambda *v: (ctypes.c_void_p * 3)(*v)  # noqa: E731
+        i64 = lambda *v: (ctypes.c_int64 * 3)(*v)  # noqa: E731
+        ws = workspace(dev)
+        call("da_gemm_segments", x2d.data_ptr(), x2d.stride(0), m, k, dtype_code(x2d.dtype), 3,
+             ptrs(wq.data_ptr(), wk.data_ptr(), wv.data_ptr()), i64(wq.stride(0), wk.stride(0), wv.stride(0)),
+             i64(hr, hr, d), ptrs(proj.data_ptr(), proj.data_ptr() + hr * proj.element_size(), value.data_ptr()),
+             i64(2 * hr, 2 * hr, d), (ctypes.c_int * 3)(dtype_code(x2d.dtype), dtype_code(x2d.dtype), _lib.DA_BF16),
+             ptrs(None, None, None if bv is None else bv.data_ptr()), ws.status.data_ptr(), stream_ptr(dev))
+        ctx.save_for_backward(x2d, wq, wk, wv)
+        ctx.has_bias = bv is not None
+        return proj, value
+
+    @staticmethod
+    def backward(ctx, dproj: Tensor | None, dvalue: Tensor | None):  # type: ignore[override]
+        x2d, wq, wk, wv = ctx.saved_tensors
+        need = ctx.needs_input_grad
+        m, k = x2d.shape
+        hr = wq.shape[0]
+        dt = x2d.dtype
+        dx = dwq = dwk = dwv = dbv = None
+        if dproj is not None:
+            dproj = dproj.to(dt).contiguous()
+            if need[0]:
+                dx = torch.empty(m, k, dtype=dt, device=x2d.device)
+                gemm(dproj, False, torch.cat((wq, wk), 0), True, m, k, 2 * hr, dx)   # dX = dC . [Wq; Wk]
+            if need[1] or need[2]:
+                dw = torch.empty(2 * hr, k, dtype=torch.float32, device=x2d.device)
+                gemm(dproj, True, x2d, True, 2 * hr, k, m, dw)                       # dW = dC^T . X (fp32)
+                dwq, dwk = dw[:hr].to(wq.dtype), dw[hr:].to(wk.dtype)
+        if dvalue is not None:
+            dv = dvalue.to(dt)
+            if need[0]:
+                dx = dv @ wv if dx is None else dx.addmm_(dv, wv)
+            if need[3]:
+                dwv = (dv.t() @ x2d).to(wv.dtype)
+            if ctx.has_bias and need[4]:
+                dbv = dvalue.float().sum(0).to(wv.dtype)
+        return dx, dwq, dwk, dwv, dbv
+
+
+def qkv_projection(x: Tensor, wq: Tensor, wk: Tensor, wv: Tensor, bv: Tensor | None) -> tuple[Tensor, Tensor]:
+    """``x [B, T, K]`` -> projected ``[B*T, 2*H*R]`` (x's dtype) and value ``[B*T, D]`` (bf16)."""
+    x2d = x.reshape(-1, x.shape[-1])
+    if not x2d.is_contiguous():
+        x2d = x2d.contiguous()
+    return _QKVProjection.apply(x2d, wq.contiguous(), wk.contiguous(), wv.contiguous(),
+                                None if bv is None else bv.contiguous())
 
 
 def qk_projection(x: Tensor, fused_weight: Tensor) -> Tensor:

@@ -68,12 +68,21 @@ DA_API int da_dict_norm_fwd(const float* raw, int64_t R, int64_t M, float eps, i
 /* Both banks of a dictionary in one launch (the module path normalises the
  * key and value banks every forward, modules.py:45-48, :229-231): the key
  * bank as da_dict_norm_fwd in key_dtype (key, key_t, key_denom, key_max),
- * the value bank in bf16 (value, value_t, value_denom).  raw_value may equal
- * raw_key (tied dictionary in a dtype other than bf16) or be null (key only).
- * Every output pointer may be null. */
-DA_API int da_dict_norm_pair_fwd(const float* raw_key, const float* raw_value, int64_t R, int64_t M, float eps,
-                                 int key_dtype, void* key, void* key_t, float* key_denom, float* key_max,
+ * the value bank in bf16 (value, value_t, value_denom).  The raw banks are
+ * [R, M] in raw_dtype (DA_F32, or the half type of a module cast to it);
+ * raw_value may equal raw_key (tied dictionary in a dtype other than bf16) or
+ * be null (key only).  Every output pointer may be null. */
+DA_API int da_dict_norm_pair_fwd(const void* raw_key, const void* raw_value, int raw_dtype, int64_t R, int64_t M,
+                                 float eps, int key_dtype, void* key, void* key_t, float* key_denom, float* key_max,
                                  void* value, void* value_t, float* value_denom, void* stream);
+
+/* The temperatures of the path in one launch (modules.py:130-132 and
+ * ops.py:160-161): beta = exp(clamp(log_beta, beta_lo, beta_hi)) and
+ * gamma_s = exp(clamp(log_scales[s], scale_lo, scale_hi)), written in fp32
+ * from logs held in fp32, bf16 or fp16.  Either input may be null. */
+DA_API int da_temperatures(const void* log_beta, int beta_dtype, float beta_lo, float beta_hi,
+                           const void* log_scales, int scales_dtype, int maps, float scale_lo, float scale_hi,
+                           float* beta_out, float* scales_out, void* stream);
 
 /* Backward of da_dict_norm_fwd (autograd of F.normalize, modules.py:46-47).
  * grad: [R, M] fp32 and/or grad_t: [M, R] fp32 (summed when both are given).
@@ -203,6 +212,18 @@ DA_API int da_attn_bwd_mixed(const void* q, int64_t q_rows, int64_t q_base, int6
 DA_API int da_gemm(const void* A, int64_t lda, int a_mn_major, const void* B, int64_t ldb, int b_mn_major, void* C,
                    int64_t ldc, int64_t M, int64_t N, int64_t K, int dtype, int out_f32, int accumulate, int* status,
                    void* stream);
+
+/* Several projections of one input in one launch: C_s = A . B_s^T (+ bias_s)
+ * for nseg <= 3 weight matrices B_s [N_s, K] (row stride ldb[s]) sharing A
+ * [M, K] (row stride lda); C_s [M, N_s] with row stride ldc[s] in out_dtype[s]
+ * (DA_F16 / DA_BF16 / DA_F32); bias_s [N_s] in the operand dtype, or null.
+ * Replaces F.linear(x, cat(W_q, W_k)) (modules.py:143-157) together with the
+ * value projection, writing V in the bf16 the attention consumes.  Every N_s
+ * a multiple of 128.  B, ldb, N, C, ldc, out_dtype, bias are host arrays. */
+DA_API int da_gemm_segments(const void* A, int64_t lda, int64_t M, int64_t K, int dtype, int nseg,
+                            const void* const* B, const int64_t* ldb, const int64_t* N, void* const* C,
+                            const int64_t* ldc, const int* out_dtype, const void* const* bias, int* status,
+                            void* stream);
 
 /* Split-K variant for reductions over many rows (the dictionary gradients
  * dDk = q^T dL and dDv = g^T P, triton_kernels.py:1939, :1961):

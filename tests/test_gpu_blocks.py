@@ -96,7 +96,7 @@ def test_dict_norm_pair_matches_single_bank_calls(dtype: torch.dtype, r: int, m:
     val, val_t = (torch.empty(r, m, device=dev, dtype=torch.bfloat16),
                   torch.empty(m, r, device=dev, dtype=torch.bfloat16))
     kden, vden, kmax = torch.empty(m, device=dev), torch.empty(m, device=dev), torch.empty(1, device=dev)
-    _lib.call("da_dict_norm_pair_fwd", raw_k.data_ptr(), raw_v.data_ptr(), r, m, eps, _lib.dtype_code(dtype),
+    _lib.call("da_dict_norm_pair_fwd", raw_k.data_ptr(), raw_v.data_ptr(), _lib.DA_F32, r, m, eps, _lib.dtype_code(dtype),
               key.data_ptr(), key_t.data_ptr(), kden.data_ptr(), kmax.data_ptr(), val.data_ptr(), val_t.data_ptr(),
               vden.data_ptr(), _lib.stream_ptr())
     torch.testing.assert_close(key, torch.nn.functional.normalize(raw_k, dim=0, eps=eps).to(dtype))
