@@ -431,6 +431,9 @@ def _mode_words(cfg) -> str:
 def run_reference(args, cfg, world, rank):
     if rank != 0:
         return
+    # torchrun sets OMP_NUM_THREADS=1 for every rank; the reference arm runs on rank 0 alone and uses
+    # every host core
+    torch.set_num_threads(os.cpu_count() or 1)
     tps, threads, n, sb, sec = cpu_reference(cfg, args.cpu_seconds, steps=args.steps, warmup=args.warmup)
     sample = (f"{n} steps of the fp32 CPU oracle {_mode_words(cfg)} on {sb}x{cfg['seq']} tokens "
               f"(median {sec * 1e3:.1f} ms/step), tokens/s of that sample")
@@ -520,6 +523,7 @@ def run_b200(args, cfg, world, rank, local):
                               if k != top},
         }
         if world == 1:
+            torch.set_num_threads(os.cpu_count() or 1)
             tps, threads, n, sb, sec = cpu_reference(cfg, args.cpu_seconds)
             cpu_base = {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port",
                         "sample": f"{n} fp32 CPU oracle {_mode_words(cfg)} steps on {sb}x{cfg['seq']} tokens in "
