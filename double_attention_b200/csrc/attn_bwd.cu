@@ -15,6 +15,8 @@ namespace bwd {
 template <typename T>
 __global__ void delta_kernel(const T* __restrict__ dy, const T* __restrict__ y, int64_t rows, int D,
                              float* __restrict__ delta) {
+  grid_dependency_wait();
+  grid_launch_dependents();
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   if (row >= rows) return;
@@ -49,12 +51,8 @@ extern "C" int da_attn_bwd_delta(const void* dy, const void* y, int64_t rows, in
   const unsigned grid = (unsigned)((rows + per_block - 1) / per_block);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (dtype == DA_BF16)
-    attn::bwd::delta_kernel<__nv_bfloat16><<<grid, 32 * per_block, 0, st>>>(
-        static_cast<const __nv_bfloat16*>(dy), static_cast<const __nv_bfloat16*>(y), rows, D, delta);
-  else
-    attn::bwd::delta_kernel<__half><<<grid, 32 * per_block, 0, st>>>(
-        static_cast<const __half*>(dy), static_cast<const __half*>(y), rows, D, delta);
-  if (cudaPeekAtLastError() != cudaSuccess) return record_cuda_error();
-  note_launch();
-  return DA_OK;
+    return launch_kernel(attn::bwd::delta_kernel<__nv_bfloat16>, dim3(grid), dim3(32 * per_block), 0, st, false,
+                         static_cast<const __nv_bfloat16*>(dy), static_cast<const __nv_bfloat16*>(y), rows, D, delta);
+  return launch_kernel(attn::bwd::delta_kernel<__half>, dim3(grid), dim3(32 * per_block), 0, st, false,
+                       static_cast<const __half*>(dy), static_cast<const __half*>(y), rows, D, delta);
 }

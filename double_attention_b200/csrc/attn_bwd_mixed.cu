@@ -169,6 +169,8 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
   __syncthreads();
   cluster_sync();
   tc_fence_after();
+  grid_dependency_wait();  // predecessors' outputs are visible from here on
+  grid_launch_dependents();
   const uint32_t tmem = tmem_base;
 
   // unit u -> (sweep tile g, tile j within the sweep, map s)
@@ -576,6 +578,8 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
   __syncthreads();
   cluster_sync();
   tc_fence_after();
+  grid_dependency_wait();  // predecessors' outputs are visible from here on
+  grid_launch_dependents();
   const uint32_t tmem = tmem_base;
 
   auto unit_g = [&](int u) { return u / maps; };  // query tile (0 .. ni-1)
@@ -907,21 +911,7 @@ int launch_pair(Kern kern, const Layout& L, int pairs, const CUtensorMap& tq, co
   const int smem = (L.smem < 120 * 1024 ? 120 * 1024 : L.smem) + 1024;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return record_cuda_error();
-  cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
-  cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, kern, tq, tk, tv, tdy, p) != cudaSuccess) return record_cuda_error();
-  note_launch();
-  return DA_OK;
+  return launch_kernel(kern, dim3((unsigned)(2 * pairs), 1, 1), dim3(kThreads, 1, 1), smem, st, true, tq, tk, tv, tdy, p);
 }
 
 }  // namespace bwdm

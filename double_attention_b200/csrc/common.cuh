@@ -172,6 +172,16 @@ DA_DEV void trace_time(int* trace, int slot) {
   if (trace) trace_at(trace, blockIdx.x * 8 + slot);
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// Kernels are launched with programmatic stream serialisation allowed: a
+// kernel may start (and run its setup) while the previous kernel on the
+// stream drains.  Every kernel calls grid_dependency_wait() after its setup
+// and before touching global memory, which returns once the previous kernels
+// have completed and their writes are visible; grid_launch_dependents() lets
+// the next kernel be scheduled as soon as every CTA of this one has started.
+DA_DEV void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+DA_DEV void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------- TMA
 DA_DEV void prefetch_tmap(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" :: "l"(tmap) : "memory");

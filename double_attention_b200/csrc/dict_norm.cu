@@ -27,6 +27,8 @@ __global__ void __launch_bounds__(256) dict_norm_fwd_kernel(const float* __restr
                                                             float* __restrict__ denom_out,
                                                             float* __restrict__ max_norm) {
   extern __shared__ float tile[];          // [R][33] (padded)
+  grid_dependency_wait();
+  grid_launch_dependents();
   __shared__ float part[8][33], part2[8][33], inv[32];
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
   const int j0 = blockIdx.x * 32, j = j0 + tx;
@@ -89,6 +91,8 @@ __global__ void __launch_bounds__(256) dict_norm_pair_kernel(const TR* __restric
                                                              __nv_bfloat16* __restrict__ value_t,
                                                              float* __restrict__ value_denom) {
   extern __shared__ float tile8[];  // [R][9]
+  grid_dependency_wait();
+  grid_launch_dependents();
   __shared__ float part[32][9], colden[8];
   const bool is_key = blockIdx.y == 0;
   const TR* raw = is_key ? raw_key : raw_value;
@@ -162,6 +166,8 @@ __global__ void __launch_bounds__(256) dict_norm_bwd_kernel(const float* __restr
                                                             const float* __restrict__ grad_t, int R, int M, float eps,
                                                             float* __restrict__ grad_raw, int accumulate) {
   extern __shared__ float smem_f[];
+  grid_dependency_wait();
+  grid_launch_dependents();
   float* tx_ = smem_f;              // [R][33] raw
   float* tg = smem_f + R * 33;      // [R][33] gradient
   __shared__ float part_ss[8][33], part_dot[8][33], colv[2][32];
@@ -233,16 +239,17 @@ extern "C" int da_dict_norm_fwd(const float* raw, int64_t R, int64_t M, float ep
     auto k = dict_norm_fwd_kernel<__nv_bfloat16>;
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return record_cuda_error();
-    k<<<grid, block, smem, st>>>(raw, (int)R, (int)M, eps, (__nv_bfloat16*)out, (__nv_bfloat16*)out_t, denom,
-                                 max_col_norm);
+    if (int rc = launch_kernel(k, grid, block, smem, st, false, raw, (int)R, (int)M, eps, (__nv_bfloat16*)out,
+                               (__nv_bfloat16*)out_t, denom, max_col_norm))
+      return rc;
   } else {
     auto k = dict_norm_fwd_kernel<__half>;
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return record_cuda_error();
-    k<<<grid, block, smem, st>>>(raw, (int)R, (int)M, eps, (__half*)out, (__half*)out_t, denom, max_col_norm);
+    if (int rc = launch_kernel(k, grid, block, smem, st, false, raw, (int)R, (int)M, eps, (__half*)out,
+                               (__half*)out_t, denom, max_col_norm))
+      return rc;
   }
-  if (cudaPeekAtLastError() != cudaSuccess) return record_cuda_error();
-  note_launch();
   return DA_OK;
 }
 
@@ -258,11 +265,8 @@ extern "C" int da_dict_norm_bwd(const float* raw, const float* denom, const floa
   if (cudaFuncSetAttribute(dict_norm_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
       cudaSuccess)
     return record_cuda_error();
-  dict_norm_bwd_kernel<<<dim3((unsigned)((M + 31) / 32)), dim3(256), smem, st>>>(raw, denom, grad, grad_t, (int)R,
-                                                                                  (int)M, eps, grad_raw, accumulate);
-  if (cudaPeekAtLastError() != cudaSuccess) return record_cuda_error();
-  note_launch();
-  return DA_OK;
+  return launch_kernel(dict_norm_bwd_kernel, dim3((unsigned)((M + 31) / 32)), dim3(256), smem, st, false, raw, denom,
+                       grad, grad_t, (int)R, (int)M, eps, grad_raw, accumulate);
 }
 
 // Largest column 2-norm of a [R, M] dictionary in fp16/bf16 (for callers that
@@ -271,6 +275,8 @@ namespace da {
 namespace {
 template <typename T>
 __global__ void col_norm_max_kernel(const T* __restrict__ d, int R, int M, float* __restrict__ out) {
+  grid_dependency_wait();
+  grid_launch_dependents();
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
   if (j >= M) return;
   float ss = 0.f;
@@ -292,14 +298,12 @@ extern "C" int da_col_norm_max(const void* dict, int64_t R, int64_t M, int dtype
   if (cudaMemsetAsync(out, 0, sizeof(float), st) != cudaSuccess) return record_cuda_error();
   const dim3 grid((unsigned)((M + 127) / 128)), block(128);
   if (dtype == DA_BF16)
-    col_norm_max_kernel<__nv_bfloat16><<<grid, block, 0, st>>>((const __nv_bfloat16*)dict, (int)R, (int)M, out);
-  else if (dtype == DA_F16)
-    col_norm_max_kernel<__half><<<grid, block, 0, st>>>((const __half*)dict, (int)R, (int)M, out);
-  else
-    return DA_ERR_DTYPE;
-  if (cudaPeekAtLastError() != cudaSuccess) return record_cuda_error();
-  note_launch();
-  return DA_OK;
+    return launch_kernel(col_norm_max_kernel<__nv_bfloat16>, grid, block, 0, st, false,
+                         (const __nv_bfloat16*)dict, (int)R, (int)M, out);
+  if (dtype == DA_F16)
+    return launch_kernel(col_norm_max_kernel<__half>, grid, block, 0, st, false, (const __half*)dict, (int)R,
+                         (int)M, out);
+  return DA_ERR_DTYPE;
 }
 
 extern "C" int da_dict_norm_pair_fwd(const void* raw_key, const void* raw_value, int raw_dtype, int64_t R,
@@ -321,13 +325,10 @@ extern "C" int da_dict_norm_pair_fwd(const void* raw_key, const void* raw_value,
     using TK = decltype(key_tag);
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return record_cuda_error();
-    kern<<<grid, block, smem, st>>>(static_cast<const TR*>(raw_key), static_cast<const TR*>(raw_value), (int)R,
-                                    (int)M, eps, static_cast<TK*>(key), static_cast<TK*>(key_t), key_denom, key_max,
-                                    static_cast<__nv_bfloat16*>(value), static_cast<__nv_bfloat16*>(value_t),
-                                    value_denom);
-    if (cudaPeekAtLastError() != cudaSuccess) return record_cuda_error();
-    note_launch();
-    return DA_OK;
+    return launch_kernel(kern, grid, block, smem, st, false, static_cast<const TR*>(raw_key),
+                         static_cast<const TR*>(raw_value), (int)R, (int)M, eps, static_cast<TK*>(key),
+                         static_cast<TK*>(key_t), key_denom, key_max, static_cast<__nv_bfloat16*>(value),
+                         static_cast<__nv_bfloat16*>(value_t), value_denom);
   };
   const bool kb = key_dtype == DA_BF16;
   if (raw_dtype == DA_F32)
@@ -355,6 +356,8 @@ DA_DEV float load_any(const void* p, int dtype, int i) {
 __global__ void temperatures_kernel(const void* log_beta, int beta_dtype, float beta_lo, float beta_hi,
                                     const void* log_scales, int scales_dtype, int maps, float scale_lo,
                                     float scale_hi, float* beta_out, float* scales_out) {
+  grid_dependency_wait();
+  grid_launch_dependents();
   const int i = threadIdx.x;
   if (i == 0 && log_beta) beta_out[0] = expf(fminf(fmaxf(load_any(log_beta, beta_dtype, 0), beta_lo), beta_hi));
   if (i < maps && log_scales)
@@ -372,10 +375,7 @@ extern "C" int da_temperatures(const void* log_beta, int beta_dtype, float beta_
   if (maps < 0 || maps > 32) return DA_ERR_SHAPE;
   for (int d : {beta_dtype, scales_dtype})
     if (d != DA_F32 && d != DA_BF16 && d != DA_F16) return DA_ERR_DTYPE;
-  temperatures_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(log_beta, beta_dtype, beta_lo, beta_hi,
-                                                                         log_scales, scales_dtype, maps, scale_lo,
-                                                                         scale_hi, beta_out, scales_out);
-  if (cudaPeekAtLastError() != cudaSuccess) return record_cuda_error();
-  note_launch();
-  return DA_OK;
+  return launch_kernel(temperatures_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), false, log_beta,
+                       beta_dtype, beta_lo, beta_hi, log_scales, scales_dtype, maps, scale_lo, scale_hi, beta_out,
+                       scales_out);
 }

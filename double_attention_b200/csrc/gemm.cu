@@ -70,6 +70,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  grid_dependency_wait();  // predecessors' outputs are visible from here on
+  grid_launch_dependents();
   const uint32_t tmem = tmem_base;
 
   if (warp == 0) {
@@ -225,6 +227,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_seg_kernel(const __grid_cons
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  grid_dependency_wait();  // predecessors' outputs are visible from here on
+  grid_launch_dependents();
   const uint32_t tmem = tmem_base;
 
   if (warp == 0) {
@@ -326,10 +330,7 @@ int launch(const void* A, int64_t lda, const void* B, int64_t ldb, const Params&
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return record_cuda_error();
   dim3 grid((unsigned)((p.M + kBM - 1) / kBM), (unsigned)((p.N + kN - 1) / kN), (unsigned)splits);
-  kern<<<grid, kThreads, smem, st>>>(ta, tb, p);
-  if (cudaPeekAtLastError() != cudaSuccess) return record_cuda_error();
-  note_launch();
-  return DA_OK;
+  return launch_kernel(kern, grid, dim3(kThreads), smem, st, false, ta, tb, p);
 }
 
 template <typename T>
@@ -452,10 +453,7 @@ extern "C" int da_gemm_segments(const void* A, int64_t lda, int64_t M, int64_t K
   auto run = [&](auto kern, int smem_bytes) -> int {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes) != cudaSuccess)
       return record_cuda_error();
-    kern<<<grid, kThreads, smem_bytes, st>>>(ta, tb[0], tb[1], tb[2], p);
-    if (cudaPeekAtLastError() != cudaSuccess) return record_cuda_error();
-    note_launch();
-    return DA_OK;
+    return launch_kernel(kern, grid, dim3(kThreads), smem_bytes, st, false, ta, tb[0], tb[1], tb[2], p);
   };
   const bool bf16 = dtype == DA_BF16;
   if (n_tile == 256)

@@ -140,6 +140,8 @@ __global__ void __launch_bounds__(kThreads, 1) route_bwd_kernel(const __grid_con
   __syncthreads();
   cluster_sync();
   tc_fence_after();
+  grid_dependency_wait();  // predecessors' outputs are visible from here on
+  grid_launch_dependents();
   const uint32_t tmem = tmem_base;
 
   if (warp == 0 && lane == 0) {
@@ -527,21 +529,7 @@ int launch(const RouteBwdArgs& a, cudaStream_t st) {
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return record_cuda_error();
   const long pairs = (long)a.groups * ((a.rows + 127) / 128);
-  cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
-  cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, kern, tq, tdk, tdv, p) != cudaSuccess) return record_cuda_error();
-  note_launch();
-  return DA_OK;
+  return launch_kernel(kern, dim3((unsigned)(2 * pairs), 1, 1), dim3(kThreads, 1, 1), smem, st, true, tq, tdk, tdv, p);
 }
 
 }  // namespace bwd

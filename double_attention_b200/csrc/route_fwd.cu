@@ -222,6 +222,8 @@ __global__ void __launch_bounds__(192, 1) route_fwd_kernel(const __grid_constant
   __syncthreads();
   cluster_sync();
   tc_fence_after();
+  grid_dependency_wait();  // predecessors' outputs are visible from here on
+  grid_launch_dependents();
   const uint32_t tmem = tmem_base;
   if (threadIdx.x == 0) trace_time(p.trace, 1);
 
@@ -647,6 +649,8 @@ __global__ void __launch_bounds__(192, 1) route_fwd_wide_kernel(const __grid_con
   __syncthreads();
   cluster_sync();
   tc_fence_after();
+  grid_dependency_wait();  // predecessors' outputs are visible from here on
+  grid_launch_dependents();
   const uint32_t tmem = tmem_base;
   if (threadIdx.x == 0) trace_time(p.trace, 1);
 
@@ -985,21 +989,7 @@ int launch_fwd(const RouteFwdArgs& a, cudaStream_t st) {
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return record_cuda_error();
   const long pairs = (long)a.groups * ((a.rows + 127) / 128);
-  cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
-  cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
-  cfg.blockDim = dim3(C::kThreads, 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, kern, tq, tdk, tdv, p) != cudaSuccess) return record_cuda_error();
-  note_launch();
-  return DA_OK;
+  return launch_kernel(kern, dim3((unsigned)(2 * pairs), 1, 1), dim3(C::kThreads, 1, 1), smem, st, true, tq, tdk, tdv, p);
 }
 
 int route_fwd(const RouteFwdArgs& a, cudaStream_t st) {
