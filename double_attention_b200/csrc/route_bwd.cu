@@ -288,15 +288,21 @@ __global__ void __launch_bounds__(kThreads, 1) route_bwd_kernel(const __grid_con
     const float beta = *p.beta;
     const int hw = R / 2;  // columns of this thread's half of the row
 
-    // ---- g = d r from z and dz (this thread: columns half*hw .. +hw)
-    const T* zrow = reinterpret_cast<const T*>(p.z) + idx * R + half * hw;
-    const T* dzrow = reinterpret_cast<const T*>(p.dz) + idx * R + half * hw;
+    // ---- g = d r from z and dz (this thread: columns half*hw .. +hw), 8 x 16-byte loads in flight
+    const uint4* zrow = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.z) + idx * R + half * hw);
+    const uint4* dzrow = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.dz) + idx * R + half * hw);
+    const float on = live ? __ldg(p.out_norm + idx) : 1.f;
     float zd = 0.f, zz = 0.f;
-    if (live) {
-      for (int c = 0; c < hw; c += 8) {
-        const uint4 a = *reinterpret_cast<const uint4*>(zrow + c);
-        const uint4 d = *reinterpret_cast<const uint4*>(dzrow + c);
-        const uint32_t wa[4] = {a.x, a.y, a.z, a.w}, wd[4] = {d.x, d.y, d.z, d.w};
+    for (int c0 = 0; c0 < hw / 8; c0 += 8) {
+      uint4 a[8], d[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        a[i] = live ? __ldg(zrow + c0 + i) : make_uint4(0u, 0u, 0u, 0u);
+        d[i] = live ? __ldg(dzrow + c0 + i) : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const uint32_t wa[4] = {a[i].x, a[i].y, a[i].z, a[i].w}, wd[4] = {d[i].x, d[i].y, d[i].z, d[i].w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float2 fa = unpack2<T>(wa[e]), fd = unpack2<T>(wd[e]);
@@ -311,7 +317,6 @@ __global__ void __launch_bounds__(kThreads, 1) route_bwd_kernel(const __grid_con
     zd += red[l ^ 64];
     zz += red[128 + (l ^ 64)];
     named_bar_sync(1, 128);
-    const float on = live ? p.out_norm[idx] : 1.f;
     // g = ca * dz - cb * z;  delta = <r, g> with r = z * max(on, eps) (normalised) or z
     float ca = 1.f, cb = 0.f, delta = zd;
     if (p.normalize_output) {
@@ -326,22 +331,27 @@ __global__ void __launch_bounds__(kThreads, 1) route_bwd_kernel(const __grid_con
     }
     {
       const uint32_t gsm = smem_u32(smem + L.off_g);
-      __nv_bfloat16* grow_out = p.g_out + idx * R + half * hw;
-      for (int c = 0; c < hw; c += 8) {
-        uint32_t w[4] = {0u, 0u, 0u, 0u};
-        if (live) {
-          const uint4 a = *reinterpret_cast<const uint4*>(zrow + c);
-          const uint4 d = *reinterpret_cast<const uint4*>(dzrow + c);
-          const uint32_t wa[4] = {a.x, a.y, a.z, a.w}, wd[4] = {d.x, d.y, d.z, d.w};
+      uint4* grow_out = reinterpret_cast<uint4*>(p.g_out + idx * R + half * hw);
+      for (int c0 = 0; c0 < hw / 8; c0 += 8) {
+        uint4 a[8], d[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          a[i] = live ? __ldg(zrow + c0 + i) : make_uint4(0u, 0u, 0u, 0u);
+          d[i] = live ? __ldg(dzrow + c0 + i) : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint32_t wa[4] = {a[i].x, a[i].y, a[i].z, a[i].w}, wd[4] = {d[i].x, d[i].y, d[i].z, d[i].w};
+          uint32_t w[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const float2 fa = unpack2<T>(wa[e]), fd = unpack2<T>(wd[e]);
-            w[e] = pack_bf16x2(ca * fd.x - cb * fa.x, ca * fd.y - cb * fa.y);
+            w[e] = live ? pack_bf16x2(ca * fd.x - cb * fa.x, ca * fd.y - cb * fa.y) : 0u;
           }
-          *reinterpret_cast<uint4*>(grow_out + c) = make_uint4(w[0], w[1], w[2], w[3]);
+          if (live) grow_out[c0 + i] = make_uint4(w[0], w[1], w[2], w[3]);
+          const int col = half * hw + (c0 + i) * 8;
+          st_shared_v4(gsm + (col >> 6) * (kRows * 128) + sw128_offset(r, (col & 63) >> 3), w[0], w[1], w[2], w[3]);
         }
-        const int col = half * hw + c;
-        st_shared_v4(gsm + (col >> 6) * (kRows * 128) + sw128_offset(r, (col & 63) >> 3), w[0], w[1], w[2], w[3]);
       }
       fence_proxy_async();
     }
