@@ -32,7 +32,10 @@
 namespace da {
 namespace attn {
 
-constexpr int kThreads = 192;   // warp0 TMA (lane 0 keys, lane 1 values), warp1 MMA, warps2-5 softmax/epilogue
+// warp0 keys (TMA), warp1 MMA, warps2-5 softmax/epilogue, warp6 values (TMA): the issues of one warp
+// are serialised, so the two operand streams come from two warps.
+constexpr int kThreads = 224;
+constexpr int kValueWarp = 6;
 constexpr int kRows = 64;       // query rows per CTA
 constexpr int kMaxK = 8, kMaxV = 4, kMaxSB = 4, kMaxPB = 2;
 
@@ -105,6 +108,7 @@ struct FwdParams {
   int64_t q_rows, q_base, q_sb, q_sbr;
   int64_t k_rows, k_base, k_sb, k_sbr;
   int B, T, R, D, maps, group, causal;
+  int dsplit, Dp;  // value columns split over dsplit pairs of Dp columns each
   int branch0[kMaxMaps];
   const float* scales;
   const float* weights;
@@ -129,11 +133,13 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
 
-  const Layout L = make_layout(p.maps, p.group, p.R, p.D, kMix);
+  const Layout L = make_layout(p.maps, p.group, p.R, p.Dp, kMix);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const uint32_t rank = cluster_ctarank() & 1u;
   const int tiles = (p.T + 127) / 128;
-  const int pair = blockIdx.x / 2;
+  const int dslice = (blockIdx.x / 2) % p.dsplit;  // the slices of one query tile run side by side
+  const int dcol0 = dslice * p.Dp;
+  const int pair = blockIdx.x / (2 * p.dsplit);
   const int b = pair / tiles;
   const int t0 = (tiles - 1 - pair % tiles) * 128;  // heaviest (latest) query tiles first
   const int nk = L.nk;
@@ -212,7 +218,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         for (int c = (kc > L.nks ? kc - L.nks : 0); c < kc; ++c)
           mbar_wait_drain(&k_full[c % L.nks], (c / L.nks) & 1u);
       }
-    } else if (lane == 1) {
+    }
+  } else if (warp == kValueWarp) {
+    if (lane == 0) {
       prefetch_tmap(&tv);
       int vc = 0;
       const int64_t vrows = (int64_t)p.B * p.T;
@@ -227,7 +235,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
           for (int i = 0; i < L.npv; ++i)
             for (int bx = 0; bx < L.per; ++bx)
               tma_load_2d_pair(&tv, vf, smem + L.off_v + st * L.v_stage + (i * L.per + bx) * (64 * 128),
-                               i * L.nc + (int)rank * (L.nc / 2) + bx * 64, y);
+                               dcol0 + i * L.nc + (int)rank * (L.nc / 2) + bx * 64, y);
         }
         if (!ok) break;
       }
@@ -503,7 +511,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     if (ok) {
       const size_t row_off = ((size_t)b * p.T + (live ? t : 0)) * p.D;
       for (int i = 0; i < L.npv; ++i) {
-        const int col0 = i * L.nc + half * (L.nc / 2);
+        const int col0 = dcol0 + i * L.nc + half * (L.nc / 2);
         for (int c = 0; c < L.nc / 2; c += 32) {
           float o[32];
           tmem_ld32(tmem + lane_base + (uint32_t)(i * (L.nc / 2) + c), o);
@@ -518,7 +526,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
           }
         }
       }
-      if (live && half == 0) {
+      if (live && half == 0 && dslice == 0) {  // every slice forms the same row statistics
         const float kLn2 = 0.6931471805599453f;
         for (int s = 0; s < maps; ++s) {
           p.lse[((size_t)b * p.maps + s) * p.T + t] = bound2[s] * kLn2;
@@ -536,9 +544,22 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   if (warp == 1) tmem_dealloc<2>(tmem, L.tmem_cols);
 }
 
+// Value-column slices per query tile.  A tile's pair streams every key and
+// value row of its causal prefix; when the tiles do not fill half the SMs,
+// splitting D over 2 or 4 pairs (each recomputing the scores, R <= D) puts
+// more SMs on the stream and shortens the longest pair.
+inline int value_split(long pairs, int D, int sms) {
+  int split = 1;
+  while (split < 4 && D % (2 * split * 128) == 0 && pairs * 2 * split <= sms / 2) split *= 2;
+  return split;
+}
+
 template <typename T, bool kMix>
 int launch(const AttnFwdArgs& a, cudaStream_t st) {
-  const Layout L = make_layout(a.maps, a.group, a.R, a.D, kMix);
+  const long pairs = (long)a.B * ((a.T + 127) / 128);
+  const int dsplit = value_split(pairs, a.D, sm_count());
+  const int Dp = a.D / dsplit;
+  const Layout L = make_layout(a.maps, a.group, a.R, Dp, kMix);
   const CUtensorMapDataType qdt =
       std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap tq, tk, tv;
@@ -565,6 +586,8 @@ int launch(const AttnFwdArgs& a, cudaStream_t st) {
   p.maps = a.maps;
   p.group = a.group;
   p.causal = a.causal;
+  p.dsplit = dsplit;
+  p.Dp = Dp;
   for (int s = 0; s < kMaxMaps; ++s) p.branch0[s] = a.branch0[s];
   p.scales = a.scales;
   p.weights = a.weights;
@@ -578,8 +601,7 @@ int launch(const AttnFwdArgs& a, cudaStream_t st) {
   const int smem = L.smem + 1024;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return record_cuda_error();
-  const long pairs = (long)a.B * ((a.T + 127) / 128);
-  return launch_kernel(kern, dim3((unsigned)(2 * pairs), 1, 1), dim3(kThreads, 1, 1), smem, st, true, tq, tk, tv, p);
+  return launch_kernel(kern, dim3((unsigned)(2 * pairs * dsplit), 1, 1), dim3(kThreads, 1, 1), smem, st, true, tq, tk, tv, p);
 }
 
 int attn_fwd(const AttnFwdArgs& a, cudaStream_t st) {

@@ -547,6 +547,8 @@ struct WideLayout {
 };
 
 constexpr int kWideMaxK = 8, kWideMaxV = 4, kWideMaxSB = 4, kWideMaxPB = 2;
+constexpr int kWideThreads = 224;  // warp0 keys, warp1 MMA, warps2-5 softmax/epilogue, warp6 values
+constexpr int kValueWarp = 6;
 
 __host__ __device__ inline WideLayout wide_layout(int R, int M) {
   WideLayout L;
@@ -596,7 +598,7 @@ __host__ __device__ inline WideLayout wide_layout(int R, int M) {
 }
 
 template <int kR, typename T>
-__global__ void __launch_bounds__(192, 1) route_fwd_wide_kernel(const __grid_constant__ CUtensorMap tq,
+__global__ void __launch_bounds__(kWideThreads, 1) route_fwd_wide_kernel(const __grid_constant__ CUtensorMap tq,
                                                                 const __grid_constant__ CUtensorMap tdk,
                                                                 const __grid_constant__ CUtensorMap tdv,
                                                                 const FwdParams p) {
@@ -681,7 +683,11 @@ __global__ void __launch_bounds__(192, 1) route_fwd_wide_kernel(const __grid_con
         for (int c = (kc > L.nks ? kc - L.nks : 0); c < kc; ++c)
           mbar_wait_drain(&k_full[c % L.nks], (c / L.nks) & 1u);
       }
-    } else if (lane == 1) {  // value rows (this CTA's R/2 slice of every N block) in 64-atom K chunks
+    }
+  } else if (warp == kValueWarp) {
+    // ---------------------------------------------------------------- value producer (its own warp:
+    // TMA issues of one warp are serialised, so keys and values stream from two warps)
+    if (lane == 0) {  // value rows (this CTA's R/2 slice of every N block) in 64-atom K chunks
       prefetch_tmap(&tdv);
       int vc = 0;
       bool ok = true;
@@ -989,7 +995,7 @@ int launch_fwd(const RouteFwdArgs& a, cudaStream_t st) {
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return record_cuda_error();
   const long pairs = (long)a.groups * ((a.rows + 127) / 128);
-  return launch_kernel(kern, dim3((unsigned)(2 * pairs), 1, 1), dim3(C::kThreads, 1, 1), smem, st, true, tq, tdk, tdv, p);
+  return launch_kernel(kern, dim3((unsigned)(2 * pairs), 1, 1), dim3(wide ? kWideThreads : C::kThreads, 1, 1), smem, st, true, tq, tdk, tdv, p);
 }
 
 int route_fwd(const RouteFwdArgs& a, cudaStream_t st) {
