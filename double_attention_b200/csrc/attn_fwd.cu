@@ -88,6 +88,18 @@ __host__ __device__ inline Layout make_layout(int maps, int group, int R, int D,
     const int rest = avail - L.q_bytes - L.p_bytes - 2 * L.v_stage - red;
     L.nks = rest / L.k_stage > kMaxK ? kMaxK : rest / L.k_stage;
   }
+  // The value ring feeds P.V, which waits for a whole softmax tile: stages
+  // moved from the key ring (while it still holds a full score tile of keys)
+  // let the values of the next tile land during that softmax.
+  {
+    const int ring = avail - L.q_bytes - L.npb * L.p_bytes - red;  // bytes of both rings
+    while (L.nvs < kMaxV) {
+      const int nks = (ring - (L.nvs + 1) * L.v_stage) / L.k_stage;
+      if (nks < L.kchunks * (mix ? maps : 1) || nks < 2) break;  // keep a key tile of every map
+      ++L.nvs;
+      L.nks = nks > kMaxK ? kMaxK : nks;
+    }
+  }
   L.s_cols = L.nk / 2;
   L.tmem_s = D / 2;
   const int nsb = (512 - D / 2) / L.s_cols;
@@ -384,6 +396,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         ok = __all_sync(0xffffffffu, ok);
         if (ok) {
           tc_fence_after();
+          // the per-map state is indexed by a runtime map: accumulate in registers, store once
+          const float sc = scale2[s], bd = bound2[s];
+          float msum = 0.f, mmx = -INFINITY;
           for (int ch = 0; ch < hc / 32; ++ch) {
             float v[32];
             tmem_ld32(tmem + lane_base + L.tmem_s + (uint32_t)(sb * L.s_cols + ch * 32), v);
@@ -392,11 +407,13 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
 #pragma unroll
             for (int i = 0; i < 32; ++i)
               if (i < lim) {
-                const float a = v[i] * scale2[s];
-                mx[s] = fmaxf(mx[s], a);
-                sum[s] += ex2(a - bound2[s]);
+                const float a = v[i] * sc;
+                mmx = fmaxf(mmx, a);
+                msum += ex2(a - bd);
               }
           }
+          sum[s] += msum;
+          mx[s] = fmaxf(mx[s], mmx);
         }
         finish_unit(u, false);
       }

@@ -427,28 +427,152 @@ def _route_backward(ctx, dz: Tensor):
             None, None, None, None, None, None)
 
 
+# ----------------------------------------------------------------------------- route variants
+# Flag bits of the variant row stages (include/da_b200.h DA_ROUTE_*).
+ROUTE_SILU_LOGITS, ROUTE_STANDARDIZE, ROUTE_DIRECT_SILU, ROUTE_NORM_INPUT = 1, 2, 4, 8
+
+
+@dataclass(frozen=True)
+class RouteVariant:
+    """The switches of dictionary_route_reference (ops.py:16-62) other than
+    identity logits with softmax assignment: ``flags`` (ROUTE_* bits), the
+    direct-SiLU gain and the standardised-logit scale."""
+
+    flags: int
+    silu_gain: float = 1.0
+    std_scale: float = 1.0
+
+
+def route_variant(activation: str, assignment: str, silu_gain: float, standardize: bool,
+                  standardized_logit_scale: float | None, routing_dim: int) -> RouteVariant | None:
+    """The variant of a route configuration, or None for identity logits with softmax (the fused kernel)."""
+    if activation not in ("identity", "silu"):
+        raise ValueError(f"unsupported dictionary activation: {activation}")
+    if assignment not in ("softmax", "silu"):
+        raise ValueError(f"unsupported dictionary assignment: {assignment}")
+    flags = (ROUTE_SILU_LOGITS if activation == "silu" else 0) | (ROUTE_STANDARDIZE if standardize else 0) \
+        | (ROUTE_DIRECT_SILU if assignment == "silu" else 0)
+    if not flags:
+        return None
+    scale = routing_dim ** -0.5 if standardized_logit_scale is None else float(standardized_logit_scale)
+    return RouteVariant(flags, float(silu_gain), scale)
+
+
+def _variant_supported(r: int, m: int) -> None:
+    if r % 128:
+        raise NotImplementedError(f"route variants need a routing width divisible by 128, got {r}")
+    if m % 128 or m > 2048:
+        raise NotImplementedError(f"route variants need a dictionary size divisible by 128 and <= 2048, got {m}")
+
+
+class _RouteVariantFn(torch.autograd.Function):
+    """A route variant over ``groups`` column blocks of a [rows, cols] matrix.
+
+    Per group: S = q.Dk on the tcgen05 GEMM, the variant's row stage
+    (da_route_var_weights), r = W.Dv^T on the GEMM, the output normalisation;
+    backward the same products in reverse (da_route_var_* row stages around
+    da_gemm / da_gemm_splitk)."""
+
+    @staticmethod
+    def forward(ctx, q: Tensor, key: Tensor, key_t: Tensor, value: Tensor, value_t: Tensor,  # type: ignore[override]
+                key_anchor: Tensor, value_anchor: Tensor, beta: Tensor, rows: int, groups: int, col_stride: int,
+                eps: float, normalize_input: bool, normalize_output: bool, variant: RouteVariant):
+        m, r = key_t.shape
+        _variant_supported(r, m)
+        dev, dt = q.device, dtype_code(q.dtype)
+        flags = variant.flags | (ROUTE_NORM_INPUT if normalize_input else 0)
+        z = torch.empty(groups, rows, r, dtype=q.dtype, device=dev)
+        onorm = torch.empty(groups, rows, dtype=torch.float32, device=dev)
+        stats = torch.empty(groups, rows, 4, dtype=torch.float32, device=dev)
+        s_buf = torch.empty(rows, m, dtype=torch.float32, device=dev)
+        w_buf = torch.empty(rows, m, dtype=torch.bfloat16, device=dev)
+        r_buf = torch.empty(rows, r, dtype=torch.float32, device=dev)
+        beta32 = beta.detach().float().reshape(1).contiguous()
+        st = stream_ptr(dev)
+        for g in range(groups):
+            qg = q[:, g * col_stride:]
+            gemm(qg, False, key_t, False, rows, m, r, s_buf)  # S = q . Dk
+            call("da_route_var_weights", s_buf.data_ptr(), rows, m, qg.data_ptr(), q.stride(0), r, dt, flags,
+                 variant.silu_gain, variant.std_scale, beta32.data_ptr(), eps, w_buf.data_ptr(), stats[g].data_ptr(),
+                 st)
+            gemm(w_buf, False, value, False, rows, r, m, r_buf)  # r = W . Dv^T
+            call("da_route_var_output", r_buf.data_ptr(), rows, r, dt, int(normalize_output), eps, z[g].data_ptr(),
+                 onorm[g].data_ptr(), st)
+        ctx.save_for_backward(q, key, key_t, value_t, beta32, z, onorm, stats)
+        ctx.meta = (rows, groups, col_stride, eps, normalize_input, normalize_output, flags, variant,
+                    key_anchor.dtype, value_anchor.dtype, beta.shape, beta.dtype)
+        return z
+
+    @staticmethod
+    def backward(ctx, dz: Tensor):  # type: ignore[override]
+        q, key, key_t, value_t, beta32, z, onorm, stats = ctx.saved_tensors
+        (rows, groups, col_stride, eps, ni, no, flags, variant, key_dtype, value_dtype, beta_shape,
+         beta_dtype) = ctx.meta
+        need = ctx.needs_input_grad
+        m, r = key_t.shape
+        dev, dt = q.device, dtype_code(q.dtype)
+        st = stream_ptr(dev)
+        dz = dz.to(z.dtype).contiguous()
+        full = groups * col_stride == q.shape[1] and col_stride == r and q.stride(0) == q.shape[1]
+        dq = torch.empty_like(q) if full else torch.zeros_like(q)
+        softmax = not flags & ROUTE_DIRECT_SILU
+        dbeta = torch.zeros(1, dtype=torch.float32, device=dev) if need[7] and softmax else None
+        d_key = torch.zeros(r, m, dtype=torch.float32, device=dev) if need[5] else None
+        d_value = torch.zeros(r, m, dtype=torch.float32, device=dev) if need[6] else None
+        g_buf = torch.empty(rows, r, dtype=torch.bfloat16, device=dev)
+        delta = torch.empty(rows, dtype=torch.float32, device=dev)
+        s_buf = torch.empty(rows, m, dtype=torch.float32, device=dev)
+        dw_buf = torch.empty(rows, m, dtype=torch.float32, device=dev)
+        ds_buf = torch.empty(rows, m, dtype=q.dtype, device=dev)
+        w_buf = torch.empty(rows, m, dtype=torch.bfloat16, device=dev)
+        u_buf = torch.empty(rows, r, dtype=torch.float32, device=dev)
+        for g in range(groups):
+            qg = q[:, g * col_stride:]
+            call("da_route_var_output_bwd", z[g].data_ptr(), dz[g].data_ptr(), onorm[g].data_ptr(), rows, r, dt,
+                 int(no), eps, g_buf.data_ptr(), delta.data_ptr(), st)
+            gemm(qg, False, key_t, False, rows, m, r, s_buf)  # S = q . Dk again
+            gemm(g_buf, False, value_t, False, rows, m, r, dw_buf)  # dW = g . Dv
+            call("da_route_var_weights_bwd", s_buf.data_ptr(), dw_buf.data_ptr(), rows, m, stats[g].data_ptr(),
+                 delta.data_ptr(), flags, variant.silu_gain, variant.std_scale, beta32.data_ptr(), dt, ds_buf.data_ptr(),
+                 w_buf.data_ptr(), ptr(dbeta), st)
+            if need[0]:
+                gemm(ds_buf, False, key, False, rows, r, m, u_buf)  # u = dS . Dk^T
+                call("da_route_var_input_bwd", u_buf.data_ptr(), qg.data_ptr(), q.stride(0), stats[g].data_ptr(),
+                     rows, r, dt, int(ni), eps, dq[:, g * col_stride:].data_ptr(), dq.stride(0), st)
+            if d_key is not None:  # dDk += q_g^T dS_g
+                gemm_splitk(qg, q.stride(0), True, ds_buf, m, True, r, m, rows, d_key)
+            if d_value is not None:  # dDv += g_g^T W_g
+                gemm_splitk(g_buf, r, True, w_buf, m, True, r, m, rows, d_value)
+        return (dq if need[0] else None, None, None, None, None,
+                None if d_key is None else d_key.to(key_dtype),
+                None if d_value is None else d_value.to(value_dtype),
+                None if dbeta is None else dbeta.view(beta_shape).to(beta_dtype),
+                None, None, None, None, None, None, None)
+
+
+def _route_rows(q: Tensor, views: DictionaryViews, beta: Tensor, rows: int, groups: int, col_stride: int, eps: float,
+                normalize_input: bool, normalize_output: bool, variant: RouteVariant | None) -> Tensor:
+    if variant is None:
+        return _Route.apply(q, views.key, views.key_t, views.value, views.value_t, views.key_max, views.key_anchor,
+                            views.value_anchor, beta, rows, groups, col_stride, eps, normalize_input,
+                            normalize_output)
+    return _RouteVariantFn.apply(q, views.key, views.key_t, views.value, views.value_t, views.key_anchor,
+                                 views.value_anchor, beta, rows, groups, col_stride, eps, normalize_input,
+                                 normalize_output, variant)
+
+
 def route_projected(projected: Tensor, views: DictionaryViews, beta: Tensor, cfg, batch: int, length: int) -> Tensor:
     """Route the Q and K branches of a fused projection ``[B*T, 2*H*R]``.
 
     Returns ``[2, H, B, T, R]`` (index 0: routed queries, 1: routed keys);
     the concatenation of modules.py:239 is only an index mapping here.
     """
-    _check_variant(cfg)
     h, r = cfg.qk_branches, cfg.routing_dim
-    z = _Route.apply(projected, views.key, views.key_t, views.value, views.value_t, views.key_max, views.key_anchor,
-                     views.value_anchor, beta, batch * length, 2 * h, r, cfg.eps, cfg.normalize_routing_input,
-                     cfg.normalize_routing_output)
+    variant = route_variant(cfg.dictionary_activation, cfg.dictionary_assignment, cfg.dictionary_silu_gain,
+                            cfg.standardize_dictionary_logits, cfg.standardized_logit_scale, r)
+    z = _route_rows(projected, views, beta, batch * length, 2 * h, r, cfg.eps, cfg.normalize_routing_input,
+                    cfg.normalize_routing_output, variant)
     return z.view(2, h, batch, length, r)
-
-
-def _check_variant(cfg) -> None:
-    if cfg.dictionary_activation != "identity" or cfg.dictionary_assignment != "softmax" \
-            or cfg.standardize_dictionary_logits:
-        raise NotImplementedError(
-            "the B200 route kernels implement identity logits with softmax assignment; "
-            f"got activation={cfg.dictionary_activation!r}, assignment={cfg.dictionary_assignment!r}, "
-            f"standardize_logits={cfg.standardize_dictionary_logits}"
-        )
 
 
 def dictionary_route(
@@ -471,9 +595,9 @@ def dictionary_route(
     (already column-normalised, same fp16/bf16 dtype as ``input``).
     """
     _check_half_cuda("dictionary route", input, dictionary_key, dictionary_value)
-    if silu_logits or direct_silu or standardize_logits:
-        raise NotImplementedError("the B200 route kernels implement identity logits with softmax assignment")
     r = input.shape[-1]
+    variant = route_variant("silu" if silu_logits else "identity", "silu" if direct_silu else "softmax", silu_gain,
+                            standardize_logits, standardized_logit_scale, r)
     if dictionary_key.shape[0] != r or dictionary_value.shape != dictionary_key.shape:
         raise ValueError("dictionaries must be [routing_dim, M] matching the input")
     shape = input.shape
@@ -481,8 +605,7 @@ def dictionary_route(
     views = dictionary_views_from_normalized(dictionary_key, dictionary_value, input.dtype)
     if not torch.is_tensor(beta):
         beta = torch.tensor(float(beta), device=input.device)
-    z = _Route.apply(flat, views.key, views.key_t, views.value, views.value_t, views.key_max, views.key_anchor,
-                     views.value_anchor, beta, flat.shape[0], 1, r, eps, normalize_input, normalize_output)
+    z = _route_rows(flat, views, beta, flat.shape[0], 1, r, eps, normalize_input, normalize_output, variant)
     return z.view(shape)
 
 

@@ -132,6 +132,61 @@ DA_API int da_route_fwd_static(const void* q, int64_t rows, int64_t q_cols, int6
                                int normalize_input, int normalize_output, void* z, float* lse, float* out_norm,
                                int* argmax, int* status, void* stream);
 
+/* ---- dictionary route variants (row stages) ---------------------------
+ * The variants of dictionary_route_reference (ops.py:16-62) other than
+ * identity logits with softmax assignment -- SiLU logits (:39-41),
+ * standardised logits (:44-53) and direct-SiLU assignment (:56-57), the
+ * silu_logits / standardize_logits / direct_silu switches of
+ * dictionary_route_triton (triton_kernels.py:1984-2019, kernels :215-228,
+ * :417-448) -- run as the two dictionary products on da_gemm with these
+ * row stages between them, one warp per route row (M <= 2048).
+ * flags: OR of the DA_ROUTE_* bits below; silu_gain > 0 for direct-SiLU
+ * assignment; std_scale > 0 (the reference's R^-1/2 default or its explicit
+ * standardized_logit_scale) for standardised logits. */
+enum {
+  DA_ROUTE_SILU_LOGITS = 1, /* a = 2 silu(l) */
+  DA_ROUTE_STANDARDIZE = 2, /* a' = (a - mean) rsqrt(var + eps) std_scale */
+  DA_ROUTE_DIRECT_SILU = 4, /* w = (2 / gain) silu(gain a') instead of softmax(beta a') */
+  DA_ROUTE_NORM_INPUT = 8   /* l = (q / max(||q||, eps)) . Dk, else q . Dk */
+};
+
+/* Forward row stage.  S [rows, M] fp32 = q . Dk (raw q); q rows (dtype,
+ * row stride q_stride) for the input norm; beta (device fp32 scalar, unused
+ * with direct-SiLU).  Writes W [rows, M] bf16 (the assignment weights) and
+ * stats [rows, 4] fp32 = (1/||q|| or 1, mean, inverse std, log-sum-exp of
+ * beta a') for the backward. */
+DA_API int da_route_var_weights(const float* S, int64_t rows, int M, const void* q, int64_t q_stride, int R,
+                                int dtype, int flags, float silu_gain, float std_scale, const float* beta, float eps,
+                                void* W, float* stats, void* stream);
+
+/* Output normalisation: z [rows, R] (dtype) = r / max(||r||, eps) when
+ * normalize, else r; out_norm [rows] = ||r||.  r [rows, R] fp32 = W . Dv^T. */
+DA_API int da_route_var_output(const float* r, int64_t rows, int R, int dtype, int normalize, float eps, void* z,
+                               float* out_norm, void* stream);
+
+/* Its backward: g [rows, R] bf16 = dL/dr from z, dz (dtype) and out_norm,
+ * and delta [rows] fp32 = <g, r> (r rebuilt from z and out_norm), which is
+ * the softmax backward's <W, dW> in closed form. */
+DA_API int da_route_var_output_bwd(const void* z, const void* dz, const float* out_norm, int64_t rows, int R,
+                                   int dtype, int normalize, float eps, void* g, float* delta, void* stream);
+
+/* Backward row stage.  S [rows, M] fp32 = q . Dk again, dW [rows, M] fp32 =
+ * g . Dv, stats from the forward, delta from da_route_var_output_bwd (or
+ * null: <W, dW> is then summed from dW).  Writes dS [rows, M] (dtype) = dL/d(q . Dk)
+ * (the logit gradient times 1/||q||: dDk = q^T dS, u = dS . Dk^T), W
+ * [rows, M] bf16 again (dDv = g^T W) and adds the beta gradient to *dbeta
+ * (softmax assignment; may be null). */
+DA_API int da_route_var_weights_bwd(const float* S, const float* dW, int64_t rows, int M, const float* stats,
+                                    const float* delta, int flags, float silu_gain, float std_scale,
+                                    const float* beta, int dtype, void* dS, void* W, float* dbeta, void* stream);
+
+/* Input-normalisation backward: dq [rows, R] (dtype, row stride dq_stride)
+ * = u - q_hat <q_hat, u> (u = dS . Dk^T [rows, R] fp32) when normalize and
+ * ||q|| > eps, else u. */
+DA_API int da_route_var_input_bwd(const float* u, const void* q, int64_t q_stride, const float* stats, int64_t rows,
+                                  int R, int dtype, int normalize, float eps, void* dq, int64_t dq_stride,
+                                  void* stream);
+
 /* ---- dictionary route, backward --------------------------------------
  * Replaces _DictionaryRouteFunction.backward (triton_kernels.py:1873-1981)
  * with its row-normalisation and scaled-softmax backward kernels

@@ -52,8 +52,14 @@ def dictionary_route(
     standardized_logit_scale: float | None = None,
     normalize_input: bool = True,
     normalize_output: bool = True,
+    inspect: dict | None = None,
 ) -> Tensor:
-    """ops.py:16-62: z = norm(Dv softmax(beta * Dk^T norm(x)))  (+ variants)."""
+    """ops.py:16-62: z = norm(Dv softmax(beta * Dk^T norm(x)))  (+ variants).
+
+    ``inspect`` (test use): receives the final logits and the softmax input
+    (``logits``, ``scaled``; the latter retains its gradient), from which a
+    test bounds the conditioning of the beta gradient, the sum over every
+    route row and atom of logits * d loss / d scaled."""
     q = _normalize(x, -1, eps) if normalize_input else x
     logits = torch.matmul(q, dictionary_key)
     if activation == "silu":
@@ -66,7 +72,11 @@ def dictionary_route(
         scale = x.shape[-1] ** -0.5 if standardized_logit_scale is None else standardized_logit_scale
         logits = centered * inv_std * scale
     if assignment == "softmax":  # ops.py:54-59
-        weights = torch.softmax(logits * beta, dim=-1)
+        scaled = logits * beta
+        if inspect is not None:
+            scaled.retain_grad()
+            inspect.update(logits=logits, scaled=scaled)
+        weights = torch.softmax(scaled, dim=-1)
     elif assignment == "silu":
         weights = (2.0 / silu_gain) * F.silu(silu_gain * logits)
     else:
