@@ -33,7 +33,11 @@ namespace da {
 namespace attn {
 namespace bwdm {
 
-constexpr int kThreads = 192;
+// warp 0: TMA producer of the resident rows and the score / accumulation operands; warp 1: their
+// MMA issuer; warps 2-5: softmax; warp 6: TMA producer of the dP operands (V and dY); warp 7: the
+// dP issuer.  dP runs as its own stream so the other products never wait behind it.
+constexpr int kThreads = 256;
+constexpr int kDpWarp = 6;
 constexpr int kRows = 64;      // rows (queries or keys) per CTA
 constexpr int kTile = 128;     // columns (keys or queries) per tile and pair
 constexpr int kStage = 16384;  // ring stage bytes
@@ -65,11 +69,14 @@ DA_DEV int64_t row_of(int64_t base, int64_t sb, int64_t sbr, int b, int branch, 
 
 struct Layout {
   int kw, W, rpb, ncol, nins;
-  int off_a, off_b, off_t, off_red, off_ring, nst, smem;
+  int off_a, off_b, off_t, off_red, off_ring, nst, off_pring, nsp, smem;
   int tmem_acc, tmem_s, tmem_p, tmem_cols;
 };
 
-// kind 0: dQ (A = Q of all maps, B = dY), 1: dK (A = K of all maps, B = V), 2: dV (A = K of all maps)
+// kind 0: dQ, 1: dK, 2: dV.  The kernel's own rows of Q (dQ) or K (dK, dV) of
+// every map stay resident; V and dY, needed only for dP, stream through the
+// ring a 64-column chunk of each per stage (resident they would leave room
+// for 3 stages, too few to cover the load latency).
 __host__ __device__ inline Layout make_layout(int kind, int maps, int group, int R, int D) {
   Layout L;
   L.kw = group * R;
@@ -79,13 +86,16 @@ __host__ __device__ inline Layout make_layout(int kind, int maps, int group, int
   L.nins = L.kw / L.ncol;
   L.off_a = 0;
   L.off_b = L.off_a + kRows * L.W * 2;
-  const int b_bytes = kind == 2 ? 0 : kRows * D * 2;
+  const int b_bytes = 0;
   L.off_t = L.off_b + b_bytes;                 // two dS / P tiles
   L.off_red = L.off_t + 2 * kRows * kTile * 2;
   L.off_ring = L.off_red + 8192;
   const int avail = 225 * 1024 - L.off_ring;
-  L.nst = avail / kStage > kMaxStages ? kMaxStages : avail / kStage;
-  L.smem = L.off_ring + L.nst * kStage;
+  const int total = avail / kStage;
+  L.nsp = kind == 2 ? 0 : (total >= 8 ? 4 : total / 2);  // dP ring: V and dY chunks
+  L.nst = total - L.nsp > kMaxStages ? kMaxStages : total - L.nsp;
+  L.off_pring = L.off_ring + L.nst * kStage;
+  L.smem = L.off_pring + L.nsp * kStage;
   L.tmem_acc = 0;
   const int acc = kind == 2 ? D / 2 : L.W / 2;
   L.tmem_s = acc;
@@ -120,6 +130,7 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ uint64_t in_full, o_full, r_full[kMaxStages], r_empty[kMaxStages];
+  __shared__ uint64_t rp_full[kMaxStages], rp_empty[kMaxStages], dp_done;
   __shared__ uint64_t s_full[2], p_full[2], dp_full[2], dp_free[2], ds_empty[2];
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
@@ -151,7 +162,10 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
     for (int i = 0; i < kMaxStages; ++i) {
       mbar_init(&r_full[i], 1);
       mbar_init(&r_empty[i], 1);
+      mbar_init(&rp_full[i], 1);
+      mbar_init(&rp_empty[i], 1);
     }
+    mbar_init(&dp_done, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 2);
@@ -178,20 +192,18 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
   auto unit_s = [&](int u) { return u % maps; };
   auto unit_g = [&](int u) { return u / maps; };  // sweep-major tile counter (dP products)
 
+  const int tq_row = t0 + 64 * (int)rank;
+  const int dy_row = (int)min((int64_t)b * p.T + tq_row, rowsBT - 1);
+  const int dps = sweeps * nj;  // dP products: one per key tile and sweep
   if (warp == 0 && lane == 0) {
-    // ---------------------------------------------------------------- TMA producer
+    // ---------------------------------------------------------------- TMA producer: Q, then K for S and dQ
     prefetch_tmap(&tq);
     prefetch_tmap(&tk);
-    prefetch_tmap(&tv);
-    prefetch_tmap(&tdy);
     const uint32_t inf = mapa_shared(smem_u32(&in_full), 0);
-    if (rank == 0) mbar_arrive_expect_tx(&in_full, 2 * (kRows * L.W * 2 + kRows * p.D * 2));
-    const int tq_row = t0 + 64 * (int)rank;
+    if (rank == 0) mbar_arrive_expect_tx(&in_full, 2 * (kRows * L.W * 2));
     for (int s = 0; s < maps; ++s)
       for (int cc = 0; cc < L.kw / 128; ++cc)
         load_map_chunk(&tq, qm, p, inf, smem + L.off_a + (s * (L.kw / 64) + cc * 2) * kBox, b, s, cc, 2, tq_row);
-    const int dy_row = (int)min((int64_t)b * p.T + tq_row, rowsBT - 1);
-    for (int cb = 0; cb < p.D / 64; ++cb) tma_load_2d_pair(&tdy, inf, smem + L.off_b + cb * kBox, cb * 64, dy_row);
     int it = 0;
     bool ok = true;
     auto stage = [&](int bytes) -> uint8_t* {
@@ -201,16 +213,6 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
       return smem + L.off_ring + st * kStage;
     };
     auto stage_bar = [&]() { return mapa_shared(smem_u32(&r_full[it % L.nst]), 0); };
-    auto emit_dp = [&](int u) {  // value rows of this CTA's 64 keys, 128 columns per stage
-      const int krow0 = unit_j(u) * kTile + 64 * (int)rank;
-      const int y = (int)min((int64_t)b * p.T + krow0, rowsBT - 1);
-      for (int cc = 0; ok && cc < p.D / 128; ++cc, ++it) {
-        uint8_t* dst = stage(2 * kBox);
-        if (!ok) return;
-        const uint32_t bar = stage_bar();
-        for (int bx = 0; bx < 2; ++bx) tma_load_2d_pair(&tv, bar, dst + bx * kBox, cc * 128 + bx * 64, y);
-      }
-    };
     auto emit_s = [&](int u) {  // key rows of map s for this CTA's 64 keys
       const int krow0 = unit_j(u) * kTile + 64 * (int)rank;
       for (int cc = 0; ok && cc < L.kw / 128; ++cc, ++it) {
@@ -234,19 +236,66 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
           }
         }
     };
-    emit_dp(0);
     emit_s(0);
-    for (int u = 0; ok && u < U; ++u) {
-      if (u + 1 < U) {
-        if (unit_s(u + 1) == 0) emit_dp(u + 1);
-        emit_s(u + 1);
-      }
+    for (int u = 0; ok && u < U; ++u) {  // same order as the S / dQ issuer
+      if (u + 1 < U) emit_s(u + 1);
       if (u >= u_dq) emit_dq(u);
     }
-    if (rank == 0) {
+    if (rank == 0) {  // drain: no TMA may be in flight at teardown
       mbar_wait_drain(&in_full, 0);
       for (int i = (it > L.nst ? it - L.nst : 0); i < it; ++i) mbar_wait_drain(&r_full[i % L.nst], (i / L.nst) & 1u);
     }
+  } else if (warp == kDpWarp && lane == 0) {
+    // ---------------------------------------------------------------- TMA producer: V and dY for dP
+    prefetch_tmap(&tv);
+    prefetch_tmap(&tdy);
+    int it = 0;
+    bool ok = true;
+    for (int g = 0; ok && g < dps; ++g) {
+      const int y = (int)min((int64_t)b * p.T + (g % nj) * kTile + 64 * (int)rank, rowsBT - 1);
+      for (int cc = 0; cc < p.D / 64; ++cc, ++it) {  // per 64 value columns: V rows of 64 keys, dY rows
+        const int st = it % L.nsp;
+        if (!mbar_wait(&rp_empty[st], ((it / L.nsp) & 1u) ^ 1u, ab, 13)) { ok = false; break; }
+        if (rank == 0) mbar_arrive_expect_tx(&rp_full[st], 2 * 2 * kBox);
+        const uint32_t bar = mapa_shared(smem_u32(&rp_full[st]), 0);
+        uint8_t* dst = smem + L.off_pring + st * kStage;
+        tma_load_2d_pair(&tv, bar, dst, cc * 64, y);
+        tma_load_2d_pair(&tdy, bar, dst + kBox, cc * 64, dy_row);
+      }
+    }
+    if (rank == 0)
+      for (int i = (it > L.nsp ? it - L.nsp : 0); i < it; ++i)
+        mbar_wait_drain(&rp_full[i % L.nsp], (i / L.nsp) & 1u);
+  } else if (warp == kDpWarp + 1 && lane == 0 && rank == 0) {
+    // ---------------------------------------------------------------- dP issuer (leader): dP = dY V^T
+    // Its own thread, so the score and dQ products never wait behind the value stream.
+    const uint32_t idesc = idesc_f16(128, kTile, kBf16, false, false);
+    int it = 0;
+    bool ok = true;
+    for (int g = 0; ok && g < dps; ++g) {
+      const int db = g & 1;
+      if (g < 200) trace_at(ft, 1024 + 4 * g);
+      if (g >= 2 && !mbar_wait(&dp_free[db], ((g - 2) >> 1) & 1u, ab, 27)) break;
+      for (int cc = 0; cc < p.D / 64; ++cc, ++it) {  // stage: [V box | dY box] of 64 value columns
+        const int st = it % L.nsp;
+        if (!mbar_wait(&rp_full[st], (it / L.nsp) & 1u, ab, 28)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t sa = smem_u32(smem + L.off_pring + st * kStage);
+        for (int k = 0; k < 4; ++k) {
+          const uint64_t ad = sdesc_sw128(sa + kBox + k * 32, 16, 1024);
+          const uint64_t bd = sdesc_sw128(sa + k * 32, 16, 1024);
+          mma_f16_ss<2>(tmem + L.tmem_p + db * (kTile / 2), ad, bd, idesc, (cc | k) ? 1u : 0u);
+        }
+        mma_commit<2>(smem_u32(&rp_empty[st]));
+        mma_commit<2>(mapa_shared(smem_u32(&rp_empty[st]), 1));
+      }
+      if (!ok) break;
+      mma_commit<2>(smem_u32(&dp_full[db]));
+      mma_commit<2>(mapa_shared(smem_u32(&dp_full[db]), 1));
+      if (g < 200) trace_at(ft, 1025 + 4 * g);
+    }
+    mma_commit<2>(smem_u32(&dp_done));  // every dP product has completed before teardown
+    mbar_wait_drain(&dp_done, 0);
   } else if (warp == 1 && lane == 0 && rank == 0) {
     // ---------------------------------------------------------------- MMA issuer (leader)
     const uint32_t idesc_s = idesc_f16(128, kTile, kBf16, false, false);
@@ -264,25 +313,7 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
       return true;
     };
     auto give = [&]() { commit_both(&r_empty[it % L.nst]); ++it; };
-    const uint32_t qa = smem_u32(smem + L.off_a), dya = smem_u32(smem + L.off_b);
-    auto issue_dp = [&](int u) -> bool {
-      const int g = unit_g(u), db = g & 1;
-      if (g < 200) trace_at(ft, 1024 + 4 * g);
-      if (g >= 2 && !mbar_wait(&dp_free[db], ((g - 2) >> 1) & 1u, ab, 27)) return false;
-      for (int cc = 0; cc < p.D / 128; ++cc) {
-        uint32_t st;
-        if (!take(&st)) return false;
-        for (int k = 0; k < 8; ++k) {
-          const uint64_t ad = sdesc_sw128(dya + (cc * 2 + (k >> 2)) * kBox + (k & 3) * 32, 16, 1024);
-          const uint64_t bd = sdesc_sw128(st + (k >> 2) * kBox + (k & 3) * 32, 16, 1024);
-          mma_f16_ss<2>(tmem + L.tmem_p + db * (kTile / 2), ad, bd, idesc_s, (cc | k) ? 1u : 0u);
-        }
-        give();
-      }
-      commit_both(&dp_full[db]);
-      if (g < 200) trace_at(ft, 1025 + 4 * g);
-      return true;
-    };
+    const uint32_t qa = smem_u32(smem + L.off_a);
     auto issue_s = [&](int u) -> bool {
       const int sb = u & 1, s = unit_s(u);
       if (u < 300) trace_at(ft, 2048 + 4 * u);
@@ -326,18 +357,14 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
     };
     bool ok = mbar_wait(&in_full, 0, ab, 21);
     tc_fence_after();
-    if (ok) ok = issue_dp(0);
     if (ok) ok = issue_s(0);
     for (int u = 0; ok && u < U; ++u) {
-      if (u + 1 < U) {
-        if (unit_s(u + 1) == 0) ok = issue_dp(u + 1);
-        if (ok) ok = issue_s(u + 1);
-      }
+      if (u + 1 < U) ok = issue_s(u + 1);
       if (ok && u >= u_dq) ok = issue_dq(u);
     }
     commit_both(&o_full);
     mbar_wait_drain(&o_full, 0);
-  } else if (warp >= 2) {
+  } else if (warp >= 2 && warp < 6) {
     // ---------------------------------------------------------------- softmax + epilogue
     const int quad = warp & 3;
     const int l = quad * 32 + lane;
@@ -531,6 +558,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ uint64_t in_full, o_full, r_full[kMaxStages], r_empty[kMaxStages];
+  __shared__ uint64_t rp_full[kMaxStages], rp_empty[kMaxStages], dp_done;
   __shared__ uint64_t s_full[2], p_full[2], dp_full[2], dp_free[2], t_empty[2];
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
@@ -560,7 +588,10 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
     for (int i = 0; i < kMaxStages; ++i) {
       mbar_init(&r_full[i], 1);
       mbar_init(&r_empty[i], 1);
+      mbar_init(&rp_full[i], 1);
+      mbar_init(&rp_empty[i], 1);
     }
+    mbar_init(&dp_done, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 2);
@@ -585,22 +616,18 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
   auto unit_g = [&](int u) { return u / maps; };  // query tile (0 .. ni-1)
   auto unit_s = [&](int u) { return u % maps; };
 
+  const int krow = k0 + 64 * (int)rank;
+  const int vy = (int)min((int64_t)b * p.T + krow, rowsBT - 1);
   if (warp == 0 && lane == 0) {
-    // ---------------------------------------------------------------- TMA producer
+    // ---------------------------------------------------------------- TMA producer: K, then Q (and dY for dV)
     prefetch_tmap(&tq);
     prefetch_tmap(&tk);
-    prefetch_tmap(&tv);
     prefetch_tmap(&tdy);
     const uint32_t inf = mapa_shared(smem_u32(&in_full), 0);
-    if (rank == 0) mbar_arrive_expect_tx(&in_full, 2 * (kRows * L.W * 2 + (kDK ? kRows * p.D * 2 : 0)));
-    const int krow = k0 + 64 * (int)rank;
+    if (rank == 0) mbar_arrive_expect_tx(&in_full, 2 * (kRows * L.W * 2));
     for (int s = 0; s < maps; ++s)
       for (int cc = 0; cc < L.kw / 128; ++cc)
         load_map_chunk(&tk, km, p, inf, smem + L.off_a + (s * (L.kw / 64) + cc * 2) * kBox, b, s, cc, 2, krow);
-    if (kDK) {
-      const int vy = (int)min((int64_t)b * p.T + krow, rowsBT - 1);
-      for (int cb = 0; cb < p.D / 64; ++cb) tma_load_2d_pair(&tv, inf, smem + L.off_b + cb * kBox, cb * 64, vy);
-    }
     int it = 0;
     bool ok = true;
     auto stage = [&](int bytes) -> uint8_t* {
@@ -610,16 +637,6 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
       return smem + L.off_ring + st * kStage;
     };
     auto stage_bar = [&]() { return mapa_shared(smem_u32(&r_full[it % L.nst]), 0); };
-    auto emit_dp = [&](int u) {  // dY rows of this CTA's 64 queries, 128 columns per stage
-      const int q = (i0 + unit_g(u)) * kTile + 64 * (int)rank;
-      const int y = (int)min((int64_t)b * p.T + q, rowsBT - 1);
-      for (int cc = 0; ok && cc < p.D / 128; ++cc, ++it) {
-        uint8_t* dst = stage(2 * kBox);
-        if (!ok) return;
-        const uint32_t bar = stage_bar();
-        for (int bx = 0; bx < 2; ++bx) tma_load_2d_pair(&tdy, bar, dst + bx * kBox, cc * 128 + bx * 64, y);
-      }
-    };
     auto emit_s = [&](int u) {  // query rows of map s for this CTA's 64 queries
       const int q = (i0 + unit_g(u)) * kTile + 64 * (int)rank;
       for (int cc = 0; ok && cc < L.kw / 128; ++cc, ++it) {
@@ -659,19 +676,63 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
       }
     };
     // same order as the MMA warp below
-    if (kDK) emit_dp(0);
     emit_s(0);
     for (int u = 0; ok && u < U; ++u) {
-      if (u + 1 < U) {
-        if (kDK && unit_s(u + 1) == 0) emit_dp(u + 1);
-        emit_s(u + 1);
-      }
+      if (u + 1 < U) emit_s(u + 1);
       if (kDK || unit_s(u) == maps - 1) emit_acc(u);
     }
-    if (rank == 0) {
+    if (rank == 0) {  // drain: no TMA may be in flight at teardown
       mbar_wait_drain(&in_full, 0);
       for (int i = (it > L.nst ? it - L.nst : 0); i < it; ++i) mbar_wait_drain(&r_full[i % L.nst], (i / L.nst) & 1u);
     }
+  } else if (kDK && warp == kDpWarp && lane == 0) {
+    // ---------------------------------------------------------------- TMA producer: dY and V for dP^T
+    prefetch_tmap(&tv);
+    prefetch_tmap(&tdy);
+    int it = 0;
+    bool ok = true;
+    for (int g = 0; ok && g < ni; ++g) {
+      const int y = (int)min((int64_t)b * p.T + (i0 + g) * kTile + 64 * (int)rank, rowsBT - 1);
+      for (int cc = 0; cc < p.D / 64; ++cc, ++it) {  // per 64 value columns: dY rows of 64 queries, V rows
+        const int st = it % L.nsp;
+        if (!mbar_wait(&rp_empty[st], ((it / L.nsp) & 1u) ^ 1u, ab, 13)) { ok = false; break; }
+        if (rank == 0) mbar_arrive_expect_tx(&rp_full[st], 2 * 2 * kBox);
+        const uint32_t bar = mapa_shared(smem_u32(&rp_full[st]), 0);
+        uint8_t* dst = smem + L.off_pring + st * kStage;
+        tma_load_2d_pair(&tdy, bar, dst, cc * 64, y);
+        tma_load_2d_pair(&tv, bar, dst + kBox, cc * 64, vy);
+      }
+    }
+    if (rank == 0)
+      for (int i = (it > L.nsp ? it - L.nsp : 0); i < it; ++i)
+        mbar_wait_drain(&rp_full[i % L.nsp], (i / L.nsp) & 1u);
+  } else if (kDK && warp == kDpWarp + 1 && lane == 0 && rank == 0) {
+    // ---------------------------------------------------------------- dP^T issuer (leader): dP^T = V dY^T
+    const uint32_t idesc = idesc_f16(128, kTile, kBf16, false, false);
+    int it = 0;
+    bool ok = true;
+    for (int g = 0; ok && g < ni; ++g) {
+      const int db = g & 1;
+      if (g >= 2 && !mbar_wait(&dp_free[db], ((g - 2) >> 1) & 1u, ab, 27)) break;
+      for (int cc = 0; cc < p.D / 64; ++cc, ++it) {  // stage: [dY box | V box] of 64 value columns
+        const int st = it % L.nsp;
+        if (!mbar_wait(&rp_full[st], (it / L.nsp) & 1u, ab, 28)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t sa = smem_u32(smem + L.off_pring + st * kStage);
+        for (int k = 0; k < 4; ++k) {
+          const uint64_t ad = sdesc_sw128(sa + kBox + k * 32, 16, 1024);
+          const uint64_t bd = sdesc_sw128(sa + k * 32, 16, 1024);
+          mma_f16_ss<2>(tmem + L.tmem_p + db * (kTile / 2), ad, bd, idesc, (cc | k) ? 1u : 0u);
+        }
+        mma_commit<2>(smem_u32(&rp_empty[st]));
+        mma_commit<2>(mapa_shared(smem_u32(&rp_empty[st]), 1));
+      }
+      if (!ok) break;
+      mma_commit<2>(smem_u32(&dp_full[db]));
+      mma_commit<2>(mapa_shared(smem_u32(&dp_full[db]), 1));
+    }
+    mma_commit<2>(smem_u32(&dp_done));  // every dP^T product has completed before teardown
+    mbar_wait_drain(&dp_done, 0);
   } else if (warp == 1 && lane == 0 && rank == 0) {
     // ---------------------------------------------------------------- MMA issuer (leader)
     const uint32_t idesc_s = idesc_f16(128, kTile, kBf16, false, false);
@@ -690,23 +751,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
       return true;
     };
     auto give = [&]() { commit_both(&r_empty[it % L.nst]); ++it; };
-    const uint32_t ka = smem_u32(smem + L.off_a), va = smem_u32(smem + L.off_b);
-    auto issue_dp = [&](int u) -> bool {  // dP^T = V dY^T
-      const int g = unit_g(u), db = g & 1;
-      if (g >= 2 && !mbar_wait(&dp_free[db], ((g - 2) >> 1) & 1u, ab, 27)) return false;
-      for (int cc = 0; cc < p.D / 128; ++cc) {
-        uint32_t st;
-        if (!take(&st)) return false;
-        for (int k = 0; k < 8; ++k) {
-          const uint64_t ad = sdesc_sw128(va + (cc * 2 + (k >> 2)) * kBox + (k & 3) * 32, 16, 1024);
-          const uint64_t bd = sdesc_sw128(st + (k >> 2) * kBox + (k & 3) * 32, 16, 1024);
-          mma_f16_ss<2>(tmem + L.tmem_p + db * (kTile / 2), ad, bd, idesc_s, (cc | k) ? 1u : 0u);
-        }
-        give();
-      }
-      commit_both(&dp_full[db]);
-      return true;
-    };
+    const uint32_t ka = smem_u32(smem + L.off_a);
     auto issue_s = [&](int u) -> bool {  // S^T = K_s Q_s^T
       const int sb = u & 1, s = unit_s(u);
       if (u >= 2 && !mbar_wait(&p_full[sb], ((u - 2) >> 1) & 1u, ab, 22)) return false;
@@ -751,18 +796,14 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
     };
     bool ok = mbar_wait(&in_full, 0, ab, 21);
     tc_fence_after();
-    if (ok && kDK) ok = issue_dp(0);
     if (ok) ok = issue_s(0);
     for (int u = 0; ok && u < U; ++u) {
-      if (u + 1 < U) {
-        if (kDK && unit_s(u + 1) == 0) ok = issue_dp(u + 1);
-        if (ok) ok = issue_s(u + 1);
-      }
+      if (u + 1 < U) ok = issue_s(u + 1);
       if (ok && (kDK || unit_s(u) == maps - 1)) ok = issue_acc(u);
     }
     commit_both(&o_full);
     mbar_wait_drain(&o_full, 0);
-  } else if (warp >= 2) {
+  } else if (warp >= 2 && warp < 6) {
     // ---------------------------------------------------------------- softmax + epilogue
     const int quad = warp & 3;
     const int l = quad * 32 + lane;
