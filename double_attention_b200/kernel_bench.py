@@ -113,19 +113,33 @@ def make_case(kernel: str, config: int, device: torch.device):
             ops.gemm_splitk(g_out.view(-1, r), r, True, p_out.view(-1, m), m, True, r, m, groups * rows, d_value)
 
         return run, 4.0 * r * m * groups * rows
-    if kernel == "attention_bwd":  # the whole attention backward op (delta passes, dQ, dK/dV launches)
+    if kernel == "attention_bwd":  # the whole attention backward op (delta pass, dQ, dK and dV launches)
+        # The op as _MixedAttention.backward runs it (fresh zeroed fp32 gradients, the delta pass for
+        # one map), called directly rather than through autograd so that it can be captured.
+        maps = cfg.outer_maps
         routed = F.normalize(torch.randn(2, h, batch, seq, r, generator=g), dim=-1).to(dtype).to(device)
-        routed.requires_grad_()
-        value = torch.randn(batch, seq, d, generator=g).to(dtype).to(device).requires_grad_()
-        scales = torch.full((cfg.outer_maps,), cfg.initial_score_scale, device=device, requires_grad=True)
-        mix = (torch.full((cfg.outer_maps,), 1.0 / cfg.outer_maps, device=device, requires_grad=True)
-               if cfg.outer_maps > 1 else None)
+        value = torch.randn(batch, seq, d, generator=g).to(dtype).to(device)
+        scales = torch.full((maps,), cfg.initial_score_scale, device=device)
+        mix = torch.full((maps,), 1.0 / maps, device=device) if maps > 1 else None
         dy = torch.randn(batch, seq, d, generator=g).to(dtype).to(device)
-        y = ops.routed_attention_mixed(routed, value, scales, mix, _Cfg(cfg.outer_maps))
-        inputs = [t for t in (routed, value, scales, mix) if t is not None]
+        flat = routed.view(-1, r)
+        group, branch0 = ops._map_layout(h, maps)
+        qmap = ops.RowMap(flat, 0, seq, batch * seq)
+        kmap = ops.RowMap(flat, h * batch * seq, seq, batch * seq)
+        y, lse = ops._attention_forward(qmap, kmap, value, batch, seq, r, maps, group, branch0, True, scales, mix,
+                                        None, 1.0, dtype)
 
         def run():
-            torch.autograd.grad(y, inputs, dy, retain_graph=True)
+            droute = torch.zeros(flat.shape, dtype=torch.float32, device=device)
+            dv = torch.zeros(batch * seq, d, dtype=torch.float32, device=device)
+            dscale = torch.zeros(maps, dtype=torch.float32, device=device)
+            dweight = torch.zeros(maps, dtype=torch.float32, device=device) if mix is not None else None
+            if maps == 1:
+                delta, given = ops._attention_delta(dy, y).view(batch, 1, seq), True
+            else:
+                delta, given = torch.empty(batch, maps, seq, dtype=torch.float32, device=device), False
+            ops._attention_backward(qmap, kmap, value, dy, batch, seq, r, maps, group, branch0, True, scales, mix,
+                                    lse, delta, given, droute, droute, dv, dscale, dweight)
 
         return run, float(batch) * seq * seq * (2 * cfg.outer_maps * r + 2 * d)
     if kernel == "projection":

@@ -189,14 +189,16 @@ class SharedDictionaryAttention(nn.Module):
         if cfg.map_combine == "weighted_sum":
             combined = ops.routed_attention_mixed(routed, dense_value, score_scales, map_weights, cfg)
             output = self.output(combined.to(self._output_dtype(combined)))
-            map_weights_out = x.new_ones(1) if map_weights is None else map_weights.to(combined.dtype)
         else:
             per_map = ops.routed_attention_maps(routed, dense_value, score_scales, cfg)  # [B,S,T,D]
             output = self.output(per_map.permute(0, 2, 1, 3).flatten(2))
-            map_weights_out = x.new_full((cfg.outer_maps,), 1.0 / cfg.outer_maps)
 
         if not return_aux:
             return output
+        if cfg.map_combine == "weighted_sum":
+            map_weights_out = x.new_ones(1) if map_weights is None else map_weights.to(combined.dtype)
+        else:
+            map_weights_out = x.new_full((cfg.outer_maps,), 1.0 / cfg.outer_maps)
         score_query, score_key = ops.assemble_score_maps(routed_query, routed_key, cfg.outer_maps)
         return output, DoubleAttentionAux(
             routing_query=routed_query,
