@@ -135,7 +135,11 @@ def ptr(t: torch.Tensor | None) -> int | None:
 
 
 def stream_ptr(device: torch.device | None = None) -> int:
-    return torch.cuda.current_stream(device).cuda_stream
+    """Raw handle of the current CUDA stream of `device` (the current device if None)."""
+    idx = device.index if device is not None else None
+    if idx is None:
+        idx = torch.cuda.current_device()
+    return torch._C._cuda_getCurrentRawStream(idx)
 
 
 def dtype_code(dtype: torch.dtype) -> int:

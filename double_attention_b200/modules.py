@@ -180,7 +180,6 @@ class SharedDictionaryAttention(nn.Module):
         beta, score_scales = ops.temperatures(self.log_beta, self.log_score_scales)  # fp32, one launch
 
         routed = ops.route_projected(projected, views, beta, cfg, x.shape[0], x.shape[1])  # [2,H,B,T,R]
-        routed_query, routed_key = routed[0].permute(1, 0, 2, 3), routed[1].permute(1, 0, 2, 3)
         if cfg.map_combine == "weighted_sum" and self.map_mix_logits is not None:
             map_weights = torch.softmax(self.map_mix_logits, dim=0)
         else:
@@ -199,6 +198,7 @@ class SharedDictionaryAttention(nn.Module):
             map_weights_out = x.new_ones(1) if map_weights is None else map_weights.to(combined.dtype)
         else:
             map_weights_out = x.new_full((cfg.outer_maps,), 1.0 / cfg.outer_maps)
+        routed_query, routed_key = routed[0].permute(1, 0, 2, 3), routed[1].permute(1, 0, 2, 3)
         score_query, score_key = ops.assemble_score_maps(routed_query, routed_key, cfg.outer_maps)
         return output, DoubleAttentionAux(
             routing_query=routed_query,

@@ -14,6 +14,7 @@ no CPU or PyTorch fallback -- unsupported inputs raise.
 
 from __future__ import annotations
 
+import ctypes
 import math
 import threading
 from dataclasses import dataclass
@@ -36,6 +37,9 @@ def compute_dtype(x: Tensor) -> torch.dtype:
     return x.dtype
 
 
+_capability: dict[int, tuple[int, int]] = {}
+
+
 def resolve_backend(backend: str, x: Tensor, dtype: torch.dtype | None = None) -> str:
     """Counterpart of ops.py:142-157.  Only the B200 kernels exist here:
     ``"auto"``/``"triton"``/``"b200"`` select them and fail loudly when they
@@ -47,7 +51,11 @@ def resolve_backend(backend: str, x: Tensor, dtype: torch.dtype | None = None) -
     dtype = dtype or x.dtype
     if not x.is_cuda or dtype not in _HALF:
         raise RuntimeError("B200 backend requested but unavailable: CUDA fp16/bf16 tensors are required")
-    major, minor = torch.cuda.get_device_capability(x.device)
+    idx = x.device.index if x.device.index is not None else torch.cuda.current_device()
+    cap = _capability.get(idx)
+    if cap is None:
+        cap = _capability[idx] = torch.cuda.get_device_capability(idx)
+    major, minor = cap
     if (major, minor) != (10, 0):
         raise RuntimeError(f"B200 backend requested but unavailable: sm_100 GPU required, found sm_{major}{minor}")
     return "b200"
@@ -123,6 +131,12 @@ def device_status(device: torch.device | None = None, reset: bool = True) -> int
     if flags & 1:
         raise _lib.DAError("device status", _lib.DA_ERR_DEVICE_TIMEOUT, f"bounded wait gave up at site {site}")
     return flags
+
+
+def _grad_wanted(*tensors: Tensor | None) -> bool:
+    """True when autograd must record this op (grad mode on and an input requires grad); otherwise
+    the wrappers below call the kernels directly, without the autograd Function machinery."""
+    return torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in tensors)
 
 
 def _check_half_cuda(name: str, *tensors: Tensor) -> None:
@@ -274,18 +288,23 @@ BETA_LOG_RANGE = (math.log(0.05), math.log(64.0))     # modules.py:130-132
 SCALE_LOG_RANGE = (math.log(0.25), math.log(1024.0))  # ops.py:160-161
 
 
+def _temperatures_forward(log_beta: Tensor, log_scales: Tensor) -> tuple[Tensor, Tensor]:
+    dev = log_scales.device
+    out = torch.empty(1 + log_scales.numel(), dtype=torch.float32, device=dev)
+    beta, scales = out[:1], out[1:]
+    lb, ls = log_beta.detach().contiguous(), log_scales.detach().contiguous()
+    call("da_temperatures", lb.data_ptr(), dtype_code(lb.dtype), BETA_LOG_RANGE[0], BETA_LOG_RANGE[1],
+         ls.data_ptr(), dtype_code(ls.dtype), ls.numel(), SCALE_LOG_RANGE[0], SCALE_LOG_RANGE[1],
+         beta.data_ptr(), scales.data_ptr(), stream_ptr(dev))
+    return beta, scales
+
+
 class _Temperatures(torch.autograd.Function):
     """beta and the per-map score scales in fp32 from their logs, one launch."""
 
     @staticmethod
     def forward(ctx, log_beta: Tensor, log_scales: Tensor):  # type: ignore[override]
-        dev = log_scales.device
-        beta = torch.empty(1, dtype=torch.float32, device=dev)
-        scales = torch.empty(log_scales.numel(), dtype=torch.float32, device=dev)
-        lb, ls = log_beta.detach().contiguous(), log_scales.detach().contiguous()
-        call("da_temperatures", lb.data_ptr(), dtype_code(lb.dtype), BETA_LOG_RANGE[0], BETA_LOG_RANGE[1],
-             ls.data_ptr(), dtype_code(ls.dtype), ls.numel(), SCALE_LOG_RANGE[0], SCALE_LOG_RANGE[1],
-             beta.data_ptr(), scales.data_ptr(), stream_ptr(dev))
+        beta, scales = _temperatures_forward(log_beta, log_scales)
         ctx.save_for_backward(log_beta, log_scales, beta, scales)
         return beta, scales
 
@@ -305,13 +324,35 @@ class _Temperatures(torch.autograd.Function):
 
 def temperatures(log_beta: Tensor, log_scales: Tensor) -> tuple[Tensor, Tensor]:
     """``(beta [1], scales [S])`` in fp32: exp of the clamped logs (modules.py:130-132, ops.py:160-161)."""
+    if not _grad_wanted(log_beta, log_scales):
+        return _temperatures_forward(log_beta, log_scales)
     return _Temperatures.apply(log_beta, log_scales)
+
+
+def _dictionary_views_nograd(raw_key: Tensor, raw_value: Tensor | None, eps: float,
+                             dtype: torch.dtype) -> DictionaryViews:
+    """The views of dictionary_views without autograd (one launch)."""
+    rk = raw_key.detach().contiguous()
+    rv = rk if raw_value is None else raw_value.detach().to(rk.dtype).contiguous()
+    r, m = rk.shape
+    dev = rk.device
+    key, key_t = torch.empty(r, m, dtype=dtype, device=dev), torch.empty(m, r, dtype=dtype, device=dev)
+    value = torch.empty(r, m, dtype=torch.bfloat16, device=dev)
+    value_t = torch.empty(m, r, dtype=torch.bfloat16, device=dev)
+    stats = torch.empty(2 * m + 4, dtype=torch.float32, device=dev)  # key / value denominators, max
+    kden, vden, kmax = stats[:m], stats[m:2 * m], stats[2 * m:2 * m + 1]
+    call("da_dict_norm_pair_fwd", rk.data_ptr(), rv.data_ptr(), dtype_code(rk.dtype), r, m, eps, dtype_code(dtype),
+         key.data_ptr(), key_t.data_ptr(), kden.data_ptr(), kmax.data_ptr(), value.data_ptr(), value_t.data_ptr(),
+         vden.data_ptr(), stream_ptr(rk.device))
+    return DictionaryViews(key, key_t, value, value_t, kmax, key, value)
 
 
 def dictionary_views(raw_key: Tensor, raw_value: Tensor | None, eps: float, dtype: torch.dtype) -> DictionaryViews:
     """Normalise a bank's raw parameters into kernel operands (autograd-aware)."""
     if not raw_key.is_cuda:
         raise RuntimeError("B200 backend requested but unavailable: CUDA fp16/bf16 tensors are required")
+    if not _grad_wanted(raw_key, raw_value):
+        return _dictionary_views_nograd(raw_key, raw_value, eps, dtype)
     if raw_value is None and dtype == torch.bfloat16:  # tied dictionary: one set of bf16 views serves both
         key, key_t, key_max, key_anchor = _DictNorm.apply(raw_key, eps, dtype)
         return DictionaryViews(key, key_t, key, key_t, key_max, key_anchor, key_anchor)
@@ -552,6 +593,8 @@ class _RouteVariantFn(torch.autograd.Function):
 
 def _route_rows(q: Tensor, views: DictionaryViews, beta: Tensor, rows: int, groups: int, col_stride: int, eps: float,
                 normalize_input: bool, normalize_output: bool, variant: RouteVariant | None) -> Tensor:
+    if variant is None and not _grad_wanted(q, views.key_anchor, views.value_anchor, beta):
+        return _route_forward(q, rows, groups, col_stride, views, beta, eps, normalize_input, normalize_output)[0]
     if variant is None:
         return _Route.apply(q, views.key, views.key_t, views.value, views.value_t, views.key_max, views.key_anchor,
                             views.value_anchor, beta, rows, groups, col_stride, eps, normalize_input,
@@ -772,6 +815,15 @@ def routed_attention_mixed(routed: Tensor, value: Tensor, scales: Tensor, map_we
     maps = cfg.outer_maps
     # Routed vectors have norm <= 1 (normalised outputs, or convex combinations
     # of unit dictionary atoms), which bounds every score by gamma_s.
+    if not _grad_wanted(routed, value, scales, map_weights):
+        _two, h, batch, length, r = routed.shape
+        flat = routed.view(-1, r)
+        group, branch0 = _map_layout(h, maps)
+        y, _lse = _attention_forward(RowMap(flat, 0, length, batch * length),
+                                     RowMap(flat, h * batch * length, length, batch * length), value, batch, length,
+                                     r, maps, group, branch0, cfg.causal, scales,
+                                     map_weights if maps > 1 else None, None, 1.0, routed.dtype)
+        return y
     return _MixedAttention.apply(routed, value, scales, map_weights, maps, cfg.causal, 1.0)
 
 
@@ -931,27 +983,34 @@ class _Projection(torch.autograd.Function):
         return dx, dw
 
 
+_PTR3 = ctypes.c_void_p * 3
+_I64X3 = ctypes.c_int64 * 3
+_I32X3 = ctypes.c_int * 3
+
+
+def _qkv_forward(x2d: Tensor, wq: Tensor, wk: Tensor, wv: Tensor, bv: Tensor | None) -> tuple[Tensor, Tensor]:
+    m, k = x2d.shape
+    hr, d = wq.shape[0], wv.shape[0]
+    dev = x2d.device
+    proj = torch.empty(m, 2 * hr, dtype=x2d.dtype, device=dev)
+    value = torch.empty(m, d, dtype=torch.bfloat16, device=dev)
+    dt = dtype_code(x2d.dtype)
+    call("da_gemm_segments", x2d.data_ptr(), x2d.stride(0), m, k, dt, 3,
+         _PTR3(wq.data_ptr(), wk.data_ptr(), wv.data_ptr()), _I64X3(wq.stride(0), wk.stride(0), wv.stride(0)),
+         _I64X3(hr, hr, d), _PTR3(proj.data_ptr(), proj.data_ptr() + hr * proj.element_size(), value.data_ptr()),
+         _I64X3(2 * hr, 2 * hr, d), _I32X3(dt, dt, _lib.DA_BF16),
+         _PTR3(None, None, None if bv is None else bv.data_ptr()), workspace(dev).status.data_ptr(),
+         stream_ptr(dev))
+    return proj, value
+
+
 class _QKVProjection(torch.autograd.Function):
     """Q/K projection [B*T, 2*H*R] (compute dtype) and value projection [B*T, D] (bf16, + bias) of one
     input in one launch (modules.py:143-157 and the value Linear)."""
 
     @staticmethod
     def forward(ctx, x2d: Tensor, wq: Tensor, wk: Tensor, wv: Tensor, bv: Tensor | None):  # type: ignore[override]
-        m, k = x2d.shape
-        hr, d = wq.shape[0], wv.shape[0]
-        dev = x2d.device
-        proj = torch.empty(m, 2 * hr, dtype=x2d.dtype, device=dev)
-        value = torch.empty(m, d, dtype=torch.bfloat16, device=dev)
-        import ctypes
-
-        ptrs = lambda *v: (ctypes.c_void_p * 3)(*v)  # noqa: E731
-        i64 = lambda *v: (ctypes.c_int64 * 3)(*v)  # noqa: E731
-        ws = workspace(dev)
-        call("da_gemm_segments", x2d.data_ptr(), x2d.stride(0), m, k, dtype_code(x2d.dtype), 3,
-             ptrs(wq.data_ptr(), wk.data_ptr(), wv.data_ptr()), i64(wq.stride(0), wk.stride(0), wv.stride(0)),
-             i64(hr, hr, d), ptrs(proj.data_ptr(), proj.data_ptr() + hr * proj.element_size(), value.data_ptr()),
-             i64(2 * hr, 2 * hr, d), (ctypes.c_int * 3)(dtype_code(x2d.dtype), dtype_code(x2d.dtype), _lib.DA_BF16),
-             ptrs(None, None, None if bv is None else bv.data_ptr()), ws.status.data_ptr(), stream_ptr(dev))
+        proj, value = _qkv_forward(x2d, wq, wk, wv, bv)
         ctx.save_for_backward(x2d, wq, wk, wv)
         ctx.has_bias = bv is not None
         return proj, value
@@ -989,8 +1048,10 @@ def qkv_projection(x: Tensor, wq: Tensor, wk: Tensor, wv: Tensor, bv: Tensor | N
     x2d = x.reshape(-1, x.shape[-1])
     if not x2d.is_contiguous():
         x2d = x2d.contiguous()
-    return _QKVProjection.apply(x2d, wq.contiguous(), wk.contiguous(), wv.contiguous(),
-                                None if bv is None else bv.contiguous())
+    args = (x2d, wq.contiguous(), wk.contiguous(), wv.contiguous(), None if bv is None else bv.contiguous())
+    if not _grad_wanted(*args):
+        return _qkv_forward(*args)
+    return _QKVProjection.apply(*args)
 
 
 def qk_projection(x: Tensor, fused_weight: Tensor) -> Tensor:
