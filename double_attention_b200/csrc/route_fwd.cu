@@ -83,11 +83,10 @@ struct FwdParams {
   int* trace;           // optional progress markers (debug)
 };
 
-// Exact fp32 recomputation of the listed rows by one CTA (rare path).
+// Exact fp32 recomputation of `count` listed rows (global indices g * rows + row) by one CTA (rare path).
 template <int kR, typename T>
-__device__ void repair_listed_rows(const FwdParams& p, float* buf) {
+__device__ void repair_rows(const FwdParams& p, const int* list, int count, float* buf) {
   const int nthr = blockDim.x, tid = threadIdx.x;
-  const int count = min(p.work[1], p.repair_cap);
   float* prob = buf;            // [M]
   float* vec = prob + p.M;      // [kR]
   float* red = vec + kR;        // [32]
@@ -113,7 +112,7 @@ __device__ void repair_listed_rows(const FwdParams& p, float* buf) {
   const T* dkt = reinterpret_cast<const T*>(p.dk_t);
   const __nv_bfloat16* dv = reinterpret_cast<const __nv_bfloat16*>(p.dv);
   for (int it = 0; it < count; ++it) {
-    const int idx = p.work[2 + it];
+    const int idx = list[it];
     const int g = idx / p.rows, row = idx % p.rows;
     const T* qrow = reinterpret_cast<const T*>(p.q) + (size_t)row * p.q_row_stride + (size_t)g * p.col_stride;
     float ss = 0.f;
@@ -517,7 +516,7 @@ __global__ void __launch_bounds__(192, 1) route_fwd_kernel(const __grid_constant
   __syncthreads();
   if (is_last) {
     __threadfence();
-    repair_listed_rows<kR, T>(p, reinterpret_cast<float*>(smem));
+    repair_rows<kR, T>(p, p.work + 2, min(p.work[1], p.repair_cap), reinterpret_cast<float*>(smem));
     __syncthreads();
     if (threadIdx.x == 0) {
       p.work[1] = 0;
@@ -608,7 +607,8 @@ __global__ void __launch_bounds__(kWideThreads, 1) route_fwd_wide_kernel(const _
   __shared__ uint64_t k_full[kWideMaxK], k_empty[kWideMaxK], v_full[kWideMaxV], v_empty[kWideMaxV];
   __shared__ uint64_t s_full[kWideMaxSB], p_full[kWideMaxSB], p_empty[kWideMaxPB];
   __shared__ uint32_t tmem_base;
-  __shared__ int abort_flag, is_last;
+  __shared__ int abort_flag, n_listed;
+  __shared__ int listed[64];  // this CTA's rows whose mass fell below the fixed offset's range
 
   const WideLayout L = wide_layout(kR, p.M);
   constexpr int kRows = 64;
@@ -626,6 +626,7 @@ __global__ void __launch_bounds__(kWideThreads, 1) route_fwd_wide_kernel(const _
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
+    n_listed = 0;
     mbar_init(&q_full, 1);
     mbar_init(&o_full, 1);
     for (int i = 0; i < kWideMaxK; ++i) {
@@ -913,12 +914,7 @@ __global__ void __launch_bounds__(kWideThreads, 1) route_fwd_wide_kernel(const _
       p.lse[idx] = (bound + log2f(sum_all)) * kLn2;
       p.out_norm[idx] = onorm / sum_all;
       if (want_argmax) p.argmax[idx] = amax_all;
-      if (mx_all - bound < -100.f || !(sum_all > 0.f)) {
-        const int slot = atomicAdd(&p.work[1], 1);
-        if (slot < p.repair_cap) p.work[2 + slot] = (int)idx;
-        else atomicOr(p.status, DA_DEV_ROW_OVERFLOW);
-        __threadfence();  // the listed row is visible before this CTA takes its ticket
-      }
+      if (mx_all - bound < -100.f || !(sum_all > 0.f)) listed[atomicAdd(&n_listed, 1)] = (int)idx;
     }
   }
 
@@ -927,22 +923,8 @@ __global__ void __launch_bounds__(kWideThreads, 1) route_fwd_wide_kernel(const _
   cluster_sync();
   if (warp == 1) tmem_dealloc<2>(tmem, L.tmem_cols);
 
-  // The last CTA to finish repairs the listed rows and resets the counters.
-  if (threadIdx.x == 0) {
-    __threadfence();
-    is_last = atomicAdd(&p.work[0], 1) == (int)gridDim.x - 1;
-  }
-  __syncthreads();
-  if (is_last) {
-    __threadfence();
-    repair_listed_rows<kR, T>(p, reinterpret_cast<float*>(smem));
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      p.work[1] = 0;
-      p.work[0] = 0;
-      __threadfence();
-    }
-  }
+  // This CTA recomputes its own listed rows exactly (rare); the pipeline's shared memory is free now.
+  if (n_listed > 0) repair_rows<kR, T>(p, listed, n_listed, reinterpret_cast<float*>(smem));
   if (threadIdx.x == 0) trace_time(p.trace, 7);
 }
 
