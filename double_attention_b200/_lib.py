@@ -51,6 +51,7 @@ SIGNATURES: dict[str, list] = {
                     _p, _i32, _i32, _p, _p, _p, _f32, _p, _p, _p, _p],
     "da_attn_bwd_delta": [_p, _p, _i64, _i32, _i32, _p, _p],
     "da_gemm_splitk": [_p, _i64, _i32, _p, _i64, _i32, _p, _i64, _i64, _i64, _i64, _i32, _i32, _p, _p],
+    "da_gemm_splitk_grouped": [_p, _i64, _i64, _p, _i64, _p, _i64, _i64, _i64, _i64, _i32, _i32, _i32, _p, _p],
     "da_route_bwd": [_p, _i64, _i64, _i64, _i32, _i64, _i64, _i64, _i32, _p, _p, _p, _f32, _i32, _i32, _p, _p, _p,
                      _p, _p, _p, _p, _p, _p, _p, _p],
     "da_attn_bwd_mixed": [_p, _i64, _i64, _i64, _i64, _p, _i64, _i64, _i64, _i64, _p, _p, _i32, _i32, _i32, _i32,

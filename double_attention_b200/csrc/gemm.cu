@@ -34,6 +34,9 @@ struct Params {
   int accumulate;  // C += A.B (else C = A.B)
   int* status;
   int kps;         // K stages per split (split-K when gridDim.z > 1), 0 = all
+  // grouped K (MN-major A only): K stage kb belongs to group kb / kseg, whose A columns start
+  // a_goff further right and whose A rows restart at 0; 0 = one group
+  int kseg = 0, a_goff = 0, a_inner = 0;
 };
 
 template <typename T, int kN, bool kAmn, bool kBmn>
@@ -88,8 +91,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         if (!kAmn) {
           tma_load_2d(&ta, &full[s], sa, (kb0 + kb) * kBK, m0);
         } else {
-          tma_load_2d(&ta, &full[s], sa, m0, (kb0 + kb) * kBK);
-          tma_load_2d(&ta, &full[s], sa + kBK * 128, m0 + 64, (kb0 + kb) * kBK);
+          const int kbg = kb0 + kb;
+          const int grp = p.kseg ? kbg / p.kseg : 0;
+          const int ax = m0 + grp * p.a_goff, ay = (kbg - grp * p.kseg) * kBK;
+          tma_load_2d(&ta, &full[s], sa, ax, ay);
+          tma_load_2d(&ta, &full[s], sa + kBK * 128, ax + 64, ay);
         }
         if (!kBmn) {
           tma_load_2d(&tb, &full[s], sb, (kb0 + kb) * kBK, n0);
@@ -319,7 +325,8 @@ int launch(const void* A, int64_t lda, const void* B, int64_t ldb, const Params&
   const CUtensorMapDataType dt =
       std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap ta, tb;
-  int rc = kAmn ? make_tmap_2d(&ta, A, dt, 2, p.M, p.K, (uint64_t)lda * 2, 64, kBK)
+  int rc = kAmn ? (p.kseg ? make_tmap_2d(&ta, A, dt, 2, p.a_inner, (uint64_t)p.kseg * kBK, (uint64_t)lda * 2, 64, kBK)
+                          : make_tmap_2d(&ta, A, dt, 2, p.M, p.K, (uint64_t)lda * 2, 64, kBK))
                 : make_tmap_2d(&ta, A, dt, 2, p.K, p.M, (uint64_t)lda * 2, 64, kBM);
   if (rc) return rc;
   rc = kBmn ? make_tmap_2d(&tb, B, dt, 2, p.N, p.K, (uint64_t)ldb * 2, 64, kBK)
@@ -461,4 +468,34 @@ extern "C" int da_gemm_segments(const void* A, int64_t lda, int64_t M, int64_t K
                 : run(gemm_seg_kernel<__half, 256>, Cfg<256>::kSmem + 1024);
   return bf16 ? run(gemm_seg_kernel<__nv_bfloat16, 128>, Cfg<128>::kSmem + 1024)
               : run(gemm_seg_kernel<__half, 128>, Cfg<128>::kSmem + 1024);
+}
+
+extern "C" int da_gemm_splitk_grouped(const void* A, int64_t lda, int64_t a_group_cols, const void* B, int64_t ldb,
+                                      float* C, int64_t ldc, int64_t M, int64_t N, int64_t K_group, int groups,
+                                      int dtype, int splits, int* status, void* stream) {
+  using namespace da;
+  if (!A || !B || !C || !status) return DA_ERR_NULL;
+  if (int rc = bind_device(A)) return rc;
+  if (dtype != DA_BF16 && dtype != DA_F16) return DA_ERR_DTYPE;
+  if (M <= 0 || N <= 0 || K_group <= 0 || groups <= 0 || N % 128 || M % 128 || K_group % gemm::kBK)
+    return DA_ERR_SHAPE;
+  if (a_group_cols < 0 || a_group_cols % 8 || (lda % 8) || (ldb % 8)) return DA_ERR_ALIGN;
+  if ((int64_t)(groups - 1) * a_group_cols + M > lda) return DA_ERR_SHAPE;
+  if ((reinterpret_cast<uintptr_t>(C) & 15) || (ldc % 4)) return DA_ERR_ALIGN;
+  const int64_t K = K_group * groups;
+  const int nk = (int)(K / gemm::kBK);
+  if (splits <= 0) {  // about two CTAs per SM-sized wave of output tiles
+    const int tiles = (int)((M / 128) * (N / 128));
+    splits = (2 * sm_count() + tiles - 1) / tiles;
+  }
+  int kps = (nk + splits - 1) / splits;
+  if (kps < 1) kps = 1;
+  splits = (nk + kps - 1) / kps;
+  gemm::Params p{(int)M, (int)N, (int)K, C, ldc, 1, 1, status, kps};
+  p.kseg = (int)(K_group / gemm::kBK);
+  p.a_goff = (int)a_group_cols;
+  p.a_inner = (int)((groups - 1) * a_group_cols + M);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == DA_BF16) return gemm::dispatch<__nv_bfloat16>(1, 1, 128, A, lda, B, ldb, p, splits, st);
+  return gemm::dispatch<__half>(1, 1, 128, A, lda, B, ldb, p, splits, st);
 }

@@ -108,8 +108,7 @@ def make_case(kernel: str, config: int, device: torch.device):
         d_value = torch.zeros(r, m, device=device)
 
         def run():
-            for gi in range(groups):
-                ops.gemm_splitk(proj[:, gi * r:], proj.stride(0), True, dl_out[gi], m, True, r, m, rows, d_key)
+            ops.key_dictionary_grad(proj, r, dl_out, d_key)
             ops.gemm_splitk(g_out.view(-1, r), r, True, p_out.view(-1, m), m, True, r, m, groups * rows, d_value)
 
         return run, 4.0 * r * m * groups * rows

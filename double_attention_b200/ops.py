@@ -433,6 +433,22 @@ def gemm_splitk(a: Tensor, lda: int, a_mn: bool, b: Tensor, ldb: int, b_mn: bool
     return out
 
 
+def key_dictionary_grad(q: Tensor, col_stride: int, dl: Tensor, out: Tensor) -> Tensor:
+    """out [R, M] fp32 += sum_g q_g^T dl[g]: q_g the g-th column block (width R, stride col_stride) of
+    the routed matrix q [rows, cols], dl [groups, rows, M] -- one split-K launch over every group
+    when the rows divide into 64-row stages, else one per group."""
+    groups, rows, m = dl.shape
+    r = out.shape[0]
+    if groups > 1 and rows % 64 == 0 and col_stride % 8 == 0:
+        call("da_gemm_splitk_grouped", q.data_ptr(), q.stride(0), col_stride, dl.data_ptr(), m, out.data_ptr(),
+             out.stride(0), r, m, rows, groups, dtype_code(q.dtype), 0, workspace(q.device).status.data_ptr(),
+             stream_ptr(q.device))
+    else:
+        for g in range(groups):
+            gemm_splitk(q[:, g * col_stride:], q.stride(0), True, dl[g], m, True, r, m, rows, out)
+    return out
+
+
 def _route_backward(ctx, dz: Tensor):
     """dq, fp32 dDk / dDv (into the anchors) and dbeta of one route call."""
     q, key_t, value_t, beta, z, lse, onorm = ctx.saved_tensors
@@ -456,8 +472,7 @@ def _route_backward(ctx, dz: Tensor):
     d_key = d_value = None
     if need[6]:  # dDk = sum_groups q_g^T dL'_g  (dL' already carries 1 / ||q||)
         d_key = torch.zeros(r, m, dtype=torch.float32, device=dev)
-        for g in range(groups):
-            gemm_splitk(q[:, g * col_stride:], q.stride(0), True, dl_out[g], m, True, r, m, rows, d_key)
+        key_dictionary_grad(q, col_stride, dl_out, d_key)
     if need[7]:  # dDv = G^T P over every routed row
         d_value = torch.zeros(r, m, dtype=torch.float32, device=dev)
         gemm_splitk(g_out.view(-1, r), r, True, p_out.view(-1, m), m, True, r, m, groups * rows, d_value)

@@ -290,6 +290,16 @@ DA_API int da_gemm_splitk(const void* A, int64_t lda, int a_mn_major, const void
                           float* C, int64_t ldc, int64_t M, int64_t N, int64_t K, int dtype, int splits, int* status,
                           void* stream);
 
+/* The same sum over several groups at once: C [M, N] fp32 += sum over g < groups and k < K_group of
+ * A(m, g, k) B(n, g, k) with A MN-major, its group g starting a_group_cols columns to the right
+ * (A(m, g, k) = A[k * lda + g * a_group_cols + m]), and B MN-major with the groups stacked along K
+ * (B(n, g, k) = B[(g * K_group + k) * ldb + n]).  This is the key-dictionary gradient of the route
+ * backward, dDk = sum_groups q_g^T dL'_g (triton_kernels.py:1939), in one launch instead of one per
+ * group.  K_group a multiple of 64, M and N multiples of 128, a_group_cols a multiple of 8. */
+DA_API int da_gemm_splitk_grouped(const void* A, int64_t lda, int64_t a_group_cols, const void* B, int64_t ldb,
+                                  float* C, int64_t ldc, int64_t M, int64_t N, int64_t K_group, int groups, int dtype,
+                                  int splits, int* status, void* stream);
+
 /* ---- building-block check -------------------------------------------
  * No reference counterpart: D[128, n] = A[128, k] * B^T computed by one
  * tcgen05 tile (cta_group 1 or 2) for testing the descriptor layouts.

@@ -50,3 +50,22 @@ def test_projection_autograd() -> None:
     torch.testing.assert_close(y.float(), yr, atol=2e-2, rtol=1e-2)
     torch.testing.assert_close(x.grad.float(), xr.grad, atol=5e-2, rtol=2e-2)
     torch.testing.assert_close(w.grad.float(), wr.grad, atol=1e-1, rtol=2e-2)
+
+
+@pytest.mark.parametrize(("groups", "rows", "r", "m", "cs"), [(8, 512, 128, 512, 128), (2, 4096, 256, 512, 256),
+                                                             (3, 192, 128, 384, 136)])
+def test_grouped_splitk_matches_reference(groups, rows, r, m, cs) -> None:
+    """da_gemm_splitk_grouped: C += sum_g A_g^T B_g with A_g the g-th column block of a row-major matrix."""
+    dev = torch.device("cuda")
+    g = torch.Generator().manual_seed(groups + rows)
+    a = torch.randn(rows, (groups - 1) * cs + r + 8, generator=g).to(torch.bfloat16)
+    b = torch.randn(groups, rows, m, generator=g).to(torch.bfloat16)
+    out = torch.zeros(r, m, dtype=torch.float32, device=dev)
+    ad, bd = a.to(dev), b.to(dev)
+    ws = ops.workspace(dev)
+    ops.call("da_gemm_splitk_grouped", ad.data_ptr(), ad.stride(0), cs, bd.data_ptr(), m, out.data_ptr(), m, r, m,
+             rows, groups, 1, 0, ws.status.data_ptr(), ops.stream_ptr(dev))
+    torch.cuda.synchronize()
+    ref = sum(a[:, k * cs:k * cs + r].double().t() @ b[k].double() for k in range(groups))
+    err = (out.double().cpu() - ref).abs().max().item()
+    assert err <= 1e-3 * ref.abs().max().item(), err
