@@ -63,6 +63,7 @@ struct Params {
   __nv_bfloat16* g_out;    // [groups, rows, R]
   float* dbeta;            // accumulated (may be null)
   int* status;
+  int* trace;              // optional progress stamps (debug)
 };
 
 struct Layout {
@@ -96,10 +97,12 @@ template <typename T>
 __global__ void __launch_bounds__(kThreads, 1) route_bwd_kernel(const __grid_constant__ CUtensorMap tq,
                                                                 const __grid_constant__ CUtensorMap tdk,
                                                                 const __grid_constant__ CUtensorMap tdv,
+                                                                const __grid_constant__ CUtensorMap tz,
+                                                                const __grid_constant__ CUtensorMap tdz,
                                                                 const Params p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ uint64_t in_full, g_full, o_full, r_full[kMaxStages], r_empty[kMaxStages];
+  __shared__ uint64_t in_full, g_full, o_full, zd_full, r_full[kMaxStages], r_empty[kMaxStages];
   __shared__ uint64_t s_full[2], p_full[2], dl_empty[2];
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
@@ -114,13 +117,20 @@ __global__ void __launch_bounds__(kThreads, 1) route_bwd_kernel(const __grid_con
   const int grp = pair / tiles_per_group;
   const int row0 = (pair % tiles_per_group) * 128;
   const int NJ = p.M / kNA;
+  // R <= 256: this CTA's z rows land in the (not yet used) dL' buffer and its dz rows in the g
+  // buffer by TMA, so the output-normalisation backward reads both from shared memory once
+  const bool zd_tma = R <= 256;
   Abort ab{&abort_flag, p.status};
+  // debug trace: 8 phase stamps per CTA, then per-tile stamps of the first pair
+  int* ft = (p.trace && blockIdx.x < 2) ? p.trace + gridDim.x * 8 + blockIdx.x * 256 : nullptr;
+  if (threadIdx.x == 0) trace_time(p.trace, 0);
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
     mbar_init(&in_full, 1);
     mbar_init(&g_full, 2);  // one arrival per CTA of the pair
     mbar_init(&o_full, 1);
+    mbar_init(&zd_full, 1);
     for (int i = 0; i < kMaxStages; ++i) {
       mbar_init(&r_full[i], 1);
       mbar_init(&r_empty[i], 1);
@@ -143,6 +153,7 @@ __global__ void __launch_bounds__(kThreads, 1) route_bwd_kernel(const __grid_con
   grid_dependency_wait();  // predecessors' outputs are visible from here on
   grid_launch_dependents();
   const uint32_t tmem = tmem_base;
+  if (threadIdx.x == 0) trace_time(p.trace, 1);
 
   if (warp == 0 && lane == 0) {
     // ---------------------------------------------------------------- TMA producer
@@ -156,6 +167,16 @@ __global__ void __launch_bounds__(kThreads, 1) route_bwd_kernel(const __grid_con
     const int qcol = (int)(grp * p.col_stride);
     for (int cb = 0; cb < R / 64; ++cb)
       tma_load_2d_pair(&tq, inf, smem + L.off_q + cb * (kRows * 128), qcol + cb * 64, qrow);
+    if (zd_tma) {  // this CTA's own rows of z and dz, on its own barrier
+      prefetch_tmap(&tz);
+      prefetch_tmap(&tdz);
+      mbar_arrive_expect_tx(&zd_full, 2 * kRows * R * 2);
+      const int zrow = (int)((int64_t)grp * p.rows + qrow);
+      for (int cb = 0; cb < R / 64; ++cb) {
+        tma_load_2d(&tz, &zd_full, smem + L.off_dl + cb * (kRows * 128), cb * 64, zrow);
+        tma_load_2d(&tdz, &zd_full, smem + L.off_g + cb * (kRows * 128), cb * 64, zrow);
+      }
+    }
     int it = 0;
     bool ok = true;
     auto stage = [&](int bytes) -> uint8_t* {
@@ -194,6 +215,7 @@ __global__ void __launch_bounds__(kThreads, 1) route_bwd_kernel(const __grid_con
       if (j + 1 < NJ) items_sdp(j + 1);
       items_u(j);
     }
+    if (zd_tma) mbar_wait_drain(&zd_full, 0);
     if (rank == 0) {
       mbar_wait_drain(&in_full, 0);
       for (int i = (it > L.nst ? it - L.nst : 0); i < it; ++i) mbar_wait_drain(&r_full[i % L.nst], (i / L.nst) & 1u);
@@ -220,7 +242,9 @@ __global__ void __launch_bounds__(kThreads, 1) route_bwd_kernel(const __grid_con
     bool g_ready = false;
     auto issue_sdp = [&](int j) -> bool {
       const int sb = j & 1;
+      trace_at(ft, 16 + 4 * j);
       if (j >= 2 && !mbar_wait(&p_full[sb], ((j - 2) >> 1) & 1u, ab, 22)) return false;
+      trace_at(ft, 17 + 4 * j);
       for (int pass = 0; pass < 2; ++pass) {
         if (pass == 1 && !g_ready) {
           if (!mbar_wait(&g_full, 0, ab, 26)) return false;
@@ -243,11 +267,13 @@ __global__ void __launch_bounds__(kThreads, 1) route_bwd_kernel(const __grid_con
         }
       }
       commit_both(&s_full[sb]);
+      trace_at(ft, 18 + 4 * j);
       return true;
     };
     auto issue_u = [&](int j) -> bool {
       const int sb = j & 1;
       if (!mbar_wait(&p_full[sb], (j >> 1) & 1u, ab, 24)) return false;
+      trace_at(ft, 19 + 4 * j);
       tc_fence_after();
       const uint32_t dla = smem_u32(smem + L.off_dl + sb * (kRows * kNA * 2));
       for (int kc = 0; kc < kNA / 64; ++kc)
@@ -293,7 +319,26 @@ __global__ void __launch_bounds__(kThreads, 1) route_bwd_kernel(const __grid_con
     const uint4* dzrow = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.dz) + idx * R + half * hw);
     const float on = live ? __ldg(p.out_norm + idx) : 1.f;
     float zd = 0.f, zz = 0.f;
-    for (int c0 = 0; c0 < hw / 8; c0 += 8) {
+    const uint32_t zsm = smem_u32(smem + L.off_dl), dzsm = smem_u32(smem + L.off_g);
+    auto zd_addr = [&](int col) { return (uint32_t)((col >> 6) * (kRows * 128)) + sw128_offset(r, (col & 63) >> 3); };
+    bool zd_ok = true;
+    if (zd_tma) {
+      zd_ok = __all_sync(0xffffffffu, mbar_wait(&zd_full, 0, ab, 36));
+      if (zd_ok)
+        for (int c = 0; c < hw / 8; ++c) {
+          const uint32_t o = zd_addr(half * hw + c * 8);
+          const uint4 a = ld_shared_v4(zsm + o), d = ld_shared_v4(dzsm + o);
+          const uint32_t wa[4] = {a.x, a.y, a.z, a.w}, wd[4] = {d.x, d.y, d.z, d.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 fa = unpack2<T>(wa[e]), fd = unpack2<T>(wd[e]);
+            zd = fmaf(fa.x, fd.x, fmaf(fa.y, fd.y, zd));
+            zz = fmaf(fa.x, fa.x, fmaf(fa.y, fa.y, zz));
+          }
+        }
+      if (!live) zd = zz = 0.f;
+    }
+    for (int c0 = 0; !zd_tma && c0 < hw / 8; c0 += 8) {
       uint4 a[8], d[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
@@ -329,7 +374,24 @@ __global__ void __launch_bounds__(kThreads, 1) route_bwd_kernel(const __grid_con
         delta = zd;
       }
     }
-    {
+    if (zd_tma) {  // g in place of dz (each thread rewrites only what it read)
+      uint4* grow_out = reinterpret_cast<uint4*>(p.g_out + idx * R + half * hw);
+      if (zd_ok)
+        for (int c = 0; c < hw / 8; ++c) {
+          const uint32_t o = zd_addr(half * hw + c * 8);
+          const uint4 a = ld_shared_v4(zsm + o), d = ld_shared_v4(dzsm + o);
+          const uint32_t wa[4] = {a.x, a.y, a.z, a.w}, wd[4] = {d.x, d.y, d.z, d.w};
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 fa = unpack2<T>(wa[e]), fd = unpack2<T>(wd[e]);
+            w[e] = live ? pack_bf16x2(ca * fd.x - cb * fa.x, ca * fd.y - cb * fa.y) : 0u;
+          }
+          if (live) grow_out[c] = make_uint4(w[0], w[1], w[2], w[3]);
+          st_shared_v4(dzsm + o, w[0], w[1], w[2], w[3]);
+        }
+      fence_proxy_async();
+    } else {
       const uint32_t gsm = smem_u32(smem + L.off_g);
       uint4* grow_out = reinterpret_cast<uint4*>(p.g_out + idx * R + half * hw);
       for (int c0 = 0; c0 < hw / 8; c0 += 8) {
@@ -357,6 +419,7 @@ __global__ void __launch_bounds__(kThreads, 1) route_bwd_kernel(const __grid_con
     }
     named_bar_sync(1, 128);
     if (arriver) mbar_arrive_cluster(mapa_shared(smem_u32(&g_full), 0));
+    if (arriver) trace_time(p.trace, 2);
 
     // ---- per atom tile: P, dL' (shared memory + rows for the dictionary gradients), dbeta
     const float lse2 = live ? p.lse[idx] * kLog2e : 0.f;
@@ -368,7 +431,9 @@ __global__ void __launch_bounds__(kThreads, 1) route_bwd_kernel(const __grid_con
     __nv_bfloat16* p_row = p.p_out + idx * p.M;
     for (int j = 0; j < NJ; ++j) {
       const int sb = j & 1;
+      if (arriver) trace_at(ft, 128 + 4 * j);
       if (ok) ok = mbar_wait(&s_full[sb], (j >> 1) & 1u, ab, 32);
+      if (arriver) trace_at(ft, 129 + 4 * j);
       if (j == 0 && ok) {  // S_0 complete: the q tile has landed in both CTAs
         const uint32_t qa = smem_u32(smem + L.off_q);
         float qn2 = 0.f;
@@ -429,10 +494,12 @@ __global__ void __launch_bounds__(kThreads, 1) route_bwd_kernel(const __grid_con
         }
         fence_proxy_async();
       }
+      if (arriver) trace_at(ft, 130 + 4 * j);
       tc_fence_before();
       named_bar_sync(1, 128);
       if (arriver) mbar_arrive_cluster(pf_leader + sb * 8);
     }
+    if (arriver) trace_time(p.trace, 3);
     if (p.dbeta) {
       for (int o = 16; o; o >>= 1) dbeta += __shfl_xor_sync(0xffffffffu, dbeta, o);
       if (lane == 0 && ok) atomicAdd(p.dbeta, dbeta);
@@ -440,6 +507,7 @@ __global__ void __launch_bounds__(kThreads, 1) route_bwd_kernel(const __grid_con
 
     // ---- epilogue: dq = u - q_hat <q_hat, u>   (u = invn * dq_hat, folded TMEM)
     if (ok) ok = mbar_wait(&o_full, 0, ab, 34);
+    if (arriver) trace_time(p.trace, 4);
     ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
     const uint32_t qa = smem_u32(smem + L.off_q);
@@ -499,6 +567,7 @@ __global__ void __launch_bounds__(kThreads, 1) route_bwd_kernel(const __grid_con
   __syncthreads();
   cluster_sync();
   if (warp == 1) tmem_dealloc<2>(tmem, L.tmem_cols);
+  if (threadIdx.x == 0) trace_time(p.trace, 5);
 }
 
 template <typename T>
@@ -513,6 +582,13 @@ int launch(const RouteBwdArgs& a, cudaStream_t st) {
   if (rc) return rc;
   rc = make_tmap_2d(&tdv, a.dv_t, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.R, a.M, (uint64_t)a.R * 2, 64, 64);
   if (rc) return rc;
+  CUtensorMap tz = tq, tdz = tq;  // z and dz rows [groups * rows, R] (used for R <= 256)
+  if (a.R <= 256) {
+    rc = make_tmap_2d(&tz, a.z, qdt, 2, a.R, (uint64_t)a.groups * a.rows, (uint64_t)a.R * 2, 64, 64);
+    if (rc) return rc;
+    rc = make_tmap_2d(&tdz, a.dz, qdt, 2, a.R, (uint64_t)a.groups * a.rows, (uint64_t)a.R * 2, 64, 64);
+    if (rc) return rc;
+  }
   Params p;
   p.rows = a.rows;
   p.q_row_stride = a.q_row_stride;
@@ -534,12 +610,13 @@ int launch(const RouteBwdArgs& a, cudaStream_t st) {
   p.g_out = static_cast<__nv_bfloat16*>(a.g_out);
   p.dbeta = a.dbeta;
   p.status = a.status;
+  p.trace = debug_trace();
   auto kern = route_bwd_kernel<T>;
   const int smem = (L.smem < 120 * 1024 ? 120 * 1024 : L.smem) + 1024;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return record_cuda_error();
   const long pairs = (long)a.groups * ((a.rows + 127) / 128);
-  return launch_kernel(kern, dim3((unsigned)(2 * pairs), 1, 1), dim3(kThreads, 1, 1), smem, st, true, tq, tdk, tdv, p);
+  return launch_kernel(kern, dim3((unsigned)(2 * pairs), 1, 1), dim3(kThreads, 1, 1), smem, st, true, tq, tdk, tdv, tz, tdz, p);
 }
 
 }  // namespace bwd
