@@ -81,6 +81,7 @@ struct FwdParams {
   int repair_cap;
   int* status;
   int* trace;           // optional progress markers (debug)
+  int compact;          // wide kernel: the two-CTAs-per-SM layout (see wide_layout)
 };
 
 // Exact fp32 recomputation of `count` listed rows (global indices g * rows + row) by one CTA (rare path).
@@ -549,7 +550,10 @@ constexpr int kWideMaxK = 8, kWideMaxV = 4, kWideMaxSB = 4, kWideMaxPB = 2;
 constexpr int kWideThreads = 224;  // warp0 keys, warp1 MMA, warps2-5 softmax/epilogue, warp6 values
 constexpr int kValueWarp = 6;
 
-__host__ __device__ inline WideLayout wide_layout(int R, int M) {
+// compact: a layout two CTAs of which fit one SM (<= 256 TMEM columns, ~108 KB of shared memory),
+// so that one pair's serial chain (setup, scores, softmax, epilogue) overlaps another's when there
+// are more pairs than SMs; 128-atom tiles and shorter rings.
+__host__ __device__ inline WideLayout wide_layout(int R, int M, bool compact = false) {
   WideLayout L;
   L.kchunks = R / 64;
   L.nc = R < 256 ? R : 256;
@@ -557,9 +561,9 @@ __host__ __device__ inline WideLayout wide_layout(int R, int M) {
   L.q_bytes = 64 * R * 2;
   L.v_stage = (R / 2) * 128;  // this CTA's R/2 value rows x 64 atoms
   const int red = 2 * 128 * 4;
-  const int avail = 225 * 1024;
+  const int avail = compact ? 108 * 1024 : 225 * 1024;
   L.nk = 0;
-  for (int nk = (M % 256 == 0) ? 256 : 128; nk >= 128 && L.nk == 0; nk -= 128) {
+  for (int nk = (M % 256 == 0 && !compact) ? 256 : 128; nk >= 128 && L.nk == 0; nk -= 128) {
     if (M % nk) continue;
     for (int npb = 2; npb >= 1 && L.nk == 0; --npb) {
       const int k_stage = (nk / 2) * 128, p_bytes = 64 * nk * 2;
@@ -582,7 +586,7 @@ __host__ __device__ inline WideLayout wide_layout(int R, int M) {
   }
   L.s_cols = L.nk / 2;
   L.tmem_s = R / 2;
-  const int nsb = (512 - R / 2) / L.s_cols;
+  const int nsb = ((compact ? 256 : 512) - R / 2) / L.s_cols;
   L.nsb = nsb > kWideMaxSB ? kWideMaxSB : nsb;
   L.off_q = 0;
   L.off_k = L.off_q + L.q_bytes;
@@ -590,14 +594,14 @@ __host__ __device__ inline WideLayout wide_layout(int R, int M) {
   L.off_p = L.off_v + L.nvs * L.v_stage;
   L.off_red = L.off_p + L.npb * L.p_bytes;
   const int used = L.off_red + red;
-  L.smem = used < 120 * 1024 ? 120 * 1024 : used;  // one CTA per SM
+  L.smem = (used < 120 * 1024 && !compact) ? 120 * 1024 : used;  // one CTA per SM unless compact
   const int cols = R / 2 + L.nsb * L.s_cols;
   L.tmem_cols = cols <= 128 ? 128 : (cols <= 256 ? 256 : 512);
   return L;
 }
 
-template <int kR, typename T>
-__global__ void __launch_bounds__(kWideThreads, 1) route_fwd_wide_kernel(const __grid_constant__ CUtensorMap tq,
+template <int kR, typename T, int kMinBlocks>
+__global__ void __launch_bounds__(kWideThreads, kMinBlocks) route_fwd_wide_kernel(const __grid_constant__ CUtensorMap tq,
                                                                 const __grid_constant__ CUtensorMap tdk,
                                                                 const __grid_constant__ CUtensorMap tdv,
                                                                 const FwdParams p) {
@@ -610,7 +614,7 @@ __global__ void __launch_bounds__(kWideThreads, 1) route_fwd_wide_kernel(const _
   __shared__ int abort_flag, n_listed;
   __shared__ int listed[64];  // this CTA's rows whose mass fell below the fixed offset's range
 
-  const WideLayout L = wide_layout(kR, p.M);
+  const WideLayout L = wide_layout(kR, p.M, p.compact != 0);
   constexpr int kRows = 64;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const uint32_t rank = cluster_ctarank() & 1u;
@@ -963,7 +967,13 @@ int launch_fwd(const RouteFwdArgs& a, cudaStream_t st) {
   p.repair_cap = a.repair_cap;
   p.status = a.status;
   p.trace = debug_trace();
-  const WideLayout W = wide_layout(kR, (int)a.M);
+  const long pairs = (long)a.groups * ((a.rows + 127) / 128);
+  // two CTAs per SM when every SM gets several pairs and the compact layout exists for this shape
+  const WideLayout Wc = wide_layout(kR, (int)a.M, true);
+  const bool compact = kR >= 128 && kR <= 256 && pairs >= sm_count() && Wc.nk != 0 && Wc.nks >= 3 && Wc.nsb >= 2 &&
+                       Wc.tmem_cols <= 256;
+  p.compact = compact ? 1 : 0;
+  const WideLayout W = compact ? Wc : wide_layout(kR, (int)a.M);
   const bool wide = kR >= 128 && W.nk != 0 && W.nks >= 3 && W.nsb >= 2;
   if (wide) {  // re-encode the key / value maps with the wide tile's boxes
     rc = make_tmap_2d(&tdk, a.dk_t, qdt, 2, kR, a.M, (uint64_t)kR * 2, 64, W.nk / 2);
@@ -972,11 +982,11 @@ int launch_fwd(const RouteFwdArgs& a, cudaStream_t st) {
     if (rc) return rc;
     if ((a.M + kR + 64) * 4 > W.smem) return DA_ERR_SHAPE;  // repair scratch must fit
   }
-  auto kern = wide ? route_fwd_wide_kernel<kR, T> : route_fwd_kernel<kR, T>;
+  auto kern = !wide ? route_fwd_kernel<kR, T>
+                    : (compact ? route_fwd_wide_kernel<kR, T, 2> : route_fwd_wide_kernel<kR, T, 1>);
   const int smem = (wide ? W.smem : C::kSmem) + 1024;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return record_cuda_error();
-  const long pairs = (long)a.groups * ((a.rows + 127) / 128);
   return launch_kernel(kern, dim3((unsigned)(2 * pairs), 1, 1), dim3(wide ? kWideThreads : C::kThreads, 1, 1), smem, st, true, tq, tdk, tdv, p);
 }
 

@@ -43,6 +43,8 @@ def _inputs(rows: int, r: int, m: int, dtype: torch.dtype, seed: int, scale: flo
         (300, 128, 512, 4.0),       # qk4-s4 width, ragged tail tile
         (1000, 512, 1536, 4.0 * 2**0.5),  # a1-r512-d1536
         (102, 64, 128, 4.0),        # reference parity-suite width
+        (20000, 256, 512, 4.0),     # more pairs than SMs: two CTAs per SM (compact layout), ragged
+        (19500, 128, 512, 4.0),     # the same at the qk4-s4 width
     ],
 )
 def test_route_forward_matches_oracle(rows: int, r: int, m: int, beta: float, dtype: torch.dtype) -> None:
@@ -101,14 +103,15 @@ def test_route_unnormalized_input_and_output_flags() -> None:
         assert _cos(got, expected) >= MIN_COS, (nin, nout)
 
 
-def test_route_low_mass_rows_are_repaired() -> None:
+@pytest.mark.parametrize("rows", [512, 20000])  # one CTA per SM, and two (compact layout)
+def test_route_low_mass_rows_are_repaired(rows: int) -> None:
     """A huge temperature with unnormalised inputs drives the fixed softmax
     offset far above the true row maximum; those rows must come back exact."""
     dev = torch.device("cuda")
-    x, dk, dv = _inputs(512, 128, 512, torch.bfloat16, seed=5, scale=3.0)
+    x, dk, dv = _inputs(rows, 128, 512, torch.bfloat16, seed=5, scale=3.0)
     beta = 60.0
     views = ops.dictionary_views_from_normalized(dk.to(dev), dv.to(dev), torch.bfloat16)
-    z, lse, _ = ops._route_forward(x.to(dev), 512, 1, 128, views, torch.tensor(beta, device=dev), 1e-6, False, True)
+    z, lse, _ = ops._route_forward(x.to(dev), rows, 1, 128, views, torch.tensor(beta, device=dev), 1e-6, False, True)
     torch.cuda.synchronize()
     assert ops.device_status(dev) == 0
     expected = oracle.dictionary_route(x.float(), dk.float(), dv.to(torch.bfloat16).float(), beta,
