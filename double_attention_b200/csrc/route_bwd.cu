@@ -64,37 +64,42 @@ struct Params {
   float* dbeta;            // accumulated (may be null)
   int* status;
   int* trace;              // optional progress stamps (debug)
+  int compact;             // the two-CTAs-per-SM layout (make_layout)
 };
 
 struct Layout {
   int rchunks, ncol, nins, nst, smem;
+  int nb;  // score / dP / dL' tile buffers (2; 1 in the compact layout)
   int off_q, off_g, off_dl, off_red, off_ring;
   int tmem_u, tmem_s, tmem_p, tmem_cols;
 };
 
-__host__ __device__ inline Layout make_layout(int R) {
+// compact: single-buffered tiles so that two CTAs fit one SM (<= 256 TMEM columns, ~100 KB of shared
+// memory, R <= 128); the other CTA's work then overlaps what double buffering used to.
+__host__ __device__ inline Layout make_layout(int R, bool compact = false) {
   Layout L;
+  L.nb = compact ? 1 : 2;
   L.rchunks = (R + 127) / 128;     // 128-column K chunks of the score / dP products
   L.ncol = R < 256 ? R : 256;      // N of one u instruction
   L.nins = R / L.ncol;
   L.off_q = 0;
   L.off_g = L.off_q + kRows * R * 2;
   L.off_dl = L.off_g + kRows * R * 2;
-  L.off_red = L.off_dl + 2 * kRows * kNA * 2;
+  L.off_red = L.off_dl + L.nb * kRows * kNA * 2;
   L.off_ring = L.off_red + 2048;
-  const int avail = 225 * 1024 - L.off_ring;
+  const int avail = (compact ? 108 * 1024 : 225 * 1024) - L.off_ring;
   L.nst = avail / kStage > kMaxStages ? kMaxStages : avail / kStage;
   L.smem = L.off_ring + L.nst * kStage;
   L.tmem_u = 0;
   L.tmem_s = R / 2;
-  L.tmem_p = L.tmem_s + 2 * (kNA / 2);
-  const int cols = L.tmem_p + 2 * (kNA / 2);
+  L.tmem_p = L.tmem_s + L.nb * (kNA / 2);
+  const int cols = L.tmem_p + L.nb * (kNA / 2);
   L.tmem_cols = cols <= 256 ? 256 : 512;
   return L;
 }
 
-template <typename T>
-__global__ void __launch_bounds__(kThreads, 1) route_bwd_kernel(const __grid_constant__ CUtensorMap tq,
+template <typename T, int kMinBlocks>
+__global__ void __launch_bounds__(kThreads, kMinBlocks) route_bwd_kernel(const __grid_constant__ CUtensorMap tq,
                                                                 const __grid_constant__ CUtensorMap tdk,
                                                                 const __grid_constant__ CUtensorMap tdv,
                                                                 const __grid_constant__ CUtensorMap tz,
@@ -109,7 +114,8 @@ __global__ void __launch_bounds__(kThreads, 1) route_bwd_kernel(const __grid_con
 
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   const int R = p.R;
-  const Layout L = make_layout(R);
+  const Layout L = make_layout(R, p.compact != 0);
+  const int nb = L.nb;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const uint32_t rank = cluster_ctarank() & 1u;
   const int tiles_per_group = (int)((p.rows + 127) / 128);
@@ -119,7 +125,7 @@ __global__ void __launch_bounds__(kThreads, 1) route_bwd_kernel(const __grid_con
   const int NJ = p.M / kNA;
   // R <= 256: this CTA's z rows land in the (not yet used) dL' buffer and its dz rows in the g
   // buffer by TMA, so the output-normalisation backward reads both from shared memory once
-  const bool zd_tma = R <= 256;
+  const bool zd_tma = R <= 128 * L.nb;  // z fills the dL' buffers
   Abort ab{&abort_flag, p.status};
   // debug trace: 8 phase stamps per CTA, then per-tile stamps of the first pair
   int* ft = (p.trace && blockIdx.x < 2) ? p.trace + gridDim.x * 8 + blockIdx.x * 256 : nullptr;
@@ -241,9 +247,9 @@ __global__ void __launch_bounds__(kThreads, 1) route_bwd_kernel(const __grid_con
     const uint32_t qa = smem_u32(smem + L.off_q), ga = smem_u32(smem + L.off_g);
     bool g_ready = false;
     auto issue_sdp = [&](int j) -> bool {
-      const int sb = j & 1;
+      const int sb = j % nb;
       trace_at(ft, 16 + 4 * j);
-      if (j >= 2 && !mbar_wait(&p_full[sb], ((j - 2) >> 1) & 1u, ab, 22)) return false;
+      if (j >= nb && !mbar_wait(&p_full[sb], ((j - nb) / nb) & 1u, ab, 22)) return false;
       trace_at(ft, 17 + 4 * j);
       for (int pass = 0; pass < 2; ++pass) {
         if (pass == 1 && !g_ready) {
@@ -271,8 +277,8 @@ __global__ void __launch_bounds__(kThreads, 1) route_bwd_kernel(const __grid_con
       return true;
     };
     auto issue_u = [&](int j) -> bool {
-      const int sb = j & 1;
-      if (!mbar_wait(&p_full[sb], (j >> 1) & 1u, ab, 24)) return false;
+      const int sb = j % nb;
+      if (!mbar_wait(&p_full[sb], (j / nb) & 1u, ab, 24)) return false;
       trace_at(ft, 19 + 4 * j);
       tc_fence_after();
       const uint32_t dla = smem_u32(smem + L.off_dl + sb * (kRows * kNA * 2));
@@ -430,9 +436,9 @@ __global__ void __launch_bounds__(kThreads, 1) route_bwd_kernel(const __grid_con
     T* dl_row = reinterpret_cast<T*>(p.dl_out) + idx * p.M;
     __nv_bfloat16* p_row = p.p_out + idx * p.M;
     for (int j = 0; j < NJ; ++j) {
-      const int sb = j & 1;
+      const int sb = j % nb;
       if (arriver) trace_at(ft, 128 + 4 * j);
-      if (ok) ok = mbar_wait(&s_full[sb], (j >> 1) & 1u, ab, 32);
+      if (ok) ok = mbar_wait(&s_full[sb], (j / nb) & 1u, ab, 32);
       if (arriver) trace_at(ft, 129 + 4 * j);
       if (j == 0 && ok) {  // S_0 complete: the q tile has landed in both CTAs
         const uint32_t qa = smem_u32(smem + L.off_q);
@@ -451,7 +457,7 @@ __global__ void __launch_bounds__(kThreads, 1) route_bwd_kernel(const __grid_con
         qn = sqrtf(qn2);
         invn = p.normalize_input ? 1.f / fmaxf(qn, p.eps) : 1.f;
       }
-      if (ok && j >= 2) ok = mbar_wait(&dl_empty[sb], ((j - 2) >> 1) & 1u, ab, 33);
+      if (ok && j >= nb) ok = mbar_wait(&dl_empty[sb], ((j - nb) / nb) & 1u, ab, 33);
       ok = __all_sync(0xffffffffu, ok);
       if (ok) {
         tc_fence_after();
@@ -572,7 +578,9 @@ __global__ void __launch_bounds__(kThreads, 1) route_bwd_kernel(const __grid_con
 
 template <typename T>
 int launch(const RouteBwdArgs& a, cudaStream_t st) {
-  const Layout L = make_layout((int)a.R);
+  const long pairs = (long)a.groups * ((a.rows + 127) / 128);
+  const bool compact = a.R <= 128 && pairs >= sm_count() && make_layout((int)a.R, true).nst >= 3;
+  const Layout L = make_layout((int)a.R, compact);
   const CUtensorMapDataType qdt =
       std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap tq, tdk, tdv;
@@ -611,11 +619,11 @@ int launch(const RouteBwdArgs& a, cudaStream_t st) {
   p.dbeta = a.dbeta;
   p.status = a.status;
   p.trace = debug_trace();
-  auto kern = route_bwd_kernel<T>;
-  const int smem = (L.smem < 120 * 1024 ? 120 * 1024 : L.smem) + 1024;
+  p.compact = compact ? 1 : 0;
+  auto kern = compact ? route_bwd_kernel<T, 2> : route_bwd_kernel<T, 1>;
+  const int smem = ((L.smem < 120 * 1024 && !compact) ? 120 * 1024 : L.smem) + 1024;  // one CTA per SM unless compact
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return record_cuda_error();
-  const long pairs = (long)a.groups * ((a.rows + 127) / 128);
   return launch_kernel(kern, dim3((unsigned)(2 * pairs), 1, 1), dim3(kThreads, 1, 1), smem, st, true, tq, tdk, tdv, tz, tdz, p);
 }
 

@@ -43,6 +43,7 @@ def _close(name: str, got: torch.Tensor, ref: torch.Tensor, rel: float = 2e-2, m
         (1000, 512, 1536, 4.0 * 2**0.5, True, True),  # a1-r512-d1536
         (513, 128, 512, 4.0, False, True),          # unnormalised input
         (256, 256, 512, 4.0, True, False),          # unnormalised output
+        (20000, 128, 512, 4.0, True, True),         # more pairs than SMs: two CTAs per SM (compact)
     ],
 )
 def test_route_backward_matches_oracle(rows, r, m, beta, ni, no, dtype) -> None:
