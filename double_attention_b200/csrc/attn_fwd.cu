@@ -32,10 +32,13 @@
 namespace da {
 namespace attn {
 
-// warp0 keys (TMA), warp1 MMA, warps2-5 softmax/epilogue, warp6 values (TMA): the issues of one warp
-// are serialised, so the two operand streams come from two warps.
-constexpr int kThreads = 224;
+// warp0 keys (TMA), warp1 score MMAs, warps2-5 softmax/epilogue, warp6 values (TMA), warp7 P.V MMAs.
+// The issues of one warp are serialised, so the two operand streams come from two warps; the score
+// and P.V products have their own issuing threads, so a P.V product never queues behind the key
+// chunks of a score tile further ahead (and the reverse).
+constexpr int kThreads = 256;
 constexpr int kValueWarp = 6;
+constexpr int kPvWarp = 7;
 constexpr int kRows = 64;       // query rows per CTA
 constexpr int kMaxK = 8, kMaxV = 4, kMaxSB = 4, kMaxPB = 2;
 
@@ -47,6 +50,7 @@ constexpr int kMaxK = 8, kMaxV = 4, kMaxSB = 4, kMaxPB = 2;
 // memory and 512 TMEM columns.
 struct Layout {
   int kw, nk, kchunks, rpb;
+  int kbb, kslots;  // key chunks per TMA box (one issue), ring slots of kbb chunks
   int nc, npv, per;
   int q_bytes, k_stage, v_stage, p_bytes;
   int nks, nvs, nsb, npb;
@@ -100,6 +104,15 @@ __host__ __device__ inline Layout make_layout(int maps, int group, int R, int D,
       L.nks = nks > kMaxK ? kMaxK : nks;
     }
   }
+  // Each TMA issue costs about the same whatever its size, so key chunks of the same rows are
+  // fetched several column blocks per box while the ring keeps at least three boxes in flight.
+  L.kbb = 1;
+  for (int b = 4; b >= 2; b /= 2)
+    if (L.rpb % b == 0 && L.nks / b >= 3) {
+      L.kbb = b;
+      break;
+    }
+  L.kslots = L.nks / L.kbb;
   L.s_cols = L.nk / 2;
   L.tmem_s = D / 2;
   const int nsb = (512 - D / 2) / L.s_cols;
@@ -141,7 +154,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ uint64_t q_full, o_full;
   __shared__ uint64_t k_full[kMaxK], k_empty[kMaxK], v_full[kMaxV], v_empty[kMaxV];
-  __shared__ uint64_t s_full[kMaxSB], p_full[kMaxSB], p_empty[kMaxPB];
+  __shared__ uint64_t s_full[kMaxSB], p_full[kMaxSB], p_empty[kMaxPB], pv_full[kMaxPB];
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
 
@@ -158,6 +171,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   const int nk_all = (p.T + nk - 1) / nk;
   const int nj = p.causal ? min(nk_all, (t0 + 127) / nk + 1) : nk_all;
   const int maps = kMix ? p.maps : 1;
+  // Key tiles are visited from a per-pair starting tile (any order gives the same sums: the softmax
+  // offset is fixed), so the pairs of one sequence that run side by side read different key and
+  // value lines instead of all requesting the same ones at once.
+  const int rot = (blockIdx.x / 2) % nj;
   const int sweep_units = nj * maps;
   const int U = kMix ? 2 * sweep_units : sweep_units;  // S units: (sweep, key tile, map)
   const int u2 = kMix ? sweep_units : 0;               // first unit of the P.V sweep
@@ -181,7 +198,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 2);
     }
-    for (int i = 0; i < kMaxPB; ++i) mbar_init(&p_empty[i], 1);
+    for (int i = 0; i < kMaxPB; ++i) {
+      mbar_init(&p_empty[i], 1);
+      mbar_init(&pv_full[i], 2);  // a probability tile is complete in both CTAs
+    }
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -210,25 +230,26 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
           for (int kb = 0; kb < L.rpb; ++kb)
             tma_load_2d_pair(&tq, qf, smem + L.off_q + ((s * p.group + gi) * L.rpb + kb) * (kRows * 128), kb * 64, y);
         }
-      int kc = 0;
+      int kx = 0;  // key boxes issued
+      const int box_bytes = L.kbb * L.k_stage;
       for (int u = 0; u < U; ++u) {
         const int rem = u % sweep_units, j = rem / maps, s = rem % maps;
         bool ok = true;
-        for (int c = 0; c < L.kchunks; ++c, ++kc) {
-          const int st = kc % L.nks;
-          if (!mbar_wait(&k_empty[st], ((kc / L.nks) & 1u) ^ 1u, ab, 11)) { ok = false; break; }
-          if (rank == 0) mbar_arrive_expect_tx(&k_full[st], 2 * L.k_stage);
-          const int gi = c / L.rpb, kb = c % L.rpb;
-          const int64_t row = p.k_base + b * p.k_sb + (p.branch0[s] + gi) * p.k_sbr + j * nk + (int)rank * (nk / 2);
-          tma_load_2d_pair(&tk, mapa_shared(smem_u32(&k_full[st]), 0), smem + L.off_k + st * L.k_stage, kb * 64,
-                           (int)min(row, p.k_rows - 1));
+        for (int c = 0; c < L.kchunks; c += L.kbb, ++kx) {
+          const int st = kx % L.kslots;
+          if (!mbar_wait(&k_empty[st], ((kx / L.kslots) & 1u) ^ 1u, ab, 11)) { ok = false; break; }
+          if (rank == 0) mbar_arrive_expect_tx(&k_full[st], 2 * box_bytes);
+          const int gi = c / L.rpb, kb = c % L.rpb;  // kbb divides rpb: a box never spans two branches
+          const int64_t row = p.k_base + b * p.k_sb + (p.branch0[s] + gi) * p.k_sbr + ((j + rot) % nj) * nk + (int)rank * (nk / 2);
+          tma_load_3d_pair(&tk, mapa_shared(smem_u32(&k_full[st]), 0), smem + L.off_k + st * box_bytes, 0,
+                           (int)min(row, p.k_rows - 1), kb);
         }
         if (!ok) break;
       }
       if (rank == 0) {  // drain: no TMA may be in flight at teardown
         mbar_wait_drain(&q_full, 0);
-        for (int c = (kc > L.nks ? kc - L.nks : 0); c < kc; ++c)
-          mbar_wait_drain(&k_full[c % L.nks], (c / L.nks) & 1u);
+        for (int c = (kx > L.kslots ? kx - L.kslots : 0); c < kx; ++c)
+          mbar_wait_drain(&k_full[c % L.kslots], (c / L.kslots) & 1u);
       }
     }
   } else if (warp == kValueWarp) {
@@ -243,11 +264,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
           if (!mbar_wait(&v_empty[st], ((vc / L.nvs) & 1u) ^ 1u, ab, 12)) { ok = false; break; }
           if (rank == 0) mbar_arrive_expect_tx(&v_full[st], 2 * L.v_stage);
           const uint32_t vf = mapa_shared(smem_u32(&v_full[st]), 0);
-          const int y = (int)min((int64_t)b * p.T + v * nk + c * 64, vrows - 1);
-          for (int i = 0; i < L.npv; ++i)
-            for (int bx = 0; bx < L.per; ++bx)
-              tma_load_2d_pair(&tv, vf, smem + L.off_v + st * L.v_stage + (i * L.per + bx) * (64 * 128),
-                               dcol0 + i * L.nc + (int)rank * (L.nc / 2) + bx * 64, y);
+          const int y = (int)min((int64_t)b * p.T + ((v + rot) % nj) * nk + c * 64, vrows - 1);
+          // one box: 64 keys x this CTA's per column blocks of each of the npv value groups
+          tma_load_4d_pair(&tv, vf, smem + L.off_v + st * L.v_stage, 0, y, (int)rank * L.per, dcol0 / L.nc);
         }
         if (!ok) break;
       }
@@ -255,8 +274,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         for (int c = (vc > L.nvs ? vc - L.nvs : 0); c < vc; ++c)
           mbar_wait_drain(&v_full[c % L.nvs], (c / L.nvs) & 1u);
     }
-  } else if (warp == 1) {
-    // ---------------------------------------------------------------- MMA issuer (leader)
+  } else if (warp == 1 || warp == kPvWarp) {
+    // ---------------------------------------------------------------- MMA issuers (leader): scores on warp 1,
+    // P.V on warp 7
     if (rank == 0 && lane == 0) {
       const uint32_t idesc_s = idesc_f16(128, nk, std::is_same<T, __nv_bfloat16>::value, false, false);
       const uint32_t idesc_o = idesc_f16(128, L.nc, true, false, true);  // B = V, MN-major
@@ -265,70 +285,75 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         mma_commit<2>(mapa_shared(smem_u32(bar), 1));
       };
       const uint32_t qa = smem_u32(smem + L.off_q);
-      int kc = 0, vc = 0;
-      auto issue_s = [&](int u) -> bool {
-        const int sb = u % L.nsb;
-        const int s = (u % sweep_units) % maps;
-        if (u < 256) trace_at(ft, 1024 + 4 * u);
-        if (u >= L.nsb && !mbar_wait(&p_full[sb], ((u - L.nsb) / L.nsb) & 1u, ab, 22)) return false;
-        if (u < 256) trace_at(ft, 1025 + 4 * u);
-        const uint32_t d = tmem + L.tmem_s + (uint32_t)(sb * L.s_cols);
-        for (int c = 0; c < L.kchunks; ++c, ++kc) {
-          const int st = kc % L.nks;
-          if (!mbar_wait(&k_full[st], (kc / L.nks) & 1u, ab, 23)) return false;
-          tc_fence_after();
-          const uint64_t ad0 = sdesc_sw128(qa + (s * L.kchunks + c) * (kRows * 128), 16, 1024);
-          const uint64_t bd0 = sdesc_sw128(smem_u32(smem + L.off_k + st * L.k_stage), 16, 1024);
-#pragma unroll
-          for (int kin = 0; kin < 4; ++kin)  // +32 B per K step of 16 = +2 in the encoded address
-            mma_f16_ss<2>(d, ad0 + 2 * kin, bd0 + 2 * kin, idesc_s, (c | kin) ? 1u : 0u);
-          commit_both(&k_empty[st]);
-        }
-        commit_both(&s_full[sb]);
-        if (u < 256) trace_at(ft, 1026 + 4 * u);
-        return true;
-      };
-      auto issue_pv = [&](int v) -> bool {
-        const int ulast = u2 + v * maps + maps - 1;
-        const int pb = v % L.npb;
-        if (v < 256) trace_at(ft, 2048 + 4 * v);
-        if (!mbar_wait(&p_full[ulast % L.nsb], (ulast / L.nsb) & 1u, ab, 24)) return false;
-        if (v < 256) trace_at(ft, 2049 + 4 * v);
-        const uint32_t pa = smem_u32(smem + L.off_p + pb * L.p_bytes);
-        for (int c = 0; c < nk / 64; ++c, ++vc) {
-          const int st = vc % L.nvs;
-          if (!mbar_wait(&v_full[st], (vc / L.nvs) & 1u, ab, 25)) return false;
-          tc_fence_after();
-          const uint32_t va = smem_u32(smem + L.off_v + st * L.v_stage);
-          for (int i = 0; i < L.npv; ++i) {
-            // MN-major V: rows are keys (K), 128 B = 64 value columns (N);
-            // LBO = distance between 64-column boxes, SBO = 8 key rows.
-            const uint64_t bd0 = sdesc_sw128(va + i * L.per * (64 * 128), 64 * 128, 1024);
-            const uint64_t ad0 = sdesc_sw128(pa + c * (kRows * 128), 16, 1024);
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)  // K step of 16 keys: A +32 B (+2), B +16 rows x 128 B (+128)
-              mma_f16_ss<2>(tmem + (uint32_t)(i * (L.nc / 2)), ad0 + 2 * kk, bd0 + 128 * kk, idesc_o,
-                            (v | c | kk) ? 1u : 0u);
-          }
-          commit_both(&v_empty[st]);
-        }
-        commit_both(&p_empty[pb]);
-        if (v < 256) trace_at(ft, 2050 + 4 * v);
-        return true;
-      };
-      trace_at(ft, 0);
+      if (warp == 1) trace_at(ft, 0);
       bool ok = mbar_wait(&q_full, 0, ab, 21);
-      trace_at(ft, 1);
+      if (warp == 1) trace_at(ft, 1);
       tc_fence_after();
-      // Scores run up to nsb units ahead of the probability products.
-      int next_u = 0;
-      for (int v = 0; ok && v < nj; ++v) {
-        const int ulast = u2 + v * maps + maps - 1;
-        while (ok && next_u < U && next_u < ulast + L.nsb) ok = issue_s(next_u++);
-        if (ok) ok = issue_pv(v);
+      if (warp == 1) {
+        // S units in order; a score buffer is reused once the softmax has consumed its previous unit.
+        int kx = 0, st = 0;  // key boxes consumed, current slot
+        for (int u = 0; ok && u < U; ++u) {
+          const int sb = u % L.nsb;
+          const int s = (u % sweep_units) % maps;
+          if (u < 256) trace_at(ft, 1024 + 4 * u);
+          if (u >= L.nsb && !mbar_wait(&p_full[sb], ((u - L.nsb) / L.nsb) & 1u, ab, 22)) { ok = false; break; }
+          if (u < 256) trace_at(ft, 1025 + 4 * u);
+          const uint32_t d = tmem + L.tmem_s + (uint32_t)(sb * L.s_cols);
+          for (int c = 0; ok && c < L.kchunks; ++c) {
+            const int cib = c % L.kbb;  // chunk inside the current box
+            if (cib == 0) {
+              st = kx % L.kslots;
+              if (!mbar_wait(&k_full[st], (kx / L.kslots) & 1u, ab, 23)) { ok = false; break; }
+              tc_fence_after();
+            }
+            const uint64_t ad0 = sdesc_sw128(qa + (s * L.kchunks + c) * (kRows * 128), 16, 1024);
+            const uint64_t bd0 =
+                sdesc_sw128(smem_u32(smem + L.off_k + (st * L.kbb + cib) * L.k_stage), 16, 1024);
+#pragma unroll
+            for (int kin = 0; kin < 4; ++kin)  // +32 B per K step of 16 = +2 in the encoded address
+              mma_f16_ss<2>(d, ad0 + 2 * kin, bd0 + 2 * kin, idesc_s, (c | kin) ? 1u : 0u);
+            if (cib == L.kbb - 1) {
+              commit_both(&k_empty[st]);
+              ++kx;
+            }
+          }
+          if (!ok) break;
+          commit_both(&s_full[sb]);
+          if (u < 256) trace_at(ft, 1026 + 4 * u);
+        }
+      } else {
+        // P.V per key tile, as soon as its probability tile and value rows are in shared memory.
+        int vc = 0;
+        for (int v = 0; ok && v < nj; ++v) {
+          const int pb = v % L.npb;
+          if (v < 256) trace_at(ft, 2048 + 4 * v);
+          if (!mbar_wait(&pv_full[pb], (v / L.npb) & 1u, ab, 24)) { ok = false; break; }
+          if (v < 256) trace_at(ft, 2049 + 4 * v);
+          const uint32_t pa = smem_u32(smem + L.off_p + pb * L.p_bytes);
+          for (int c = 0; ok && c < nk / 64; ++c, ++vc) {
+            const int st = vc % L.nvs;
+            if (!mbar_wait(&v_full[st], (vc / L.nvs) & 1u, ab, 25)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t va = smem_u32(smem + L.off_v + st * L.v_stage);
+            for (int i = 0; i < L.npv; ++i) {
+              // MN-major V: rows are keys (K), 128 B = 64 value columns (N);
+              // LBO = distance between 64-column boxes, SBO = 8 key rows.
+              const uint64_t bd0 = sdesc_sw128(va + i * L.per * (64 * 128), 64 * 128, 1024);
+              const uint64_t ad0 = sdesc_sw128(pa + c * (kRows * 128), 16, 1024);
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk)  // K step of 16 keys: A +32 B (+2), B +16 rows x 128 B (+128)
+                mma_f16_ss<2>(tmem + (uint32_t)(i * (L.nc / 2)), ad0 + 2 * kk, bd0 + 128 * kk, idesc_o,
+                              (v | c | kk) ? 1u : 0u);
+            }
+            commit_both(&v_empty[st]);
+          }
+          if (!ok) break;
+          commit_both(&p_empty[pb]);
+          if (v < 256) trace_at(ft, 2050 + 4 * v);
+        }
+        commit_both(&o_full);
+        mbar_wait_drain(&o_full, 0);  // every P.V product (and so every score product) has completed
       }
-      commit_both(&o_full);
-      mbar_wait_drain(&o_full, 0);
     }
   } else {
     // ---------------------------------------------------------------- softmax + epilogue
@@ -379,12 +404,17 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       if (p.causal) lim = min(lim, t - k0 + 1);
       return max(0, min(32, lim));
     };
-    auto finish_unit = [&](int u, bool wrote_p) {
-      if (wrote_p) fence_proxy_async();
+    const uint32_t pv_leader = mapa_shared(smem_u32(&pv_full[0]), 0);
+    // pb >= 0: this unit completed probability tile buffer pb
+    auto finish_unit = [&](int u, int pb) {
+      if (pb >= 0) fence_proxy_async();
       tc_fence_before();
       if (arriver && u < 256) trace_at(ft, 3074 + 4 * u);
       named_bar_sync(1, 128);
-      if (arriver) mbar_arrive_cluster(pf_leader + (u % L.nsb) * 8);
+      if (arriver) {
+        mbar_arrive_cluster(pf_leader + (u % L.nsb) * 8);
+        if (pb >= 0) mbar_arrive_cluster(pv_leader + pb * 8);
+      }
       if (arriver && u < 256) trace_at(ft, 3075 + 4 * u);
     };
 
@@ -403,7 +433,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
             float v[32];
             tmem_ld32(tmem + lane_base + L.tmem_s + (uint32_t)(sb * L.s_cols + ch * 32), v);
             tmem_wait_ld();
-            const int lim = key_limit(j * nk + half * hc + ch * 32);
+            const int lim = key_limit(((j + rot) % nj) * nk + half * hc + ch * 32);
 #pragma unroll
             for (int i = 0; i < 32; ++i)
               if (i < lim) {
@@ -415,7 +445,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
           sum[s] += msum;
           mx[s] = fmaxf(mx[s], mmx);
         }
-        finish_unit(u, false);
+        finish_unit(u, -1);
       }
       for (int s = 0; s < maps; ++s) {
         red[s * 128 + l] = sum[s];
@@ -452,7 +482,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
             float sv[32];
             tmem_ld32(tmem + lane_base + L.tmem_s + (uint32_t)(sb * L.s_cols + ch * 32), sv);
             tmem_wait_ld();
-            const int k0 = v * nk + half * hc + ch * 32;
+            const int k0 = ((v + rot) % nj) * nk + half * hc + ch * 32;
             const int lim = key_limit(k0);
             if constexpr (kMix) {
 #pragma unroll
@@ -504,7 +534,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
             }
           }
         }
-        finish_unit(u, !kMix || s == maps - 1);
+        finish_unit(u, (!kMix || s == maps - 1) ? pb : -1);
       }
     }
 
@@ -582,11 +612,21 @@ int launch(const AttnFwdArgs& a, cudaStream_t st) {
   CUtensorMap tq, tk, tv;
   int rc = make_tmap_2d(&tq, a.q.ptr, qdt, 2, a.R, a.q.rows, (uint64_t)a.R * 2, 64, kRows);
   if (rc) return rc;
-  rc = make_tmap_2d(&tk, a.k.ptr, qdt, 2, a.R, a.k.rows, (uint64_t)a.R * 2, 64, L.nk / 2);
-  if (rc) return rc;
-  rc = make_tmap_2d(&tv, a.v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.D, (uint64_t)a.B * a.T, (uint64_t)a.D * 2, 64,
-                    64);
-  if (rc) return rc;
+  {  // keys: [rows, R] as (64-column block, row, block index); a box is nk/2 rows x kbb blocks
+    const uint64_t dims[3] = {64, (uint64_t)a.k.rows, (uint64_t)a.R / 64};
+    const uint64_t strides[2] = {(uint64_t)a.R * 2, 128};
+    const uint32_t box[3] = {64, (uint32_t)(L.nk / 2), (uint32_t)L.kbb};
+    rc = make_tmap_blocks(&tk, a.k.ptr, qdt, 2, 3, dims, strides, box);
+    if (rc) return rc;
+  }
+  {  // values: [B*T, D] as (64-column block, row, block inside an nc-wide group, group); a box is
+     // 64 keys x this CTA's nc/128 blocks of each of the npv groups of its value slice
+    const uint64_t dims[4] = {64, (uint64_t)a.B * a.T, (uint64_t)L.nc / 64, (uint64_t)a.D / L.nc};
+    const uint64_t strides[3] = {(uint64_t)a.D * 2, 128, (uint64_t)L.nc * 2};
+    const uint32_t box[4] = {64, 64, (uint32_t)L.per, (uint32_t)L.npv};
+    rc = make_tmap_blocks(&tv, a.v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 4, dims, strides, box);
+    if (rc) return rc;
+  }
   FwdParams p;
   p.q_rows = a.q.rows;
   p.q_base = a.q.base;

@@ -214,6 +214,21 @@ DA_DEV void tma_load_2d_pair(const void* tmap, uint32_t bar_cluster_addr, void* 
       :: "r"(smem_u32(dst)), "l"(tmap), "r"(bar_cluster_addr), "r"(x), "r"(y) : "memory");
 }
 
+// 3-D / 4-D tiled loads for a CTA pair (see tma_load_2d_pair): one issue
+// brings several 128-byte column blocks of the same rows (make_tmap_blocks).
+DA_DEV void tma_load_3d_pair(const void* tmap, uint32_t bar_cluster_addr, void* dst, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];"
+      :: "r"(smem_u32(dst)), "l"(tmap), "r"(bar_cluster_addr), "r"(x), "r"(y), "r"(z) : "memory");
+}
+DA_DEV void tma_load_4d_pair(const void* tmap, uint32_t bar_cluster_addr, void* dst, int x, int y, int z, int w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];"
+      :: "r"(smem_u32(dst)), "l"(tmap), "r"(bar_cluster_addr), "r"(x), "r"(y), "r"(z), "r"(w) : "memory");
+}
+
 // 2-D tiled store from shared memory (bulk-group completion).
 DA_DEV void tma_store_2d(const void* tmap, const void* src, int x, int y) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];"

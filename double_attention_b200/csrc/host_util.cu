@@ -57,6 +57,32 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, 
   return DA_OK;
 }
 
+int make_tmap_blocks(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes, int rank,
+                     const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return record_cuda_error_code(static_cast<int>(cudaErrorNotSupported));
+  if (rank < 3 || rank > 5) return DA_ERR_SHAPE;
+  if (reinterpret_cast<uintptr_t>(base) & 15) return DA_ERR_ALIGN;
+  if (dims[0] * static_cast<uint64_t>(elem_bytes) != 128 || box[0] != dims[0]) return DA_ERR_ALIGN;
+  cuuint64_t d[5], st[4];
+  cuuint32_t b[5], e[5];
+  for (int i = 0; i < rank; ++i) {
+    if (dims[i] == 0 || box[i] == 0 || box[i] > 256 || box[i] > dims[i]) return DA_ERR_SHAPE;
+    d[i] = dims[i];
+    b[i] = box[i];
+    e[i] = 1;
+  }
+  for (int i = 0; i < rank - 1; ++i) {
+    if (strides_bytes[i] & 15) return DA_ERR_ALIGN;
+    st[i] = strides_bytes[i];
+  }
+  CUresult r = fn(map, dtype, static_cast<cuuint32_t>(rank), const_cast<void*>(base), d, st, b, e,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return record_cuda_error_code(static_cast<int>(r));
+  return DA_OK;
+}
+
 int bind_device(const void* ptr) {
   // One device per host thread (one process per GPU; autograd keeps one
   // worker thread per device), so the binding is done once per thread.

@@ -547,8 +547,12 @@ struct WideLayout {
 };
 
 constexpr int kWideMaxK = 8, kWideMaxV = 4, kWideMaxSB = 4, kWideMaxPB = 2;
-constexpr int kWideThreads = 224;  // warp0 keys, warp1 MMA, warps2-5 softmax/epilogue, warp6 values
+// warp0 keys, warp1 score MMAs, warps2-5 softmax/epilogue, warp6 values, warp7 P.Dv^T MMAs: the two
+// products have their own issuing threads, so a P.Dv^T product never waits behind the key chunks of
+// a score tile further ahead (and the reverse).
+constexpr int kWideThreads = 256;
 constexpr int kValueWarp = 6;
+constexpr int kPvWarp = 7;
 
 // compact: a layout two CTAs of which fit one SM (<= 256 TMEM columns, ~108 KB of shared memory),
 // so that one pair's serial chain (setup, scores, softmax, epilogue) overlaps another's when there
@@ -627,6 +631,8 @@ __global__ void __launch_bounds__(kWideThreads, kMinBlocks) route_fwd_wide_kerne
   const int rot = pair % NJ;  // pairs start at different atom tiles
   Abort ab{&abort_flag, p.status};
   if (threadIdx.x == 0) trace_time(p.trace, 0);
+  // post-mortem per-tile timeline of the first pair (debug trace only): 4096 ints per CTA after the 8-int slots
+  int* ft = (p.trace && blockIdx.x < 2) ? p.trace + 8 * gridDim.x + blockIdx.x * 4096 : nullptr;
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
@@ -712,8 +718,9 @@ __global__ void __launch_bounds__(kWideThreads, kMinBlocks) route_fwd_wide_kerne
         for (int c = (vc > L.nvs ? vc - L.nvs : 0); c < vc; ++c)
           mbar_wait_drain(&v_full[c % L.nvs], (c / L.nvs) & 1u);
     }
-  } else if (warp == 1) {
-    // ---------------------------------------------------------------- MMA issuer (leader)
+  } else if (warp == 1 || warp == kPvWarp) {
+    // ---------------------------------------------------------------- MMA issuers (leader): scores on
+    // warp 1, probability products on warp 7
     if (rank == 0 && lane == 0) {
       const uint32_t idesc_s = idesc_f16(128, nk, std::is_same<T, __nv_bfloat16>::value, false, false);
       const uint32_t idesc_o = idesc_f16(128, L.nc, true, false, false);  // Dv rows are K-major (atoms contiguous)
@@ -722,58 +729,67 @@ __global__ void __launch_bounds__(kWideThreads, kMinBlocks) route_fwd_wide_kerne
         mma_commit<2>(mapa_shared(smem_u32(bar), 1));
       };
       const uint32_t qa = smem_u32(smem + L.off_q);
-      int kc = 0, vc = 0;
-      auto issue_s = [&](int j) -> bool {
-        const int sb = j % L.nsb;
-        if (j >= L.nsb && !mbar_wait(&p_full[sb], ((j - L.nsb) / L.nsb) & 1u, ab, 22)) return false;
-        const uint32_t d = tmem + L.tmem_s + (uint32_t)(sb * L.s_cols);
-        for (int c = 0; c < L.kchunks; ++c, ++kc) {
-          const int st = kc % L.nks;
-          if (!mbar_wait(&k_full[st], (kc / L.nks) & 1u, ab, 23)) return false;
-          tc_fence_after();
-          const uint64_t ad0 = sdesc_sw128(qa + c * (kRows * 128), 16, 1024);
-          const uint64_t bd0 = sdesc_sw128(smem_u32(smem + L.off_k + st * L.k_stage), 16, 1024);
-#pragma unroll
-          for (int kin = 0; kin < 4; ++kin)  // +32 B per K step of 16 = +2 in the encoded address
-            mma_f16_ss<2>(d, ad0 + 2 * kin, bd0 + 2 * kin, idesc_s, (c | kin) ? 1u : 0u);
-          commit_both(&k_empty[st]);
-        }
-        commit_both(&s_full[sb]);
-        return true;
-      };
-      auto issue_pv = [&](int j) -> bool {
-        const int pb = j % L.npb;
-        if (!mbar_wait(&p_full[j % L.nsb], (j / L.nsb) & 1u, ab, 24)) return false;
-        const uint32_t pa = smem_u32(smem + L.off_p + pb * L.p_bytes);
-        for (int c = 0; c < nk / 64; ++c, ++vc) {
-          const int st = vc % L.nvs;
-          if (!mbar_wait(&v_full[st], (vc / L.nvs) & 1u, ab, 25)) return false;
-          tc_fence_after();
-          const uint32_t va = smem_u32(smem + L.off_v + st * L.v_stage);
-          const uint64_t ad0 = sdesc_sw128(pa + c * (kRows * 128), 16, 1024);
-          for (int i = 0; i < L.npv; ++i) {
-            const uint64_t bd0 = sdesc_sw128(va + i * ((L.nc / 2) * 128), 16, 1024);
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              mma_f16_ss<2>(tmem + (uint32_t)(i * (L.nc / 2)), ad0 + 2 * kk, bd0 + 2 * kk, idesc_o,
-                            (j | c | kk) ? 1u : 0u);
-          }
-          commit_both(&v_empty[st]);
-        }
-        commit_both(&p_empty[pb]);
-        return true;
-      };
       bool ok = mbar_wait(&q_full, 0, ab, 21);
-      trace_time(p.trace, 2);
+      if (warp == 1) trace_time(p.trace, 2);
       tc_fence_after();
-      int next_s = 0;  // scores run up to nsb tiles ahead of the probability products
-      for (int j = 0; ok && j < NJ; ++j) {
-        while (ok && next_s < NJ && next_s < j + L.nsb) ok = issue_s(next_s++);
-        if (ok) ok = issue_pv(j);
+      if (warp == 1) {
+        // score tiles in order; a score buffer is reused once the softmax has consumed its previous tile
+        int kc = 0;
+        for (int j = 0; ok && j < NJ; ++j) {
+          const int sb = j % L.nsb;
+          if (j < 256) trace_at(ft, 1024 + 4 * j);
+          if (j >= L.nsb && !mbar_wait(&p_full[sb], ((j - L.nsb) / L.nsb) & 1u, ab, 22)) { ok = false; break; }
+          if (j < 256) trace_at(ft, 1025 + 4 * j);
+          const uint32_t d = tmem + L.tmem_s + (uint32_t)(sb * L.s_cols);
+          for (int c = 0; ok && c < L.kchunks; ++c, ++kc) {
+            const int st = kc % L.nks;
+            if (!mbar_wait(&k_full[st], (kc / L.nks) & 1u, ab, 23)) { ok = false; break; }
+            tc_fence_after();
+            const uint64_t ad0 = sdesc_sw128(qa + c * (kRows * 128), 16, 1024);
+            const uint64_t bd0 = sdesc_sw128(smem_u32(smem + L.off_k + st * L.k_stage), 16, 1024);
+#pragma unroll
+            for (int kin = 0; kin < 4; ++kin)  // +32 B per K step of 16 = +2 in the encoded address
+              mma_f16_ss<2>(d, ad0 + 2 * kin, bd0 + 2 * kin, idesc_s, (c | kin) ? 1u : 0u);
+            commit_both(&k_empty[st]);
+          }
+          if (!ok) break;
+          commit_both(&s_full[sb]);
+          if (j < 256) trace_at(ft, 1026 + 4 * j);
+        }
+        trace_time(p.trace, 3);
+      } else {
+        // P_j . Dv_j^T once probability tile j and its value rows are in shared memory.  The wait on
+        // p_full[j % nsb] cannot alias a later phase: tile j + nsb's probabilities need P buffer
+        // (j + nsb) % npb back, i.e. the product of tile j + nsb - npb >= j (nsb >= npb).
+        int vc = 0;
+        for (int j = 0; ok && j < NJ; ++j) {
+          const int pb = j % L.npb;
+          if (j < 256) trace_at(ft, 2048 + 4 * j);
+          if (!mbar_wait(&p_full[j % L.nsb], (j / L.nsb) & 1u, ab, 24)) { ok = false; break; }
+          if (j < 256) trace_at(ft, 2049 + 4 * j);
+          const uint32_t pa = smem_u32(smem + L.off_p + pb * L.p_bytes);
+          for (int c = 0; ok && c < nk / 64; ++c, ++vc) {
+            const int st = vc % L.nvs;
+            if (!mbar_wait(&v_full[st], (vc / L.nvs) & 1u, ab, 25)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t va = smem_u32(smem + L.off_v + st * L.v_stage);
+            const uint64_t ad0 = sdesc_sw128(pa + c * (kRows * 128), 16, 1024);
+            for (int i = 0; i < L.npv; ++i) {
+              const uint64_t bd0 = sdesc_sw128(va + i * ((L.nc / 2) * 128), 16, 1024);
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk)
+                mma_f16_ss<2>(tmem + (uint32_t)(i * (L.nc / 2)), ad0 + 2 * kk, bd0 + 2 * kk, idesc_o,
+                              (j | c | kk) ? 1u : 0u);
+            }
+            commit_both(&v_empty[st]);
+          }
+          if (!ok) break;
+          commit_both(&p_empty[pb]);
+          if (j < 256) trace_at(ft, 2050 + 4 * j);
+        }
+        commit_both(&o_full);
+        mbar_wait_drain(&o_full, 0);  // every probability product (and so every score product) has completed
       }
-      commit_both(&o_full);
-      trace_time(p.trace, 3);
-      mbar_wait_drain(&o_full, 0);
     }
   } else {
     // ---------------------------------------------------------------- softmax + epilogue (warps 2..5)
@@ -814,47 +830,67 @@ __global__ void __launch_bounds__(kWideThreads, kMinBlocks) route_fwd_wide_kerne
     int amax = 0;
     const bool want_argmax = p.argmax != nullptr;
 
+    // A tile's probabilities are formed in registers first and stored once the P buffer is free, so
+    // with a single P buffer the softmax of tile j + 1 overlaps the product of tile j.
+    constexpr int kMaxCh = kMinBlocks == 2 ? 2 : 4;  // 32-atom chunks per thread per tile (compact: nk = 128)
+    const int nch = hc / 32;
     for (int j = 0; j < NJ; ++j) {
       const int sb = j % L.nsb, pb = j % L.npb;
       const int jj = (j + rot) % NJ;
+      if (arriver && j < 256) trace_at(ft, 3072 + 4 * j);
       if (ok && j > 0) ok = mbar_wait(&s_full[sb], (j / L.nsb) & 1u, ab, 32);
-      if (ok && j >= L.npb) ok = mbar_wait(&p_empty[pb], ((j - L.npb) / L.npb) & 1u, ab, 33);
+      if (arriver && j < 256) trace_at(ft, 3073 + 4 * j);
       ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-collective
+      uint32_t packed[kMaxCh][16];
       if (ok) {
         tc_fence_after();
-        const uint32_t pa = smem_u32(smem + L.off_p + pb * L.p_bytes);
-        for (int ch = 0; ch < hc / 32; ++ch) {
-          float v[32];
-          tmem_ld32(tmem + lane_base + L.tmem_s + (uint32_t)(sb * L.s_cols + ch * 32), v);
-          tmem_wait_ld();
-          const int kc = half * hc + ch * 32;  // atom column inside the tile
-          uint32_t packed[16];
 #pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            const float a = v[i] * scale, b = v[i + 1] * scale;
-            if (want_argmax) {  // first index of the maximum, whatever the visiting order
-              const int base = jj * nk + kc + i;
-              if (a > mx || (a == mx && base < amax)) amax = base;
-              const float ma = fmaxf(mx, a);
-              if (b > ma || (b == ma && base + 1 < amax)) amax = base + 1;
+        for (int ch = 0; ch < kMaxCh; ++ch) {
+          if (ch < nch) {
+            float v[32];
+            tmem_ld32(tmem + lane_base + L.tmem_s + (uint32_t)(sb * L.s_cols + ch * 32), v);
+            tmem_wait_ld();
+            const int kc = half * hc + ch * 32;  // atom column inside the tile
+#pragma unroll
+            for (int i = 0; i < 32; i += 2) {
+              const float a = v[i] * scale, b = v[i + 1] * scale;
+              if (want_argmax) {  // first index of the maximum, whatever the visiting order
+                const int base = jj * nk + kc + i;
+                if (a > mx || (a == mx && base < amax)) amax = base;
+                const float ma = fmaxf(mx, a);
+                if (b > ma || (b == ma && base + 1 < amax)) amax = base + 1;
+              }
+              mx = fmaxf(mx, fmaxf(a, b));
+              const float ea = ex2(a - bound), eb = ex2(b - bound);
+              sum += ea + eb;
+              packed[ch][i / 2] = pack_bf16x2(ea, eb);
             }
-            mx = fmaxf(mx, fmaxf(a, b));
-            const float ea = ex2(a - bound), eb = ex2(b - bound);
-            sum += ea + eb;
-            packed[i / 2] = pack_bf16x2(ea, eb);
           }
-          const uint32_t box = pa + (kc >> 6) * (kRows * 128);
-          const int cb = (kc & 63) >> 3;
+        }
+      }
+      if (ok && j >= L.npb) ok = mbar_wait(&p_empty[pb], ((j - L.npb) / L.npb) & 1u, ab, 33);
+      if (arriver && j < 256) trace_at(ft, 3074 + 4 * j);
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok) {
+        const uint32_t pa = smem_u32(smem + L.off_p + pb * L.p_bytes);
 #pragma unroll
-          for (int e = 0; e < 4; ++e)
-            st_shared_v4(box + sw128_offset(r, cb + e), packed[4 * e], packed[4 * e + 1], packed[4 * e + 2],
-                         packed[4 * e + 3]);
+        for (int ch = 0; ch < kMaxCh; ++ch) {
+          if (ch < nch) {
+            const int kc = half * hc + ch * 32;
+            const uint32_t box = pa + (kc >> 6) * (kRows * 128);
+            const int cb = (kc & 63) >> 3;
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              st_shared_v4(box + sw128_offset(r, cb + e), packed[ch][4 * e], packed[ch][4 * e + 1],
+                           packed[ch][4 * e + 2], packed[ch][4 * e + 3]);
+          }
         }
         fence_proxy_async();
       }
       tc_fence_before();
       named_bar_sync(1, 128);
       if (arriver) mbar_arrive_cluster(pf_leader + sb * 8);
+      if (arriver && j < 256) trace_at(ft, 3075 + 4 * j);
     }
 
     // ---- epilogue: combine the two column halves of each row, normalise, store.
@@ -970,11 +1006,13 @@ int launch_fwd(const RouteFwdArgs& a, cudaStream_t st) {
   const long pairs = (long)a.groups * ((a.rows + 127) / 128);
   // two CTAs per SM when every SM gets several pairs and the compact layout exists for this shape
   const WideLayout Wc = wide_layout(kR, (int)a.M, true);
-  const bool compact = kR >= 128 && kR <= 256 && pairs >= sm_count() && Wc.nk != 0 && Wc.nks >= 3 && Wc.nsb >= 2 &&
-                       Wc.tmem_cols <= 256;
+  // (the compact kernel holds a tile's probabilities for nk = 128 in registers; both layouts need
+  // nsb >= npb, see the probability-product issuer)
+  const bool compact = kR >= 128 && kR <= 256 && pairs >= sm_count() && Wc.nk == 128 && Wc.nks >= 3 && Wc.nsb >= 2 &&
+                       Wc.nsb >= Wc.npb && Wc.tmem_cols <= 256;
   p.compact = compact ? 1 : 0;
   const WideLayout W = compact ? Wc : wide_layout(kR, (int)a.M);
-  const bool wide = kR >= 128 && W.nk != 0 && W.nks >= 3 && W.nsb >= 2;
+  const bool wide = kR >= 128 && W.nk != 0 && W.nks >= 3 && W.nsb >= 2 && W.nsb >= W.npb;
   if (wide) {  // re-encode the key / value maps with the wide tile's boxes
     rc = make_tmap_2d(&tdk, a.dk_t, qdt, 2, kR, a.M, (uint64_t)kR * 2, 64, W.nk / 2);
     if (rc) return rc;
