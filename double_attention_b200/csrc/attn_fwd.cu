@@ -32,13 +32,16 @@
 namespace da {
 namespace attn {
 
-// warp0 keys (TMA), warp1 score MMAs, warps2-5 softmax/epilogue, warp6 values (TMA), warp7 P.V MMAs.
-// The issues of one warp are serialised, so the two operand streams come from two warps; the score
-// and P.V products have their own issuing threads, so a P.V product never queues behind the key
-// chunks of a score tile further ahead (and the reverse).
-constexpr int kThreads = 256;
+// warps 0 and 8 keys (TMA), warp 1 score MMAs, warps 2-5 softmax/epilogue, warps 6 and 9 values
+// (TMA), warp 7 P.V MMAs.  One warp's TMA stages complete one after another (about 1 us per stage
+// for paired loads, nearly whatever the stage's size), so each stream has two producer warps
+// taking alternate stages, and stages are made as large as the ring allows; the score and P.V
+// products have their own issuing threads, so a P.V product never queues behind the key chunks
+// of a score tile further ahead (and the reverse).
+constexpr int kThreads = 320;
 constexpr int kValueWarp = 6;
 constexpr int kPvWarp = 7;
+constexpr int kKeyWarp2 = 8, kValueWarp2 = 9;  // the second producer of each stream
 constexpr int kRows = 64;       // query rows per CTA
 constexpr int kMaxK = 8, kMaxV = 4, kMaxSB = 4, kMaxPB = 2;
 
@@ -68,13 +71,14 @@ __host__ __device__ inline Layout make_layout(int maps, int group, int R, int D,
   L.per = (L.nc / 2) / 64;
   L.q_bytes = kRows * L.kw * 2;
   L.v_stage = 64 * D;  // 64 keys x D/2 columns (bf16) per CTA
-  const int red = 128 * 8 * 4;
+  // the 4 KB reduction buffer aliases P buffer 0: it is used only while no P.V product reads P
+  const int red = 0;
   const int avail = 225 * 1024;
   L.nk = 0;
   for (int nk = mix ? 128 : 256; nk >= 128 && L.nk == 0; nk -= 128) {
     const int k_stage = (nk / 2) * 128, p_bytes = kRows * nk * 2;
     const int rest = avail - L.q_bytes - 2 * p_bytes - 2 * L.v_stage - red;
-    if (rest >= 2 * k_stage) {
+    if (rest >= (nk == 256 ? 4 : 2) * k_stage) {  // 256-key tiles only with two 32 KB key boxes
       L.nk = nk;
       L.k_stage = k_stage;
       L.p_bytes = p_bytes;
@@ -104,15 +108,16 @@ __host__ __device__ inline Layout make_layout(int maps, int group, int R, int D,
       L.nks = nks > kMaxK ? kMaxK : nks;
     }
   }
-  // Each TMA issue costs about the same whatever its size, so key chunks of the same rows are
-  // fetched several column blocks per box while the ring keeps at least three boxes in flight.
+  // A stage costs about the same whatever its size, so key chunks of the same rows are fetched
+  // several column blocks per box (up to 32 KB) while the ring keeps two boxes, one per producer.
   L.kbb = 1;
   for (int b = 4; b >= 2; b /= 2)
-    if (L.rpb % b == 0 && L.nks / b >= 3) {
+    if (L.rpb % b == 0 && L.nks / b >= 2 && b * L.k_stage <= 32768) {
       L.kbb = b;
       break;
     }
   L.kslots = L.nks / L.kbb;
+  L.nks = L.kslots * L.kbb;
   L.s_cols = L.nk / 2;
   L.tmem_s = D / 2;
   const int nsb = (512 - D / 2) / L.s_cols;
@@ -121,8 +126,8 @@ __host__ __device__ inline Layout make_layout(int maps, int group, int R, int D,
   L.off_k = L.off_q + L.q_bytes;
   L.off_v = L.off_k + L.nks * L.k_stage;
   L.off_p = L.off_v + L.nvs * L.v_stage;
-  L.off_red = L.off_p + L.npb * L.p_bytes;
-  const int used = L.off_red + red;
+  L.off_red = L.off_p;  // aliases P buffer 0 (p_bytes >= 16 KB > 4 KB)
+  const int used = L.off_p + L.npb * L.p_bytes;
   L.smem = used < 120 * 1024 ? 120 * 1024 : used;  // one CTA per SM
   const int cols = D / 2 + L.nsb * L.s_cols;
   L.tmem_cols = cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : cols <= 256 ? 256 : 512;
@@ -216,26 +221,31 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   grid_launch_dependents();
   const uint32_t tmem = tmem_base;
 
-  if (warp == 0) {
-    // ---------------------------------------------------------------- TMA producers (both CTAs)
+  if (warp == 0 || warp == kKeyWarp2) {
+    // ---------------------------------------------------------------- key producers (both CTAs): warp 0
+    // takes the even key boxes (and loads q), warp 8 the odd ones
     if (lane == 0) {
-      prefetch_tmap(&tq);
+      const int pi = warp == 0 ? 0 : 1;
       prefetch_tmap(&tk);
-      if (rank == 0) mbar_arrive_expect_tx(&q_full, 2 * L.q_bytes);
-      const uint32_t qf = mapa_shared(smem_u32(&q_full), 0);
-      for (int s = 0; s < maps; ++s)
-        for (int gi = 0; gi < p.group; ++gi) {
-          const int64_t row = p.q_base + b * p.q_sb + (p.branch0[s] + gi) * p.q_sbr + t0 + 64 * (int)rank;
-          const int y = (int)min(row, p.q_rows - 1);  // boxes never start outside the matrix
-          for (int kb = 0; kb < L.rpb; ++kb)
-            tma_load_2d_pair(&tq, qf, smem + L.off_q + ((s * p.group + gi) * L.rpb + kb) * (kRows * 128), kb * 64, y);
-        }
-      int kx = 0;  // key boxes issued
+      if (pi == 0) {
+        prefetch_tmap(&tq);
+        if (rank == 0) mbar_arrive_expect_tx(&q_full, 2 * L.q_bytes);
+        const uint32_t qf = mapa_shared(smem_u32(&q_full), 0);
+        for (int s = 0; s < maps; ++s)
+          for (int gi = 0; gi < p.group; ++gi) {
+            const int64_t row = p.q_base + b * p.q_sb + (p.branch0[s] + gi) * p.q_sbr + t0 + 64 * (int)rank;
+            const int y = (int)min(row, p.q_rows - 1);  // boxes never start outside the matrix
+            for (int kb = 0; kb < L.rpb; ++kb)
+              tma_load_2d_pair(&tq, qf, smem + L.off_q + ((s * p.group + gi) * L.rpb + kb) * (kRows * 128), kb * 64, y);
+          }
+      }
+      int kx = 0;  // key boxes of both producers
       const int box_bytes = L.kbb * L.k_stage;
       for (int u = 0; u < U; ++u) {
         const int rem = u % sweep_units, j = rem / maps, s = rem % maps;
         bool ok = true;
         for (int c = 0; c < L.kchunks; c += L.kbb, ++kx) {
+          if ((kx & 1) != pi) continue;
           const int st = kx % L.kslots;
           if (!mbar_wait(&k_empty[st], ((kx / L.kslots) & 1u) ^ 1u, ab, 11)) { ok = false; break; }
           if (rank == 0) mbar_arrive_expect_tx(&k_full[st], 2 * box_bytes);
@@ -246,20 +256,24 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         }
         if (!ok) break;
       }
-      if (rank == 0) {  // drain: no TMA may be in flight at teardown
-        mbar_wait_drain(&q_full, 0);
+      if (rank == 0) {  // drain: none of this producer's loads may be in flight at teardown
+        if (pi == 0) mbar_wait_drain(&q_full, 0);
         for (int c = (kx > L.kslots ? kx - L.kslots : 0); c < kx; ++c)
-          mbar_wait_drain(&k_full[c % L.kslots], (c / L.kslots) & 1u);
+          if ((c & 1) == pi) mbar_wait_drain(&k_full[c % L.kslots], (c / L.kslots) & 1u);
       }
     }
-  } else if (warp == kValueWarp) {
+  } else if (warp == kValueWarp || warp == kValueWarp2) {
+    // ---------------------------------------------------------------- value producers: warp 6 even
+    // stages, warp 9 odd ones
     if (lane == 0) {
+      const int pi = warp == kValueWarp ? 0 : 1;
       prefetch_tmap(&tv);
       int vc = 0;
       const int64_t vrows = (int64_t)p.B * p.T;
       for (int v = 0; v < nj; ++v) {
         bool ok = true;
         for (int c = 0; c < nk / 64; ++c, ++vc) {
+          if ((vc & 1) != pi) continue;
           const int st = vc % L.nvs;
           if (!mbar_wait(&v_empty[st], ((vc / L.nvs) & 1u) ^ 1u, ab, 12)) { ok = false; break; }
           if (rank == 0) mbar_arrive_expect_tx(&v_full[st], 2 * L.v_stage);
@@ -272,7 +286,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       }
       if (rank == 0)
         for (int c = (vc > L.nvs ? vc - L.nvs : 0); c < vc; ++c)
-          mbar_wait_drain(&v_full[c % L.nvs], (c / L.nvs) & 1u);
+          if ((c & 1) == pi) mbar_wait_drain(&v_full[c % L.nvs], (c / L.nvs) & 1u);
     }
   } else if (warp == 1 || warp == kPvWarp) {
     // ---------------------------------------------------------------- MMA issuers (leader): scores on warp 1,
