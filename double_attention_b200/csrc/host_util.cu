@@ -63,7 +63,7 @@ int make_tmap_blocks(CUtensorMap* map, const void* base, CUtensorMapDataType dty
   if (!fn) return record_cuda_error_code(static_cast<int>(cudaErrorNotSupported));
   if (rank < 3 || rank > 5) return DA_ERR_SHAPE;
   if (reinterpret_cast<uintptr_t>(base) & 15) return DA_ERR_ALIGN;
-  if (dims[0] * static_cast<uint64_t>(elem_bytes) != 128 || box[0] != dims[0]) return DA_ERR_ALIGN;
+  if (box[0] * static_cast<uint32_t>(elem_bytes) != 128) return DA_ERR_ALIGN;
   cuuint64_t d[5], st[4];
   cuuint32_t b[5], e[5];
   for (int i = 0; i < rank; ++i) {

@@ -24,12 +24,13 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, 
                  uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
                  uint32_t box_outer, bool swizzle128 = true);
 
-// Encodes a tiled tensor map of rank 3..5 whose innermost dimension is one
-// 64-element (128-byte) column block with 128-byte swizzling: dims[0] must be
-// 128 / elem_bytes; strides_bytes[i] is the byte stride of dims[i + 1] (any
-// order: a dimension may step across column blocks of the same rows, so one
-// box gathers several [box[1] x 128 B] blocks, each laid out in shared memory
-// exactly like a separate 2-D box).  Returns DA_OK or a DA_ERR_* status.
+// Encodes a tiled tensor map of rank 3..5 with 128-byte swizzling whose box is
+// 128 bytes wide in the innermost dimension (box[0] = 128 / elem_bytes);
+// strides_bytes[i] is the byte stride of dims[i + 1] in any order, so a
+// dimension may step across 64-column blocks of the same rows (dims[0] = 64)
+// or across row groups, and one box gathers several [box[1] x 128 B] blocks,
+// each laid out in shared memory exactly like a separate 2-D box.  Returns
+// DA_OK or a DA_ERR_* status.
 int make_tmap_blocks(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes, int rank,
                      const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box);
 

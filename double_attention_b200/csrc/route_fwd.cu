@@ -540,6 +540,7 @@ __global__ void __launch_bounds__(192, 1) route_fwd_kernel(const __grid_constant
 // normalisation, exact repair of low-mass rows) is the one above.
 struct WideLayout {
   int nk, kchunks, nc, npv;
+  int kbb, kslots;  // key chunks per TMA box, ring slots of kbb chunks
   int q_bytes, k_stage, v_stage, p_bytes;
   int nks, nvs, nsb, npb;
   int off_q, off_k, off_v, off_p, off_red, smem;
@@ -547,12 +548,17 @@ struct WideLayout {
 };
 
 constexpr int kWideMaxK = 8, kWideMaxV = 4, kWideMaxSB = 4, kWideMaxPB = 2;
-// warp0 keys, warp1 score MMAs, warps2-5 softmax/epilogue, warp6 values, warp7 P.Dv^T MMAs: the two
-// products have their own issuing threads, so a P.Dv^T product never waits behind the key chunks of
-// a score tile further ahead (and the reverse).
-constexpr int kWideThreads = 256;
+// warp0 keys, warp1 score MMAs, warps2-5 softmax/epilogue, warp6 values, warp7 P.Dv^T MMAs, and in
+// the one-CTA-per-SM layout warps 8 and 9 as second key and value producers.  The two products have
+// their own issuing threads, so a P.Dv^T product never waits behind the key chunks of a score tile
+// further ahead (and the reverse).  One warp's TMA stages complete one after another (about 1 us
+// per stage for paired loads, nearly whatever the stage's size), so stages are as large as the
+// rings allow and, where registers permit, each stream has two producers taking alternate stages.
 constexpr int kValueWarp = 6;
 constexpr int kPvWarp = 7;
+constexpr int kKeyWarp2 = 8, kValueWarp2 = 9;
+template <int kMinBlocks>
+constexpr int wide_threads() { return kMinBlocks == 2 ? 256 : 320; }
 
 // compact: a layout two CTAs of which fit one SM (<= 256 TMEM columns, ~108 KB of shared memory),
 // so that one pair's serial chain (setup, scores, softmax, epilogue) overlaps another's when there
@@ -588,6 +594,15 @@ __host__ __device__ inline WideLayout wide_layout(int R, int M, bool compact = f
     L.smem = 0;
     return L;
   }
+  // several 64-column key chunks of the same atoms per box (<= 32 KB), keeping at least two slots
+  L.kbb = 1;
+  for (int b = 4; b >= 2; b /= 2)
+    if (L.kchunks % b == 0 && L.nks / b >= 2 && b * L.k_stage <= 32768) {
+      L.kbb = b;
+      break;
+    }
+  L.kslots = L.nks / L.kbb;
+  L.nks = L.kslots * L.kbb;
   L.s_cols = L.nk / 2;
   L.tmem_s = R / 2;
   const int nsb = ((compact ? 256 : 512) - R / 2) / L.s_cols;
@@ -605,7 +620,7 @@ __host__ __device__ inline WideLayout wide_layout(int R, int M, bool compact = f
 }
 
 template <int kR, typename T, int kMinBlocks>
-__global__ void __launch_bounds__(kWideThreads, kMinBlocks) route_fwd_wide_kernel(const __grid_constant__ CUtensorMap tq,
+__global__ void __launch_bounds__(wide_threads<kMinBlocks>(), kMinBlocks) route_fwd_wide_kernel(const __grid_constant__ CUtensorMap tq,
                                                                 const __grid_constant__ CUtensorMap tdk,
                                                                 const __grid_constant__ CUtensorMap tdv,
                                                                 const FwdParams p) {
@@ -667,56 +682,63 @@ __global__ void __launch_bounds__(kWideThreads, kMinBlocks) route_fwd_wide_kerne
   const uint32_t tmem = tmem_base;
   if (threadIdx.x == 0) trace_time(p.trace, 1);
 
-  if (warp == 0) {
-    // ---------------------------------------------------------------- TMA producers (both CTAs)
-    if (lane == 0) {  // q rows, then key rows in 64-column K chunks
-      prefetch_tmap(&tq);
+  constexpr int kProducers = kMinBlocks == 2 ? 1 : 2;  // per stream
+  if (warp == 0 || (kProducers == 2 && warp == kKeyWarp2)) {
+    // ---------------------------------------------------------------- key producers (both CTAs): warp 0
+    // loads q and the even key boxes, warp 8 (if present) the odd ones
+    if (lane == 0) {
+      const int pi = warp == 0 ? 0 : 1;
       prefetch_tmap(&tdk);
-      if (rank == 0) mbar_arrive_expect_tx(&q_full, 2 * L.q_bytes);
-      const uint32_t qf = mapa_shared(smem_u32(&q_full), 0);
-      const int qrow = min(row0 + 64 * (int)rank, p.rows - 1);  // boxes never start outside the matrix
-      for (int kb = 0; kb < kR / 64; ++kb)
-        tma_load_2d_pair(&tq, qf, smem + L.off_q + kb * (kRows * 128), g * p.col_stride + kb * 64, qrow);
-      int kc = 0;
+      if (pi == 0) {
+        prefetch_tmap(&tq);
+        if (rank == 0) mbar_arrive_expect_tx(&q_full, 2 * L.q_bytes);
+        const uint32_t qf = mapa_shared(smem_u32(&q_full), 0);
+        const int qrow = min(row0 + 64 * (int)rank, p.rows - 1);  // boxes never start outside the matrix
+        for (int kb = 0; kb < kR / 64; ++kb)
+          tma_load_2d_pair(&tq, qf, smem + L.off_q + kb * (kRows * 128), g * p.col_stride + kb * 64, qrow);
+      }
+      const int box_bytes = L.kbb * L.k_stage;
+      int kx = 0;  // key boxes of all producers
       bool ok = true;
       for (int j = 0; ok && j < NJ; ++j) {
         const int jj = (j + rot) % NJ;
-        for (int c = 0; c < L.kchunks; ++c, ++kc) {
-          const int st = kc % L.nks;
-          if (!mbar_wait(&k_empty[st], ((kc / L.nks) & 1u) ^ 1u, ab, 11)) { ok = false; break; }
-          if (rank == 0) mbar_arrive_expect_tx(&k_full[st], 2 * L.k_stage);
-          tma_load_2d_pair(&tdk, mapa_shared(smem_u32(&k_full[st]), 0), smem + L.off_k + st * L.k_stage, c * 64,
-                           jj * nk + (int)rank * (nk / 2));
+        for (int c = 0; c < L.kchunks; c += L.kbb, ++kx) {
+          if (kx % kProducers != pi) continue;
+          const int st = kx % L.kslots;
+          if (!mbar_wait(&k_empty[st], ((kx / L.kslots) & 1u) ^ 1u, ab, 11)) { ok = false; break; }
+          if (rank == 0) mbar_arrive_expect_tx(&k_full[st], 2 * box_bytes);
+          tma_load_3d_pair(&tdk, mapa_shared(smem_u32(&k_full[st]), 0), smem + L.off_k + st * box_bytes, 0,
+                           jj * nk + (int)rank * (nk / 2), c);
         }
       }
-      if (rank == 0) {  // drain: no TMA may be in flight at teardown
-        mbar_wait_drain(&q_full, 0);
-        for (int c = (kc > L.nks ? kc - L.nks : 0); c < kc; ++c)
-          mbar_wait_drain(&k_full[c % L.nks], (c / L.nks) & 1u);
+      if (rank == 0) {  // drain: none of this producer's loads may be in flight at teardown
+        if (pi == 0) mbar_wait_drain(&q_full, 0);
+        for (int c = (kx > L.kslots ? kx - L.kslots : 0); c < kx; ++c)
+          if (c % kProducers == pi) mbar_wait_drain(&k_full[c % L.kslots], (c / L.kslots) & 1u);
       }
     }
-  } else if (warp == kValueWarp) {
-    // ---------------------------------------------------------------- value producer (its own warp:
-    // TMA issues of one warp are serialised, so keys and values stream from two warps)
-    if (lane == 0) {  // value rows (this CTA's R/2 slice of every N block) in 64-atom K chunks
+  } else if (warp == kValueWarp || (kProducers == 2 && warp == kValueWarp2)) {
+    // ---------------------------------------------------------------- value producers: this CTA's R/2
+    // value rows of every N block, 64 atoms per stage, one box per stage
+    if (lane == 0) {
+      const int pi = warp == kValueWarp ? 0 : 1;
       prefetch_tmap(&tdv);
       int vc = 0;
       bool ok = true;
       for (int j = 0; ok && j < NJ; ++j) {
         const int jj = (j + rot) % NJ;
         for (int c = 0; c < nk / 64; ++c, ++vc) {
+          if (vc % kProducers != pi) continue;
           const int st = vc % L.nvs;
           if (!mbar_wait(&v_empty[st], ((vc / L.nvs) & 1u) ^ 1u, ab, 12)) { ok = false; break; }
           if (rank == 0) mbar_arrive_expect_tx(&v_full[st], 2 * L.v_stage);
-          const uint32_t vf = mapa_shared(smem_u32(&v_full[st]), 0);
-          for (int i = 0; i < L.npv; ++i)
-            tma_load_2d_pair(&tdv, vf, smem + L.off_v + st * L.v_stage + i * ((L.nc / 2) * 128), jj * nk + c * 64,
-                             i * L.nc + (int)rank * (L.nc / 2));
+          tma_load_3d_pair(&tdv, mapa_shared(smem_u32(&v_full[st]), 0), smem + L.off_v + st * L.v_stage,
+                           jj * nk + c * 64, (int)rank * (L.nc / 2), 0);
         }
       }
       if (rank == 0)
         for (int c = (vc > L.nvs ? vc - L.nvs : 0); c < vc; ++c)
-          mbar_wait_drain(&v_full[c % L.nvs], (c / L.nvs) & 1u);
+          if (c % kProducers == pi) mbar_wait_drain(&v_full[c % L.nvs], (c / L.nvs) & 1u);
     }
   } else if (warp == 1 || warp == kPvWarp) {
     // ---------------------------------------------------------------- MMA issuers (leader): scores on
@@ -734,23 +756,29 @@ __global__ void __launch_bounds__(kWideThreads, kMinBlocks) route_fwd_wide_kerne
       tc_fence_after();
       if (warp == 1) {
         // score tiles in order; a score buffer is reused once the softmax has consumed its previous tile
-        int kc = 0;
+        int kx = 0, st = 0;  // key boxes consumed, current slot
         for (int j = 0; ok && j < NJ; ++j) {
           const int sb = j % L.nsb;
           if (j < 256) trace_at(ft, 1024 + 4 * j);
           if (j >= L.nsb && !mbar_wait(&p_full[sb], ((j - L.nsb) / L.nsb) & 1u, ab, 22)) { ok = false; break; }
           if (j < 256) trace_at(ft, 1025 + 4 * j);
           const uint32_t d = tmem + L.tmem_s + (uint32_t)(sb * L.s_cols);
-          for (int c = 0; ok && c < L.kchunks; ++c, ++kc) {
-            const int st = kc % L.nks;
-            if (!mbar_wait(&k_full[st], (kc / L.nks) & 1u, ab, 23)) { ok = false; break; }
-            tc_fence_after();
+          for (int c = 0; ok && c < L.kchunks; ++c) {
+            const int cib = c % L.kbb;  // chunk inside the current box
+            if (cib == 0) {
+              st = kx % L.kslots;
+              if (!mbar_wait(&k_full[st], (kx / L.kslots) & 1u, ab, 23)) { ok = false; break; }
+              tc_fence_after();
+            }
             const uint64_t ad0 = sdesc_sw128(qa + c * (kRows * 128), 16, 1024);
-            const uint64_t bd0 = sdesc_sw128(smem_u32(smem + L.off_k + st * L.k_stage), 16, 1024);
+            const uint64_t bd0 = sdesc_sw128(smem_u32(smem + L.off_k + (st * L.kbb + cib) * L.k_stage), 16, 1024);
 #pragma unroll
             for (int kin = 0; kin < 4; ++kin)  // +32 B per K step of 16 = +2 in the encoded address
               mma_f16_ss<2>(d, ad0 + 2 * kin, bd0 + 2 * kin, idesc_s, (c | kin) ? 1u : 0u);
-            commit_both(&k_empty[st]);
+            if (cib == L.kbb - 1) {
+              commit_both(&k_empty[st]);
+              ++kx;
+            }
           }
           if (!ok) break;
           commit_both(&s_full[sb]);
@@ -1014,10 +1042,21 @@ int launch_fwd(const RouteFwdArgs& a, cudaStream_t st) {
   const WideLayout W = compact ? Wc : wide_layout(kR, (int)a.M);
   const bool wide = kR >= 128 && W.nk != 0 && W.nks >= 3 && W.nsb >= 2 && W.nsb >= W.npb;
   if (wide) {  // re-encode the key / value maps with the wide tile's boxes
-    rc = make_tmap_2d(&tdk, a.dk_t, qdt, 2, kR, a.M, (uint64_t)kR * 2, 64, W.nk / 2);
-    if (rc) return rc;
-    rc = make_tmap_2d(&tdv, a.dv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.M, kR, (uint64_t)a.M * 2, 64, W.nc / 2);
-    if (rc) return rc;
+    {  // keys Dk^T [M, R]: (64-column block, atom, block index); a box is nk/2 atoms x kbb blocks
+      const uint64_t dims[3] = {64, (uint64_t)a.M, (uint64_t)kR / 64};
+      const uint64_t strides[2] = {(uint64_t)kR * 2, 128};
+      const uint32_t box[3] = {64, (uint32_t)(W.nk / 2), (uint32_t)W.kbb};
+      rc = make_tmap_blocks(&tdk, a.dk_t, qdt, 2, 3, dims, strides, box);
+      if (rc) return rc;
+    }
+    {  // values Dv [R, M]: (64 atoms, row inside an nc-row group, group); a box is 64 atoms x this
+       // CTA's nc/2 rows of each of the npv groups
+      const uint64_t dims[3] = {(uint64_t)a.M, (uint64_t)W.nc, (uint64_t)kR / W.nc};
+      const uint64_t strides[2] = {(uint64_t)a.M * 2, (uint64_t)W.nc * a.M * 2};
+      const uint32_t box[3] = {64, (uint32_t)(W.nc / 2), (uint32_t)W.npv};
+      rc = make_tmap_blocks(&tdv, a.dv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 3, dims, strides, box);
+      if (rc) return rc;
+    }
     if ((a.M + kR + 64) * 4 > W.smem) return DA_ERR_SHAPE;  // repair scratch must fit
   }
   auto kern = !wide ? route_fwd_kernel<kR, T>
@@ -1025,7 +1064,8 @@ int launch_fwd(const RouteFwdArgs& a, cudaStream_t st) {
   const int smem = (wide ? W.smem : C::kSmem) + 1024;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return record_cuda_error();
-  return launch_kernel(kern, dim3((unsigned)(2 * pairs), 1, 1), dim3(wide ? kWideThreads : C::kThreads, 1, 1), smem, st, true, tq, tdk, tdv, p);
+  const int threads = !wide ? C::kThreads : (compact ? wide_threads<2>() : wide_threads<1>());
+  return launch_kernel(kern, dim3((unsigned)(2 * pairs), 1, 1), dim3(threads, 1, 1), smem, st, true, tq, tdk, tdv, p);
 }
 
 int route_fwd(const RouteFwdArgs& a, cudaStream_t st) {
