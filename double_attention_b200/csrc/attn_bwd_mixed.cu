@@ -35,12 +35,17 @@ namespace bwdm {
 
 // warp 0: TMA producer of the resident rows and the score / accumulation operands; warp 1: their
 // MMA issuer; warps 2-5: softmax; warp 6: TMA producer of the dP operands (V and dY); warp 7: the
-// dP issuer.  dP runs as its own stream so the other products never wait behind it.
-constexpr int kThreads = 256;
+// dP issuer; warps 8 and 9: second producers of the two rings.  dP runs as its own stream so the
+// other products never wait behind it.  One warp's TMA stages complete one after another (about
+// 1 us per stage for paired loads, nearly whatever the stage's size), so each ring is filled by two
+// producer warps taking alternate stages.
+constexpr int kThreads = 320;
 constexpr int kDpWarp = 6;
+constexpr int kProd2 = 8, kDpProd2 = 9;
 constexpr int kRows = 64;      // rows (queries or keys) per CTA
 constexpr int kTile = 128;     // columns (keys or queries) per tile and pair
-constexpr int kStage = 16384;  // ring stage bytes
+constexpr int kStage = 16384;  // main ring stage bytes
+constexpr int kDpStage = 32768;  // dP ring stage: two 64-column blocks of each of V and dY
 constexpr int kMaxStages = 8;
 constexpr int kBox = kRows * 128;  // one 64-row x 128-byte swizzled box
 
@@ -69,6 +74,7 @@ DA_DEV int64_t row_of(int64_t base, int64_t sb, int64_t sbr, int b, int branch, 
 
 struct Layout {
   int kw, W, rpb, ncol, nins;
+  int acc_merge;  // the accumulation operand (dQ: K, dK: Q rows, MN-major) comes as one 128-row box per stage
   int off_a, off_b, off_t, off_red, off_ring, nst, off_pring, nsp, smem;
   int tmem_acc, tmem_s, tmem_p, tmem_cols;
 };
@@ -84,6 +90,7 @@ __host__ __device__ inline Layout make_layout(int kind, int maps, int group, int
   L.rpb = R / 64;
   L.ncol = L.kw < 256 ? L.kw : 256;
   L.nins = L.kw / L.ncol;
+  L.acc_merge = kind != 2 && L.ncol == 128;  // one 64-column block per CTA: both 64-row chunks in one box
   L.off_a = 0;
   L.off_b = L.off_a + kRows * L.W * 2;
   const int b_bytes = 0;
@@ -91,11 +98,13 @@ __host__ __device__ inline Layout make_layout(int kind, int maps, int group, int
   L.off_red = L.off_t + 2 * kRows * kTile * 2;
   L.off_ring = L.off_red + 8192;
   const int avail = 225 * 1024 - L.off_ring;
-  const int total = avail / kStage;
-  L.nsp = kind == 2 ? 0 : (total >= 8 ? 4 : total / 2);  // dP ring: V and dY chunks
-  L.nst = total - L.nsp > kMaxStages ? kMaxStages : total - L.nsp;
+  // One warp's TMA stages complete one after another at a nearly size-independent cost, so the dP
+  // operands come as 32 KB stages (two 64-column blocks of V and of dY, one box each).
+  L.nsp = kind == 2 ? 0 : 2;
+  const int rest = (avail - L.nsp * kDpStage) / kStage;
+  L.nst = rest > kMaxStages ? kMaxStages : rest;
   L.off_pring = L.off_ring + L.nst * kStage;
-  L.smem = L.off_pring + L.nsp * kStage;
+  L.smem = L.off_pring + L.nsp * kDpStage;
   L.tmem_acc = 0;
   const int acc = kind == 2 ? D / 2 : L.W / 2;
   L.tmem_s = acc;
@@ -126,6 +135,7 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
                                                                const __grid_constant__ CUtensorMap tk,
                                                                const __grid_constant__ CUtensorMap tv,
                                                                const __grid_constant__ CUtensorMap tdy,
+                                                               const __grid_constant__ CUtensorMap tacc,
                                                                const Params p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -195,15 +205,19 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
   const int tq_row = t0 + 64 * (int)rank;
   const int dy_row = (int)min((int64_t)b * p.T + tq_row, rowsBT - 1);
   const int dps = sweeps * nj;  // dP products: one per key tile and sweep
-  if (warp == 0 && lane == 0) {
-    // ---------------------------------------------------------------- TMA producer: Q, then K for S and dQ
-    prefetch_tmap(&tq);
+  if ((warp == 0 || warp == kProd2) && lane == 0) {
+    // ---------------------------------------------------------------- TMA producers: Q (warp 0), then K
+    // for S and dQ, even stages from warp 0 and odd ones from warp 8
+    const int pi = warp == 0 ? 0 : 1;
     prefetch_tmap(&tk);
-    const uint32_t inf = mapa_shared(smem_u32(&in_full), 0);
-    if (rank == 0) mbar_arrive_expect_tx(&in_full, 2 * (kRows * L.W * 2));
-    for (int s = 0; s < maps; ++s)
-      for (int cc = 0; cc < L.kw / 128; ++cc)
-        load_map_chunk(&tq, qm, p, inf, smem + L.off_a + (s * (L.kw / 64) + cc * 2) * kBox, b, s, cc, 2, tq_row);
+    if (pi == 0) {
+      prefetch_tmap(&tq);
+      const uint32_t inf = mapa_shared(smem_u32(&in_full), 0);
+      if (rank == 0) mbar_arrive_expect_tx(&in_full, 2 * (kRows * L.W * 2));
+      for (int s = 0; s < maps; ++s)
+        for (int cc = 0; cc < L.kw / 128; ++cc)
+          load_map_chunk(&tq, qm, p, inf, smem + L.off_a + (s * (L.kw / 64) + cc * 2) * kBox, b, s, cc, 2, tq_row);
+    }
     int it = 0;
     bool ok = true;
     auto stage = [&](int bytes) -> uint8_t* {
@@ -216,6 +230,7 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
     auto emit_s = [&](int u) {  // key rows of map s for this CTA's 64 keys
       const int krow0 = unit_j(u) * kTile + 64 * (int)rank;
       for (int cc = 0; ok && cc < L.kw / 128; ++cc, ++it) {
+        if ((it & 1) != pi) continue;
         uint8_t* dst = stage(2 * kBox);
         if (!ok) return;
         load_map_chunk(&tk, km, p, stage_bar(), dst, b, unit_s(u), cc, 2, krow0);
@@ -223,8 +238,21 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
     };
     auto emit_dq = [&](int u) {  // key rows of all 128 keys, MN-major, this CTA's half of each N block
       const int per = (L.ncol / 2) / 64, s = unit_s(u), j = unit_j(u);
+      if (L.acc_merge) {  // one stage per N block: a 128-key x 64-column box
+        for (int ins = 0; ok && ins < L.nins; ++ins, ++it) {
+          if ((it & 1) != pi) continue;
+          uint8_t* dst = stage(2 * kBox);
+          if (!ok) return;
+          const int mb = (ins * L.ncol + (int)rank * (L.ncol / 2)) / 64;
+          const int gi = mb / L.rpb, x = (mb % L.rpb) * 64;
+          const int64_t row = row_of(km.base, km.sb, km.sbr, b, p.branch0[s] + gi, j * kTile);
+          tma_load_2d_pair(&tacc, stage_bar(), dst, x, (int)min(row, km.rows - 1));
+        }
+        return;
+      }
       for (int kc = 0; ok && kc < kTile / 64; ++kc)
         for (int ins = 0; ok && ins < L.nins; ++ins, ++it) {
+          if ((it & 1) != pi) continue;
           uint8_t* dst = stage(per * kBox);
           if (!ok) return;
           const uint32_t bar = stage_bar();
@@ -241,31 +269,35 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
       if (u + 1 < U) emit_s(u + 1);
       if (u >= u_dq) emit_dq(u);
     }
-    if (rank == 0) {  // drain: no TMA may be in flight at teardown
-      mbar_wait_drain(&in_full, 0);
-      for (int i = (it > L.nst ? it - L.nst : 0); i < it; ++i) mbar_wait_drain(&r_full[i % L.nst], (i / L.nst) & 1u);
+    if (rank == 0) {  // drain: none of this producer's loads may be in flight at teardown
+      if (pi == 0) mbar_wait_drain(&in_full, 0);
+      for (int i = (it > L.nst ? it - L.nst : 0); i < it; ++i)
+        if ((i & 1) == pi) mbar_wait_drain(&r_full[i % L.nst], (i / L.nst) & 1u);
     }
-  } else if (warp == kDpWarp && lane == 0) {
-    // ---------------------------------------------------------------- TMA producer: V and dY for dP
+  } else if ((warp == kDpWarp || warp == kDpProd2) && lane == 0) {
+    // ---------------------------------------------------------------- TMA producers: V and dY for dP
+    // (even stages from warp 6, odd ones from warp 9)
+    const int pi = warp == kDpWarp ? 0 : 1;
     prefetch_tmap(&tv);
     prefetch_tmap(&tdy);
     int it = 0;
     bool ok = true;
     for (int g = 0; ok && g < dps; ++g) {
       const int y = (int)min((int64_t)b * p.T + (g % nj) * kTile + 64 * (int)rank, rowsBT - 1);
-      for (int cc = 0; cc < p.D / 64; ++cc, ++it) {  // per 64 value columns: V rows of 64 keys, dY rows
+      for (int cc = 0; cc < p.D / 128; ++cc, ++it) {  // per 128 value columns: V rows of 64 keys, dY rows
+        if ((it & 1) != pi) continue;
         const int st = it % L.nsp;
         if (!mbar_wait(&rp_empty[st], ((it / L.nsp) & 1u) ^ 1u, ab, 13)) { ok = false; break; }
-        if (rank == 0) mbar_arrive_expect_tx(&rp_full[st], 2 * 2 * kBox);
+        if (rank == 0) mbar_arrive_expect_tx(&rp_full[st], 2 * kDpStage);
         const uint32_t bar = mapa_shared(smem_u32(&rp_full[st]), 0);
-        uint8_t* dst = smem + L.off_pring + st * kStage;
-        tma_load_2d_pair(&tv, bar, dst, cc * 64, y);
-        tma_load_2d_pair(&tdy, bar, dst + kBox, cc * 64, dy_row);
+        uint8_t* dst = smem + L.off_pring + st * kDpStage;
+        tma_load_3d_pair(&tv, bar, dst, 0, y, cc * 2);
+        tma_load_3d_pair(&tdy, bar, dst + 2 * kBox, 0, dy_row, cc * 2);
       }
     }
     if (rank == 0)
       for (int i = (it > L.nsp ? it - L.nsp : 0); i < it; ++i)
-        mbar_wait_drain(&rp_full[i % L.nsp], (i / L.nsp) & 1u);
+        if ((i & 1) == pi) mbar_wait_drain(&rp_full[i % L.nsp], (i / L.nsp) & 1u);
   } else if (warp == kDpWarp + 1 && lane == 0 && rank == 0) {
     // ---------------------------------------------------------------- dP issuer (leader): dP = dY V^T
     // Its own thread, so the score and dQ products never wait behind the value stream.
@@ -276,14 +308,15 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
       const int db = g & 1;
       if (g < 200) trace_at(ft, 1024 + 4 * g);
       if (g >= 2 && !mbar_wait(&dp_free[db], ((g - 2) >> 1) & 1u, ab, 27)) break;
-      for (int cc = 0; cc < p.D / 64; ++cc, ++it) {  // stage: [V box | dY box] of 64 value columns
+      for (int cc = 0; cc < p.D / 128; ++cc, ++it) {  // stage: [V 2 blocks | dY 2 blocks] of 128 columns
         const int st = it % L.nsp;
         if (!mbar_wait(&rp_full[st], (it / L.nsp) & 1u, ab, 28)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t sa = smem_u32(smem + L.off_pring + st * kStage);
-        for (int k = 0; k < 4; ++k) {
-          const uint64_t ad = sdesc_sw128(sa + kBox + k * 32, 16, 1024);
-          const uint64_t bd = sdesc_sw128(sa + k * 32, 16, 1024);
+        const uint32_t sa = smem_u32(smem + L.off_pring + st * kDpStage);
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t blk = (uint32_t)(k >> 2) * kBox + (k & 3) * 32;
+          const uint64_t ad = sdesc_sw128(sa + 2 * kBox + blk, 16, 1024);
+          const uint64_t bd = sdesc_sw128(sa + blk, 16, 1024);
           mma_f16_ss<2>(tmem + L.tmem_p + db * (kTile / 2), ad, bd, idesc, (cc | k) ? 1u : 0u);
         }
         mma_commit<2>(smem_u32(&rp_empty[st]));
@@ -340,18 +373,33 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
       if (u < 300) trace_at(ft, 2051 + 4 * u);
       tc_fence_after();
       const uint32_t dsa = smem_u32(smem + L.off_t + (v & 1) * (kRows * kTile * 2));
-      for (int kc = 0; kc < kTile / 64; ++kc)
+      if (L.acc_merge) {  // stage = 128 keys x 64 columns: both 64-key chunks
         for (int ins = 0; ins < L.nins; ++ins) {
           uint32_t st;
           if (!take(&st)) return false;
-          for (int kk = 0; kk < 4; ++kk) {
+          for (int k = 0; k < 8; ++k) {
+            const int kc = k >> 2, kk = k & 3;
             const uint64_t ad = sdesc_sw128(dsa + kc * kBox + kk * 32, 16, 1024);
-            const uint64_t bd = sdesc_sw128(st + kk * 16 * 128, 64 * 128, 1024);
+            const uint64_t bd = sdesc_sw128(st + kc * kBox + kk * 16 * 128, 64 * 128, 1024);
             mma_f16_ss<2>(tmem + L.tmem_acc + s * (L.kw / 2) + ins * (L.ncol / 2), ad, bd, idesc_q,
-                          (j | kc | kk) ? 1u : 0u);
+                          (j | k) ? 1u : 0u);
           }
           give();
         }
+      } else {
+        for (int kc = 0; kc < kTile / 64; ++kc)
+          for (int ins = 0; ins < L.nins; ++ins) {
+            uint32_t st;
+            if (!take(&st)) return false;
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t ad = sdesc_sw128(dsa + kc * kBox + kk * 32, 16, 1024);
+              const uint64_t bd = sdesc_sw128(st + kk * 16 * 128, 64 * 128, 1024);
+              mma_f16_ss<2>(tmem + L.tmem_acc + s * (L.kw / 2) + ins * (L.ncol / 2), ad, bd, idesc_q,
+                            (j | kc | kk) ? 1u : 0u);
+            }
+            give();
+          }
+      }
       commit_both(&ds_empty[v & 1]);
       return true;
     };
@@ -554,6 +602,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
                                                                 const __grid_constant__ CUtensorMap tk,
                                                                 const __grid_constant__ CUtensorMap tv,
                                                                 const __grid_constant__ CUtensorMap tdy,
+                                                                const __grid_constant__ CUtensorMap tacc,
                                                                 const Params p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -618,16 +667,20 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
 
   const int krow = k0 + 64 * (int)rank;
   const int vy = (int)min((int64_t)b * p.T + krow, rowsBT - 1);
-  if (warp == 0 && lane == 0) {
-    // ---------------------------------------------------------------- TMA producer: K, then Q (and dY for dV)
+  if ((warp == 0 || warp == kProd2) && lane == 0) {
+    // ---------------------------------------------------------------- TMA producers: K (warp 0), then Q
+    // (and dY for dV), even stages from warp 0 and odd ones from warp 8
+    const int pi = warp == 0 ? 0 : 1;
     prefetch_tmap(&tq);
-    prefetch_tmap(&tk);
     prefetch_tmap(&tdy);
-    const uint32_t inf = mapa_shared(smem_u32(&in_full), 0);
-    if (rank == 0) mbar_arrive_expect_tx(&in_full, 2 * (kRows * L.W * 2));
-    for (int s = 0; s < maps; ++s)
-      for (int cc = 0; cc < L.kw / 128; ++cc)
-        load_map_chunk(&tk, km, p, inf, smem + L.off_a + (s * (L.kw / 64) + cc * 2) * kBox, b, s, cc, 2, krow);
+    if (pi == 0) {
+      prefetch_tmap(&tk);
+      const uint32_t inf = mapa_shared(smem_u32(&in_full), 0);
+      if (rank == 0) mbar_arrive_expect_tx(&in_full, 2 * (kRows * L.W * 2));
+      for (int s = 0; s < maps; ++s)
+        for (int cc = 0; cc < L.kw / 128; ++cc)
+          load_map_chunk(&tk, km, p, inf, smem + L.off_a + (s * (L.kw / 64) + cc * 2) * kBox, b, s, cc, 2, krow);
+    }
     int it = 0;
     bool ok = true;
     auto stage = [&](int bytes) -> uint8_t* {
@@ -640,6 +693,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
     auto emit_s = [&](int u) {  // query rows of map s for this CTA's 64 queries
       const int q = (i0 + unit_g(u)) * kTile + 64 * (int)rank;
       for (int cc = 0; ok && cc < L.kw / 128; ++cc, ++it) {
+        if ((it & 1) != pi) continue;
         uint8_t* dst = stage(2 * kBox);
         if (!ok) return;
         load_map_chunk(&tq, qm, p, stage_bar(), dst, b, unit_s(u), cc, 2, q);
@@ -647,10 +701,21 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
     };
     auto emit_acc = [&](int u) {  // MN-major operand of the accumulating product, all 128 queries
       const int i = i0 + unit_g(u), s = unit_s(u);
-      if (kDK) {
+      if (kDK && L.acc_merge) {  // one stage per N block: a 128-query x 64-column box
+        for (int ins = 0; ok && ins < L.nins; ++ins, ++it) {
+          if ((it & 1) != pi) continue;
+          uint8_t* dst = stage(2 * kBox);
+          if (!ok) return;
+          const int mb = (ins * L.ncol + (int)rank * (L.ncol / 2)) / 64;
+          const int gi = mb / L.rpb, x = (mb % L.rpb) * 64;
+          const int64_t row = row_of(qm.base, qm.sb, qm.sbr, b, p.branch0[s] + gi, i * kTile);
+          tma_load_2d_pair(&tacc, stage_bar(), dst, x, (int)min(row, qm.rows - 1));
+        }
+      } else if (kDK) {
         const int per = (L.ncol / 2) / 64;
         for (int qc = 0; ok && qc < kTile / 64; ++qc)
           for (int ins = 0; ok && ins < L.nins; ++ins, ++it) {
+            if ((it & 1) != pi) continue;
             uint8_t* dst = stage(per * kBox);
             if (!ok) return;
             const uint32_t bar = stage_bar();
@@ -666,11 +731,10 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
         for (int qc = 0; ok && qc < kTile / 64; ++qc) {
           const int y = (int)min((int64_t)b * p.T + i * kTile + qc * 64, rowsBT - 1);
           for (int ins = 0; ok && ins < dins; ++ins, ++it) {
-            uint8_t* dst = stage(dper * kBox);
+            if ((it & 1) != pi) continue;
+            uint8_t* dst = stage(dper * kBox);  // dper = 2 (dn = 256): one box of two column blocks
             if (!ok) return;
-            const uint32_t bar = stage_bar();
-            for (int bx = 0; bx < dper; ++bx)
-              tma_load_2d_pair(&tdy, bar, dst + bx * kBox, ins * dn + (int)rank * (dn / 2) + bx * 64, y);
+            tma_load_3d_pair(&tdy, stage_bar(), dst, 0, y, (ins * dn + (int)rank * (dn / 2)) / 64);
           }
         }
       }
@@ -681,31 +745,35 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
       if (u + 1 < U) emit_s(u + 1);
       if (kDK || unit_s(u) == maps - 1) emit_acc(u);
     }
-    if (rank == 0) {  // drain: no TMA may be in flight at teardown
-      mbar_wait_drain(&in_full, 0);
-      for (int i = (it > L.nst ? it - L.nst : 0); i < it; ++i) mbar_wait_drain(&r_full[i % L.nst], (i / L.nst) & 1u);
+    if (rank == 0) {  // drain: none of this producer's loads may be in flight at teardown
+      if (pi == 0) mbar_wait_drain(&in_full, 0);
+      for (int i = (it > L.nst ? it - L.nst : 0); i < it; ++i)
+        if ((i & 1) == pi) mbar_wait_drain(&r_full[i % L.nst], (i / L.nst) & 1u);
     }
-  } else if (kDK && warp == kDpWarp && lane == 0) {
-    // ---------------------------------------------------------------- TMA producer: dY and V for dP^T
+  } else if (kDK && (warp == kDpWarp || warp == kDpProd2) && lane == 0) {
+    // ---------------------------------------------------------------- TMA producers: dY and V for dP^T
+    // (even stages from warp 6, odd ones from warp 9)
+    const int pi = warp == kDpWarp ? 0 : 1;
     prefetch_tmap(&tv);
     prefetch_tmap(&tdy);
     int it = 0;
     bool ok = true;
     for (int g = 0; ok && g < ni; ++g) {
       const int y = (int)min((int64_t)b * p.T + (i0 + g) * kTile + 64 * (int)rank, rowsBT - 1);
-      for (int cc = 0; cc < p.D / 64; ++cc, ++it) {  // per 64 value columns: dY rows of 64 queries, V rows
+      for (int cc = 0; cc < p.D / 128; ++cc, ++it) {  // per 128 value columns: dY rows of 64 queries, V rows
+        if ((it & 1) != pi) continue;
         const int st = it % L.nsp;
         if (!mbar_wait(&rp_empty[st], ((it / L.nsp) & 1u) ^ 1u, ab, 13)) { ok = false; break; }
-        if (rank == 0) mbar_arrive_expect_tx(&rp_full[st], 2 * 2 * kBox);
+        if (rank == 0) mbar_arrive_expect_tx(&rp_full[st], 2 * kDpStage);
         const uint32_t bar = mapa_shared(smem_u32(&rp_full[st]), 0);
-        uint8_t* dst = smem + L.off_pring + st * kStage;
-        tma_load_2d_pair(&tdy, bar, dst, cc * 64, y);
-        tma_load_2d_pair(&tv, bar, dst + kBox, cc * 64, vy);
+        uint8_t* dst = smem + L.off_pring + st * kDpStage;
+        tma_load_3d_pair(&tdy, bar, dst, 0, y, cc * 2);
+        tma_load_3d_pair(&tv, bar, dst + 2 * kBox, 0, vy, cc * 2);
       }
     }
     if (rank == 0)
       for (int i = (it > L.nsp ? it - L.nsp : 0); i < it; ++i)
-        mbar_wait_drain(&rp_full[i % L.nsp], (i / L.nsp) & 1u);
+        if ((i & 1) == pi) mbar_wait_drain(&rp_full[i % L.nsp], (i / L.nsp) & 1u);
   } else if (kDK && warp == kDpWarp + 1 && lane == 0 && rank == 0) {
     // ---------------------------------------------------------------- dP^T issuer (leader): dP^T = V dY^T
     const uint32_t idesc = idesc_f16(128, kTile, kBf16, false, false);
@@ -714,14 +782,15 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
     for (int g = 0; ok && g < ni; ++g) {
       const int db = g & 1;
       if (g >= 2 && !mbar_wait(&dp_free[db], ((g - 2) >> 1) & 1u, ab, 27)) break;
-      for (int cc = 0; cc < p.D / 64; ++cc, ++it) {  // stage: [dY box | V box] of 64 value columns
+      for (int cc = 0; cc < p.D / 128; ++cc, ++it) {  // stage: [dY 2 blocks | V 2 blocks] of 128 columns
         const int st = it % L.nsp;
         if (!mbar_wait(&rp_full[st], (it / L.nsp) & 1u, ab, 28)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t sa = smem_u32(smem + L.off_pring + st * kStage);
-        for (int k = 0; k < 4; ++k) {
-          const uint64_t ad = sdesc_sw128(sa + kBox + k * 32, 16, 1024);
-          const uint64_t bd = sdesc_sw128(sa + k * 32, 16, 1024);
+        const uint32_t sa = smem_u32(smem + L.off_pring + st * kDpStage);
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t blk = (uint32_t)(k >> 2) * kBox + (k & 3) * 32;
+          const uint64_t ad = sdesc_sw128(sa + 2 * kBox + blk, 16, 1024);
+          const uint64_t bd = sdesc_sw128(sa + blk, 16, 1024);
           mma_f16_ss<2>(tmem + L.tmem_p + db * (kTile / 2), ad, bd, idesc, (cc | k) ? 1u : 0u);
         }
         mma_commit<2>(smem_u32(&rp_empty[st]));
@@ -779,6 +848,22 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
       const uint32_t ta = smem_u32(smem + L.off_t + tb * (kRows * kTile * 2));
       const int nins = kDK ? L.nins : dins;
       const int ncol = kDK ? L.ncol : dn;
+      if (kDK && L.acc_merge) {  // stage = 128 queries x 64 columns: both 64-query chunks
+        for (int ins = 0; ins < nins; ++ins) {
+          uint32_t st;
+          if (!take(&st)) return false;
+          for (int k = 0; k < 8; ++k) {
+            const int qc = k >> 2, kk = k & 3;
+            const uint64_t ad = sdesc_sw128(ta + qc * kBox + kk * 32, 16, 1024);
+            const uint64_t bd = sdesc_sw128(st + qc * kBox + kk * 16 * 128, 64 * 128, 1024);
+            const uint32_t d = tmem + L.tmem_acc + s * (L.kw / 2) + ins * (ncol / 2);
+            mma_f16_ss<2>(d, ad, bd, idesc_acc, (g | k) ? 1u : 0u);
+          }
+          give();
+        }
+        commit_both(&t_empty[tb]);
+        return true;
+      }
       for (int qc = 0; qc < kTile / 64; ++qc)
         for (int ins = 0; ins < nins; ++ins) {
           uint32_t st;
@@ -948,11 +1033,13 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
 
 template <typename Kern>
 int launch_pair(Kern kern, const Layout& L, int pairs, const CUtensorMap& tq, const CUtensorMap& tk,
-                const CUtensorMap& tv, const CUtensorMap& tdy, const Params& p, cudaStream_t st) {
+                const CUtensorMap& tv, const CUtensorMap& tdy, const CUtensorMap& tacc, const Params& p,
+                cudaStream_t st) {
   const int smem = (L.smem < 120 * 1024 ? 120 * 1024 : L.smem) + 1024;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return record_cuda_error();
-  return launch_kernel(kern, dim3((unsigned)(2 * pairs), 1, 1), dim3(kThreads, 1, 1), smem, st, true, tq, tk, tv, tdy, p);
+  return launch_kernel(kern, dim3((unsigned)(2 * pairs), 1, 1), dim3(kThreads, 1, 1), smem, st, true, tq, tk, tv, tdy,
+                       tacc, p);
 }
 
 }  // namespace bwdm
@@ -999,35 +1086,45 @@ extern "C" int da_attn_bwd_mixed(const void* q, int64_t q_rows, int64_t q_base, 
   p.dq = dq; p.dk = dk; p.dv = dv; p.dscale = dscale; p.dweight = dweight; p.status = status;
   p.trace = debug_trace();
   const CUtensorMapDataType tdt = dtype == DA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  CUtensorMap tq, tk, tv, tdy;
+  CUtensorMap tq, tk, tv, tdy, tq128, tk128;
   int rc = make_tmap_2d(&tq, q, tdt, 2, R, q_rows, (uint64_t)R * 2, 64, 64);
   if (rc) return rc;
   rc = make_tmap_2d(&tk, k, tdt, 2, R, k_rows, (uint64_t)R * 2, 64, 64);
   if (rc) return rc;
-  rc = make_tmap_2d(&tv, v, tdt, 2, D, (uint64_t)B * T, (uint64_t)D * 2, 64, 64);
+  // 128-row boxes of the MN-major accumulation operands (K for dQ, Q for dK)
+  rc = make_tmap_2d(&tq128, q, tdt, 2, R, q_rows, (uint64_t)R * 2, 64, 128);
   if (rc) return rc;
-  rc = make_tmap_2d(&tdy, dy, tdt, 2, D, (uint64_t)B * T, (uint64_t)D * 2, 64, 64);
+  rc = make_tmap_2d(&tk128, k, tdt, 2, R, k_rows, (uint64_t)R * 2, 64, 128);
   if (rc) return rc;
+  {  // V and dY: [B*T, D] as (64-column block, row, block index); a box is 64 rows x 2 blocks
+    const uint64_t dims[3] = {64, (uint64_t)B * T, (uint64_t)D / 64};
+    const uint64_t strides[2] = {(uint64_t)D * 2, 128};
+    const uint32_t box[3] = {64, 64, 2};
+    rc = make_tmap_blocks(&tv, v, tdt, 2, 3, dims, strides, box);
+    if (rc) return rc;
+    rc = make_tmap_blocks(&tdy, dy, tdt, 2, 3, dims, strides, box);
+    if (rc) return rc;
+  }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int pairs = B * ((T + kTile - 1) / kTile);
   const bool bf16 = dtype == DA_BF16;
   // the query-parallel kernel runs first: without a given delta it produces it for the other two
   if (dq || dscale || !delta_given) {
     const Layout L = make_layout(0, maps, group, R, D);
-    rc = bf16 ? launch_pair(dq_mixed_kernel<__nv_bfloat16>, L, pairs, tq, tk, tv, tdy, p, st)
-              : launch_pair(dq_mixed_kernel<__half>, L, pairs, tq, tk, tv, tdy, p, st);
+    rc = bf16 ? launch_pair(dq_mixed_kernel<__nv_bfloat16>, L, pairs, tq, tk, tv, tdy, tk128, p, st)
+              : launch_pair(dq_mixed_kernel<__half>, L, pairs, tq, tk, tv, tdy, tk128, p, st);
     if (rc) return rc;
   }
   if (dk) {
     const Layout L = make_layout(1, maps, group, R, D);
-    rc = bf16 ? launch_pair(dkv_mixed_kernel<__nv_bfloat16, true>, L, pairs, tq, tk, tv, tdy, p, st)
-              : launch_pair(dkv_mixed_kernel<__half, true>, L, pairs, tq, tk, tv, tdy, p, st);
+    rc = bf16 ? launch_pair(dkv_mixed_kernel<__nv_bfloat16, true>, L, pairs, tq, tk, tv, tdy, tq128, p, st)
+              : launch_pair(dkv_mixed_kernel<__half, true>, L, pairs, tq, tk, tv, tdy, tq128, p, st);
     if (rc) return rc;
   }
   if (dv) {
     const Layout L = make_layout(2, maps, group, R, D);
-    rc = bf16 ? launch_pair(dkv_mixed_kernel<__nv_bfloat16, false>, L, pairs, tq, tk, tv, tdy, p, st)
-              : launch_pair(dkv_mixed_kernel<__half, false>, L, pairs, tq, tk, tv, tdy, p, st);
+    rc = bf16 ? launch_pair(dkv_mixed_kernel<__nv_bfloat16, false>, L, pairs, tq, tk, tv, tdy, tq128, p, st)
+              : launch_pair(dkv_mixed_kernel<__half, false>, L, pairs, tq, tk, tv, tdy, tq128, p, st);
   }
   return rc;
 }
