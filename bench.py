@@ -336,7 +336,7 @@ def kernel_rooflines(cfg, config: int, device):
     out = {}
     for name in ROOFLINE_KERNELS[cfg["mode"]]:
         run, flops = kernel_bench.make_case(name, config, device)
-        ms = kernel_bench.time_kernel(run, 20, device)
+        ms = kernel_bench.time_kernel(run, 20, device, graph=name in kernel_bench.GRAPH_CASES)
         out[name] = (ms, flops)
         del run
     torch.cuda.empty_cache()

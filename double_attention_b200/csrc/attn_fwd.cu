@@ -61,7 +61,9 @@ struct Layout {
   int tmem_s, s_cols, tmem_cols;
 };
 
-__host__ __device__ inline Layout make_layout(int maps, int group, int R, int D, bool mix) {
+// coarse: many query tiles per SM (throughput-bound), so key boxes of up to 32 KB; otherwise every
+// pair has only a few key tiles and 16 KB boxes let the first products start sooner.
+__host__ __device__ inline Layout make_layout(int maps, int group, int R, int D, bool mix, bool coarse = true) {
   Layout L;
   L.kw = maps * group * R;
   L.rpb = R / 64;
@@ -112,7 +114,7 @@ __host__ __device__ inline Layout make_layout(int maps, int group, int R, int D,
   // several column blocks per box (up to 32 KB) while the ring keeps two boxes, one per producer.
   L.kbb = 1;
   for (int b = 4; b >= 2; b /= 2)
-    if (L.rpb % b == 0 && L.nks / b >= 2 && b * L.k_stage <= 32768) {
+    if (L.rpb % b == 0 && L.nks / b >= 2 && b * L.k_stage <= (coarse ? 32768 : 16384)) {
       L.kbb = b;
       break;
     }
@@ -139,6 +141,7 @@ struct FwdParams {
   int64_t k_rows, k_base, k_sb, k_sbr;
   int B, T, R, D, maps, group, causal;
   int dsplit, Dp;  // value columns split over dsplit pairs of Dp columns each
+  int coarse;      // tile plan for many query tiles per SM (make_layout)
   int branch0[kMaxMaps];
   const float* scales;
   const float* weights;
@@ -163,7 +166,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
 
-  const Layout L = make_layout(p.maps, p.group, p.R, p.Dp, kMix);
+  const Layout L = make_layout(p.maps, p.group, p.R, p.Dp, kMix, p.coarse != 0);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const uint32_t rank = cluster_ctarank() & 1u;
   const int tiles = (p.T + 127) / 128;
@@ -620,7 +623,8 @@ int launch(const AttnFwdArgs& a, cudaStream_t st) {
   const long pairs = (long)a.B * ((a.T + 127) / 128);
   const int dsplit = value_split(pairs, a.D, sm_count());
   const int Dp = a.D / dsplit;
-  const Layout L = make_layout(a.maps, a.group, a.R, Dp, kMix);
+  const bool coarse = pairs * dsplit >= sm_count();
+  const Layout L = make_layout(a.maps, a.group, a.R, Dp, kMix, coarse);
   const CUtensorMapDataType qdt =
       std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap tq, tk, tv;
@@ -659,6 +663,7 @@ int launch(const AttnFwdArgs& a, cudaStream_t st) {
   p.causal = a.causal;
   p.dsplit = dsplit;
   p.Dp = Dp;
+  p.coarse = coarse ? 1 : 0;
   for (int s = 0; s < kMaxMaps; ++s) p.branch0[s] = a.branch0[s];
   p.scales = a.scales;
   p.weights = a.weights;

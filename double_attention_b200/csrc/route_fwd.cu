@@ -82,6 +82,7 @@ struct FwdParams {
   int* status;
   int* trace;           // optional progress markers (debug)
   int compact;          // wide kernel: the two-CTAs-per-SM layout (see wide_layout)
+  int coarse;           // wide kernel: tile plan for more pairs than SMs (see wide_layout)
 };
 
 // Exact fp32 recomputation of `count` listed rows (global indices g * rows + row) by one CTA (rare path).
@@ -563,7 +564,9 @@ constexpr int wide_threads() { return kMinBlocks == 2 ? 256 : 320; }
 // compact: a layout two CTAs of which fit one SM (<= 256 TMEM columns, ~108 KB of shared memory),
 // so that one pair's serial chain (setup, scores, softmax, epilogue) overlaps another's when there
 // are more pairs than SMs; 128-atom tiles and shorter rings.
-__host__ __device__ inline WideLayout wide_layout(int R, int M, bool compact = false) {
+// coarse: more pairs than SMs (throughput-bound): key boxes of up to 32 KB; with fewer pairs every
+// pair has few atom tiles and 16 KB boxes let the first products start sooner.
+__host__ __device__ inline WideLayout wide_layout(int R, int M, bool compact = false, bool coarse = true) {
   WideLayout L;
   L.kchunks = R / 64;
   L.nc = R < 256 ? R : 256;
@@ -597,7 +600,7 @@ __host__ __device__ inline WideLayout wide_layout(int R, int M, bool compact = f
   // several 64-column key chunks of the same atoms per box (<= 32 KB), keeping at least two slots
   L.kbb = 1;
   for (int b = 4; b >= 2; b /= 2)
-    if (L.kchunks % b == 0 && L.nks / b >= 2 && b * L.k_stage <= 32768) {
+    if (L.kchunks % b == 0 && L.nks / b >= 2 && b * L.k_stage <= (coarse ? 32768 : 16384)) {
       L.kbb = b;
       break;
     }
@@ -633,7 +636,7 @@ __global__ void __launch_bounds__(wide_threads<kMinBlocks>(), kMinBlocks) route_
   __shared__ int abort_flag, n_listed;
   __shared__ int listed[64];  // this CTA's rows whose mass fell below the fixed offset's range
 
-  const WideLayout L = wide_layout(kR, p.M, p.compact != 0);
+  const WideLayout L = wide_layout(kR, p.M, p.compact != 0, p.coarse != 0);
   constexpr int kRows = 64;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const uint32_t rank = cluster_ctarank() & 1u;
@@ -1039,7 +1042,9 @@ int launch_fwd(const RouteFwdArgs& a, cudaStream_t st) {
   const bool compact = kR >= 128 && kR <= 256 && pairs >= sm_count() && Wc.nk == 128 && Wc.nks >= 3 && Wc.nsb >= 2 &&
                        Wc.nsb >= Wc.npb && Wc.tmem_cols <= 256;
   p.compact = compact ? 1 : 0;
-  const WideLayout W = compact ? Wc : wide_layout(kR, (int)a.M);
+  const bool coarse = pairs >= sm_count();
+  p.coarse = coarse ? 1 : 0;
+  const WideLayout W = compact ? wide_layout(kR, (int)a.M, true, coarse) : wide_layout(kR, (int)a.M, false, coarse);
   const bool wide = kR >= 128 && W.nk != 0 && W.nks >= 3 && W.nsb >= 2 && W.nsb >= W.npb;
   if (wide) {  // re-encode the key / value maps with the wide tile's boxes
     {  // keys Dk^T [M, R]: (64-column block, atom, block index); a box is nk/2 atoms x kbb blocks

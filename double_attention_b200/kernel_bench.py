@@ -153,26 +153,37 @@ def make_case(kernel: str, config: int, device: torch.device):
     raise ValueError(f"unknown kernel {kernel!r}")
 
 
-def time_kernel(run, reps: int, device: torch.device) -> float:
-    """Mean device time (ms) of `run`, L2 flushed before each launch."""
+# cases that enqueue several launches (and memsets): timed as CUDA-graph replays so that host
+# enqueue work cannot fall inside the timed region
+GRAPH_CASES = ("attention_bwd",)
+
+
+def time_kernel(run, reps: int, device: torch.device, graph: bool = False) -> float:
+    """Mean device time (ms) of `run`, L2 flushed before each launch.
+
+    Each launch is bracketed by CUDA events on the launching stream right behind a 512 MiB flush
+    (~0.1 ms of device work, during which the host has long enqueued the events and the launch), so
+    the bracket holds the kernel and its launch latency only.  With `graph` the launches are
+    replayed from a CUDA graph instead (for multi-launch cases whose host enqueue takes longer).
+    """
     flush = torch.empty(512 << 20, dtype=torch.uint8, device=device)
     stream = torch.cuda.current_stream(device)
     for _ in range(3):
         run()
-    # capture the launch in a CUDA graph so host overhead cannot leak into the timing
-    graph = torch.cuda.CUDAGraph()
-    try:
-        side = torch.cuda.Stream(device)
-        side.wait_stream(stream)
-        with torch.cuda.stream(side):
-            run()
-        stream.wait_stream(side)
-        with torch.cuda.graph(graph):
-            run()
-        launch = graph.replay
-    except RuntimeError:  # not capturable: time eager launches (host overhead included)
-        torch.cuda.synchronize()
-        launch = run
+    launch = run
+    if graph:
+        g = torch.cuda.CUDAGraph()
+        try:
+            side = torch.cuda.Stream(device)
+            side.wait_stream(stream)
+            with torch.cuda.stream(side):
+                run()
+            stream.wait_stream(side)
+            with torch.cuda.graph(g):
+                run()
+            launch = g.replay
+        except RuntimeError:  # not capturable: time eager launches
+            torch.cuda.synchronize()
     events = []
     for _ in range(reps):
         flush.zero_()
@@ -198,7 +209,7 @@ def main(argv=None) -> int:
             raise SystemExit(f"unknown kernel {kernel!r}")
         run, flops = make_case(kernel, args.config, device)
         if args.time:
-            ms = time_kernel(run, args.reps, device)
+            ms = time_kernel(run, args.reps, device, graph=kernel in GRAPH_CASES)
             print(json.dumps({"kernel": kernel, "config": args.config, "ms": ms, "flops": flops,
                               "tflops": flops / (ms / 1e3) / 1e12}))
         else:
