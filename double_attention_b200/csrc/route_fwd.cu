@@ -558,8 +558,10 @@ constexpr int kWideMaxK = 8, kWideMaxV = 4, kWideMaxSB = 4, kWideMaxPB = 2;
 constexpr int kValueWarp = 6;
 constexpr int kPvWarp = 7;
 constexpr int kKeyWarp2 = 8, kValueWarp2 = 9;
-template <int kMinBlocks>
-constexpr int wide_threads() { return kMinBlocks == 2 ? 256 : 320; }
+// kLat: the latency layout for fewer pairs than SMs (one producer per stream, one interleaved MMA
+// issuer, probabilities stored chunk by chunk), warps 0-6 only.
+template <int kMinBlocks, bool kLat>
+constexpr int wide_threads() { return kLat ? 224 : (kMinBlocks == 2 ? 256 : 320); }
 
 // compact: a layout two CTAs of which fit one SM (<= 256 TMEM columns, ~108 KB of shared memory),
 // so that one pair's serial chain (setup, scores, softmax, epilogue) overlaps another's when there
@@ -622,8 +624,8 @@ __host__ __device__ inline WideLayout wide_layout(int R, int M, bool compact = f
   return L;
 }
 
-template <int kR, typename T, int kMinBlocks>
-__global__ void __launch_bounds__(wide_threads<kMinBlocks>(), kMinBlocks) route_fwd_wide_kernel(const __grid_constant__ CUtensorMap tq,
+template <int kR, typename T, int kMinBlocks, bool kLat>
+__global__ void __launch_bounds__(wide_threads<kMinBlocks, kLat>(), kMinBlocks) route_fwd_wide_kernel(const __grid_constant__ CUtensorMap tq,
                                                                 const __grid_constant__ CUtensorMap tdk,
                                                                 const __grid_constant__ CUtensorMap tdv,
                                                                 const FwdParams p) {
@@ -685,7 +687,7 @@ __global__ void __launch_bounds__(wide_threads<kMinBlocks>(), kMinBlocks) route_
   const uint32_t tmem = tmem_base;
   if (threadIdx.x == 0) trace_time(p.trace, 1);
 
-  constexpr int kProducers = kMinBlocks == 2 ? 1 : 2;  // per stream
+  constexpr int kProducers = (kMinBlocks == 2 || kLat) ? 1 : 2;  // per stream
   if (warp == 0 || (kProducers == 2 && warp == kKeyWarp2)) {
     // ---------------------------------------------------------------- key producers (both CTAs): warp 0
     // loads q and the even key boxes, warp 8 (if present) the odd ones
@@ -754,72 +756,86 @@ __global__ void __launch_bounds__(wide_threads<kMinBlocks>(), kMinBlocks) route_
         mma_commit<2>(mapa_shared(smem_u32(bar), 1));
       };
       const uint32_t qa = smem_u32(smem + L.off_q);
+      int kx = 0, kst = 0, vc = 0;  // key boxes consumed and current key slot; value stages consumed
+      auto issue_s = [&](int j) -> bool {  // S_j = q . Dk_j into score buffer j % nsb
+        const int sb = j % L.nsb;
+        if (j < 256) trace_at(ft, 1024 + 4 * j);
+        if (j >= L.nsb && !mbar_wait(&p_full[sb], ((j - L.nsb) / L.nsb) & 1u, ab, 22)) return false;
+        if (j < 256) trace_at(ft, 1025 + 4 * j);
+        const uint32_t d = tmem + L.tmem_s + (uint32_t)(sb * L.s_cols);
+        for (int c = 0; c < L.kchunks; ++c) {
+          const int cib = c % L.kbb;  // chunk inside the current box
+          if (cib == 0) {
+            kst = kx % L.kslots;
+            if (!mbar_wait(&k_full[kst], (kx / L.kslots) & 1u, ab, 23)) return false;
+            tc_fence_after();
+          }
+          const uint64_t ad0 = sdesc_sw128(qa + c * (kRows * 128), 16, 1024);
+          const uint64_t bd0 = sdesc_sw128(smem_u32(smem + L.off_k + (kst * L.kbb + cib) * L.k_stage), 16, 1024);
+#pragma unroll
+          for (int kin = 0; kin < 4; ++kin)  // +32 B per K step of 16 = +2 in the encoded address
+            mma_f16_ss<2>(d, ad0 + 2 * kin, bd0 + 2 * kin, idesc_s, (c | kin) ? 1u : 0u);
+          if (cib == L.kbb - 1) {
+            commit_both(&k_empty[kst]);
+            ++kx;
+          }
+        }
+        commit_both(&s_full[sb]);
+        if (j < 256) trace_at(ft, 1026 + 4 * j);
+        return true;
+      };
+      // P_j . Dv_j^T once probability tile j and its value rows are in shared memory.  The wait on
+      // p_full[j % nsb] cannot alias a later phase: tile j + nsb's probabilities need P buffer
+      // (j + nsb) % npb back, i.e. the product of tile j + nsb - npb >= j (nsb >= npb).
+      auto issue_pv = [&](int j) -> bool {
+        const int pb = j % L.npb;
+        if (j < 256) trace_at(ft, 2048 + 4 * j);
+        if (!mbar_wait(&p_full[j % L.nsb], (j / L.nsb) & 1u, ab, 24)) return false;
+        if (j < 256) trace_at(ft, 2049 + 4 * j);
+        const uint32_t pa = smem_u32(smem + L.off_p + pb * L.p_bytes);
+        for (int c = 0; c < nk / 64; ++c, ++vc) {
+          const int st = vc % L.nvs;
+          if (!mbar_wait(&v_full[st], (vc / L.nvs) & 1u, ab, 25)) return false;
+          tc_fence_after();
+          const uint32_t va = smem_u32(smem + L.off_v + st * L.v_stage);
+          const uint64_t ad0 = sdesc_sw128(pa + c * (kRows * 128), 16, 1024);
+          for (int i = 0; i < L.npv; ++i) {
+            const uint64_t bd0 = sdesc_sw128(va + i * ((L.nc / 2) * 128), 16, 1024);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              mma_f16_ss<2>(tmem + (uint32_t)(i * (L.nc / 2)), ad0 + 2 * kk, bd0 + 2 * kk, idesc_o,
+                            (j | c | kk) ? 1u : 0u);
+          }
+          commit_both(&v_empty[st]);
+        }
+        commit_both(&p_empty[pb]);
+        if (j < 256) trace_at(ft, 2050 + 4 * j);
+        return true;
+      };
       bool ok = mbar_wait(&q_full, 0, ab, 21);
       if (warp == 1) trace_time(p.trace, 2);
       tc_fence_after();
-      if (warp == 1) {
-        // score tiles in order; a score buffer is reused once the softmax has consumed its previous tile
-        int kx = 0, st = 0;  // key boxes consumed, current slot
-        for (int j = 0; ok && j < NJ; ++j) {
-          const int sb = j % L.nsb;
-          if (j < 256) trace_at(ft, 1024 + 4 * j);
-          if (j >= L.nsb && !mbar_wait(&p_full[sb], ((j - L.nsb) / L.nsb) & 1u, ab, 22)) { ok = false; break; }
-          if (j < 256) trace_at(ft, 1025 + 4 * j);
-          const uint32_t d = tmem + L.tmem_s + (uint32_t)(sb * L.s_cols);
-          for (int c = 0; ok && c < L.kchunks; ++c) {
-            const int cib = c % L.kbb;  // chunk inside the current box
-            if (cib == 0) {
-              st = kx % L.kslots;
-              if (!mbar_wait(&k_full[st], (kx / L.kslots) & 1u, ab, 23)) { ok = false; break; }
-              tc_fence_after();
-            }
-            const uint64_t ad0 = sdesc_sw128(qa + c * (kRows * 128), 16, 1024);
-            const uint64_t bd0 = sdesc_sw128(smem_u32(smem + L.off_k + (st * L.kbb + cib) * L.k_stage), 16, 1024);
-#pragma unroll
-            for (int kin = 0; kin < 4; ++kin)  // +32 B per K step of 16 = +2 in the encoded address
-              mma_f16_ss<2>(d, ad0 + 2 * kin, bd0 + 2 * kin, idesc_s, (c | kin) ? 1u : 0u);
-            if (cib == L.kbb - 1) {
-              commit_both(&k_empty[st]);
-              ++kx;
-            }
-          }
-          if (!ok) break;
-          commit_both(&s_full[sb]);
-          if (j < 256) trace_at(ft, 1026 + 4 * j);
+      if (!kLat) {
+        // many pairs per SM: the two products from their own threads, so neither waits behind the
+        // other's operand stream
+        if (warp == 1) {
+          for (int j = 0; ok && j < NJ; ++j) ok = issue_s(j);
+          trace_time(p.trace, 3);
+        } else {
+          for (int j = 0; ok && j < NJ; ++j) ok = issue_pv(j);
+          commit_both(&o_full);
+          mbar_wait_drain(&o_full, 0);  // every probability product (and so every score product) has completed
         }
-        trace_time(p.trace, 3);
-      } else {
-        // P_j . Dv_j^T once probability tile j and its value rows are in shared memory.  The wait on
-        // p_full[j % nsb] cannot alias a later phase: tile j + nsb's probabilities need P buffer
-        // (j + nsb) % npb back, i.e. the product of tile j + nsb - npb >= j (nsb >= npb).
-        int vc = 0;
+      } else if (warp == 1) {
+        // a few atom tiles per pair: one thread, scores up to nsb tiles ahead of the products
+        int next_s = 0;
         for (int j = 0; ok && j < NJ; ++j) {
-          const int pb = j % L.npb;
-          if (j < 256) trace_at(ft, 2048 + 4 * j);
-          if (!mbar_wait(&p_full[j % L.nsb], (j / L.nsb) & 1u, ab, 24)) { ok = false; break; }
-          if (j < 256) trace_at(ft, 2049 + 4 * j);
-          const uint32_t pa = smem_u32(smem + L.off_p + pb * L.p_bytes);
-          for (int c = 0; ok && c < nk / 64; ++c, ++vc) {
-            const int st = vc % L.nvs;
-            if (!mbar_wait(&v_full[st], (vc / L.nvs) & 1u, ab, 25)) { ok = false; break; }
-            tc_fence_after();
-            const uint32_t va = smem_u32(smem + L.off_v + st * L.v_stage);
-            const uint64_t ad0 = sdesc_sw128(pa + c * (kRows * 128), 16, 1024);
-            for (int i = 0; i < L.npv; ++i) {
-              const uint64_t bd0 = sdesc_sw128(va + i * ((L.nc / 2) * 128), 16, 1024);
-#pragma unroll
-              for (int kk = 0; kk < 4; ++kk)
-                mma_f16_ss<2>(tmem + (uint32_t)(i * (L.nc / 2)), ad0 + 2 * kk, bd0 + 2 * kk, idesc_o,
-                              (j | c | kk) ? 1u : 0u);
-            }
-            commit_both(&v_empty[st]);
-          }
-          if (!ok) break;
-          commit_both(&p_empty[pb]);
-          if (j < 256) trace_at(ft, 2050 + 4 * j);
+          while (ok && next_s < NJ && next_s < j + L.nsb) ok = issue_s(next_s++);
+          if (ok) ok = issue_pv(j);
         }
         commit_both(&o_full);
-        mbar_wait_drain(&o_full, 0);  // every probability product (and so every score product) has completed
+        trace_time(p.trace, 3);
+        mbar_wait_drain(&o_full, 0);
       }
     }
   } else {
@@ -871,7 +887,45 @@ __global__ void __launch_bounds__(wide_threads<kMinBlocks>(), kMinBlocks) route_
       if (arriver && j < 256) trace_at(ft, 3072 + 4 * j);
       if (ok && j > 0) ok = mbar_wait(&s_full[sb], (j / L.nsb) & 1u, ab, 32);
       if (arriver && j < 256) trace_at(ft, 3073 + 4 * j);
+      if (kLat && ok && j >= L.npb) ok = mbar_wait(&p_empty[pb], ((j - L.npb) / L.npb) & 1u, ab, 33);
       ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-collective
+      if constexpr (kLat) {  // P buffer already free: each 32-atom chunk is stored as soon as it is formed
+        if (ok) {
+          tc_fence_after();
+          const uint32_t pa = smem_u32(smem + L.off_p + pb * L.p_bytes);
+          for (int ch = 0; ch < nch; ++ch) {
+            float v[32];
+            tmem_ld32(tmem + lane_base + L.tmem_s + (uint32_t)(sb * L.s_cols + ch * 32), v);
+            tmem_wait_ld();
+            const int kc = half * hc + ch * 32;
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 32; i += 2) {
+              const float a = v[i] * scale, b = v[i + 1] * scale;
+              if (want_argmax) {
+                const int base = jj * nk + kc + i;
+                if (a > mx || (a == mx && base < amax)) amax = base;
+                const float ma = fmaxf(mx, a);
+                if (b > ma || (b == ma && base + 1 < amax)) amax = base + 1;
+              }
+              mx = fmaxf(mx, fmaxf(a, b));
+              const float ea = ex2(a - bound), eb = ex2(b - bound);
+              sum += ea + eb;
+              pk[i / 2] = pack_bf16x2(ea, eb);
+            }
+            const uint32_t box = pa + (kc >> 6) * (kRows * 128);
+            const int cb = (kc & 63) >> 3;
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              st_shared_v4(box + sw128_offset(r, cb + e), pk[4 * e], pk[4 * e + 1], pk[4 * e + 2], pk[4 * e + 3]);
+          }
+          fence_proxy_async();
+        }
+        tc_fence_before();
+        named_bar_sync(1, 128);
+        if (arriver) mbar_arrive_cluster(pf_leader + sb * 8);
+        continue;
+      }
       uint32_t packed[kMaxCh][16];
       if (ok) {
         tc_fence_after();
@@ -1064,12 +1118,15 @@ int launch_fwd(const RouteFwdArgs& a, cudaStream_t st) {
     }
     if ((a.M + kR + 64) * 4 > W.smem) return DA_ERR_SHAPE;  // repair scratch must fit
   }
+  const bool lat = !compact && !coarse;
   auto kern = !wide ? route_fwd_kernel<kR, T>
-                    : (compact ? route_fwd_wide_kernel<kR, T, 2> : route_fwd_wide_kernel<kR, T, 1>);
+                    : (compact ? route_fwd_wide_kernel<kR, T, 2, false>
+                               : (lat ? route_fwd_wide_kernel<kR, T, 1, true> : route_fwd_wide_kernel<kR, T, 1, false>));
   const int smem = (wide ? W.smem : C::kSmem) + 1024;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return record_cuda_error();
-  const int threads = !wide ? C::kThreads : (compact ? wide_threads<2>() : wide_threads<1>());
+  const int threads = !wide ? C::kThreads
+                            : (compact ? wide_threads<2, false>() : (lat ? wide_threads<1, true>() : wide_threads<1, false>()));
   return launch_kernel(kern, dim3((unsigned)(2 * pairs), 1, 1), dim3(threads, 1, 1), smem, st, true, tq, tdk, tdv, p);
 }
 
