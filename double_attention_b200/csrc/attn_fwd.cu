@@ -39,6 +39,9 @@ namespace attn {
 // products have their own issuing threads, so a P.V product never queues behind the key chunks
 // of a score tile further ahead (and the reverse).
 constexpr int kThreads = 320;
+// kLat (fewer query tiles than SMs): one producer per stream, warps 0-7 only
+template <bool kLat>
+constexpr int fwd_threads() { return kLat ? 256 : kThreads; }
 constexpr int kValueWarp = 6;
 constexpr int kPvWarp = 7;
 constexpr int kKeyWarp2 = 8, kValueWarp2 = 9;  // the second producer of each stream
@@ -153,8 +156,8 @@ struct FwdParams {
   int* trace;
 };
 
-template <typename T, bool kMix>
-__global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_constant__ CUtensorMap tq,
+template <typename T, bool kMix, bool kLat>
+__global__ void __launch_bounds__(fwd_threads<kLat>(), 1) attn_fwd_kernel(const __grid_constant__ CUtensorMap tq,
                                                                const __grid_constant__ CUtensorMap tk,
                                                                const __grid_constant__ CUtensorMap tv,
                                                                const FwdParams p) {
@@ -224,7 +227,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   grid_launch_dependents();
   const uint32_t tmem = tmem_base;
 
-  if (warp == 0 || warp == kKeyWarp2) {
+  constexpr int kProd = kLat ? 1 : 2;  // producers per stream
+  if (warp == 0 || (!kLat && warp == kKeyWarp2)) {
     // ---------------------------------------------------------------- key producers (both CTAs): warp 0
     // takes the even key boxes (and loads q), warp 8 the odd ones
     if (lane == 0) {
@@ -248,7 +252,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         const int rem = u % sweep_units, j = rem / maps, s = rem % maps;
         bool ok = true;
         for (int c = 0; c < L.kchunks; c += L.kbb, ++kx) {
-          if ((kx & 1) != pi) continue;
+          if (kx % kProd != pi) continue;
           const int st = kx % L.kslots;
           if (!mbar_wait(&k_empty[st], ((kx / L.kslots) & 1u) ^ 1u, ab, 11)) { ok = false; break; }
           if (rank == 0) mbar_arrive_expect_tx(&k_full[st], 2 * box_bytes);
@@ -262,10 +266,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       if (rank == 0) {  // drain: none of this producer's loads may be in flight at teardown
         if (pi == 0) mbar_wait_drain(&q_full, 0);
         for (int c = (kx > L.kslots ? kx - L.kslots : 0); c < kx; ++c)
-          if ((c & 1) == pi) mbar_wait_drain(&k_full[c % L.kslots], (c / L.kslots) & 1u);
+          if (c % kProd == pi) mbar_wait_drain(&k_full[c % L.kslots], (c / L.kslots) & 1u);
       }
     }
-  } else if (warp == kValueWarp || warp == kValueWarp2) {
+  } else if (warp == kValueWarp || (!kLat && warp == kValueWarp2)) {
     // ---------------------------------------------------------------- value producers: warp 6 even
     // stages, warp 9 odd ones
     if (lane == 0) {
@@ -276,7 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       for (int v = 0; v < nj; ++v) {
         bool ok = true;
         for (int c = 0; c < nk / 64; ++c, ++vc) {
-          if ((vc & 1) != pi) continue;
+          if (vc % kProd != pi) continue;
           const int st = vc % L.nvs;
           if (!mbar_wait(&v_empty[st], ((vc / L.nvs) & 1u) ^ 1u, ab, 12)) { ok = false; break; }
           if (rank == 0) mbar_arrive_expect_tx(&v_full[st], 2 * L.v_stage);
@@ -289,7 +293,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       }
       if (rank == 0)
         for (int c = (vc > L.nvs ? vc - L.nvs : 0); c < vc; ++c)
-          if ((c & 1) == pi) mbar_wait_drain(&v_full[c % L.nvs], (c / L.nvs) & 1u);
+          if (c % kProd == pi) mbar_wait_drain(&v_full[c % L.nvs], (c / L.nvs) & 1u);
     }
   } else if (warp == 1 || warp == kPvWarp) {
     // ---------------------------------------------------------------- MMA issuers (leader): scores on warp 1,
@@ -673,11 +677,12 @@ int launch(const AttnFwdArgs& a, cudaStream_t st) {
   p.lse = a.lse;
   p.status = a.status;
   p.trace = debug_trace();
-  auto kern = attn_fwd_kernel<T, kMix>;
+  auto kern = coarse ? attn_fwd_kernel<T, kMix, false> : attn_fwd_kernel<T, kMix, true>;
   const int smem = L.smem + 1024;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return record_cuda_error();
-  return launch_kernel(kern, dim3((unsigned)(2 * pairs * dsplit), 1, 1), dim3(kThreads, 1, 1), smem, st, true, tq, tk, tv, p);
+  return launch_kernel(kern, dim3((unsigned)(2 * pairs * dsplit), 1, 1),
+                       dim3(coarse ? fwd_threads<false>() : fwd_threads<true>(), 1, 1), smem, st, true, tq, tk, tv, p);
 }
 
 int attn_fwd(const AttnFwdArgs& a, cudaStream_t st) {
