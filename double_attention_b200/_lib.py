@@ -64,6 +64,9 @@ SIGNATURES: dict[str, list] = {
     "da_route_var_input_bwd": [_p, _p, _i64, _p, _i64, _i32, _i32, _i32, _f32, _p, _i64, _p],
     "da_route_fwd": [_p, _i64, _i64, _i64, _i32, _i64, _i64, _i64, _i32, _p, _p, _p, _p, _f32, _i32, _i32,
                      _p, _p, _p, _p, _p, _i32, _p, _p],
+    "da_add_layernorm_fwd": [_p, _p, _i32, _p, _p, _i64, _i64, _f32, _p, _p, _i32, _p, _p, _p],
+    "da_add_layernorm_bwd": [_p, _i32, _p, _p, _p, _p, _p, _i64, _i64, _p, _p, _i32, _p, _i32, _p, _p, _p],
+    "da_layernorm_bwd_blocks": [_i64],
 }
 
 _lock = threading.Lock()

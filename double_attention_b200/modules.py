@@ -243,8 +243,15 @@ class DoubleAttentionBlock(nn.Module):
 
     def forward(self, x: Tensor, bank: SharedDictionaryBank, *,
                 normalized_dictionary: tuple[Tensor, Tensor] | None = None) -> Tensor:
-        x = x + self.attention(self.attention_norm(x), bank=bank, normalized_dictionary=normalized_dictionary)
-        normalized_x = self.feedforward_norm(x)
+        if ops.layernorm_supported(x, self.attention_norm, self.feedforward_norm):
+            # fp32 residual stream: each norm (and the residual add before the second) is one kernel that
+            # writes the rows in the dtype the next Linear reads
+            branch = self.attention(ops.layernorm(x, self.attention_norm), bank=bank,
+                                    normalized_dictionary=normalized_dictionary)
+            x, normalized_x = ops.add_layernorm(x, branch, self.feedforward_norm)
+        else:
+            x = x + self.attention(self.attention_norm(x), bank=bank, normalized_dictionary=normalized_dictionary)
+            normalized_x = self.feedforward_norm(x)
         if not self.attention.config.q_dictionary_feedforward:
             return x + self.feedforward(normalized_x)
         if normalized_dictionary is None:
@@ -315,8 +322,11 @@ class DoubleAttentionLM(nn.Module):
         if length > self.max_sequence_length:
             raise ValueError(f"sequence length {length} exceeds configured maximum {self.max_sequence_length}")
         positions = torch.arange(length, device=token_ids.device)
-        hidden = self.token_embedding(token_ids) + self.position_embedding(positions)[None]
-        logits = self.lm_head(self.final_norm(self.stack(hidden)))
+        hidden = self.stack(self.token_embedding(token_ids) + self.position_embedding(positions)[None])
+        if ops.layernorm_supported(hidden, self.final_norm):
+            logits = self.lm_head(ops.layernorm(hidden, self.final_norm))
+        else:
+            logits = self.lm_head(self.final_norm(hidden))
         loss = None
         if targets is not None:
             if targets.shape != token_ids.shape:

@@ -1075,3 +1075,113 @@ def qk_projection(x: Tensor, fused_weight: Tensor) -> Tensor:
     if not x2d.is_contiguous():
         x2d = x2d.contiguous()
     return _Projection.apply(x2d, fused_weight.contiguous())
+
+
+# ----------------------------------------------------------------------------- residual add + LayerNorm
+# The glue around the block (modules.py:294-356, :415-460): ``x + branch`` on the fp32 residual
+# stream followed by ``nn.LayerNorm``.  One kernel adds, normalises and writes the normalised rows
+# directly in the dtype the next Linear reads (the autocast dtype under autocast, else x's dtype),
+# so the reference's separate add, fp32 LayerNorm output and autocast cast become one pass; the
+# backward adds the residual gradient and writes the branch gradient in the same pass.
+LAYERNORM_WIDTHS = (256, 512, 768, 1024)
+
+
+def layernorm_supported(x: Tensor, *norms) -> bool:
+    """Whether the fused kernels cover ``norm(x)`` for every given ``nn.LayerNorm``."""
+    if not (x.is_cuda and x.dtype == torch.float32 and x.shape[-1] in LAYERNORM_WIDTHS):
+        return False
+    for n in norms:
+        if (n.weight is None or n.bias is None or n.weight.dtype != torch.float32
+                or tuple(n.normalized_shape) != (x.shape[-1],)):
+            return False
+    return True
+
+
+def _layernorm_out_dtype(x: Tensor) -> torch.dtype:
+    if torch.is_autocast_enabled("cuda"):
+        return torch.get_autocast_dtype("cuda")
+    return x.dtype
+
+
+def _ln_forward(x: Tensor, branch: Tensor | None, weight: Tensor, bias: Tensor, eps: float,
+                out_dtype: torch.dtype) -> tuple[Tensor | None, Tensor, Tensor, Tensor]:
+    d = x.shape[-1]
+    rows = x.numel() // d
+    x_out = torch.empty_like(x) if branch is not None else None
+    y = torch.empty(x.shape, dtype=out_dtype, device=x.device)
+    mean = torch.empty(rows, dtype=torch.float32, device=x.device)
+    rstd = torch.empty(rows, dtype=torch.float32, device=x.device)
+    call("da_add_layernorm_fwd", x.data_ptr(), ptr(branch), dtype_code(branch.dtype) if branch is not None else 0,
+         weight.data_ptr(), bias.data_ptr(), rows, d, float(eps), ptr(x_out), y.data_ptr(), dtype_code(out_dtype),
+         mean.data_ptr(), rstd.data_ptr(), stream_ptr(x.device))
+    return x_out, y, mean, rstd
+
+
+def _ln_backward(ctx, d_res: Tensor | None, dy: Tensor | None):
+    x_norm, mean, rstd, weight = ctx.saved_tensors
+    need = ctx.needs_input_grad
+    d = x_norm.shape[-1]
+    rows = x_norm.numel() // d
+    if dy is None:  # y unused downstream: the residual gradient passes through
+        dx = d_res if d_res is not None else torch.zeros_like(x_norm)
+        db = dx.to(ctx.branch_dtype) if ctx.has_branch and need[1] else None
+        return dx, db, None, None
+    dy = dy.contiguous()
+    d_res = None if d_res is None else d_res.contiguous()
+    dx = torch.empty_like(x_norm)
+    db = torch.empty(x_norm.shape, dtype=ctx.branch_dtype, device=x_norm.device) if ctx.has_branch and need[1] else None
+    blocks = int(_lib.lib().da_layernorm_bwd_blocks(rows))
+    partial = torch.empty((blocks, 2, d), dtype=torch.float32, device=x_norm.device)
+    wi = 2 if ctx.has_branch else 1
+    dgamma = torch.empty(d, dtype=torch.float32, device=x_norm.device) if need[wi] else None
+    dbeta = torch.empty(d, dtype=torch.float32, device=x_norm.device) if need[wi + 1] else None
+    call("da_add_layernorm_bwd", dy.data_ptr(), dtype_code(dy.dtype), ptr(d_res), x_norm.data_ptr(), mean.data_ptr(),
+         rstd.data_ptr(), weight.data_ptr(), rows, d, dx.data_ptr(), ptr(db),
+         dtype_code(ctx.branch_dtype) if ctx.has_branch else 0, partial.data_ptr(), blocks, ptr(dgamma), ptr(dbeta),
+         stream_ptr(x_norm.device))
+    return dx, db, dgamma, dbeta
+
+
+class _LayerNormCast(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight, bias, eps, out_dtype):
+        _, y, mean, rstd = _ln_forward(x, None, weight, bias, eps, out_dtype)
+        ctx.save_for_backward(x, mean, rstd, weight)
+        ctx.has_branch, ctx.branch_dtype = False, None
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        dx, _, dgamma, dbeta = _ln_backward(ctx, None, dy)
+        return dx, dgamma, dbeta, None, None
+
+
+class _AddLayerNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, branch, weight, bias, eps, out_dtype):
+        x_out, y, mean, rstd = _ln_forward(x, branch, weight, bias, eps, out_dtype)
+        ctx.save_for_backward(x_out, mean, rstd, weight)
+        ctx.has_branch, ctx.branch_dtype = True, branch.dtype
+        return x_out, y
+
+    @staticmethod
+    def backward(ctx, d_xout, dy):
+        dx, db, dgamma, dbeta = _ln_backward(ctx, d_xout, dy)
+        return dx, db, dgamma, dbeta, None, None
+
+
+def layernorm(x: Tensor, norm) -> Tensor:
+    """``norm(x)`` for an ``nn.LayerNorm`` over the last dimension of fp32 ``x``, written in the dtype the
+    next Linear reads (the autocast dtype under autocast)."""
+    xc = x if x.is_contiguous() else x.contiguous()
+    return _LayerNormCast.apply(xc, norm.weight, norm.bias, norm.eps, _layernorm_out_dtype(x))
+
+
+def add_layernorm(x: Tensor, branch: Tensor, norm) -> tuple[Tensor, Tensor]:
+    """``(x + branch, norm(x + branch))``: the residual update (fp32) and its normalised rows (in the
+    dtype the next Linear reads)."""
+    if branch.shape != x.shape:
+        raise ValueError(f"branch shape {tuple(branch.shape)} does not match the residual {tuple(x.shape)}")
+    xc = x if x.is_contiguous() else x.contiguous()
+    bc = branch if branch.is_contiguous() else branch.contiguous()
+    return _AddLayerNorm.apply(xc, bc, norm.weight, norm.bias, norm.eps, _layernorm_out_dtype(x))

@@ -300,6 +300,27 @@ DA_API int da_gemm_splitk_grouped(const void* A, int64_t lda, int64_t a_group_co
                                   float* C, int64_t ldc, int64_t M, int64_t N, int64_t K_group, int groups, int dtype,
                                   int splits, int* status, void* stream);
 
+/* ---- residual add + LayerNorm around the block -----------------------
+ * Replaces x + branch followed by nn.LayerNorm in DoubleAttentionBlock.forward
+ * (modules.py:294-356) and the final norm of DoubleAttentionLM (modules.py:415-460).
+ * Forward: x_out = x + branch (fp32 [rows, D]; branch in branch_dtype, or null,
+ * then x_out is not written and x itself is normalised), y = LayerNorm(x_out) *
+ * gamma + beta written in y_dtype, per-row mean and rstd (fp32 [rows]).
+ * D in {256, 512, 768, 1024}; every pointer 16-byte aligned. */
+DA_API int da_add_layernorm_fwd(const float* x, const void* branch, int branch_dtype, const float* gamma,
+                                const float* beta, int64_t rows, int64_t D, float eps, float* x_out, void* y,
+                                int y_dtype, float* mean, float* rstd, void* stream);
+/* Backward: dx = d_res (fp32, or null for 0) + LayerNorm backward of dy (in
+ * dy_dtype); d_branch (optional, branch_dtype) = dx; dgamma, dbeta (fp32 [D],
+ * optional) written from per-block partial sums in `partial`, a caller-provided
+ * fp32 buffer of [partial_blocks, 2, D] with partial_blocks =
+ * da_layernorm_bwd_blocks(rows) (DA_ERR_WORKSPACE otherwise). */
+DA_API int da_layernorm_bwd_blocks(int64_t rows);
+DA_API int da_add_layernorm_bwd(const void* dy, int dy_dtype, const float* d_res, const float* x_out,
+                                const float* mean, const float* rstd, const float* gamma, int64_t rows, int64_t D,
+                                float* dx, void* d_branch, int branch_dtype, float* partial, int partial_blocks,
+                                float* dgamma, float* dbeta, void* stream);
+
 /* ---- building-block check -------------------------------------------
  * No reference counterpart: D[128, n] = A[128, k] * B^T computed by one
  * tcgen05 tile (cta_group 1 or 2) for testing the descriptor layouts.
