@@ -244,16 +244,28 @@ class DoubleAttentionBlock(nn.Module):
     def forward(self, x: Tensor, bank: SharedDictionaryBank, *,
                 normalized_dictionary: tuple[Tensor, Tensor] | None = None) -> Tensor:
         if ops.layernorm_supported(x, self.attention_norm, self.feedforward_norm):
-            # fp32 residual stream: each norm (and the residual add before the second) is one kernel that
-            # writes the rows in the dtype the next Linear reads
-            branch = self.attention(ops.layernorm(x, self.attention_norm), bank=bank,
-                                    normalized_dictionary=normalized_dictionary)
-            x, normalized_x = ops.add_layernorm(x, branch, self.feedforward_norm)
+            x, branch = self._forward_fused(x, None, bank, normalized_dictionary)
+            return x + branch
+        x = x + self.attention(self.attention_norm(x), bank=bank, normalized_dictionary=normalized_dictionary)
+        return x + self._feedforward_branch(self.feedforward_norm(x), bank, normalized_dictionary)
+
+    def _forward_fused(self, x: Tensor, pending: Tensor | None, bank: SharedDictionaryBank,
+                       normalized_dictionary: tuple[Tensor, Tensor] | None) -> tuple[Tensor, Tensor]:
+        """The block on the fp32 residual stream with fused norms: ``x + pending`` (the previous block's
+        feed-forward branch, not yet added) is normalised by the same kernel that adds it; returns the
+        residual after the attention branch and this block's feed-forward branch, still to be added."""
+        if pending is None:
+            normalized_x = ops.layernorm(x, self.attention_norm)
         else:
-            x = x + self.attention(self.attention_norm(x), bank=bank, normalized_dictionary=normalized_dictionary)
-            normalized_x = self.feedforward_norm(x)
+            x, normalized_x = ops.add_layernorm(x, pending, self.attention_norm)
+        branch = self.attention(normalized_x, bank=bank, normalized_dictionary=normalized_dictionary)
+        x, normalized_x = ops.add_layernorm(x, branch, self.feedforward_norm)
+        return x, self._feedforward_branch(normalized_x, bank, normalized_dictionary)
+
+    def _feedforward_branch(self, normalized_x: Tensor, bank: SharedDictionaryBank,
+                            normalized_dictionary: tuple[Tensor, Tensor] | None) -> Tensor:
         if not self.attention.config.q_dictionary_feedforward:
-            return x + self.feedforward(normalized_x)
+            return self.feedforward(normalized_x)
         if normalized_dictionary is None:
             dictionary_key, _ = bank.normalized(self.attention.config.eps)
         else:
@@ -262,7 +274,7 @@ class DoubleAttentionBlock(nn.Module):
         if dictionary_key.dtype != query.dtype:
             dictionary_key = dictionary_key.to(query.dtype)
         hidden = F.linear(query, dictionary_key.transpose(0, 1).contiguous())
-        return x + self.feedforward(hidden)
+        return self.feedforward(hidden)
 
 
 class DoubleAttentionStack(nn.Module):
@@ -292,11 +304,22 @@ class DoubleAttentionStack(nn.Module):
         # One normalisation per bank per forward; every block of the group
         # reuses it, so gradients accumulate before one normalisation
         # backward (modules.py:398-412).
+        x, pending = self._forward_pending(x)
+        return x if pending is None else x + pending
+
+    def _forward_pending(self, x: Tensor) -> tuple[Tensor, Tensor | None]:
+        """Runs the blocks; with the fused norms the last block's feed-forward branch is returned
+        unadded (``pending``), so that a following norm can add it in its own kernel."""
         normalized = tuple(bank.normalized(self.config.eps) for bank in self.banks)
+        fused = all(ops.layernorm_supported(x, b.attention_norm, b.feedforward_norm) for b in self.blocks)
+        pending = None
         for index, block in enumerate(self.blocks):
             bank_index = min(index // self.dictionary_group_size, len(self.banks) - 1)
-            x = block(x, self.banks[bank_index], normalized_dictionary=normalized[bank_index])
-        return x
+            if fused:
+                x, pending = block._forward_fused(x, pending, self.banks[bank_index], normalized[bank_index])
+            else:
+                x = block(x, self.banks[bank_index], normalized_dictionary=normalized[bank_index])
+        return x, pending
 
 
 class DoubleAttentionLM(nn.Module):
@@ -322,11 +345,17 @@ class DoubleAttentionLM(nn.Module):
         if length > self.max_sequence_length:
             raise ValueError(f"sequence length {length} exceeds configured maximum {self.max_sequence_length}")
         positions = torch.arange(length, device=token_ids.device)
-        hidden = self.stack(self.token_embedding(token_ids) + self.position_embedding(positions)[None])
-        if ops.layernorm_supported(hidden, self.final_norm):
-            logits = self.lm_head(ops.layernorm(hidden, self.final_norm))
+        hidden, pending = self.stack._forward_pending(
+            self.token_embedding(token_ids) + self.position_embedding(positions)[None])
+        if pending is not None and ops.layernorm_supported(hidden, self.final_norm):
+            logits = self.lm_head(ops.add_layernorm(hidden, pending, self.final_norm)[1])
         else:
-            logits = self.lm_head(self.final_norm(hidden))
+            if pending is not None:
+                hidden = hidden + pending
+            if ops.layernorm_supported(hidden, self.final_norm):
+                logits = self.lm_head(ops.layernorm(hidden, self.final_norm))
+            else:
+                logits = self.lm_head(self.final_norm(hidden))
         loss = None
         if targets is not None:
             if targets.shape != token_ids.shape:
