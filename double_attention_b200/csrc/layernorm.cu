@@ -195,18 +195,29 @@ __global__ void __launch_bounds__(kLnWarps * 32) add_ln_bwd_kernel(const void* d
   }
 }
 
-// d gamma, d beta: sums of the [blocks, 2, D] partials over blocks (one thread per output).
+// d gamma, d beta: sums of the [blocks, 2, D] partials over blocks.  One CTA per 32 output columns
+// of the 2 x D outputs: its 8 warps split the block range (lane = column, coalesced rows), then the
+// 8 partial sums are added in a fixed order (deterministic).
 __global__ void __launch_bounds__(256) ln_partial_sum_kernel(const float* __restrict__ partial, int blocks, int D,
                                                              float* __restrict__ dgamma, float* __restrict__ dbeta) {
+  __shared__ float red[8][32];
   grid_dependency_wait();
   grid_launch_dependents();
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= 2 * D) return;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int i = blockIdx.x * 32 + lane;  // output index in [0, 2 D)
   const int which = i / D, col = i % D;
   float t = 0.f;
-  for (int k = 0; k < blocks; ++k) t += partial[((size_t)k * 2 + which) * D + col];
-  float* out = which == 0 ? dgamma : dbeta;
-  if (out) out[col] = t;
+  if (i < 2 * D)
+    for (int k = w; k < blocks; k += 8) t += partial[((size_t)k * 2 + which) * D + col];
+  red[w][lane] = t;
+  __syncthreads();
+  if (w == 0 && i < 2 * D) {
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) s += red[k][lane];
+    float* out = which == 0 ? dgamma : dbeta;
+    if (out) out[col] = s;
+  }
 }
 
 inline int ln_blocks(int64_t rows) {
@@ -270,6 +281,6 @@ extern "C" int da_add_layernorm_bwd(const void* dy, int dy_dtype, const float* d
   if (rc) return rc;
   if (!dgamma && !dbeta) return DA_OK;
   const int n = 2 * (int)D;
-  return launch_kernel(ln_partial_sum_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, false,
+  return launch_kernel(ln_partial_sum_kernel, dim3((unsigned)((n + 31) / 32)), dim3(256), 0, st, false,
                        (const float*)partial, partial_blocks, (int)D, dgamma, dbeta);
 }
