@@ -992,8 +992,8 @@ class _Projection(torch.autograd.Function):
             dx = torch.empty(m, k, dtype=x2d.dtype, device=x2d.device)
             gemm(dout, False, weight, True, m, k, n, dx)          # dX = dC . W
         if ctx.needs_input_grad[1]:
-            dw = torch.empty(n, k, dtype=torch.float32, device=x2d.device)
-            gemm(dout, True, x2d, True, n, k, m, dw)              # dW = dC^T . X (fp32)
+            dw = torch.zeros(n, k, dtype=torch.float32, device=x2d.device)
+            gemm_splitk(dout, dout.stride(0), True, x2d, x2d.stride(0), True, n, k, m, dw)  # dW = dC^T . X, rows split
             dw = dw.to(weight.dtype)
         return dx, dw
 
@@ -1044,8 +1044,10 @@ class _QKVProjection(torch.autograd.Function):
                 dx = torch.empty(m, k, dtype=dt, device=x2d.device)
                 gemm(dproj, False, torch.cat((wq, wk), 0), True, m, k, 2 * hr, dx)   # dX = dC . [Wq; Wk]
             if need[1] or need[2]:
-                dw = torch.empty(2 * hr, k, dtype=torch.float32, device=x2d.device)
-                gemm(dproj, True, x2d, True, 2 * hr, k, m, dw)                       # dW = dC^T . X (fp32)
+                # dW = dC^T . X (fp32): a [2HR, K] output of a few tiles over all B*T rows, so the row
+                # dimension is split over CTAs (partial sums added in fp32)
+                dw = torch.zeros(2 * hr, k, dtype=torch.float32, device=x2d.device)
+                gemm_splitk(dproj, dproj.stride(0), True, x2d, x2d.stride(0), True, 2 * hr, k, m, dw)
                 dwq, dwk = dw[:hr].to(wq.dtype), dw[hr:].to(wk.dtype)
         if dvalue is not None:
             dv = dvalue.to(dt)
