@@ -42,6 +42,9 @@ namespace bwdm {
 constexpr int kThreads = 320;
 constexpr int kDpWarp = 6;
 constexpr int kProd2 = 8, kDpProd2 = 9;
+// dQ kernel: one producer per ring and a second softmax warpgroup (warps 8-11) instead: its second
+// sweep is bound by the softmax's per-row arithmetic, and 384 threads x 168 registers fit the SM
+constexpr int kDqThreads = 384, kDqProd = 1, kDqSoftmax2 = 8;
 constexpr int kRows = 64;      // rows (queries or keys) per CTA
 constexpr int kTile = 128;     // columns (keys or queries) per tile and pair
 constexpr int kStage = 16384;  // main ring stage bytes
@@ -131,7 +134,7 @@ DA_DEV void load_map_chunk(const CUtensorMap* tm, const MapRows& m, const Params
 
 // =============================================================================== dQ kernel
 template <typename T>
-__global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_constant__ CUtensorMap tq,
+__global__ void __launch_bounds__(kDqThreads, 1) dq_mixed_kernel(const __grid_constant__ CUtensorMap tq,
                                                                const __grid_constant__ CUtensorMap tk,
                                                                const __grid_constant__ CUtensorMap tv,
                                                                const __grid_constant__ CUtensorMap tdy,
@@ -205,10 +208,10 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
   const int tq_row = t0 + 64 * (int)rank;
   const int dy_row = (int)min((int64_t)b * p.T + tq_row, rowsBT - 1);
   const int dps = sweeps * nj;  // dP products: one per key tile and sweep
-  if ((warp == 0 || warp == kProd2) && lane == 0) {
+  if (warp == 0 && lane == 0) {
     // ---------------------------------------------------------------- TMA producers: Q (warp 0), then K
     // for S and dQ, even stages from warp 0 and odd ones from warp 8
-    const int pi = warp == 0 ? 0 : 1;
+    const int pi = 0;
     prefetch_tmap(&tk);
     if (pi == 0) {
       prefetch_tmap(&tq);
@@ -230,7 +233,7 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
     auto emit_s = [&](int u) {  // key rows of map s for this CTA's 64 keys
       const int krow0 = unit_j(u) * kTile + 64 * (int)rank;
       for (int cc = 0; ok && cc < L.kw / 128; ++cc, ++it) {
-        if ((it & 1) != pi) continue;
+        if ((it % kDqProd) != pi) continue;
         uint8_t* dst = stage(2 * kBox);
         if (!ok) return;
         load_map_chunk(&tk, km, p, stage_bar(), dst, b, unit_s(u), cc, 2, krow0);
@@ -240,7 +243,7 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
       const int per = (L.ncol / 2) / 64, s = unit_s(u), j = unit_j(u);
       if (L.acc_merge) {  // one stage per N block: a 128-key x 64-column box
         for (int ins = 0; ok && ins < L.nins; ++ins, ++it) {
-          if ((it & 1) != pi) continue;
+          if ((it % kDqProd) != pi) continue;
           uint8_t* dst = stage(2 * kBox);
           if (!ok) return;
           const int mb = (ins * L.ncol + (int)rank * (L.ncol / 2)) / 64;
@@ -252,7 +255,7 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
       }
       for (int kc = 0; ok && kc < kTile / 64; ++kc)
         for (int ins = 0; ok && ins < L.nins; ++ins, ++it) {
-          if ((it & 1) != pi) continue;
+          if ((it % kDqProd) != pi) continue;
           uint8_t* dst = stage(per * kBox);
           if (!ok) return;
           const uint32_t bar = stage_bar();
@@ -272,12 +275,12 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
     if (rank == 0) {  // drain: none of this producer's loads may be in flight at teardown
       if (pi == 0) mbar_wait_drain(&in_full, 0);
       for (int i = (it > L.nst ? it - L.nst : 0); i < it; ++i)
-        if ((i & 1) == pi) mbar_wait_drain(&r_full[i % L.nst], (i / L.nst) & 1u);
+        if ((i % kDqProd) == pi) mbar_wait_drain(&r_full[i % L.nst], (i / L.nst) & 1u);
     }
-  } else if ((warp == kDpWarp || warp == kDpProd2) && lane == 0) {
+  } else if (warp == kDpWarp && lane == 0) {
     // ---------------------------------------------------------------- TMA producers: V and dY for dP
     // (even stages from warp 6, odd ones from warp 9)
-    const int pi = warp == kDpWarp ? 0 : 1;
+    const int pi = 0;
     prefetch_tmap(&tv);
     prefetch_tmap(&tdy);
     int it = 0;
@@ -285,7 +288,7 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
     for (int g = 0; ok && g < dps; ++g) {
       const int y = (int)min((int64_t)b * p.T + (g % nj) * kTile + 64 * (int)rank, rowsBT - 1);
       for (int cc = 0; cc < p.D / 128; ++cc, ++it) {  // per 128 value columns: V rows of 64 keys, dY rows
-        if ((it & 1) != pi) continue;
+        if ((it % kDqProd) != pi) continue;
         const int st = it % L.nsp;
         if (!mbar_wait(&rp_empty[st], ((it / L.nsp) & 1u) ^ 1u, ab, 13)) { ok = false; break; }
         if (rank == 0) mbar_arrive_expect_tx(&rp_full[st], 2 * kDpStage);
@@ -297,7 +300,7 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
     }
     if (rank == 0)
       for (int i = (it > L.nsp ? it - L.nsp : 0); i < it; ++i)
-        if ((i & 1) == pi) mbar_wait_drain(&rp_full[i % L.nsp], (i / L.nsp) & 1u);
+        if ((i % kDqProd) == pi) mbar_wait_drain(&rp_full[i % L.nsp], (i / L.nsp) & 1u);
   } else if (warp == kDpWarp + 1 && lane == 0 && rank == 0) {
     // ---------------------------------------------------------------- dP issuer (leader): dP = dY V^T
     // Its own thread, so the score and dQ products never wait behind the value stream.
@@ -412,8 +415,10 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
     }
     commit_both(&o_full);
     mbar_wait_drain(&o_full, 0);
-  } else if (warp >= 2 && warp < 6) {
-    // ---------------------------------------------------------------- softmax + epilogue
+  } else if ((warp >= 2 && warp < 6) || warp >= kDqSoftmax2) {
+    // ---------------------------------------------------------------- softmax + epilogue: two warpgroups,
+    // warps 2-5 take the first 32 of each thread's 64 key columns and warps 8-11 the other 32
+    const int wg = warp >= kDqSoftmax2 ? 1 : 0;
     const int quad = warp & 3;
     const int l = quad * 32 + lane;
     const int r = l & 63, half = l >> 6;
@@ -449,8 +454,8 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
       if (arriver && u < 300) trace_at(ft, 3072 + 4 * u);
       if (ok) ok = mbar_wait(&s_full[sb], (u >> 1) & 1u, ab, 32);
       if (ok && s == 0) ok = mbar_wait(&dp_full[g & 1], (g >> 1) & 1u, ab, 35);
-      if (arriver && u < 300) trace_at(ft, 3073 + 4 * u);
       if (ok && form_ds && v >= 2) ok = mbar_wait(&ds_empty[v & 1], ((v - 2) >> 1) & 1u, ab, 33);
+      if (arriver && u < 300) trace_at(ft, 3073 + 4 * u);
       ok = __all_sync(0xffffffffu, ok);
       if (ok) {
         tc_fence_after();
@@ -458,8 +463,8 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
         // this map's row constants in registers (the per-map arrays live in local memory)
         const float sc2 = scale2[s], ls2 = lse2[s], dl = delta[s], al = alpha[s];
         float dsum = 0.f, a_acc = 0.f, b_acc = 0.f, c_acc = 0.f;
-#pragma unroll
-        for (int ch = 0; ch < 2; ++ch) {
+        {
+          const int ch = wg;
           float sv[32], pv[32];
           tmem_ld32(tmem + lane_base + L.tmem_s + sb * (kTile / 2) + ch * 32, sv);
           tmem_ld32(tmem + lane_base + L.tmem_p + (g & 1) * (kTile / 2) + ch * 32, pv);
@@ -517,21 +522,24 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
       }
       if (arriver && u < 300) trace_at(ft, 3074 + 4 * u);
       tc_fence_before();
-      named_bar_sync(1, 128);
+      named_bar_sync(1, 256);
       if (arriver) {
         if (u < 300) trace_at(ft, 3075 + 4 * u);
         mbar_arrive_cluster(pf_leader + sb * 8);
         if (s == maps - 1) mbar_arrive_cluster(df_leader + (g & 1) * 8);
       }
       if (!p.delta_given && u == per_sweep - 1) {
-        // end of the first sweep: whole-row delta_s (two halves), stored for the key-parallel kernels
-        for (int m = 0; m < maps; ++m) red[m * 128 + l] = delta[m];
-        named_bar_sync(1, 128);
-        for (int m = 0; m < maps; ++m) delta[m] += red[m * 128 + (l ^ 64)];
-        named_bar_sync(1, 128);
+        // end of the first sweep: whole-row delta_s (two halves x two warpgroups), stored for the
+        // key-parallel kernels
+        for (int m = 0; m < maps; ++m) red[(m * 2 + wg) * 128 + l] = delta[m];
+        named_bar_sync(1, 256);
+        for (int m = 0; m < maps; ++m)
+          delta[m] = red[(m * 2) * 128 + l] + red[(m * 2) * 128 + (l ^ 64)] + red[(m * 2 + 1) * 128 + l] +
+                     red[(m * 2 + 1) * 128 + (l ^ 64)];
+        named_bar_sync(1, 256);
         for (int m = 0; m < maps; ++m) {
-          if (ok && live && half == 0) p.delta[((int64_t)b * maps + m) * p.T + t] = delta[m];
-          if (p.dweight) {
+          if (ok && live && half == 0 && wg == 0) p.delta[((int64_t)b * maps + m) * p.T + t] = delta[m];
+          if (p.dweight && wg == 0) {
             float w = (ok && live && half == 0) ? delta[m] : 0.f;
             for (int o = 16; o; o >>= 1) w += __shfl_xor_sync(0xffffffffu, w, o);
             if (lane == 0 && w != 0.f) atomicAdd(p.dweight + m, w);
@@ -539,14 +547,30 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
         }
       }
     }
-    // ---- d gamma_s from each row's own sums (both halves), then the dQ epilogue
+    // ---- d gamma_s from each row's own sums (both warpgroups, both halves), then the dQ epilogue
     if (p.dscale) {
+      if (wg == 1)
+        for (int m = 0; m < maps; ++m) {
+          red[(3 * m) * 128 + l] = sA[m];
+          red[(3 * m + 1) * 128 + l] = sB[m];
+          red[(3 * m + 2) * 128 + l] = sC[m];
+        }
+      named_bar_sync(1, 256);
+      if (wg == 0)
+        for (int m = 0; m < maps; ++m) {
+          sA[m] += red[(3 * m) * 128 + l];
+          sB[m] += red[(3 * m + 1) * 128 + l];
+          sC[m] += red[(3 * m + 2) * 128 + l];
+        }
+      named_bar_sync(1, 256);
+    }
+    if (p.dscale && wg == 0) {
       for (int m = 0; m < maps; ++m) {
         red[(3 * m) * 128 + l] = sA[m];
         red[(3 * m + 1) * 128 + l] = sB[m];
         red[(3 * m + 2) * 128 + l] = sC[m];
       }
-      named_bar_sync(1, 128);
+      named_bar_sync(2, 128);
       for (int m = 0; m < maps; ++m) {
         float dg = 0.f;
         if (half == 0 && live && ok) {
@@ -559,10 +583,10 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
         if (lane == 0 && dg != 0.f) atomicAdd(p.dscale + m, dg * gsc);
       }
     }
-    if (ok) ok = mbar_wait(&o_full, 0, ab, 34);
+    if (wg == 0 && ok) ok = mbar_wait(&o_full, 0, ab, 34);
     ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
-    if (ok && p.dq) {
+    if (wg == 0 && ok && p.dq) {
       for (int m = 0; m < maps; ++m) {
         const float gamma = p.scales[m] * gsc;
         for (int ins = 0; ins < L.nins; ++ins)
@@ -1034,11 +1058,11 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
 template <typename Kern>
 int launch_pair(Kern kern, const Layout& L, int pairs, const CUtensorMap& tq, const CUtensorMap& tk,
                 const CUtensorMap& tv, const CUtensorMap& tdy, const CUtensorMap& tacc, const Params& p,
-                cudaStream_t st) {
+                cudaStream_t st, int threads = kThreads) {
   const int smem = (L.smem < 120 * 1024 ? 120 * 1024 : L.smem) + 1024;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return record_cuda_error();
-  return launch_kernel(kern, dim3((unsigned)(2 * pairs), 1, 1), dim3(kThreads, 1, 1), smem, st, true, tq, tk, tv, tdy,
+  return launch_kernel(kern, dim3((unsigned)(2 * pairs), 1, 1), dim3(threads, 1, 1), smem, st, true, tq, tk, tv, tdy,
                        tacc, p);
 }
 
@@ -1111,8 +1135,8 @@ extern "C" int da_attn_bwd_mixed(const void* q, int64_t q_rows, int64_t q_base, 
   // the query-parallel kernel runs first: without a given delta it produces it for the other two
   if (dq || dscale || !delta_given) {
     const Layout L = make_layout(0, maps, group, R, D);
-    rc = bf16 ? launch_pair(dq_mixed_kernel<__nv_bfloat16>, L, pairs, tq, tk, tv, tdy, tk128, p, st)
-              : launch_pair(dq_mixed_kernel<__half>, L, pairs, tq, tk, tv, tdy, tk128, p, st);
+    rc = bf16 ? launch_pair(dq_mixed_kernel<__nv_bfloat16>, L, pairs, tq, tk, tv, tdy, tk128, p, st, kDqThreads)
+              : launch_pair(dq_mixed_kernel<__half>, L, pairs, tq, tk, tv, tdy, tk128, p, st, kDqThreads);
     if (rc) return rc;
   }
   if (dk) {
