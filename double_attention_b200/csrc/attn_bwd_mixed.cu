@@ -34,17 +34,14 @@ namespace attn {
 namespace bwdm {
 
 // warp 0: TMA producer of the resident rows and the score / accumulation operands; warp 1: their
-// MMA issuer; warps 2-5: softmax; warp 6: TMA producer of the dP operands (V and dY); warp 7: the
-// dP issuer; warps 8 and 9: second producers of the two rings.  dP runs as its own stream so the
-// other products never wait behind it.  One warp's TMA stages complete one after another (about
-// 1 us per stage for paired loads, nearly whatever the stage's size), so each ring is filled by two
-// producer warps taking alternate stages.
-constexpr int kThreads = 320;
+// MMA issuer; warps 2-5 and 8-11: softmax, two warpgroups each taking 32 of a thread's 64 columns
+// (the per-element arithmetic of dS and P, with one warp per SM sub-partition, paced the kernels);
+// warp 6: TMA producer of the dP operands (V and dY); warp 7: the dP issuer.  dP runs as its own
+// stream so the other products never wait behind it.
+constexpr int kThreads = 384;
 constexpr int kDpWarp = 6;
-constexpr int kProd2 = 8, kDpProd2 = 9;
-// dQ kernel: one producer per ring and a second softmax warpgroup (warps 8-11) instead: its second
-// sweep is bound by the softmax's per-row arithmetic, and 384 threads x 168 registers fit the SM
-constexpr int kDqThreads = 384, kDqProd = 1, kDqSoftmax2 = 8;
+constexpr int kProducers = 1;  // producer warps per ring (stage filters below take stage % kProducers)
+constexpr int kSoftmax2 = 8;   // first warp of the second softmax warpgroup
 constexpr int kRows = 64;      // rows (queries or keys) per CTA
 constexpr int kTile = 128;     // columns (keys or queries) per tile and pair
 constexpr int kStage = 16384;  // main ring stage bytes
@@ -134,7 +131,7 @@ DA_DEV void load_map_chunk(const CUtensorMap* tm, const MapRows& m, const Params
 
 // =============================================================================== dQ kernel
 template <typename T>
-__global__ void __launch_bounds__(kDqThreads, 1) dq_mixed_kernel(const __grid_constant__ CUtensorMap tq,
+__global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_constant__ CUtensorMap tq,
                                                                const __grid_constant__ CUtensorMap tk,
                                                                const __grid_constant__ CUtensorMap tv,
                                                                const __grid_constant__ CUtensorMap tdy,
@@ -233,7 +230,7 @@ __global__ void __launch_bounds__(kDqThreads, 1) dq_mixed_kernel(const __grid_co
     auto emit_s = [&](int u) {  // key rows of map s for this CTA's 64 keys
       const int krow0 = unit_j(u) * kTile + 64 * (int)rank;
       for (int cc = 0; ok && cc < L.kw / 128; ++cc, ++it) {
-        if ((it % kDqProd) != pi) continue;
+        if ((it % kProducers) != pi) continue;
         uint8_t* dst = stage(2 * kBox);
         if (!ok) return;
         load_map_chunk(&tk, km, p, stage_bar(), dst, b, unit_s(u), cc, 2, krow0);
@@ -243,7 +240,7 @@ __global__ void __launch_bounds__(kDqThreads, 1) dq_mixed_kernel(const __grid_co
       const int per = (L.ncol / 2) / 64, s = unit_s(u), j = unit_j(u);
       if (L.acc_merge) {  // one stage per N block: a 128-key x 64-column box
         for (int ins = 0; ok && ins < L.nins; ++ins, ++it) {
-          if ((it % kDqProd) != pi) continue;
+          if ((it % kProducers) != pi) continue;
           uint8_t* dst = stage(2 * kBox);
           if (!ok) return;
           const int mb = (ins * L.ncol + (int)rank * (L.ncol / 2)) / 64;
@@ -255,7 +252,7 @@ __global__ void __launch_bounds__(kDqThreads, 1) dq_mixed_kernel(const __grid_co
       }
       for (int kc = 0; ok && kc < kTile / 64; ++kc)
         for (int ins = 0; ok && ins < L.nins; ++ins, ++it) {
-          if ((it % kDqProd) != pi) continue;
+          if ((it % kProducers) != pi) continue;
           uint8_t* dst = stage(per * kBox);
           if (!ok) return;
           const uint32_t bar = stage_bar();
@@ -275,7 +272,7 @@ __global__ void __launch_bounds__(kDqThreads, 1) dq_mixed_kernel(const __grid_co
     if (rank == 0) {  // drain: none of this producer's loads may be in flight at teardown
       if (pi == 0) mbar_wait_drain(&in_full, 0);
       for (int i = (it > L.nst ? it - L.nst : 0); i < it; ++i)
-        if ((i % kDqProd) == pi) mbar_wait_drain(&r_full[i % L.nst], (i / L.nst) & 1u);
+        if ((i % kProducers) == pi) mbar_wait_drain(&r_full[i % L.nst], (i / L.nst) & 1u);
     }
   } else if (warp == kDpWarp && lane == 0) {
     // ---------------------------------------------------------------- TMA producers: V and dY for dP
@@ -288,7 +285,7 @@ __global__ void __launch_bounds__(kDqThreads, 1) dq_mixed_kernel(const __grid_co
     for (int g = 0; ok && g < dps; ++g) {
       const int y = (int)min((int64_t)b * p.T + (g % nj) * kTile + 64 * (int)rank, rowsBT - 1);
       for (int cc = 0; cc < p.D / 128; ++cc, ++it) {  // per 128 value columns: V rows of 64 keys, dY rows
-        if ((it % kDqProd) != pi) continue;
+        if ((it % kProducers) != pi) continue;
         const int st = it % L.nsp;
         if (!mbar_wait(&rp_empty[st], ((it / L.nsp) & 1u) ^ 1u, ab, 13)) { ok = false; break; }
         if (rank == 0) mbar_arrive_expect_tx(&rp_full[st], 2 * kDpStage);
@@ -300,7 +297,7 @@ __global__ void __launch_bounds__(kDqThreads, 1) dq_mixed_kernel(const __grid_co
     }
     if (rank == 0)
       for (int i = (it > L.nsp ? it - L.nsp : 0); i < it; ++i)
-        if ((i % kDqProd) == pi) mbar_wait_drain(&rp_full[i % L.nsp], (i / L.nsp) & 1u);
+        if ((i % kProducers) == pi) mbar_wait_drain(&rp_full[i % L.nsp], (i / L.nsp) & 1u);
   } else if (warp == kDpWarp + 1 && lane == 0 && rank == 0) {
     // ---------------------------------------------------------------- dP issuer (leader): dP = dY V^T
     // Its own thread, so the score and dQ products never wait behind the value stream.
@@ -415,10 +412,10 @@ __global__ void __launch_bounds__(kDqThreads, 1) dq_mixed_kernel(const __grid_co
     }
     commit_both(&o_full);
     mbar_wait_drain(&o_full, 0);
-  } else if ((warp >= 2 && warp < 6) || warp >= kDqSoftmax2) {
+  } else if ((warp >= 2 && warp < 6) || warp >= kSoftmax2) {
     // ---------------------------------------------------------------- softmax + epilogue: two warpgroups,
     // warps 2-5 take the first 32 of each thread's 64 key columns and warps 8-11 the other 32
-    const int wg = warp >= kDqSoftmax2 ? 1 : 0;
+    const int wg = warp >= kSoftmax2 ? 1 : 0;
     const int quad = warp & 3;
     const int l = quad * 32 + lane;
     const int r = l & 63, half = l >> 6;
@@ -691,10 +688,10 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
 
   const int krow = k0 + 64 * (int)rank;
   const int vy = (int)min((int64_t)b * p.T + krow, rowsBT - 1);
-  if ((warp == 0 || warp == kProd2) && lane == 0) {
+  if (warp == 0 && lane == 0) {
     // ---------------------------------------------------------------- TMA producers: K (warp 0), then Q
     // (and dY for dV), even stages from warp 0 and odd ones from warp 8
-    const int pi = warp == 0 ? 0 : 1;
+    const int pi = 0;
     prefetch_tmap(&tq);
     prefetch_tmap(&tdy);
     if (pi == 0) {
@@ -717,7 +714,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
     auto emit_s = [&](int u) {  // query rows of map s for this CTA's 64 queries
       const int q = (i0 + unit_g(u)) * kTile + 64 * (int)rank;
       for (int cc = 0; ok && cc < L.kw / 128; ++cc, ++it) {
-        if ((it & 1) != pi) continue;
+        if ((it % kProducers) != pi) continue;
         uint8_t* dst = stage(2 * kBox);
         if (!ok) return;
         load_map_chunk(&tq, qm, p, stage_bar(), dst, b, unit_s(u), cc, 2, q);
@@ -727,7 +724,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
       const int i = i0 + unit_g(u), s = unit_s(u);
       if (kDK && L.acc_merge) {  // one stage per N block: a 128-query x 64-column box
         for (int ins = 0; ok && ins < L.nins; ++ins, ++it) {
-          if ((it & 1) != pi) continue;
+          if ((it % kProducers) != pi) continue;
           uint8_t* dst = stage(2 * kBox);
           if (!ok) return;
           const int mb = (ins * L.ncol + (int)rank * (L.ncol / 2)) / 64;
@@ -739,7 +736,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
         const int per = (L.ncol / 2) / 64;
         for (int qc = 0; ok && qc < kTile / 64; ++qc)
           for (int ins = 0; ok && ins < L.nins; ++ins, ++it) {
-            if ((it & 1) != pi) continue;
+            if ((it % kProducers) != pi) continue;
             uint8_t* dst = stage(per * kBox);
             if (!ok) return;
             const uint32_t bar = stage_bar();
@@ -755,7 +752,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
         for (int qc = 0; ok && qc < kTile / 64; ++qc) {
           const int y = (int)min((int64_t)b * p.T + i * kTile + qc * 64, rowsBT - 1);
           for (int ins = 0; ok && ins < dins; ++ins, ++it) {
-            if ((it & 1) != pi) continue;
+            if ((it % kProducers) != pi) continue;
             uint8_t* dst = stage(dper * kBox);  // dper = 2 (dn = 256): one box of two column blocks
             if (!ok) return;
             tma_load_3d_pair(&tdy, stage_bar(), dst, 0, y, (ins * dn + (int)rank * (dn / 2)) / 64);
@@ -772,12 +769,12 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
     if (rank == 0) {  // drain: none of this producer's loads may be in flight at teardown
       if (pi == 0) mbar_wait_drain(&in_full, 0);
       for (int i = (it > L.nst ? it - L.nst : 0); i < it; ++i)
-        if ((i & 1) == pi) mbar_wait_drain(&r_full[i % L.nst], (i / L.nst) & 1u);
+        if ((i % kProducers) == pi) mbar_wait_drain(&r_full[i % L.nst], (i / L.nst) & 1u);
     }
-  } else if (kDK && (warp == kDpWarp || warp == kDpProd2) && lane == 0) {
+  } else if (kDK && warp == kDpWarp && lane == 0) {
     // ---------------------------------------------------------------- TMA producers: dY and V for dP^T
     // (even stages from warp 6, odd ones from warp 9)
-    const int pi = warp == kDpWarp ? 0 : 1;
+    const int pi = 0;
     prefetch_tmap(&tv);
     prefetch_tmap(&tdy);
     int it = 0;
@@ -785,7 +782,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
     for (int g = 0; ok && g < ni; ++g) {
       const int y = (int)min((int64_t)b * p.T + (i0 + g) * kTile + 64 * (int)rank, rowsBT - 1);
       for (int cc = 0; cc < p.D / 128; ++cc, ++it) {  // per 128 value columns: dY rows of 64 queries, V rows
-        if ((it & 1) != pi) continue;
+        if ((it % kProducers) != pi) continue;
         const int st = it % L.nsp;
         if (!mbar_wait(&rp_empty[st], ((it / L.nsp) & 1u) ^ 1u, ab, 13)) { ok = false; break; }
         if (rank == 0) mbar_arrive_expect_tx(&rp_full[st], 2 * kDpStage);
@@ -797,7 +794,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
     }
     if (rank == 0)
       for (int i = (it > L.nsp ? it - L.nsp : 0); i < it; ++i)
-        if ((i & 1) == pi) mbar_wait_drain(&rp_full[i % L.nsp], (i / L.nsp) & 1u);
+        if ((i % kProducers) == pi) mbar_wait_drain(&rp_full[i % L.nsp], (i / L.nsp) & 1u);
   } else if (kDK && warp == kDpWarp + 1 && lane == 0 && rank == 0) {
     // ---------------------------------------------------------------- dP^T issuer (leader): dP^T = V dY^T
     const uint32_t idesc = idesc_f16(128, kTile, kBf16, false, false);
@@ -912,8 +909,10 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
     }
     commit_both(&o_full);
     mbar_wait_drain(&o_full, 0);
-  } else if (warp >= 2 && warp < 6) {
-    // ---------------------------------------------------------------- softmax + epilogue
+  } else if ((warp >= 2 && warp < 6) || warp >= kSoftmax2) {
+    // ---------------------------------------------------------------- softmax + epilogue: two warpgroups,
+    // warps 2-5 take the first 32 of each thread's 64 query columns and warps 8-11 the other 32
+    const int wg = warp >= kSoftmax2 ? 1 : 0;
     const int quad = warp & 3;
     const int l = quad * 32 + lane;
     const int r = l & 63, half = l >> 6;
@@ -932,13 +931,13 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
       scale2[s] = s < maps ? p.scales[s] * gsc * kLog2e : 0.f;
       alpha[s] = (s < maps && p.weights) ? p.weights[s] : 1.f;
     }
-    float pm[kDK ? 1 : 64];
+    float pm[kDK ? 1 : 32];
     bool ok = true;
     for (int u = 0; u < U; ++u) {
       const int sb = u & 1, s = unit_s(u), g = unit_g(u);
       const int qt = (i0 + g) * kTile;
       float* rt = red + (g & 1) * (2 * kMaxMaps * 128);
-      if (s == 0) {  // stage this query tile's log-sum-exp (and delta) of every map
+      if (s == 0 && wg == 0) {  // stage this query tile's log-sum-exp (and delta) of every map
         for (int m = 0; m < maps; ++m) {
           const int q = qt + l;
           const bool qv = q < p.T;
@@ -951,7 +950,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
       // the tile buffer written by this unit must have been read by the product two uses ago
       if (ok && kDK && u >= 2) ok = mbar_wait(&t_empty[u & 1], ((u - 2) >> 1) & 1u, ab, 33);
       if (ok && !kDK && s == 0 && g >= 2) ok = mbar_wait(&t_empty[g & 1], ((g - 2) >> 1) & 1u, ab, 33);
-      if (s == 0) named_bar_sync(1, 128);  // staged lse / delta visible
+      if (s == 0) named_bar_sync(1, 256);  // staged lse / delta visible
       ok = __all_sync(0xffffffffu, ok);
       if (ok) {
         tc_fence_after();
@@ -959,8 +958,8 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
         const float sc2 = scale2[s], al = alpha[s];
         const float* lse_row = rt + s * 128;
         const float* delta_row = rt + (kMaxMaps + s) * 128;
-#pragma unroll
-        for (int ch = 0; ch < 2; ++ch) {
+        {
+          const int ch = wg;
           float sv[32], dpv[32];
           tmem_ld32(tmem + lane_base + L.tmem_s + sb * (kTile / 2) + ch * 32, sv);
           if (kDK) tmem_ld32(tmem + lane_base + L.tmem_p + (g & 1) * (kTile / 2) + ch * 32, dpv);
@@ -978,9 +977,9 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
               packed[e / 2] = pack2<T>(al * p0 * (dpv[e] - delta_row[qc0 + e]),
                                        al * p1 * (dpv[e + 1] - delta_row[qc0 + e + 1]));
             } else {
-              pm[ch * 32 + e] = s == 0 ? al * p0 : fmaf(al, p0, pm[ch * 32 + e]);
-              pm[ch * 32 + e + 1] = s == 0 ? al * p1 : fmaf(al, p1, pm[ch * 32 + e + 1]);
-              packed[e / 2] = pack2<T>(pm[ch * 32 + e], pm[ch * 32 + e + 1]);
+              pm[e] = s == 0 ? al * p0 : fmaf(al, p0, pm[e]);
+              pm[e + 1] = s == 0 ? al * p1 : fmaf(al, p1, pm[e + 1]);
+              packed[e / 2] = pack2<T>(pm[e], pm[e + 1]);
             }
           }
           if (kDK || s == maps - 1) {
@@ -993,16 +992,16 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
         if (kDK || s == maps - 1) fence_proxy_async();
       }
       tc_fence_before();
-      named_bar_sync(1, 128);
+      named_bar_sync(1, 256);
       if (arriver) {
         mbar_arrive_cluster(pf_leader + sb * 8);
         if (kDK && s == maps - 1) mbar_arrive_cluster(df_leader + (g & 1) * 8);
       }
     }
-    if (ok) ok = mbar_wait(&o_full, 0, ab, 34);
+    if (wg == 0 && ok) ok = mbar_wait(&o_full, 0, ab, 34);
     ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
-    if (ok && kDK && p.dk) {
+    if (wg == 0 && ok && kDK && p.dk) {
       for (int m = 0; m < maps; ++m) {
         const float gamma = p.scales[m] * gsc;
         for (int ins = 0; ins < L.nins; ++ins)
@@ -1028,7 +1027,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
           }
       }
     }
-    if (ok && !kDK && p.dv) {
+    if (wg == 0 && ok && !kDK && p.dv) {
       for (int ins = 0; ins < dins; ++ins)
         for (int c = 0; c < dn / 2; c += 32) {
           float vv[32];
@@ -1058,11 +1057,11 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
 template <typename Kern>
 int launch_pair(Kern kern, const Layout& L, int pairs, const CUtensorMap& tq, const CUtensorMap& tk,
                 const CUtensorMap& tv, const CUtensorMap& tdy, const CUtensorMap& tacc, const Params& p,
-                cudaStream_t st, int threads = kThreads) {
+                cudaStream_t st) {
   const int smem = (L.smem < 120 * 1024 ? 120 * 1024 : L.smem) + 1024;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return record_cuda_error();
-  return launch_kernel(kern, dim3((unsigned)(2 * pairs), 1, 1), dim3(threads, 1, 1), smem, st, true, tq, tk, tv, tdy,
+  return launch_kernel(kern, dim3((unsigned)(2 * pairs), 1, 1), dim3(kThreads, 1, 1), smem, st, true, tq, tk, tv, tdy,
                        tacc, p);
 }
 
@@ -1135,8 +1134,8 @@ extern "C" int da_attn_bwd_mixed(const void* q, int64_t q_rows, int64_t q_base, 
   // the query-parallel kernel runs first: without a given delta it produces it for the other two
   if (dq || dscale || !delta_given) {
     const Layout L = make_layout(0, maps, group, R, D);
-    rc = bf16 ? launch_pair(dq_mixed_kernel<__nv_bfloat16>, L, pairs, tq, tk, tv, tdy, tk128, p, st, kDqThreads)
-              : launch_pair(dq_mixed_kernel<__half>, L, pairs, tq, tk, tv, tdy, tk128, p, st, kDqThreads);
+    rc = bf16 ? launch_pair(dq_mixed_kernel<__nv_bfloat16>, L, pairs, tq, tk, tv, tdy, tk128, p, st)
+              : launch_pair(dq_mixed_kernel<__half>, L, pairs, tq, tk, tv, tdy, tk128, p, st);
     if (rc) return rc;
   }
   if (dk) {
