@@ -52,3 +52,31 @@ def test_argument_validation_happens_before_any_device_work() -> None:
         _lib.check("da_gemm", _lib.DA_ERR_SHAPE)
     with pytest.raises(NotImplementedError):
         _lib.check("da_attn_fwd", _lib.DA_ERR_UNSUPPORTED)
+
+
+def test_layernorm_entry_points_validate_on_the_host() -> None:
+    handle = _lib.lib()
+    f32 = ctypes.c_float(1e-5)
+    # a null input, then an unsupported width: both refused before any CUDA call
+    assert handle.da_add_layernorm_fwd(None, None, 0, None, None, 8, 512, f32, None, None, 1, None, None,
+                                       None) == _lib.DA_ERR_NULL
+    buf = (ctypes.c_float * 4096)()
+    p = ctypes.addressof(buf)
+    assert handle.da_add_layernorm_fwd(p, None, 0, p, p, 8, 500, f32, None, p, 1, p, p, None) == _lib.DA_ERR_SHAPE
+    assert handle.da_add_layernorm_fwd(p, None, 0, p, p, 8, 512, f32, None, p, 7, p, p, None) == _lib.DA_ERR_DTYPE
+    # the backward's partial-sum buffer must have the queried number of blocks
+    blocks = handle.da_layernorm_bwd_blocks(1)
+    assert blocks == 1
+    assert handle.da_add_layernorm_bwd(p, 1, None, p, p, p, p, 1, 512, p, None, 0, p, blocks + 1, None, None,
+                                       None) == _lib.DA_ERR_WORKSPACE
+
+
+def test_fused_norms_only_for_cuda_fp32_rows() -> None:
+    import torch
+    import torch.nn as nn
+
+    from double_attention_b200 import ops
+
+    norm = nn.LayerNorm(512)
+    assert not ops.layernorm_supported(torch.zeros(2, 512), norm)            # CPU tensor: plain nn.LayerNorm
+    assert not ops.layernorm_supported(torch.zeros(2, 500), nn.LayerNorm(500))
