@@ -1090,8 +1090,8 @@ LAYERNORM_WIDTHS = (256, 512, 768, 1024)
 
 def layernorm_supported(x: Tensor, *norms) -> bool:
     """Whether the fused kernels cover ``norm(x)`` for every given ``nn.LayerNorm``."""
-    if not (x.is_cuda and x.dtype == torch.float32 and x.shape[-1] in LAYERNORM_WIDTHS):
-        return False
+    if not (x.is_cuda and x.dtype == torch.float32 and x.numel() > 0 and x.shape[-1] in LAYERNORM_WIDTHS):
+        return False  # (an empty batch keeps nn.LayerNorm's behaviour)
     for n in norms:
         if (n.weight is None or n.bias is None or n.weight.dtype != torch.float32
                 or tuple(n.normalized_shape) != (x.shape[-1],)):
