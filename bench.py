@@ -1,10 +1,12 @@
 #!/usr/bin/env python
 """Routed-attention throughput on B200 (the BASELINE.json metric).
 
-Default workload: preset ``a1``
-SharedDictionaryAttention forward in fp16, batch 8 x seq 512 per GPU.
+Default workload (the largest single-GPU module
+configuration and the forward+backward half of the metric): preset ``qk4-s4``
+SharedDictionaryAttention forward+backward in bf16, global batch 16 x seq 2048
+split over the GPUs, dY ~ N(0,1).
 Other workloads (``--config``):
-  3  qk4-s4 SharedDictionaryAttention forward+backward, bf16, global batch 16 x 2048 (dY ~ N(0,1))
+  2  a1 SharedDictionaryAttention forward, fp16, batch 8 x seq 512 per GPU
   4  a1-r512-d1536 forward, bf16, batch 4 x 8192 per GPU
   5  DoubleAttentionLM training step (a1, 6 layers, one bank, FFN 1536, vocab 2048, T 1024),
      bf16 autocast, AdamW, global batch 256 data-parallel with NCCL gradient averaging
@@ -48,7 +50,9 @@ L2_FLUSH_BYTES = 512 << 20
 CONFIGS = {
     # a1 forward, fp16, B8 T512 per GPU
     2: dict(kind="module", preset="a1", dtype=torch.float16, batch=8, seq=512, mode="fwd", scaling="weak",
-            workload="a1 SharedDictionaryAttention forward, fp16, B8 T512 per GPU"),
+            workload="a1 SharedDictionaryAttention forward, fp16, B8 T512 per GPU",
+            operands="fp16 projection and route operands; the probability-value products of the route and the "
+                     "attention take bf16 operands (V and the value dictionary in bf16), fp32 accumulation"),
     # qk4-s4 forward+backward, bf16, B16 T2048 split over the GPUs
     3: dict(kind="module", preset="qk4-s4", dtype=torch.bfloat16, batch=16, seq=2048, mode="fwdbwd",
             scaling="strong",
@@ -75,7 +79,7 @@ def parse_args(argv=None):
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=None, help="timed steps (default per config)")
     p.add_argument("--warmup", type=int, default=10)
-    p.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS))
+    p.add_argument("--config", type=int, default=3, choices=sorted(CONFIGS))
     p.add_argument("--impl", choices=("b200", "reference"), default="b200")
     p.add_argument("--no-graph", action="store_true", help="time eager launches instead of a CUDA graph")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
@@ -519,8 +523,9 @@ def run_b200(args, cfg, world, rank, local):
             "frac": achieved / peak_tf, "peak_source": f"{peak_kind} bf16 dense (burst)",
             "flops_per_launch": flops_top, "ms_per_launch": ms_top,
             "traffic": load_traffic(top, f"config{args.config}"),
-            "other_kernels": {k: {"ms": v[0], "tflops": v[1] / (v[0] / 1e3) / 1e12} for k, v in kernels.items()
-                              if k != top},
+            "other_kernels": {k: {"ms": v[0], "tflops": v[1] / (v[0] / 1e3) / 1e12,
+                                  "traffic": load_traffic(k, f"config{args.config}")}
+                              for k, v in kernels.items() if k != top},
         }
         if world == 1:
             torch.set_num_threads(os.cpu_count() or 1)
@@ -546,6 +551,7 @@ def run_b200(args, cfg, world, rank, local):
             "data": "synthetic",
             "config": {
                 "workload": cfg["workload"], "preset": cfg["preset"],
+                **({"operands": cfg["operands"]} if "operands" in cfg else {}),
                 "batch_per_gpu": per_rank_batch(cfg, world), "global_batch": per_rank_batch(cfg, world) * world,
                 "seq_len": cfg["seq"], "mode": cfg["mode"], "parallelism": f"dp{world}",
                 "l2": "flushed before every timed step (512 MiB write)", "cuda_graph": used_graph,

@@ -57,6 +57,7 @@ SIGNATURES: dict[str, list] = {
     "da_attn_bwd_mixed": [_p, _i64, _i64, _i64, _i64, _p, _i64, _i64, _i64, _i64, _p, _p, _i32, _i32, _i32, _i32,
                           _i32, _i32, _p, _i32, _i32, _p, _p, _p, _p, _i32, _p, _p, _p, _p, _p, _p, _p],
     "da_selftest_mma": [_i32, _i32, _i32, _i32, _p, _p, _p, _p, _p],
+    "da_selftest_wait_timeout": [_i64, _i32, _p, _p, _p],
     "da_route_var_weights": [_p, _i64, _i32, _p, _i64, _i32, _i32, _i32, _f32, _f32, _p, _f32, _p, _p, _p],
     "da_route_var_output": [_p, _i64, _i32, _i32, _i32, _f32, _p, _p, _p],
     "da_route_var_output_bwd": [_p, _p, _p, _i64, _i32, _i32, _i32, _f32, _p, _p, _p],

@@ -117,14 +117,17 @@ struct Abort {
 // Wait until the barrier phase with the given parity has completed.
 // Returns false when the wait gave up (timeout, or another role of this CTA
 // aborted).  `site` identifies the wait in status[1] when it times out.
-DA_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, const Abort& ab, int site = 0) {
+// `timeout_ns` bounds the wait (kWaitTimeoutNs for every kernel wait; the
+// failure-detection self-test passes a short limit).
+DA_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, const Abort& ab, int site = 0,
+                      unsigned long long timeout_ns = kWaitTimeoutNs) {
   const uint32_t addr = smem_u32(bar);
   if (mbar_test(addr, parity)) return true;
   const unsigned long long t0 = globaltimer();
   while (true) {
     if (mbar_test(addr, parity)) return true;
     if (*reinterpret_cast<volatile int*>(ab.smem_flag)) return false;
-    if (globaltimer() - t0 > kWaitTimeoutNs) {
+    if (globaltimer() - t0 > timeout_ns) {
       *reinterpret_cast<volatile int*>(ab.smem_flag) = 1;
       if (ab.status) {
         atomicOr(ab.status, DA_DEV_TIMEOUT);

@@ -22,7 +22,9 @@
 //     graphs replayed concurrently) race on it and must be serialised;
 //   * the array's device address is looked up (cudaGetSymbolAddress) the first
 //     time the entry point runs on a device, with that device made current;
-//     that first call should therefore happen before any stream capture.
+//     that first call should therefore happen before any stream capture;
+//   * the call makes q's device current while it runs and restores the
+//     caller's current device before it returns.
 #include <mutex>
 
 #include "common.cuh"
@@ -39,20 +41,35 @@ static __device__ __align__(256) int g_route_scratch[2 + kStaticRouteRows];
 std::mutex g_scratch_mutex;
 int* g_scratch_addr[64] = {nullptr};
 
-// Device of `ptr`, made current on this thread (no context-creating or
-// allocating runtime call beyond cudaSetDevice).
-int current_device_of(const void* ptr, int* dev) {
-  cudaPointerAttributes attr;
-  if (cudaPointerGetAttributes(&attr, ptr) != cudaSuccess) return da::record_cuda_error();
-  if (attr.type != cudaMemoryTypeDevice && attr.type != cudaMemoryTypeManaged) return DA_ERR_NULL;
-  int cur = -1;
-  if (cudaGetDevice(&cur) != cudaSuccess || cur != attr.device) {
-    cudaGetLastError();
-    if (cudaSetDevice(attr.device) != cudaSuccess) return da::record_cuda_error();
+// Makes the device that owns `ptr` current for the lifetime of the guard and
+// puts the caller's previous device back when it goes out of scope, so the
+// entry point leaves the calling thread's current device as it found it.
+class DeviceGuard {
+ public:
+  int enter(const void* ptr) {
+    cudaPointerAttributes attr;
+    if (cudaPointerGetAttributes(&attr, ptr) != cudaSuccess) return da::record_cuda_error();
+    if (attr.type != cudaMemoryTypeDevice && attr.type != cudaMemoryTypeManaged) return DA_ERR_NULL;
+    if (cudaGetDevice(&prev_) != cudaSuccess) {
+      cudaGetLastError();
+      prev_ = -1;
+    }
+    if (prev_ != attr.device) {
+      if (cudaSetDevice(attr.device) != cudaSuccess) return da::record_cuda_error();
+      switched_ = true;
+    }
+    device_ = attr.device;
+    return DA_OK;
   }
-  *dev = attr.device;
-  return DA_OK;
-}
+  int device() const { return device_; }
+  ~DeviceGuard() {
+    if (switched_ && prev_ >= 0) cudaSetDevice(prev_);
+  }
+
+ private:
+  int prev_ = -1, device_ = -1;
+  bool switched_ = false;
+};
 
 // Device address of the static work area on device `dev` (looked up once).
 int scratch_address(int dev, int** out) {
@@ -84,10 +101,10 @@ extern "C" int da_route_fwd_static(const void* q, int64_t rows, int64_t q_cols, 
   if ((int64_t)(groups - 1) * group_col_stride + R > q_cols || q_row_stride < q_cols) return DA_ERR_SHAPE;
   if (group_col_stride % 64 || (reinterpret_cast<uintptr_t>(z) & 15)) return DA_ERR_ALIGN;
   if ((int64_t)groups * rows > kStaticRouteRows) return DA_ERR_WORKSPACE;  // beyond the static work area
-  int dev = -1;
-  if (int rc = current_device_of(q, &dev)) return rc;
+  DeviceGuard guard;  // q's device is current until this call returns
+  if (int rc = guard.enter(q)) return rc;
   int* work = nullptr;
-  if (int rc = scratch_address(dev, &work)) return rc;
+  if (int rc = scratch_address(guard.device(), &work)) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // The counters must start at zero; the row list needs no clearing.
   if (cudaMemsetAsync(work, 0, 2 * sizeof(int), st) != cudaSuccess) return record_cuda_error();

@@ -149,8 +149,50 @@ int launch_selftest(const void* A, const void* B, int K, float* D, int* status, 
   return DA_OK;
 }
 
+// Failure-detection check: warp 0 waits on a barrier that nothing arrives on,
+// bounded by `timeout_ns`; when the wait gives up it records DA_DEV_TIMEOUT
+// and `site` in the status words and sets the CTA's abort flag.  Warp 1
+// waits on a second barrier that nothing arrives on either, with the regular
+// limit, and must leave as soon as the abort flag is set.  Both then return
+// normally, so the context stays usable.  (The limits are the only way these
+// waits end; the barriers are never signalled.)
+__global__ void __launch_bounds__(64) selftest_wait_kernel(unsigned long long timeout_ns, int site, int* status,
+                                                           unsigned long long* elapsed_ns) {
+  __shared__ uint64_t never_a, never_b;
+  __shared__ int abort_flag;
+  Abort ab{&abort_flag, status};
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    mbar_init(&never_a, 1);
+    mbar_init(&never_b, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const unsigned long long t0 = globaltimer();
+  bool ok = true;
+  if (threadIdx.x == 0) ok = mbar_wait(&never_a, 0, ab, site, timeout_ns);
+  if (threadIdx.x == 32) ok = mbar_wait(&never_b, 0, ab, site + 1);
+  if (threadIdx.x == 32 && elapsed_ns) elapsed_ns[1] = globaltimer() - t0;
+  if (threadIdx.x == 0 && elapsed_ns) elapsed_ns[0] = globaltimer() - t0;
+  (void)ok;
+}
+
 }  // namespace
 }  // namespace da
+
+extern "C" int da_selftest_wait_timeout(int64_t timeout_ns, int site, int* status, uint64_t* elapsed_ns,
+                                        void* stream) {
+  using namespace da;
+  if (!status) return DA_ERR_NULL;
+  if (int rc = bind_device(status)) return rc;
+  if (timeout_ns <= 0 || timeout_ns > 100000000ll || site <= 0) return DA_ERR_SHAPE;  // at most 0.1 s
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  selftest_wait_kernel<<<1, 64, 0, st>>>(static_cast<unsigned long long>(timeout_ns), site, status,
+                                         reinterpret_cast<unsigned long long*>(elapsed_ns));
+  if (cudaGetLastError() != cudaSuccess) return record_cuda_error();
+  note_launch();
+  return DA_OK;
+}
 
 extern "C" int da_selftest_mma(int cta_group, int n, int b_mn_major, int k, const void* A, const void* B,
                                float* D, int* status, void* stream) {

@@ -20,6 +20,7 @@ CPU tests):
 
 from __future__ import annotations
 
+import datetime
 from collections.abc import Iterable
 
 import torch
@@ -86,8 +87,14 @@ class GradientAllReduce:
         self._flat[i] = flat
         self._handles[i] = dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=self.group, async_op=True)
 
-    def finish(self) -> None:
-        """Wait for every bucket (launching any whose hooks did not fire) and write the averages back."""
+    def finish(self, timeout: datetime.timedelta | None = None) -> None:
+        """Wait for every bucket (launching any whose hooks did not fire) and write the averages back.
+
+        A rank that stops taking part (it raised, exited or hangs before its own all-reduce) makes the
+        others' waits fail: with the process group's timeout, or ``timeout`` for each bucket's wait when
+        given, or as soon as the backend sees the peer's connection close.  That failure is raised here
+        as a RuntimeError naming the bucket, before the optimiser could step on partial gradients; the
+        reducer is reset, and the process group should then be torn down."""
         if self.world == 1:
             self.reset()
             return
@@ -95,7 +102,15 @@ class GradientAllReduce:
             if self._handles[i] is None:
                 self._launch(i)
         for i, bucket in enumerate(self.buckets):
-            self._handles[i].wait()
+            try:
+                if timeout is None:
+                    self._handles[i].wait()
+                else:
+                    self._handles[i].wait(timeout)
+            except Exception as exc:  # backend-specific error types (DistBackendError, RuntimeError, ...)
+                self.reset()
+                raise RuntimeError(f"gradient all-reduce of bucket {i} of {len(self.buckets)} failed "
+                                   f"(a rank left the step?): {exc}") from exc
             flat = self._flat[i]
             offset = 0
             for p in bucket:

@@ -125,7 +125,9 @@ DA_API int da_route_fwd(const void* q, int64_t rows, int64_t q_cols, int64_t q_r
  * else DA_ERR_WORKSPACE.  Every GPU that loads the library holds the array
  * (about 256 KiB) until exit; all calls on a device share it, so calls that
  * can overlap on the GPU race.  The first call on each device looks the
- * array's address up and should come before any stream capture. */
+ * array's address up and should come before any stream capture.  The call
+ * makes q's device current while it runs and restores the calling thread's
+ * current device before it returns. */
 DA_API int da_route_fwd_static(const void* q, int64_t rows, int64_t q_cols, int64_t q_row_stride, int groups,
                                int64_t group_col_stride, int64_t R, int64_t M, int dtype, const void* dict_key_t,
                                const void* dict_value, const float* beta, const float* dk_max, float eps,
@@ -325,6 +327,16 @@ DA_API int da_add_layernorm_bwd(const void* dy, int dy_dtype, const float* d_res
  * No reference counterpart: D[128, n] = A[128, k] * B^T computed by one
  * tcgen05 tile (cta_group 1 or 2) for testing the descriptor layouts.
  * A: [128, k] bf16; B: [n, k] bf16 (b_mn_major = 0) or [k, n] (= 1). */
+/* No reference counterpart: the failure-detection path of every kernel wait.
+ * One CTA waits on a barrier that nothing signals, bounded by timeout_ns
+ * (at most 0.1 s); when the limit runs out the wait records DA_DEV_TIMEOUT
+ * in status[0] and `site` in status[1] (status: int32 [2] on the device,
+ * zeroed by the caller) and a second waiter of the same CTA leaves on the
+ * CTA's abort flag.  The kernel then returns normally and the context stays
+ * usable.  elapsed_ns (device uint64 [2], may be null) receives how long each
+ * waiter waited. */
+DA_API int da_selftest_wait_timeout(int64_t timeout_ns, int site, int* status, uint64_t* elapsed_ns, void* stream);
+
 DA_API int da_selftest_mma(int cta_group, int n, int b_mn_major, int k, const void* A, const void* B, float* D,
                     int* status, void* stream);
 

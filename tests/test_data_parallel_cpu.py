@@ -87,6 +87,57 @@ def test_bucketed_average_on_two_gloo_ranks() -> None:
         assert launched_early == buckets - 1, "early buckets should launch during backward"
 
 
+def _failing_worker(rank: int, world: int, port: int, out) -> None:
+    """Rank 1 raises in its forward pass (it never reaches the all-reduce); rank 0 runs backward and
+    finish(), whose wait must end with an error well inside the process group's timeout."""
+    import datetime
+    import time
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
+    torch.manual_seed(0)
+    net = _Net()
+    reducer = GradientAllReduce(net.parameters(), last=[net.bank], bucket_bytes=1024)
+    x = torch.randn(5, 16)
+    if rank == 1:
+        out.put((rank, "raised", 0.0))
+        out.close()
+        out.join_thread()  # flush the queue before leaving
+        os._exit(3)  # the failure: this rank leaves without joining any collective
+    t0 = time.monotonic()
+    try:
+        net(x).square().mean().backward()
+        reducer.finish(timeout=datetime.timedelta(seconds=5))
+        out.put((rank, "no error", time.monotonic() - t0))
+    except RuntimeError as exc:
+        out.put((rank, f"error: {exc}", time.monotonic() - t0))
+    out.close()
+    out.join_thread()
+    os._exit(0)  # skip the process-group teardown with a dead peer
+
+
+def test_a_rank_that_leaves_makes_the_others_finish_fail() -> None:
+    world = 2
+    ctx = mp.get_context("spawn")
+    out = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_worker, args=(r, world, port, out)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    for _ in range(world):
+        rank, what, seconds = out.get(timeout=90)
+        results[rank] = (what, seconds)
+    for p in procs:
+        p.join(timeout=60)
+    assert procs[1].exitcode == 3
+    assert procs[0].exitcode == 0
+    what, seconds = results[0]
+    assert what.startswith("error: gradient all-reduce of bucket"), what
+    assert seconds < 20.0, f"the failure took {seconds:.1f} s to surface"
+
+
 def test_single_process_is_a_no_op() -> None:
     net = _Net()
     reducer = GradientAllReduce(net.parameters(), last=[net.bank])

@@ -5,9 +5,17 @@ they run the route (code under CUDA stream capture, or engines that hand a
 plugin only its inputs and outputs): its work area is a __device__ array
 inside the library.  Here it is called through the C ABI and checked against
 the regular entry point (da_route_fwd, which takes a caller-allocated work
-buffer) on the same inputs, twice in a row, including a case whose rows need
-the exact repair pass that uses the work area.  The file is named so pytest
-collects it last.
+buffer) on the same inputs, twice in a row.
+
+Only the 64-atom-tile route kernel uses the work area (a CTA ticket, a count
+of rows to recompute exactly and their list, recomputed by the last CTA); the
+wide-tile kernels that R >= 128 with M a multiple of 128 select keep their
+repair lists in shared memory.  So the cases that exercise the array use
+R = 64, or M not a multiple of 128, and include inputs whose every row takes
+the exact repair pass (beta 60, unnormalised inputs of norm ~3 sqrt(R)), plus
+a call at the array's limit of 65536 route rows.  The wide-tile cases check
+that the entry point also serves the shapes that never touch the array.  The
+file is named so pytest collects it last.
 """
 
 from __future__ import annotations
@@ -18,6 +26,7 @@ import pytest
 import torch
 import torch.nn.functional as F
 
+import oracle
 from double_attention_b200 import _lib, ops
 
 pytestmark = pytest.mark.gpu
@@ -56,9 +65,15 @@ def _static_call(q, rows, groups, views, beta, normalize_input):
 @pytest.mark.parametrize(
     ("rows", "r", "m", "groups", "dtype", "beta", "scale", "normalize_input"),
     [
-        (4096, 256, 512, 2, torch.float16, 4.0, 1.0, True),     # config-2 route rows (Q and K groups)
-        (300, 128, 512, 1, torch.bfloat16, 4.0, 1.0, True),     # ragged tail tile
-        (512, 128, 512, 1, torch.bfloat16, 60.0, 3.0, False),   # every row takes the exact repair pass
+        # 64-atom-tile kernel: global ticket, repair count and row list in the static array
+        (4096, 64, 128, 1, torch.bfloat16, 4.0, 1.0, True),
+        (1000, 128, 192, 2, torch.float16, 4.0, 1.0, True),      # M not a multiple of 128, two groups
+        (2000, 64, 128, 1, torch.bfloat16, 60.0, 3.0, False),    # every row repaired from the array's list
+        (700, 128, 192, 1, torch.bfloat16, 60.0, 3.0, False),    # the same with a ragged tail tile
+        (32768, 64, 128, 2, torch.bfloat16, 4.0, 1.0, True),     # groups * rows == 65536, the array's limit
+        # wide-tile kernels (repair lists in shared memory)
+        (4096, 256, 512, 2, torch.float16, 4.0, 1.0, True),      # config-2 route rows (Q and K groups)
+        (512, 128, 512, 1, torch.bfloat16, 60.0, 3.0, False),    # every row repaired
     ],
 )
 def test_static_entry_matches_regular_entry_twice(rows, r, m, groups, dtype, beta, scale, normalize_input) -> None:
@@ -67,6 +82,12 @@ def test_static_entry_matches_regular_entry_twice(rows, r, m, groups, dtype, bet
     z_ref, lse_ref, on_ref = ops._route_forward(q, rows, groups, r, views, torch.tensor(beta, device=dev), 1e-6,
                                                 normalize_input, True)
     torch.cuda.synchronize()
+    # the regular entry itself against the fp32 oracle (value dictionary as the bf16 operand it reads)
+    dk, dv = views.key_t.t().float().cpu(), views.value.float().cpu()
+    for grp in range(groups):
+        expected = oracle.dictionary_route(q[:, grp * r:(grp + 1) * r].float().cpu(), dk, dv, beta, 1e-6,
+                                           normalize_input=normalize_input)
+        assert (z_ref[grp].float().cpu() - expected).abs().max().item() <= MAX_ABS
     for _ in range(2):  # the shared work area must come back clean for the next call
         z, lse, onorm = _static_call(q, rows, groups, views, beta, normalize_input)
         assert torch.isfinite(z.float()).all()
