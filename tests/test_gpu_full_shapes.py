@@ -18,8 +18,8 @@ configurations and check the results against the CPU oracle on a subset:
 Bars as in the other parity tests: outputs max-abs 2e-2 and cosine >= 0.9995;
 route argmax identical on >= 99.9% of rows once fp32 near-ties (top-2 gap
 <= 4e-3) are set aside, with strict agreement printed; module parameter
-gradients cosine >= 0.999 and max-abs 3e-2 * max(1, max |g_ref|); scalars and
-per-map vectors within 5e-2 relative + 5e-2 absolute.
+gradients cosine >= 0.999 and max-abs 3e-2 * max(1, max |g_ref|) (the cosine only where
+max |g_ref| >= 1e-2); scalars and per-map vectors within 5e-2 relative + 5e-2 absolute.
 """
 
 from __future__ import annotations
@@ -62,7 +62,10 @@ def _check_grads(pairs) -> None:
             continue
         bound = 3e-2 * max(1.0, ref.abs().max().item())
         err, cos = (got - ref).abs().max().item(), _cos(got, ref)
-        if err > bound or cos < 0.999:
+        # A gradient whose entries are all below 1e-2 is a sum that cancels (the LM's final-norm bias:
+        # 2048 bf16-rounded token gradients summing to ~1e-3); its direction is set by bf16 rounding under
+        # autocast, so only the absolute bound applies to it.
+        if err > bound or (cos < 0.999 and ref.abs().max().item() >= 1e-2):
             failures.append(f"{key}: max-abs {err:.3e} (bound {bound:.3e}) cosine {cos:.6f}")
     assert not failures, "; ".join(failures)
 
@@ -242,34 +245,34 @@ def test_module_config4_forward() -> None:
 def test_lm_config5_per_gpu_batch() -> None:
     """The config-5 LM (a1, 6 layers, one bank, FFN 1536, vocab 2048, T 1024) at its one-GPU batch of 256
     sequences under bf16 autocast: 524288 route rows per layer (compact route forward, R 256 route backward),
-    coarse attention.  The loss gradient is taken as sum(logits * G) with G non-zero on sequences 0 and 255
-    only, so the parameter gradients are those two sequences' contributions."""
+    coarse attention.  The training loss (cross-entropy, mean over tokens) is taken over sequences 0 and 255
+    only, so the parameter gradients are those two sequences' contributions while every kernel runs on the
+    whole batch."""
     dev = torch.device("cuda")
-    vocab, seq, batch, layers, live = 2048, 1024, 256, 6, (0, 255)
+    vocab, seq, batch, layers, live = 2048, 1024, 256, 6, [0, 255]
     torch.manual_seed(0)
     model = DoubleAttentionLM(vocab, seq, experiment_config("a1"), layers, dictionary_group_size=layers,
                               feedforward_dim=1536).to(dev)
     g = torch.Generator().manual_seed(2)
-    ids = torch.randint(0, vocab, (batch, seq), generator=g)
-    grad = torch.zeros(len(live), seq, vocab)
-    grad.normal_(generator=g)
+    ids = torch.randint(0, vocab, (batch, seq + 1), generator=g)
+    x, y = ids[:, :-1], ids[:, 1:]
     with torch.autocast("cuda", dtype=torch.bfloat16):
-        logits, _ = model(ids.to(dev))
-    full_grad = torch.zeros(batch, seq, vocab, device=dev)
-    full_grad[list(live)] = grad.to(dev)
-    logits.float().backward(full_grad)
+        logits, _ = model(x.to(dev))
+        loss = F.cross_entropy(logits[live].flatten(0, 1), y[live].flatten().to(dev))
+    loss.backward()
     torch.cuda.synchronize()
     assert ops.device_status(dev) == 0
-    got_logits = logits[list(live)].detach().float().cpu()
-    del logits, full_grad
+    got_logits = logits[live].detach().float().cpu()
+    del logits
 
     params, state = _params_for_oracle(model)
     state["lm_head.weight"] = state["token_embedding.weight"]
-    ref_logits, _ = oracle.lm_forward(state, ids[list(live)], None, model.stack.config, layers, layers)
-    ref_logits.backward(grad)
+    ref_logits, ref_loss = oracle.lm_forward(state, x[live], y[live], model.stack.config, layers, layers)
+    ref_loss.backward()
     # the untrained tied-embedding LM's logits reach ~30: the bar scales with their range
     _check("logits (live sequences)", got_logits, ref_logits.detach(),
            max_abs=2e-2 * max(1.0, ref_logits.abs().max().item()))
+    assert abs(loss.item() - ref_loss.item()) <= 2e-3 * max(1.0, abs(ref_loss.item())), (loss.item(), ref_loss.item())
     _check_grads([(k, p.grad, params[k].grad) for k, p in model.named_parameters()])
 
 
