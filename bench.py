@@ -69,8 +69,8 @@ CONFIGS = {
 # kernels whose live duration is measured for the roofline, per mode
 ROOFLINE_KERNELS = {
     "fwd": ("route", "attention"),
-    "fwdbwd": ("route", "attention", "route_bwd", "dict_grads", "attention_bwd"),
-    "train": ("route", "attention", "route_bwd", "dict_grads", "attention_bwd"),
+    "fwdbwd": ("route", "attention", "route_bwd", "attention_bwd"),
+    "train": ("route", "attention", "route_bwd", "attention_bwd"),
 }
 
 
@@ -83,6 +83,8 @@ def parse_args(argv=None):
     p.add_argument("--impl", choices=("b200", "reference"), default="b200")
     p.add_argument("--no-graph", action="store_true", help="time eager launches instead of a CUDA graph")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
+    p.add_argument("--no-reference-gpu", action="store_true",
+                   help="skip timing the reference's own GPU path (baseline/_ref, backend='auto')")
     args = p.parse_args(argv)
     if args.steps is None:
         args.steps = {2: 200, 3: 20, 4: 20, 5: 10}[args.config]
@@ -427,6 +429,81 @@ def cpu_reference(cfg, seconds: float, steps: int | None = None, warmup: int = 0
     return sample_batch * seq / sec, threads, len(times), sample_batch, sec
 
 
+REF_DIR = REPO / "baseline" / "_ref"
+
+
+def reference_gpu(cfg, device, steps: int, flush: torch.Tensor, ours_out: torch.Tensor | None):
+    """The reference's own GPU path as the speed bar: the UNMODIFIED Ahnd6474/double-attention package
+    (installed into baseline/_ref) with backend="auto" -- its Triton kernels and cuBLAS -- on the same
+    seeded weights and inputs, timed like this arm (CUDA events, L2 flushed, eager launches as in the
+    reference's benchmarks/benchmark_attention.py).  Returns a dict for the JSON line, or None when the
+    package is not installed."""
+    if not (REF_DIR / "double_attention").is_dir():
+        return {"unavailable": "reference not installed in baseline/_ref"}
+    sys.path.insert(0, str(REF_DIR))
+    try:
+        import double_attention as ref
+        from double_attention.config import experiment_config as ref_config
+        from double_attention.triton_kernels import TRITON_AVAILABLE
+    finally:
+        sys.path.remove(str(REF_DIR))
+    if not ref.__file__.startswith(str(REF_DIR)):
+        return {"unavailable": f"imported another double_attention ({ref.__file__})"}
+    if not TRITON_AVAILABLE:
+        return {"unavailable": "triton does not import on this box"}
+    stream = torch.cuda.current_stream(device)
+    if cfg["kind"] == "lm":
+        torch.manual_seed(0)
+        model = ref.DoubleAttentionLM(cfg["vocab"], cfg["seq"], ref_config(cfg["preset"], backend="auto"),
+                                      cfg["layers"], dictionary_group_size=cfg["layers"],
+                                      feedforward_dim=cfg["ffn"]).to(device).train()
+        opt = torch.optim.AdamW(model.parameters(), lr=3e-4, fused=True)
+        ids = _token_ids(cfg["batch"], cfg["seq"], cfg["vocab"], seed=2).to(device)
+
+        def step():
+            opt.zero_grad(set_to_none=True)
+            with torch.autocast("cuda", dtype=cfg["dtype"]):
+                _, loss = model(ids[:, :-1], ids[:, 1:])
+            loss.backward()
+            opt.step()
+        out = None
+    else:
+        torch.manual_seed(0)
+        module = ref.SharedDictionaryAttention(ref_config(cfg["preset"], backend="auto"))
+        module = module.to(device=device, dtype=cfg["dtype"]).train(cfg["mode"] == "fwdbwd")
+        shape = (cfg["batch"], cfg["seq"], 512)
+        x = _seeded_normal(shape, 1, cfg["dtype"]).to(device)
+        train = cfg["mode"] == "fwdbwd"
+        if train:
+            dy = _seeded_normal(shape, 1000, cfg["dtype"]).to(device)
+            x.requires_grad_(True)
+
+        def step():
+            if not train:
+                with torch.no_grad():
+                    module(x)
+                return
+            for p in module.parameters():
+                p.grad = None
+            x.grad = None
+            module(x).backward(dy)
+        with torch.no_grad():
+            out = module(x.detach())
+    for _ in range(3):  # includes Triton's JIT compilation
+        step()
+    torch.cuda.synchronize()
+    with ClockSampler(device.index or 0) as clocks:
+        time.sleep(0.05)
+        times = time_steps(step, steps, flush, stream)
+    ms = sum(times) / len(times)
+    line = {"impl": "Ahnd6474/double-attention 0.1.0, unmodified, backend='auto' (Triton kernels + cuBLAS)",
+            "value": cfg["batch"] * cfg["seq"] / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
+            "steps": steps, "clocks": clocks.summary()}
+    if out is not None and ours_out is not None:
+        line["max_abs_vs_this_output"] = float((out.float() - ours_out.float()).abs().max())
+    return line
+
+
 def _mode_words(cfg) -> str:
     return {"fwd": "forward", "fwdbwd": "forward+backward", "train": "LM training step (fwd, bwd, AdamW)"}[cfg["mode"]]
 
@@ -509,7 +586,11 @@ def run_b200(args, cfg, world, rank, local):
     h2d, d2h = work.h2d, work.d2h
 
     # --- roofline of the dominant kernel (rank 0 only; each kernel timed alone, L2 flushed)
-    roofline = cpu_base = None
+    roofline = cpu_base = ref_gpu = None
+    ours_out = None
+    if rank == 0 and world == 1 and cfg["kind"] == "module" and not args.no_reference_gpu:
+        with torch.no_grad():
+            ours_out = work.module(work.x.detach()).float()
     if rank == 0:
         del work, step, graph
         torch.cuda.empty_cache()
@@ -527,6 +608,15 @@ def run_b200(args, cfg, world, rank, local):
                                   "traffic": load_traffic(k, f"config{args.config}")}
                               for k, v in kernels.items() if k != top},
         }
+        if world == 1 and not args.no_reference_gpu:
+            try:
+                ref_gpu = reference_gpu(cfg, device, min(args.steps, 10), flush, ours_out)
+            except Exception as exc:  # reported, never fatal to this arm
+                ref_gpu = {"unavailable": f"{type(exc).__name__}: {exc}"[:300]}
+            if ref_gpu.get("value"):
+                ref_gpu["ratio_this_over_reference"] = value / ref_gpu["value"]
+            del ours_out
+            torch.cuda.empty_cache()
         if world == 1:
             torch.set_num_threads(os.cpu_count() or 1)
             tps, threads, n, sb, sec = cpu_reference(cfg, args.cpu_seconds)
@@ -560,6 +650,7 @@ def run_b200(args, cfg, world, rank, local):
                     "ms_per_step": e2e_ms},
             "roofline": roofline,
             "cpu_baseline": cpu_base,
+            "reference_gpu": ref_gpu,
             "clocks": clock_summary,
             "gpu_launches": launches_per_step * args.steps,
         }

@@ -54,6 +54,9 @@ SIGNATURES: dict[str, list] = {
     "da_gemm_splitk_grouped": [_p, _i64, _i64, _p, _i64, _p, _i64, _i64, _i64, _i64, _i32, _i32, _i32, _p, _p],
     "da_route_bwd": [_p, _i64, _i64, _i64, _i32, _i64, _i64, _i64, _i32, _p, _p, _p, _f32, _i32, _i32, _p, _p, _p,
                      _p, _p, _p, _p, _p, _p, _p, _p],
+    "da_route_bwd_workspace_size": [_i64, _i32, _i64, _i64],  # returns int64 (set below)
+    "da_route_bwd_fused": [_p, _i64, _i64, _i64, _i32, _i64, _i64, _i64, _i32, _p, _p, _p, _f32, _i32, _i32, _p,
+                           _p, _p, _p, _p, _p, _p, _p, _p, _i64, _p, _p],
     "da_attn_bwd_mixed": [_p, _i64, _i64, _i64, _i64, _p, _i64, _i64, _i64, _i64, _p, _p, _i32, _i32, _i32, _i32,
                           _i32, _i32, _p, _i32, _i32, _p, _p, _p, _p, _i32, _p, _p, _p, _p, _p, _p, _p],
     "da_selftest_mma": [_i32, _i32, _i32, _i32, _p, _p, _p, _p, _p],
@@ -105,6 +108,8 @@ def lib() -> ctypes.CDLL:
             handle.da_version.restype = ctypes.c_char_p
             handle.da_last_cuda_error.argtypes = []
             handle.da_last_cuda_error.restype = ctypes.c_int
+            handle.da_route_bwd_workspace_size.argtypes = [_i64, _i32, _i64, _i64]
+            handle.da_route_bwd_workspace_size.restype = ctypes.c_int64
             handle.da_kernel_launches.argtypes = []
             handle.da_kernel_launches.restype = ctypes.c_uint64
             _lib = handle

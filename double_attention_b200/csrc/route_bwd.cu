@@ -62,6 +62,7 @@ struct Params {
   void* dl_out;            // [groups, rows, M] dtype: invn * beta * dLs
   __nv_bfloat16* g_out;    // [groups, rows, R]
   float* dbeta;            // accumulated (may be null)
+  float* row_stats;        // [groups, rows, 2]: invn, delta (may be null)
   int* status;
   int* trace;              // optional progress stamps (debug)
   int compact;             // the two-CTAs-per-SM layout (make_layout)
@@ -456,6 +457,8 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks) route_bwd_kernel(const _
           }
         qn = sqrtf(qn2);
         invn = p.normalize_input ? 1.f / fmaxf(qn, p.eps) : 1.f;
+        if (p.row_stats && live && half == 0)
+          *reinterpret_cast<float2*>(p.row_stats + 2 * idx) = make_float2(invn, delta);
       }
       if (ok && j >= nb) ok = mbar_wait(&dl_empty[sb], ((j - nb) / nb) & 1u, ab, 33);
       ok = __all_sync(0xffffffffu, ok);
@@ -488,7 +491,7 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks) route_bwd_kernel(const _
           for (int e = 0; e < 4; ++e)
             st_shared_v4(dla + half * (kRows * 128) + sw128_offset(r, ch * 4 + e), dk[4 * e], dk[4 * e + 1],
                          dk[4 * e + 2], dk[4 * e + 3]);
-          if (live) {
+          if (live && p.p_out) {
             uint4* pd = reinterpret_cast<uint4*>(p_row + j * kNA + a0);
             uint4* dd = reinterpret_cast<uint4*>(dl_row + j * kNA + a0);
 #pragma unroll
@@ -617,6 +620,7 @@ int launch(const RouteBwdArgs& a, cudaStream_t st) {
   p.dl_out = a.dl_out;
   p.g_out = static_cast<__nv_bfloat16*>(a.g_out);
   p.dbeta = a.dbeta;
+  p.row_stats = a.row_stats;
   p.status = a.status;
   p.trace = debug_trace();
   p.compact = compact ? 1 : 0;
@@ -643,9 +647,9 @@ extern "C" int da_route_bwd(const void* q, int64_t rows, int64_t q_cols, int64_t
                             const float* out_norm, void* dq, void* p_out, void* dl_out, void* g_out, float* dbeta,
                             int* status, void* stream) {
   using namespace da;
-  if (!q || !dict_key_t || !dict_value_t || !beta || !z || !dz || !lse || !out_norm || !dq || !p_out || !dl_out ||
-      !g_out || !status)
+  if (!q || !dict_key_t || !dict_value_t || !beta || !z || !dz || !lse || !out_norm || !dq || !g_out || !status)
     return DA_ERR_NULL;
+  if ((p_out == nullptr) != (dl_out == nullptr)) return DA_ERR_NULL;  // both or neither
   if (int rc = bind_device(q)) return rc;
   if (dtype != DA_BF16 && dtype != DA_F16) return DA_ERR_DTYPE;
   if (rows <= 0 || groups <= 0 || M <= 0) return DA_ERR_SHAPE;

@@ -50,14 +50,23 @@ struct RouteBwdArgs {
   const float* lse;         // [groups, rows] from the forward
   const float* out_norm;    // [groups, rows] from the forward
   void* dq;                 // gradient of q, layout of q (dtype)
-  void* p_out;              // [groups, rows, M] bf16 assignment weights
-  void* dl_out;             // [groups, rows, M] dtype: invn * beta * dLs
+  void* p_out;              // [groups, rows, M] bf16 assignment weights (may be null)
+  void* dl_out;             // [groups, rows, M] dtype: invn * beta * dLs (may be null)
   void* g_out;              // [groups, rows, R] bf16 gradient of the reconstruction
   float* dbeta;             // accumulated, may be null
   int* status;
+  float* row_stats = nullptr;  // [groups, rows, 2] fp32: input inverse norm, delta = <P, dP> (optional)
 };
 
 int route_bwd(const RouteBwdArgs& a, cudaStream_t st);
+
+// The whole route backward with deterministic dictionary gradients (route_dict_grad.cu): the row pass
+// above (dq, g and row_stats into the workspace, no [rows, M] outputs), then the atom-parallel
+// dictionary-gradient kernel and the fixed-order reduction of its partial sums.
+bool route_bwd_fused_supported(const RouteBwdArgs& a);
+int64_t route_bwd_workspace_bytes(int64_t rows, int groups, int64_t R, int64_t M);
+int route_bwd_fused(RouteBwdArgs a, void* workspace, int64_t workspace_bytes, float* d_key, float* d_value,
+                    float* dbeta, cudaStream_t st);
 
 }  // namespace route
 }  // namespace da

@@ -33,7 +33,7 @@ SHAPES = {
 }
 
 
-KERNELS = ("route", "attention", "route_bwd", "dict_grads", "attention_bwd", "projection")
+KERNELS = ("route", "attention", "route_bwd", "route_bwd_rows", "dict_grads_splitk", "attention_bwd", "projection")
 
 
 class _Cfg:
@@ -72,7 +72,10 @@ def make_case(kernel: str, config: int, device: torch.device):
             ops.routed_attention_mixed(routed, value, scales, mix, c)
 
         return run, float(batch) * seq * seq * (cfg.outer_maps * r + d)
-    if kernel == "route_bwd":  # the fused route backward kernel alone (da_route_bwd)
+    if kernel in ("route_bwd", "route_bwd_rows"):
+        # route_bwd: the whole route backward as autograd runs it (da_route_bwd_fused: the row pass, the
+        # atom-parallel dictionary-gradient kernel and the fixed-order reduction of its partial sums);
+        # route_bwd_rows: the row pass alone (da_route_bwd without [rows, M] outputs)
         proj = torch.randn(batch * seq, 2 * h * r, generator=g).to(dtype).to(device)
         dk = F.normalize(torch.randn(r, m, generator=g), dim=0).to(dtype).to(device)
         dv = F.normalize(torch.randn(r, m, generator=g), dim=0).to(dtype).to(device)
@@ -82,23 +85,26 @@ def make_case(kernel: str, config: int, device: torch.device):
         z, lse, onorm = ops._route_forward(proj, rows, groups, r, views, beta, cfg.eps, True, True)
         dz = torch.randn(groups, rows, r, generator=g).to(dtype).to(device)
         dq = torch.empty_like(proj)
-        p_out = torch.empty(groups, rows, m, dtype=torch.bfloat16, device=device)
-        dl_out = torch.empty(groups, rows, m, dtype=dtype, device=device)
-        g_out = torch.empty(groups, rows, r, dtype=torch.bfloat16, device=device)
-        dbeta = torch.zeros(1, device=device)
         ws = ops.workspace(device)
         beta32 = beta.float().reshape(1)
+        if kernel == "route_bwd":
+            def run():
+                ops._route_backward_fused(proj, views.key_t, views.value_t, beta32, z, dz, lse, onorm, dq, rows,
+                                          groups, r, cfg.eps, True, True, True, True, True)
+
+            # dP, dq_hat, dDv and dDk over every route row
+            return run, 8.0 * r * m * groups * rows
+        g_out = torch.empty(groups, rows, r, dtype=torch.bfloat16, device=device)
 
         def run():
             ops.call("da_route_bwd", proj.data_ptr(), rows, proj.shape[1], proj.stride(0), groups, r, r, m,
                      ops.dtype_code(dtype), views.key_t.data_ptr(), views.value_t.data_ptr(), beta32.data_ptr(),
                      cfg.eps, 1, 1, z.data_ptr(), dz.data_ptr(), lse.data_ptr(), onorm.data_ptr(), dq.data_ptr(),
-                     p_out.data_ptr(), dl_out.data_ptr(), g_out.data_ptr(), dbeta.data_ptr(),
-                     ws.status.data_ptr(), ops.stream_ptr(device))
+                     None, None, g_out.data_ptr(), None, ws.status.data_ptr(), ops.stream_ptr(device))
 
-        # dP and dq_hat (the dictionary-gradient GEMMs are timed as "dict_grads")
+        # dP and dq_hat
         return run, 4.0 * r * m * groups * rows
-    if kernel == "dict_grads":  # dDk and dDv split-K GEMMs over all route rows
+    if kernel == "dict_grads_splitk":  # the unfused path's dDk and dDv split-K GEMMs over stored [rows, M] rows
         rows, groups = batch * seq, 2 * h
         proj = torch.randn(rows, 2 * h * r, generator=g).to(dtype).to(device)
         dl_out = (torch.randn(groups, rows, m, generator=g) * 1e-2).to(dtype).to(device)
@@ -155,7 +161,7 @@ def make_case(kernel: str, config: int, device: torch.device):
 
 # cases that enqueue several launches (and memsets): timed as CUDA-graph replays so that host
 # enqueue work cannot fall inside the timed region
-GRAPH_CASES = ("attention_bwd",)
+GRAPH_CASES = ("attention_bwd", "route_bwd")
 
 
 def time_kernel(run, reps: int, device: torch.device, graph: bool = False) -> float:

@@ -449,6 +449,33 @@ def key_dictionary_grad(q: Tensor, col_stride: int, dl: Tensor, out: Tensor) -> 
     return out
 
 
+def route_bwd_fused_supported(q: Tensor, rows: int, col_stride: int, r: int, m: int) -> bool:
+    """Shapes the deterministic fused route backward (da_route_bwd_fused) takes; others use da_route_bwd
+    plus split-K GEMMs over stored [rows, M] weights."""
+    return (r in (128, 256) and m % 128 == 0 and q.shape[1] % 64 == 0 and col_stride % 64 == 0
+            and q.stride(0) % 8 == 0 and rows >= (128 if r == 128 else 64))
+
+
+def _route_backward_fused(q: Tensor, key_t: Tensor, value_t: Tensor, beta: Tensor, z: Tensor, dz: Tensor,
+                          lse: Tensor, onorm: Tensor, dq: Tensor, rows: int, groups: int, col_stride: int, eps: float,
+                          ni: bool, no: bool, need_key: bool, need_value: bool, need_beta: bool):
+    """dq (into ``dq``) and fp32 dDk, dDv [R, M], dbeta [1] from one da_route_bwd_fused call."""
+    m, r = key_t.shape
+    dev = q.device
+    handle = _lib.lib()
+    ws_bytes = int(handle.da_route_bwd_workspace_size(rows, groups, r, m))
+    scratch = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    d_key = torch.empty(r, m, dtype=torch.float32, device=dev) if need_key else None
+    d_value = torch.empty(r, m, dtype=torch.float32, device=dev) if need_value else None
+    dbeta = torch.empty(1, dtype=torch.float32, device=dev) if need_beta else None
+    beta32 = beta.detach().float().reshape(1).contiguous()
+    call("da_route_bwd_fused", q.data_ptr(), rows, q.shape[1], q.stride(0), groups, col_stride, r, m,
+         dtype_code(q.dtype), key_t.data_ptr(), value_t.data_ptr(), beta32.data_ptr(), eps, int(ni), int(no),
+         z.data_ptr(), dz.data_ptr(), lse.data_ptr(), onorm.data_ptr(), dq.data_ptr(), ptr(d_key), ptr(d_value),
+         ptr(dbeta), scratch.data_ptr(), ws_bytes, workspace(dev).status.data_ptr(), stream_ptr(dev))
+    return d_key, d_value, dbeta
+
+
 def _route_backward(ctx, dz: Tensor):
     """dq, fp32 dDk / dDv (into the anchors) and dbeta of one route call."""
     q, key_t, value_t, beta, z, lse, onorm = ctx.saved_tensors
@@ -459,6 +486,14 @@ def _route_backward(ctx, dz: Tensor):
     dz = dz.to(z.dtype).contiguous()
     full = groups * col_stride == q.shape[1] and col_stride == r and q.stride(0) == q.shape[1]
     dq = torch.empty_like(q) if full else torch.zeros_like(q)
+    if route_bwd_fused_supported(q, rows, col_stride, r, m):
+        d_key, d_value, dbeta = _route_backward_fused(q, key_t, value_t, beta, z, dz, lse, onorm, dq, rows, groups,
+                                                      col_stride, eps, ni, no, need[6], need[7], need[8])
+        return (dq if need[0] else None, None, None, None, None, None,
+                None if d_key is None else d_key.to(key_dtype),
+                None if d_value is None else d_value.to(value_dtype),
+                None if dbeta is None else dbeta.view(beta.shape).to(beta.dtype),
+                None, None, None, None, None, None)
     p_out = torch.empty(groups, rows, m, dtype=torch.bfloat16, device=dev)
     dl_out = torch.empty(groups, rows, m, dtype=q.dtype, device=dev)
     g_out = torch.empty(groups, rows, r, dtype=torch.bfloat16, device=dev)

@@ -203,12 +203,40 @@ DA_API int da_route_var_input_bwd(const float* u, const void* q, int64_t q_strid
  * assignment weights; dl_out [groups, rows, M] dtype = the logit gradient
  * divided by the input norm (dDk = sum_groups q_g^T dl_out_g); g_out
  * [groups, rows, R] bf16 = gradient of the reconstruction (dDv = g_out^T
- * p_out); dbeta (may be null) is accumulated (+=). */
+ * p_out); p_out and dl_out may both be null (then only dq and g_out are
+ * written, as da_route_bwd_fused's row pass does); dbeta (may be null) is
+ * accumulated (+=) with fp32 atomics (not bit-reproducible; the fused entry's
+ * dbeta is). */
 DA_API int da_route_bwd(const void* q, int64_t rows, int64_t q_cols, int64_t q_row_stride, int groups,
                         int64_t group_col_stride, int64_t R, int64_t M, int dtype, const void* dict_key_t,
                         const void* dict_value_t, const float* beta, float eps, int normalize_input,
                         int normalize_output, const void* z, const void* dz, const float* lse, const float* out_norm,
                         void* dq, void* p_out, void* dl_out, void* g_out, float* dbeta, int* status, void* stream);
+
+/* The whole route backward with deterministic dictionary gradients: replaces
+ * _DictionaryRouteFunction.backward (triton_kernels.py:1873-1981) including
+ * the two dictionary-gradient GEMMs it leaves to cuBLAS (:1706-1707 fused
+ * path, :1938-1961 multi-kernel path) and its per-row beta gradient
+ * (:1447-1501).  Arguments as da_route_bwd; R in {128, 256}, M a multiple of
+ * 128, q_cols and group_col_stride multiples of 64, rows >= 128 (R = 128) or
+ * >= 64 (R = 256); other shapes return DA_ERR_UNSUPPORTED (use da_route_bwd).
+ * Outputs: dq as da_route_bwd; d_key, d_value [R, M] fp32 = dDk, dDv summed
+ * over every routed row of every group (overwritten; either may be null);
+ * dbeta [1] fp32 (overwritten; may be null).  No [rows, M] tensor is written:
+ * an atom-parallel kernel recomputes the scores and dP per 128-atom tile with
+ * the tile's dictionary rows resident in shared memory, keeps dDk / dDv in
+ * TMEM over a chunk of rows and stores per-chunk partial sums, which a second
+ * kernel adds in a fixed order, so the results are bit-identical from run to
+ * run.  workspace: device memory of at least da_route_bwd_workspace_size()
+ * bytes (16-byte aligned), else DA_ERR_WORKSPACE; its contents need no
+ * initialisation. */
+DA_API int64_t da_route_bwd_workspace_size(int64_t rows, int groups, int64_t R, int64_t M);
+DA_API int da_route_bwd_fused(const void* q, int64_t rows, int64_t q_cols, int64_t q_row_stride, int groups,
+                              int64_t group_col_stride, int64_t R, int64_t M, int dtype, const void* dict_key_t,
+                              const void* dict_value_t, const float* beta, float eps, int normalize_input,
+                              int normalize_output, const void* z, const void* dz, const float* lse,
+                              const float* out_norm, void* dq, float* d_key, float* d_value, float* dbeta,
+                              void* workspace, int64_t workspace_bytes, int* status, void* stream);
 
 /* ---- outer routed attention with the map mix, forward -------------------
  * Replaces routed_attention_triton / _routed_attention_triton_forward
