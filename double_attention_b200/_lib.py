@@ -50,21 +50,24 @@ SIGNATURES: dict[str, list] = {
     "da_attn_fwd": [_p, _i64, _i64, _i64, _i64, _p, _i64, _i64, _i64, _i64, _p, _i32, _i32, _i32, _i32, _i32, _i32,
                     _p, _i32, _i32, _p, _p, _p, _f32, _p, _p, _p, _p],
     "da_attn_bwd_delta": [_p, _p, _i64, _i32, _i32, _p, _p],
-    "da_gemm_splitk": [_p, _i64, _i32, _p, _i64, _i32, _p, _i64, _i64, _i64, _i64, _i32, _i32, _p, _p],
-    "da_gemm_splitk_grouped": [_p, _i64, _i64, _p, _i64, _p, _i64, _i64, _i64, _i64, _i32, _i32, _i32, _p, _p],
+    "da_gemm_splitk_workspace_elems": [_i64, _i64, _i64, _i32],  # returns int64 (set below)
+    "da_gemm_splitk": [_p, _i64, _i32, _p, _i64, _i32, _p, _i64, _i64, _i64, _i64, _i32, _i32, _p, _i64, _p, _p],
+    "da_gemm_splitk_grouped": [_p, _i64, _i64, _p, _i64, _p, _i64, _i64, _i64, _i64, _i32, _i32, _i32, _p, _i64, _p,
+                               _p],
     "da_route_bwd": [_p, _i64, _i64, _i64, _i32, _i64, _i64, _i64, _i32, _p, _p, _p, _f32, _i32, _i32, _p, _p, _p,
-                     _p, _p, _p, _p, _p, _p, _p, _p],
+                     _p, _p, _p, _p, _p, _p, _p, _i64, _p, _p],
     "da_route_bwd_workspace_size": [_i64, _i32, _i64, _i64],  # returns int64 (set below)
     "da_route_bwd_fused": [_p, _i64, _i64, _i64, _i32, _i64, _i64, _i64, _i32, _p, _p, _p, _f32, _i32, _i32, _p,
                            _p, _p, _p, _p, _p, _p, _p, _p, _i64, _p, _p],
+    "da_attn_bwd_workspace_size": [_i32, _i32, _i32],  # returns int64 (set below)
     "da_attn_bwd_mixed": [_p, _i64, _i64, _i64, _i64, _p, _i64, _i64, _i64, _i64, _p, _p, _i32, _i32, _i32, _i32,
-                          _i32, _i32, _p, _i32, _i32, _p, _p, _p, _p, _i32, _p, _p, _p, _p, _p, _p, _p],
+                          _i32, _i32, _p, _i32, _i32, _p, _p, _p, _p, _i32, _p, _p, _p, _p, _p, _p, _i64, _p, _p],
     "da_selftest_mma": [_i32, _i32, _i32, _i32, _p, _p, _p, _p, _p],
     "da_selftest_wait_timeout": [_i64, _i32, _p, _p, _p],
     "da_route_var_weights": [_p, _i64, _i32, _p, _i64, _i32, _i32, _i32, _f32, _f32, _p, _f32, _p, _p, _p],
     "da_route_var_output": [_p, _i64, _i32, _i32, _i32, _f32, _p, _p, _p],
     "da_route_var_output_bwd": [_p, _p, _p, _i64, _i32, _i32, _i32, _f32, _p, _p, _p],
-    "da_route_var_weights_bwd": [_p, _p, _i64, _i32, _p, _p, _i32, _f32, _f32, _p, _i32, _p, _p, _p, _p],
+    "da_route_var_weights_bwd": [_p, _p, _i64, _i32, _p, _p, _i32, _f32, _f32, _p, _i32, _p, _p, _p, _p, _i64, _p],
     "da_route_var_input_bwd": [_p, _p, _i64, _p, _i64, _i32, _i32, _i32, _f32, _p, _i64, _p],
     "da_route_fwd": [_p, _i64, _i64, _i64, _i32, _i64, _i64, _i64, _i32, _p, _p, _p, _p, _f32, _i32, _i32,
                      _p, _p, _p, _p, _p, _i32, _p, _p],
@@ -110,6 +113,8 @@ def lib() -> ctypes.CDLL:
             handle.da_last_cuda_error.restype = ctypes.c_int
             handle.da_route_bwd_workspace_size.argtypes = [_i64, _i32, _i64, _i64]
             handle.da_route_bwd_workspace_size.restype = ctypes.c_int64
+            handle.da_attn_bwd_workspace_size.restype = ctypes.c_int64
+            handle.da_gemm_splitk_workspace_elems.restype = ctypes.c_int64
             handle.da_kernel_launches.argtypes = []
             handle.da_kernel_launches.restype = ctypes.c_uint64
             _lib = handle

@@ -64,6 +64,8 @@ struct Params {
   float* dv;             // fp32 [B*T, D], +=
   float* dscale;         // [maps] d gamma_s, += (may be null)
   float* dweight;        // [maps] d alpha_s, += (dQ kernel with the first sweep; may be null)
+  float* scalar_part;    // [2, 2 * pairs, 4, maps]: per-(CTA, warp) partial sums of d alpha_s and d gamma_s,
+                         // added in a fixed order by scalar_reduce_kernel (null: fp32 atomics)
   int* status;
   int* trace;            // optional post-mortem timeline (debug)
 };
@@ -539,7 +541,11 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
           if (p.dweight && wg == 0) {
             float w = (ok && live && half == 0) ? delta[m] : 0.f;
             for (int o = 16; o; o >>= 1) w += __shfl_xor_sync(0xffffffffu, w, o);
-            if (lane == 0 && w != 0.f) atomicAdd(p.dweight + m, w);
+            if (p.scalar_part) {
+              if (lane == 0) p.scalar_part[((size_t)blockIdx.x * 4 + quad) * maps + m] = w;
+            } else if (lane == 0 && w != 0.f) {
+              atomicAdd(p.dweight + m, w);
+            }
           }
         }
       }
@@ -577,7 +583,11 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
           dg = alpha[m] * (A - C * Bs);
         }
         for (int o = 16; o; o >>= 1) dg += __shfl_xor_sync(0xffffffffu, dg, o);
-        if (lane == 0 && dg != 0.f) atomicAdd(p.dscale + m, dg * gsc);
+        if (p.scalar_part) {
+          if (lane == 0) p.scalar_part[(((size_t)gridDim.x + blockIdx.x) * 4 + quad) * maps + m] = dg * gsc;
+        } else if (lane == 0 && dg != 0.f) {
+          atomicAdd(p.dscale + m, dg * gsc);
+        }
       }
     }
     if (wg == 0 && ok) ok = mbar_wait(&o_full, 0, ab, 34);
@@ -1054,6 +1064,28 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
   if (warp == 1) tmem_dealloc<2>(tmem, L.tmem_cols);
 }
 
+// d alpha_s (kind 0) and d gamma_s (kind 1) += the sum of the dQ kernel's n per-(CTA, warp) partials of
+// map s: every thread adds a strided subset in index order, then a fixed-shape tree over the block.
+__global__ void __launch_bounds__(256) scalar_reduce_kernel(const float* part, int n, int maps, float* dweight,
+                                                            float* dscale) {
+  __shared__ float red[256];
+  grid_dependency_wait();
+  grid_launch_dependents();
+  const int m = blockIdx.x, kind = blockIdx.y;
+  float* out = kind == 0 ? dweight : dscale;
+  if (!out) return;
+  const float* src = part + (size_t)kind * n * maps;
+  float s = 0.f;
+  for (int i = threadIdx.x; i < n; i += 256) s += src[(size_t)i * maps + m];
+  red[threadIdx.x] = s;
+  __syncthreads();
+  for (int w = 128; w; w >>= 1) {
+    if (threadIdx.x < w) red[threadIdx.x] += red[threadIdx.x + w];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) out[m] += red[0];
+}
+
 template <typename Kern>
 int launch_pair(Kern kern, const Layout& L, int pairs, const CUtensorMap& tq, const CUtensorMap& tk,
                 const CUtensorMap& tv, const CUtensorMap& tdy, const CUtensorMap& tacc, const Params& p,
@@ -1069,12 +1101,19 @@ int launch_pair(Kern kern, const Layout& L, int pairs, const CUtensorMap& tq, co
 }  // namespace attn
 }  // namespace da
 
+extern "C" int64_t da_attn_bwd_workspace_size(int B, int T, int maps) {
+  if (B <= 0 || T <= 0 || maps < 1 || maps > da::attn::kMaxMaps) return -1;
+  const int64_t pairs = (int64_t)B * ((T + da::attn::bwdm::kTile - 1) / da::attn::bwdm::kTile);
+  return 2 * (2 * pairs * 4) * maps * (int64_t)sizeof(float);
+}
+
 extern "C" int da_attn_bwd_mixed(const void* q, int64_t q_rows, int64_t q_base, int64_t q_sb, int64_t q_sbr,
                                  const void* k, int64_t k_rows, int64_t k_base, int64_t k_sb, int64_t k_sbr,
                                  const void* v, const void* dy, int B, int T, int R, int D, int maps, int group,
                                  const int* branch0, int causal, int dtype, const float* scales,
                                  const float* weights, const float* lse, float* delta, int delta_given, float* dq,
-                                 float* dk, float* dv, float* dscale, float* dweight, int* status, void* stream) {
+                                 float* dk, float* dv, float* dscale, float* dweight, void* workspace,
+                                 int64_t workspace_bytes, int* status, void* stream) {
   using namespace da;
   using namespace da::attn::bwdm;
   if (!q || !k || !v || !dy || !branch0 || !scales || !lse || !delta || !status) return DA_ERR_NULL;
@@ -1107,6 +1146,14 @@ extern "C" int da_attn_bwd_mixed(const void* q, int64_t q_rows, int64_t q_base, 
   if (q_base < 0 || k_base < 0) return DA_ERR_SHAPE;
   p.scales = scales; p.weights = weights; p.lse = lse; p.delta = delta; p.delta_given = delta_given;
   p.dq = dq; p.dk = dk; p.dv = dv; p.dscale = dscale; p.dweight = dweight; p.status = status;
+  const int npairs = B * ((T + kTile - 1) / kTile);
+  const int64_t n_part = (int64_t)2 * npairs * 4;  // partials per map and kind: (CTA, softmax warp)
+  p.scalar_part = nullptr;
+  if (dscale || (dweight && !delta_given)) {
+    if (!workspace || workspace_bytes < 2 * n_part * maps * (int64_t)sizeof(float)) return DA_ERR_WORKSPACE;
+    if (reinterpret_cast<uintptr_t>(workspace) & 15) return DA_ERR_ALIGN;
+    p.scalar_part = static_cast<float*>(workspace);
+  }
   p.trace = debug_trace();
   const CUtensorMapDataType tdt = dtype == DA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap tq, tk, tv, tdy, tq128, tk128;
@@ -1137,6 +1184,12 @@ extern "C" int da_attn_bwd_mixed(const void* q, int64_t q_rows, int64_t q_base, 
     rc = bf16 ? launch_pair(dq_mixed_kernel<__nv_bfloat16>, L, pairs, tq, tk, tv, tdy, tk128, p, st)
               : launch_pair(dq_mixed_kernel<__half>, L, pairs, tq, tk, tv, tdy, tk128, p, st);
     if (rc) return rc;
+    if (p.scalar_part) {
+      rc = launch_kernel(scalar_reduce_kernel, dim3((unsigned)maps, 2, 1), dim3(256, 1, 1), 0, st, false,
+                         (const float*)p.scalar_part, (int)n_part, maps, delta_given ? (float*)nullptr : dweight,
+                         dscale);
+      if (rc) return rc;
+    }
   }
   if (dk) {
     const Layout L = make_layout(1, maps, group, R, D);

@@ -37,6 +37,10 @@ struct Params {
   // grouped K (MN-major A only): K stage kb belongs to group kb / kseg, whose A columns start
   // a_goff further right and whose A rows restart at 0; 0 = one group
   int kseg = 0, a_goff = 0, a_inner = 0;
+  // split-K partial sums: with `partial` set every split stores its [M, N] partial (dense, row stride N) at
+  // partial + split * M * N and splitk_reduce_kernel adds them in split order (deterministic); null: each
+  // split adds its partial into C with fp32 atomics (order-dependent rounding)
+  float* partial = nullptr;
 };
 
 template <typename T, int kN, bool kAmn, bool kBmn>
@@ -145,7 +149,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + c, v);
         tmem_wait_ld();
         if (!live || n0 + c >= p.N) continue;
-        if (split) {
+        if (split && p.partial) {
+          float4* dst = reinterpret_cast<float4*>(p.partial + ((size_t)blockIdx.z * p.M + row) * p.N + n0 + c);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) dst[e] = make_float4(v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3]);
+        } else if (split) {
           float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.c) + (size_t)row * p.ldc + n0 + c);
 #pragma unroll
           for (int e = 0; e < 8; ++e) atomicAdd(dst + e, make_float4(v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3]));
@@ -319,6 +327,46 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_seg_kernel(const __grid_cons
   if (warp == 1) tmem_dealloc<1>(tmem, kN);
 }
 
+// C[m, n] += sum over splits z, in index order, of partial[z, m, n] (four columns per thread).
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* partial, int splits, int M, int N, float* c,
+                                                            int64_t ldc) {
+  grid_dependency_wait();
+  grid_launch_dependents();
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // float4 index
+  const int64_t per_row = N / 4;
+  if (i >= (int64_t)M * per_row) return;
+  const int64_t row = i / per_row, col = (i % per_row) * 4;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int z = 0; z < splits; ++z) {
+    const float4 v = *reinterpret_cast<const float4*>(partial + ((size_t)z * M + row) * N + col);
+    acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+  }
+  float4* dst = reinterpret_cast<float4*>(c + row * ldc + col);
+  float4 o = *dst;
+  o.x += acc.x; o.y += acc.y; o.z += acc.z; o.w += acc.w;
+  *dst = o;
+}
+
+// Split count and K stages per split of a split-K product (the same plan for the workspace query and the
+// launch): about two CTAs per SM-sized wave of 128 x 128 output tiles unless `splits` asks otherwise.
+inline void splitk_plan(int64_t M, int64_t N, int64_t K, int splits, int* out_splits, int* out_kps) {
+  const int nk = (int)((K + kBK - 1) / kBK);
+  if (splits <= 0) {
+    const int tiles = (int)((M / 128) * (N / 128));
+    splits = (2 * sm_count() + tiles - 1) / tiles;
+  }
+  int kps = (nk + splits - 1) / splits;
+  if (kps < 1) kps = 1;
+  *out_splits = (nk + kps - 1) / kps;  // every split gets at least one K stage
+  *out_kps = kps;
+}
+
+inline int splitk_reduce(const Params& p, int splits, cudaStream_t st) {
+  const int64_t n4 = (int64_t)p.M * (p.N / 4);
+  return launch_kernel(splitk_reduce_kernel, dim3((unsigned)((n4 + 255) / 256)), dim3(256), 0, st, false,
+                       (const float*)p.partial, splits, p.M, p.N, reinterpret_cast<float*>(p.c), p.ldc);
+}
+
 template <typename T, int kN, bool kAmn, bool kBmn>
 int launch(const void* A, int64_t lda, const void* B, int64_t ldb, const Params& p, int splits, cudaStream_t st) {
   using C = Cfg<kN>;
@@ -378,9 +426,16 @@ extern "C" int da_gemm(const void* A, int64_t lda, int a_mn_major, const void* B
   return gemm::dispatch<__half>(a_mn_major, b_mn_major, n_tile, A, lda, B, ldb, p, 1, st);
 }
 
+extern "C" int64_t da_gemm_splitk_workspace_elems(int64_t M, int64_t N, int64_t K, int splits) {
+  if (M <= 0 || N <= 0 || K <= 0 || M % 128 || N % 128) return -1;
+  int s = 0, kps = 0;
+  da::gemm::splitk_plan(M, N, K, splits, &s, &kps);
+  return (int64_t)s * M * N;
+}
+
 extern "C" int da_gemm_splitk(const void* A, int64_t lda, int a_mn_major, const void* B, int64_t ldb, int b_mn_major,
                               float* C, int64_t ldc, int64_t M, int64_t N, int64_t K, int dtype, int splits,
-                              int* status, void* stream) {
+                              float* workspace, int64_t workspace_elems, int* status, void* stream) {
   using namespace da;
   if (!A || !B || !C || !status) return DA_ERR_NULL;
   if (int rc = bind_device(A)) return rc;
@@ -388,20 +443,22 @@ extern "C" int da_gemm_splitk(const void* A, int64_t lda, int a_mn_major, const 
   if (M <= 0 || N <= 0 || K <= 0 || N % 128 || M % 128) return DA_ERR_SHAPE;
   if ((lda % 8) || (ldb % 8)) return DA_ERR_ALIGN;
   if ((reinterpret_cast<uintptr_t>(C) & 15) || (ldc % 4)) return DA_ERR_ALIGN;
-  const int nk = (int)((K + gemm::kBK - 1) / gemm::kBK);
   const int n_tile = 128;
-  if (splits <= 0) {  // about two CTAs per SM-sized wave of output tiles
-    const int tiles = (int)((M / 128) * (N / n_tile));
-    splits = (2 * sm_count() + tiles - 1) / tiles;
-  }
-  int kps = (nk + splits - 1) / splits;
-  if (kps < 1) kps = 1;
-  splits = (nk + kps - 1) / kps;  // every split gets at least one K stage
+  int kps = 0;
+  gemm::splitk_plan(M, N, K, splits, &splits, &kps);
   gemm::Params p{(int)M, (int)N, (int)K, C, ldc, 1, 1, status, kps};
+  if (workspace) {
+    if (workspace_elems < (int64_t)splits * M * N) return DA_ERR_WORKSPACE;
+    if (reinterpret_cast<uintptr_t>(workspace) & 15) return DA_ERR_ALIGN;
+    p.partial = workspace;
+  }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (dtype == DA_BF16)
-    return gemm::dispatch<__nv_bfloat16>(a_mn_major, b_mn_major, n_tile, A, lda, B, ldb, p, splits, st);
-  return gemm::dispatch<__half>(a_mn_major, b_mn_major, n_tile, A, lda, B, ldb, p, splits, st);
+  int rc = dtype == DA_BF16
+               ? gemm::dispatch<__nv_bfloat16>(a_mn_major, b_mn_major, n_tile, A, lda, B, ldb, p, splits, st)
+               : gemm::dispatch<__half>(a_mn_major, b_mn_major, n_tile, A, lda, B, ldb, p, splits, st);
+  // one split accumulates straight into C (the kernel's non-split epilogue)
+  if (rc || !p.partial || splits == 1) return rc;
+  return gemm::splitk_reduce(p, splits, st);
 }
 
 extern "C" int da_gemm_segments(const void* A, int64_t lda, int64_t M, int64_t K, int dtype, int nseg,
@@ -472,7 +529,8 @@ extern "C" int da_gemm_segments(const void* A, int64_t lda, int64_t M, int64_t K
 
 extern "C" int da_gemm_splitk_grouped(const void* A, int64_t lda, int64_t a_group_cols, const void* B, int64_t ldb,
                                       float* C, int64_t ldc, int64_t M, int64_t N, int64_t K_group, int groups,
-                                      int dtype, int splits, int* status, void* stream) {
+                                      int dtype, int splits, float* workspace, int64_t workspace_elems,
+                                      int* status, void* stream) {
   using namespace da;
   if (!A || !B || !C || !status) return DA_ERR_NULL;
   if (int rc = bind_device(A)) return rc;
@@ -483,19 +541,20 @@ extern "C" int da_gemm_splitk_grouped(const void* A, int64_t lda, int64_t a_grou
   if ((int64_t)(groups - 1) * a_group_cols + M > lda) return DA_ERR_SHAPE;
   if ((reinterpret_cast<uintptr_t>(C) & 15) || (ldc % 4)) return DA_ERR_ALIGN;
   const int64_t K = K_group * groups;
-  const int nk = (int)(K / gemm::kBK);
-  if (splits <= 0) {  // about two CTAs per SM-sized wave of output tiles
-    const int tiles = (int)((M / 128) * (N / 128));
-    splits = (2 * sm_count() + tiles - 1) / tiles;
-  }
-  int kps = (nk + splits - 1) / splits;
-  if (kps < 1) kps = 1;
-  splits = (nk + kps - 1) / kps;
+  int kps = 0;
+  gemm::splitk_plan(M, N, K, splits, &splits, &kps);
   gemm::Params p{(int)M, (int)N, (int)K, C, ldc, 1, 1, status, kps};
   p.kseg = (int)(K_group / gemm::kBK);
   p.a_goff = (int)a_group_cols;
   p.a_inner = (int)((groups - 1) * a_group_cols + M);
+  if (workspace) {
+    if (workspace_elems < (int64_t)splits * M * N) return DA_ERR_WORKSPACE;
+    if (reinterpret_cast<uintptr_t>(workspace) & 15) return DA_ERR_ALIGN;
+    p.partial = workspace;
+  }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (dtype == DA_BF16) return gemm::dispatch<__nv_bfloat16>(1, 1, 128, A, lda, B, ldb, p, splits, st);
-  return gemm::dispatch<__half>(1, 1, 128, A, lda, B, ldb, p, splits, st);
+  int rc = dtype == DA_BF16 ? gemm::dispatch<__nv_bfloat16>(1, 1, 128, A, lda, B, ldb, p, splits, st)
+                            : gemm::dispatch<__half>(1, 1, 128, A, lda, B, ldb, p, splits, st);
+  if (rc || !p.partial || splits == 1) return rc;
+  return gemm::splitk_reduce(p, splits, st);
 }

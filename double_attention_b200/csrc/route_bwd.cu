@@ -63,6 +63,7 @@ struct Params {
   __nv_bfloat16* g_out;    // [groups, rows, R]
   float* dbeta;            // accumulated (may be null)
   float* row_stats;        // [groups, rows, 2]: invn, delta (may be null)
+  float* dbeta_part;       // [2 * pairs * 4]: per-(CTA, warp) dbeta partials summed in order (null: atomics)
   int* status;
   int* trace;              // optional progress stamps (debug)
   int compact;             // the two-CTAs-per-SM layout (make_layout)
@@ -511,7 +512,11 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks) route_bwd_kernel(const _
     if (arriver) trace_time(p.trace, 3);
     if (p.dbeta) {
       for (int o = 16; o; o >>= 1) dbeta += __shfl_xor_sync(0xffffffffu, dbeta, o);
-      if (lane == 0 && ok) atomicAdd(p.dbeta, dbeta);
+      if (p.dbeta_part) {
+        if (lane == 0) p.dbeta_part[blockIdx.x * 4 + quad] = ok ? dbeta : 0.f;
+      } else if (lane == 0 && ok) {
+        atomicAdd(p.dbeta, dbeta);
+      }
     }
 
     // ---- epilogue: dq = u - q_hat <q_hat, u>   (u = invn * dq_hat, folded TMEM)
@@ -579,6 +584,22 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks) route_bwd_kernel(const _
   if (threadIdx.x == 0) trace_time(p.trace, 5);
 }
 
+// *dbeta += the sum of n partials: strided in index order per thread, then a fixed tree.
+__global__ void __launch_bounds__(256) dbeta_sum_kernel(const float* part, int n, float* dbeta) {
+  __shared__ float red[256];
+  grid_dependency_wait();
+  grid_launch_dependents();
+  float s = 0.f;
+  for (int i = threadIdx.x; i < n; i += 256) s += part[i];
+  red[threadIdx.x] = s;
+  __syncthreads();
+  for (int w = 128; w; w >>= 1) {
+    if (threadIdx.x < w) red[threadIdx.x] += red[threadIdx.x + w];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *dbeta += red[0];
+}
+
 template <typename T>
 int launch(const RouteBwdArgs& a, cudaStream_t st) {
   const long pairs = (long)a.groups * ((a.rows + 127) / 128);
@@ -621,6 +642,7 @@ int launch(const RouteBwdArgs& a, cudaStream_t st) {
   p.g_out = static_cast<__nv_bfloat16*>(a.g_out);
   p.dbeta = a.dbeta;
   p.row_stats = a.row_stats;
+  p.dbeta_part = a.dbeta ? a.dbeta_part : nullptr;
   p.status = a.status;
   p.trace = debug_trace();
   p.compact = compact ? 1 : 0;
@@ -628,7 +650,12 @@ int launch(const RouteBwdArgs& a, cudaStream_t st) {
   const int smem = ((L.smem < 120 * 1024 && !compact) ? 120 * 1024 : L.smem) + 1024;  // one CTA per SM unless compact
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return record_cuda_error();
-  return launch_kernel(kern, dim3((unsigned)(2 * pairs), 1, 1), dim3(kThreads, 1, 1), smem, st, true, tq, tdk, tdv, tz, tdz, p);
+  if (int rc = launch_kernel(kern, dim3((unsigned)(2 * pairs), 1, 1), dim3(kThreads, 1, 1), smem, st, true, tq, tdk,
+                             tdv, tz, tdz, p))
+    return rc;
+  if (!p.dbeta_part) return DA_OK;
+  return launch_kernel(dbeta_sum_kernel, dim3(1), dim3(256), 0, st, false, (const float*)p.dbeta_part,
+                       (int)(8 * pairs), a.dbeta);
 }
 
 }  // namespace bwd
@@ -645,7 +672,7 @@ extern "C" int da_route_bwd(const void* q, int64_t rows, int64_t q_cols, int64_t
                             const void* dict_value_t, const float* beta, float eps, int normalize_input,
                             int normalize_output, const void* z, const void* dz, const float* lse,
                             const float* out_norm, void* dq, void* p_out, void* dl_out, void* g_out, float* dbeta,
-                            int* status, void* stream) {
+                            float* dbeta_work, int64_t dbeta_work_elems, int* status, void* stream) {
   using namespace da;
   if (!q || !dict_key_t || !dict_value_t || !beta || !z || !dz || !lse || !out_norm || !dq || !g_out || !status)
     return DA_ERR_NULL;
@@ -670,5 +697,9 @@ extern "C" int da_route_bwd(const void* q, int64_t rows, int64_t q_cols, int64_t
                         eps,    normalize_input, normalize_output, z,          dz,     lse,
                         out_norm, dq,      p_out,            dl_out,           g_out,  dbeta,
                         status};
+  if (dbeta && dbeta_work) {
+    if (dbeta_work_elems < 8 * (int64_t)groups * ((rows + 127) / 128)) return DA_ERR_WORKSPACE;
+    a.dbeta_part = dbeta_work;
+  }
   return route::route_bwd(a, static_cast<cudaStream_t>(stream));
 }

@@ -56,6 +56,7 @@ struct RouteBwdArgs {
   float* dbeta;             // accumulated, may be null
   int* status;
   float* row_stats = nullptr;  // [groups, rows, 2] fp32: input inverse norm, delta = <P, dP> (optional)
+  float* dbeta_part = nullptr; // [8 * pairs] per-(CTA, warp) dbeta partials, summed in order (optional)
 };
 
 int route_bwd(const RouteBwdArgs& a, cudaStream_t st);

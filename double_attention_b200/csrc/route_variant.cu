@@ -210,7 +210,7 @@ __global__ void __launch_bounds__(32 * kWarps) weights_bwd_kernel(const float* _
                                                                  const float4* __restrict__ stats,
                                                                  const float* __restrict__ delta, RowCfg c,
                                                                  T* __restrict__ dS, __nv_bfloat16* __restrict__ W,
-                                                                 float* __restrict__ dbeta) {
+                                                                 float* __restrict__ dbeta_part) {
   grid_dependency_wait();
   grid_launch_dependents();
   const int lane = threadIdx.x % 32;
@@ -280,7 +280,7 @@ __global__ void __launch_bounds__(32 * kWarps) weights_bwd_kernel(const float* _
       if (lane + 32 * i < c.M) dS[row * c.M + lane + 32 * i] = from_f<T>(d[i] * invn);
     }
   }
-  if (dbeta && !(c.flags & DA_ROUTE_DIRECT_SILU)) {
+  if (dbeta_part && !(c.flags & DA_ROUTE_DIRECT_SILU)) {  // this block's beta-gradient partial (fixed order)
     __shared__ float part[kWarps];
     db = warp_sum(db);
     if (lane == 0) part[threadIdx.x / 32] = db;
@@ -288,9 +288,25 @@ __global__ void __launch_bounds__(32 * kWarps) weights_bwd_kernel(const float* _
     if (threadIdx.x == 0) {
       float t = 0.f;
       for (int i = 0; i < kWarps; ++i) t += part[i];
-      atomicAdd(dbeta, t);
+      dbeta_part[blockIdx.x] = t;
     }
   }
+}
+
+// *dbeta += the sum of n per-block partials: strided in index order per thread, then a fixed tree.
+__global__ void __launch_bounds__(256) dbeta_reduce_kernel(const float* part, int n, float* dbeta) {
+  __shared__ float red[256];
+  grid_dependency_wait();
+  grid_launch_dependents();
+  float s = 0.f;
+  for (int i = threadIdx.x; i < n; i += 256) s += part[i];
+  red[threadIdx.x] = s;
+  __syncthreads();
+  for (int w = 128; w; w >>= 1) {
+    if (threadIdx.x < w) red[threadIdx.x] += red[threadIdx.x + w];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *dbeta += red[0];
 }
 
 // Input-normalisation backward: dq = u - q_hat <q_hat, u> with u = dS . Dk^T
@@ -329,11 +345,16 @@ int launch_weights(const float* S, int64_t rows, const void* q, int64_t q_stride
 
 template <typename T, int NPL>
 int launch_weights_bwd(const float* S, const float* dW, int64_t rows, const float* stats, const float* delta,
-                       const RowCfg& c, void* dS, void* W, float* dbeta, cudaStream_t st) {
+                       const RowCfg& c, void* dS, void* W, float* dbeta, float* dbeta_part, cudaStream_t st) {
   const dim3 grid((unsigned)((rows + kWarps - 1) / kWarps));
-  return launch_kernel(weights_bwd_kernel<T, NPL>, grid, dim3(32 * kWarps), 0, st, false, S, dW, rows,
-                       reinterpret_cast<const float4*>(stats), delta, c, static_cast<T*>(dS),
-                       static_cast<__nv_bfloat16*>(W), dbeta);
+  const bool want_beta = dbeta && !(c.flags & DA_ROUTE_DIRECT_SILU);
+  if (int rc = launch_kernel(weights_bwd_kernel<T, NPL>, grid, dim3(32 * kWarps), 0, st, false, S, dW, rows,
+                             reinterpret_cast<const float4*>(stats), delta, c, static_cast<T*>(dS),
+                             static_cast<__nv_bfloat16*>(W), want_beta ? dbeta_part : (float*)nullptr))
+    return rc;
+  if (!want_beta) return DA_OK;
+  return launch_kernel(dbeta_reduce_kernel, dim3(1), dim3(256), 0, st, false, (const float*)dbeta_part,
+                       (int)grid.x, dbeta);
 }
 
 // Values per lane for a row of M (M <= 2048).
@@ -415,11 +436,13 @@ extern "C" int da_route_var_output_bwd(const void* z, const void* dz, const floa
 extern "C" int da_route_var_weights_bwd(const float* S, const float* dW, int64_t rows, int M, const float* stats,
                                         const float* delta, int flags, float silu_gain, float std_scale,
                                         const float* beta, int dtype, void* dS, void* W, float* dbeta,
-                                        void* stream) {
+                                        float* dbeta_work, int64_t dbeta_work_elems, void* stream) {
   using namespace da;
   using namespace da::route_var;
   if (!S || !dW || !stats || !dS || !W || (!beta && !(flags & DA_ROUTE_DIRECT_SILU))) return DA_ERR_NULL;
   if (int rc = check_cfg(rows, M, flags, silu_gain, std_scale)) return rc;
+  if (dbeta && !(flags & DA_ROUTE_DIRECT_SILU) && (!dbeta_work || dbeta_work_elems < (rows + kWarps - 1) / kWarps))
+    return DA_ERR_WORKSPACE;
   if (dtype != DA_F16 && dtype != DA_BF16) return DA_ERR_DTYPE;
   if (int rc = bind_device(S)) return rc;
   const RowCfg c{M, flags, silu_gain, std_scale, 0.f, beta};
@@ -427,10 +450,10 @@ extern "C" int da_route_var_weights_bwd(const float* S, const float* dW, int64_t
   const int npl = npl_for(M);
 #define DA_RV_B(TT)                                                                                  \
   switch (npl) {                                                                                     \
-    case 16: return launch_weights_bwd<TT, 16>(S, dW, rows, stats, delta, c, dS, W, dbeta, st);             \
-    case 32: return launch_weights_bwd<TT, 32>(S, dW, rows, stats, delta, c, dS, W, dbeta, st);             \
-    case 48: return launch_weights_bwd<TT, 48>(S, dW, rows, stats, delta, c, dS, W, dbeta, st);             \
-    default: return launch_weights_bwd<TT, 64>(S, dW, rows, stats, delta, c, dS, W, dbeta, st);             \
+    case 16: return launch_weights_bwd<TT, 16>(S, dW, rows, stats, delta, c, dS, W, dbeta, dbeta_work, st);             \
+    case 32: return launch_weights_bwd<TT, 32>(S, dW, rows, stats, delta, c, dS, W, dbeta, dbeta_work, st);             \
+    case 48: return launch_weights_bwd<TT, 48>(S, dW, rows, stats, delta, c, dS, W, dbeta, dbeta_work, st);             \
+    default: return launch_weights_bwd<TT, 64>(S, dW, rows, stats, delta, c, dS, W, dbeta, dbeta_work, st);             \
   }
   if (dtype == DA_BF16) { DA_RV_B(__nv_bfloat16) }
   DA_RV_B(__half)

@@ -100,7 +100,7 @@ def make_case(kernel: str, config: int, device: torch.device):
             ops.call("da_route_bwd", proj.data_ptr(), rows, proj.shape[1], proj.stride(0), groups, r, r, m,
                      ops.dtype_code(dtype), views.key_t.data_ptr(), views.value_t.data_ptr(), beta32.data_ptr(),
                      cfg.eps, 1, 1, z.data_ptr(), dz.data_ptr(), lse.data_ptr(), onorm.data_ptr(), dq.data_ptr(),
-                     None, None, g_out.data_ptr(), None, ws.status.data_ptr(), ops.stream_ptr(device))
+                     None, None, g_out.data_ptr(), None, None, 0, ws.status.data_ptr(), ops.stream_ptr(device))
 
         # dP and dq_hat
         return run, 4.0 * r * m * groups * rows

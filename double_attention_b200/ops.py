@@ -426,10 +426,14 @@ class _Route(torch.autograd.Function):
 
 def gemm_splitk(a: Tensor, lda: int, a_mn: bool, b: Tensor, ldb: int, b_mn: bool, m: int, n: int, k: int,
                 out: Tensor, splits: int = 0) -> Tensor:
-    """out[m, n] += sum_k A(m, k) B(n, k) in fp32, K split over CTAs (see da_gemm_splitk)."""
+    """out[m, n] += sum_k A(m, k) B(n, k) in fp32, K split over CTAs whose partial sums are added in a fixed
+    order (see da_gemm_splitk), so the result is bit-reproducible."""
     ws = workspace(out.device)
+    elems = int(_lib.lib().da_gemm_splitk_workspace_elems(m, n, k, splits))
+    part = torch.empty(max(elems, 4), dtype=torch.float32, device=out.device)
     call("da_gemm_splitk", a.data_ptr(), lda, int(a_mn), b.data_ptr(), ldb, int(b_mn), out.data_ptr(), out.stride(0),
-         m, n, k, dtype_code(a.dtype), splits, ws.status.data_ptr(), stream_ptr(out.device))
+         m, n, k, dtype_code(a.dtype), splits, part.data_ptr(), part.numel(), ws.status.data_ptr(),
+         stream_ptr(out.device))
     return out
 
 
@@ -440,9 +444,11 @@ def key_dictionary_grad(q: Tensor, col_stride: int, dl: Tensor, out: Tensor) -> 
     groups, rows, m = dl.shape
     r = out.shape[0]
     if groups > 1 and rows % 64 == 0 and col_stride % 8 == 0:
+        elems = int(_lib.lib().da_gemm_splitk_workspace_elems(r, m, rows * groups, 0))
+        part = torch.empty(max(elems, 4), dtype=torch.float32, device=q.device)
         call("da_gemm_splitk_grouped", q.data_ptr(), q.stride(0), col_stride, dl.data_ptr(), m, out.data_ptr(),
-             out.stride(0), r, m, rows, groups, dtype_code(q.dtype), 0, workspace(q.device).status.data_ptr(),
-             stream_ptr(q.device))
+             out.stride(0), r, m, rows, groups, dtype_code(q.dtype), 0, part.data_ptr(), part.numel(),
+             workspace(q.device).status.data_ptr(), stream_ptr(q.device))
     else:
         for g in range(groups):
             gemm_splitk(q[:, g * col_stride:], q.stride(0), True, dl[g], m, True, r, m, rows, out)
@@ -498,12 +504,15 @@ def _route_backward(ctx, dz: Tensor):
     dl_out = torch.empty(groups, rows, m, dtype=q.dtype, device=dev)
     g_out = torch.empty(groups, rows, r, dtype=torch.bfloat16, device=dev)
     dbeta = torch.zeros(1, dtype=torch.float32, device=dev) if need[8] else None
+    # per-(CTA, warp) dbeta partials, added in a fixed order by the library
+    dbeta_work = torch.empty(8 * groups * ((rows + 127) // 128), dtype=torch.float32, device=dev) if need[8] else None
     ws = workspace(dev)
     beta32 = beta.detach().float().reshape(1).contiguous()
     call("da_route_bwd", q.data_ptr(), rows, q.shape[1], q.stride(0), groups, col_stride, r, m, dtype_code(q.dtype),
          key_t.data_ptr(), value_t.data_ptr(), beta32.data_ptr(), eps, int(ni), int(no), z.data_ptr(), dz.data_ptr(),
          lse.data_ptr(), onorm.data_ptr(), dq.data_ptr(), p_out.data_ptr(), dl_out.data_ptr(), g_out.data_ptr(),
-         ptr(dbeta), ws.status.data_ptr(), stream_ptr(dev))
+         ptr(dbeta), ptr(dbeta_work), 0 if dbeta_work is None else dbeta_work.numel(), ws.status.data_ptr(),
+         stream_ptr(dev))
     d_key = d_value = None
     if need[6]:  # dDk = sum_groups q_g^T dL'_g  (dL' already carries 1 / ||q||)
         d_key = torch.zeros(r, m, dtype=torch.float32, device=dev)
@@ -617,6 +626,7 @@ class _RouteVariantFn(torch.autograd.Function):
         ds_buf = torch.empty(rows, m, dtype=q.dtype, device=dev)
         w_buf = torch.empty(rows, m, dtype=torch.bfloat16, device=dev)
         u_buf = torch.empty(rows, r, dtype=torch.float32, device=dev)
+        dbeta_work = torch.empty((rows + 7) // 8, dtype=torch.float32, device=dev)  # per-8-row dbeta partials
         for g in range(groups):
             qg = q[:, g * col_stride:]
             call("da_route_var_output_bwd", z[g].data_ptr(), dz[g].data_ptr(), onorm[g].data_ptr(), rows, r, dt,
@@ -625,7 +635,7 @@ class _RouteVariantFn(torch.autograd.Function):
             gemm(g_buf, False, value_t, False, rows, m, r, dw_buf)  # dW = g . Dv
             call("da_route_var_weights_bwd", s_buf.data_ptr(), dw_buf.data_ptr(), rows, m, stats[g].data_ptr(),
                  delta.data_ptr(), flags, variant.silu_gain, variant.std_scale, beta32.data_ptr(), dt, ds_buf.data_ptr(),
-                 w_buf.data_ptr(), ptr(dbeta), st)
+                 w_buf.data_ptr(), ptr(dbeta), dbeta_work.data_ptr(), dbeta_work.numel(), st)
             if need[0]:
                 gemm(ds_buf, False, key, False, rows, r, m, u_buf)  # u = dS . Dk^T
                 call("da_route_var_input_bwd", u_buf.data_ptr(), qg.data_ptr(), q.stride(0), stats[g].data_ptr(),
@@ -783,11 +793,14 @@ def _attention_backward(q: RowMap, k: RowMap, v: Tensor, dy: Tensor, batch: int,
     dev = v.device
     ws = workspace(dev)
     b0 = (ctypes_int_array(MAX_MAPS))(*(branch0 + [0] * (MAX_MAPS - len(branch0))))
+    # per-(CTA, warp) partial sums of d gamma / d alpha, added in a fixed order by the library
+    part_bytes = int(_lib.lib().da_attn_bwd_workspace_size(batch, length, maps))
+    part = torch.empty(part_bytes, dtype=torch.uint8, device=dev)
     call("da_attn_bwd_mixed", q.tensor.data_ptr(), q.rows, q.base, q.sb, q.sbr, k.tensor.data_ptr(), k.rows, k.base,
          k.sb, k.sbr, v.data_ptr(), dy.data_ptr(), batch, length, r, d, maps, group, ctypes_addressof(b0),
          int(causal), dtype_code(q.tensor.dtype), scales.data_ptr(), ptr(weights), lse.data_ptr(), delta.data_ptr(),
-         int(delta_given), ptr(dq), ptr(dk), ptr(dv), ptr(dscale), ptr(dweight), ws.status.data_ptr(),
-         stream_ptr(dev))
+         int(delta_given), ptr(dq), ptr(dk), ptr(dv), ptr(dscale), ptr(dweight), part.data_ptr(), part_bytes,
+         ws.status.data_ptr(), stream_ptr(dev))
 
 
 def ctypes_int_array(n: int):

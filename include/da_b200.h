@@ -177,10 +177,13 @@ DA_API int da_route_var_output_bwd(const void* z, const void* dz, const float* o
  * null: <W, dW> is then summed from dW).  Writes dS [rows, M] (dtype) = dL/d(q . Dk)
  * (the logit gradient times 1/||q||: dDk = q^T dS, u = dS . Dk^T), W
  * [rows, M] bf16 again (dDv = g^T W) and adds the beta gradient to *dbeta
- * (softmax assignment; may be null). */
+ * (softmax assignment; may be null): one partial per 8 rows goes to
+ * dbeta_work (fp32, at least ceil(rows / 8) elements, else DA_ERR_WORKSPACE)
+ * and a second kernel adds them in a fixed order (bit-reproducible). */
 DA_API int da_route_var_weights_bwd(const float* S, const float* dW, int64_t rows, int M, const float* stats,
                                     const float* delta, int flags, float silu_gain, float std_scale,
-                                    const float* beta, int dtype, void* dS, void* W, float* dbeta, void* stream);
+                                    const float* beta, int dtype, void* dS, void* W, float* dbeta,
+                                    float* dbeta_work, int64_t dbeta_work_elems, void* stream);
 
 /* Input-normalisation backward: dq [rows, R] (dtype, row stride dq_stride)
  * = u - q_hat <q_hat, u> (u = dS . Dk^T [rows, R] fp32) when normalize and
@@ -205,13 +208,15 @@ DA_API int da_route_var_input_bwd(const float* u, const void* q, int64_t q_strid
  * [groups, rows, R] bf16 = gradient of the reconstruction (dDv = g_out^T
  * p_out); p_out and dl_out may both be null (then only dq and g_out are
  * written, as da_route_bwd_fused's row pass does); dbeta (may be null) is
- * accumulated (+=) with fp32 atomics (not bit-reproducible; the fused entry's
- * dbeta is). */
+ * accumulated (+=): with dbeta_work (fp32, at least 8 * groups *
+ * ceil(rows / 128) elements, else DA_ERR_WORKSPACE) from per-warp partials
+ * added in a fixed order (bit-reproducible), without it by fp32 atomics. */
 DA_API int da_route_bwd(const void* q, int64_t rows, int64_t q_cols, int64_t q_row_stride, int groups,
                         int64_t group_col_stride, int64_t R, int64_t M, int dtype, const void* dict_key_t,
                         const void* dict_value_t, const float* beta, float eps, int normalize_input,
                         int normalize_output, const void* z, const void* dz, const float* lse, const float* out_norm,
-                        void* dq, void* p_out, void* dl_out, void* g_out, float* dbeta, int* status, void* stream);
+                        void* dq, void* p_out, void* dl_out, void* g_out, float* dbeta, float* dbeta_work,
+                        int64_t dbeta_work_elems, int* status, void* stream);
 
 /* The whole route backward with deterministic dictionary gradients: replaces
  * _DictionaryRouteFunction.backward (triton_kernels.py:1873-1981) including
@@ -278,13 +283,21 @@ DA_API int da_attn_bwd_delta(const void* dy, const void* y, int64_t rows, int D,
  * sweep and written.  Accumulates (+=) into fp32 dq / dk (Q / K rows; may be
  * one buffer), dv [B*T, D], dscale [maps] (d gamma_s) and, when delta is
  * computed, dweight [maps] (d alpha_s); any output may be null.
- * D in {256, 512}; group*R in {128, 256, 512}; maps*group*R <= 512. */
+ * D in {256, 512}; group*R in {128, 256, 512}; maps*group*R <= 512.
+ * dscale and dweight are sums over every query row: the dQ kernel stores
+ * one partial per (CTA, warp) in `workspace` (device memory of at least
+ * da_attn_bwd_workspace_size(B, T, maps) bytes, 16-byte aligned; needed when
+ * dscale or a computed dweight is requested, else DA_ERR_WORKSPACE) and a
+ * second kernel adds them in a fixed order, so every output of this call is
+ * bit-identical from run to run. */
+DA_API int64_t da_attn_bwd_workspace_size(int B, int T, int maps);
 DA_API int da_attn_bwd_mixed(const void* q, int64_t q_rows, int64_t q_base, int64_t q_sb, int64_t q_sbr,
                              const void* k, int64_t k_rows, int64_t k_base, int64_t k_sb, int64_t k_sbr,
                              const void* v, const void* dy, int B, int T, int R, int D, int maps, int group,
                              const int* branch0, int causal, int dtype, const float* scales, const float* weights,
                              const float* lse, float* delta, int delta_given, float* dq, float* dk, float* dv,
-                             float* dscale, float* dweight, int* status, void* stream);
+                             float* dscale, float* dweight, void* workspace, int64_t workspace_bytes,
+                             int* status, void* stream);
 /* ---- dense GEMM (fused Q/K projection and its backward) -----------------
  * Replaces the cuBLAS GEMM of _project_query_key (modules.py:143-157,
  * F.linear(x, cat(W_q, W_k))) and its autograd backward.
@@ -313,22 +326,28 @@ DA_API int da_gemm_segments(const void* A, int64_t lda, int64_t M, int64_t K, in
 /* Split-K variant for reductions over many rows (the dictionary gradients
  * dDk = q^T dL and dDv = g^T P, triton_kernels.py:1939, :1961):
  * C[M, N] += sum_k A(m, k) B(n, k) in fp32, the K range split over `splits`
- * CTAs per output tile (0 = pick from the SM count) whose partial sums are
- * added atomically, so C must hold its initial value (e.g. zeros).  M and N
- * multiples of 128. */
+ * CTAs per output tile (0 = pick from the SM count), so C must hold its
+ * initial value (e.g. zeros).  M and N multiples of 128.  With a workspace
+ * (fp32, at least da_gemm_splitk_workspace_elems(M, N, K, splits) elements,
+ * 16-byte aligned, else DA_ERR_WORKSPACE) every split stores its partial sum
+ * there and a second kernel adds them to C in split order: the result is
+ * bit-identical from run to run.  With workspace = null the partial sums are
+ * added with fp32 atomics, whose order (and so the last bits) varies. */
+DA_API int64_t da_gemm_splitk_workspace_elems(int64_t M, int64_t N, int64_t K, int splits);
 DA_API int da_gemm_splitk(const void* A, int64_t lda, int a_mn_major, const void* B, int64_t ldb, int b_mn_major,
-                          float* C, int64_t ldc, int64_t M, int64_t N, int64_t K, int dtype, int splits, int* status,
-                          void* stream);
+                          float* C, int64_t ldc, int64_t M, int64_t N, int64_t K, int dtype, int splits,
+                          float* workspace, int64_t workspace_elems, int* status, void* stream);
 
 /* The same sum over several groups at once: C [M, N] fp32 += sum over g < groups and k < K_group of
  * A(m, g, k) B(n, g, k) with A MN-major, its group g starting a_group_cols columns to the right
  * (A(m, g, k) = A[k * lda + g * a_group_cols + m]), and B MN-major with the groups stacked along K
  * (B(n, g, k) = B[(g * K_group + k) * ldb + n]).  This is the key-dictionary gradient of the route
  * backward, dDk = sum_groups q_g^T dL'_g (triton_kernels.py:1939), in one launch instead of one per
- * group.  K_group a multiple of 64, M and N multiples of 128, a_group_cols a multiple of 8. */
+ * group.  K_group a multiple of 64, M and N multiples of 128, a_group_cols a multiple of 8.  Workspace as
+ * da_gemm_splitk with K = K_group * groups. */
 DA_API int da_gemm_splitk_grouped(const void* A, int64_t lda, int64_t a_group_cols, const void* B, int64_t ldb,
                                   float* C, int64_t ldc, int64_t M, int64_t N, int64_t K_group, int groups, int dtype,
-                                  int splits, int* status, void* stream);
+                                  int splits, float* workspace, int64_t workspace_elems, int* status, void* stream);
 
 /* ---- residual add + LayerNorm around the block -----------------------
  * Replaces x + branch followed by nn.LayerNorm in DoubleAttentionBlock.forward

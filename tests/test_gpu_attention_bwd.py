@@ -156,14 +156,18 @@ def test_op_level_routed_attention_backward(causal: bool) -> None:
 
 
 def test_backward_is_repeatable() -> None:
-    """Two backward passes on the same inputs give the same gradients."""
+    """Two backward passes on the same inputs give bit-identical gradients, the score scales' and the
+    map weights' (sums over every query row, added in a fixed order) included."""
     dev = torch.device("cuda")
-    routed, value, dy, scales, mix = _inputs(4, 4, 1, 256, 128, 512, 16.0, torch.bfloat16, seed=3)
+    routed, value, dy, scales, mix = _inputs(4, 4, 3, 700, 128, 512, 16.0, torch.bfloat16, seed=3)
     grads = []
     for _ in range(2):
         rd = routed.to(dev).requires_grad_()
         vd = value.to(dev).requires_grad_()
-        ops.routed_attention_mixed(rd, vd, scales.to(dev), mix.to(dev), _Cfg(4)).backward(dy.to(dev))
-        grads.append((rd.grad.clone(), vd.grad.clone()))
+        sd = scales.to(dev).requires_grad_()
+        md = mix.to(dev).requires_grad_()
+        ops.routed_attention_mixed(rd, vd, sd, md, _Cfg(4)).backward(dy.to(dev))
+        grads.append((rd.grad.clone(), vd.grad.clone(), sd.grad.clone(), md.grad.clone()))
     torch.cuda.synchronize()
-    assert torch.equal(grads[0][0], grads[1][0]) and torch.equal(grads[0][1], grads[1][1])
+    for name, a, b in zip(("routed", "value", "scales", "map weights"), grads[0], grads[1]):
+        assert torch.equal(a, b), f"d {name} differs between two identical backward passes"

@@ -5,7 +5,7 @@ from __future__ import annotations
 import pytest
 import torch
 
-from double_attention_b200 import ops
+from double_attention_b200 import _lib, ops
 
 pytestmark = pytest.mark.gpu
 
@@ -54,18 +54,42 @@ def test_projection_autograd() -> None:
 
 @pytest.mark.parametrize(("groups", "rows", "r", "m", "cs"), [(8, 512, 128, 512, 128), (2, 4096, 256, 512, 256),
                                                              (3, 192, 128, 384, 136)])
-def test_grouped_splitk_matches_reference(groups, rows, r, m, cs) -> None:
-    """da_gemm_splitk_grouped: C += sum_g A_g^T B_g with A_g the g-th column block of a row-major matrix."""
+@pytest.mark.parametrize("deterministic", [True, False])
+def test_grouped_splitk_matches_reference(groups, rows, r, m, cs, deterministic) -> None:
+    """da_gemm_splitk_grouped: C += sum_g A_g^T B_g with A_g the g-th column block of a row-major matrix,
+    the splits' partial sums added in a fixed order through a workspace, or with atomics without one."""
     dev = torch.device("cuda")
     g = torch.Generator().manual_seed(groups + rows)
     a = torch.randn(rows, (groups - 1) * cs + r + 8, generator=g).to(torch.bfloat16)
     b = torch.randn(groups, rows, m, generator=g).to(torch.bfloat16)
-    out = torch.zeros(r, m, dtype=torch.float32, device=dev)
     ad, bd = a.to(dev), b.to(dev)
     ws = ops.workspace(dev)
-    ops.call("da_gemm_splitk_grouped", ad.data_ptr(), ad.stride(0), cs, bd.data_ptr(), m, out.data_ptr(), m, r, m,
-             rows, groups, 1, 0, ws.status.data_ptr(), ops.stream_ptr(dev))
+    elems = int(_lib.lib().da_gemm_splitk_workspace_elems(r, m, rows * groups, 0))
+    part = torch.empty(elems, device=dev) if deterministic else None
+    outs = []
+    for _ in range(2):
+        out = torch.full((r, m), 0.5, dtype=torch.float32, device=dev)  # C += ...: the initial value stays
+        ops.call("da_gemm_splitk_grouped", ad.data_ptr(), ad.stride(0), cs, bd.data_ptr(), m, out.data_ptr(), m, r,
+                 m, rows, groups, 1, 0, None if part is None else part.data_ptr(), 0 if part is None else elems,
+                 ws.status.data_ptr(), ops.stream_ptr(dev))
+        outs.append(out)
     torch.cuda.synchronize()
-    ref = sum(a[:, k * cs:k * cs + r].double().t() @ b[k].double() for k in range(groups))
-    err = (out.double().cpu() - ref).abs().max().item()
+    ref = sum(a[:, k * cs:k * cs + r].double().t() @ b[k].double() for k in range(groups)) + 0.5
+    err = (outs[0].double().cpu() - ref).abs().max().item()
     assert err <= 1e-3 * ref.abs().max().item(), err
+    if deterministic:
+        assert torch.equal(outs[0], outs[1])
+
+
+def test_splitk_rejects_a_short_workspace() -> None:
+    dev = torch.device("cuda")
+    a = torch.zeros(1024, 256, dtype=torch.bfloat16, device=dev)
+    b = torch.zeros(1024, 512, dtype=torch.bfloat16, device=dev)
+    out = torch.zeros(256, 512, device=dev)
+    elems = int(_lib.lib().da_gemm_splitk_workspace_elems(256, 512, 1024, 0))
+    assert elems >= 256 * 512
+    part = torch.empty(elems - 4, device=dev)
+    rc = _lib.lib().da_gemm_splitk(a.data_ptr(), 256, 1, b.data_ptr(), 512, 1, out.data_ptr(), 512, 256, 512, 1024,
+                                   _lib.DA_BF16, 0, part.data_ptr(), part.numel(),
+                                   ops.workspace(dev).status.data_ptr(), ops.stream_ptr(dev))
+    assert rc == _lib.DA_ERR_WORKSPACE

@@ -87,10 +87,13 @@ def test_route_backward_is_repeatable() -> None:
     grads = []
     for _ in range(2):
         xd = x.clone().requires_grad_()
-        ops.dictionary_route(xd, dk, dv, torch.tensor(4.0, device=dev)).backward(dz)
-        grads.append(xd.grad.clone())
+        dkd, dvd = dk.clone().requires_grad_(), dv.clone().requires_grad_()
+        bd = torch.tensor(4.0, device=dev, requires_grad=True)
+        ops.dictionary_route(xd, dkd, dvd, bd).backward(dz)
+        grads.append((xd.grad.clone(), dkd.grad.clone(), dvd.grad.clone(), bd.grad.clone()))
     torch.cuda.synchronize()
-    assert torch.equal(grads[0], grads[1])
+    for name, a, b in zip(("input", "key dictionary", "value dictionary", "beta"), grads[0], grads[1]):
+        assert torch.equal(a, b), f"d {name} differs between two identical backward passes"
 
 
 @pytest.mark.parametrize(

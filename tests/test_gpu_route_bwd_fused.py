@@ -124,7 +124,7 @@ def test_fused_route_backward_agrees_with_the_stored_weights_path() -> None:
     ops.call("da_route_bwd", qd.data_ptr(), rows, qd.shape[1], qd.stride(0), groups, r, r, m, _lib.DA_BF16,
              views.key_t.data_ptr(), views.value_t.data_ptr(), beta_t.data_ptr(), 1e-6, 1, 1, z.data_ptr(),
              dz.to(dev).data_ptr(), lse.data_ptr(), onorm.data_ptr(), dq2.data_ptr(), p_out.data_ptr(),
-             dl_out.data_ptr(), g_out.data_ptr(), dbeta2.data_ptr(), ops.workspace(dev).status.data_ptr(),
+             dl_out.data_ptr(), g_out.data_ptr(), dbeta2.data_ptr(), None, 0, ops.workspace(dev).status.data_ptr(),
              ops.stream_ptr(dev))
     d_key2 = torch.zeros(r, m, device=dev)
     ops.key_dictionary_grad(qd, r, dl_out, d_key2)
