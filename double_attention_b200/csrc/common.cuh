@@ -232,6 +232,13 @@ DA_DEV void tma_load_4d_pair(const void* tmap, uint32_t bar_cluster_addr, void* 
       :: "r"(smem_u32(dst)), "l"(tmap), "r"(bar_cluster_addr), "r"(x), "r"(y), "r"(z), "r"(w) : "memory");
 }
 
+// 1-D bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned) from global memory into
+// this CTA's shared memory, completion signalled on a barrier of this CTA.
+DA_DEV void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               :: "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+
 // 2-D tiled store from shared memory (bulk-group completion).
 DA_DEV void tma_store_2d(const void* tmap, const void* src, int x, int y) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];"

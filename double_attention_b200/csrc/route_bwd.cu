@@ -62,7 +62,7 @@ struct Params {
   void* dl_out;            // [groups, rows, M] dtype: invn * beta * dLs
   __nv_bfloat16* g_out;    // [groups, rows, R]
   float* dbeta;            // accumulated (may be null)
-  float* row_stats;        // [groups, rows, 2]: invn, delta (may be null)
+  float* row_stats;        // [groups, rows_pad, 4]: lse2, invn, delta, 0 (may be null)
   float* dbeta_part;       // [2 * pairs * 4]: per-(CTA, warp) dbeta partials summed in order (null: atomics)
   int* status;
   int* trace;              // optional progress stamps (debug)
@@ -145,7 +145,7 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks) route_bwd_kernel(const _
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 2);
+      mbar_init(&p_full[i], 8);  // one arrival per row-math warp of the pair
       mbar_init(&dl_empty[i], 1);
     }
     fence_mbar_init();
@@ -458,8 +458,11 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks) route_bwd_kernel(const _
           }
         qn = sqrtf(qn2);
         invn = p.normalize_input ? 1.f / fmaxf(qn, p.eps) : 1.f;
-        if (p.row_stats && live && half == 0)
-          *reinterpret_cast<float2*>(p.row_stats + 2 * idx) = make_float2(invn, delta);
+        if (p.row_stats && half == 0) {  // every row of the tile, dead rows too (no probability mass)
+          const int64_t prow = (int64_t)grp * tiles_per_group * 128 + row0 + 64 * (int)rank + r;
+          *reinterpret_cast<float4*>(p.row_stats + 4 * prow) =
+              live ? make_float4(lse2, invn, delta, 0.f) : make_float4(INFINITY, 0.f, 0.f, 0.f);
+        }
       }
       if (ok && j >= nb) ok = mbar_wait(&dl_empty[sb], ((j - nb) / nb) & 1u, ab, 33);
       ok = __all_sync(0xffffffffu, ok);
@@ -506,8 +509,8 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks) route_bwd_kernel(const _
       }
       if (arriver) trace_at(ft, 130 + 4 * j);
       tc_fence_before();
-      named_bar_sync(1, 128);
-      if (arriver) mbar_arrive_cluster(pf_leader + sb * 8);
+      __syncwarp();  // this warp's TMEM reads are done and its dL' stores fenced: it arrives by itself
+      if (lane == 0) mbar_arrive_cluster(pf_leader + sb * 8);
     }
     if (arriver) trace_time(p.trace, 3);
     if (p.dbeta) {

@@ -55,7 +55,9 @@ struct RouteBwdArgs {
   void* g_out;              // [groups, rows, R] bf16 gradient of the reconstruction
   float* dbeta;             // accumulated, may be null
   int* status;
-  float* row_stats = nullptr;  // [groups, rows, 2] fp32: input inverse norm, delta = <P, dP> (optional)
+  // [groups, rows_pad, 4] fp32 with rows_pad = rows rounded up to 128 (optional): per row
+  // {lse * log2(e), input inverse norm, delta = <P, dP>, 0}; rows past `rows` get {+inf, 0, 0, 0}
+  float* row_stats = nullptr;
   float* dbeta_part = nullptr; // [8 * pairs] per-(CTA, warp) dbeta partials, summed in order (optional)
 };
 

@@ -43,8 +43,12 @@ namespace da {
 namespace route {
 namespace dgrad {
 
-constexpr int kThreads = 224;  // warp 0 ring-A TMA, 1 MMA, 2-5 softmax, 6 ring-B TMA
+// warp 0 ring-A TMA, 1 MMA, 2-5 and 7-10 softmax (two warpgroups, each thread half of its row range:
+// with one softmax warp per SM sub-partition the per-element chain left the latencies exposed and paced
+// the kernel at ~2.6 us per row tile), 6 ring-B TMA
+constexpr int kThreads = 352;
 constexpr int kRingBWarp = 6;
+constexpr int kSoftmax2 = 7;  // first warp of the second softmax warpgroup
 constexpr int kAtoms = 64;     // atoms per CTA (128 per pair)
 
 template <int kR>
@@ -58,12 +62,15 @@ struct Cfg {
   static constexpr int kOffDk = 0;
   static constexpr int kOffDv = kOffDk + kDictBytes;
   static constexpr int kOffA = kOffDv + kDictBytes;            // 2 stages x (q, g)
-  static constexpr int kOffB = kOffA + 2 * 2 * kXBytes;        // 2 stages x (q, g)
-  static constexpr int kOffP = kOffB + 2 * 2 * kYBytes;
-  static constexpr int kOffDl = kOffP + kPBytes;
-  static constexpr int kOffStats = kOffDl + kPBytes;           // 2 buffers x {lse2, invn, delta} x kTR
-  static constexpr int kOffRed = kOffStats + 2 * 3 * kTR * 4;
+  static constexpr int kStatBytes = kTR * 16;                 // the tile's rows: {lse2, invn, delta, 0}
+  static constexpr int kBStage = 2 * kYBytes + kStatBytes;     // ring B stage: q, g, row statistics
+  static constexpr int kOffB = kOffA + 2 * 2 * kXBytes;        // 2 stages
+  static constexpr int kOffP = kOffB + 2 * kBStage;
+  static constexpr int kOffDl = kOffP + kPBytes;               // 2 buffers (P: one, released early)
+  static constexpr int kCols = kTR / 4;                        // tile rows (score columns) per softmax thread
+  static constexpr int kOffRed = kOffDl + 2 * kPBytes;
   static constexpr int kSmem = kOffRed + 64;
+  static_assert(kCols == 32 || kCols == 16, "softmax column split");
   static_assert(kSmem + 1024 <= 232448, "dictionary-gradient tile does not fit in shared memory");
   // TMEM: dDk^T (R/2 folded columns), dDv^T, then 2 x S^T and 2 x dP^T (kTR/2 each)
   static constexpr int kTmemDk = 0;
@@ -84,10 +91,12 @@ struct Params {
   int chunks;              // row chunks (pairs = chunks * M / 128)
   const float* beta;
   const float* lse;        // [groups, rows]
-  const float* row_stats;  // [groups, rows, 2]: invn, delta
+  const float* row_stats;  // [groups, rows_pad, 4]: lse2, invn, delta, 0 (dead rows: +inf, 0, 0, 0)
+  int64_t rows_pad;        // rows rounded up to 128
   float* part;             // [chunks, 2, M, R]: dDk^T then dDv^T partial sums
   float* part_beta;        // [pairs * 2]
   int* status;
+  int* trace;              // optional post-mortem timeline of the first pair (debug)
 };
 
 template <typename T, int kR>
@@ -102,7 +111,8 @@ __global__ void __launch_bounds__(kThreads, 1) dict_grad_kernel(const __grid_con
   constexpr int kTR = C::kTR;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ uint64_t dict_full, full_a[2], empty_a[2], full_b[2], empty_b[2], s_full[2], p_full[2], pl_empty, done;
+  __shared__ uint64_t dict_full, full_a[2], empty_a[2], full_b[2], empty_b[2], s_full[2], p_full[2], p_empty, dl_empty[2],
+      stats_full[2], done;
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
 
@@ -115,6 +125,12 @@ __global__ void __launch_bounds__(kThreads, 1) dict_grad_kernel(const __grid_con
   const int64_t f0 = (int64_t)chunk * p.tiles / p.chunks, f1 = (int64_t)(chunk + 1) * p.tiles / p.chunks;
   const int nt = (int)(f1 - f0);  // >= 1: the host never makes more chunks than tiles
   Abort ab{&abort_flag, p.status};
+  // debug timeline of the first pair: 4096 stamps per CTA, [role * 1024 + 4 * tile + event], after the
+  // 2^18 slots the row pass may stamp
+  int* ft = (p.trace && blockIdx.x < 2) ? p.trace + (1 << 18) + blockIdx.x * 4096 : nullptr;
+  auto stamp = [&](int role, int t, int ev) {
+    if (t < 256) trace_at(ft, role * 1024 + 4 * t + ev);
+  };
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
@@ -125,9 +141,13 @@ __global__ void __launch_bounds__(kThreads, 1) dict_grad_kernel(const __grid_con
       mbar_init(&full_b[i], 1);
       mbar_init(&empty_b[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 2);  // one arrival per CTA of the pair
+      mbar_init(&p_full[i], 16);  // one arrival per softmax warp of the pair
     }
-    mbar_init(&pl_empty, 1);
+    mbar_init(&p_empty, 1);
+    mbar_init(&stats_full[0], 1);  // this CTA's own copy of the tile's row statistics
+    mbar_init(&stats_full[1], 1);
+    mbar_init(&dl_empty[0], 1);
+    mbar_init(&dl_empty[1], 1);
     mbar_init(&done, 1);
     fence_mbar_init();
   }
@@ -154,7 +174,7 @@ __global__ void __launch_bounds__(kThreads, 1) dict_grad_kernel(const __grid_con
     const bool ring_a = warp == 0;
     uint64_t* full = ring_a ? full_a : full_b;
     uint64_t* empty = ring_a ? empty_a : empty_b;
-    const int bytes = ring_a ? 2 * C::kXBytes : 2 * C::kYBytes;
+    const int bytes = ring_a ? 2 * C::kXBytes : 2 * C::kYBytes;  // paired tensor loads (the leader counts both CTAs)
     if (ring_a) {
       prefetch_tmap(&tqa);
       prefetch_tmap(&tga);
@@ -173,7 +193,9 @@ __global__ void __launch_bounds__(kThreads, 1) dict_grad_kernel(const __grid_con
     bool ok = true;
     for (int t = 0; ok && t < nt; ++t) {
       const int s = t & 1;
+      stamp(ring_a ? 0 : 1, t, 0);
       if (!mbar_wait(&empty[s], ((t >> 1) & 1u) ^ 1u, ab, ring_a ? 51 : 52)) { ok = false; break; }
+      stamp(ring_a ? 0 : 1, t, 1);
       if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * bytes);
       const uint32_t bar = mapa_shared(smem_u32(&full[s]), 0);
       int g;
@@ -184,17 +206,22 @@ __global__ void __launch_bounds__(kThreads, 1) dict_grad_kernel(const __grid_con
         const int r = (int)(row0 + (int64_t)rank * C::kHalfRows);
         tma_load_3d_pair(&tqa, bar, dst, 0, r, (int)(g * p.col_stride / 64));
         tma_load_3d_pair(&tga, bar, dst + C::kXBytes, 0, (int)(g * p.rows + r), 0);
-      } else {  // every row of the tile, this CTA's half of the columns
-        uint8_t* dst = smem + C::kOffB + s * 2 * C::kYBytes;
+      } else {  // every row of the tile, this CTA's half of the columns, and the rows' statistics
+        uint8_t* dst = smem + C::kOffB + s * C::kBStage;
         const int cb = (int)rank * (kR / 128);
         tma_load_3d_pair(&tqb, bar, dst, 0, (int)row0, (int)(g * p.col_stride / 64) + cb);
         tma_load_3d_pair(&tgb, bar, dst + C::kYBytes, 0, (int)(g * p.rows + row0), cb);
+        mbar_arrive_expect_tx(&stats_full[s], C::kStatBytes);
+        bulk_load(dst + 2 * C::kYBytes, p.row_stats + 4 * ((int64_t)g * p.rows_pad + row0), C::kStatBytes,
+                  &stats_full[s]);
       }
     }
     if (rank == 0) {  // drain: the leader's barriers count both CTAs' bytes
       if (ring_a) mbar_wait_drain(&dict_full, 0);
       for (int t = (nt > 2 ? nt - 2 : 0); t < nt; ++t) mbar_wait_drain(&full[t & 1], (t >> 1) & 1u);
     }
+    if (!ring_a)  // each CTA's own statistics copies
+      for (int t = (nt > 2 ? nt - 2 : 0); t < nt; ++t) mbar_wait_drain(&stats_full[t & 1], (t >> 1) & 1u);
   } else if (warp == 1 && lane == 0 && rank == 0) {
     // ---------------------------------------------------------------- MMA issuer (pair leader)
     const uint32_t idesc_s = idesc_f16(128, kTR, kBf16, false, false);
@@ -209,8 +236,10 @@ __global__ void __launch_bounds__(kThreads, 1) dict_grad_kernel(const __grid_con
     const uint32_t p_a = smem_u32(smem + C::kOffP), dl_a = smem_u32(smem + C::kOffDl);
     auto issue_sdp = [&](int t) -> bool {
       const int b = t & 1;
+      stamp(2, t, 0);
       if (t >= 2 && !mbar_wait(&p_full[b], ((t - 2) >> 1) & 1u, ab, 53)) return false;
       if (!mbar_wait(&full_a[b], (t >> 1) & 1u, ab, 54)) return false;
+      stamp(2, t, 1);
       tc_fence_after();
       const uint32_t qx = smem_u32(smem + C::kOffA + b * 2 * C::kXBytes), gx = qx + C::kXBytes;
       const uint32_t ds = tmem + C::kTmemS + b * (kTR / 2), dp = tmem + C::kTmemP + b * (kTR / 2);
@@ -230,24 +259,28 @@ __global__ void __launch_bounds__(kThreads, 1) dict_grad_kernel(const __grid_con
     };
     auto issue_dd = [&](int t) -> bool {
       const int b = t & 1;
+      stamp(2, t, 2);
       if (!mbar_wait(&p_full[b], (t >> 1) & 1u, ab, 55)) return false;
       tc_fence_after();
       if (!mbar_wait(&full_b[b], (t >> 1) & 1u, ab, 56)) return false;
+      stamp(2, t, 3);
       tc_fence_after();
-      const uint32_t qy = smem_u32(smem + C::kOffB + b * 2 * C::kYBytes), gy = qy + C::kYBytes;
+      const uint32_t qy = smem_u32(smem + C::kOffB + b * C::kBStage), gy = qy + C::kYBytes;
 #pragma unroll
       for (int kk = 0; kk < kTR / 16; ++kk) {  // dDv^T += P^T . g   (K = rows of the tile)
         const uint32_t ka = (kk >> 2) * (kAtoms * 128) + (kk & 3) * 32;
         mma_f16_ss<2>(tmem + C::kTmemDv, sdesc_sw128(p_a + ka, 16, 1024),
                       sdesc_sw128(gy + kk * 16 * 128, kTR * 128, 1024), idesc_v, (t | kk) ? 1u : 0u);
       }
+      commit_both(&p_empty);  // the P tile is free for the next row tile while dDk runs
+      const uint32_t dlb = dl_a + b * C::kPBytes;
 #pragma unroll
       for (int kk = 0; kk < kTR / 16; ++kk) {  // dDk^T += dL'^T . q
         const uint32_t ka = (kk >> 2) * (kAtoms * 128) + (kk & 3) * 32;
-        mma_f16_ss<2>(tmem + C::kTmemDk, sdesc_sw128(dl_a + ka, 16, 1024),
+        mma_f16_ss<2>(tmem + C::kTmemDk, sdesc_sw128(dlb + ka, 16, 1024),
                       sdesc_sw128(qy + kk * 16 * 128, kTR * 128, 1024), idesc_k, (t | kk) ? 1u : 0u);
       }
-      commit_both(&pl_empty);
+      commit_both(&dl_empty[b]);
       commit_both(&empty_b[b]);
       return true;
     };
@@ -260,108 +293,117 @@ __global__ void __launch_bounds__(kThreads, 1) dict_grad_kernel(const __grid_con
     }
     commit_both(&done);
     mbar_wait_drain(&done, 0);
-  } else if (warp >= 2 && warp <= 5) {
-    // ---------------------------------------------------------------- softmax warpgroup (thread = atom x row half)
+  } else if ((warp >= 2 && warp <= 5) || warp >= kSoftmax2) {
+    // ---------------------------------------------------------------- softmax (thread = atom x kCols tile rows)
+    // TMEM lane l holds atom l % 64 and tile rows (l / 64) * kTR/2 + [0, kTR/2); warpgroup wg takes kCols of
+    // them.  The warps issue no global loads (a proxy fence waits for a thread's outstanding loads, which
+    // put ~1 us into every tile): each tile's row statistics arrive in ring B's stage by a bulk copy.  Each
+    // warp arrives on the pair leader's barrier itself, so no named barrier runs per tile.
+    constexpr int kCols = C::kCols;
+    const int wg = warp >= kSoftmax2 ? 1 : 0;
     const int quad = warp & 3;
     const int l = quad * 32 + lane;
     const int a = l & 63, h = l >> 6;
+    const int wslot = wg * 4 + quad;
+    const int rr0 = h * (kTR / 2) + wg * kCols;  // first tile row of this thread
     const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
-    const bool arriver = (warp == 2 && lane == 0);
-    float* stats = reinterpret_cast<float*>(smem + C::kOffStats);
     const float kLog2e = 1.4426950408889634f;
     const float beta = *p.beta;
     const uint32_t p_a = smem_u32(smem + C::kOffP), dl_a = smem_u32(smem + C::kOffDl);
     const uint32_t pf_leader = mapa_shared(smem_u32(&p_full[0]), 0);
     float dbeta = 0.f;
     bool ok = true;
+    const bool tracer = warp == 2 && lane == 0;
     for (int t = 0; t < nt; ++t) {
       const int b = t & 1;
-      int g;
-      int64_t row0;
-      tile_of(t, g, row0);
-      float* st = stats + b * 3 * kTR;  // lse2 | invn | delta of the tile's rows
-      if (l < kTR) {
-        const int64_t row = row0 + l;
-        const bool live = row < p.rows;
-        const int64_t idx = (int64_t)g * p.rows + (live ? row : 0);
-        st[l] = live ? __ldg(p.lse + idx) * kLog2e : INFINITY;  // dead rows: P = 0
-        st[kTR + l] = live ? __ldg(p.row_stats + 2 * idx) : 0.f;
-        st[2 * kTR + l] = live ? __ldg(p.row_stats + 2 * idx + 1) : 0.f;
-      }
-      named_bar_sync(1, 128);
+      // this thread's rows' {lse2, invn, delta}, copied into ring B's stage by its producer
+      const float4* st4 = reinterpret_cast<const float4*>(smem + C::kOffB + b * C::kBStage + 2 * C::kYBytes) + rr0;
+      if (tracer) stamp(3, t, 0);
       if (ok) ok = mbar_wait(&s_full[b], (t >> 1) & 1u, ab, 58);
+      if (ok) ok = mbar_wait(&stats_full[b], (t >> 1) & 1u, ab, 62);
       ok = __all_sync(0xffffffffu, ok);
+      if (tracer) stamp(3, t, 1);
       if (ok) {
         tc_fence_after();
-#pragma unroll
-        for (int ch = 0; ch < kTR / 64; ++ch) {  // 32 of this thread's kTR/2 rows per chunk
-          float sv[32], dpv[32];
-          tmem_ld32(tmem + lane_base + C::kTmemS + b * (kTR / 2) + ch * 32, sv);
-          tmem_ld32(tmem + lane_base + C::kTmemP + b * (kTR / 2) + ch * 32, dpv);
-          tmem_wait_ld();
-          const int rr0 = h * (kTR / 2) + ch * 32;  // first tile row of this chunk
-          uint32_t pk[16], dk[16];
-#pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            float pr[2], dl[2];
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const int rr = rr0 + i + e;
-              const float invn = st[kTR + rr];
-              pr[e] = ex2(sv[i + e] * (beta * invn * kLog2e) - st[rr]);
-              const float dls = pr[e] * (dpv[i + e] - st[2 * kTR + rr]);
-              dbeta = fmaf(sv[i + e] * invn, dls, dbeta);
-              dl[e] = dls * invn * beta;
-            }
-            pk[i / 2] = pack_bf16x2(pr[0], pr[1]);
-            dk[i / 2] = pack2<T>(dl[0], dl[1]);
-          }
-          if (ch == 0 && t > 0) {  // the previous tile's dD products have read the P / dL' tiles
-            bool w = mbar_wait(&pl_empty, (t - 1) & 1u, ab, 59);
-            ok = __all_sync(0xffffffffu, w);
-          }
-          if (ok) {
-            const uint32_t kb = (uint32_t)(rr0 >> 6) * (kAtoms * 128);
-            const uint32_t c0 = (uint32_t)(rr0 & 63) >> 3;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              st_shared_v4(p_a + kb + sw128_offset(a, c0 + e), pk[4 * e], pk[4 * e + 1], pk[4 * e + 2], pk[4 * e + 3]);
-              st_shared_v4(dl_a + kb + sw128_offset(a, c0 + e), dk[4 * e], dk[4 * e + 1], dk[4 * e + 2], dk[4 * e + 3]);
-            }
-          }
+        float sv[kCols], dpv[kCols];
+        const uint32_t col = b * (kTR / 2) + wg * kCols;
+        if constexpr (kCols == 32) {
+          tmem_ld32(tmem + lane_base + C::kTmemS + col, sv);
+          tmem_ld32(tmem + lane_base + C::kTmemP + col, dpv);
+        } else {
+          tmem_ld16(tmem + lane_base + C::kTmemS + col, sv);
+          tmem_ld16(tmem + lane_base + C::kTmemP + col, dpv);
         }
-        fence_proxy_async();
+        tmem_wait_ld();
+        tc_fence_before();
+        uint32_t pk[kCols / 2], dk[kCols / 2];
+#pragma unroll
+        for (int i = 0; i < kCols; i += 2) {
+          float pr[2], dl[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const float4 rs = st4[i + e];  // lse2, invn, delta
+            const float invn = rs.y;
+            pr[e] = ex2(sv[i + e] * (beta * invn * kLog2e) - rs.x);
+            const float dls = pr[e] * (dpv[i + e] - rs.z);
+            dbeta = fmaf(sv[i + e] * invn, dls, dbeta);
+            dl[e] = dls * invn * beta;
+          }
+          pk[i / 2] = pack_bf16x2(pr[0], pr[1]);
+          dk[i / 2] = pack2<T>(dl[0], dl[1]);
+        }
+        {  // the previous tile's dDv product has read P; the one before the previous tile's dDk, dL' buffer b
+          bool w = true;
+          if (t > 0) w = mbar_wait(&p_empty, (t - 1) & 1u, ab, 59);
+          if (w && t > 1) w = mbar_wait(&dl_empty[b], ((t - 2) >> 1) & 1u, ab, 61);
+          ok = ok && __all_sync(0xffffffffu, w);
+        }
+        if (tracer) stamp(3, t, 2);
+        if (ok) {
+          const uint32_t kb = (uint32_t)(rr0 >> 6) * (kAtoms * 128);
+          const uint32_t c0 = (uint32_t)(rr0 & 63) >> 3;
+#pragma unroll
+          for (int e = 0; e < kCols / 8; ++e) {
+            st_shared_v4(p_a + kb + sw128_offset(a, c0 + e), pk[4 * e], pk[4 * e + 1], pk[4 * e + 2], pk[4 * e + 3]);
+            st_shared_v4(dl_a + b * C::kPBytes + kb + sw128_offset(a, c0 + e), dk[4 * e], dk[4 * e + 1],
+                         dk[4 * e + 2], dk[4 * e + 3]);
+          }
+          fence_proxy_async();  // this thread's P / dL' stores, visible to the tensor core
+        }
       }
-      tc_fence_before();
-      named_bar_sync(1, 128);
-      if (arriver) mbar_arrive_cluster(pf_leader + b * 8);
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(pf_leader + b * 8);  // this warp: TMEM read, tiles written
+      if (tracer) stamp(3, t, 3);
     }
 
-    // ---- epilogue: this CTA's [64 atoms, R] partial sums, then the dbeta partial
+    // ---- epilogue: this CTA's [64 atoms, R] partial sums (warpgroup wg stores the kind wg), then dbeta
     if (ok) ok = mbar_wait(&done, 0, ab, 60);
     ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
     if (ok) {
       const int atom = jt * 2 * kAtoms + kAtoms * (int)rank + a;
-      for (int kind = 0; kind < 2; ++kind) {
-        float* dst = p.part + (((size_t)chunk * 2 + kind) * p.M + atom) * kR + h * (kR / 2);
-        const uint32_t col0 = kind == 0 ? C::kTmemDk : C::kTmemDv;
+      const int kind = wg;
+      float* dst = p.part + (((size_t)chunk * 2 + kind) * p.M + atom) * kR + h * (kR / 2);
+      const uint32_t col0 = kind == 0 ? C::kTmemDk : C::kTmemDv;
 #pragma unroll
-        for (int c = 0; c < kR / 2; c += 32) {
-          float v[32];
-          tmem_ld32(tmem + lane_base + col0 + c, v);
-          tmem_wait_ld();
+      for (int c = 0; c < kR / 2; c += 32) {
+        float v[32];
+        tmem_ld32(tmem + lane_base + col0 + c, v);
+        tmem_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 8; ++e)
-            reinterpret_cast<float4*>(dst + c)[e] = make_float4(v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3]);
-        }
+        for (int e = 0; e < 8; ++e)
+          reinterpret_cast<float4*>(dst + c)[e] = make_float4(v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3]);
       }
     }
     for (int o = 16; o; o >>= 1) dbeta += __shfl_xor_sync(0xffffffffu, dbeta, o);
     float* red = reinterpret_cast<float*>(smem + C::kOffRed);
-    if (lane == 0) red[quad] = dbeta;
-    named_bar_sync(1, 128);
-    if (l == 0) p.part_beta[2 * pair + rank] = ok ? ((red[0] + red[1]) + (red[2] + red[3])) : 0.f;
+    if (lane == 0) red[wslot] = dbeta;
+    named_bar_sync(1, 256);
+    if (wg == 0 && l == 0) {
+      float sum = 0.f;
+      for (int i = 0; i < 8; ++i) sum += red[i];
+      p.part_beta[2 * pair + rank] = ok ? sum : 0.f;
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -427,7 +469,7 @@ inline WorkLayout work_layout(int64_t rows, int groups, int64_t R, int64_t M) {
   W.pairs = W.chunks * nj;
   W.off_g = 0;
   W.off_stats = align256(W.off_g + (size_t)groups * rows * R * 2);
-  W.off_part = align256(W.off_stats + (size_t)groups * rows * 2 * 4);
+  W.off_part = align256(W.off_stats + (size_t)groups * ((rows + 127) / 128 * 128) * 4 * 4);
   W.off_beta = align256(W.off_part + (size_t)W.chunks * 2 * M * R * 4);
   W.bytes = align256(W.off_beta + (size_t)W.pairs * 2 * 4);
   return W;
@@ -477,9 +519,11 @@ int launch(const RouteBwdArgs& a, const WorkLayout& W, uint8_t* ws, float* d_key
   p.beta = a.beta;
   p.lse = a.lse;
   p.row_stats = reinterpret_cast<const float*>(ws + W.off_stats);
+  p.rows_pad = (a.rows + 127) / 128 * 128;
   p.part = reinterpret_cast<float*>(ws + W.off_part);
   p.part_beta = reinterpret_cast<float*>(ws + W.off_beta);
   p.status = a.status;
+  p.trace = debug_trace();
   auto kern = dict_grad_kernel<T, kR>;
   const int smem = C::kSmem + 1024;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)

@@ -42,10 +42,11 @@ class _Cfg:
         self.causal = True
 
 
-def make_case(kernel: str, config: int, device: torch.device):
+def make_case(kernel: str, config: int, device: torch.device, batch: int | None = None):
     from .config import experiment_config
 
-    preset, batch, seq, dtype = SHAPES[config]
+    preset, default_batch, seq, dtype = SHAPES[config]
+    batch = batch or default_batch
     cfg = experiment_config(preset)
     h, r, m, d = cfg.qk_branches, cfg.routing_dim, cfg.dictionary_size, cfg.model_dim
     g = torch.Generator().manual_seed(config)
@@ -207,13 +208,14 @@ def main(argv=None) -> int:
     p.add_argument("--kernel", required=True, help=f"comma-separated list of {', '.join(KERNELS)}")
     p.add_argument("--config", type=int, choices=sorted(SHAPES), default=2)
     p.add_argument("--reps", type=int, default=3)
+    p.add_argument("--batch", type=int, default=None, help="override the config's per-GPU batch (small captures)")
     p.add_argument("--time", action="store_true")
     args = p.parse_args(argv)
     device = torch.device("cuda", 0)
     for kernel in args.kernel.split(","):
         if kernel not in KERNELS:
             raise SystemExit(f"unknown kernel {kernel!r}")
-        run, flops = make_case(kernel, args.config, device)
+        run, flops = make_case(kernel, args.config, device, args.batch)
         if args.time:
             ms = time_kernel(run, args.reps, device, graph=kernel in GRAPH_CASES)
             print(json.dumps({"kernel": kernel, "config": args.config, "ms": ms, "flops": flops,

@@ -82,9 +82,11 @@ def test_fused_route_backward_matches_oracle(rows, groups, r, m, col_stride, dty
     br = torch.tensor(beta, requires_grad=True)
     qr = q.float().requires_grad_()
     total = 0.0
+    seen = []
     for grp in range(groups):
+        seen.append({})
         zr = oracle.dictionary_route(qr[:, grp * col_stride:grp * col_stride + r], dkr, dvr, br, 1e-6,
-                                     normalize_input=ni, normalize_output=no)
+                                     normalize_input=ni, normalize_output=no, inspect=seen[-1])
         total = total + (zr * dz[grp].float()).sum()
     total.backward()
     for grp in range(groups):
@@ -92,7 +94,12 @@ def test_fused_route_backward_matches_oracle(rows, groups, r, m, col_stride, dty
         _close(f"d q (group {grp})", dq[:, sl], qr.grad[:, sl])
     _close("d key dictionary", d_key, dkr.grad)
     _close("d value dictionary", d_value, dvr.grad)
-    assert abs(dbeta.item() - br.grad.item()) <= 2e-2 * max(abs(br.grad.item()), 1e-3), (dbeta.item(), br.grad.item())
+    # d beta = sum over rows and atoms of logit * d loss / d (beta logit): terms of both signs that cancel
+    # (they sum to zero over the atoms of a row), so the bf16 rounding of g moves it by more than its own
+    # size suggests.  Bar as for the route variants: 2e-2 relative plus 1e-4 of the summed term magnitude.
+    terms = sum((d["logits"] * d["scaled"].grad).abs().sum().item() for d in seen)
+    tol = 2e-2 * abs(br.grad.item()) + 1e-4 * terms
+    assert abs(dbeta.item() - br.grad.item()) <= tol, f"d beta {dbeta.item()} vs {br.grad.item()} (tol {tol})"
 
 
 @pytest.mark.parametrize(("r", "dtype"), [(128, torch.bfloat16), (256, torch.float16)])
