@@ -79,6 +79,7 @@ struct Layout {
   int acc_merge;  // the accumulation operand (dQ: K, dK: Q rows, MN-major) comes as one 128-row box per stage
   int off_a, off_b, off_t, off_red, off_ring, nst, off_pring, nsp, smem;
   int tmem_acc, tmem_s, tmem_p, tmem_cols;
+  int nsb;  // score (TMEM) buffers
 };
 
 // kind 0: dQ, 1: dK, 2: dV.  The kernel's own rows of Q (dQ) or K (dK, dV) of
@@ -110,7 +111,10 @@ __host__ __device__ inline Layout make_layout(int kind, int maps, int group, int
   L.tmem_acc = 0;
   const int acc = kind == 2 ? D / 2 : L.W / 2;
   L.tmem_s = acc;
-  L.tmem_p = L.tmem_s + 2 * (kTile / 2);
+  // score buffers: the dV kernel has no dP tiles, so its TMEM holds four (score products run three units
+  // ahead of the softmax); the dQ and dK kernels hold two next to their two dP buffers
+  L.nsb = kind == 2 ? 4 : 2;
+  L.tmem_p = L.tmem_s + L.nsb * (kTile / 2);
   const int cols = L.tmem_p + (kind == 2 ? 0 : 2 * (kTile / 2));
   L.tmem_cols = cols <= 256 ? 256 : (cols <= 512 ? 512 : 1024);
   return L;
@@ -143,7 +147,7 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ uint64_t in_full, o_full, r_full[kMaxStages], r_empty[kMaxStages];
   __shared__ uint64_t rp_full[kMaxStages], rp_empty[kMaxStages], dp_done;
-  __shared__ uint64_t s_full[2], p_full[2], dp_full[2], dp_free[2], ds_empty[2];
+  __shared__ uint64_t s_full[2], s_free[2], p_full[2], dp_full[2], dp_free[2], ds_empty[2];
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
 
@@ -180,6 +184,7 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
     mbar_init(&dp_done, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 16);  // score tile read out of TMEM: each softmax warp of the pair
       mbar_init(&p_full[i], 2);
       mbar_init(&dp_full[i], 1);
       mbar_init(&dp_free[i], 2);
@@ -352,7 +357,7 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
     auto issue_s = [&](int u) -> bool {
       const int sb = u & 1, s = unit_s(u);
       if (u < 300) trace_at(ft, 2048 + 4 * u);
-      if (u >= 2 && !mbar_wait(&p_full[sb], ((u - 2) >> 1) & 1u, ab, 22)) return false;
+      if (u >= 2 && !mbar_wait(&s_free[sb], ((u - 2) >> 1) & 1u, ab, 22)) return false;
       for (int cc = 0; cc < L.kw / 128; ++cc) {
         uint32_t st;
         if (!take(&st)) return false;
@@ -426,6 +431,7 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
     const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
     const uint32_t pf_leader = mapa_shared(smem_u32(&p_full[0]), 0);
     const uint32_t df_leader = mapa_shared(smem_u32(&dp_free[0]), 0);
+    const uint32_t sf_leader = mapa_shared(smem_u32(&s_free[0]), 0);
     const bool arriver = (warp == 2 && lane == 0);
     float* red = reinterpret_cast<float*>(smem + L.off_red);
     const float kLog2e = 1.4426950408889634f;
@@ -468,6 +474,9 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
           tmem_ld32(tmem + lane_base + L.tmem_s + sb * (kTile / 2) + ch * 32, sv);
           tmem_ld32(tmem + lane_base + L.tmem_p + (g & 1) * (kTile / 2) + ch * 32, pv);
           tmem_wait_ld();
+          tc_fence_before();  // the score buffer is free for the next product while this warp computes
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster_relaxed(sf_leader + sb * 8);
           const int k0 = j * kTile + half * 64 + ch * 32;
           int lim = p.T - k0;
           if (p.causal) lim = min(lim, t - k0 + 1);
@@ -520,6 +529,7 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
         }
       }
       if (arriver && u < 300) trace_at(ft, 3074 + 4 * u);
+      if (!ok && lane == 0) mbar_arrive_cluster_relaxed(sf_leader + sb * 8);  // aborted unit: counts stay whole
       tc_fence_before();
       named_bar_sync(1, 256);
       if (arriver) {
@@ -639,7 +649,8 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ uint64_t in_full, o_full, r_full[kMaxStages], r_empty[kMaxStages];
   __shared__ uint64_t rp_full[kMaxStages], rp_empty[kMaxStages], dp_done;
-  __shared__ uint64_t s_full[2], p_full[2], dp_full[2], dp_free[2], t_empty[2];
+  constexpr int kNSB = kDK ? 2 : 4;  // score buffers (Layout::nsb)
+  __shared__ uint64_t s_full[kNSB], s_free[kNSB], p_full[2], dp_full[2], dp_free[2], t_empty[2];
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
 
@@ -672,8 +683,11 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
       mbar_init(&rp_empty[i], 1);
     }
     mbar_init(&dp_done, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kNSB; ++i) {
       mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 16);  // score tile read out of TMEM: each softmax warp of the pair
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&p_full[i], 2);
       mbar_init(&dp_full[i], 1);
       mbar_init(&dp_free[i], 2);
@@ -771,9 +785,9 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
       }
     };
     // same order as the MMA warp below
-    emit_s(0);
+    for (int u = 0; u < kNSB - 1 && u < U; ++u) emit_s(u);  // same order as the MMA issuer
     for (int u = 0; ok && u < U; ++u) {
-      if (u + 1 < U) emit_s(u + 1);
+      if (u + kNSB - 1 < U) emit_s(u + kNSB - 1);
       if (kDK || unit_s(u) == maps - 1) emit_acc(u);
     }
     if (rank == 0) {  // drain: none of this producer's loads may be in flight at teardown
@@ -853,8 +867,8 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
     auto give = [&]() { commit_both(&r_empty[it % L.nst]); ++it; };
     const uint32_t ka = smem_u32(smem + L.off_a);
     auto issue_s = [&](int u) -> bool {  // S^T = K_s Q_s^T
-      const int sb = u & 1, s = unit_s(u);
-      if (u >= 2 && !mbar_wait(&p_full[sb], ((u - 2) >> 1) & 1u, ab, 22)) return false;
+      const int sb = u % kNSB, s = unit_s(u);
+      if (u >= kNSB && !mbar_wait(&s_free[sb], ((u / kNSB) - 1) & 1u, ab, 22)) return false;
       for (int cc = 0; cc < L.kw / 128; ++cc) {
         uint32_t st;
         if (!take(&st)) return false;
@@ -874,7 +888,9 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
     auto issue_acc = [&](int u) -> bool {
       const int g = unit_g(u), s = unit_s(u);
       const int tb = kDK ? (u & 1) : (g & 1);
-      if (!mbar_wait(&p_full[u & 1], (u >> 1) & 1u, ab, 24)) return false;
+      // dK: one dS tile per unit; dV: one mixed-probability tile per query tile
+      if (kDK ? !mbar_wait(&p_full[u & 1], (u >> 1) & 1u, ab, 24) : !mbar_wait(&p_full[g & 1], (g >> 1) & 1u, ab, 24))
+        return false;
       tc_fence_after();
       const uint32_t ta = smem_u32(smem + L.off_t + tb * (kRows * kTile * 2));
       const int nins = kDK ? L.nins : dins;
@@ -912,9 +928,9 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
     };
     bool ok = mbar_wait(&in_full, 0, ab, 21);
     tc_fence_after();
-    if (ok) ok = issue_s(0);
+    for (int u = 0; ok && u < kNSB - 1 && u < U; ++u) ok = issue_s(u);
     for (int u = 0; ok && u < U; ++u) {
-      if (u + 1 < U) ok = issue_s(u + 1);
+      if (u + kNSB - 1 < U) ok = issue_s(u + kNSB - 1);
       if (ok && (kDK || unit_s(u) == maps - 1)) ok = issue_acc(u);
     }
     commit_both(&o_full);
@@ -931,6 +947,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
     const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
     const uint32_t pf_leader = mapa_shared(smem_u32(&p_full[0]), 0);
     const uint32_t df_leader = mapa_shared(smem_u32(&dp_free[0]), 0);
+    const uint32_t sf_leader = mapa_shared(smem_u32(&s_free[0]), 0);
     const bool arriver = (warp == 2 && lane == 0);
     float* red = reinterpret_cast<float*>(smem + L.off_red);  // [tile parity][2][maps][128]: lse2, delta
     const float kLog2e = 1.4426950408889634f;
@@ -944,7 +961,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
     float pm[kDK ? 1 : 32];
     bool ok = true;
     for (int u = 0; u < U; ++u) {
-      const int sb = u & 1, s = unit_s(u), g = unit_g(u);
+      const int sb = u % kNSB, s = unit_s(u), g = unit_g(u);
       const int qt = (i0 + g) * kTile;
       float* rt = red + (g & 1) * (2 * kMaxMaps * 128);
       if (s == 0 && wg == 0) {  // stage this query tile's log-sum-exp (and delta) of every map
@@ -955,7 +972,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
           if (kDK) rt[(kMaxMaps + m) * 128 + l] = qv ? p.delta[((int64_t)b * maps + m) * p.T + q] : 0.f;
         }
       }
-      if (ok) ok = mbar_wait(&s_full[sb], (u >> 1) & 1u, ab, 32);
+      if (ok) ok = mbar_wait(&s_full[sb], (u / kNSB) & 1u, ab, 32);
       if (ok && kDK && s == 0) ok = mbar_wait(&dp_full[g & 1], (g >> 1) & 1u, ab, 35);
       // the tile buffer written by this unit must have been read by the product two uses ago
       if (ok && kDK && u >= 2) ok = mbar_wait(&t_empty[u & 1], ((u - 2) >> 1) & 1u, ab, 33);
@@ -974,6 +991,9 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
           tmem_ld32(tmem + lane_base + L.tmem_s + sb * (kTile / 2) + ch * 32, sv);
           if (kDK) tmem_ld32(tmem + lane_base + L.tmem_p + (g & 1) * (kTile / 2) + ch * 32, dpv);
           tmem_wait_ld();
+          tc_fence_before();  // the score buffer is free for the next product while this warp computes
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster_relaxed(sf_leader + sb * 8);
           const int qc0 = half * 64 + ch * 32;  // query column inside the tile
           // valid query columns e: lo <= e < hi (causal: queries at or after this key)
           const int hi = live ? p.T - (qt + qc0) : 0;
@@ -1001,10 +1021,12 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
         }
         if (kDK || s == maps - 1) fence_proxy_async();
       }
+      if (!ok && lane == 0) mbar_arrive_cluster_relaxed(sf_leader + sb * 8);  // aborted unit: counts stay whole
       tc_fence_before();
       named_bar_sync(1, 256);
       if (arriver) {
-        mbar_arrive_cluster(pf_leader + sb * 8);
+        if (kDK) mbar_arrive_cluster(pf_leader + (u & 1) * 8);
+        else if (s == maps - 1) mbar_arrive_cluster(pf_leader + (g & 1) * 8);
         if (kDK && s == maps - 1) mbar_arrive_cluster(df_leader + (g & 1) * 8);
       }
     }

@@ -88,6 +88,12 @@ DA_DEV void mbar_arrive_cluster(uint32_t cluster_addr) {
                :: "r"(cluster_addr) : "memory");
 }
 
+// Arrive with relaxed semantics (no memory ordering): for barriers that only count events, such as
+// "this warp has read its TMEM columns" after tcgen05.fence::before_thread_sync.
+DA_DEV void mbar_arrive_cluster_relaxed(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" :: "r"(cluster_addr) : "memory");
+}
+
 // Upper bound on how long one probe may suspend the thread (the hardware
 // resumes it earlier when the phase completes).
 #ifndef DA_SUSPEND_HINT_NS
