@@ -50,6 +50,8 @@ SIGNATURES: dict[str, list] = {
     "da_attn_fwd": [_p, _i64, _i64, _i64, _i64, _p, _i64, _i64, _i64, _i64, _p, _i32, _i32, _i32, _i32, _i32, _i32,
                     _p, _i32, _i32, _p, _p, _p, _f32, _p, _p, _p, _p],
     "da_attn_bwd_delta": [_p, _p, _i64, _i32, _i32, _p, _p],
+    "da_gemm_ex": [_p, _i64, _p, _i64, _i32, _i64, _p, _i64, _p, _i64, _i64, _p, _i64, _i64, _i64, _i32, _p, _i32,
+                   _p, _i64, _p, _p],
     "da_gemm_splitk_workspace_elems": [_i64, _i64, _i64, _i32],  # returns int64 (set below)
     "da_gemm_splitk": [_p, _i64, _i32, _p, _i64, _i32, _p, _i64, _i64, _i64, _i64, _i32, _i32, _p, _i64, _p, _p],
     "da_gemm_splitk_grouped": [_p, _i64, _i64, _p, _i64, _p, _i64, _i64, _i64, _i64, _i32, _i32, _i32, _p, _i64, _p,

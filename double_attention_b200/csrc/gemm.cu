@@ -41,11 +41,29 @@ struct Params {
   // partial + split * M * N and splitk_reduce_kernel adds them in split order (deterministic); null: each
   // split adds its partial into C with fp32 atomics (order-dependent rounding)
   float* partial = nullptr;
+  // a second K segment: K stages kb >= nk1 come from the second pair of tensor maps (C = A.B^T + A2.B2^T);
+  // nk1 = 0: one segment
+  int nk1 = 0;
+  // epilogue of the operand-dtype output: + bias[n] (operand dtype, or null), then act 1: GELU (the
+  // pre-activation also stored in aux when aux is set), act 2: times GELU'(aux[m, n]); aux [M, N] with row
+  // stride ldaux in the operand dtype
+  const void* bias = nullptr;
+  int act = 0;
+  void* aux = nullptr;
+  int64_t ldaux = 0;
 };
+
+// GELU with the exact erf form (nn.GELU's default) and its derivative.
+DA_DEV float gelu_f(float z) { return 0.5f * z * (1.f + erff(z * 0.70710678118654752f)); }
+DA_DEV float gelu_grad_f(float z) {
+  return 0.5f * (1.f + erff(z * 0.70710678118654752f)) + z * 0.39894228040143268f * expf(-0.5f * z * z);
+}
 
 template <typename T, int kN, bool kAmn, bool kBmn>
 __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap ta,
-                                                           const __grid_constant__ CUtensorMap tb, const Params p) {
+                                                           const __grid_constant__ CUtensorMap tb,
+                                                           const __grid_constant__ CUtensorMap ta2,
+                                                           const __grid_constant__ CUtensorMap tb2, const Params p) {
   using C = Cfg<kN>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -54,7 +72,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   __shared__ int abort_flag;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int m0 = blockIdx.x * kBM, n0 = blockIdx.y * kN;
-  const int nk_all = (p.K + kBK - 1) / kBK;  // TMA zero-fills the ragged last K stage
+  const int nk_all = p.nk1 ? p.nk1 + (p.K - p.nk1 * kBK + kBK - 1) / kBK  // two segments (K = K1 + K2)
+                           : (p.K + kBK - 1) / kBK;  // TMA zero-fills the ragged last K stage
   // split-K: this CTA reduces K stages [kb0, kb0 + nk) and adds its partial sum atomically
   const bool split = gridDim.z > 1;
   const int kb0 = split ? (int)blockIdx.z * p.kps : 0;
@@ -85,6 +104,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     if (lane == 0) {
       prefetch_tmap(&ta);
       prefetch_tmap(&tb);
+      if (p.nk1) {
+        prefetch_tmap(&ta2);
+        prefetch_tmap(&tb2);
+      }
       int issued = 0;
       for (int kb = 0; kb < nk; ++kb) {
         const int s = kb % C::kStages;
@@ -92,20 +115,23 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         mbar_arrive_expect_tx(&full[s], C::kABytes + C::kBBytes);
         uint8_t* sa = smem + s * (C::kABytes + C::kBBytes);
         uint8_t* sb = sa + C::kABytes;
+        const bool second = p.nk1 && kb0 + kb >= p.nk1;
+        const CUtensorMap* tA = second ? &ta2 : &ta;
+        const CUtensorMap* tB = second ? &tb2 : &tb;
+        const int kk = second ? kb0 + kb - p.nk1 : kb0 + kb;  // K stage inside its segment
         if (!kAmn) {
-          tma_load_2d(&ta, &full[s], sa, (kb0 + kb) * kBK, m0);
+          tma_load_2d(tA, &full[s], sa, kk * kBK, m0);
         } else {
-          const int kbg = kb0 + kb;
-          const int grp = p.kseg ? kbg / p.kseg : 0;
-          const int ax = m0 + grp * p.a_goff, ay = (kbg - grp * p.kseg) * kBK;
-          tma_load_2d(&ta, &full[s], sa, ax, ay);
-          tma_load_2d(&ta, &full[s], sa + kBK * 128, ax + 64, ay);
+          const int grp = p.kseg ? kk / p.kseg : 0;
+          const int ax = m0 + grp * p.a_goff, ay = (kk - grp * p.kseg) * kBK;
+          tma_load_2d(tA, &full[s], sa, ax, ay);
+          tma_load_2d(tA, &full[s], sa + kBK * 128, ax + 64, ay);
         }
         if (!kBmn) {
-          tma_load_2d(&tb, &full[s], sb, (kb0 + kb) * kBK, n0);
+          tma_load_2d(tB, &full[s], sb, kk * kBK, n0);
         } else {
           for (int i = 0; i < kN / 64; ++i)
-            tma_load_2d(&tb, &full[s], sb + i * kBK * 128, n0 + i * 64, (kb0 + kb) * kBK);
+            tma_load_2d(tB, &full[s], sb + i * kBK * 128, n0 + i * 64, kk * kBK);
         }
         issued = kb + 1;
       }
@@ -170,6 +196,46 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
           }
         } else {
           T* dst = reinterpret_cast<T*>(p.c) + (size_t)row * p.ldc + n0 + c;
+          if (p.bias) {
+            const uint4* b4 = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.bias) + n0 + c);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const uint4 bv = __ldg(b4 + e);
+              const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
+#pragma unroll
+              for (int h = 0; h < 4; ++h) {
+                const float2 f = unpack2<T>(bw[h]);
+                v[8 * e + 2 * h] += f.x;
+                v[8 * e + 2 * h + 1] += f.y;
+              }
+            }
+          }
+          if (p.act == 1) {  // GELU; the pre-activation (rounded as stored) kept for the backward
+            if (p.aux) {
+              T* za = reinterpret_cast<T*>(p.aux) + (size_t)row * p.ldaux + n0 + c;
+              uint32_t zw[16];
+#pragma unroll
+              for (int e = 0; e < 16; ++e) zw[e] = pack2<T>(v[2 * e], v[2 * e + 1]);
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                reinterpret_cast<uint4*>(za)[e] = make_uint4(zw[4 * e], zw[4 * e + 1], zw[4 * e + 2], zw[4 * e + 3]);
+            }
+#pragma unroll
+            for (int e = 0; e < 32; ++e) v[e] = gelu_f(v[e]);
+          } else if (p.act == 2) {  // times GELU' of the stored pre-activation
+            const uint4* z4 = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.aux) + (size_t)row * p.ldaux + n0 + c);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const uint4 zv = z4[e];
+              const uint32_t zw[4] = {zv.x, zv.y, zv.z, zv.w};
+#pragma unroll
+              for (int h = 0; h < 4; ++h) {
+                const float2 f = unpack2<T>(zw[h]);
+                v[8 * e + 2 * h] *= gelu_grad_f(f.x);
+                v[8 * e + 2 * h + 1] *= gelu_grad_f(f.y);
+              }
+            }
+          }
           uint32_t w[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e) w[e] = pack2<T>(v[2 * e], v[2 * e + 1]);
@@ -327,6 +393,270 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_seg_kernel(const __grid_cons
   if (warp == 1) tmem_dealloc<1>(tmem, kN);
 }
 
+// ----------------------------------------------------------------------------------------------- persistent
+// The operand-dtype GEMM of the layers around the routed attention (da_gemm_ex), persistent: one CTA per
+// SM walks the 128 x 256 output tiles (N fastest, so CTAs running side by side read the same A rows from
+// L2).  Two producer warps take alternate 48 KB stages (each completes about one stage per 0.4 us, and a
+// stage feeds 4.2 MFLOP, 0.27 us of the SM's tensor pipe), and the accumulator is double-buffered in TMEM
+// (2 x 256 columns), so the epilogue of one tile (bias, GELU or GELU', conversion, stores) runs while the
+// tensor core computes the next.
+namespace pk {
+constexpr int kN = 256;
+constexpr int kStages = 4;
+constexpr int kABytes = kBM * kBK * 2;          // 16 KB
+constexpr int kBBytes = kN * kBK * 2;           // 32 KB
+constexpr int kStageBytes = kABytes + kBBytes;  // 48 KB
+constexpr int kSmem = kStages * kStageBytes;
+constexpr int kThreads = 224;                   // warps 0 and 6 TMA, 1 MMA, 2-5 epilogue
+constexpr int kProducer2 = 6;
+}  // namespace pk
+
+template <typename T>
+DA_DEV void epilogue_tile_chunk(const Params& p, int row, int col, float (&v)[32]) {
+  T* dst = reinterpret_cast<T*>(p.c) + (size_t)row * p.ldc + col;
+  if (p.bias) {
+    const uint4* b4 = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.bias) + col);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const uint4 bv = __ldg(b4 + e);
+      const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const float2 f = unpack2<T>(bw[h]);
+        v[8 * e + 2 * h] += f.x;
+        v[8 * e + 2 * h + 1] += f.y;
+      }
+    }
+  }
+  if (p.act == 1) {
+    if (p.aux) {
+      T* za = reinterpret_cast<T*>(p.aux) + (size_t)row * p.ldaux + col;
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        reinterpret_cast<uint4*>(za)[e] = make_uint4(pack2<T>(v[8 * e], v[8 * e + 1]), pack2<T>(v[8 * e + 2], v[8 * e + 3]),
+                                                     pack2<T>(v[8 * e + 4], v[8 * e + 5]), pack2<T>(v[8 * e + 6], v[8 * e + 7]));
+    }
+#pragma unroll
+    for (int e = 0; e < 32; ++e) v[e] = gelu_f(v[e]);
+  } else if (p.act == 2) {
+    const uint4* z4 = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.aux) + (size_t)row * p.ldaux + col);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const uint4 zv = z4[e];
+      const uint32_t zw[4] = {zv.x, zv.y, zv.z, zv.w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const float2 f = unpack2<T>(zw[h]);
+        v[8 * e + 2 * h] *= gelu_grad_f(f.x);
+        v[8 * e + 2 * h + 1] *= gelu_grad_f(f.y);
+      }
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < 4; ++e)
+    reinterpret_cast<uint4*>(dst)[e] = make_uint4(pack2<T>(v[8 * e], v[8 * e + 1]), pack2<T>(v[8 * e + 2], v[8 * e + 3]),
+                                                  pack2<T>(v[8 * e + 4], v[8 * e + 5]), pack2<T>(v[8 * e + 6], v[8 * e + 7]));
+}
+
+template <typename T, bool kAmn, bool kBmn>
+__global__ void __launch_bounds__(pk::kThreads, 1) gemm_pk_kernel(const __grid_constant__ CUtensorMap ta,
+                                                                  const __grid_constant__ CUtensorMap tb,
+                                                                  const __grid_constant__ CUtensorMap ta2,
+                                                                  const __grid_constant__ CUtensorMap tb2,
+                                                                  const Params p) {
+  using namespace pk;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t full[kStages], empty[kStages], acc_full[2], acc_empty[2];
+  __shared__ uint32_t tmem_base;
+  __shared__ int abort_flag;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  // work items: output tiles, each split into `splits` K ranges of p.kps stages (split-K, fp32 partial tiles
+  // into p.partial); splits = 1 writes the epilogue output
+  const int n_tiles = (p.N + kN - 1) / kN, m_tiles = (p.M + kBM - 1) / kBM;
+  const int nk_all = p.nk1 ? p.nk1 + (p.K - p.nk1 * kBK + kBK - 1) / kBK : (p.K + kBK - 1) / kBK;
+  const int splits = p.partial ? (nk_all + p.kps - 1) / p.kps : 1;
+  const int tiles = n_tiles * m_tiles * splits;
+  const int my_tiles = blockIdx.x < tiles ? (tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  Abort ab{&abort_flag, p.status};
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
+    }
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc<1>(&tmem_base, 2 * kN);
+    tmem_relinquish<1>();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  grid_dependency_wait();
+  grid_launch_dependents();
+  const uint32_t tmem = tmem_base;
+  auto tile_mn = [&](int i, int& m0, int& n0, int& kb0, int& nk) {
+    const int w = (int)blockIdx.x + i * (int)gridDim.x;
+    const int t = w / splits, z = w % splits;  // splits of one tile run side by side
+    m0 = (t / n_tiles) * kBM;
+    n0 = (t % n_tiles) * kN;
+    kb0 = z * (splits > 1 ? p.kps : 0);
+    nk = splits > 1 ? min(p.kps, nk_all - kb0) : nk_all;
+  };
+
+  if ((warp == 0 || warp == kProducer2) && lane == 0) {
+    // ---------------------------------------------------------------- TMA producers (alternate stages)
+    const int pi = warp == 0 ? 0 : 1;
+    prefetch_tmap(&ta);
+    prefetch_tmap(&tb);
+    if (p.nk1) {
+      prefetch_tmap(&ta2);
+      prefetch_tmap(&tb2);
+    }
+    bool ok = true;
+    int it = 0, last = -1;
+    for (int i = 0; ok && i < my_tiles; ++i) {
+      int m0, n0, kb0, nk;
+      tile_mn(i, m0, n0, kb0, nk);
+      for (int kb = kb0; kb < kb0 + nk; ++kb, ++it) {
+        if ((it & 1) != pi) continue;
+        const int s = it % kStages;
+        if (!mbar_wait(&empty[s], ((it / kStages) & 1u) ^ 1u, ab, 44)) { ok = false; break; }
+        mbar_arrive_expect_tx(&full[s], kStageBytes);
+        uint8_t* sa = smem + s * kStageBytes;
+        uint8_t* sb = sa + kABytes;
+        const bool second = p.nk1 && kb >= p.nk1;
+        const CUtensorMap* tA = second ? &ta2 : &ta;
+        const CUtensorMap* tB = second ? &tb2 : &tb;
+        const int kk = second ? kb - p.nk1 : kb;
+        if (!kAmn) {
+          tma_load_2d(tA, &full[s], sa, kk * kBK, m0);
+        } else {  // A stored [K, M]: this stage's 64 K rows, the tile's 128 M columns as two boxes
+          tma_load_2d(tA, &full[s], sa, m0, kk * kBK);
+          tma_load_2d(tA, &full[s], sa + kBK * 128, m0 + 64, kk * kBK);
+        }
+        if (!kBmn) {
+          tma_load_2d(tB, &full[s], sb, kk * kBK, n0);
+        } else {
+          for (int j = 0; j < kN / 64; ++j) tma_load_2d(tB, &full[s], sb + j * kBK * 128, n0 + j * 64, kk * kBK);
+        }
+        last = it;
+      }
+    }
+    // drain this producer's last loads (at most kStages / 2 of them can be in flight)
+    for (int j = (last - kStages + 1 > 0 ? last - kStages + 1 : 0); j <= last; ++j)
+      if ((j & 1) == pi) mbar_wait_drain(&full[j % kStages], (j / kStages) & 1u);
+  } else if (warp == 1 && lane == 0) {
+    // ---------------------------------------------------------------- MMA issuer
+    const uint32_t idesc = idesc_f16(kBM, kN, std::is_same<T, __nv_bfloat16>::value, kAmn, kBmn);
+    bool ok = true;
+    int it = 0;
+    for (int i = 0; ok && i < my_tiles; ++i) {
+      const int buf = i & 1;
+      int m0, n0, kb0, nk;
+      tile_mn(i, m0, n0, kb0, nk);
+      if (i >= 2 && !mbar_wait(&acc_empty[buf], ((i >> 1) - 1) & 1u, ab, 45)) break;
+      tc_fence_after();
+      const uint32_t d = tmem + buf * kN;
+      for (int kb = 0; kb < nk; ++kb, ++it) {
+        const int s = it % kStages;
+        if (!mbar_wait(&full[s], (it / kStages) & 1u, ab, 46)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t sa = smem_u32(smem + s * kStageBytes);
+        const uint32_t sb = sa + kABytes;
+#pragma unroll
+        for (int k = 0; k < kBK / 16; ++k) {
+          const uint64_t ad = kAmn ? sdesc_sw128(sa + k * 16 * 128, kBK * 128, 1024) : sdesc_sw128(sa + k * 32, 16, 1024);
+          const uint64_t bd = kBmn ? sdesc_sw128(sb + k * 16 * 128, kBK * 128, 1024) : sdesc_sw128(sb + k * 32, 16, 1024);
+          mma_f16_ss<1>(d, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+        }
+        mma_commit<1>(smem_u32(&empty[s]));
+      }
+      if (ok) mma_commit<1>(smem_u32(&acc_full[buf]));
+    }
+  } else if (warp >= 2 && warp <= 5) {
+    // ---------------------------------------------------------------- epilogue (thread = output row)
+    const int quad = warp & 3;
+    bool ok = true;
+    for (int i = 0; i < my_tiles; ++i) {
+      const int buf = i & 1;
+      int m0, n0, kb0, nk;
+      tile_mn(i, m0, n0, kb0, nk);
+      if (ok) ok = mbar_wait(&acc_full[buf], (i >> 1) & 1u, ab, 47);
+      ok = __all_sync(0xffffffffu, ok);
+      tc_fence_after();
+      const int row = m0 + quad * 32 + lane;
+      if (ok) {
+        for (int c = 0; c < kN; c += 32) {
+          float v[32];
+          tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + buf * kN + c, v);
+          tmem_wait_ld();
+          if (row >= p.M || n0 + c >= p.N) continue;
+          if (splits > 1) {  // this split's fp32 partial tile (added in split order by splitk_reduce_kernel)
+            const int z = kb0 / p.kps;
+            float4* dst = reinterpret_cast<float4*>(p.partial + ((size_t)z * p.M + row) * p.N + n0 + c);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) dst[e] = make_float4(v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3]);
+          } else {
+            epilogue_tile_chunk<T>(p, row, n0 + c, v);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc<1>(tmem, 2 * kN);
+}
+
+template <typename T, bool kAmn, bool kBmn>
+int launch_pk(const void* A, int64_t lda, const void* B, int64_t ldb, const void* A2, int64_t lda2, const void* B2,
+              int64_t ldb2, int64_t K2, const Params& p, cudaStream_t st) {
+  const CUtensorMapDataType dt =
+      std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const int64_t K1 = A2 ? (int64_t)p.nk1 * kBK : p.K;
+  CUtensorMap ta, tb, ta2, tb2;
+  if (kAmn) {  // A stored [K, M]
+    if (int rc = make_tmap_2d(&ta, A, dt, 2, p.M, K1, (uint64_t)lda * 2, 64, kBK)) return rc;
+  } else {
+    if (int rc = make_tmap_2d(&ta, A, dt, 2, K1, p.M, (uint64_t)lda * 2, 64, kBM)) return rc;
+  }
+  if (kBmn) {
+    if (int rc = make_tmap_2d(&tb, B, dt, 2, p.N, K1, (uint64_t)ldb * 2, 64, kBK)) return rc;
+  } else {
+    if (int rc = make_tmap_2d(&tb, B, dt, 2, K1, p.N, (uint64_t)ldb * 2, 64, pk::kN)) return rc;
+  }
+  ta2 = ta;
+  tb2 = tb;
+  if (A2) {
+    if (int rc = make_tmap_2d(&ta2, A2, dt, 2, K2, p.M, (uint64_t)lda2 * 2, 64, kBM)) return rc;
+    if (kBmn) {
+      if (int rc = make_tmap_2d(&tb2, B2, dt, 2, p.N, K2, (uint64_t)ldb2 * 2, 64, kBK)) return rc;
+    } else {
+      if (int rc = make_tmap_2d(&tb2, B2, dt, 2, K2, p.N, (uint64_t)ldb2 * 2, 64, pk::kN)) return rc;
+    }
+  }
+  auto kern = gemm_pk_kernel<T, kAmn, kBmn>;
+  const int smem = pk::kSmem + 1024;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return record_cuda_error();
+  const int nk_all = p.nk1 ? p.nk1 + (int)((p.K - p.nk1 * kBK + kBK - 1) / kBK) : (int)((p.K + kBK - 1) / kBK);
+  const int splits = p.partial ? (nk_all + p.kps - 1) / p.kps : 1;
+  const int tiles = (int)(((p.M + kBM - 1) / kBM) * ((p.N + pk::kN - 1) / pk::kN)) * splits;
+  const int grid = tiles < sm_count() ? tiles : sm_count();
+  return launch_kernel(kern, dim3((unsigned)grid), dim3(pk::kThreads), smem, st, false, ta, tb, ta2, tb2, p);
+}
+
 // C[m, n] += sum over splits z, in index order, of partial[z, m, n] (four columns per thread).
 __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* partial, int splits, int M, int N, float* c,
                                                             int64_t ldc) {
@@ -385,7 +715,34 @@ int launch(const void* A, int64_t lda, const void* B, int64_t ldb, const Params&
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return record_cuda_error();
   dim3 grid((unsigned)((p.M + kBM - 1) / kBM), (unsigned)((p.N + kN - 1) / kN), (unsigned)splits);
-  return launch_kernel(kern, grid, dim3(kThreads), smem, st, false, ta, tb, p);
+  return launch_kernel(kern, grid, dim3(kThreads), smem, st, false, ta, tb, ta, tb, p);
+}
+
+// The same with a second K segment (A2 [M, K2] / B2 in the modes of A / B): C = A.B^T + A2.B2^T.
+template <typename T, int kN, bool kAmn, bool kBmn>
+int launch2(const void* A, int64_t lda, const void* B, int64_t ldb, const void* A2, int64_t lda2, const void* B2,
+            int64_t ldb2, int64_t K2, const Params& p, cudaStream_t st) {
+  static_assert(!kAmn, "the second segment takes a K-major A");
+  using C = Cfg<kN>;
+  const CUtensorMapDataType dt =
+      std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const int64_t K1 = (int64_t)p.nk1 * kBK;
+  CUtensorMap ta, tb, ta2, tb2;
+  if (int rc = make_tmap_2d(&ta, A, dt, 2, K1, p.M, (uint64_t)lda * 2, 64, kBM)) return rc;
+  if (int rc = make_tmap_2d(&ta2, A2, dt, 2, K2, p.M, (uint64_t)lda2 * 2, 64, kBM)) return rc;
+  if (kBmn) {
+    if (int rc = make_tmap_2d(&tb, B, dt, 2, p.N, K1, (uint64_t)ldb * 2, 64, kBK)) return rc;
+    if (int rc = make_tmap_2d(&tb2, B2, dt, 2, p.N, K2, (uint64_t)ldb2 * 2, 64, kBK)) return rc;
+  } else {
+    if (int rc = make_tmap_2d(&tb, B, dt, 2, K1, p.N, (uint64_t)ldb * 2, 64, kN)) return rc;
+    if (int rc = make_tmap_2d(&tb2, B2, dt, 2, K2, p.N, (uint64_t)ldb2 * 2, 64, kN)) return rc;
+  }
+  auto kern = gemm_kernel<T, kN, kAmn, kBmn>;
+  const int smem = C::kSmem + 1024;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return record_cuda_error();
+  dim3 grid((unsigned)((p.M + kBM - 1) / kBM), (unsigned)((p.N + kN - 1) / kN), 1);
+  return launch_kernel(kern, grid, dim3(kThreads), smem, st, false, ta, tb, ta2, tb2, p);
 }
 
 template <typename T>
@@ -426,6 +783,60 @@ extern "C" int da_gemm(const void* A, int64_t lda, int a_mn_major, const void* B
   return gemm::dispatch<__half>(a_mn_major, b_mn_major, n_tile, A, lda, B, ldb, p, 1, st);
 }
 
+extern "C" int da_gemm_ex(const void* A, int64_t lda, const void* B, int64_t ldb, int b_mn_major, int64_t K,
+                          const void* A2, int64_t lda2, const void* B2, int64_t ldb2, int64_t K2, void* C,
+                          int64_t ldc, int64_t M, int64_t N, int dtype, const void* bias, int act, void* aux,
+                          int64_t ldaux, int* status, void* stream) {
+  using namespace da;
+  if (!A || !B || !C || !status) return DA_ERR_NULL;
+  if ((A2 == nullptr) != (B2 == nullptr)) return DA_ERR_NULL;
+  if (act < 0 || act > 2) return DA_ERR_UNSUPPORTED;
+  if (act == 2 && !aux) return DA_ERR_NULL;
+  if (int rc = bind_device(A)) return rc;
+  if (dtype != DA_BF16 && dtype != DA_F16) return DA_ERR_DTYPE;
+  if (M <= 0 || N <= 0 || K <= 0 || N % 128 || (A2 && (K2 <= 0 || K % gemm::kBK))) return DA_ERR_SHAPE;
+  if ((lda % 8) || (ldb % 8) || (A2 && ((lda2 % 8) || (ldb2 % 8))) || (ldc % 8) || (aux && (ldaux % 8)))
+    return DA_ERR_ALIGN;
+  const uintptr_t any = reinterpret_cast<uintptr_t>(C) | reinterpret_cast<uintptr_t>(bias) |
+                        reinterpret_cast<uintptr_t>(aux);
+  if (any & 15) return DA_ERR_ALIGN;
+  gemm::Params p{(int)M, (int)N, (int)(K + (A2 ? K2 : 0)), C, ldc, 0, 0, status, 0};
+  p.nk1 = A2 ? (int)(K / gemm::kBK) : 0;
+  p.bias = bias;
+  p.act = act;
+  p.aux = aux;
+  p.ldaux = ldaux;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool bf = dtype == DA_BF16;
+  if (N % 256 == 0) {  // the persistent kernel (256-column tiles)
+    if (bf) return b_mn_major ? gemm::launch_pk<__nv_bfloat16, false, true>(A, lda, B, ldb, A2, lda2, B2, ldb2, K2, p, st)
+                              : gemm::launch_pk<__nv_bfloat16, false, false>(A, lda, B, ldb, A2, lda2, B2, ldb2, K2, p, st);
+    return b_mn_major ? gemm::launch_pk<__half, false, true>(A, lda, B, ldb, A2, lda2, B2, ldb2, K2, p, st)
+                      : gemm::launch_pk<__half, false, false>(A, lda, B, ldb, A2, lda2, B2, ldb2, K2, p, st);
+  }
+  const int n_tile = (N % 256 == 0 && (M / 128) * (N / 256) >= 120) ? 256 : 128;
+  if (!A2) {
+    if (bf) return gemm::dispatch<__nv_bfloat16>(0, b_mn_major, n_tile, A, lda, B, ldb, p, 1, st);
+    return gemm::dispatch<__half>(0, b_mn_major, n_tile, A, lda, B, ldb, p, 1, st);
+  }
+#define DA_GEMM2_CASE(TT, NT, BMN)                                                                       \
+  if (n_tile == NT && (b_mn_major != 0) == BMN)                                                         \
+    return gemm::launch2<TT, NT, false, BMN>(A, lda, B, ldb, A2, lda2, B2, ldb2, K2, p, st);
+  if (bf) {
+    DA_GEMM2_CASE(__nv_bfloat16, 128, false)
+    DA_GEMM2_CASE(__nv_bfloat16, 256, false)
+    DA_GEMM2_CASE(__nv_bfloat16, 128, true)
+    DA_GEMM2_CASE(__nv_bfloat16, 256, true)
+  } else {
+    DA_GEMM2_CASE(__half, 128, false)
+    DA_GEMM2_CASE(__half, 256, false)
+    DA_GEMM2_CASE(__half, 128, true)
+    DA_GEMM2_CASE(__half, 256, true)
+  }
+#undef DA_GEMM2_CASE
+  return DA_ERR_UNSUPPORTED;
+}
+
 extern "C" int64_t da_gemm_splitk_workspace_elems(int64_t M, int64_t N, int64_t K, int splits) {
   if (M <= 0 || N <= 0 || K <= 0 || M % 128 || N % 128) return -1;
   int s = 0, kps = 0;
@@ -453,6 +864,14 @@ extern "C" int da_gemm_splitk(const void* A, int64_t lda, int a_mn_major, const 
     p.partial = workspace;
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (p.partial && splits > 1 && a_mn_major && b_mn_major && N % 256 == 0) {
+    // the weight gradients of the block's layers: the persistent kernel's split-K work items
+    const int rc = dtype == DA_BF16
+                       ? gemm::launch_pk<__nv_bfloat16, true, true>(A, lda, B, ldb, nullptr, 0, nullptr, 0, 0, p, st)
+                       : gemm::launch_pk<__half, true, true>(A, lda, B, ldb, nullptr, 0, nullptr, 0, 0, p, st);
+    if (rc) return rc;
+    return gemm::splitk_reduce(p, splits, st);
+  }
   int rc = dtype == DA_BF16
                ? gemm::dispatch<__nv_bfloat16>(a_mn_major, b_mn_major, n_tile, A, lda, B, ldb, p, splits, st)
                : gemm::dispatch<__half>(a_mn_major, b_mn_major, n_tile, A, lda, B, ldb, p, splits, st);

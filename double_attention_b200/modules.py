@@ -187,7 +187,10 @@ class SharedDictionaryAttention(nn.Module):
 
         if cfg.map_combine == "weighted_sum":
             combined = ops.routed_attention_mixed(routed, dense_value, score_scales, map_weights, cfg)
-            output = self.output(combined.to(self._output_dtype(combined)))
+            if isinstance(self.output, nn.Linear) and ops.linear_supported(combined, self.output):
+                output = ops.linear(combined, self.output)  # the output projection on the tcgen05 GEMM
+            else:
+                output = self.output(combined.to(self._output_dtype(combined)))
         else:
             per_map = ops.routed_attention_maps(routed, dense_value, score_scales, cfg)  # [B,S,T,D]
             output = self.output(per_map.permute(0, 2, 1, 3).flatten(2))
@@ -265,6 +268,9 @@ class DoubleAttentionBlock(nn.Module):
     def _feedforward_branch(self, normalized_x: Tensor, bank: SharedDictionaryBank,
                             normalized_dictionary: tuple[Tensor, Tensor] | None) -> Tensor:
         if not self.attention.config.q_dictionary_feedforward:
+            first, act, second, drop = self.feedforward
+            if act.approximate == "none" and ops.feedforward_supported(normalized_x, first, second):
+                return drop(ops.feedforward(normalized_x, first, second))  # GELU fused into the GEMMs
             return self.feedforward(normalized_x)
         if normalized_dictionary is None:
             dictionary_key, _ = bank.normalized(self.attention.config.eps)

@@ -1017,6 +1017,154 @@ def gemm(a: Tensor, a_mn: bool, b: Tensor, b_mn: bool, m: int, n: int, k: int, o
     return out
 
 
+def gemm_ex(a: Tensor, b: Tensor, b_mn: bool, out: Tensor, a2: Tensor | None = None, b2: Tensor | None = None,
+            bias: Tensor | None = None, act: int = 0, aux: Tensor | None = None) -> Tensor:
+    """out [M, N] = act(A . B^T [+ A2 . B2^T] + bias) in the operand dtype (see da_gemm_ex): A [M, K] row-major;
+    B [N, K], or [K, N] with ``b_mn``; act 0 none, 1 GELU (pre-activation into ``aux`` when given), 2 times
+    GELU'(aux)."""
+    m, k = a.shape
+    n = out.shape[1]
+    k2 = 0 if a2 is None else a2.shape[1]
+    for t in (a, b, out, a2, b2, bias, aux):
+        if t is not None and (t.dtype != a.dtype or t.stride(-1) != 1):
+            raise ValueError("gemm_ex tensors must be row-major and share the operand dtype")
+    call("da_gemm_ex", a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0), int(b_mn), k, ptr(a2),
+         0 if a2 is None else a2.stride(0), ptr(b2), 0 if b2 is None else b2.stride(0), k2, out.data_ptr(),
+         out.stride(0), m, n, dtype_code(a.dtype), ptr(bias), act, ptr(aux), 0 if aux is None else aux.stride(0),
+         workspace(a.device).status.data_ptr(), stream_ptr(a.device))
+    return out
+
+
+def _bias_grad(d: Tensor) -> Tensor:
+    """Column sums of a [rows, N] gradient, accumulated in fp32 (the bias gradient of a Linear)."""
+    return torch.sum(d, dim=0, dtype=torch.float32)
+
+
+class _Linear(torch.autograd.Function):
+    """y [M, N] = x [M, K] . W[N, K]^T (+ b) on the tcgen05 GEMM, in the compute dtype: the output projection
+    of SharedDictionaryAttention (modules.py:272) and any Linear of the block."""
+
+    @staticmethod
+    def forward(ctx, x2d: Tensor, weight: Tensor, bias: Tensor | None, dtype: torch.dtype):  # type: ignore[override]
+        w = weight.to(dtype)
+        b = None if bias is None else bias.to(dtype)
+        out = torch.empty(x2d.shape[0], w.shape[0], dtype=dtype, device=x2d.device)
+        gemm_ex(x2d, w, False, out, bias=b)
+        ctx.save_for_backward(x2d, w)
+        ctx.param_dtypes = (weight.dtype, None if bias is None else bias.dtype)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout: Tensor):  # type: ignore[override]
+        x2d, w = ctx.saved_tensors
+        need = ctx.needs_input_grad
+        dout = dout.to(w.dtype).contiguous()
+        m, k = x2d.shape
+        n = w.shape[0]
+        dx = dw = db = None
+        if need[0]:
+            dx = torch.empty(m, k, dtype=w.dtype, device=x2d.device)
+            gemm_ex(dout, w, True, dx)  # dX = dY . W
+        if need[1]:
+            dw = torch.zeros(n, k, dtype=torch.float32, device=x2d.device)
+            gemm_splitk(dout, dout.stride(0), True, x2d, x2d.stride(0), True, n, k, m, dw)  # dW = dY^T . X
+            dw = dw.to(ctx.param_dtypes[0])
+        if need[2]:
+            db = _bias_grad(dout).to(ctx.param_dtypes[1])
+        return dx, dw, db, None
+
+
+def _linear_dtype(x: Tensor) -> torch.dtype:
+    return torch.get_autocast_dtype("cuda") if torch.is_autocast_enabled("cuda") else x.dtype
+
+
+def linear_supported(x: Tensor, layer: torch.nn.Linear) -> bool:
+    """Whether the tcgen05 GEMM covers ``layer(x)``: CUDA, half-precision compute (autocast, or x and the
+    weight in one half dtype, as F.linear requires), widths multiples of 128 (out) and 8 (in)."""
+    dtype = _linear_dtype(x)
+    return (x.is_cuda and x.numel() > 0 and dtype in _HALF and layer.out_features % 128 == 0
+            and layer.in_features % 8 == 0
+            and (torch.is_autocast_enabled("cuda") or layer.weight.dtype == dtype))
+
+
+def linear(x: Tensor, layer: torch.nn.Linear) -> Tensor:
+    """``layer(x)`` on the tcgen05 GEMM, with F.linear's autocast behaviour (operands and output in the
+    autocast dtype under autocast, else in x's dtype)."""
+    dtype = _linear_dtype(x)
+    x2d = x.reshape(-1, x.shape[-1]).to(dtype)
+    if not x2d.is_contiguous():
+        x2d = x2d.contiguous()
+    out = _Linear.apply(x2d, layer.weight, layer.bias, dtype)
+    return out.view(*x.shape[:-1], out.shape[-1])
+
+
+class _FeedForward(torch.autograd.Function):
+    """Linear -> GELU -> Linear (modules.py:339-346, the block's feed-forward branch) on the tcgen05 GEMM:
+    the first product's epilogue adds its bias, applies GELU and keeps the pre-activation; the backward's
+    first product (dOut . W2) multiplies by GELU'(pre-activation) in its epilogue, so no separate GELU
+    pass runs in either direction."""
+
+    @staticmethod
+    def forward(ctx, x2d: Tensor, w1: Tensor, b1: Tensor | None, w2: Tensor, b2: Tensor | None,  # type: ignore[override]
+                dtype: torch.dtype):
+        m = x2d.shape[0]
+        w1c, w2c = w1.to(dtype), w2.to(dtype)
+        b1c = None if b1 is None else b1.to(dtype)
+        b2c = None if b2 is None else b2.to(dtype)
+        hidden = w1c.shape[0]
+        z = torch.empty(m, hidden, dtype=dtype, device=x2d.device)
+        h = torch.empty(m, hidden, dtype=dtype, device=x2d.device)
+        gemm_ex(x2d, w1c, False, h, bias=b1c, act=1, aux=z)  # h = GELU(x W1^T + b1), z kept
+        out = torch.empty(m, w2c.shape[0], dtype=dtype, device=x2d.device)
+        gemm_ex(h, w2c, False, out, bias=b2c)
+        ctx.save_for_backward(x2d, w1c, w2c, z, h)
+        ctx.param_dtypes = (w1.dtype, None if b1 is None else b1.dtype, w2.dtype, None if b2 is None else b2.dtype)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout: Tensor):  # type: ignore[override]
+        x2d, w1c, w2c, z, h = ctx.saved_tensors
+        need = ctx.needs_input_grad
+        dt = w1c.dtype
+        dout = dout.to(dt).contiguous()
+        m, k = x2d.shape
+        hidden, n = w1c.shape[0], w2c.shape[0]
+        pd = ctx.param_dtypes
+        dx = dw1 = db1 = dw2 = db2 = None
+        if need[3]:
+            dw2 = torch.zeros(n, hidden, dtype=torch.float32, device=x2d.device)
+            gemm_splitk(dout, dout.stride(0), True, h, h.stride(0), True, n, hidden, m, dw2)  # dW2 = dOut^T . h
+            dw2 = dw2.to(pd[2])
+        if need[4]:
+            db2 = _bias_grad(dout).to(pd[3])
+        dz = torch.empty(m, hidden, dtype=dt, device=x2d.device)
+        gemm_ex(dout, w2c, True, dz, act=2, aux=z)  # dZ = (dOut . W2) * GELU'(z)
+        if need[1]:
+            dw1 = torch.zeros(hidden, k, dtype=torch.float32, device=x2d.device)
+            gemm_splitk(dz, dz.stride(0), True, x2d, x2d.stride(0), True, hidden, k, m, dw1)  # dW1 = dZ^T . x
+            dw1 = dw1.to(pd[0])
+        if need[2]:
+            db1 = _bias_grad(dz).to(pd[1])
+        if need[0]:
+            dx = torch.empty(m, k, dtype=dt, device=x2d.device)
+            gemm_ex(dz, w1c, True, dx)  # dX = dZ . W1
+        return dx, dw1, db1, dw2, db2, None
+
+
+def feedforward_supported(x: Tensor, first: torch.nn.Linear, second: torch.nn.Linear) -> bool:
+    return linear_supported(x, first) and linear_supported(x, second) and first.out_features == second.in_features
+
+
+def feedforward(x: Tensor, first: torch.nn.Linear, second: torch.nn.Linear) -> Tensor:
+    """``second(GELU(first(x)))`` (F.linear autocast behaviour) on the tcgen05 GEMM with fused GELU."""
+    dtype = _linear_dtype(x)
+    x2d = x.reshape(-1, x.shape[-1]).to(dtype)
+    if not x2d.is_contiguous():
+        x2d = x2d.contiguous()
+    out = _FeedForward.apply(x2d, first.weight, first.bias, second.weight, second.bias, dtype)
+    return out.view(*x.shape[:-1], out.shape[-1])
+
+
 class _Projection(torch.autograd.Function):
     """[B*T, N] = x [B*T, K] . W[N, K]^T  (the fused Q/K projection)."""
 
@@ -1086,25 +1234,32 @@ class _QKVProjection(torch.autograd.Function):
         hr = wq.shape[0]
         dt = x2d.dtype
         dx = dwq = dwk = dwv = dbv = None
+        dv = None if dvalue is None else dvalue.to(dt).contiguous()
         if dproj is not None:
             dproj = dproj.to(dt).contiguous()
-            if need[0]:
-                dx = torch.empty(m, k, dtype=dt, device=x2d.device)
-                gemm(dproj, False, torch.cat((wq, wk), 0), True, m, k, 2 * hr, dx)   # dX = dC . [Wq; Wk]
-            if need[1] or need[2]:
-                # dW = dC^T . X (fp32): a [2HR, K] output of a few tiles over all B*T rows, so the row
-                # dimension is split over CTAs (partial sums added in fp32)
-                dw = torch.zeros(2 * hr, k, dtype=torch.float32, device=x2d.device)
-                gemm_splitk(dproj, dproj.stride(0), True, x2d, x2d.stride(0), True, 2 * hr, k, m, dw)
-                dwq, dwk = dw[:hr].to(wq.dtype), dw[hr:].to(wk.dtype)
-        if dvalue is not None:
-            dv = dvalue.to(dt)
-            if need[0]:
-                dx = dv @ wv if dx is None else dx.addmm_(dv, wv)
-            if need[3]:
-                dwv = (dv.t() @ x2d).to(wv.dtype)
+        if need[0]:  # dX = dC . [Wq; Wk] + dV . Wv in one launch (two K segments)
+            dx = torch.empty(m, k, dtype=dt, device=x2d.device)
+            if dproj is not None and dv is not None:
+                gemm_ex(dproj, torch.cat((wq, wk), 0), True, dx, a2=dv, b2=wv)
+            elif dproj is not None:
+                gemm_ex(dproj, torch.cat((wq, wk), 0), True, dx)
+            elif dv is not None:
+                gemm_ex(dv, wv, True, dx)
+            else:
+                dx = None
+        if dproj is not None and (need[1] or need[2]):
+            # dW = dC^T . X (fp32): a [2HR, K] output of a few tiles over all B*T rows, so the row
+            # dimension is split over CTAs (partial sums added in a fixed order)
+            dw = torch.zeros(2 * hr, k, dtype=torch.float32, device=x2d.device)
+            gemm_splitk(dproj, dproj.stride(0), True, x2d, x2d.stride(0), True, 2 * hr, k, m, dw)
+            dwq, dwk = dw[:hr].to(wq.dtype), dw[hr:].to(wk.dtype)
+        if dv is not None:
+            if need[3]:  # dWv = dV^T . X, rows split over CTAs as above
+                dwv32 = torch.zeros(wv.shape[0], k, dtype=torch.float32, device=x2d.device)
+                gemm_splitk(dv, dv.stride(0), True, x2d, x2d.stride(0), True, wv.shape[0], k, m, dwv32)
+                dwv = dwv32.to(wv.dtype)
             if ctx.has_bias and need[4]:
-                dbv = dvalue.float().sum(0).to(wv.dtype)
+                dbv = _bias_grad(dvalue).to(wv.dtype)
         return dx, dwq, dwk, dwv, dbv
 
 

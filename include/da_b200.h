@@ -311,6 +311,24 @@ DA_API int da_gemm(const void* A, int64_t lda, int a_mn_major, const void* B, in
                    int64_t ldc, int64_t M, int64_t N, int64_t K, int dtype, int out_f32, int accumulate, int* status,
                    void* stream);
 
+/* The GEMM with an epilogue and an optional second K segment, for the
+ * Linear layers around the routed attention (no reference counterpart of its
+ * own: it replaces the cuBLAS calls and the eager GELU of the value-projection
+ * backward, the output projection (modules.py:272) and the feed-forward
+ * branch (modules.py:339-346)):
+ *   C[M, N] = act(sum_k A(m, k) B(n, k) [+ sum_k A2(m, k) B2(n, k)] + bias[n])
+ * in the operand dtype (fp32 accumulation).  A [M, K] row-major (K-major);
+ * B [N, K] (b_mn_major = 0) or [K, N] (= 1); A2 [M, K2] / B2 likewise (both
+ * null for one segment; with two, K is a multiple of 64).  bias [N] in the
+ * operand dtype or null.  act 0: none; 1: GELU (erf form), with the
+ * pre-activation also stored in aux [M, N] (row stride ldaux) when aux is
+ * not null; 2: times GELU'(aux[m, n]) (the backward of act 1 through the
+ * next product).  N a multiple of 128; strides multiples of 8 elements. */
+DA_API int da_gemm_ex(const void* A, int64_t lda, const void* B, int64_t ldb, int b_mn_major, int64_t K,
+                      const void* A2, int64_t lda2, const void* B2, int64_t ldb2, int64_t K2, void* C, int64_t ldc,
+                      int64_t M, int64_t N, int dtype, const void* bias, int act, void* aux, int64_t ldaux,
+                      int* status, void* stream);
+
 /* Several projections of one input in one launch: C_s = A . B_s^T (+ bias_s)
  * for nseg <= 3 weight matrices B_s [N_s, K] (row stride ldb[s]) sharing A
  * [M, K] (row stride lda); C_s [M, N_s] with row stride ldc[s] in out_dtype[s]
