@@ -157,8 +157,9 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
   const uint32_t rank = cluster_ctarank() & 1u;
   const int tiles = (p.T + kTile - 1) / kTile;
   const int pair = blockIdx.x / 2;
-  const int b = pair / tiles;
-  const int t0 = (tiles - 1 - pair % tiles) * kTile;
+  // longest pairs first across every sequence (the latest query tiles see the most keys)
+  const int b = pair % p.B;
+  const int t0 = (tiles - 1 - pair / p.B) * kTile;
   const int nj = p.causal ? t0 / kTile + 1 : tiles;
   const int maps = p.maps;
   const int sweeps = p.delta_given ? 1 : 2;
@@ -660,8 +661,9 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
   const uint32_t rank = cluster_ctarank() & 1u;
   const int tiles = (p.T + kTile - 1) / kTile;
   const int pair = blockIdx.x / 2;
-  const int b = pair / tiles;
-  const int k0 = (pair % tiles) * kTile;     // first key of this pair (early keys have the most queries)
+  // longest pairs first across every sequence (early keys have the most queries)
+  const int b = pair % p.B;
+  const int k0 = (pair / p.B) * kTile;       // first key of this pair
   const int i0 = p.causal ? k0 / kTile : 0;  // first query tile
   const int ni = tiles - i0;
   const int maps = p.maps;

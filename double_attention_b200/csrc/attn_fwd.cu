@@ -176,8 +176,10 @@ __global__ void __launch_bounds__(fwd_threads<kLat>(), 1) attn_fwd_kernel(const 
   const int dslice = (blockIdx.x / 2) % p.dsplit;  // the slices of one query tile run side by side
   const int dcol0 = dslice * p.Dp;
   const int pair = blockIdx.x / (2 * p.dsplit);
-  const int b = pair / tiles;
-  const int t0 = (tiles - 1 - pair % tiles) * 128;  // heaviest (latest) query tiles first
+  // heaviest (latest) query tiles of every sequence first, then the next heaviest: causal work per pair
+  // varies with the tile, and this order (longest first across the whole grid) keeps the last wave short
+  const int b = pair % p.B;
+  const int t0 = (tiles - 1 - pair / p.B) * 128;
   const int nk = L.nk;
   const int nk_all = (p.T + nk - 1) / nk;
   const int nj = p.causal ? min(nk_all, (t0 + 127) / nk + 1) : nk_all;
