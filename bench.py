@@ -335,13 +335,13 @@ def capture(fn, device, stream):
         return None
 
 
-def kernel_rooflines(cfg, config: int, device):
-    """Live per-launch duration and algorithmic FLOPs of the main kernels at this workload's shapes."""
+def kernel_rooflines(cfg, config: int, device, batch: int):
+    """Live per-launch duration and algorithmic FLOPs of the main kernels at the shapes one rank runs."""
     from double_attention_b200 import kernel_bench
 
     out = {}
     for name in ROOFLINE_KERNELS[cfg["mode"]]:
-        run, flops = kernel_bench.make_case(name, config, device)
+        run, flops = kernel_bench.make_case(name, config, device, batch=batch)
         ms = kernel_bench.time_kernel(run, 20, device, graph=name in kernel_bench.GRAPH_CASES)
         out[name] = (ms, flops)
         del run
@@ -594,7 +594,7 @@ def run_b200(args, cfg, world, rank, local):
     if rank == 0:
         del work, step, graph
         torch.cuda.empty_cache()
-        kernels = kernel_rooflines(cfg, args.config, device)
+        kernels = kernel_rooflines(cfg, args.config, device, per_rank_batch(cfg, world))
         top = max(kernels, key=lambda k: kernels[k][0])
         peak_tf, _hbm, peak_kind = load_peaks()
         ms_top, flops_top = kernels[top]

@@ -33,19 +33,24 @@ namespace da {
 namespace attn {
 namespace bwdm {
 
-// warp 0: TMA producer of the resident rows and the score / accumulation operands; warp 1: their
-// MMA issuer; warps 2-5 and 8-11: softmax, two warpgroups each taking 32 of a thread's 64 columns
-// (the per-element arithmetic of dS and P, with one warp per SM sub-partition, paced the kernels);
-// warp 6: TMA producer of the dP operands (V and dY); warp 7: the dP issuer.  dP runs as its own
-// stream so the other products never wait behind it.
-constexpr int kThreads = 384;
+// warps 0 and 12: TMA producers of the resident rows and the score / accumulation operands (even and
+// odd ring stages); warp 1: their MMA issuer; warps 2-5 and 8-11: softmax, two warpgroups each taking
+// 32 of a thread's 64 columns (the per-element arithmetic of dS and P, with one warp per SM
+// sub-partition, paced the kernels); warps 6 and 13: TMA producers of the dP operands (V and dY);
+// warp 7: the dP issuer.  dP runs as its own stream so the other products never wait behind it.  A
+// producer warp completes about one paired stage per microsecond whatever the stage holds, so each
+// ring has two.
+constexpr int kThreads = 448;
 constexpr int kDpWarp = 6;
-constexpr int kProducers = 1;  // producer warps per ring (stage filters below take stage % kProducers)
-constexpr int kSoftmax2 = 8;   // first warp of the second softmax warpgroup
+constexpr int kAccProducer = 12;  // TMA producer of the accumulation ring
+constexpr int kAccIssuer = 13;    // issuer of the accumulating products (dQ, dK or dV)
+constexpr int kSoftmax2 = 8;      // first warp of the second softmax warpgroup
 constexpr int kRows = 64;      // rows (queries or keys) per CTA
 constexpr int kTile = 128;     // columns (keys or queries) per tile and pair
 constexpr int kStage = 16384;  // main ring stage bytes
-constexpr int kDpStage = 32768;  // dP ring stage: two 64-column blocks of each of V and dY
+constexpr int kDpBlocks = 1;    // 64-column blocks of each of V and dY per dP ring stage
+constexpr int kDpStage = 2 * kDpBlocks * kRows * 128;
+constexpr int kDpStages = 3;
 constexpr int kMaxStages = 8;
 constexpr int kBox = kRows * 128;  // one 64-row x 128-byte swizzled box
 
@@ -77,7 +82,7 @@ DA_DEV int64_t row_of(int64_t base, int64_t sb, int64_t sbr, int b, int branch, 
 struct Layout {
   int kw, W, rpb, ncol, nins;
   int acc_merge;  // the accumulation operand (dQ: K, dK: Q rows, MN-major) comes as one 128-row box per stage
-  int off_a, off_b, off_t, off_red, off_ring, nst, off_pring, nsp, smem;
+  int off_a, off_b, off_t, off_red, off_ring, nst, off_qring, nsq, off_pring, nsp, smem;
   int tmem_acc, tmem_s, tmem_p, tmem_cols;
   int nsb;  // score (TMEM) buffers
 };
@@ -98,15 +103,29 @@ __host__ __device__ inline Layout make_layout(int kind, int maps, int group, int
   L.off_b = L.off_a + kRows * L.W * 2;
   const int b_bytes = 0;
   L.off_t = L.off_b + b_bytes;                 // two dS / P tiles
-  L.off_red = L.off_t + 2 * kRows * kTile * 2;
-  L.off_ring = L.off_red + 8192;
+  // The dQ kernel's row reductions (delta at the end of the first sweep, d gamma after the last product)
+  // borrow the dS tiles' space, idle at both points; the key-parallel kernels stage each query tile's
+  // log-sum-exp and delta in a buffer of their own.
+  L.off_red = kind == 0 ? L.off_t : L.off_t + 2 * kRows * kTile * 2;
+  L.off_ring = kind == 0 ? L.off_t + 2 * kRows * kTile * 2 : L.off_red + 8192;
   const int avail = 225 * 1024 - L.off_ring;
-  // One warp's TMA stages complete one after another at a nearly size-independent cost, so the dP
-  // operands come as 32 KB stages (two 64-column blocks of V and of dY, one box each).
-  L.nsp = kind == 2 ? 0 : 2;
-  const int rest = (avail - L.nsp * kDpStage) / kStage;
-  L.nst = rest > kMaxStages ? kMaxStages : rest;
-  L.off_pring = L.off_ring + L.nst * kStage;
+  // Stage depth over stage size: the score / accumulation ring holds a stage for the dS product of the
+  // unit in the softmax while the next units' score operands load, so with three stages a score operand
+  // waited on the product two units back and the load latency surfaced in every unit.  The dP operands
+  // therefore come as three 16 KB stages (one 64-column block of each of V and dY), leaving four or
+  // more ring stages.
+  L.nsp = kind == 2 ? 0 : (kind == 1 ? kDpStages - 1 : kDpStages);
+  int rest = (avail - L.nsp * kDpStage) / kStage;
+  if (rest > 2 * kMaxStages) rest = 2 * kMaxStages;
+  // Two rings, each with its own producer and issuer: the score operands (run ahead as far as the two
+  // score buffers allow) and the accumulation operands (held until the softmax hands over the unit's dS
+  // or P tile).  The dV kernel's accumulation items are the four dY stages of a query tile.
+  L.nsq = kind == 2 ? (rest - 3 < 4 ? rest - 3 : 4) : 2;
+  if (L.nsq > kMaxStages) L.nsq = kMaxStages;
+  L.nst = rest - L.nsq;
+  if (L.nst > kMaxStages) L.nst = kMaxStages;
+  L.off_qring = L.off_ring + L.nst * kStage;
+  L.off_pring = L.off_qring + L.nsq * kStage;
   L.smem = L.off_pring + L.nsp * kDpStage;
   L.tmem_acc = 0;
   const int acc = kind == 2 ? D / 2 : L.W / 2;
@@ -145,7 +164,8 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
                                                                const Params p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ uint64_t in_full, o_full, r_full[kMaxStages], r_empty[kMaxStages];
+  __shared__ uint64_t in_full, o_full, s_done, r_full[kMaxStages], r_empty[kMaxStages];
+  __shared__ uint64_t q_full[kMaxStages], q_empty[kMaxStages];
   __shared__ uint64_t rp_full[kMaxStages], rp_empty[kMaxStages], dp_done;
   __shared__ uint64_t s_full[2], s_free[2], p_full[2], dp_full[2], dp_free[2], ds_empty[2];
   __shared__ uint32_t tmem_base;
@@ -169,16 +189,20 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
   const MapRows qm{p.q_rows, p.q_base, p.q_sb, p.q_sbr}, km{p.k_rows, p.k_base, p.k_sb, p.k_sbr};
   const int64_t rowsBT = (int64_t)p.B * p.T;
   Abort ab{&abort_flag, p.status};
-  // post-mortem per-unit timeline of the first pair (debug trace only)
-  int* ft = (p.trace && blockIdx.x < 2) ? p.trace + blockIdx.x * 4096 : nullptr;
+  // post-mortem per-unit timeline of the first pair (debug trace only): per CTA 16384 words, dP issuer
+  // at 4g, MMA issuer at 1024 + 8u, softmax at 5120 + 4u, ring producers at 7168 + 4096 ring + 2 item
+  int* ft = (p.trace && blockIdx.x < 2) ? p.trace + blockIdx.x * 16384 : nullptr;
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
     mbar_init(&in_full, 1);
     mbar_init(&o_full, 1);
+    mbar_init(&s_done, 1);
     for (int i = 0; i < kMaxStages; ++i) {
       mbar_init(&r_full[i], 1);
       mbar_init(&r_empty[i], 1);
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
       mbar_init(&rp_full[i], 1);
       mbar_init(&rp_empty[i], 1);
     }
@@ -213,12 +237,14 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
   const int tq_row = t0 + 64 * (int)rank;
   const int dy_row = (int)min((int64_t)b * p.T + tq_row, rowsBT - 1);
   const int dps = sweeps * nj;  // dP products: one per key tile and sweep
-  if (warp == 0 && lane == 0) {
-    // ---------------------------------------------------------------- TMA producers: Q (warp 0), then K
-    // for S and dQ, even stages from warp 0 and odd ones from warp 8
-    const int pi = 0;
+  if ((warp == 0 || warp == kAccProducer) && lane == 0) {
+    // ---------------------------------------------------------------- TMA producers: warp 0 loads the
+    // resident Q rows, then the score operands (K rows of this CTA's 64 keys, per map) into the score
+    // ring; warp 12 loads the dQ operands (K rows of all 128 keys, MN-major) into the accumulation ring
+    const int acc = warp == kAccProducer ? 1 : 0;
     prefetch_tmap(&tk);
-    if (pi == 0) {
+    prefetch_tmap(&tacc);
+    if (!acc) {
       prefetch_tmap(&tq);
       const uint32_t inf = mapa_shared(smem_u32(&in_full), 0);
       if (rank == 0) mbar_arrive_expect_tx(&in_full, 2 * (kRows * L.W * 2));
@@ -226,19 +252,24 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
         for (int cc = 0; cc < L.kw / 128; ++cc)
           load_map_chunk(&tq, qm, p, inf, smem + L.off_a + (s * (L.kw / 64) + cc * 2) * kBox, b, s, cc, 2, tq_row);
     }
+    const int nst = acc ? L.nsq : L.nst;
+    uint64_t* fullb = acc ? q_full : r_full;
+    uint64_t* emptyb = acc ? q_empty : r_empty;
+    uint8_t* ring = smem + (acc ? L.off_qring : L.off_ring);
     int it = 0;
     bool ok = true;
     auto stage = [&](int bytes) -> uint8_t* {
-      const int st = it % L.nst;
-      if (!mbar_wait(&r_empty[st], ((it / L.nst) & 1u) ^ 1u, ab, 11)) { ok = false; return nullptr; }
-      if (rank == 0) mbar_arrive_expect_tx(&r_full[st], 2 * bytes);
-      return smem + L.off_ring + st * kStage;
+      const int st = it % nst;
+      if (it < 2048) trace_at(ft, 7168 + 4096 * acc + 2 * it);
+      if (!mbar_wait(&emptyb[st], ((it / nst) & 1u) ^ 1u, ab, 11 + acc)) { ok = false; return nullptr; }
+      if (it < 2048) trace_at(ft, 7169 + 4096 * acc + 2 * it);
+      if (rank == 0) mbar_arrive_expect_tx(&fullb[st], 2 * bytes);
+      return ring + st * kStage;
     };
-    auto stage_bar = [&]() { return mapa_shared(smem_u32(&r_full[it % L.nst]), 0); };
+    auto stage_bar = [&]() { return mapa_shared(smem_u32(&fullb[it % nst]), 0); };
     auto emit_s = [&](int u) {  // key rows of map s for this CTA's 64 keys
       const int krow0 = unit_j(u) * kTile + 64 * (int)rank;
       for (int cc = 0; ok && cc < L.kw / 128; ++cc, ++it) {
-        if ((it % kProducers) != pi) continue;
         uint8_t* dst = stage(2 * kBox);
         if (!ok) return;
         load_map_chunk(&tk, km, p, stage_bar(), dst, b, unit_s(u), cc, 2, krow0);
@@ -248,7 +279,6 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
       const int per = (L.ncol / 2) / 64, s = unit_s(u), j = unit_j(u);
       if (L.acc_merge) {  // one stage per N block: a 128-key x 64-column box
         for (int ins = 0; ok && ins < L.nins; ++ins, ++it) {
-          if ((it % kProducers) != pi) continue;
           uint8_t* dst = stage(2 * kBox);
           if (!ok) return;
           const int mb = (ins * L.ncol + (int)rank * (L.ncol / 2)) / 64;
@@ -260,7 +290,6 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
       }
       for (int kc = 0; ok && kc < kTile / 64; ++kc)
         for (int ins = 0; ok && ins < L.nins; ++ins, ++it) {
-          if ((it % kProducers) != pi) continue;
           uint8_t* dst = stage(per * kBox);
           if (!ok) return;
           const uint32_t bar = stage_bar();
@@ -272,40 +301,34 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
           }
         }
     };
-    emit_s(0);
-    for (int u = 0; ok && u < U; ++u) {  // same order as the S / dQ issuer
-      if (u + 1 < U) emit_s(u + 1);
-      if (u >= u_dq) emit_dq(u);
-    }
+    if (!acc)
+      for (int u = 0; ok && u < U; ++u) emit_s(u);  // same order as the score issuer
+    else
+      for (int u = u_dq; ok && u < U; ++u) emit_dq(u);  // same order as the dQ issuer
     if (rank == 0) {  // drain: none of this producer's loads may be in flight at teardown
-      if (pi == 0) mbar_wait_drain(&in_full, 0);
-      for (int i = (it > L.nst ? it - L.nst : 0); i < it; ++i)
-        if ((i % kProducers) == pi) mbar_wait_drain(&r_full[i % L.nst], (i / L.nst) & 1u);
+      if (!acc) mbar_wait_drain(&in_full, 0);
+      for (int i = (it > nst ? it - nst : 0); i < it; ++i) mbar_wait_drain(&fullb[i % nst], (i / nst) & 1u);
     }
   } else if (warp == kDpWarp && lane == 0) {
-    // ---------------------------------------------------------------- TMA producers: V and dY for dP
-    // (even stages from warp 6, odd ones from warp 9)
-    const int pi = 0;
+    // ---------------------------------------------------------------- TMA producer: V and dY for dP
     prefetch_tmap(&tv);
     prefetch_tmap(&tdy);
     int it = 0;
     bool ok = true;
     for (int g = 0; ok && g < dps; ++g) {
       const int y = (int)min((int64_t)b * p.T + (g % nj) * kTile + 64 * (int)rank, rowsBT - 1);
-      for (int cc = 0; cc < p.D / 128; ++cc, ++it) {  // per 128 value columns: V rows of 64 keys, dY rows
-        if ((it % kProducers) != pi) continue;
+      for (int cb = 0; cb < p.D / (64 * kDpBlocks); ++cb, ++it) {  // V rows of 64 keys, then dY rows
         const int st = it % L.nsp;
         if (!mbar_wait(&rp_empty[st], ((it / L.nsp) & 1u) ^ 1u, ab, 13)) { ok = false; break; }
         if (rank == 0) mbar_arrive_expect_tx(&rp_full[st], 2 * kDpStage);
         const uint32_t bar = mapa_shared(smem_u32(&rp_full[st]), 0);
         uint8_t* dst = smem + L.off_pring + st * kDpStage;
-        tma_load_3d_pair(&tv, bar, dst, 0, y, cc * 2);
-        tma_load_3d_pair(&tdy, bar, dst + 2 * kBox, 0, dy_row, cc * 2);
+        tma_load_3d_pair(&tv, bar, dst, 0, y, cb * kDpBlocks);
+        tma_load_3d_pair(&tdy, bar, dst + kDpBlocks * kBox, 0, dy_row, cb * kDpBlocks);
       }
     }
     if (rank == 0)
-      for (int i = (it > L.nsp ? it - L.nsp : 0); i < it; ++i)
-        if ((i % kProducers) == pi) mbar_wait_drain(&rp_full[i % L.nsp], (i / L.nsp) & 1u);
+      for (int i = (it > L.nsp ? it - L.nsp : 0); i < it; ++i) mbar_wait_drain(&rp_full[i % L.nsp], (i / L.nsp) & 1u);
   } else if (warp == kDpWarp + 1 && lane == 0 && rank == 0) {
     // ---------------------------------------------------------------- dP issuer (leader): dP = dY V^T
     // Its own thread, so the score and dQ products never wait behind the value stream.
@@ -314,54 +337,59 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
     bool ok = true;
     for (int g = 0; ok && g < dps; ++g) {
       const int db = g & 1;
-      if (g < 200) trace_at(ft, 1024 + 4 * g);
+      if (g < 256) trace_at(ft, 4 * g);
       if (g >= 2 && !mbar_wait(&dp_free[db], ((g - 2) >> 1) & 1u, ab, 27)) break;
-      for (int cc = 0; cc < p.D / 128; ++cc, ++it) {  // stage: [V 2 blocks | dY 2 blocks] of 128 columns
+      if (g < 256) trace_at(ft, 4 * g + 1);
+      for (int cb = 0; cb < p.D / (64 * kDpBlocks); ++cb, ++it) {  // stage: [V blocks | dY blocks]
         const int st = it % L.nsp;
         if (!mbar_wait(&rp_full[st], (it / L.nsp) & 1u, ab, 28)) { ok = false; break; }
         tc_fence_after();
         const uint32_t sa = smem_u32(smem + L.off_pring + st * kDpStage);
-        for (int k = 0; k < 8; ++k) {
+        for (int k = 0; k < 4 * kDpBlocks; ++k) {
           const uint32_t blk = (uint32_t)(k >> 2) * kBox + (k & 3) * 32;
-          const uint64_t ad = sdesc_sw128(sa + 2 * kBox + blk, 16, 1024);
+          const uint64_t ad = sdesc_sw128(sa + kDpBlocks * kBox + blk, 16, 1024);
           const uint64_t bd = sdesc_sw128(sa + blk, 16, 1024);
-          mma_f16_ss<2>(tmem + L.tmem_p + db * (kTile / 2), ad, bd, idesc, (cc | k) ? 1u : 0u);
+          mma_f16_ss<2>(tmem + L.tmem_p + db * (kTile / 2), ad, bd, idesc, (cb | k) ? 1u : 0u);
         }
-        mma_commit<2>(smem_u32(&rp_empty[st]));
-        mma_commit<2>(mapa_shared(smem_u32(&rp_empty[st]), 1));
+        mma_commit_pair(smem_u32(&rp_empty[st]));
       }
       if (!ok) break;
-      mma_commit<2>(smem_u32(&dp_full[db]));
-      mma_commit<2>(mapa_shared(smem_u32(&dp_full[db]), 1));
-      if (g < 200) trace_at(ft, 1025 + 4 * g);
+      mma_commit_pair(smem_u32(&dp_full[db]));
+      if (g < 256) trace_at(ft, 4 * g + 2);
     }
     mma_commit<2>(smem_u32(&dp_done));  // every dP product has completed before teardown
     mbar_wait_drain(&dp_done, 0);
-  } else if (warp == 1 && lane == 0 && rank == 0) {
-    // ---------------------------------------------------------------- MMA issuer (leader)
+  } else if ((warp == 1 || warp == kAccIssuer) && lane == 0 && rank == 0) {
+    // ---------------------------------------------------------------- MMA issuers (leader): warp 1 the
+    // score products S_s = Q_s K_s^T, warp 13 the dQ products; each consumes its own ring, so a score
+    // product never waits behind the hand-over of a dS tile
+    const int acc = warp == kAccIssuer ? 1 : 0;
     const uint32_t idesc_s = idesc_f16(128, kTile, kBf16, false, false);
     const uint32_t idesc_q = idesc_f16(128, L.ncol, kBf16, false, true);  // B = K rows, MN-major
-    auto commit_both = [&](uint64_t* bar) {
-      mma_commit<2>(smem_u32(bar));
-      mma_commit<2>(mapa_shared(smem_u32(bar), 1));
-    };
+    auto commit_both = [&](uint64_t* bar) { mma_commit_pair(smem_u32(bar)); };
+    const int nst = acc ? L.nsq : L.nst;
+    uint64_t* fullb = acc ? q_full : r_full;
+    uint64_t* emptyb = acc ? q_empty : r_empty;
+    uint8_t* ring = smem + (acc ? L.off_qring : L.off_ring);
     int it = 0;
     auto take = [&](uint32_t* addr) -> bool {
-      const int st = it % L.nst;
-      if (!mbar_wait(&r_full[st], (it / L.nst) & 1u, ab, 23)) return false;
+      const int st = it % nst;
+      if (!mbar_wait(&fullb[st], (it / nst) & 1u, ab, 23)) return false;
       tc_fence_after();
-      *addr = smem_u32(smem + L.off_ring + st * kStage);
+      *addr = smem_u32(ring + st * kStage);
       return true;
     };
-    auto give = [&]() { commit_both(&r_empty[it % L.nst]); ++it; };
+    auto give = [&]() { commit_both(&emptyb[it % nst]); ++it; };
     const uint32_t qa = smem_u32(smem + L.off_a);
     auto issue_s = [&](int u) -> bool {
       const int sb = u & 1, s = unit_s(u);
-      if (u < 300) trace_at(ft, 2048 + 4 * u);
+      if (u < 512) trace_at(ft, 1024 + 8 * u);
       if (u >= 2 && !mbar_wait(&s_free[sb], ((u - 2) >> 1) & 1u, ab, 22)) return false;
+      if (u < 512) trace_at(ft, 1025 + 8 * u);
       for (int cc = 0; cc < L.kw / 128; ++cc) {
         uint32_t st;
         if (!take(&st)) return false;
+        if (u < 512 && cc == 0) trace_at(ft, 1026 + 8 * u);
         for (int k = 0; k < 8; ++k) {
           const uint64_t ad =
               sdesc_sw128(qa + (s * (L.kw / 64) + cc * 2 + (k >> 2)) * kBox + (k & 3) * 32, 16, 1024);
@@ -371,20 +399,21 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
         give();
       }
       commit_both(&s_full[sb]);
-      if (u < 300) trace_at(ft, 2049 + 4 * u);
+      if (u < 512) trace_at(ft, 1027 + 8 * u);
       return true;
     };
     auto issue_dq = [&](int u) -> bool {
       const int v = u - u_dq, s = unit_s(u), j = unit_j(u);
-      if (u < 300) trace_at(ft, 2050 + 4 * u);
-      if (!mbar_wait(&p_full[u & 1], (u >> 1) & 1u, ab, 24)) return false;
-      if (u < 300) trace_at(ft, 2051 + 4 * u);
+      if (u < 512) trace_at(ft, 1028 + 8 * u);
+      if (!mbar_wait(&p_full[v & 1], (v >> 1) & 1u, ab, 24)) return false;
+      if (u < 512) trace_at(ft, 1029 + 8 * u);
       tc_fence_after();
       const uint32_t dsa = smem_u32(smem + L.off_t + (v & 1) * (kRows * kTile * 2));
       if (L.acc_merge) {  // stage = 128 keys x 64 columns: both 64-key chunks
         for (int ins = 0; ins < L.nins; ++ins) {
           uint32_t st;
           if (!take(&st)) return false;
+          if (u < 512 && ins == 0) trace_at(ft, 1030 + 8 * u);
           for (int k = 0; k < 8; ++k) {
             const int kc = k >> 2, kk = k & 3;
             const uint64_t ad = sdesc_sw128(dsa + kc * kBox + kk * 32, 16, 1024);
@@ -409,18 +438,22 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
           }
       }
       commit_both(&ds_empty[v & 1]);
+      if (u < 512) trace_at(ft, 1031 + 8 * u);
       return true;
     };
-    bool ok = mbar_wait(&in_full, 0, ab, 21);
-    tc_fence_after();
-    if (ok) ok = issue_s(0);
-    for (int u = 0; ok && u < U; ++u) {
-      if (u + 1 < U) ok = issue_s(u + 1);
-      if (ok && u >= u_dq) ok = issue_dq(u);
+    if (!acc) {
+      bool ok = mbar_wait(&in_full, 0, ab, 21);
+      tc_fence_after();
+      for (int u = 0; ok && u < U; ++u) ok = issue_s(u);
+      mma_commit<2>(smem_u32(&s_done));  // every score product has completed before teardown
+      mbar_wait_drain(&s_done, 0);
+    } else {
+      bool ok = true;
+      for (int u = u_dq; ok && u < U; ++u) ok = issue_dq(u);
+      commit_both(&o_full);
+      mbar_wait_drain(&o_full, 0);
     }
-    commit_both(&o_full);
-    mbar_wait_drain(&o_full, 0);
-  } else if ((warp >= 2 && warp < 6) || warp >= kSoftmax2) {
+  } else if ((warp >= 2 && warp < 6) || (warp >= kSoftmax2 && warp < kSoftmax2 + 4)) {
     // ---------------------------------------------------------------- softmax + epilogue: two warpgroups,
     // warps 2-5 take the first 32 of each thread's 64 key columns and warps 8-11 the other 32
     const int wg = warp >= kSoftmax2 ? 1 : 0;
@@ -457,11 +490,11 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
       const int sb = u & 1, s = unit_s(u), j = unit_j(u), g = unit_g(u);
       const bool form_ds = u >= u_dq;
       const int v = u - u_dq;
-      if (arriver && u < 300) trace_at(ft, 3072 + 4 * u);
+      if (arriver && u < 512) trace_at(ft, 5120 + 4 * u);
       if (ok) ok = mbar_wait(&s_full[sb], (u >> 1) & 1u, ab, 32);
       if (ok && s == 0) ok = mbar_wait(&dp_full[g & 1], (g >> 1) & 1u, ab, 35);
       if (ok && form_ds && v >= 2) ok = mbar_wait(&ds_empty[v & 1], ((v - 2) >> 1) & 1u, ab, 33);
-      if (arriver && u < 300) trace_at(ft, 3073 + 4 * u);
+      if (arriver && u < 512) trace_at(ft, 5121 + 4 * u);
       ok = __all_sync(0xffffffffu, ok);
       if (ok) {
         tc_fence_after();
@@ -529,14 +562,17 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
           delta[s] += dsum;
         }
       }
-      if (arriver && u < 300) trace_at(ft, 3074 + 4 * u);
+      if (arriver && u < 512) trace_at(ft, 5122 + 4 * u);
       if (!ok && lane == 0) mbar_arrive_cluster_relaxed(sf_leader + sb * 8);  // aborted unit: counts stay whole
       tc_fence_before();
       named_bar_sync(1, 256);
       if (arriver) {
-        if (u < 300) trace_at(ft, 3075 + 4 * u);
-        mbar_arrive_cluster(pf_leader + sb * 8);
-        if (s == maps - 1) mbar_arrive_cluster(df_leader + (g & 1) * 8);
+        if (u < 512) trace_at(ft, 5123 + 4 * u);
+        // dS tile v handed to the dQ issuer (second sweep only: phase v / 2 of barrier v % 2, which the
+        // issuer waits for in order; the softmax cannot run two phases ahead, as unit v + 2 first waits
+        // for the product of unit v)
+        if (form_ds) mbar_arrive_remote(pf_leader + (v & 1) * 8);
+        if (s == maps - 1) mbar_arrive_cluster_relaxed(df_leader + (g & 1) * 8);
       }
       if (!p.delta_given && u == per_sweep - 1) {
         // end of the first sweep: whole-row delta_s (two halves x two warpgroups), stored for the
@@ -561,7 +597,12 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
         }
       }
     }
-    // ---- d gamma_s from each row's own sums (both warpgroups, both halves), then the dQ epilogue
+    // ---- d gamma_s from each row's own sums (both warpgroups, both halves), then the dQ epilogue.  The
+    // reduction buffer shares the dS tiles' space: every product (the last dQ ones read those tiles) has
+    // completed first.
+    if (ok) ok = mbar_wait(&o_full, 0, ab, 34);
+    ok = __all_sync(0xffffffffu, ok);
+    tc_fence_after();
     if (p.dscale) {
       if (wg == 1)
         for (int m = 0; m < maps; ++m) {
@@ -601,9 +642,6 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
         }
       }
     }
-    if (wg == 0 && ok) ok = mbar_wait(&o_full, 0, ab, 34);
-    ok = __all_sync(0xffffffffu, ok);
-    tc_fence_after();
     if (wg == 0 && ok && p.dq) {
       for (int m = 0; m < maps; ++m) {
         const float gamma = p.scales[m] * gsc;
@@ -648,7 +686,8 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
                                                                 const Params p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ uint64_t in_full, o_full, r_full[kMaxStages], r_empty[kMaxStages];
+  __shared__ uint64_t in_full, o_full, s_done, r_full[kMaxStages], r_empty[kMaxStages];
+  __shared__ uint64_t q_full[kMaxStages], q_empty[kMaxStages];
   __shared__ uint64_t rp_full[kMaxStages], rp_empty[kMaxStages], dp_done;
   constexpr int kNSB = kDK ? 2 : 4;  // score buffers (Layout::nsb)
   __shared__ uint64_t s_full[kNSB], s_free[kNSB], p_full[2], dp_full[2], dp_free[2], t_empty[2];
@@ -678,9 +717,12 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
     abort_flag = 0;
     mbar_init(&in_full, 1);
     mbar_init(&o_full, 1);
+    mbar_init(&s_done, 1);
     for (int i = 0; i < kMaxStages; ++i) {
       mbar_init(&r_full[i], 1);
       mbar_init(&r_empty[i], 1);
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
       mbar_init(&rp_full[i], 1);
       mbar_init(&rp_empty[i], 1);
     }
@@ -714,13 +756,16 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
 
   const int krow = k0 + 64 * (int)rank;
   const int vy = (int)min((int64_t)b * p.T + krow, rowsBT - 1);
-  if (warp == 0 && lane == 0) {
-    // ---------------------------------------------------------------- TMA producers: K (warp 0), then Q
-    // (and dY for dV), even stages from warp 0 and odd ones from warp 8
-    const int pi = 0;
+  if ((warp == 0 || warp == kAccProducer) && lane == 0) {
+    // ---------------------------------------------------------------- TMA producers: warp 0 loads the
+    // resident K rows, then the score operands (Q rows of this CTA's 64 queries, per map) into the score
+    // ring; warp 12 loads the operands of the accumulating product (dK: Q rows of all 128 queries,
+    // MN-major; dV: dY rows) into the accumulation ring
+    const int acc = warp == kAccProducer ? 1 : 0;
     prefetch_tmap(&tq);
     prefetch_tmap(&tdy);
-    if (pi == 0) {
+    prefetch_tmap(&tacc);
+    if (!acc) {
       prefetch_tmap(&tk);
       const uint32_t inf = mapa_shared(smem_u32(&in_full), 0);
       if (rank == 0) mbar_arrive_expect_tx(&in_full, 2 * (kRows * L.W * 2));
@@ -728,19 +773,22 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
         for (int cc = 0; cc < L.kw / 128; ++cc)
           load_map_chunk(&tk, km, p, inf, smem + L.off_a + (s * (L.kw / 64) + cc * 2) * kBox, b, s, cc, 2, krow);
     }
+    const int nst = acc ? L.nsq : L.nst;
+    uint64_t* fullb = acc ? q_full : r_full;
+    uint64_t* emptyb = acc ? q_empty : r_empty;
+    uint8_t* ring = smem + (acc ? L.off_qring : L.off_ring);
     int it = 0;
     bool ok = true;
     auto stage = [&](int bytes) -> uint8_t* {
-      const int st = it % L.nst;
-      if (!mbar_wait(&r_empty[st], ((it / L.nst) & 1u) ^ 1u, ab, 11)) { ok = false; return nullptr; }
-      if (rank == 0) mbar_arrive_expect_tx(&r_full[st], 2 * bytes);
-      return smem + L.off_ring + st * kStage;
+      const int st = it % nst;
+      if (!mbar_wait(&emptyb[st], ((it / nst) & 1u) ^ 1u, ab, 11 + acc)) { ok = false; return nullptr; }
+      if (rank == 0) mbar_arrive_expect_tx(&fullb[st], 2 * bytes);
+      return ring + st * kStage;
     };
-    auto stage_bar = [&]() { return mapa_shared(smem_u32(&r_full[it % L.nst]), 0); };
+    auto stage_bar = [&]() { return mapa_shared(smem_u32(&fullb[it % nst]), 0); };
     auto emit_s = [&](int u) {  // query rows of map s for this CTA's 64 queries
       const int q = (i0 + unit_g(u)) * kTile + 64 * (int)rank;
       for (int cc = 0; ok && cc < L.kw / 128; ++cc, ++it) {
-        if ((it % kProducers) != pi) continue;
         uint8_t* dst = stage(2 * kBox);
         if (!ok) return;
         load_map_chunk(&tq, qm, p, stage_bar(), dst, b, unit_s(u), cc, 2, q);
@@ -750,8 +798,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
       const int i = i0 + unit_g(u), s = unit_s(u);
       if (kDK && L.acc_merge) {  // one stage per N block: a 128-query x 64-column box
         for (int ins = 0; ok && ins < L.nins; ++ins, ++it) {
-          if ((it % kProducers) != pi) continue;
-          uint8_t* dst = stage(2 * kBox);
+            uint8_t* dst = stage(2 * kBox);
           if (!ok) return;
           const int mb = (ins * L.ncol + (int)rank * (L.ncol / 2)) / 64;
           const int gi = mb / L.rpb, x = (mb % L.rpb) * 64;
@@ -762,8 +809,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
         const int per = (L.ncol / 2) / 64;
         for (int qc = 0; ok && qc < kTile / 64; ++qc)
           for (int ins = 0; ok && ins < L.nins; ++ins, ++it) {
-            if ((it % kProducers) != pi) continue;
-            uint8_t* dst = stage(per * kBox);
+                uint8_t* dst = stage(per * kBox);
             if (!ok) return;
             const uint32_t bar = stage_bar();
             for (int bx = 0; bx < per; ++bx) {
@@ -778,49 +824,43 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
         for (int qc = 0; ok && qc < kTile / 64; ++qc) {
           const int y = (int)min((int64_t)b * p.T + i * kTile + qc * 64, rowsBT - 1);
           for (int ins = 0; ok && ins < dins; ++ins, ++it) {
-            if ((it % kProducers) != pi) continue;
-            uint8_t* dst = stage(dper * kBox);  // dper = 2 (dn = 256): one box of two column blocks
+                uint8_t* dst = stage(dper * kBox);  // dper = 2 (dn = 256): one box of two column blocks
             if (!ok) return;
             tma_load_3d_pair(&tdy, stage_bar(), dst, 0, y, (ins * dn + (int)rank * (dn / 2)) / 64);
           }
         }
       }
     };
-    // same order as the MMA warp below
-    for (int u = 0; u < kNSB - 1 && u < U; ++u) emit_s(u);  // same order as the MMA issuer
-    for (int u = 0; ok && u < U; ++u) {
-      if (u + kNSB - 1 < U) emit_s(u + kNSB - 1);
-      if (kDK || unit_s(u) == maps - 1) emit_acc(u);
-    }
+    // same orders as the two issuers below
+    if (!acc)
+      for (int u = 0; ok && u < U; ++u) emit_s(u);
+    else
+      for (int u = 0; ok && u < U; ++u)
+        if (kDK || unit_s(u) == maps - 1) emit_acc(u);
     if (rank == 0) {  // drain: none of this producer's loads may be in flight at teardown
-      if (pi == 0) mbar_wait_drain(&in_full, 0);
-      for (int i = (it > L.nst ? it - L.nst : 0); i < it; ++i)
-        if ((i % kProducers) == pi) mbar_wait_drain(&r_full[i % L.nst], (i / L.nst) & 1u);
+      if (!acc) mbar_wait_drain(&in_full, 0);
+      for (int i = (it > nst ? it - nst : 0); i < it; ++i) mbar_wait_drain(&fullb[i % nst], (i / nst) & 1u);
     }
   } else if (kDK && warp == kDpWarp && lane == 0) {
-    // ---------------------------------------------------------------- TMA producers: dY and V for dP^T
-    // (even stages from warp 6, odd ones from warp 9)
-    const int pi = 0;
+    // ---------------------------------------------------------------- TMA producer: dY and V for dP^T
     prefetch_tmap(&tv);
     prefetch_tmap(&tdy);
     int it = 0;
     bool ok = true;
     for (int g = 0; ok && g < ni; ++g) {
       const int y = (int)min((int64_t)b * p.T + (i0 + g) * kTile + 64 * (int)rank, rowsBT - 1);
-      for (int cc = 0; cc < p.D / 128; ++cc, ++it) {  // per 128 value columns: dY rows of 64 queries, V rows
-        if ((it % kProducers) != pi) continue;
+      for (int cb = 0; cb < p.D / (64 * kDpBlocks); ++cb, ++it) {  // dY rows of 64 queries, then V rows
         const int st = it % L.nsp;
         if (!mbar_wait(&rp_empty[st], ((it / L.nsp) & 1u) ^ 1u, ab, 13)) { ok = false; break; }
         if (rank == 0) mbar_arrive_expect_tx(&rp_full[st], 2 * kDpStage);
         const uint32_t bar = mapa_shared(smem_u32(&rp_full[st]), 0);
         uint8_t* dst = smem + L.off_pring + st * kDpStage;
-        tma_load_3d_pair(&tdy, bar, dst, 0, y, cc * 2);
-        tma_load_3d_pair(&tv, bar, dst + 2 * kBox, 0, vy, cc * 2);
+        tma_load_3d_pair(&tdy, bar, dst, 0, y, cb * kDpBlocks);
+        tma_load_3d_pair(&tv, bar, dst + kDpBlocks * kBox, 0, vy, cb * kDpBlocks);
       }
     }
     if (rank == 0)
-      for (int i = (it > L.nsp ? it - L.nsp : 0); i < it; ++i)
-        if ((i % kProducers) == pi) mbar_wait_drain(&rp_full[i % L.nsp], (i / L.nsp) & 1u);
+      for (int i = (it > L.nsp ? it - L.nsp : 0); i < it; ++i) mbar_wait_drain(&rp_full[i % L.nsp], (i / L.nsp) & 1u);
   } else if (kDK && warp == kDpWarp + 1 && lane == 0 && rank == 0) {
     // ---------------------------------------------------------------- dP^T issuer (leader): dP^T = V dY^T
     const uint32_t idesc = idesc_f16(128, kTile, kBf16, false, false);
@@ -829,44 +869,45 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
     for (int g = 0; ok && g < ni; ++g) {
       const int db = g & 1;
       if (g >= 2 && !mbar_wait(&dp_free[db], ((g - 2) >> 1) & 1u, ab, 27)) break;
-      for (int cc = 0; cc < p.D / 128; ++cc, ++it) {  // stage: [dY 2 blocks | V 2 blocks] of 128 columns
+      for (int cb = 0; cb < p.D / (64 * kDpBlocks); ++cb, ++it) {  // stage: [dY blocks | V blocks]
         const int st = it % L.nsp;
         if (!mbar_wait(&rp_full[st], (it / L.nsp) & 1u, ab, 28)) { ok = false; break; }
         tc_fence_after();
         const uint32_t sa = smem_u32(smem + L.off_pring + st * kDpStage);
-        for (int k = 0; k < 8; ++k) {
+        for (int k = 0; k < 4 * kDpBlocks; ++k) {
           const uint32_t blk = (uint32_t)(k >> 2) * kBox + (k & 3) * 32;
-          const uint64_t ad = sdesc_sw128(sa + 2 * kBox + blk, 16, 1024);
+          const uint64_t ad = sdesc_sw128(sa + kDpBlocks * kBox + blk, 16, 1024);
           const uint64_t bd = sdesc_sw128(sa + blk, 16, 1024);
-          mma_f16_ss<2>(tmem + L.tmem_p + db * (kTile / 2), ad, bd, idesc, (cc | k) ? 1u : 0u);
+          mma_f16_ss<2>(tmem + L.tmem_p + db * (kTile / 2), ad, bd, idesc, (cb | k) ? 1u : 0u);
         }
-        mma_commit<2>(smem_u32(&rp_empty[st]));
-        mma_commit<2>(mapa_shared(smem_u32(&rp_empty[st]), 1));
+        mma_commit_pair(smem_u32(&rp_empty[st]));
       }
       if (!ok) break;
-      mma_commit<2>(smem_u32(&dp_full[db]));
-      mma_commit<2>(mapa_shared(smem_u32(&dp_full[db]), 1));
+      mma_commit_pair(smem_u32(&dp_full[db]));
     }
     mma_commit<2>(smem_u32(&dp_done));  // every dP^T product has completed before teardown
     mbar_wait_drain(&dp_done, 0);
-  } else if (warp == 1 && lane == 0 && rank == 0) {
-    // ---------------------------------------------------------------- MMA issuer (leader)
+  } else if ((warp == 1 || warp == kAccIssuer) && lane == 0 && rank == 0) {
+    // ---------------------------------------------------------------- MMA issuers (leader): warp 1 the
+    // score products S_s^T = K_s Q_s^T, warp 13 the dK (or dV) products, each on its own ring
+    const int acc = warp == kAccIssuer ? 1 : 0;
     const uint32_t idesc_s = idesc_f16(128, kTile, kBf16, false, false);
     const uint32_t idesc_acc = kDK ? idesc_f16(128, L.ncol, kBf16, false, true)   // B = Q rows, MN-major
                                    : idesc_f16(128, dn, kBf16, false, true);      // B = dY rows, MN-major
-    auto commit_both = [&](uint64_t* bar) {
-      mma_commit<2>(smem_u32(bar));
-      mma_commit<2>(mapa_shared(smem_u32(bar), 1));
-    };
+    auto commit_both = [&](uint64_t* bar) { mma_commit_pair(smem_u32(bar)); };
+    const int nst = acc ? L.nsq : L.nst;
+    uint64_t* fullb = acc ? q_full : r_full;
+    uint64_t* emptyb = acc ? q_empty : r_empty;
+    uint8_t* ring = smem + (acc ? L.off_qring : L.off_ring);
     int it = 0;
     auto take = [&](uint32_t* addr) -> bool {
-      const int st = it % L.nst;
-      if (!mbar_wait(&r_full[st], (it / L.nst) & 1u, ab, 23)) return false;
+      const int st = it % nst;
+      if (!mbar_wait(&fullb[st], (it / nst) & 1u, ab, 23)) return false;
       tc_fence_after();
-      *addr = smem_u32(smem + L.off_ring + st * kStage);
+      *addr = smem_u32(ring + st * kStage);
       return true;
     };
-    auto give = [&]() { commit_both(&r_empty[it % L.nst]); ++it; };
+    auto give = [&]() { commit_both(&emptyb[it % nst]); ++it; };
     const uint32_t ka = smem_u32(smem + L.off_a);
     auto issue_s = [&](int u) -> bool {  // S^T = K_s Q_s^T
       const int sb = u % kNSB, s = unit_s(u);
@@ -928,16 +969,20 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
       commit_both(&t_empty[tb]);
       return true;
     };
-    bool ok = mbar_wait(&in_full, 0, ab, 21);
-    tc_fence_after();
-    for (int u = 0; ok && u < kNSB - 1 && u < U; ++u) ok = issue_s(u);
-    for (int u = 0; ok && u < U; ++u) {
-      if (u + kNSB - 1 < U) ok = issue_s(u + kNSB - 1);
-      if (ok && (kDK || unit_s(u) == maps - 1)) ok = issue_acc(u);
+    if (!acc) {
+      bool ok = mbar_wait(&in_full, 0, ab, 21);
+      tc_fence_after();
+      for (int u = 0; ok && u < U; ++u) ok = issue_s(u);
+      mma_commit<2>(smem_u32(&s_done));  // every score product has completed before teardown
+      mbar_wait_drain(&s_done, 0);
+    } else {
+      bool ok = true;
+      for (int u = 0; ok && u < U; ++u)
+        if (kDK || unit_s(u) == maps - 1) ok = issue_acc(u);
+      commit_both(&o_full);
+      mbar_wait_drain(&o_full, 0);
     }
-    commit_both(&o_full);
-    mbar_wait_drain(&o_full, 0);
-  } else if ((warp >= 2 && warp < 6) || warp >= kSoftmax2) {
+  } else if ((warp >= 2 && warp < 6) || (warp >= kSoftmax2 && warp < kSoftmax2 + 4)) {
     // ---------------------------------------------------------------- softmax + epilogue: two warpgroups,
     // warps 2-5 take the first 32 of each thread's 64 query columns and warps 8-11 the other 32
     const int wg = warp >= kSoftmax2 ? 1 : 0;
@@ -1027,9 +1072,9 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
       tc_fence_before();
       named_bar_sync(1, 256);
       if (arriver) {
-        if (kDK) mbar_arrive_cluster(pf_leader + (u & 1) * 8);
-        else if (s == maps - 1) mbar_arrive_cluster(pf_leader + (g & 1) * 8);
-        if (kDK && s == maps - 1) mbar_arrive_cluster(df_leader + (g & 1) * 8);
+        if (kDK) mbar_arrive_remote(pf_leader + (u & 1) * 8);
+        else if (s == maps - 1) mbar_arrive_remote(pf_leader + (g & 1) * 8);
+        if (kDK && s == maps - 1) mbar_arrive_cluster_relaxed(df_leader + (g & 1) * 8);
       }
     }
     if (wg == 0 && ok) ok = mbar_wait(&o_full, 0, ab, 34);
@@ -1149,7 +1194,7 @@ extern "C" int da_attn_bwd_mixed(const void* q, int64_t q_rows, int64_t q_base, 
   if ((kw != 128 && kw != 256 && kw != 512) || maps * kw > 512) return DA_ERR_UNSUPPORTED;
   for (int kind = 0; kind < 3; ++kind) {
     const Layout L = make_layout(kind, maps, group, R, D);
-    if (L.nst < 2 || L.tmem_cols > 512) return DA_ERR_UNSUPPORTED;
+    if (L.nst < 2 || L.nsq < 2 || L.tmem_cols > 512) return DA_ERR_UNSUPPORTED;
   }
   if ((reinterpret_cast<uintptr_t>(dq) | reinterpret_cast<uintptr_t>(dk) | reinterpret_cast<uintptr_t>(dv)) & 15)
     return DA_ERR_ALIGN;
@@ -1190,13 +1235,18 @@ extern "C" int da_attn_bwd_mixed(const void* q, int64_t q_rows, int64_t q_base, 
   if (rc) return rc;
   rc = make_tmap_2d(&tk128, k, tdt, 2, R, k_rows, (uint64_t)R * 2, 64, 128);
   if (rc) return rc;
-  {  // V and dY: [B*T, D] as (64-column block, row, block index); a box is 64 rows x 2 blocks
+  CUtensorMap tdy2;
+  {  // V and dY: [B*T, D] as (64-column block, row, block index); a box is 64 rows x kDpBlocks blocks for
+     // the dP stages, 64 rows x 2 blocks for the dV kernel's dY operand
     const uint64_t dims[3] = {64, (uint64_t)B * T, (uint64_t)D / 64};
     const uint64_t strides[2] = {(uint64_t)D * 2, 128};
-    const uint32_t box[3] = {64, 64, 2};
+    const uint32_t box[3] = {64, 64, kDpBlocks};
     rc = make_tmap_blocks(&tv, v, tdt, 2, 3, dims, strides, box);
     if (rc) return rc;
     rc = make_tmap_blocks(&tdy, dy, tdt, 2, 3, dims, strides, box);
+    if (rc) return rc;
+    const uint32_t box2[3] = {64, 64, 2};
+    rc = make_tmap_blocks(&tdy2, dy, tdt, 2, 3, dims, strides, box2);
     if (rc) return rc;
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -1223,8 +1273,8 @@ extern "C" int da_attn_bwd_mixed(const void* q, int64_t q_rows, int64_t q_base, 
   }
   if (dv) {
     const Layout L = make_layout(2, maps, group, R, D);
-    rc = bf16 ? launch_pair(dkv_mixed_kernel<__nv_bfloat16, false>, L, pairs, tq, tk, tv, tdy, tq128, p, st)
-              : launch_pair(dkv_mixed_kernel<__half, false>, L, pairs, tq, tk, tv, tdy, tq128, p, st);
+    rc = bf16 ? launch_pair(dkv_mixed_kernel<__nv_bfloat16, false>, L, pairs, tq, tk, tv, tdy2, tq128, p, st)
+              : launch_pair(dkv_mixed_kernel<__half, false>, L, pairs, tq, tk, tv, tdy2, tq128, p, st);
   }
   return rc;
 }

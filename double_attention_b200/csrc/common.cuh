@@ -88,6 +88,12 @@ DA_DEV void mbar_arrive_cluster(uint32_t cluster_addr) {
                :: "r"(cluster_addr) : "memory");
 }
 
+// Arrive (release at CTA scope, the default) on a barrier that may live in another CTA of the cluster:
+// the hand-off of shared-memory tiles written with generic stores and fenced to the async proxy.
+DA_DEV void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" :: "r"(cluster_addr) : "memory");
+}
+
 // Arrive with relaxed semantics (no memory ordering): for barriers that only count events, such as
 // "this warp has read its TMEM columns" after tcgen05.fence::before_thread_sync.
 DA_DEV void mbar_arrive_cluster_relaxed(uint32_t cluster_addr) {
@@ -316,6 +322,13 @@ DA_DEV void mma_commit(uint32_t bar_cluster_addr) {
   else
     asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];"
                  :: "r"(bar_cluster_addr) : "memory");
+}
+
+// Paired-CTA form of mma_commit: one arrive on the barrier at this shared-memory offset in each CTA of
+// the pair (a multicast commit instead of one per CTA).
+DA_DEV void mma_commit_pair(uint32_t bar_smem_addr) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+               :: "r"(bar_smem_addr), "h"((uint16_t)0x3) : "memory");
 }
 
 // 32 lanes x 32 bit, 32 consecutive columns: thread i of the warp receives
