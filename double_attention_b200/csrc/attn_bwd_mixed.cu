@@ -471,6 +471,8 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
     const float kLog2e = 1.4426950408889634f;
     const float gsc = rsqrtf((float)p.group);
     float scale2[kMaxMaps], lse2[kMaxMaps], delta[kMaxMaps], alpha[kMaxMaps];
+    // per map: sum of dS * S (d gamma), and with a given delta also sum P * S and sum P * dP (the exact
+    // row delta), which correct d gamma from the given delta to this kernel's own P and dP
     float sA[kMaxMaps], sB[kMaxMaps], sC[kMaxMaps];
 #pragma unroll
     for (int s = 0; s < kMaxMaps; ++s) {
@@ -516,33 +518,57 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
           if (p.causal) lim = min(lim, t - k0 + 1);
           if (!live) lim = 0;
           uint32_t packed[16];
-          // branch-free: masked columns get probability 0 (a select, so any value the
-          // exponential takes there is discarded); two partial sums shorten the chains
+          // masked columns get probability 0 (a select, so any value the exponential takes there is
+          // discarded; tiles below the diagonal skip the selects); two partial sums shorten the chains
           if (form_ds) {
+            // dS = alpha P (dP - delta) = P (alpha dP - alpha delta); d gamma accumulates dS * S
+            const float ald = al * dl;
             float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f, c0 = 0.f, c1 = 0.f;
+            auto body = [&](auto masked, auto exact) {
 #pragma unroll
-            for (int i = 0; i < 32; i += 2) {
-              const float e0 = ex2(sv[i] * sc2 - ls2), e1 = ex2(sv[i + 1] * sc2 - ls2);
-              const float p0 = i < lim ? e0 : 0.f, p1 = i + 1 < lim ? e1 : 0.f;
-              const float q0 = p0 * pv[i], q1 = p1 * pv[i + 1];
-              a0 = fmaf(q0, sv[i], a0);
-              a1 = fmaf(q1, sv[i + 1], a1);
-              b0 = fmaf(p0, sv[i], b0);
-              b1 = fmaf(p1, sv[i + 1], b1);
-              c0 += q0;
-              c1 += q1;
-              packed[i / 2] = pack2<T>(al * (q0 - p0 * dl), al * (q1 - p1 * dl));
+              for (int i = 0; i < 32; i += 2) {
+                float p0 = ex2(fmaf(sv[i], sc2, -ls2)), p1 = ex2(fmaf(sv[i + 1], sc2, -ls2));
+                if (masked) {
+                  p0 = i < lim ? p0 : 0.f;
+                  p1 = i + 1 < lim ? p1 : 0.f;
+                }
+                const float d0 = p0 * fmaf(al, pv[i], -ald), d1 = p1 * fmaf(al, pv[i + 1], -ald);
+                a0 = fmaf(d0, sv[i], a0);
+                a1 = fmaf(d1, sv[i + 1], a1);
+                if (exact) {
+                  b0 = fmaf(p0, sv[i], b0);
+                  b1 = fmaf(p1, sv[i + 1], b1);
+                  c0 = fmaf(p0, pv[i], c0);
+                  c1 = fmaf(p1, pv[i + 1], c1);
+                }
+                packed[i / 2] = pack2<T>(d0, d1);
+              }
+            };
+            if (p.delta_given) {
+              if (lim >= 32) body(std::false_type{}, std::true_type{});
+              else body(std::true_type{}, std::true_type{});
+            } else {
+              if (lim >= 32) body(std::false_type{}, std::false_type{});
+              else body(std::true_type{}, std::false_type{});
             }
             a_acc += a0 + a1;
             b_acc += b0 + b1;
             c_acc += c0 + c1;
           } else {
             float d0 = 0.f, d1 = 0.f;
+            if (lim >= 32) {
 #pragma unroll
-            for (int i = 0; i < 32; i += 2) {
-              const float e0 = ex2(sv[i] * sc2 - ls2), e1 = ex2(sv[i + 1] * sc2 - ls2);
-              d0 = fmaf(i < lim ? e0 : 0.f, pv[i], d0);
-              d1 = fmaf(i + 1 < lim ? e1 : 0.f, pv[i + 1], d1);
+              for (int i = 0; i < 32; i += 2) {
+                d0 = fmaf(ex2(fmaf(sv[i], sc2, -ls2)), pv[i], d0);
+                d1 = fmaf(ex2(fmaf(sv[i + 1], sc2, -ls2)), pv[i + 1], d1);
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; i += 2) {
+                const float e0 = ex2(fmaf(sv[i], sc2, -ls2)), e1 = ex2(fmaf(sv[i + 1], sc2, -ls2));
+                d0 = fmaf(i < lim ? e0 : 0.f, pv[i], d0);
+                d1 = fmaf(i + 1 < lim ? e1 : 0.f, pv[i + 1], d1);
+              }
             }
             dsum += d0 + d1;
           }
@@ -632,7 +658,8 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
           const float A = sA[m] + red[(3 * m) * 128 + (l ^ 64)];
           const float Bs = sB[m] + red[(3 * m + 1) * 128 + (l ^ 64)];
           const float C = sC[m] + red[(3 * m + 2) * 128 + (l ^ 64)];
-          dg = alpha[m] * (A - C * Bs);
+          // sum dS S = alpha (sum P dP S - delta sum P S); with a given delta, delta -> the exact sum P dP
+          dg = p.delta_given ? A + alpha[m] * (delta[m] - C) * Bs : A;
         }
         for (int o = 16; o; o >>= 1) dg += __shfl_xor_sync(0xffffffffu, dg, o);
         if (p.scalar_part) {
@@ -1016,7 +1043,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
           const int q = qt + l;
           const bool qv = q < p.T;
           rt[m * 128 + l] = qv ? p.lse[((int64_t)b * maps + m) * p.T + q] * kLog2e : 0.f;
-          if (kDK) rt[(kMaxMaps + m) * 128 + l] = qv ? p.delta[((int64_t)b * maps + m) * p.T + q] : 0.f;
+          if (kDK) rt[(kMaxMaps + m) * 128 + l] = qv ? alpha[m] * p.delta[((int64_t)b * maps + m) * p.T + q] : 0.f;
         }
       }
       if (ok) ok = mbar_wait(&s_full[sb], (u / kNSB) & 1u, ab, 32);
@@ -1046,19 +1073,36 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
           const int hi = live ? p.T - (qt + qc0) : 0;
           const int lo = p.causal ? key - (qt + qc0) : 0;
           uint32_t packed[16];
+          // staged per query column: log2-domain log-sum-exp and alpha_s * delta (16-byte aligned rows)
+          const float4* lse4 = reinterpret_cast<const float4*>(lse_row + qc0);
+          const float4* ald4 = reinterpret_cast<const float4*>(delta_row + qc0);
+          auto body = [&](auto masked) {
 #pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            const float x0 = ex2(sv[e] * sc2 - lse_row[qc0 + e]), x1 = ex2(sv[e + 1] * sc2 - lse_row[qc0 + e + 1]);
-            const float p0 = (e >= lo && e < hi) ? x0 : 0.f, p1 = (e + 1 >= lo && e + 1 < hi) ? x1 : 0.f;
-            if (kDK) {
-              packed[e / 2] = pack2<T>(al * p0 * (dpv[e] - delta_row[qc0 + e]),
-                                       al * p1 * (dpv[e + 1] - delta_row[qc0 + e + 1]));
-            } else {
-              pm[e] = s == 0 ? al * p0 : fmaf(al, p0, pm[e]);
-              pm[e + 1] = s == 0 ? al * p1 : fmaf(al, p1, pm[e + 1]);
-              packed[e / 2] = pack2<T>(pm[e], pm[e + 1]);
+            for (int e4 = 0; e4 < 8; ++e4) {
+              const float4 ls = lse4[e4];
+              float4 ad = make_float4(0.f, 0.f, 0.f, 0.f);
+              if (kDK) ad = ald4[e4];
+              const float lsv[4] = {ls.x, ls.y, ls.z, ls.w}, adv[4] = {ad.x, ad.y, ad.z, ad.w};
+#pragma unroll
+              for (int c = 0; c < 4; c += 2) {
+                const int e = e4 * 4 + c;
+                float p0 = ex2(fmaf(sv[e], sc2, -lsv[c])), p1 = ex2(fmaf(sv[e + 1], sc2, -lsv[c + 1]));
+                if (masked) {
+                  p0 = (e >= lo && e < hi) ? p0 : 0.f;
+                  p1 = (e + 1 >= lo && e + 1 < hi) ? p1 : 0.f;
+                }
+                if (kDK) {  // dS^T = P^T (alpha dP^T - alpha delta)
+                  packed[e / 2] = pack2<T>(p0 * fmaf(al, dpv[e], -adv[c]), p1 * fmaf(al, dpv[e + 1], -adv[c + 1]));
+                } else {
+                  pm[e] = s == 0 ? al * p0 : fmaf(al, p0, pm[e]);
+                  pm[e + 1] = s == 0 ? al * p1 : fmaf(al, p1, pm[e + 1]);
+                  packed[e / 2] = pack2<T>(pm[e], pm[e + 1]);
+                }
+              }
             }
-          }
+          };
+          if (lo <= 0 && hi >= 32) body(std::false_type{});
+          else body(std::true_type{});
           if (kDK || s == maps - 1) {
 #pragma unroll
             for (int e = 0; e < 4; ++e)
