@@ -53,6 +53,8 @@ SIGNATURES: dict[str, list] = {
     "da_gemm_ex": [_p, _i64, _p, _i64, _i32, _i64, _p, _i64, _p, _i64, _i64, _p, _i64, _i64, _i64, _i32, _p, _i32,
                    _p, _i64, _p, _p],
     "da_gemm_splitk_workspace_elems": [_i64, _i64, _i64, _i32],  # returns int64 (set below)
+    "da_col_sum_workspace_elems": [_i64, _i64],  # returns int64 (set below)
+    "da_col_sum": [_p, _i64, _i64, _i64, _i32, _p, _p, _i64, _p],
     "da_gemm_splitk": [_p, _i64, _i32, _p, _i64, _i32, _p, _i64, _i64, _i64, _i64, _i32, _i32, _p, _i64, _p, _p],
     "da_gemm_splitk_grouped": [_p, _i64, _i64, _p, _i64, _p, _i64, _i64, _i64, _i64, _i32, _i32, _i32, _p, _i64, _p,
                                _p],
@@ -117,6 +119,7 @@ def lib() -> ctypes.CDLL:
             handle.da_route_bwd_workspace_size.restype = ctypes.c_int64
             handle.da_attn_bwd_workspace_size.restype = ctypes.c_int64
             handle.da_gemm_splitk_workspace_elems.restype = ctypes.c_int64
+            handle.da_col_sum_workspace_elems.restype = ctypes.c_int64
             handle.da_kernel_launches.argtypes = []
             handle.da_kernel_launches.restype = ctypes.c_uint64
             _lib = handle

@@ -1036,8 +1036,18 @@ def gemm_ex(a: Tensor, b: Tensor, b_mn: bool, out: Tensor, a2: Tensor | None = N
 
 
 def _bias_grad(d: Tensor) -> Tensor:
-    """Column sums of a [rows, N] gradient, accumulated in fp32 (the bias gradient of a Linear)."""
-    return torch.sum(d, dim=0, dtype=torch.float32)
+    """Column sums of a [rows, N] bf16/fp16 gradient in fp32 (the bias gradient of a Linear), one
+    HBM pass whose partial sums are added in a fixed order (da_col_sum)."""
+    d = d.reshape(-1, d.shape[-1])
+    if d.stride(-1) != 1:
+        d = d.contiguous()
+    rows, cols = d.shape
+    elems = int(_lib.lib().da_col_sum_workspace_elems(rows, cols))
+    work = torch.empty(max(elems, 4), dtype=torch.float32, device=d.device)
+    out = torch.empty(cols, dtype=torch.float32, device=d.device)
+    call("da_col_sum", d.data_ptr(), rows, cols, d.stride(0), dtype_code(d.dtype), out.data_ptr(), work.data_ptr(),
+         work.numel(), stream_ptr(d.device))
+    return out
 
 
 class _Linear(torch.autograd.Function):
@@ -1259,7 +1269,7 @@ class _QKVProjection(torch.autograd.Function):
                 gemm_splitk(dv, dv.stride(0), True, x2d, x2d.stride(0), True, wv.shape[0], k, m, dwv32)
                 dwv = dwv32.to(wv.dtype)
             if ctx.has_bias and need[4]:
-                dbv = _bias_grad(dvalue).to(wv.dtype)
+                dbv = _bias_grad(dv).to(wv.dtype)
         return dx, dwq, dwk, dwv, dbv
 
 

@@ -367,6 +367,17 @@ DA_API int da_gemm_splitk_grouped(const void* A, int64_t lda, int64_t a_group_co
                                   float* C, int64_t ldc, int64_t M, int64_t N, int64_t K_group, int groups, int dtype,
                                   int splits, float* workspace, int64_t workspace_elems, int* status, void* stream);
 
+/* Bias gradient of a Linear layer: out[c] = sum over rows of d[r, c] in fp32
+ * (d: [rows, cols] bf16 / fp16 with row stride ld; cols and ld multiples of 8,
+ * d 16-byte aligned).  Replaces the autograd column sum of nn.Linear's bias
+ * gradient in the block layers (reference modules.py:212, :272, :339-346).
+ * Partial sums per row chunk go to `workspace` (fp32, at least
+ * da_col_sum_workspace_elems(rows, cols) elements; DA_ERR_WORKSPACE otherwise)
+ * and are added in a fixed order, so the result is bit-reproducible. */
+DA_API int64_t da_col_sum_workspace_elems(int64_t rows, int64_t cols);
+DA_API int da_col_sum(const void* d, int64_t rows, int64_t cols, int64_t ld, int dtype, float* out,
+                      float* workspace, int64_t workspace_elems, void* stream);
+
 /* ---- residual add + LayerNorm around the block -----------------------
  * Replaces x + branch followed by nn.LayerNorm in DoubleAttentionBlock.forward
  * (modules.py:294-356) and the final norm of DoubleAttentionLM (modules.py:415-460).

@@ -126,3 +126,23 @@ def test_feedforward_backward_is_bit_reproducible() -> None:
     torch.cuda.synchronize()
     for a, b in zip(*grads):
         assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize(("rows", "cols", "ld"), [(1, 8, 8), (1000, 512, 512), (3000, 1536, 1536), (777, 264, 520),
+                                                  (262144, 512, 512)])
+def test_bias_grad_column_sums(rows, cols, ld, dtype) -> None:
+    """da_col_sum against an fp64 column sum of the same rounded values; two calls agree bit for bit."""
+    dev = torch.device("cuda")
+    g = torch.Generator().manual_seed(rows + cols)
+    full = torch.randn(rows, ld, generator=g).to(dtype)
+    d = full.to(dev)[:, :cols]
+    got = ops._bias_grad(d)
+    again = ops._bias_grad(d)
+    torch.cuda.synchronize()
+    assert ops.device_status(dev) == 0
+    assert got.dtype == torch.float32 and got.shape == (cols,)
+    ref = full[:, :cols].double().sum(0)
+    bound = 1e-5 * rows ** 0.5 * 4 + 1e-6 * ref.abs().max().item()
+    assert (got.double().cpu() - ref).abs().max().item() <= bound
+    assert torch.equal(got, again)
