@@ -303,10 +303,7 @@ __global__ void __launch_bounds__(fwd_threads<kLat>(), 1) attn_fwd_kernel(const 
     if (rank == 0 && lane == 0) {
       const uint32_t idesc_s = idesc_f16(128, nk, std::is_same<T, __nv_bfloat16>::value, false, false);
       const uint32_t idesc_o = idesc_f16(128, L.nc, true, false, true);  // B = V, MN-major
-      auto commit_both = [&](uint64_t* bar) {
-        mma_commit<2>(smem_u32(bar));
-        mma_commit<2>(mapa_shared(smem_u32(bar), 1));
-      };
+      auto commit_both = [&](uint64_t* bar) { mma_commit_pair(smem_u32(bar)); };
       const uint32_t qa = smem_u32(smem + L.off_q);
       if (warp == 1) trace_at(ft, 0);
       bool ok = mbar_wait(&q_full, 0, ab, 21);
@@ -435,8 +432,8 @@ __global__ void __launch_bounds__(fwd_threads<kLat>(), 1) attn_fwd_kernel(const 
       if (arriver && u < 256) trace_at(ft, 3074 + 4 * u);
       named_bar_sync(1, 128);
       if (arriver) {
-        mbar_arrive_cluster(pf_leader + (u % L.nsb) * 8);
-        if (pb >= 0) mbar_arrive_cluster(pv_leader + pb * 8);
+        mbar_arrive_cluster_relaxed(pf_leader + (u % L.nsb) * 8);  // score buffer read
+        if (pb >= 0) mbar_arrive_remote(pv_leader + pb * 8);         // probability tile written
       }
       if (arriver && u < 256) trace_at(ft, 3075 + 4 * u);
     };

@@ -233,10 +233,7 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks) route_bwd_kernel(const _
     const uint32_t idesc_s = idesc_f16(128, kNA, kBf16, false, false);
     const uint32_t idesc_p = idesc_f16(128, kNA, true, false, false);      // g and Dv are bf16
     const uint32_t idesc_u = idesc_f16(128, L.ncol, kBf16, false, true);   // B = Dk rows, MN-major
-    auto commit_both = [&](uint64_t* bar) {
-      mma_commit<2>(smem_u32(bar));
-      mma_commit<2>(mapa_shared(smem_u32(bar), 1));
-    };
+    auto commit_both = [&](uint64_t* bar) { mma_commit_pair(smem_u32(bar)); };
     int it = 0;
     auto take = [&](uint32_t* addr) -> bool {
       const int s = it % L.nst;
@@ -426,7 +423,7 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks) route_bwd_kernel(const _
       fence_proxy_async();
     }
     named_bar_sync(1, 128);
-    if (arriver) mbar_arrive_cluster(mapa_shared(smem_u32(&g_full), 0));
+    if (arriver) mbar_arrive_remote(mapa_shared(smem_u32(&g_full), 0));
     if (arriver) trace_time(p.trace, 2);
 
     // ---- per atom tile: P, dL' (shared memory + rows for the dictionary gradients), dbeta
@@ -510,7 +507,7 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks) route_bwd_kernel(const _
       if (arriver) trace_at(ft, 130 + 4 * j);
       tc_fence_before();
       __syncwarp();  // this warp's TMEM reads are done and its dL' stores fenced: it arrives by itself
-      if (lane == 0) mbar_arrive_cluster(pf_leader + sb * 8);
+      if (lane == 0) mbar_arrive_remote(pf_leader + sb * 8);
     }
     if (arriver) trace_time(p.trace, 3);
     if (p.dbeta) {

@@ -228,10 +228,7 @@ __global__ void __launch_bounds__(kThreads, 1) dict_grad_kernel(const __grid_con
     const uint32_t idesc_p = idesc_f16(128, kTR, true, false, false);   // Dv and g are bf16
     const uint32_t idesc_v = idesc_f16(128, kR, true, false, true);     // P^T . g, g MN-major
     const uint32_t idesc_k = idesc_f16(128, kR, kBf16, false, true);    // dL'^T . q, q MN-major
-    auto commit_both = [&](uint64_t* bar) {
-      mma_commit<2>(smem_u32(bar));
-      mma_commit<2>(mapa_shared(smem_u32(bar), 1));
-    };
+    auto commit_both = [&](uint64_t* bar) { mma_commit_pair(smem_u32(bar)); };
     const uint32_t dk_a = smem_u32(smem + C::kOffDk), dv_a = smem_u32(smem + C::kOffDv);
     const uint32_t p_a = smem_u32(smem + C::kOffP), dl_a = smem_u32(smem + C::kOffDl);
     auto issue_sdp = [&](int t) -> bool {
@@ -372,7 +369,7 @@ __global__ void __launch_bounds__(kThreads, 1) dict_grad_kernel(const __grid_con
         }
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(pf_leader + b * 8);  // this warp: TMEM read, tiles written
+      if (lane == 0) mbar_arrive_remote(pf_leader + b * 8);  // this warp: TMEM read, tiles written
       if (tracer) stamp(3, t, 3);
     }
 

@@ -286,10 +286,7 @@ __global__ void __launch_bounds__(192, 1) route_fwd_kernel(const __grid_constant
       const uint32_t idesc_o = idesc_f16(128, C::kNc, true, false, false);
       bool ok = mbar_wait(&q_full, 0, ab, 21);
       tc_fence_after();
-      auto commit_both = [&](uint64_t* bar) {
-        mma_commit<2>(smem_u32(bar));
-        mma_commit<2>(mapa_shared(smem_u32(bar), 1));
-      };
+      auto commit_both = [&](uint64_t* bar) { mma_commit_pair(smem_u32(bar)); };
       auto issue_s = [&](int j) -> bool {
         const int sb = j % C::kB, s = j % C::kStages;
         trace_at(ft, 100 + 2 * j);
@@ -429,7 +426,7 @@ __global__ void __launch_bounds__(192, 1) route_fwd_kernel(const __grid_constant
       named_bar_sync(1, 128);
       if (arriver) {
         trace_at(ft, 405 + 8 * j);
-        mbar_arrive_cluster(pf_leader + sb * 8);
+        mbar_arrive_remote(pf_leader + sb * 8);
         trace_at(ft, 406 + 8 * j);
       }
     }
@@ -751,10 +748,7 @@ __global__ void __launch_bounds__(wide_threads<kMinBlocks, kLat>(), kMinBlocks) 
     if (rank == 0 && lane == 0) {
       const uint32_t idesc_s = idesc_f16(128, nk, std::is_same<T, __nv_bfloat16>::value, false, false);
       const uint32_t idesc_o = idesc_f16(128, L.nc, true, false, false);  // Dv rows are K-major (atoms contiguous)
-      auto commit_both = [&](uint64_t* bar) {
-        mma_commit<2>(smem_u32(bar));
-        mma_commit<2>(mapa_shared(smem_u32(bar), 1));
-      };
+      auto commit_both = [&](uint64_t* bar) { mma_commit_pair(smem_u32(bar)); };
       const uint32_t qa = smem_u32(smem + L.off_q);
       int kx = 0, kst = 0, vc = 0;  // key boxes consumed and current key slot; value stages consumed
       auto issue_s = [&](int j) -> bool {  // S_j = q . Dk_j into score buffer j % nsb
@@ -923,7 +917,7 @@ __global__ void __launch_bounds__(wide_threads<kMinBlocks, kLat>(), kMinBlocks) 
         }
         tc_fence_before();
         named_bar_sync(1, 128);
-        if (arriver) mbar_arrive_cluster(pf_leader + sb * 8);
+        if (arriver) mbar_arrive_remote(pf_leader + sb * 8);
         continue;
       }
       uint32_t packed[kMaxCh][16];
@@ -974,7 +968,7 @@ __global__ void __launch_bounds__(wide_threads<kMinBlocks, kLat>(), kMinBlocks) 
       }
       tc_fence_before();
       named_bar_sync(1, 128);
-      if (arriver) mbar_arrive_cluster(pf_leader + sb * 8);
+      if (arriver) mbar_arrive_remote(pf_leader + sb * 8);
       if (arriver && j < 256) trace_at(ft, 3075 + 4 * j);
     }
 
