@@ -495,9 +495,9 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
       if (arriver && u < 512) trace_at(ft, 5120 + 4 * u);
       if (ok) ok = mbar_wait(&s_full[sb], (u >> 1) & 1u, ab, 32);
       if (ok && s == 0) ok = mbar_wait(&dp_full[g & 1], (g >> 1) & 1u, ab, 35);
-      if (ok && form_ds && v >= 2) ok = mbar_wait(&ds_empty[v & 1], ((v - 2) >> 1) & 1u, ab, 33);
       if (arriver && u < 512) trace_at(ft, 5121 + 4 * u);
       ok = __all_sync(0xffffffffu, ok);
+      const bool entered = ok;  // the unit's TMEM reads (and s_free arrival) happen only then
       if (ok) {
         tc_fence_after();
         const uint32_t dsa = smem_u32(smem + L.off_t + (v & 1) * (kRows * kTile * 2));
@@ -573,10 +573,18 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
             dsum += d0 + d1;
           }
           if (form_ds) {
+            // the dS tile of unit v - 2 must have been read by its dQ product: waited for only now, so the
+            // arithmetic above overlaps that product
+            bool free_tile = v < 2 || mbar_wait(&ds_empty[v & 1], ((v - 2) >> 1) & 1u, ab, 33);
+            free_tile = __all_sync(0xffffffffu, free_tile);
+            if (free_tile) {
 #pragma unroll
-            for (int e = 0; e < 4; ++e)
-              st_shared_v4(dsa + half * kBox + sw128_offset(r, ch * 4 + e), packed[4 * e], packed[4 * e + 1],
-                           packed[4 * e + 2], packed[4 * e + 3]);
+              for (int e = 0; e < 4; ++e)
+                st_shared_v4(dsa + half * kBox + sw128_offset(r, ch * 4 + e), packed[4 * e], packed[4 * e + 1],
+                             packed[4 * e + 2], packed[4 * e + 3]);
+            } else {
+              ok = false;
+            }
           }
         }
         if (form_ds) {
@@ -589,7 +597,7 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
         }
       }
       if (arriver && u < 512) trace_at(ft, 5122 + 4 * u);
-      if (!ok && lane == 0) mbar_arrive_cluster_relaxed(sf_leader + sb * 8);  // aborted unit: counts stay whole
+      if (!entered && lane == 0) mbar_arrive_cluster_relaxed(sf_leader + sb * 8);  // aborted unit: counts stay whole
       tc_fence_before();
       named_bar_sync(1, 256);
       if (arriver) {
@@ -1048,11 +1056,9 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
       }
       if (ok) ok = mbar_wait(&s_full[sb], (u / kNSB) & 1u, ab, 32);
       if (ok && kDK && s == 0) ok = mbar_wait(&dp_full[g & 1], (g >> 1) & 1u, ab, 35);
-      // the tile buffer written by this unit must have been read by the product two uses ago
-      if (ok && kDK && u >= 2) ok = mbar_wait(&t_empty[u & 1], ((u - 2) >> 1) & 1u, ab, 33);
-      if (ok && !kDK && s == 0 && g >= 2) ok = mbar_wait(&t_empty[g & 1], ((g - 2) >> 1) & 1u, ab, 33);
       if (s == 0) named_bar_sync(1, 256);  // staged lse / delta visible
       ok = __all_sync(0xffffffffu, ok);
+      const bool entered = ok;  // the unit's TMEM reads (and s_free arrival) happen only then
       if (ok) {
         tc_fence_after();
         const uint32_t ta = smem_u32(smem + L.off_t + (kDK ? (u & 1) : (g & 1)) * (kRows * kTile * 2));
@@ -1104,15 +1110,25 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
           if (lo <= 0 && hi >= 32) body(std::false_type{});
           else body(std::true_type{});
           if (kDK || s == maps - 1) {
+            // the tile buffer written here must have been read by the product two uses ago (dK: unit u - 2,
+            // dV: query tile g - 2); waited for only now, so the arithmetic above overlaps that product
+            bool free_tile = true;
+            if (kDK && u >= 2) free_tile = mbar_wait(&t_empty[u & 1], ((u - 2) >> 1) & 1u, ab, 33);
+            if (!kDK && g >= 2) free_tile = mbar_wait(&t_empty[g & 1], ((g - 2) >> 1) & 1u, ab, 33);
+            free_tile = __all_sync(0xffffffffu, free_tile);
+            if (free_tile) {
 #pragma unroll
-            for (int e = 0; e < 4; ++e)
-              st_shared_v4(ta + half * kBox + sw128_offset(r, ch * 4 + e), packed[4 * e], packed[4 * e + 1],
-                           packed[4 * e + 2], packed[4 * e + 3]);
+              for (int e = 0; e < 4; ++e)
+                st_shared_v4(ta + half * kBox + sw128_offset(r, ch * 4 + e), packed[4 * e], packed[4 * e + 1],
+                             packed[4 * e + 2], packed[4 * e + 3]);
+            } else {
+              ok = false;
+            }
           }
         }
         if (kDK || s == maps - 1) fence_proxy_async();
       }
-      if (!ok && lane == 0) mbar_arrive_cluster_relaxed(sf_leader + sb * 8);  // aborted unit: counts stay whole
+      if (!entered && lane == 0) mbar_arrive_cluster_relaxed(sf_leader + sb * 8);  // aborted unit: counts stay whole
       tc_fence_before();
       named_bar_sync(1, 256);
       if (arriver) {
