@@ -187,7 +187,8 @@ class SharedDictionaryAttention(nn.Module):
 
         if cfg.map_combine == "weighted_sum":
             combined = ops.routed_attention_mixed(routed, dense_value, score_scales, map_weights, cfg)
-            if isinstance(self.output, nn.Linear) and ops.linear_supported(combined, self.output):
+            if (ops.BLOCK_LINEAR_ON_TCGEN05 and isinstance(self.output, nn.Linear)
+                    and ops.linear_supported(combined, self.output)):
                 output = ops.linear(combined, self.output)  # the output projection on the tcgen05 GEMM
             else:
                 output = self.output(combined.to(self._output_dtype(combined)))
@@ -269,7 +270,8 @@ class DoubleAttentionBlock(nn.Module):
                             normalized_dictionary: tuple[Tensor, Tensor] | None) -> Tensor:
         if not self.attention.config.q_dictionary_feedforward:
             first, act, second, drop = self.feedforward
-            if act.approximate == "none" and ops.feedforward_supported(normalized_x, first, second):
+            if (ops.BLOCK_LINEAR_ON_TCGEN05 and act.approximate == "none"
+                    and ops.feedforward_supported(normalized_x, first, second)):
                 return drop(ops.feedforward(normalized_x, first, second))  # GELU fused into the GEMMs
             return self.feedforward(normalized_x)
         if normalized_dictionary is None:

@@ -1088,6 +1088,15 @@ def _linear_dtype(x: Tensor) -> torch.dtype:
     return torch.get_autocast_dtype("cuda") if torch.is_autocast_enabled("cuda") else x.dtype
 
 
+# The block's plain Linear layers (SharedDictionaryAttention's output projection, modules.py:272, and the
+# feed-forward branch of the block, modules.py:339-346) lie outside the routed-attention path.  PyTorch's
+# cuBLAS runs them faster on B200 than this library's persistent GEMM does, even with GELU fused into the
+# latter's epilogues (LM training step, a1, 6 layers, B256 T1024: 89.7 ms against 96.2 ms per step), so
+# the modules call F.linear / nn.GELU for them by default, as the reference does; True routes them
+# through ops.linear / ops.feedforward on the tcgen05 GEMM.
+BLOCK_LINEAR_ON_TCGEN05 = False
+
+
 def linear_supported(x: Tensor, layer: torch.nn.Linear) -> bool:
     """Whether the tcgen05 GEMM covers ``layer(x)``: CUDA, half-precision compute (autocast, or x and the
     weight in one half dtype, as F.linear requires), widths multiples of 128 (out) and 8 (in)."""

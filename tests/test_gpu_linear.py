@@ -146,3 +146,29 @@ def test_bias_grad_column_sums(rows, cols, ld, dtype) -> None:
     bound = 1e-5 * rows ** 0.5 * 4 + 1e-6 * ref.abs().max().item()
     assert (got.double().cpu() - ref).abs().max().item() <= bound
     assert torch.equal(got, again)
+
+
+def test_block_linear_layers_on_either_gemm_agree(monkeypatch) -> None:
+    """The block's output projection and feed-forward branch run on cuBLAS by default
+    (ops.BLOCK_LINEAR_ON_TCGEN05 = False) or on the tcgen05 GEMM; the two LM steps agree."""
+    from double_attention_b200 import DoubleAttentionLM, experiment_config
+
+    dev = torch.device("cuda")
+    ids = torch.randint(0, 512, (2, 257), generator=torch.Generator().manual_seed(4)).to(dev)
+    results = []
+    for flag in (False, True):
+        monkeypatch.setattr(ops, "BLOCK_LINEAR_ON_TCGEN05", flag)
+        torch.manual_seed(0)
+        model = DoubleAttentionLM(512, 256, experiment_config("a1"), 2, dictionary_group_size=2,
+                                  feedforward_dim=1536).to(dev)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            logits, loss = model(ids[:, :-1], ids[:, 1:])
+        loss.backward()
+        torch.cuda.synchronize()
+        assert ops.device_status(dev) == 0
+        results.append((logits.float().cpu(), loss.item(), {n: p.grad.float().cpu() for n, p in model.named_parameters()}))
+    (l0, loss0, g0), (l1, loss1, g1) = results
+    assert abs(loss0 - loss1) <= 2e-3 * abs(loss0)
+    _close("logits", l1, l0, 2e-2, 0.9995)
+    for name in g0:
+        _close(f"d {name}", g1[name], g0[name], 3e-2, 0.999)
