@@ -171,4 +171,9 @@ def test_block_linear_layers_on_either_gemm_agree(monkeypatch) -> None:
     assert abs(loss0 - loss1) <= 2e-3 * abs(loss0)
     _close("logits", l1, l0, 2e-2, 0.9995)
     for name in g0:
-        _close(f"d {name}", g1[name], g0[name], 3e-2, 0.999)
+        ref, got = g0[name], g1[name]
+        scale = ref.abs().max().item()
+        err = (got - ref).abs().max().item()
+        assert err <= 3e-2 * max(1.0, scale), f"d {name}: max-abs {err:.3e}"
+        if scale >= 1e-2:  # the cosine of a near-zero gradient says nothing
+            assert _cos(got, ref) >= 0.999, f"d {name}: cosine {_cos(got, ref):.6f}"
