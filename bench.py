@@ -240,7 +240,7 @@ class ModuleWorkload:
         self.x.grad = None
         self.module(self.x).backward(self.dy)
 
-    def e2e_region(self, steps: int, flush: torch.Tensor, stream) -> float:
+    def e2e_region(self, steps: int, flush: torch.Tensor, stream, graphed: bool = True) -> float:
         """Device time (ms) of `steps` end-to-end steps, copies included, timed as one region.
 
         Every step copies its inputs from pinned host memory and its result (y, or dx when training)
@@ -248,20 +248,28 @@ class ModuleWorkload:
         does it: step k+1's inputs go host -> device on one copy stream while step k computes, and step
         k's result goes device -> host on a second copy stream (PCIe carries both directions at once)
         while step k+1 computes.  The region opens before the first step's input copy and closes
-        after the last step's result copy; the L2 flush before every step lies inside it.
+        after the last step's result copy; the L2 flush before every step lies inside it.  With
+        `graphed` the module step is the package's GraphedModuleStep (one graph launch per step: the
+        staged inputs are copied into its static buffers and its result into one of two result
+        buffers, device to device, inside the region); otherwise the eager module call.
         """
         if not hasattr(self, "_staging"):
+            from double_attention_b200 import GraphedModuleStep
+
             shape, dt = self.x_host.shape, self.x_host.dtype
             self._staging = {
                 "in": torch.cuda.Stream(self.device), "out": torch.cuda.Stream(self.device),
                 "x": [torch.empty(shape, dtype=dt, device=self.device) for _ in range(2)],
                 "dy": [torch.empty(shape, dtype=dt, device=self.device) for _ in range(2)] if self.train else None,
+                "res": [torch.empty(shape, dtype=dt, device=self.device) for _ in range(2)],
+                "graph": GraphedModuleStep(self.module, tuple(shape), dt, backward=self.train) if graphed else None,
             }
         st = self._staging
         copy_in, copy_out = st["in"], st["out"]
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         staged = [torch.cuda.Event() for _ in range(steps)]
         consumed = [torch.cuda.Event() for _ in range(steps)]
+        sent = [torch.cuda.Event() for _ in range(steps)]
 
         def stage(k: int) -> None:
             i = k % 2
@@ -280,20 +288,28 @@ class ModuleWorkload:
                 stage(k + 1)
             stream.wait_event(staged[k])
             i = k % 2
-            if self.train:
+            if st["graph"] is not None:
+                res = st["graph"](st["x"][i], st["dy"][i] if self.train else None)
+                if k >= 2:
+                    stream.wait_event(sent[k - 2])  # result buffer i is on its way to the host no longer
+                st["res"][i].copy_(res)
+                out = st["res"][i]
+            elif self.train:
                 for p in self.module.parameters():
                     p.grad = None
                 xd = st["x"][i].detach().requires_grad_(True)
                 self.module(xd).backward(st["dy"][i])
                 out = xd.grad  # the input gradient is the step's result
+                out.record_stream(copy_out)
             else:
                 with torch.no_grad():
                     out = self.module(st["x"][i])
+                out.record_stream(copy_out)
             consumed[k].record(stream)
-            out.record_stream(copy_out)
             copy_out.wait_event(consumed[k])
             with torch.cuda.stream(copy_out):
                 self.out_host.copy_(out, non_blocking=True)
+            sent[k].record(copy_out)
             del out
         stream.wait_stream(copy_out)
         end.record(stream)
@@ -344,7 +360,7 @@ class LMWorkload:
         tgt = self.tgt_host.to(self.device, non_blocking=True)
         self.loss_host.copy_(self._train(ids, tgt).detach().float(), non_blocking=True)
 
-    def e2e_region(self, steps: int, flush: torch.Tensor, stream) -> float:
+    def e2e_region(self, steps: int, flush: torch.Tensor, stream, graphed: bool = False) -> float:
         """Device time (ms) of `steps` end-to-end training steps (1 MB of token ids in, the loss out)."""
         return sum(time_steps(self.e2e_step, steps, flush, stream))
 
@@ -628,10 +644,14 @@ def run_b200(args, cfg, world, rank, local):
     value = work.tokens * world / (ms / 1e3)
 
     # --- end to end through the public API: pinned host in, result back to pinned host
-    work.e2e_region(3, flush, stream)
+    # the value step's graph is released first: the end-to-end step captures its own
+    del step, graph
+    torch.cuda.empty_cache()
+    e2e_graphed = work.capturable and not args.no_graph
+    work.e2e_region(3, flush, stream, graphed=e2e_graphed)
     barrier(world)
     torch.cuda.synchronize()
-    e2e_total = work.e2e_region(args.steps, flush, stream)
+    e2e_total = work.e2e_region(args.steps, flush, stream, graphed=e2e_graphed)
     barrier(world)
     e2e_ms = max_over_ranks(e2e_total / args.steps, world)
     e2e_value = work.tokens * world / (e2e_ms / 1e3)
@@ -644,7 +664,7 @@ def run_b200(args, cfg, world, rank, local):
         with torch.no_grad():
             ours_out = work.module(work.x.detach()).float()
     if rank == 0:
-        del work, step, graph
+        del work
         torch.cuda.empty_cache()
         kernels = kernel_rooflines(cfg, args.config, device, per_rank_batch(cfg, world))
         top = max(kernels, key=lambda k: kernels[k][0])
@@ -702,8 +722,10 @@ def run_b200(args, cfg, world, rank, local):
                     "ms_per_step": e2e_ms,
                     "timing": ("one region over all steps, L2 flush before every step inside it; inputs staged "
                                "double-buffered on a host-to-device copy stream, results on a device-to-host "
-                               "copy stream, eager module calls" if cfg["kind"] == "module" else
-                               "per-step events around the copies and the eager training step")},
+                               "copy stream" if cfg["kind"] == "module" else
+                               "per-step events around the copies and the eager training step"),
+                    "call": ("double_attention_b200.GraphedModuleStep (one CUDA graph launch per step)"
+                             if e2e_graphed else "eager module call")},
             "roofline": roofline,
             "cpu_baseline": cpu_base,
             "reference_gpu": ref_gpu,

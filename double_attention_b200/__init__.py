@@ -8,6 +8,7 @@ tcgen05 kernels (``libda_b200.so``, C ABI in ``include/da_b200.h``).
 """
 
 from .config import DoubleAttentionConfig, experiment_config, experiment_names
+from .graphs import GraphedModuleStep
 from .modules import (
     DoubleAttentionAux,
     DoubleAttentionBlock,
@@ -24,6 +25,7 @@ __all__ = [
     "DoubleAttentionConfig",
     "DoubleAttentionLM",
     "DoubleAttentionStack",
+    "GraphedModuleStep",
     "SharedDictionaryAttention",
     "SharedDictionaryBank",
     "assemble_score_maps",

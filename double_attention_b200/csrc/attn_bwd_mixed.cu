@@ -20,9 +20,14 @@
 //   * key-parallel (dV): per query tile, S_s^T map by map into the mixed
 //     probabilities, then one dV product.
 // Score and dP tiles are double-buffered in TMEM, so the tensor core works on
-// the next unit while the softmax warpgroup handles the current one.
-// Operands stream through one ring of 16 KB stages filled in exactly the
-// order the MMA warp consumes them.
+// the next unit while a softmax warpgroup handles the current one (dQ and dK:
+// the two warpgroups take alternate units).  Operands stream through rings of
+// 16 KB stages, each filled in exactly the order its MMA issuer consumes it.
+// Each product is a chain of dependent K = 16 instructions into one TMEM
+// accumulator; measured on B200, a lone chain of paired M = 128 instructions
+// issues one per ~205 cycles whether N is 128 or 256, two interleaved chains
+// ~146 and three ~97, so the score, dP and accumulation products have their
+// own issuing threads and their chains interleave in the tensor pipe.
 #include <math.h>
 
 #include "attn_common.h"
@@ -34,9 +39,9 @@ namespace attn {
 namespace bwdm {
 
 // warps 0 and 12: TMA producers of the resident rows and the score / accumulation operands (even and
-// odd ring stages); warp 1: their MMA issuer; warps 2-5 and 8-11: softmax, two warpgroups each taking
-// 32 of a thread's 64 columns (the per-element arithmetic of dS and P, with one warp per SM
-// sub-partition, paced the kernels); warps 6 and 13: TMA producers of the dP operands (V and dY);
+// odd ring stages); warp 1: their MMA issuer; warps 2-5 and 8-11: softmax, two warpgroups (dQ and dK:
+// taking alternate units, each thread all 64 columns of its row half; dV: each taking 32 of a thread's
+// 64 columns of every unit; one warp per SM sub-partition in each); warps 6 and 13: TMA producers of the dP operands (V and dY);
 // warp 7: the dP issuer.  dP runs as its own stream so the other products never wait behind it.  A
 // producer warp completes about one paired stage per microsecond whatever the stage holds, so each
 // ring has two.
@@ -48,9 +53,17 @@ constexpr int kSoftmax2 = 8;      // first warp of the second softmax warpgroup
 constexpr int kRows = 64;      // rows (queries or keys) per CTA
 constexpr int kTile = 128;     // columns (keys or queries) per tile and pair
 constexpr int kStage = 16384;  // main ring stage bytes
-constexpr int kDpBlocks = 1;    // 64-column blocks of each of V and dY per dP ring stage
+constexpr int kDpBlocks = 1;    // 64-column blocks of each of V and dY per dP ring stage (dK kernel)
 constexpr int kDpStage = 2 * kDpBlocks * kRows * 128;
 constexpr int kDpStages = 3;
+// The dQ kernel's dP stream (formed twice per key tile, in the delta sweep and the dS sweep): stages of
+// kDpBlocksQ 64-column blocks of each of V and dY.  Measured: one-block stages x 3 (with 3 score-ring
+// and 2 accumulation-ring stages) and two-block stages x 2 (2 + 2) run alike, as do other splits of
+// the same ring space; the kernels are paced by their MMA chains (see the issuers), not by the rings.
+constexpr int kDpBlocksQ = 1;
+constexpr int kDpStageQ = 2 * kDpBlocksQ * kRows * 128;
+constexpr int kDpStagesQ = 3;
+constexpr int kAccStages = 2;  // accumulation-ring stages of the dQ and dK kernels
 constexpr int kMaxStages = 8;
 constexpr int kBox = kRows * 128;  // one 64-row x 128-byte swizzled box
 
@@ -105,28 +118,29 @@ __host__ __device__ inline Layout make_layout(int kind, int maps, int group, int
   L.off_t = L.off_b + b_bytes;                 // two dS / P tiles
   // The dQ kernel's row reductions (delta at the end of the first sweep, d gamma after the last product)
   // borrow the dS tiles' space, idle at both points; the key-parallel kernels stage each query tile's
-  // log-sum-exp and delta in a buffer of their own.
+  // log-sum-exp and delta in a buffer of their own (the dK kernel one per warpgroup).
   L.off_red = kind == 0 ? L.off_t : L.off_t + 2 * kRows * kTile * 2;
-  L.off_ring = kind == 0 ? L.off_t + 2 * kRows * kTile * 2 : L.off_red + 8192;
+  L.off_ring = kind == 0 ? L.off_t + 2 * kRows * kTile * 2 : L.off_red + (kind == 1 ? 16384 : 8192);
   const int avail = 225 * 1024 - L.off_ring;
   // Stage depth over stage size: the score / accumulation ring holds a stage for the dS product of the
   // unit in the softmax while the next units' score operands load, so with three stages a score operand
   // waited on the product two units back and the load latency surfaced in every unit.  The dP operands
   // therefore come as three 16 KB stages (one 64-column block of each of V and dY), leaving four or
   // more ring stages.
-  L.nsp = kind == 2 ? 0 : (kind == 1 ? kDpStages - 1 : kDpStages);
-  int rest = (avail - L.nsp * kDpStage) / kStage;
+  L.nsp = kind == 2 ? 0 : (kind == 1 ? kDpStages - 1 : kDpStagesQ);
+  const int dp_stage = kind == 0 ? kDpStageQ : kDpStage;
+  int rest = (avail - L.nsp * dp_stage) / kStage;
   if (rest > 2 * kMaxStages) rest = 2 * kMaxStages;
   // Two rings, each with its own producer and issuer: the score operands (run ahead as far as the two
   // score buffers allow) and the accumulation operands (held until the softmax hands over the unit's dS
   // or P tile).  The dV kernel's accumulation items are the four dY stages of a query tile.
-  L.nsq = kind == 2 ? (rest - 3 < 4 ? rest - 3 : 4) : 2;
+  L.nsq = kind == 2 ? (rest - 3 < 4 ? rest - 3 : 4) : kAccStages;
   if (L.nsq > kMaxStages) L.nsq = kMaxStages;
   L.nst = rest - L.nsq;
   if (L.nst > kMaxStages) L.nst = kMaxStages;
   L.off_qring = L.off_ring + L.nst * kStage;
   L.off_pring = L.off_qring + L.nsq * kStage;
-  L.smem = L.off_pring + L.nsp * kDpStage;
+  L.smem = L.off_pring + L.nsp * dp_stage;
   L.tmem_acc = 0;
   const int acc = kind == 2 ? D / 2 : L.W / 2;
   L.tmem_s = acc;
@@ -209,10 +223,12 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
     mbar_init(&dp_done, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 16);  // score tile read out of TMEM: each softmax warp of the pair
+      mbar_init(&s_free[i], 8);  // score tile read out of TMEM: each warp of the owning warpgroup, both CTAs
       mbar_init(&p_full[i], 2);
       mbar_init(&dp_full[i], 1);
-      mbar_init(&dp_free[i], 2);
+      // dP tile released by each softmax warp that read it, in both CTAs (with one map a key tile is one
+      // unit, read by one warpgroup)
+      mbar_init(&dp_free[i], maps == 1 ? 8 : 16);
       mbar_init(&ds_empty[i], 1);
     }
     fence_mbar_init();
@@ -317,14 +333,14 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
     bool ok = true;
     for (int g = 0; ok && g < dps; ++g) {
       const int y = (int)min((int64_t)b * p.T + (g % nj) * kTile + 64 * (int)rank, rowsBT - 1);
-      for (int cb = 0; cb < p.D / (64 * kDpBlocks); ++cb, ++it) {  // V rows of 64 keys, then dY rows
+      for (int cb = 0; cb < p.D / (64 * kDpBlocksQ); ++cb, ++it) {  // V rows of 64 keys, then dY rows
         const int st = it % L.nsp;
         if (!mbar_wait(&rp_empty[st], ((it / L.nsp) & 1u) ^ 1u, ab, 13)) { ok = false; break; }
-        if (rank == 0) mbar_arrive_expect_tx(&rp_full[st], 2 * kDpStage);
+        if (rank == 0) mbar_arrive_expect_tx(&rp_full[st], 2 * kDpStageQ);
         const uint32_t bar = mapa_shared(smem_u32(&rp_full[st]), 0);
-        uint8_t* dst = smem + L.off_pring + st * kDpStage;
-        tma_load_3d_pair(&tv, bar, dst, 0, y, cb * kDpBlocks);
-        tma_load_3d_pair(&tdy, bar, dst + kDpBlocks * kBox, 0, dy_row, cb * kDpBlocks);
+        uint8_t* dst = smem + L.off_pring + st * kDpStageQ;
+        tma_load_3d_pair(&tv, bar, dst, 0, y, cb * kDpBlocksQ);
+        tma_load_3d_pair(&tdy, bar, dst + kDpBlocksQ * kBox, 0, dy_row, cb * kDpBlocksQ);
       }
     }
     if (rank == 0)
@@ -340,14 +356,14 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
       if (g < 256) trace_at(ft, 4 * g);
       if (g >= 2 && !mbar_wait(&dp_free[db], ((g - 2) >> 1) & 1u, ab, 27)) break;
       if (g < 256) trace_at(ft, 4 * g + 1);
-      for (int cb = 0; cb < p.D / (64 * kDpBlocks); ++cb, ++it) {  // stage: [V blocks | dY blocks]
+      for (int cb = 0; cb < p.D / (64 * kDpBlocksQ); ++cb, ++it) {  // stage: [V blocks | dY blocks]
         const int st = it % L.nsp;
         if (!mbar_wait(&rp_full[st], (it / L.nsp) & 1u, ab, 28)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t sa = smem_u32(smem + L.off_pring + st * kDpStage);
-        for (int k = 0; k < 4 * kDpBlocks; ++k) {
+        const uint32_t sa = smem_u32(smem + L.off_pring + st * kDpStageQ);
+        for (int k = 0; k < 4 * kDpBlocksQ; ++k) {
           const uint32_t blk = (uint32_t)(k >> 2) * kBox + (k & 3) * 32;
-          const uint64_t ad = sdesc_sw128(sa + kDpBlocks * kBox + blk, 16, 1024);
+          const uint64_t ad = sdesc_sw128(sa + kDpBlocksQ * kBox + blk, 16, 1024);
           const uint64_t bd = sdesc_sw128(sa + blk, 16, 1024);
           mma_f16_ss<2>(tmem + L.tmem_p + db * (kTile / 2), ad, bd, idesc, (cb | k) ? 1u : 0u);
         }
@@ -454,8 +470,10 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
       mbar_wait_drain(&o_full, 0);
     }
   } else if ((warp >= 2 && warp < 6) || (warp >= kSoftmax2 && warp < kSoftmax2 + 4)) {
-    // ---------------------------------------------------------------- softmax + epilogue: two warpgroups,
-    // warps 2-5 take the first 32 of each thread's 64 key columns and warps 8-11 the other 32
+    // ---------------------------------------------------------------- softmax + epilogue: two warpgroups
+    // taking alternate units (warps 2-5 the even ones, 8-11 the odd ones), each thread all 64 key columns
+    // of its row half in two 32-column chunks, so that one unit's hand-off chain (dS stores, barrier,
+    // hand-over to the dQ issuer, the wait for a free dS tile) overlaps the other warpgroup's arithmetic
     const int wg = warp >= kSoftmax2 ? 1 : 0;
     const int quad = warp & 3;
     const int l = quad * 32 + lane;
@@ -466,7 +484,7 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
     const uint32_t pf_leader = mapa_shared(smem_u32(&p_full[0]), 0);
     const uint32_t df_leader = mapa_shared(smem_u32(&dp_free[0]), 0);
     const uint32_t sf_leader = mapa_shared(smem_u32(&s_free[0]), 0);
-    const bool arriver = (warp == 2 && lane == 0);
+    const bool arriver = (warp == 2 || warp == kSoftmax2) && lane == 0;  // one per warpgroup
     float* red = reinterpret_cast<float*>(smem + L.off_red);
     const float kLog2e = 1.4426950408889634f;
     const float gsc = rsqrtf((float)p.group);
@@ -488,13 +506,44 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
       }
     }
     bool ok = true;
-    for (int u = 0; u < U; ++u) {
+    // Whole-row delta_s at the end of the first sweep (two halves x two warpgroups), stored for the
+    // key-parallel kernels.  Both warpgroups come here once, after their last first-sweep unit; the
+    // buffer is the dS tiles' space, which no first-sweep unit writes.
+    auto sweep_end = [&]() {
+      for (int m = 0; m < maps; ++m) red[(m * 2 + wg) * 128 + l] = delta[m];
+      named_bar_sync(1, 256);
+      for (int m = 0; m < maps; ++m)
+        delta[m] = red[(m * 2) * 128 + l] + red[(m * 2) * 128 + (l ^ 64)] + red[(m * 2 + 1) * 128 + l] +
+                   red[(m * 2 + 1) * 128 + (l ^ 64)];
+      named_bar_sync(1, 256);
+      for (int m = 0; m < maps; ++m) {
+        if (ok && live && half == 0 && wg == 0) p.delta[((int64_t)b * maps + m) * p.T + t] = delta[m];
+        if (p.dweight && wg == 0) {
+          float w = (ok && live && half == 0) ? delta[m] : 0.f;
+          for (int o = 16; o; o >>= 1) w += __shfl_xor_sync(0xffffffffu, w, o);
+          if (p.scalar_part) {
+            if (lane == 0) p.scalar_part[((size_t)blockIdx.x * 4 + quad) * maps + m] = w;
+          } else if (lane == 0 && w != 0.f) {
+            atomicAdd(p.dweight + m, w);
+          }
+        }
+      }
+    };
+    bool reduced = p.delta_given != 0;
+    // Warpgroup wg takes units wg, wg + 2, ...: score buffer u & 1 and dS tile v & 1 are its own, so it
+    // waits for their phases in order; the dP tile of a key tile is read by both warpgroups.
+    for (int u = wg; u < U; u += 2) {
+      if (!reduced && u >= per_sweep) {
+        sweep_end();
+        reduced = true;
+      }
       const int sb = u & 1, s = unit_s(u), j = unit_j(u), g = unit_g(u);
       const bool form_ds = u >= u_dq;
       const int v = u - u_dq;
       if (arriver && u < 512) trace_at(ft, 5120 + 4 * u);
       if (ok) ok = mbar_wait(&s_full[sb], (u >> 1) & 1u, ab, 32);
-      if (ok && s == 0) ok = mbar_wait(&dp_full[g & 1], (g >> 1) & 1u, ab, 35);
+      // the first unit of key tile g this warpgroup takes (maps s = 0 and 1, or the tile's only unit)
+      if (ok && s < 2) ok = mbar_wait(&dp_full[g & 1], (g >> 1) & 1u, ab, 35);
       if (arriver && u < 512) trace_at(ft, 5121 + 4 * u);
       ok = __all_sync(0xffffffffu, ok);
       const bool entered = ok;  // the unit's TMEM reads (and s_free arrival) happen only then
@@ -504,19 +553,27 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
         // this map's row constants in registers (the per-map arrays live in local memory)
         const float sc2 = scale2[s], ls2 = lse2[s], dl = delta[s], al = alpha[s];
         float dsum = 0.f, a_acc = 0.f, b_acc = 0.f, c_acc = 0.f;
-        {
-          const int ch = wg;
+        const int kb = j * kTile + half * 64;  // first key column of this thread's 64
+        int lim_row = p.T - kb;
+        if (p.causal) lim_row = min(lim_row, t - kb + 1);
+        if (!live) lim_row = 0;
+        bool free_tile = true;
+#pragma unroll 1
+        for (int ch = 0; ch < 2; ++ch) {
           float sv[32], pv[32];
           tmem_ld32(tmem + lane_base + L.tmem_s + sb * (kTile / 2) + ch * 32, sv);
           tmem_ld32(tmem + lane_base + L.tmem_p + (g & 1) * (kTile / 2) + ch * 32, pv);
           tmem_wait_ld();
-          tc_fence_before();  // the score buffer is free for the next product while this warp computes
-          __syncwarp();
-          if (lane == 0) mbar_arrive_cluster_relaxed(sf_leader + sb * 8);
-          const int k0 = j * kTile + half * 64 + ch * 32;
-          int lim = p.T - k0;
-          if (p.causal) lim = min(lim, t - k0 + 1);
-          if (!live) lim = 0;
+          if (ch == 1) {  // the score buffer is free for the unit after next while this warp computes
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+              mbar_arrive_cluster_relaxed(sf_leader + sb * 8);
+              // this warpgroup's last unit of key tile g: this warp is done with the dP buffer
+              if (s + 2 >= maps) mbar_arrive_cluster_relaxed(df_leader + (g & 1) * 8);
+            }
+          }
+          const int lim = lim_row - ch * 32;
           uint32_t packed[16];
           // masked columns get probability 0 (a select, so any value the exponential takes there is
           // discarded; tiles below the diagonal skip the selects); two partial sums shorten the chains
@@ -554,6 +611,18 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
             a_acc += a0 + a1;
             b_acc += b0 + b1;
             c_acc += c0 + c1;
+            if (ch == 0) {
+              // the dS tile of this warpgroup's previous unit must have been read by its dQ product:
+              // waited for only now, so the arithmetic above overlaps that product
+              free_tile = v < 2 || mbar_wait(&ds_empty[v & 1], ((v - 2) >> 1) & 1u, ab, 33);
+              free_tile = __all_sync(0xffffffffu, free_tile);
+            }
+            if (free_tile) {
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                st_shared_v4(dsa + half * kBox + sw128_offset(r, ch * 4 + e), packed[4 * e], packed[4 * e + 1],
+                             packed[4 * e + 2], packed[4 * e + 3]);
+            }
           } else {
             float d0 = 0.f, d1 = 0.f;
             if (lim >= 32) {
@@ -572,21 +641,8 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
             }
             dsum += d0 + d1;
           }
-          if (form_ds) {
-            // the dS tile of unit v - 2 must have been read by its dQ product: waited for only now, so the
-            // arithmetic above overlaps that product
-            bool free_tile = v < 2 || mbar_wait(&ds_empty[v & 1], ((v - 2) >> 1) & 1u, ab, 33);
-            free_tile = __all_sync(0xffffffffu, free_tile);
-            if (free_tile) {
-#pragma unroll
-              for (int e = 0; e < 4; ++e)
-                st_shared_v4(dsa + half * kBox + sw128_offset(r, ch * 4 + e), packed[4 * e], packed[4 * e + 1],
-                             packed[4 * e + 2], packed[4 * e + 3]);
-            } else {
-              ok = false;
-            }
-          }
         }
+        if (!free_tile) ok = false;
         if (form_ds) {
           sA[s] += a_acc;
           sB[s] += b_acc;
@@ -597,40 +653,24 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
         }
       }
       if (arriver && u < 512) trace_at(ft, 5122 + 4 * u);
-      if (!entered && lane == 0) mbar_arrive_cluster_relaxed(sf_leader + sb * 8);  // aborted unit: counts stay whole
-      tc_fence_before();
-      named_bar_sync(1, 256);
-      if (arriver) {
-        if (u < 512) trace_at(ft, 5123 + 4 * u);
-        // dS tile v handed to the dQ issuer (second sweep only: phase v / 2 of barrier v % 2, which the
-        // issuer waits for in order; the softmax cannot run two phases ahead, as unit v + 2 first waits
-        // for the product of unit v)
-        if (form_ds) mbar_arrive_remote(pf_leader + (v & 1) * 8);
-        if (s == maps - 1) mbar_arrive_cluster_relaxed(df_leader + (g & 1) * 8);
+      if (!entered && lane == 0) {  // aborted unit: counts stay whole
+        mbar_arrive_cluster_relaxed(sf_leader + sb * 8);
+        if (s + 2 >= maps) mbar_arrive_cluster_relaxed(df_leader + (g & 1) * 8);
       }
-      if (!p.delta_given && u == per_sweep - 1) {
-        // end of the first sweep: whole-row delta_s (two halves x two warpgroups), stored for the
-        // key-parallel kernels
-        for (int m = 0; m < maps; ++m) red[(m * 2 + wg) * 128 + l] = delta[m];
-        named_bar_sync(1, 256);
-        for (int m = 0; m < maps; ++m)
-          delta[m] = red[(m * 2) * 128 + l] + red[(m * 2) * 128 + (l ^ 64)] + red[(m * 2 + 1) * 128 + l] +
-                     red[(m * 2 + 1) * 128 + (l ^ 64)];
-        named_bar_sync(1, 256);
-        for (int m = 0; m < maps; ++m) {
-          if (ok && live && half == 0 && wg == 0) p.delta[((int64_t)b * maps + m) * p.T + t] = delta[m];
-          if (p.dweight && wg == 0) {
-            float w = (ok && live && half == 0) ? delta[m] : 0.f;
-            for (int o = 16; o; o >>= 1) w += __shfl_xor_sync(0xffffffffu, w, o);
-            if (p.scalar_part) {
-              if (lane == 0) p.scalar_part[((size_t)blockIdx.x * 4 + quad) * maps + m] = w;
-            } else if (lane == 0 && w != 0.f) {
-              atomicAdd(p.dweight + m, w);
-            }
-          }
+      if (form_ds) {
+        // dS tile v handed to the dQ issuer once all four warps stored their rows (phase v / 2 of barrier
+        // v % 2, which the issuer waits for in order; this warpgroup cannot run two phases ahead, as its
+        // next unit on that tile first waits for the product of unit v).  First-sweep units hand nothing
+        // over, so the warps of a warpgroup pass them without a barrier.
+        tc_fence_before();
+        named_bar_sync(3 + wg, 128);
+        if (arriver) {
+          if (u < 512) trace_at(ft, 5123 + 4 * u);
+          mbar_arrive_remote(pf_leader + (v & 1) * 8);
         }
       }
     }
+    if (!reduced) sweep_end();
     // ---- d gamma_s from each row's own sums (both warpgroups, both halves), then the dQ epilogue.  The
     // reduction buffer shares the dS tiles' space: every product (the last dQ ones read those tiles) has
     // completed first.
@@ -764,12 +804,15 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
     mbar_init(&dp_done, 1);
     for (int i = 0; i < kNSB; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 16);  // score tile read out of TMEM: each softmax warp of the pair
+      // score tile read out of TMEM: each warp of the owning warpgroup (dK) or of both (dV), both CTAs
+      mbar_init(&s_free[i], kDK ? 8 : 16);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&p_full[i], 2);
       mbar_init(&dp_full[i], 1);
-      mbar_init(&dp_free[i], 2);
+      // dP^T tile released by each softmax warp that read it, in both CTAs (one map: a query tile is one
+      // unit, read by one warpgroup)
+      mbar_init(&dp_free[i], maps == 1 ? 8 : 16);
       mbar_init(&t_empty[i], 1);
     }
     fence_mbar_init();
@@ -1018,8 +1061,9 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
       mbar_wait_drain(&o_full, 0);
     }
   } else if ((warp >= 2 && warp < 6) || (warp >= kSoftmax2 && warp < kSoftmax2 + 4)) {
-    // ---------------------------------------------------------------- softmax + epilogue: two warpgroups,
-    // warps 2-5 take the first 32 of each thread's 64 query columns and warps 8-11 the other 32
+    // ---------------------------------------------------------------- softmax + epilogue: two warpgroups
+    // (warps 2-5 and 8-11); dK: alternate units, dV: warps 2-5 the first 32 of each thread's 64 query
+    // columns and warps 8-11 the other 32
     const int wg = warp >= kSoftmax2 ? 1 : 0;
     const int quad = warp & 3;
     const int l = quad * 32 + lane;
@@ -1030,8 +1074,9 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
     const uint32_t pf_leader = mapa_shared(smem_u32(&p_full[0]), 0);
     const uint32_t df_leader = mapa_shared(smem_u32(&dp_free[0]), 0);
     const uint32_t sf_leader = mapa_shared(smem_u32(&s_free[0]), 0);
-    const bool arriver = (warp == 2 && lane == 0);
-    float* red = reinterpret_cast<float*>(smem + L.off_red);  // [tile parity][2][maps][128]: lse2, delta
+    const bool arriver = lane == 0 && (warp == 2 || (kDK && warp == kSoftmax2));  // dK: one per warpgroup
+    // [warpgroup (dK)][tile parity][2][maps][128]: lse2, alpha * delta
+    float* red = reinterpret_cast<float*>(smem + L.off_red);
     const float kLog2e = 1.4426950408889634f;
     const float gsc = rsqrtf((float)p.group);
     float scale2[kMaxMaps], alpha[kMaxMaps];
@@ -1042,11 +1087,19 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
     }
     float pm[kDK ? 1 : 32];
     bool ok = true;
-    for (int u = 0; u < U; ++u) {
+    // dK: warpgroup wg takes units wg, wg + 2, ... (score buffer u & 1 and dS^T tile u & 1 are its own, so
+    // it waits for their phases in order), each thread all 64 query columns of its row half in two
+    // 32-column chunks, with its own copy of the staged row constants; the dP^T tile of a query tile is
+    // read by both warpgroups.  dV: both warpgroups take every unit, 32 of a thread's 64 columns each
+    // (the mixed probabilities of a query tile sum over all its maps).
+    constexpr bool kPing = kDK;
+    constexpr int kChunks = kPing ? 2 : 1;
+    for (int u = kPing ? wg : 0; u < U; u += kPing ? 2 : 1) {
       const int sb = u % kNSB, s = unit_s(u), g = unit_g(u);
       const int qt = (i0 + g) * kTile;
-      float* rt = red + (g & 1) * (2 * kMaxMaps * 128);
-      if (s == 0 && wg == 0) {  // stage this query tile's log-sum-exp (and delta) of every map
+      float* rt = red + (kPing ? wg * (4 * kMaxMaps * 128) : 0) + (g & 1) * (2 * kMaxMaps * 128);
+      const bool first = kPing ? s < 2 : s == 0;  // this warpgroup's first unit of query tile g
+      if (first && (kPing || wg == 0)) {  // stage this query tile's log-sum-exp (and delta) of every map
         for (int m = 0; m < maps; ++m) {
           const int q = qt + l;
           const bool qv = q < p.T;
@@ -1055,8 +1108,8 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
         }
       }
       if (ok) ok = mbar_wait(&s_full[sb], (u / kNSB) & 1u, ab, 32);
-      if (ok && kDK && s == 0) ok = mbar_wait(&dp_full[g & 1], (g >> 1) & 1u, ab, 35);
-      if (s == 0) named_bar_sync(1, 256);  // staged lse / delta visible
+      if (ok && kDK && first) ok = mbar_wait(&dp_full[g & 1], (g >> 1) & 1u, ab, 35);
+      if (first) named_bar_sync(kPing ? 3 + wg : 1, kPing ? 128 : 256);  // staged lse / delta visible
       ok = __all_sync(0xffffffffu, ok);
       const bool entered = ok;  // the unit's TMEM reads (and s_free arrival) happen only then
       if (ok) {
@@ -1065,15 +1118,23 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
         const float sc2 = scale2[s], al = alpha[s];
         const float* lse_row = rt + s * 128;
         const float* delta_row = rt + (kMaxMaps + s) * 128;
-        {
-          const int ch = wg;
+        bool free_tile = true;
+#pragma unroll 1
+        for (int c = 0; c < kChunks; ++c) {
+          const int ch = kPing ? c : wg;
           float sv[32], dpv[32];
           tmem_ld32(tmem + lane_base + L.tmem_s + sb * (kTile / 2) + ch * 32, sv);
           if (kDK) tmem_ld32(tmem + lane_base + L.tmem_p + (g & 1) * (kTile / 2) + ch * 32, dpv);
           tmem_wait_ld();
-          tc_fence_before();  // the score buffer is free for the next product while this warp computes
-          __syncwarp();
-          if (lane == 0) mbar_arrive_cluster_relaxed(sf_leader + sb * 8);
+          if (c == kChunks - 1) {  // the score buffer is free for the next product while this warp computes
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+              mbar_arrive_cluster_relaxed(sf_leader + sb * 8);
+              // dK: this warpgroup's last unit of query tile g: this warp is done with the dP^T buffer
+              if (kDK && s + 2 >= maps) mbar_arrive_cluster_relaxed(df_leader + (g & 1) * 8);
+            }
+          }
           const int qc0 = half * 64 + ch * 32;  // query column inside the tile
           // valid query columns e: lo <= e < hi (causal: queries at or after this key)
           const int hi = live ? p.T - (qt + qc0) : 0;
@@ -1090,15 +1151,15 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
               if (kDK) ad = ald4[e4];
               const float lsv[4] = {ls.x, ls.y, ls.z, ls.w}, adv[4] = {ad.x, ad.y, ad.z, ad.w};
 #pragma unroll
-              for (int c = 0; c < 4; c += 2) {
-                const int e = e4 * 4 + c;
-                float p0 = ex2(fmaf(sv[e], sc2, -lsv[c])), p1 = ex2(fmaf(sv[e + 1], sc2, -lsv[c + 1]));
+              for (int cc = 0; cc < 4; cc += 2) {
+                const int e = e4 * 4 + cc;
+                float p0 = ex2(fmaf(sv[e], sc2, -lsv[cc])), p1 = ex2(fmaf(sv[e + 1], sc2, -lsv[cc + 1]));
                 if (masked) {
                   p0 = (e >= lo && e < hi) ? p0 : 0.f;
                   p1 = (e + 1 >= lo && e + 1 < hi) ? p1 : 0.f;
                 }
                 if (kDK) {  // dS^T = P^T (alpha dP^T - alpha delta)
-                  packed[e / 2] = pack2<T>(p0 * fmaf(al, dpv[e], -adv[c]), p1 * fmaf(al, dpv[e + 1], -adv[c + 1]));
+                  packed[e / 2] = pack2<T>(p0 * fmaf(al, dpv[e], -adv[cc]), p1 * fmaf(al, dpv[e + 1], -adv[cc + 1]));
                 } else {
                   pm[e] = s == 0 ? al * p0 : fmaf(al, p0, pm[e]);
                   pm[e + 1] = s == 0 ? al * p1 : fmaf(al, p1, pm[e + 1]);
@@ -1110,31 +1171,36 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
           if (lo <= 0 && hi >= 32) body(std::false_type{});
           else body(std::true_type{});
           if (kDK || s == maps - 1) {
-            // the tile buffer written here must have been read by the product two uses ago (dK: unit u - 2,
-            // dV: query tile g - 2); waited for only now, so the arithmetic above overlaps that product
-            bool free_tile = true;
-            if (kDK && u >= 2) free_tile = mbar_wait(&t_empty[u & 1], ((u - 2) >> 1) & 1u, ab, 33);
-            if (!kDK && g >= 2) free_tile = mbar_wait(&t_empty[g & 1], ((g - 2) >> 1) & 1u, ab, 33);
-            free_tile = __all_sync(0xffffffffu, free_tile);
+            // the tile buffer written here must have been read by the product two uses ago (dK: this
+            // warpgroup's previous unit, u - 2; dV: query tile g - 2); waited for only now, so the
+            // arithmetic above overlaps that product
+            if (c == 0) {
+              if (kDK && u >= 2) free_tile = mbar_wait(&t_empty[u & 1], ((u - 2) >> 1) & 1u, ab, 33);
+              if (!kDK && g >= 2) free_tile = mbar_wait(&t_empty[g & 1], ((g - 2) >> 1) & 1u, ab, 33);
+              free_tile = __all_sync(0xffffffffu, free_tile);
+            }
             if (free_tile) {
 #pragma unroll
               for (int e = 0; e < 4; ++e)
                 st_shared_v4(ta + half * kBox + sw128_offset(r, ch * 4 + e), packed[4 * e], packed[4 * e + 1],
                              packed[4 * e + 2], packed[4 * e + 3]);
-            } else {
-              ok = false;
             }
           }
         }
+        if (!free_tile) ok = false;
         if (kDK || s == maps - 1) fence_proxy_async();
       }
-      if (!entered && lane == 0) mbar_arrive_cluster_relaxed(sf_leader + sb * 8);  // aborted unit: counts stay whole
-      tc_fence_before();
-      named_bar_sync(1, 256);
-      if (arriver) {
-        if (kDK) mbar_arrive_remote(pf_leader + (u & 1) * 8);
-        else if (s == maps - 1) mbar_arrive_remote(pf_leader + (g & 1) * 8);
-        if (kDK && s == maps - 1) mbar_arrive_cluster_relaxed(df_leader + (g & 1) * 8);
+      if (!entered && lane == 0) {  // aborted unit: counts stay whole
+        mbar_arrive_cluster_relaxed(sf_leader + sb * 8);
+        if (kDK && s + 2 >= maps) mbar_arrive_cluster_relaxed(df_leader + (g & 1) * 8);
+      }
+      // the unit's tile (dK: dS^T every unit; dV: the mixed P^T after a query tile's last map) handed to
+      // the accumulation issuer once every warp stored its rows; dV units before the last map hand nothing
+      // over and pass without a barrier
+      if (kDK || s == maps - 1) {
+        tc_fence_before();
+        named_bar_sync(kPing ? 3 + wg : 1, kPing ? 128 : 256);
+        if (arriver) mbar_arrive_remote(pf_leader + (kDK ? (u & 1) : (g & 1)) * 8);
       }
     }
     if (wg == 0 && ok) ok = mbar_wait(&o_full, 0, ab, 34);
@@ -1295,9 +1361,10 @@ extern "C" int da_attn_bwd_mixed(const void* q, int64_t q_rows, int64_t q_base, 
   if (rc) return rc;
   rc = make_tmap_2d(&tk128, k, tdt, 2, R, k_rows, (uint64_t)R * 2, 64, 128);
   if (rc) return rc;
-  CUtensorMap tdy2;
+  CUtensorMap tdy2, tvq, tdyq;
   {  // V and dY: [B*T, D] as (64-column block, row, block index); a box is 64 rows x kDpBlocks blocks for
-     // the dP stages, 64 rows x 2 blocks for the dV kernel's dY operand
+     // the dK kernel's dP stages, 64 rows x kDpBlocksQ blocks for the dQ kernel's, 64 rows x 2 blocks for
+     // the dV kernel's dY operand
     const uint64_t dims[3] = {64, (uint64_t)B * T, (uint64_t)D / 64};
     const uint64_t strides[2] = {(uint64_t)D * 2, 128};
     const uint32_t box[3] = {64, 64, kDpBlocks};
@@ -1308,6 +1375,13 @@ extern "C" int da_attn_bwd_mixed(const void* q, int64_t q_rows, int64_t q_base, 
     const uint32_t box2[3] = {64, 64, 2};
     rc = make_tmap_blocks(&tdy2, dy, tdt, 2, 3, dims, strides, box2);
     if (rc) return rc;
+    // the dQ kernel's dP stages: kDpBlocksQ blocks of each of V and dY per box (the kernel's stage layout
+    // and transaction count assume exactly this box)
+    const uint32_t boxq[3] = {64, 64, kDpBlocksQ};
+    rc = make_tmap_blocks(&tvq, v, tdt, 2, 3, dims, strides, boxq);
+    if (rc) return rc;
+    rc = make_tmap_blocks(&tdyq, dy, tdt, 2, 3, dims, strides, boxq);
+    if (rc) return rc;
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int pairs = B * ((T + kTile - 1) / kTile);
@@ -1315,8 +1389,8 @@ extern "C" int da_attn_bwd_mixed(const void* q, int64_t q_rows, int64_t q_base, 
   // the query-parallel kernel runs first: without a given delta it produces it for the other two
   if (dq || dscale || !delta_given) {
     const Layout L = make_layout(0, maps, group, R, D);
-    rc = bf16 ? launch_pair(dq_mixed_kernel<__nv_bfloat16>, L, pairs, tq, tk, tv, tdy, tk128, p, st)
-              : launch_pair(dq_mixed_kernel<__half>, L, pairs, tq, tk, tv, tdy, tk128, p, st);
+    rc = bf16 ? launch_pair(dq_mixed_kernel<__nv_bfloat16>, L, pairs, tq, tk, tvq, tdyq, tk128, p, st)
+              : launch_pair(dq_mixed_kernel<__half>, L, pairs, tq, tk, tvq, tdyq, tk128, p, st);
     if (rc) return rc;
     if (p.scalar_part) {
       rc = launch_kernel(scalar_reduce_kernel, dim3((unsigned)maps, 2, 1), dim3(256, 1, 1), 0, st, false,
