@@ -196,10 +196,13 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
   const int t0 = (tiles - 1 - pair / p.B) * kTile;
   const int nj = p.causal ? t0 / kTile + 1 : tiles;
   const int maps = p.maps;
-  const int sweeps = p.delta_given ? 1 : 2;
+  // Without a given delta the first sweep computes it; with neither dQ nor d gamma requested that sweep
+  // is all the launch does (the dK kernel can then start while another launch forms dQ).
+  const bool delta_only = !p.delta_given && !p.dq && !p.dscale;
+  const int sweeps = (p.delta_given || delta_only) ? 1 : 2;
   const int per_sweep = nj * maps;
   const int U = sweeps * per_sweep;
-  const int u_dq = (sweeps - 1) * per_sweep;  // first unit that forms dS and accumulates dQ
+  const int u_dq = delta_only ? U : (sweeps - 1) * per_sweep;  // first unit that forms dS and accumulates dQ
   const MapRows qm{p.q_rows, p.q_base, p.q_sb, p.q_sbr}, km{p.k_rows, p.k_base, p.k_sb, p.k_sbr};
   const int64_t rowsBT = (int64_t)p.B * p.T;
   Abort ab{&abort_flag, p.status};

@@ -796,11 +796,60 @@ def _attention_backward(q: RowMap, k: RowMap, v: Tensor, dy: Tensor, batch: int,
     # per-(CTA, warp) partial sums of d gamma / d alpha, added in a fixed order by the library
     part_bytes = int(_lib.lib().da_attn_bwd_workspace_size(batch, length, maps))
     part = torch.empty(part_bytes, dtype=torch.uint8, device=dev)
-    call("da_attn_bwd_mixed", q.tensor.data_ptr(), q.rows, q.base, q.sb, q.sbr, k.tensor.data_ptr(), k.rows, k.base,
-         k.sb, k.sbr, v.data_ptr(), dy.data_ptr(), batch, length, r, d, maps, group, ctypes_addressof(b0),
-         int(causal), dtype_code(q.tensor.dtype), scales.data_ptr(), ptr(weights), lse.data_ptr(), delta.data_ptr(),
-         int(delta_given), ptr(dq), ptr(dk), ptr(dv), ptr(dscale), ptr(dweight), part.data_ptr(), part_bytes,
-         ws.status.data_ptr(), stream_ptr(dev))
+
+    def launch(dq_, dk_, dv_, dscale_, dweight_, given, stream) -> None:
+        call("da_attn_bwd_mixed", q.tensor.data_ptr(), q.rows, q.base, q.sb, q.sbr, k.tensor.data_ptr(), k.rows,
+             k.base, k.sb, k.sbr, v.data_ptr(), dy.data_ptr(), batch, length, r, d, maps, group, ctypes_addressof(b0),
+             int(causal), dtype_code(q.tensor.dtype), scales.data_ptr(), ptr(weights), lse.data_ptr(),
+             delta.data_ptr(), int(given), ptr(dq_), ptr(dk_), ptr(dv_), ptr(dscale_), ptr(dweight_),
+             part.data_ptr(), part_bytes, ws.status.data_ptr(), stream)
+
+    # Small batches (one kernel's CTAs, two per pair, fit on the SMs at once) leave most SMs idle in
+    # each of the three kernels, so independent launches run side by side on two more streams (fork
+    # and join on stream events, which graph capture keeps): dV, which reads neither delta nor anything
+    # the others write, beside everything; without a given delta, the delta sweep runs alone first
+    # (with d alpha), then the dK kernel on a side stream beside a single-sweep dQ launch that takes
+    # the stored delta.  The library's status word stays this stream's.
+    pairs = batch * ((length + 127) // 128)
+    if dv is not None and (dq is not None or dk is not None) and 2 * pairs <= _sm_count(dev):
+        main = torch.cuda.current_stream(dev)
+        side_v, side_k = _side_streams_of(dev)
+        side_v.wait_stream(main)
+        launch(None, None, dv, None, None, True, side_v.cuda_stream)
+        if not delta_given:
+            launch(None, None, None, None, dweight, False, main.cuda_stream)  # delta (and d alpha) only
+            dweight, delta_given = None, True
+        if dk is not None and (dq is not None or dscale is not None):
+            side_k.wait_stream(main)
+            launch(None, dk, None, None, None, True, side_k.cuda_stream)
+            launch(dq, None, None, dscale, dweight, delta_given, main.cuda_stream)
+            main.wait_stream(side_k)
+        else:
+            launch(dq, dk, None, dscale, dweight, delta_given, main.cuda_stream)
+        main.wait_stream(side_v)
+        return
+    launch(dq, dk, dv, dscale, dweight, delta_given, stream_ptr(dev))
+
+
+_side_streams: dict[int, tuple[torch.cuda.Stream, torch.cuda.Stream]] = {}
+_sm_counts: dict[int, int] = {}
+
+
+def _side_streams_of(dev: torch.device) -> tuple[torch.cuda.Stream, torch.cuda.Stream]:
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    st = _side_streams.get(idx)
+    if st is None:
+        d = torch.device("cuda", idx)
+        st = _side_streams.setdefault(idx, (torch.cuda.Stream(d), torch.cuda.Stream(d)))
+    return st
+
+
+def _sm_count(dev: torch.device) -> int:
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    n = _sm_counts.get(idx)
+    if n is None:
+        n = _sm_counts.setdefault(idx, torch.cuda.get_device_properties(idx).multi_processor_count)
+    return n
 
 
 def ctypes_int_array(n: int):
