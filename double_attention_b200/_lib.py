@@ -49,6 +49,9 @@ SIGNATURES: dict[str, list] = {
     "da_gemm": [_p, _i64, _i32, _p, _i64, _i32, _p, _i64, _i64, _i64, _i64, _i32, _i32, _i32, _p, _p],
     "da_attn_fwd": [_p, _i64, _i64, _i64, _i64, _p, _i64, _i64, _i64, _i64, _p, _i32, _i32, _i32, _i32, _i32, _i32,
                     _p, _i32, _i32, _p, _p, _p, _f32, _p, _p, _p, _p],
+    "da_attn_fwd_workspace_size": [_i32, _i32, _i32, _i32],  # returns int64 (set below)
+    "da_attn_fwd_ws": [_p, _i64, _i64, _i64, _i64, _p, _i64, _i64, _i64, _i64, _p, _i32, _i32, _i32, _i32, _i32, _i32,
+                       _p, _i32, _i32, _p, _p, _p, _f32, _p, _p, _p, _i64, _p, _p],
     "da_attn_bwd_delta": [_p, _p, _i64, _i32, _i32, _p, _p],
     "da_gemm_ex": [_p, _i64, _p, _i64, _i32, _i64, _p, _i64, _p, _i64, _i64, _p, _i64, _i64, _i64, _i32, _p, _i32,
                    _p, _i64, _p, _p],
@@ -118,6 +121,7 @@ def lib() -> ctypes.CDLL:
             handle.da_route_bwd_workspace_size.argtypes = [_i64, _i32, _i64, _i64]
             handle.da_route_bwd_workspace_size.restype = ctypes.c_int64
             handle.da_attn_bwd_workspace_size.restype = ctypes.c_int64
+            handle.da_attn_fwd_workspace_size.restype = ctypes.c_int64
             handle.da_gemm_splitk_workspace_elems.restype = ctypes.c_int64
             handle.da_col_sum_workspace_elems.restype = ctypes.c_int64
             handle.da_kernel_launches.argtypes = []

@@ -33,7 +33,13 @@ struct AttnFwdArgs {
   void* y;                   // [B, T, D] output (dtype)
   float* lse;                // [B, maps, T] natural-log sum of exp(gamma_s q.k) per map
   int* status;
+  float* part_sum = nullptr;  // key-split workspace (mixed maps, few query tiles), or null: no split
+  float* part_o = nullptr;
 };
+
+// Key shares per query tile of the mixed-map forward: 2 when the tiles' CTAs (two per pair) fit on the
+// SMs at once (the longest tile's chain of score products is then halved), else 1.
+inline int key_split(int maps, long pairs, int sms) { return (maps > 1 && 2 * pairs <= sms) ? 2 : 1; }
 
 int attn_fwd(const AttnFwdArgs& a, cudaStream_t st);
 

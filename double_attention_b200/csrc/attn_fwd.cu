@@ -145,6 +145,13 @@ struct FwdParams {
   int B, T, R, D, maps, group, causal;
   int dsplit, Dp;  // value columns split over dsplit pairs of Dp columns each
   int coarse;      // tile plan for many query tiles per SM (make_layout)
+  // Key-range split of the mixed path (few query tiles): ksplit pairs per query tile, each over its share
+  // of the key tiles.  phase 0: both sweeps in one launch (ksplit 1); 1: the first sweep only, writing
+  // each row's partial sums and maxima of every map to part_sum [ksplit][2][B][maps][T]; 2: the second
+  // sweep from the combined partials, writing the partial outputs to part_o [ksplit][B][T][D] (fp32).
+  int ksplit, phase;
+  float* part_sum;
+  float* part_o;
   int branch0[kMaxMaps];
   const float* scales;
   const float* weights;
@@ -175,22 +182,31 @@ __global__ void __launch_bounds__(fwd_threads<kLat>(), 1) attn_fwd_kernel(const 
   const int tiles = (p.T + 127) / 128;
   const int dslice = (blockIdx.x / 2) % p.dsplit;  // the slices of one query tile run side by side
   const int dcol0 = dslice * p.Dp;
-  const int pair = blockIdx.x / (2 * p.dsplit);
+  const int khalf = (blockIdx.x / (2 * p.dsplit)) % p.ksplit;  // this pair's share of the key tiles
+  const int pair = blockIdx.x / (2 * p.dsplit * p.ksplit);
   // heaviest (latest) query tiles of every sequence first, then the next heaviest: causal work per pair
   // varies with the tile, and this order (longest first across the whole grid) keeps the last wave short
   const int b = pair % p.B;
   const int t0 = (tiles - 1 - pair / p.B) * 128;
   const int nk = L.nk;
   const int nk_all = (p.T + nk - 1) / nk;
-  const int nj = p.causal ? min(nk_all, (t0 + 127) / nk + 1) : nk_all;
+  const int nj_all = p.causal ? min(nk_all, (t0 + 127) / nk + 1) : nk_all;
+  // key tiles [jb, jb + nj) of this pair's share (ksplit 1: all of them; the last share may be empty)
+  const int jspan = (nj_all + p.ksplit - 1) / p.ksplit;
+  const int jb = khalf * jspan;
+  const int nj = max(0, min(nj_all, jb + jspan) - jb);
   const int maps = kMix ? p.maps : 1;
   // Key tiles are visited from a per-pair starting tile (any order gives the same sums: the softmax
   // offset is fixed), so the pairs of one sequence that run side by side read different key and
   // value lines instead of all requesting the same ones at once.
-  const int rot = (blockIdx.x / 2) % nj;
+  const int rot = nj > 0 ? (blockIdx.x / 2) % nj : 0;
+  auto ktile = [&](int j) { return jb + (j + rot) % nj; };  // key tile of the j-th visit
+  const bool sweep1 = kMix && p.phase != 2;                // the log-sum-exp sweep runs here
+  const bool sweep2 = !kMix || p.phase != 1;               // the probability sweep and P.V run here
   const int sweep_units = nj * maps;
-  const int U = kMix ? 2 * sweep_units : sweep_units;  // S units: (sweep, key tile, map)
-  const int u2 = kMix ? sweep_units : 0;               // first unit of the P.V sweep
+  const int U = (sweep1 ? sweep_units : 0) + (sweep2 ? sweep_units : 0);  // S units: (sweep, key tile, map)
+  const int u2 = sweep1 ? sweep_units : 0;                 // first unit of the P.V sweep
+  const int nv = sweep2 ? nj : 0;                          // P.V key tiles
   Abort ab{&abort_flag, p.status};
   // post-mortem per-unit timeline of the first pair (debug trace only)
   int* ft = (p.trace && blockIdx.x < 2) ? p.trace + blockIdx.x * 4096 : nullptr;
@@ -259,7 +275,7 @@ __global__ void __launch_bounds__(fwd_threads<kLat>(), 1) attn_fwd_kernel(const 
           if (!mbar_wait(&k_empty[st], ((kx / L.kslots) & 1u) ^ 1u, ab, 11)) { ok = false; break; }
           if (rank == 0) mbar_arrive_expect_tx(&k_full[st], 2 * box_bytes);
           const int gi = c / L.rpb, kb = c % L.rpb;  // kbb divides rpb: a box never spans two branches
-          const int64_t row = p.k_base + b * p.k_sb + (p.branch0[s] + gi) * p.k_sbr + ((j + rot) % nj) * nk + (int)rank * (nk / 2);
+          const int64_t row = p.k_base + b * p.k_sb + (p.branch0[s] + gi) * p.k_sbr + ktile(j) * nk + (int)rank * (nk / 2);
           tma_load_3d_pair(&tk, mapa_shared(smem_u32(&k_full[st]), 0), smem + L.off_k + st * box_bytes, 0,
                            (int)min(row, p.k_rows - 1), kb);
         }
@@ -279,7 +295,7 @@ __global__ void __launch_bounds__(fwd_threads<kLat>(), 1) attn_fwd_kernel(const 
       prefetch_tmap(&tv);
       int vc = 0;
       const int64_t vrows = (int64_t)p.B * p.T;
-      for (int v = 0; v < nj; ++v) {
+      for (int v = 0; v < nv; ++v) {
         bool ok = true;
         for (int c = 0; c < nk / 64; ++c, ++vc) {
           if (vc % kProd != pi) continue;
@@ -287,7 +303,7 @@ __global__ void __launch_bounds__(fwd_threads<kLat>(), 1) attn_fwd_kernel(const 
           if (!mbar_wait(&v_empty[st], ((vc / L.nvs) & 1u) ^ 1u, ab, 12)) { ok = false; break; }
           if (rank == 0) mbar_arrive_expect_tx(&v_full[st], 2 * L.v_stage);
           const uint32_t vf = mapa_shared(smem_u32(&v_full[st]), 0);
-          const int y = (int)min((int64_t)b * p.T + ((v + rot) % nj) * nk + c * 64, vrows - 1);
+          const int y = (int)min((int64_t)b * p.T + ktile(v) * nk + c * 64, vrows - 1);
           // one box: 64 keys x this CTA's per column blocks of each of the npv value groups
           tma_load_4d_pair(&tv, vf, smem + L.off_v + st * L.v_stage, 0, y, (int)rank * L.per, dcol0 / L.nc);
         }
@@ -344,7 +360,7 @@ __global__ void __launch_bounds__(fwd_threads<kLat>(), 1) attn_fwd_kernel(const 
       } else {
         // P.V per key tile, as soon as its probability tile and value rows are in shared memory.
         int vc = 0;
-        for (int v = 0; ok && v < nj; ++v) {
+        for (int v = 0; ok && v < nv; ++v) {
           const int pb = v % L.npb;
           if (v < 256) trace_at(ft, 2048 + 4 * v);
           if (!mbar_wait(&pv_full[pb], (v / L.npb) & 1u, ab, 24)) { ok = false; break; }
@@ -388,7 +404,8 @@ __global__ void __launch_bounds__(fwd_threads<kLat>(), 1) attn_fwd_kernel(const 
     const float kLog2e = 1.4426950408889634f;
     const int hc = nk / 2;  // key columns per thread per tile
 
-    bool ok = mbar_wait(&s_full[0], 0, ab, 31);
+    // (a pair with an empty key share has no score unit: it writes zero partials below)
+    bool ok = U == 0 || mbar_wait(&s_full[0], 0, ab, 31);
     float scale2[kMaxMaps], bound2[kMaxMaps], off2[kMaxMaps], sum[kMaxMaps], mx[kMaxMaps];
     const float gsc = rsqrtf((float)p.group);
 #pragma unroll
@@ -440,7 +457,7 @@ __global__ void __launch_bounds__(fwd_threads<kLat>(), 1) attn_fwd_kernel(const 
 
     // ---- sweep 1 (several maps): exact per-map log-sum-exp
     if (kMix) {
-      for (int u = 0; u < sweep_units; ++u) {
+      for (int u = 0; sweep1 && u < sweep_units; ++u) {
         const int j = u / maps, s = u % maps, sb = u % L.nsb;
         if (ok && u > 0) ok = mbar_wait(&s_full[sb], (u / L.nsb) & 1u, ab, 32);
         ok = __all_sync(0xffffffffu, ok);
@@ -453,7 +470,7 @@ __global__ void __launch_bounds__(fwd_threads<kLat>(), 1) attn_fwd_kernel(const 
             float v[32];
             tmem_ld32(tmem + lane_base + L.tmem_s + (uint32_t)(sb * L.s_cols + ch * 32), v);
             tmem_wait_ld();
-            const int lim = key_limit(((j + rot) % nj) * nk + half * hc + ch * 32);
+            const int lim = key_limit(ktile(j) * nk + half * hc + ch * 32);
 #pragma unroll
             for (int i = 0; i < 32; ++i)
               if (i < lim) {
@@ -467,14 +484,37 @@ __global__ void __launch_bounds__(fwd_threads<kLat>(), 1) attn_fwd_kernel(const 
         }
         finish_unit(u, -1);
       }
-      for (int s = 0; s < maps; ++s) {
-        red[s * 128 + l] = sum[s];
-        red[(4 + s) * 128 + l] = mx[s];
+      if (sweep1) {
+        for (int s = 0; s < maps; ++s) {
+          red[s * 128 + l] = sum[s];
+          red[(4 + s) * 128 + l] = mx[s];
+        }
+        named_bar_sync(1, 128);
+        for (int s = 0; s < maps; ++s) {
+          sum[s] += red[s * 128 + (l ^ 64)];
+          mx[s] = fmaxf(mx[s], red[(4 + s) * 128 + (l ^ 64)]);
+        }
       }
-      named_bar_sync(1, 128);
+      const bool live_row = t < p.T;
+      const size_t pstride = (size_t)p.B * p.maps * p.T;  // one [B][maps][T] plane of the partials
+      if (p.phase == 1 && live_row && half == 0) {       // this key share's row sums and maxima
+        for (int s = 0; s < maps; ++s) {
+          const size_t i = ((size_t)b * p.maps + s) * p.T + t;
+          p.part_sum[(size_t)(2 * khalf) * pstride + i] = sum[s];
+          p.part_sum[(size_t)(2 * khalf + 1) * pstride + i] = mx[s];
+        }
+      }
+      if (p.phase == 2)  // every key share's sums, added in share order
+        for (int s = 0; s < maps; ++s) {
+          const size_t i = ((size_t)b * p.maps + s) * p.T + (live_row ? t : 0);
+          sum[s] = 0.f;
+          mx[s] = -INFINITY;
+          for (int h = 0; h < p.ksplit; ++h) {
+            sum[s] += p.part_sum[(size_t)(2 * h) * pstride + i];
+            mx[s] = fmaxf(mx[s], p.part_sum[(size_t)(2 * h + 1) * pstride + i]);
+          }
+        }
       for (int s = 0; s < maps; ++s) {
-        sum[s] += red[s * 128 + (l ^ 64)];
-        mx[s] = fmaxf(mx[s], red[(4 + s) * 128 + (l ^ 64)]);
         const float alpha = p.weights ? p.weights[s] : 1.f;
         const float lse2 = bound2[s] + log2f(sum[s]);
         off2[s] = lse2 - log2f(alpha);   // P term = 2^(S*scale2 - off2) = alpha * softmax
@@ -486,7 +526,7 @@ __global__ void __launch_bounds__(fwd_threads<kLat>(), 1) attn_fwd_kernel(const 
     // ---- probability tiles for P.V
     float psum = 0.f, pmx = -INFINITY;
     float pm[kMix ? 64 : 1];
-    for (int v = 0; v < nj; ++v) {
+    for (int v = 0; v < nv; ++v) {
       const int pb = v % L.npb;
       const uint32_t pa = smem_u32(smem + L.off_p + pb * L.p_bytes);
       for (int s = 0; s < maps; ++s) {
@@ -502,7 +542,7 @@ __global__ void __launch_bounds__(fwd_threads<kLat>(), 1) attn_fwd_kernel(const 
             float sv[32];
             tmem_ld32(tmem + lane_base + L.tmem_s + (uint32_t)(sb * L.s_cols + ch * 32), sv);
             tmem_wait_ld();
-            const int k0 = ((v + rot) % nj) * nk + half * hc + ch * 32;
+            const int k0 = ktile(v) * nk + half * hc + ch * 32;
             const int lim = key_limit(k0);
             if constexpr (kMix) {
 #pragma unroll
@@ -575,15 +615,24 @@ __global__ void __launch_bounds__(fwd_threads<kLat>(), 1) attn_fwd_kernel(const 
     }
     tc_fence_after();
     const bool live = t < p.T;
-    if (ok) {
+    if (ok && p.phase != 1) {  // (the first-sweep launch of a key split has written its partials)
       const size_t row_off = ((size_t)b * p.T + (live ? t : 0)) * p.D;
       for (int i = 0; i < L.npv; ++i) {
         const int col0 = dcol0 + i * L.nc + half * (L.nc / 2);
         for (int c = 0; c < L.nc / 2; c += 32) {
           float o[32];
-          tmem_ld32(tmem + lane_base + (uint32_t)(i * (L.nc / 2) + c), o);
-          tmem_wait_ld();
-          if (live) {
+          if (nv > 0) {
+            tmem_ld32(tmem + lane_base + (uint32_t)(i * (L.nc / 2) + c), o);
+            tmem_wait_ld();
+          } else {  // an empty key share adds nothing
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = 0.f;
+          }
+          if (live && p.phase == 2) {  // this share's part of the (already normalised) output, fp32
+            float4* dst = reinterpret_cast<float4*>(p.part_o + (size_t)khalf * p.B * p.T * p.D + row_off + col0 + c);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) dst[e] = make_float4(o[4 * e], o[4 * e + 1], o[4 * e + 2], o[4 * e + 3]);
+          } else if (live) {
             uint32_t w[16];
 #pragma unroll
             for (int e = 0; e < 16; ++e) w[e] = pack2<T>(o[2 * e] * inv_l, o[2 * e + 1] * inv_l);
@@ -593,7 +642,8 @@ __global__ void __launch_bounds__(fwd_threads<kLat>(), 1) attn_fwd_kernel(const 
           }
         }
       }
-      if (live && half == 0 && dslice == 0) {  // every slice forms the same row statistics
+      // every value slice and key share forms the same row statistics: the first writes them
+      if (live && half == 0 && dslice == 0 && khalf == 0) {
         const float kLn2 = 0.6931471805599453f;
         for (int s = 0; s < maps; ++s) {
           p.lse[((size_t)b * p.maps + s) * p.T + t] = bound2[s] * kLn2;
@@ -621,10 +671,30 @@ inline int value_split(long pairs, int D, int sms) {
   return split;
 }
 
+// Sum of the key shares' fp32 partial outputs, added in share order, in the output dtype.
+template <typename T>
+__global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ part_o, int ksplit, int64_t n, T* y) {
+  grid_dependency_wait();
+  grid_launch_dependents();
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x * 4;
+  for (int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4; i < n; i += stride) {
+    float4 a = *reinterpret_cast<const float4*>(part_o + i);
+    for (int h = 1; h < ksplit; ++h) {
+      const float4 c = *reinterpret_cast<const float4*>(part_o + (size_t)h * n + i);
+      a.x += c.x;
+      a.y += c.y;
+      a.z += c.z;
+      a.w += c.w;
+    }
+    *reinterpret_cast<uint2*>(y + i) = make_uint2(pack2<T>(a.x, a.y), pack2<T>(a.z, a.w));
+  }
+}
+
 template <typename T, bool kMix>
 int launch(const AttnFwdArgs& a, cudaStream_t st) {
   const long pairs = (long)a.B * ((a.T + 127) / 128);
-  const int dsplit = value_split(pairs, a.D, sm_count());
+  const int ksplit = (kMix && a.part_sum) ? key_split(a.maps, pairs, sm_count()) : 1;
+  const int dsplit = ksplit > 1 ? 1 : value_split(pairs, a.D, sm_count());
   const int Dp = a.D / dsplit;
   const bool coarse = pairs * dsplit >= sm_count();
   const Layout L = make_layout(a.maps, a.group, a.R, Dp, kMix, coarse);
@@ -667,6 +737,10 @@ int launch(const AttnFwdArgs& a, cudaStream_t st) {
   p.dsplit = dsplit;
   p.Dp = Dp;
   p.coarse = coarse ? 1 : 0;
+  p.ksplit = ksplit;
+  p.phase = 0;
+  p.part_sum = a.part_sum;
+  p.part_o = a.part_o;
   for (int s = 0; s < kMaxMaps; ++s) p.branch0[s] = a.branch0[s];
   p.scales = a.scales;
   p.weights = a.weights;
@@ -680,8 +754,18 @@ int launch(const AttnFwdArgs& a, cudaStream_t st) {
   const int smem = L.smem + 1024;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return record_cuda_error();
-  return launch_kernel(kern, dim3((unsigned)(2 * pairs * dsplit), 1, 1),
-                       dim3(coarse ? fwd_threads<false>() : fwd_threads<true>(), 1, 1), smem, st, true, tq, tk, tv, p);
+  const dim3 grid((unsigned)(2 * pairs * dsplit * ksplit)), block(coarse ? fwd_threads<false>() : fwd_threads<true>());
+  if (ksplit == 1) return launch_kernel(kern, grid, block, smem, st, true, tq, tk, tv, p);
+  // key split: the first sweep over every share, then the second from the combined row sums, then the
+  // shares' outputs added
+  p.phase = 1;
+  if (int rc = launch_kernel(kern, grid, block, smem, st, true, tq, tk, tv, p)) return rc;
+  p.phase = 2;
+  if (int rc = launch_kernel(kern, grid, block, smem, st, true, tq, tk, tv, p)) return rc;
+  const int64_t n = (int64_t)a.B * a.T * a.D;
+  const int64_t blocks = (n / 4 + 255) / 256;
+  return launch_kernel(combine_kernel<T>, dim3((unsigned)(blocks < 4 * sm_count() ? blocks : 4 * sm_count())),
+                       dim3(256), 0, st, false, (const float*)a.part_o, ksplit, n, reinterpret_cast<T*>(a.y));
 }
 
 int attn_fwd(const AttnFwdArgs& a, cudaStream_t st) {
@@ -693,12 +777,21 @@ int attn_fwd(const AttnFwdArgs& a, cudaStream_t st) {
 }  // namespace attn
 }  // namespace da
 
-extern "C" int da_attn_fwd(const void* q, int64_t q_rows, int64_t q_base, int64_t q_sb, int64_t q_sbr,
-                           const void* k, int64_t k_rows, int64_t k_base, int64_t k_sb, int64_t k_sbr,
-                           const void* v, int B, int T, int R, int D, int maps, int group, const int* branch0,
-                           int causal, int dtype, const float* scales, const float* weights,
-                           const float* key_norm_max, float key_norm_bound, void* y, float* lse, int* status,
-                           void* stream) {
+extern "C" int64_t da_attn_fwd_workspace_size(int B, int T, int maps, int D) {
+  if (B <= 0 || T <= 0 || maps < 1 || maps > da::attn::kMaxMaps || D <= 0) return -1;
+  const long pairs = (long)B * ((T + 127) / 128);
+  const int ks = da::attn::key_split(maps, pairs, da::sm_count());
+  if (ks == 1) return 0;
+  return ((int64_t)2 * ks * B * maps * T + (int64_t)ks * B * T * D) * (int64_t)sizeof(float);
+}
+
+namespace {
+
+int attn_fwd_entry(const void* q, int64_t q_rows, int64_t q_base, int64_t q_sb, int64_t q_sbr, const void* k,
+                   int64_t k_rows, int64_t k_base, int64_t k_sb, int64_t k_sbr, const void* v, int B, int T, int R,
+                   int D, int maps, int group, const int* branch0, int causal, int dtype, const float* scales,
+                   const float* weights, const float* key_norm_max, float key_norm_bound, void* y, float* lse,
+                   void* workspace, int64_t workspace_bytes, int* status, void* stream) {
   using namespace da;
   if (!q || !k || !v || !branch0 || !scales || !y || !lse || !status) return DA_ERR_NULL;
   if (int rc = bind_device(q)) return rc;
@@ -733,5 +826,39 @@ extern "C" int da_attn_fwd(const void* q, int64_t q_rows, int64_t q_base, int64_
   a.y = y;
   a.lse = lse;
   a.status = status;
+  if (workspace) {  // a key split runs when the size query asks for a workspace
+    const int64_t need = da_attn_fwd_workspace_size(B, T, maps, D);
+    if (need > 0) {
+      if (workspace_bytes < need) return DA_ERR_WORKSPACE;
+      if (reinterpret_cast<uintptr_t>(workspace) & 15) return DA_ERR_ALIGN;
+      const int ks = attn::key_split(maps, (long)B * ((T + 127) / 128), sm_count());
+      a.part_sum = static_cast<float*>(workspace);
+      a.part_o = a.part_sum + (size_t)2 * ks * B * maps * T;
+    }
+  }
   return attn::attn_fwd(a, static_cast<cudaStream_t>(stream));
+}
+
+}  // namespace
+
+extern "C" int da_attn_fwd(const void* q, int64_t q_rows, int64_t q_base, int64_t q_sb, int64_t q_sbr,
+                           const void* k, int64_t k_rows, int64_t k_base, int64_t k_sb, int64_t k_sbr,
+                           const void* v, int B, int T, int R, int D, int maps, int group, const int* branch0,
+                           int causal, int dtype, const float* scales, const float* weights,
+                           const float* key_norm_max, float key_norm_bound, void* y, float* lse, int* status,
+                           void* stream) {
+  return attn_fwd_entry(q, q_rows, q_base, q_sb, q_sbr, k, k_rows, k_base, k_sb, k_sbr, v, B, T, R, D, maps, group,
+                        branch0, causal, dtype, scales, weights, key_norm_max, key_norm_bound, y, lse, nullptr, 0,
+                        status, stream);
+}
+
+extern "C" int da_attn_fwd_ws(const void* q, int64_t q_rows, int64_t q_base, int64_t q_sb, int64_t q_sbr,
+                              const void* k, int64_t k_rows, int64_t k_base, int64_t k_sb, int64_t k_sbr,
+                              const void* v, int B, int T, int R, int D, int maps, int group, const int* branch0,
+                              int causal, int dtype, const float* scales, const float* weights,
+                              const float* key_norm_max, float key_norm_bound, void* y, float* lse, void* workspace,
+                              int64_t workspace_bytes, int* status, void* stream) {
+  return attn_fwd_entry(q, q_rows, q_base, q_sb, q_sbr, k, k_rows, k_base, k_sb, k_sbr, v, B, T, R, D, maps, group,
+                        branch0, causal, dtype, scales, weights, key_norm_max, key_norm_bound, y, lse, workspace,
+                        workspace_bytes, status, stream);
 }

@@ -757,6 +757,16 @@ def _attention_forward(q: RowMap, k: RowMap, v: Tensor, batch: int, length: int,
     kn = None if key_norm_max is None else key_norm_max.detach().float().contiguous()
     b0 = (ctypes_int_array(MAX_MAPS))(*(branch0 + [0] * (MAX_MAPS - len(branch0))))
     b0_addr = ctypes_addressof(b0)
+    # several maps over few query tiles: the library splits every tile's key range over two CTA pairs and
+    # asks for a workspace for the partial row sums and outputs
+    ws_bytes = int(_lib.lib().da_attn_fwd_workspace_size(batch, length, maps, d)) if maps > 1 else 0
+    if ws_bytes > 0:
+        work = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+        call("da_attn_fwd_ws", q.tensor.data_ptr(), q.rows, q.base, q.sb, q.sbr, k.tensor.data_ptr(), k.rows, k.base,
+             k.sb, k.sbr, v16.data_ptr(), batch, length, r, d, maps, group, b0_addr, int(causal),
+             dtype_code(q.tensor.dtype), sc.data_ptr(), ptr(wt), ptr(kn), float(key_norm_bound), y.data_ptr(),
+             lse.data_ptr(), work.data_ptr(), ws_bytes, ws.status.data_ptr(), stream_ptr(dev))
+        return y, lse
     call("da_attn_fwd", q.tensor.data_ptr(), q.rows, q.base, q.sb, q.sbr, k.tensor.data_ptr(), k.rows, k.base, k.sb,
          k.sbr, v16.data_ptr(), batch, length, r, d, maps, group, b0_addr, int(causal), dtype_code(q.tensor.dtype),
          sc.data_ptr(), ptr(wt), ptr(kn), float(key_norm_bound), y.data_ptr(), lse.data_ptr(), ws.status.data_ptr(),

@@ -262,6 +262,25 @@ DA_API int da_attn_fwd(const void* q, int64_t q_rows, int64_t q_base, int64_t q_
                        const float* scales, const float* weights, const float* key_norm_max, float key_norm_bound,
                        void* y, float* lse, int* status, void* stream);
 
+/* Bytes of device workspace da_attn_fwd_ws uses for these sizes: 0 when it
+ * runs exactly as da_attn_fwd, -1 for invalid sizes.  With several maps and
+ * few query tiles (their CTAs, two per pair, fit on the SMs of the current
+ * device at once) the key range of every query tile is split over two pairs:
+ * a first launch writes each share's per-map row sums, a second forms the
+ * probabilities from the combined sums and each share's fp32 output, a third
+ * adds the shares' outputs (in share order, so results repeat bit for bit). */
+DA_API int64_t da_attn_fwd_workspace_size(int B, int T, int maps, int D);
+
+/* da_attn_fwd with a caller-owned device workspace (16-byte aligned, at least
+ * da_attn_fwd_workspace_size bytes, DA_ERR_WORKSPACE otherwise; ignored when
+ * that size is 0).  Same reference interface and results as da_attn_fwd. */
+DA_API int da_attn_fwd_ws(const void* q, int64_t q_rows, int64_t q_base, int64_t q_sb, int64_t q_sbr, const void* k,
+                          int64_t k_rows, int64_t k_base, int64_t k_sb, int64_t k_sbr, const void* v, int B, int T,
+                          int R, int D, int maps, int group, const int* branch0, int causal, int dtype,
+                          const float* scales, const float* weights, const float* key_norm_max,
+                          float key_norm_bound, void* y, float* lse, void* workspace, int64_t workspace_bytes,
+                          int* status, void* stream);
+
 /* ---- outer routed attention, backward -----------------------------------
  * Replaces the preprocess kernel of _routed_attention_triton_backward
  * (triton_kernels.py:2093-2160): delta[r] = <dy[r, :], y[r, :]> over `rows`

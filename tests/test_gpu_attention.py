@@ -102,3 +102,42 @@ def test_attention_lse_matches() -> None:
     s = torch.einsum("bstr,bsur->bstu", zq, zk) * 16.0
     s = s.masked_fill(torch.ones(200, 200, dtype=torch.bool).triu(1), float("-inf"))
     torch.testing.assert_close(lse.cpu(), torch.logsumexp(s, -1), atol=2e-3, rtol=1e-4)
+
+
+def test_key_split_forward_matches_one_launch() -> None:
+    """Several maps over few query tiles (qk4-s4 at B2 T2048): the key range of each tile is split over two
+    CTA pairs (partial row sums, then partial outputs added in share order).  The result matches the
+    single-launch kernel (da_attn_fwd, no workspace) to fp32 reassociation and repeats bit for bit."""
+    from double_attention_b200 import _lib
+
+    dev, dtype = torch.device("cuda"), torch.bfloat16
+    h = maps = 4
+    batch, length, r, d = 2, 2048, 128, 512
+    assert int(_lib.lib().da_attn_fwd_workspace_size(batch, length, maps, d)) > 0  # the split runs here
+    routed = _routed(h, batch, length, r, dtype, seed=11).to(dev)
+    g = torch.Generator().manual_seed(12)
+    value = torch.randn(batch, length, d, generator=g).to(dtype).to(dev)
+    scales = torch.full((maps,), 16.0, device=dev)
+    mix = torch.softmax(torch.randn(maps, generator=g), 0).to(dev)
+    flat = routed.view(-1, r)
+    group, branch0 = ops._map_layout(h, maps)
+    qmap = ops.RowMap(flat, 0, length, batch * length)
+    kmap = ops.RowMap(flat, h * batch * length, length, batch * length)
+    runs = [ops._attention_forward(qmap, kmap, value, batch, length, r, maps, group, branch0, True, scales, mix,
+                                   None, 1.0, dtype) for _ in range(2)]
+    # the same op in one launch
+    y1 = torch.empty(batch, length, d, dtype=dtype, device=dev)
+    lse1 = torch.empty(batch, maps, length, dtype=torch.float32, device=dev)
+    b0 = (ops.ctypes_int_array(ops.MAX_MAPS))(*(branch0 + [0] * (ops.MAX_MAPS - len(branch0))))
+    status = torch.zeros(2, dtype=torch.int32, device=dev)
+    ops.call("da_attn_fwd", flat.data_ptr(), qmap.rows, qmap.base, qmap.sb, qmap.sbr, flat.data_ptr(), kmap.rows,
+             kmap.base, kmap.sb, kmap.sbr, value.data_ptr(), batch, length, r, d, maps, group, ops.ctypes_addressof(b0),
+             1, ops.dtype_code(dtype), scales.float().contiguous().data_ptr(), mix.float().contiguous().data_ptr(), 0,
+             1.0, y1.data_ptr(), lse1.data_ptr(), status.data_ptr(), ops.stream_ptr(dev))
+    torch.cuda.synchronize()
+    assert int(status[0]) == 0 and ops.device_status(dev) == 0
+    (ya, la), (yb, lb) = runs
+    assert torch.equal(ya, yb) and torch.equal(la, lb)
+    assert (ya.float() - y1.float()).abs().max().item() <= 1e-2
+    assert _cos(ya.float(), y1.float()) >= 0.99999
+    assert (la - lse1).abs().max().item() <= 1e-4
