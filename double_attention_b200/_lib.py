@@ -69,6 +69,8 @@ SIGNATURES: dict[str, list] = {
     "da_attn_bwd_workspace_size": [_i32, _i32, _i32],  # returns int64 (set below)
     "da_attn_bwd_mixed": [_p, _i64, _i64, _i64, _i64, _p, _i64, _i64, _i64, _i64, _p, _p, _i32, _i32, _i32, _i32,
                           _i32, _i32, _p, _i32, _i32, _p, _p, _p, _p, _i32, _p, _p, _p, _p, _p, _p, _i64, _p, _p],
+    "da_attn_bwd_mixed_ow": [_p, _i64, _i64, _i64, _i64, _p, _i64, _i64, _i64, _i64, _p, _p, _i32, _i32, _i32, _i32,
+                          _i32, _i32, _p, _i32, _i32, _p, _p, _p, _p, _i32, _p, _p, _p, _p, _p, _p, _i64, _p, _p],
     "da_selftest_mma": [_i32, _i32, _i32, _i32, _p, _p, _p, _p, _p],
     "da_selftest_wait_timeout": [_i64, _i32, _p, _p, _p],
     "da_route_var_weights": [_p, _i64, _i32, _p, _i64, _i32, _i32, _i32, _f32, _f32, _p, _f32, _p, _p, _p],

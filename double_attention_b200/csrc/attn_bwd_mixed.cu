@@ -77,9 +77,10 @@ struct Params {
   const float* lse;      // [B, maps, T] natural log
   float* delta;          // [B, maps, T]: read, or written by the dQ kernel's first sweep
   int delta_given;
-  float* dq;             // fp32 [q_rows, R], +=
-  float* dk;             // fp32 [k_rows, R], +=
-  float* dv;             // fp32 [B*T, D], +=
+  float* dq;             // fp32 [q_rows, R], +=  (overwrite: [q_rows, R] in the input dtype, =)
+  float* dk;             // fp32 [k_rows, R], +=  (overwrite: as dq)
+  float* dv;             // fp32 [B*T, D], +=     (overwrite: [B*T, D] in the input dtype, =)
+  int overwrite;         // every gradient row has one writer: store it in the input dtype
   float* dscale;         // [maps] d gamma_s, += (may be null)
   float* dweight;        // [maps] d alpha_s, += (dQ kernel with the first sweep; may be null)
   float* scalar_part;    // [2, 2 * pairs, 4, maps]: per-(CTA, warp) partial sums of d alpha_s and d gamma_s,
@@ -165,6 +166,31 @@ DA_DEV void load_map_chunk(const CUtensorMap* tm, const MapRows& m, const Params
     const int mb = cc * 2 + bx, gi = mb / (p.R / 64), x = (mb % (p.R / 64)) * 64;
     const int64_t row = row_of(m.base, m.sb, m.sbr, b, p.branch0[s] + gi, t);
     tma_load_2d_pair(tm, bar, dst + bx * kBox, x, (int)min(row, m.rows - 1));
+  }
+}
+
+// 32 consecutive gradient values of one row: added to the fp32 accumulator, or (overwrite) stored in
+// the input dtype.
+template <typename T>
+DA_DEV void store_grad32(float* acc, int64_t off, const float* v, float scale, bool overwrite) {
+  if (overwrite) {
+    uint32_t w[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) w[e] = pack2<T>(scale * v[2 * e], scale * v[2 * e + 1]);
+    uint4* d = reinterpret_cast<uint4*>(reinterpret_cast<T*>(acc) + off);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) d[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
+    return;
+  }
+  float* dst = acc + off;
+#pragma unroll
+  for (int e = 0; e < 32; e += 4) {
+    float4 o = *reinterpret_cast<float4*>(dst + e);
+    o.x += scale * v[e];
+    o.y += scale * v[e + 1];
+    o.z += scale * v[e + 2];
+    o.w += scale * v[e + 3];
+    *reinterpret_cast<float4*>(dst + e) = o;
   }
 }
 
@@ -732,16 +758,7 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
               const int col = ins * L.ncol + half * (L.ncol / 2) + c;  // map-local column, one branch
               const int gi = col / p.R;
               const int64_t row = row_of(qm.base, qm.sb, qm.sbr, b, p.branch0[m] + gi, t);
-              float* dst = p.dq + row * p.R + (col % p.R);
-#pragma unroll
-              for (int e = 0; e < 32; e += 4) {
-                float4 o = *reinterpret_cast<float4*>(dst + e);
-                o.x += gamma * vv[e];
-                o.y += gamma * vv[e + 1];
-                o.z += gamma * vv[e + 2];
-                o.w += gamma * vv[e + 3];
-                *reinterpret_cast<float4*>(dst + e) = o;
-              }
+              store_grad32<T>(p.dq, row * p.R + (col % p.R), vv, gamma, p.overwrite != 0);
             }
           }
       }
@@ -1221,16 +1238,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
               const int col = ins * L.ncol + half * (L.ncol / 2) + c;
               const int gi = col / p.R;
               const int64_t row = row_of(km.base, km.sb, km.sbr, b, p.branch0[m] + gi, key);
-              float* dst = p.dk + row * p.R + (col % p.R);
-#pragma unroll
-              for (int e = 0; e < 32; e += 4) {
-                float4 o = *reinterpret_cast<float4*>(dst + e);
-                o.x += gamma * vv[e];
-                o.y += gamma * vv[e + 1];
-                o.z += gamma * vv[e + 2];
-                o.w += gamma * vv[e + 3];
-                *reinterpret_cast<float4*>(dst + e) = o;
-              }
+              store_grad32<T>(p.dk, row * p.R + (col % p.R), vv, gamma, p.overwrite != 0);
             }
           }
       }
@@ -1241,18 +1249,9 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
           float vv[32];
           tmem_ld32(tmem + lane_base + L.tmem_acc + ins * (dn / 2) + c, vv);
           tmem_wait_ld();
-          if (live) {
-            float* dst = p.dv + ((int64_t)b * p.T + key) * p.D + ins * dn + half * (dn / 2) + c;
-#pragma unroll
-            for (int e = 0; e < 32; e += 4) {
-              float4 o = *reinterpret_cast<float4*>(dst + e);
-              o.x += vv[e];
-              o.y += vv[e + 1];
-              o.z += vv[e + 2];
-              o.w += vv[e + 3];
-              *reinterpret_cast<float4*>(dst + e) = o;
-            }
-          }
+          if (live)
+            store_grad32<T>(p.dv, ((int64_t)b * p.T + key) * p.D + ins * dn + half * (dn / 2) + c, vv, 1.f,
+                            p.overwrite != 0);
         }
     }
   }
@@ -1305,13 +1304,14 @@ extern "C" int64_t da_attn_bwd_workspace_size(int B, int T, int maps) {
   return 2 * (2 * pairs * 4) * maps * (int64_t)sizeof(float);
 }
 
-extern "C" int da_attn_bwd_mixed(const void* q, int64_t q_rows, int64_t q_base, int64_t q_sb, int64_t q_sbr,
-                                 const void* k, int64_t k_rows, int64_t k_base, int64_t k_sb, int64_t k_sbr,
-                                 const void* v, const void* dy, int B, int T, int R, int D, int maps, int group,
-                                 const int* branch0, int causal, int dtype, const float* scales,
-                                 const float* weights, const float* lse, float* delta, int delta_given, float* dq,
-                                 float* dk, float* dv, float* dscale, float* dweight, void* workspace,
-                                 int64_t workspace_bytes, int* status, void* stream) {
+namespace {
+
+int attn_bwd_entry(const void* q, int64_t q_rows, int64_t q_base, int64_t q_sb, int64_t q_sbr, const void* k,
+                   int64_t k_rows, int64_t k_base, int64_t k_sb, int64_t k_sbr, const void* v, const void* dy, int B,
+                   int T, int R, int D, int maps, int group, const int* branch0, int causal, int dtype,
+                   const float* scales, const float* weights, const float* lse, float* delta, int delta_given,
+                   float* dq, float* dk, float* dv, float* dscale, float* dweight, void* workspace,
+                   int64_t workspace_bytes, int overwrite, int* status, void* stream) {
   using namespace da;
   using namespace da::attn::bwdm;
   if (!q || !k || !v || !dy || !branch0 || !scales || !lse || !delta || !status) return DA_ERR_NULL;
@@ -1343,7 +1343,12 @@ extern "C" int da_attn_bwd_mixed(const void* q, int64_t q_rows, int64_t q_base, 
   }
   if (q_base < 0 || k_base < 0) return DA_ERR_SHAPE;
   p.scales = scales; p.weights = weights; p.lse = lse; p.delta = delta; p.delta_given = delta_given;
+  if (overwrite)  // one writer per gradient row: the maps' branch ranges must not overlap
+    for (int s1 = 0; s1 < maps; ++s1)
+      for (int s2 = s1 + 1; s2 < maps; ++s2)
+        if (branch0[s1] < branch0[s2] + group && branch0[s2] < branch0[s1] + group) return DA_ERR_UNSUPPORTED;
   p.dq = dq; p.dk = dk; p.dv = dv; p.dscale = dscale; p.dweight = dweight; p.status = status;
+  p.overwrite = overwrite ? 1 : 0;
   const int npairs = B * ((T + kTile - 1) / kTile);
   const int64_t n_part = (int64_t)2 * npairs * 4;  // partials per map and kind: (CTA, softmax warp)
   p.scalar_part = nullptr;
@@ -1414,4 +1419,31 @@ extern "C" int da_attn_bwd_mixed(const void* q, int64_t q_rows, int64_t q_base, 
               : launch_pair(dkv_mixed_kernel<__half, false>, L, pairs, tq, tk, tv, tdy2, tq128, p, st);
   }
   return rc;
+}
+
+}  // namespace
+
+extern "C" int da_attn_bwd_mixed(const void* q, int64_t q_rows, int64_t q_base, int64_t q_sb, int64_t q_sbr,
+                                 const void* k, int64_t k_rows, int64_t k_base, int64_t k_sb, int64_t k_sbr,
+                                 const void* v, const void* dy, int B, int T, int R, int D, int maps, int group,
+                                 const int* branch0, int causal, int dtype, const float* scales,
+                                 const float* weights, const float* lse, float* delta, int delta_given, float* dq,
+                                 float* dk, float* dv, float* dscale, float* dweight, void* workspace,
+                                 int64_t workspace_bytes, int* status, void* stream) {
+  return attn_bwd_entry(q, q_rows, q_base, q_sb, q_sbr, k, k_rows, k_base, k_sb, k_sbr, v, dy, B, T, R, D, maps, group,
+                        branch0, causal, dtype, scales, weights, lse, delta, delta_given, dq, dk, dv, dscale, dweight,
+                        workspace, workspace_bytes, 0, status, stream);
+}
+
+extern "C" int da_attn_bwd_mixed_ow(const void* q, int64_t q_rows, int64_t q_base, int64_t q_sb, int64_t q_sbr,
+                                    const void* k, int64_t k_rows, int64_t k_base, int64_t k_sb, int64_t k_sbr,
+                                    const void* v, const void* dy, int B, int T, int R, int D, int maps, int group,
+                                    const int* branch0, int causal, int dtype, const float* scales,
+                                    const float* weights, const float* lse, float* delta, int delta_given, void* dq,
+                                    void* dk, void* dv, float* dscale, float* dweight, void* workspace,
+                                    int64_t workspace_bytes, int* status, void* stream) {
+  return attn_bwd_entry(q, q_rows, q_base, q_sb, q_sbr, k, k_rows, k_base, k_sb, k_sbr, v, dy, B, T, R, D, maps, group,
+                        branch0, causal, dtype, scales, weights, lse, delta, delta_given, static_cast<float*>(dq),
+                        static_cast<float*>(dk), static_cast<float*>(dv), dscale, dweight, workspace, workspace_bytes,
+                        1, status, stream);
 }

@@ -120,8 +120,9 @@ def make_case(kernel: str, config: int, device: torch.device, batch: int | None 
 
         return run, 4.0 * r * m * groups * rows
     if kernel == "attention_bwd":  # the whole attention backward op (delta pass, dQ, dK and dV launches)
-        # The op as _MixedAttention.backward runs it (fresh zeroed fp32 gradients, the delta pass for
-        # one map), called directly rather than through autograd so that it can be captured.
+        # The op as _MixedAttention.backward runs it (gradients stored once in the input dtype when the
+        # maps sit on disjoint branches, else fresh zeroed fp32 ones; the delta pass for one map), called
+        # directly rather than through autograd so that it can be captured.
         maps = cfg.outer_maps
         routed = F.normalize(torch.randn(2, h, batch, seq, r, generator=g), dim=-1).to(dtype).to(device)
         value = torch.randn(batch, seq, d, generator=g).to(dtype).to(device)
@@ -135,9 +136,12 @@ def make_case(kernel: str, config: int, device: torch.device, batch: int | None 
         y, lse = ops._attention_forward(qmap, kmap, value, batch, seq, r, maps, group, branch0, True, scales, mix,
                                         None, 1.0, dtype)
 
+        overwrite = h >= maps  # as the module path: gradients stored once in the input dtype
+
         def run():
-            droute = torch.zeros(flat.shape, dtype=torch.float32, device=device)
-            dv = torch.zeros(batch * seq, d, dtype=torch.float32, device=device)
+            alloc, gdt = (torch.empty, dtype) if overwrite else (torch.zeros, torch.float32)
+            droute = alloc(flat.shape, dtype=gdt, device=device)
+            dv = alloc(batch * seq, d, dtype=gdt, device=device)
             dscale = torch.zeros(maps, dtype=torch.float32, device=device)
             dweight = torch.zeros(maps, dtype=torch.float32, device=device) if mix is not None else None
             if maps == 1:
@@ -145,7 +149,7 @@ def make_case(kernel: str, config: int, device: torch.device, batch: int | None 
             else:
                 delta, given = torch.empty(batch, maps, seq, dtype=torch.float32, device=device), False
             ops._attention_backward(qmap, kmap, value, dy, batch, seq, r, maps, group, branch0, True, scales, mix,
-                                    lse, delta, given, droute, droute, dv, dscale, dweight)
+                                    lse, delta, given, droute, droute, dv, dscale, dweight, overwrite=overwrite)
 
         return run, float(batch) * seq * seq * (2 * cfg.outer_maps * r + 2 * d)
     if kernel == "projection":

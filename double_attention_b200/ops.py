@@ -794,8 +794,11 @@ def _attention_delta(dy: Tensor, y: Tensor) -> Tensor:
 def _attention_backward(q: RowMap, k: RowMap, v: Tensor, dy: Tensor, batch: int, length: int, r: int, maps: int,
                         group: int, branch0: list[int], causal: bool, scales: Tensor, weights: Tensor | None,
                         lse: Tensor, delta: Tensor, delta_given: bool, dq: Tensor | None, dk: Tensor | None,
-                        dv: Tensor | None, dscale: Tensor | None, dweight: Tensor | None) -> None:
-    """All maps of one attention in one call (da_attn_bwd_mixed): fp32 gradients accumulated in place."""
+                        dv: Tensor | None, dscale: Tensor | None, dweight: Tensor | None,
+                        overwrite: bool = False) -> None:
+    """All maps of one attention (da_attn_bwd_mixed): fp32 gradients accumulated in place, or with
+    `overwrite` (maps on disjoint branches, da_attn_bwd_mixed_ow) every produced row of dq, dk and dv
+    stored once in the input dtype."""
     d = v.shape[-1]
     _attention_bwd_supported(r, d, group)
     if maps * group * r > 512:
@@ -807,8 +810,10 @@ def _attention_backward(q: RowMap, k: RowMap, v: Tensor, dy: Tensor, batch: int,
     part_bytes = int(_lib.lib().da_attn_bwd_workspace_size(batch, length, maps))
     part = torch.empty(part_bytes, dtype=torch.uint8, device=dev)
 
+    entry = "da_attn_bwd_mixed_ow" if overwrite else "da_attn_bwd_mixed"
+
     def launch(dq_, dk_, dv_, dscale_, dweight_, given, stream) -> None:
-        call("da_attn_bwd_mixed", q.tensor.data_ptr(), q.rows, q.base, q.sb, q.sbr, k.tensor.data_ptr(), k.rows,
+        call(entry, q.tensor.data_ptr(), q.rows, q.base, q.sb, q.sbr, k.tensor.data_ptr(), k.rows,
              k.base, k.sb, k.sbr, v.data_ptr(), dy.data_ptr(), batch, length, r, d, maps, group, ctypes_addressof(b0),
              int(causal), dtype_code(q.tensor.dtype), scales.data_ptr(), ptr(weights), lse.data_ptr(),
              delta.data_ptr(), int(given), ptr(dq_), ptr(dk_), ptr(dv_), ptr(dscale_), ptr(dweight_),
@@ -913,8 +918,13 @@ class _MixedAttention(torch.autograd.Function):
         v16 = value.detach().to(dtype).contiguous()
         dy16 = dy.to(dtype).contiguous()
         need = ctx.needs_input_grad
-        droute = torch.zeros(flat.shape, dtype=torch.float32, device=flat.device) if need[0] else None
-        dv = torch.zeros(batch * length, d, dtype=torch.float32, device=flat.device) if need[1] else None
+        # maps on disjoint branches (H >= S): every routed and value row has one writer, which stores its
+        # gradient in the input dtype -- no zero-filled fp32 buffers, no casts afterwards
+        overwrite = h >= maps
+        gdt = dtype if overwrite else torch.float32
+        alloc = torch.empty if overwrite else torch.zeros
+        droute = alloc(flat.shape, dtype=gdt, device=flat.device) if need[0] else None
+        dv = alloc(batch * length, d, dtype=gdt, device=flat.device) if need[1] else None
         dscale = torch.zeros(maps, dtype=torch.float32, device=flat.device)
         sc = scales.detach().float().contiguous()
         wt = weights.detach().float().contiguous() if has_weights and maps > 1 else None
@@ -924,7 +934,8 @@ class _MixedAttention(torch.autograd.Function):
         else:  # computed exactly by the kernel's first sweep (the per-map outputs are never stored)
             delta, given = torch.empty(batch, maps, length, dtype=torch.float32, device=flat.device), False
         _attention_backward(qmap, kmap, v16, dy16, batch, length, r, maps, group, branch0, causal, sc, wt,
-                            lse.contiguous(), delta, given, droute, droute, dv, dscale if need[2] else None, dweight)
+                            lse.contiguous(), delta, given, droute, droute, dv, dscale if need[2] else None, dweight,
+                            overwrite=overwrite)
         g_routed = droute.view(routed.shape).to(dtype) if droute is not None else None
         g_value = dv.view(value.shape).to(value.dtype) if dv is not None else None
         g_scales = dscale.to(scales.dtype) if need[2] else None

@@ -317,6 +317,21 @@ DA_API int da_attn_bwd_mixed(const void* q, int64_t q_rows, int64_t q_base, int6
                              const float* lse, float* delta, int delta_given, float* dq, float* dk, float* dv,
                              float* dscale, float* dweight, void* workspace, int64_t workspace_bytes,
                              int* status, void* stream);
+
+/* da_attn_bwd_mixed writing dq, dk and dv once each instead of adding to fp32
+ * buffers: every gradient row the op produces is stored in the input dtype
+ * (dq, dk: [rows, R]; dv: [B*T, D]), rows it does not produce are left as they
+ * are.  Needs maps whose branch ranges do not overlap (each row then has one
+ * writer; DA_ERR_UNSUPPORTED otherwise).  Same reference interface as
+ * da_attn_bwd_mixed, without the zero-filled fp32 buffers and the casts the
+ * module path otherwise runs around it. */
+DA_API int da_attn_bwd_mixed_ow(const void* q, int64_t q_rows, int64_t q_base, int64_t q_sb, int64_t q_sbr,
+                                const void* k, int64_t k_rows, int64_t k_base, int64_t k_sb, int64_t k_sbr,
+                                const void* v, const void* dy, int B, int T, int R, int D, int maps, int group,
+                                const int* branch0, int causal, int dtype, const float* scales, const float* weights,
+                                const float* lse, float* delta, int delta_given, void* dq, void* dk, void* dv,
+                                float* dscale, float* dweight, void* workspace, int64_t workspace_bytes,
+                                int* status, void* stream);
 /* ---- dense GEMM (fused Q/K projection and its backward) -----------------
  * Replaces the cuBLAS GEMM of _project_query_key (modules.py:143-157,
  * F.linear(x, cat(W_q, W_k))) and its autograd backward.

@@ -171,3 +171,37 @@ def test_backward_is_repeatable() -> None:
     torch.cuda.synchronize()
     for name, a, b in zip(("routed", "value", "scales", "map weights"), grads[0], grads[1]):
         assert torch.equal(a, b), f"d {name} differs between two identical backward passes"
+
+
+@pytest.mark.parametrize("batch", [2, 32])
+def test_overwrite_gradients_equal_the_accumulated_ones(batch: int) -> None:
+    """da_attn_bwd_mixed_ow (maps on disjoint branches: each gradient row stored once in the input dtype)
+    against da_attn_bwd_mixed into zeroed fp32 buffers then cast: the same fp32 values rounded once, so
+    bit for bit equal -- at B2 T512 (the three-stream small-batch schedule) and B32 T512 (one stream)."""
+    dev, dtype = torch.device("cuda"), torch.bfloat16
+    h = maps = 4
+    length, r, d = 512, 128, 512
+    routed, value, dy, scales, mix = _inputs(h, maps, batch, length, r, d, 16.0, dtype, seed=5)
+    routed, value, dy = routed.to(dev), value.to(dev).to(dtype), dy.to(dev).to(dtype)
+    scales, mix = scales.to(dev).float(), mix.to(dev).float()
+    flat = routed.view(-1, r)
+    group, branch0 = ops._map_layout(h, maps)
+    qmap = ops.RowMap(flat, 0, length, batch * length)
+    kmap = ops.RowMap(flat, h * batch * length, length, batch * length)
+    _y, lse = ops._attention_forward(qmap, kmap, value, batch, length, r, maps, group, branch0, True, scales, mix,
+                                     None, 1.0, dtype)
+    out = {}
+    for overwrite in (False, True):
+        gdt, alloc = (dtype, torch.empty) if overwrite else (torch.float32, torch.zeros)
+        droute = alloc(flat.shape, dtype=gdt, device=dev)
+        dv = alloc(batch * length, d, dtype=gdt, device=dev)
+        dscale = torch.zeros(maps, dtype=torch.float32, device=dev)
+        dweight = torch.zeros(maps, dtype=torch.float32, device=dev)
+        delta = torch.empty(batch, maps, length, dtype=torch.float32, device=dev)
+        ops._attention_backward(qmap, kmap, value, dy, batch, length, r, maps, group, branch0, True, scales, mix,
+                                lse, delta, False, droute, droute, dv, dscale, dweight, overwrite=overwrite)
+        out[overwrite] = (droute.to(dtype), dv.to(dtype), dscale, dweight)
+    torch.cuda.synchronize()
+    assert ops.device_status(dev) == 0
+    for name, a, b in zip(("routed", "value", "scales", "map weights"), out[False], out[True]):
+        assert torch.equal(a, b), f"d {name}: overwrite and accumulate paths differ"
