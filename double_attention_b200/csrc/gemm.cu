@@ -26,6 +26,17 @@ struct Cfg {
   static constexpr int kSmem = kStages * (kABytes + kBBytes);
 };
 
+// The segmented GEMM runs two CTAs per SM: one CTA's product (a chain of dependent K = 16 instructions
+// into its TMEM accumulator) interleaves in the tensor pipe with the other's, and each CTA's epilogue
+// overlaps the other's K loop.  Two 48 KB stages each (128 x 256 tiles), 256 TMEM columns each.
+template <int kN>
+struct SegCfg {
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = kN * kBK * 2;
+  static constexpr int kStages = kN == 256 ? 2 : 3;
+  static constexpr int kSmem = kStages * (kABytes + kBBytes);
+};
+
 struct Params {
   int M, N, K;
   void* c;
@@ -271,12 +282,12 @@ struct SegParams {
 };
 
 template <typename T, int kN>
-__global__ void __launch_bounds__(kThreads, 1) gemm_seg_kernel(const __grid_constant__ CUtensorMap ta,
+__global__ void __launch_bounds__(kThreads, 2) gemm_seg_kernel(const __grid_constant__ CUtensorMap ta,
                                                                const __grid_constant__ CUtensorMap tb0,
                                                                const __grid_constant__ CUtensorMap tb1,
                                                                const __grid_constant__ CUtensorMap tb2,
                                                                const SegParams p) {
-  using C = Cfg<kN>;
+  using C = SegCfg<kN>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ uint64_t full[C::kStages], empty[C::kStages], done;
@@ -940,10 +951,10 @@ extern "C" int da_gemm_segments(const void* A, int64_t lda, int64_t M, int64_t K
   };
   const bool bf16 = dtype == DA_BF16;
   if (n_tile == 256)
-    return bf16 ? run(gemm_seg_kernel<__nv_bfloat16, 256>, Cfg<256>::kSmem + 1024)
-                : run(gemm_seg_kernel<__half, 256>, Cfg<256>::kSmem + 1024);
-  return bf16 ? run(gemm_seg_kernel<__nv_bfloat16, 128>, Cfg<128>::kSmem + 1024)
-              : run(gemm_seg_kernel<__half, 128>, Cfg<128>::kSmem + 1024);
+    return bf16 ? run(gemm_seg_kernel<__nv_bfloat16, 256>, SegCfg<256>::kSmem + 1024)
+                : run(gemm_seg_kernel<__half, 256>, SegCfg<256>::kSmem + 1024);
+  return bf16 ? run(gemm_seg_kernel<__nv_bfloat16, 128>, SegCfg<128>::kSmem + 1024)
+              : run(gemm_seg_kernel<__half, 128>, SegCfg<128>::kSmem + 1024);
 }
 
 extern "C" int da_gemm_splitk_grouped(const void* A, int64_t lda, int64_t a_group_cols, const void* B, int64_t ldb,
