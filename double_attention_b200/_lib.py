@@ -67,6 +67,7 @@ SIGNATURES: dict[str, list] = {
     "da_route_bwd_fused": [_p, _i64, _i64, _i64, _i32, _i64, _i64, _i64, _i32, _p, _p, _p, _f32, _i32, _i32, _p,
                            _p, _p, _p, _p, _p, _p, _p, _p, _i64, _p, _p],
     "da_attn_bwd_workspace_size": [_i32, _i32, _i32],  # returns int64 (set below)
+    "da_attn_bwd_split_workspace_size": [_i32, _i32, _i32, _i32, _i32, _i32],  # returns int64 (set below)
     "da_attn_bwd_mixed": [_p, _i64, _i64, _i64, _i64, _p, _i64, _i64, _i64, _i64, _p, _p, _i32, _i32, _i32, _i32,
                           _i32, _i32, _p, _i32, _i32, _p, _p, _p, _p, _i32, _p, _p, _p, _p, _p, _p, _i64, _p, _p],
     "da_attn_bwd_mixed_ow": [_p, _i64, _i64, _i64, _i64, _p, _i64, _i64, _i64, _i64, _p, _p, _i32, _i32, _i32, _i32,
@@ -123,6 +124,7 @@ def lib() -> ctypes.CDLL:
             handle.da_route_bwd_workspace_size.argtypes = [_i64, _i32, _i64, _i64]
             handle.da_route_bwd_workspace_size.restype = ctypes.c_int64
             handle.da_attn_bwd_workspace_size.restype = ctypes.c_int64
+            handle.da_attn_bwd_split_workspace_size.restype = ctypes.c_int64
             handle.da_attn_fwd_workspace_size.restype = ctypes.c_int64
             handle.da_gemm_splitk_workspace_elems.restype = ctypes.c_int64
             handle.da_col_sum_workspace_elems.restype = ctypes.c_int64

@@ -81,6 +81,13 @@ struct Params {
   float* dk;             // fp32 [k_rows, R], +=  (overwrite: as dq)
   float* dv;             // fp32 [B*T, D], +=     (overwrite: [B*T, D] in the input dtype, =)
   int overwrite;         // every gradient row has one writer: store it in the input dtype
+  // Few pairs (several maps): every pair's key range (dQ, delta) or query range (dK, dV) split into ksplit
+  // shares, each writing fp32 partial rows (zeros for an empty share) that a combine kernel adds in share
+  // order.
+  int ksplit;
+  float* part;           // [ksplit][part_rows][R or D]: dQ/dK rows (b, map, branch, t), dV rows (b, t)
+  int64_t part_rows;
+  float* delta_part;     // delta sweep: [ksplit][B][maps][T]
   float* dscale;         // [maps] d gamma_s, += (may be null)
   float* dweight;        // [maps] d alpha_s, += (dQ kernel with the first sweep; may be null)
   float* scalar_part;    // [2, 2 * pairs, 4, maps]: per-(CTA, warp) partial sums of d alpha_s and d gamma_s,
@@ -194,6 +201,16 @@ DA_DEV void store_grad32(float* acc, int64_t off, const float* v, float scale, b
   }
 }
 
+// 32 consecutive values of one row of this share's fp32 partial plane (plain stores; an empty share stores
+// zeros, so every partial row the combine reads is written).
+DA_DEV void store_part32(float* part, int64_t off, const float* v, float scale, bool empty) {
+  float4* d = reinterpret_cast<float4*>(part + off);
+#pragma unroll
+  for (int e = 0; e < 8; ++e)
+    d[e] = empty ? make_float4(0.f, 0.f, 0.f, 0.f)
+                 : make_float4(scale * v[4 * e], scale * v[4 * e + 1], scale * v[4 * e + 2], scale * v[4 * e + 3]);
+}
+
 // =============================================================================== dQ kernel
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_constant__ CUtensorMap tq,
@@ -216,11 +233,15 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const uint32_t rank = cluster_ctarank() & 1u;
   const int tiles = (p.T + kTile - 1) / kTile;
-  const int pair = blockIdx.x / 2;
+  const int khalf = (blockIdx.x / 2) % p.ksplit;  // this pair's share of its key tiles
+  const int pair = blockIdx.x / (2 * p.ksplit);
   // longest pairs first across every sequence (the latest query tiles see the most keys)
   const int b = pair % p.B;
   const int t0 = (tiles - 1 - pair / p.B) * kTile;
-  const int nj = p.causal ? t0 / kTile + 1 : tiles;
+  const int nj_all = p.causal ? t0 / kTile + 1 : tiles;
+  const int jspan = (nj_all + p.ksplit - 1) / p.ksplit;
+  const int jb = khalf * jspan;                           // first key tile of this share
+  const int nj = max(0, min(nj_all, jb + jspan) - jb);    // (the last share may be empty)
   const int maps = p.maps;
   // Without a given delta the first sweep computes it; with neither dQ nor d gamma requested that sweep
   // is all the launch does (the dK kernel can then start while another launch forms dQ).
@@ -313,7 +334,7 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
     };
     auto stage_bar = [&]() { return mapa_shared(smem_u32(&fullb[it % nst]), 0); };
     auto emit_s = [&](int u) {  // key rows of map s for this CTA's 64 keys
-      const int krow0 = unit_j(u) * kTile + 64 * (int)rank;
+      const int krow0 = (jb + unit_j(u)) * kTile + 64 * (int)rank;
       for (int cc = 0; ok && cc < L.kw / 128; ++cc, ++it) {
         uint8_t* dst = stage(2 * kBox);
         if (!ok) return;
@@ -328,7 +349,7 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
           if (!ok) return;
           const int mb = (ins * L.ncol + (int)rank * (L.ncol / 2)) / 64;
           const int gi = mb / L.rpb, x = (mb % L.rpb) * 64;
-          const int64_t row = row_of(km.base, km.sb, km.sbr, b, p.branch0[s] + gi, j * kTile);
+          const int64_t row = row_of(km.base, km.sb, km.sbr, b, p.branch0[s] + gi, (jb + j) * kTile);
           tma_load_2d_pair(&tacc, stage_bar(), dst, x, (int)min(row, km.rows - 1));
         }
         return;
@@ -341,7 +362,7 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
           for (int bx = 0; bx < per; ++bx) {
             const int mb = (ins * L.ncol + (int)rank * (L.ncol / 2)) / 64 + bx;
             const int gi = mb / L.rpb, x = (mb % L.rpb) * 64;
-            const int64_t row = row_of(km.base, km.sb, km.sbr, b, p.branch0[s] + gi, j * kTile + kc * 64);
+            const int64_t row = row_of(km.base, km.sb, km.sbr, b, p.branch0[s] + gi, (jb + j) * kTile + kc * 64);
             tma_load_2d_pair(&tk, bar, dst + bx * kBox, x, (int)min(row, km.rows - 1));
           }
         }
@@ -361,7 +382,7 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
     int it = 0;
     bool ok = true;
     for (int g = 0; ok && g < dps; ++g) {
-      const int y = (int)min((int64_t)b * p.T + (g % nj) * kTile + 64 * (int)rank, rowsBT - 1);
+      const int y = (int)min((int64_t)b * p.T + (jb + g % nj) * kTile + 64 * (int)rank, rowsBT - 1);
       for (int cb = 0; cb < p.D / (64 * kDpBlocksQ); ++cb, ++it) {  // V rows of 64 keys, then dY rows
         const int st = it % L.nsp;
         if (!mbar_wait(&rp_empty[st], ((it / L.nsp) & 1u) ^ 1u, ab, 13)) { ok = false; break; }
@@ -516,6 +537,10 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
     const bool arriver = (warp == 2 || warp == kSoftmax2) && lane == 0;  // one per warpgroup
     float* red = reinterpret_cast<float*>(smem + L.off_red);
     const float kLog2e = 1.4426950408889634f;
+    // with a given delta, d gamma is corrected to this kernel's own exact row sum of P dP -- a product of
+    // whole-row sums, so a key share (ksplit > 1, whose delta comes from the split's own exact delta sweep)
+    // keeps the given delta instead
+    const bool exact_corr = p.delta_given && p.ksplit == 1;
     const float gsc = rsqrtf((float)p.group);
     float scale2[kMaxMaps], lse2[kMaxMaps], delta[kMaxMaps], alpha[kMaxMaps];
     // per map: sum of dS * S (d gamma), and with a given delta also sum P * S and sum P * dP (the exact
@@ -546,7 +571,11 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
                    red[(m * 2 + 1) * 128 + (l ^ 64)];
       named_bar_sync(1, 256);
       for (int m = 0; m < maps; ++m) {
-        if (ok && live && half == 0 && wg == 0) p.delta[((int64_t)b * maps + m) * p.T + t] = delta[m];
+        if (ok && live && half == 0 && wg == 0) {  // the row's delta, or this key share's part of it
+          const int64_t i = ((int64_t)b * maps + m) * p.T + t;
+          if (p.ksplit > 1) p.delta_part[(int64_t)khalf * p.B * maps * p.T + i] = delta[m];
+          else p.delta[i] = delta[m];
+        }
         if (p.dweight && wg == 0) {
           float w = (ok && live && half == 0) ? delta[m] : 0.f;
           for (int o = 16; o; o >>= 1) w += __shfl_xor_sync(0xffffffffu, w, o);
@@ -582,7 +611,7 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
         // this map's row constants in registers (the per-map arrays live in local memory)
         const float sc2 = scale2[s], ls2 = lse2[s], dl = delta[s], al = alpha[s];
         float dsum = 0.f, a_acc = 0.f, b_acc = 0.f, c_acc = 0.f;
-        const int kb = j * kTile + half * 64;  // first key column of this thread's 64
+        const int kb = (jb + j) * kTile + half * 64;  // first key column of this thread's 64
         int lim_row = p.T - kb;
         if (p.causal) lim_row = min(lim_row, t - kb + 1);
         if (!live) lim_row = 0;
@@ -630,7 +659,7 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
                 packed[i / 2] = pack2<T>(d0, d1);
               }
             };
-            if (p.delta_given) {
+            if (exact_corr) {
               if (lim >= 32) body(std::false_type{}, std::true_type{});
               else body(std::true_type{}, std::true_type{});
             } else {
@@ -736,7 +765,7 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
           const float Bs = sB[m] + red[(3 * m + 1) * 128 + (l ^ 64)];
           const float C = sC[m] + red[(3 * m + 2) * 128 + (l ^ 64)];
           // sum dS S = alpha (sum P dP S - delta sum P S); with a given delta, delta -> the exact sum P dP
-          dg = p.delta_given ? A + alpha[m] * (delta[m] - C) * Bs : A;
+          dg = exact_corr ? A + alpha[m] * (delta[m] - C) * Bs : A;
         }
         for (int o = 16; o; o >>= 1) dg += __shfl_xor_sync(0xffffffffu, dg, o);
         if (p.scalar_part) {
@@ -752,13 +781,20 @@ __global__ void __launch_bounds__(kThreads, 1) dq_mixed_kernel(const __grid_cons
         for (int ins = 0; ins < L.nins; ++ins)
           for (int c = 0; c < L.ncol / 2; c += 32) {
             float vv[32];
-            tmem_ld32(tmem + lane_base + L.tmem_acc + m * (L.kw / 2) + ins * (L.ncol / 2) + c, vv);
-            tmem_wait_ld();
+            if (nj > 0) {  // (an empty key share has no accumulator: its partial is zero)
+              tmem_ld32(tmem + lane_base + L.tmem_acc + m * (L.kw / 2) + ins * (L.ncol / 2) + c, vv);
+              tmem_wait_ld();
+            }
             if (live) {
               const int col = ins * L.ncol + half * (L.ncol / 2) + c;  // map-local column, one branch
               const int gi = col / p.R;
               const int64_t row = row_of(qm.base, qm.sb, qm.sbr, b, p.branch0[m] + gi, t);
-              store_grad32<T>(p.dq, row * p.R + (col % p.R), vv, gamma, p.overwrite != 0);
+              if (p.ksplit > 1) {  // compact partial row (b, map, branch, query)
+                const int64_t crow = (((int64_t)b * maps + m) * p.group + gi) * p.T + t;
+                store_part32(p.part, ((int64_t)khalf * p.part_rows + crow) * p.R + (col % p.R), vv, gamma, nj == 0);
+              } else {
+                store_grad32<T>(p.dq, row * p.R + (col % p.R), vv, gamma, p.overwrite != 0);
+              }
             }
           }
       }
@@ -794,12 +830,15 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const uint32_t rank = cluster_ctarank() & 1u;
   const int tiles = (p.T + kTile - 1) / kTile;
-  const int pair = blockIdx.x / 2;
+  const int khalf = (blockIdx.x / 2) % p.ksplit;  // this pair's share of its query tiles
+  const int pair = blockIdx.x / (2 * p.ksplit);
   // longest pairs first across every sequence (early keys have the most queries)
   const int b = pair % p.B;
-  const int k0 = (pair / p.B) * kTile;       // first key of this pair
-  const int i0 = p.causal ? k0 / kTile : 0;  // first query tile
-  const int ni = tiles - i0;
+  const int k0 = (pair / p.B) * kTile;        // first key of this pair
+  const int i00 = p.causal ? k0 / kTile : 0;  // first query tile of the pair
+  const int ispan = (tiles - i00 + p.ksplit - 1) / p.ksplit;
+  const int i0 = i00 + khalf * ispan;                  // first query tile of this share
+  const int ni = max(0, min(tiles, i0 + ispan) - i0);  // (the last share may be empty)
   const int maps = p.maps;
   const int U = ni * maps;
   const int dn = p.D < 256 ? p.D : 256;      // N of one dV instruction
@@ -1232,13 +1271,20 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
         for (int ins = 0; ins < L.nins; ++ins)
           for (int c = 0; c < L.ncol / 2; c += 32) {
             float vv[32];
-            tmem_ld32(tmem + lane_base + L.tmem_acc + m * (L.kw / 2) + ins * (L.ncol / 2) + c, vv);
-            tmem_wait_ld();
+            if (ni > 0) {  // (an empty query share has no accumulator: its partial is zero)
+              tmem_ld32(tmem + lane_base + L.tmem_acc + m * (L.kw / 2) + ins * (L.ncol / 2) + c, vv);
+              tmem_wait_ld();
+            }
             if (live) {
               const int col = ins * L.ncol + half * (L.ncol / 2) + c;
               const int gi = col / p.R;
               const int64_t row = row_of(km.base, km.sb, km.sbr, b, p.branch0[m] + gi, key);
-              store_grad32<T>(p.dk, row * p.R + (col % p.R), vv, gamma, p.overwrite != 0);
+              if (p.ksplit > 1) {  // compact partial row (b, map, branch, key)
+                const int64_t crow = (((int64_t)b * maps + m) * p.group + gi) * p.T + key;
+                store_part32(p.part, ((int64_t)khalf * p.part_rows + crow) * p.R + (col % p.R), vv, gamma, ni == 0);
+              } else {
+                store_grad32<T>(p.dk, row * p.R + (col % p.R), vv, gamma, p.overwrite != 0);
+              }
             }
           }
       }
@@ -1247,11 +1293,13 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
       for (int ins = 0; ins < dins; ++ins)
         for (int c = 0; c < dn / 2; c += 32) {
           float vv[32];
-          tmem_ld32(tmem + lane_base + L.tmem_acc + ins * (dn / 2) + c, vv);
-          tmem_wait_ld();
-          if (live)
-            store_grad32<T>(p.dv, ((int64_t)b * p.T + key) * p.D + ins * dn + half * (dn / 2) + c, vv, 1.f,
-                            p.overwrite != 0);
+          if (ni > 0) {
+            tmem_ld32(tmem + lane_base + L.tmem_acc + ins * (dn / 2) + c, vv);
+            tmem_wait_ld();
+          }
+          const int64_t off = ((int64_t)b * p.T + key) * p.D + ins * dn + half * (dn / 2) + c;
+          if (live && p.ksplit > 1) store_part32(p.part, (int64_t)khalf * p.part_rows * p.D + off, vv, 1.f, ni == 0);
+          else if (live) store_grad32<T>(p.dv, off, vv, 1.f, p.overwrite != 0);
         }
     }
   }
@@ -1283,6 +1331,97 @@ __global__ void __launch_bounds__(256) scalar_reduce_kernel(const float* part, i
   if (threadIdx.x == 0) out[m] += red[0];
 }
 
+// Destination rows of a split launch's compact partial rows: c = ((b * maps + s) * group + gi) * T + t
+// -> row_of(base, sb, sbr, b, branch0[s] + gi, t) (dQ, dK), or row c itself when maps == 0 (dV).
+struct SplitRows {
+  int64_t base, sb, sbr;
+  int maps, group, T;
+  int branch0[kMaxMaps];
+};
+
+// The shares of a split launch added in share order (fp32) and stored into the gradient: once in T
+// (overwrite), else added to its fp32 row.  Every thread takes 4 consecutive columns of one row.
+template <typename T>
+__global__ void __launch_bounds__(256) split_combine_kernel(const float* __restrict__ part, int ksplit, int64_t rows,
+                                                            int cols, SplitRows d, void* dst, int overwrite) {
+  grid_dependency_wait();
+  grid_launch_dependents();
+  const int c4 = cols / 4;
+  const int64_t n = rows * c4, plane = rows * cols;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t c = i / c4;
+    const int x = (int)(i % c4) * 4;
+    float4 a = *reinterpret_cast<const float4*>(part + c * cols + x);
+    for (int h = 1; h < ksplit; ++h) {
+      const float4 e = *reinterpret_cast<const float4*>(part + h * plane + c * cols + x);
+      a.x += e.x;
+      a.y += e.y;
+      a.z += e.z;
+      a.w += e.w;
+    }
+    int64_t row = c;
+    if (d.maps) {
+      const int t = (int)(c % d.T);
+      int64_t r = c / d.T;
+      const int gi = (int)(r % d.group);
+      r /= d.group;
+      row = row_of(d.base, d.sb, d.sbr, (int)(r / d.maps), d.branch0[r % d.maps] + gi, t);
+    }
+    if (overwrite) {
+      *reinterpret_cast<uint2*>(static_cast<T*>(dst) + row * cols + x) =
+          make_uint2(pack2<T>(a.x, a.y), pack2<T>(a.z, a.w));
+    } else {
+      float4* o = reinterpret_cast<float4*>(static_cast<float*>(dst) + row * cols + x);
+      float4 v = *o;
+      v.x += a.x;
+      v.y += a.y;
+      v.z += a.z;
+      v.w += a.w;
+      *o = v;
+    }
+  }
+}
+
+// delta[i] = the shares' partial row sums of a split delta sweep, added in share order.
+__global__ void __launch_bounds__(256) delta_combine_kernel(const float* __restrict__ part, int ksplit, int64_t n,
+                                                            float* delta) {
+  grid_dependency_wait();
+  grid_launch_dependents();
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    float a = part[i];
+    for (int h = 1; h < ksplit; ++h) a += part[h * n + i];
+    delta[i] = a;
+  }
+}
+
+// Byte offsets of the split form's regions in the caller's workspace (each 256-byte aligned): the
+// per-(CTA, warp) scalar partials of every share, the delta sweep's partial row sums, and the fp32
+// partial planes of dQ, dK (compact rows) and dV.
+struct SplitWorkspace {
+  int64_t scalar, delta, dq, dk, dv, total;
+};
+
+inline SplitWorkspace split_workspace(int B, int T, int R, int D, int maps, int group, int ksplit) {
+  auto up = [](int64_t x) { return (x + 255) & ~(int64_t)255; };
+  const int64_t pairs = (int64_t)B * ((T + kTile - 1) / kTile);
+  const int64_t f = (int64_t)sizeof(float);
+  const int64_t qk = (int64_t)ksplit * B * maps * group * T * R * f;
+  SplitWorkspace w;
+  w.scalar = 0;
+  w.delta = up(2 * (2 * pairs * ksplit * 4) * maps * f);
+  w.dq = w.delta + up((int64_t)ksplit * B * maps * T * f);
+  w.dk = w.dq + up(qk);
+  w.dv = w.dk + up(qk);
+  w.total = w.dv + up((int64_t)ksplit * B * T * D * f);
+  return w;
+}
+
+// Two shares when the split launches' CTAs (four per pair) fit on the SMs at once and there are several
+// maps (one map keeps its given delta's exact correction of d gamma, which needs whole rows).  Measured at
+// T = 2048, four maps, three streams: B2 (32 pairs) 219 -> 178 us; B4, where the split launches' 256 CTAs
+// queue for 148 SMs, 276 -> 322 us.
+inline int bwd_split(int maps, int64_t pairs, int sms) { return (maps > 1 && 4 * pairs <= sms) ? 2 : 1; }
+
 template <typename Kern>
 int launch_pair(Kern kern, const Layout& L, int pairs, const CUtensorMap& tq, const CUtensorMap& tk,
                 const CUtensorMap& tv, const CUtensorMap& tdy, const CUtensorMap& tacc, const Params& p,
@@ -1302,6 +1441,14 @@ extern "C" int64_t da_attn_bwd_workspace_size(int B, int T, int maps) {
   if (B <= 0 || T <= 0 || maps < 1 || maps > da::attn::kMaxMaps) return -1;
   const int64_t pairs = (int64_t)B * ((T + da::attn::bwdm::kTile - 1) / da::attn::bwdm::kTile);
   return 2 * (2 * pairs * 4) * maps * (int64_t)sizeof(float);
+}
+
+extern "C" int64_t da_attn_bwd_split_workspace_size(int B, int T, int R, int D, int maps, int group) {
+  using namespace da::attn::bwdm;
+  if (B <= 0 || T <= 0 || R <= 0 || D <= 0 || group < 1 || maps < 1 || maps > da::attn::kMaxMaps) return -1;
+  const int64_t pairs = (int64_t)B * ((T + kTile - 1) / kTile);
+  const int ks = bwd_split(maps, pairs, da::sm_count());
+  return ks > 1 ? split_workspace(B, T, R, D, maps, group, ks).total : 0;
 }
 
 namespace {
@@ -1349,10 +1496,23 @@ int attn_bwd_entry(const void* q, int64_t q_rows, int64_t q_base, int64_t q_sb, 
         if (branch0[s1] < branch0[s2] + group && branch0[s2] < branch0[s1] + group) return DA_ERR_UNSUPPORTED;
   p.dq = dq; p.dk = dk; p.dv = dv; p.dscale = dscale; p.dweight = dweight; p.status = status;
   p.overwrite = overwrite ? 1 : 0;
+  p.ksplit = 1;
+  p.part = nullptr;
+  p.part_rows = 0;
+  p.delta_part = nullptr;
   const int npairs = B * ((T + kTile - 1) / kTile);
-  const int64_t n_part = (int64_t)2 * npairs * 4;  // partials per map and kind: (CTA, softmax warp)
+  // The split form (bwd_split) when the caller's workspace holds it and every gradient row has one writer
+  // (maps on disjoint branch ranges), so that a combine can store each row once.
+  bool disjoint = true;
+  for (int s1 = 0; s1 < maps; ++s1)
+    for (int s2 = s1 + 1; s2 < maps; ++s2)
+      if (branch0[s1] < branch0[s2] + group && branch0[s2] < branch0[s1] + group) disjoint = false;
+  const int ks = bwd_split(maps, npairs, sm_count());
+  const SplitWorkspace sw = split_workspace(B, T, R, D, maps, group, ks);
+  const int ksplit = (ks > 1 && disjoint && workspace && workspace_bytes >= sw.total) ? ks : 1;
+  const int64_t n_part = (int64_t)2 * npairs * ksplit * 4;  // partials per map and kind: (CTA, softmax warp)
   p.scalar_part = nullptr;
-  if (dscale || (dweight && !delta_given)) {
+  if (ksplit > 1 || dscale || (dweight && !delta_given)) {
     if (!workspace || workspace_bytes < 2 * n_part * maps * (int64_t)sizeof(float)) return DA_ERR_WORKSPACE;
     if (reinterpret_cast<uintptr_t>(workspace) & 15) return DA_ERR_ALIGN;
     p.scalar_part = static_cast<float*>(workspace);
@@ -1392,31 +1552,87 @@ int attn_bwd_entry(const void* q, int64_t q_rows, int64_t q_base, int64_t q_sb, 
     if (rc) return rc;
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int pairs = B * ((T + kTile - 1) / kTile);
   const bool bf16 = dtype == DA_BF16;
-  // the query-parallel kernel runs first: without a given delta it produces it for the other two
-  if (dq || dscale || !delta_given) {
+  const int sms = sm_count();
+  // the query-parallel kernel, then the fixed-order sums of its d alpha / d gamma partials
+  auto run_dq = [&](const Params& pp) -> int {
     const Layout L = make_layout(0, maps, group, R, D);
-    rc = bf16 ? launch_pair(dq_mixed_kernel<__nv_bfloat16>, L, pairs, tq, tk, tvq, tdyq, tk128, p, st)
-              : launch_pair(dq_mixed_kernel<__half>, L, pairs, tq, tk, tvq, tdyq, tk128, p, st);
-    if (rc) return rc;
-    if (p.scalar_part) {
-      rc = launch_kernel(scalar_reduce_kernel, dim3((unsigned)maps, 2, 1), dim3(256, 1, 1), 0, st, false,
-                         (const float*)p.scalar_part, (int)n_part, maps, delta_given ? (float*)nullptr : dweight,
-                         dscale);
-      if (rc) return rc;
-    }
+    const int cpairs = npairs * pp.ksplit;
+    int r = bf16 ? launch_pair(dq_mixed_kernel<__nv_bfloat16>, L, cpairs, tq, tk, tvq, tdyq, tk128, pp, st)
+                 : launch_pair(dq_mixed_kernel<__half>, L, cpairs, tq, tk, tvq, tdyq, tk128, pp, st);
+    float* dw = pp.delta_given ? nullptr : pp.dweight;
+    if (r || !pp.scalar_part || (!dw && !pp.dscale)) return r;
+    return launch_kernel(scalar_reduce_kernel, dim3((unsigned)maps, 2, 1), dim3(256, 1, 1), 0, st, false,
+                         (const float*)pp.scalar_part, (int)(2 * cpairs * 4), maps, dw, pp.dscale);
+  };
+  auto run_dkv = [&](const Params& pp, bool dkk) -> int {
+    const Layout L = make_layout(dkk ? 1 : 2, maps, group, R, D);
+    const int cpairs = npairs * pp.ksplit;
+    if (dkk)
+      return bf16 ? launch_pair(dkv_mixed_kernel<__nv_bfloat16, true>, L, cpairs, tq, tk, tv, tdy, tq128, pp, st)
+                  : launch_pair(dkv_mixed_kernel<__half, true>, L, cpairs, tq, tk, tv, tdy, tq128, pp, st);
+    return bf16 ? launch_pair(dkv_mixed_kernel<__nv_bfloat16, false>, L, cpairs, tq, tk, tv, tdy2, tq128, pp, st)
+                : launch_pair(dkv_mixed_kernel<__half, false>, L, cpairs, tq, tk, tv, tdy2, tq128, pp, st);
+  };
+  auto grid_for = [&](int64_t n) {
+    const int64_t blocks = (n + 255) / 256;
+    return dim3((unsigned)(blocks < 4 * sms ? blocks : 4 * sms));
+  };
+  if (ksplit == 1) {
+    // the query-parallel kernel runs first: without a given delta it produces it for the other two
+    if (dq || dscale || !delta_given)
+      if ((rc = run_dq(p))) return rc;
+    if (dk && (rc = run_dkv(p, true))) return rc;
+    if (dv) rc = run_dkv(p, false);
+    return rc;
+  }
+  // Split form: every launch runs two CTA pairs per pair, each on one share of the long row, and a combine
+  // adds the shares' fp32 partial rows in share order.  Without a given delta the delta sweep runs first
+  // on its own (with d alpha); the dQ launch then takes the combined, exact delta.
+  char* ws = static_cast<char*>(workspace);
+  p.ksplit = ksplit;
+  p.delta_part = reinterpret_cast<float*>(ws + sw.delta);
+  SplitRows qr{q_base, q_sb, q_sbr, maps, group, T, {}}, kr{k_base, k_sb, k_sbr, maps, group, T, {}};
+  SplitRows vr{0, 0, 0, 0, 1, T, {}};
+  for (int s = 0; s < attn::kMaxMaps; ++s) qr.branch0[s] = kr.branch0[s] = vr.branch0[s] = p.branch0[s];
+  const int64_t crows = (int64_t)B * maps * group * T;
+  auto combine = [&](const float* part, int64_t rows, int cols, const SplitRows& d, void* dst) -> int {
+    const dim3 grid = grid_for(rows * cols / 4);
+    return bf16 ? launch_kernel(split_combine_kernel<__nv_bfloat16>, grid, dim3(256), 0, st, false, part, ksplit,
+                                rows, cols, d, dst, p.overwrite)
+                : launch_kernel(split_combine_kernel<__half>, grid, dim3(256), 0, st, false, part, ksplit, rows,
+                                cols, d, dst, p.overwrite);
+  };
+  if (!delta_given) {
+    Params pd = p;
+    pd.dq = nullptr;
+    pd.dscale = nullptr;
+    if ((rc = run_dq(pd))) return rc;
+    const int64_t n = (int64_t)B * maps * T;
+    if ((rc = launch_kernel(delta_combine_kernel, grid_for(n), dim3(256), 0, st, false,
+                            (const float*)p.delta_part, ksplit, n, delta)))
+      return rc;
+    p.delta_given = 1;
+    p.dweight = nullptr;
+  }
+  if (dq || dscale) {
+    Params pq = p;
+    pq.part = reinterpret_cast<float*>(ws + sw.dq);
+    pq.part_rows = crows;
+    if ((rc = run_dq(pq))) return rc;
+    if (dq && (rc = combine(pq.part, crows, R, qr, dq))) return rc;
   }
   if (dk) {
-    const Layout L = make_layout(1, maps, group, R, D);
-    rc = bf16 ? launch_pair(dkv_mixed_kernel<__nv_bfloat16, true>, L, pairs, tq, tk, tv, tdy, tq128, p, st)
-              : launch_pair(dkv_mixed_kernel<__half, true>, L, pairs, tq, tk, tv, tdy, tq128, p, st);
-    if (rc) return rc;
+    Params pk = p;
+    pk.part = reinterpret_cast<float*>(ws + sw.dk);
+    pk.part_rows = crows;
+    if ((rc = run_dkv(pk, true)) || (rc = combine(pk.part, crows, R, kr, dk))) return rc;
   }
   if (dv) {
-    const Layout L = make_layout(2, maps, group, R, D);
-    rc = bf16 ? launch_pair(dkv_mixed_kernel<__nv_bfloat16, false>, L, pairs, tq, tk, tv, tdy2, tq128, p, st)
-              : launch_pair(dkv_mixed_kernel<__half, false>, L, pairs, tq, tk, tv, tdy2, tq128, p, st);
+    Params pv = p;
+    pv.part = reinterpret_cast<float*>(ws + sw.dv);
+    pv.part_rows = (int64_t)B * T;
+    if ((rc = run_dkv(pv, false)) || (rc = combine(pv.part, (int64_t)B * T, D, vr, dv))) return rc;
   }
   return rc;
 }

@@ -795,10 +795,11 @@ def _attention_backward(q: RowMap, k: RowMap, v: Tensor, dy: Tensor, batch: int,
                         group: int, branch0: list[int], causal: bool, scales: Tensor, weights: Tensor | None,
                         lse: Tensor, delta: Tensor, delta_given: bool, dq: Tensor | None, dk: Tensor | None,
                         dv: Tensor | None, dscale: Tensor | None, dweight: Tensor | None,
-                        overwrite: bool = False) -> None:
+                        overwrite: bool = False, split: bool = True) -> None:
     """All maps of one attention (da_attn_bwd_mixed): fp32 gradients accumulated in place, or with
     `overwrite` (maps on disjoint branches, da_attn_bwd_mixed_ow) every produced row of dq, dk and dv
-    stored once in the input dtype."""
+    stored once in the input dtype.  `split=False` keeps the library's unsplit form at sizes where it
+    would split every pair's long row over two CTA pairs."""
     d = v.shape[-1]
     _attention_bwd_supported(r, d, group)
     if maps * group * r > 512:
@@ -806,8 +807,12 @@ def _attention_backward(q: RowMap, k: RowMap, v: Tensor, dy: Tensor, batch: int,
     dev = v.device
     ws = workspace(dev)
     b0 = (ctypes_int_array(MAX_MAPS))(*(branch0 + [0] * (MAX_MAPS - len(branch0))))
-    # per-(CTA, warp) partial sums of d gamma / d alpha, added in a fixed order by the library
+    # per-(CTA, warp) partial sums of d gamma / d alpha, added in a fixed order by the library; at small
+    # batches with several maps also the split form's partial rows (every pair's long row over two CTA
+    # pairs, the shares added in order by the library)
     part_bytes = int(_lib.lib().da_attn_bwd_workspace_size(batch, length, maps))
+    if split:
+        part_bytes = max(part_bytes, int(_lib.lib().da_attn_bwd_split_workspace_size(batch, length, r, d, maps, group)))
     part = torch.empty(part_bytes, dtype=torch.uint8, device=dev)
 
     entry = "da_attn_bwd_mixed_ow" if overwrite else "da_attn_bwd_mixed"

@@ -310,6 +310,22 @@ DA_API int da_attn_bwd_delta(const void* dy, const void* y, int64_t rows, int D,
  * second kernel adds them in a fixed order, so every output of this call is
  * bit-identical from run to run. */
 DA_API int64_t da_attn_bwd_workspace_size(int B, int T, int maps);
+
+/* Bytes of workspace with which da_attn_bwd_mixed and da_attn_bwd_mixed_ow run
+ * their split form at these sizes on the current device: 0 when they never
+ * split here, -1 for invalid sizes.  With several maps and few query tiles
+ * (the split launches' CTAs, four per pair, fit on the SMs at once) every
+ * pair's long row -- the keys of a query tile (delta, dQ), the queries of a
+ * key tile (dK, dV) -- is split over two CTA pairs writing fp32 partial rows
+ * into the workspace, which a combine adds in share order and stores (so
+ * results repeat bit for bit; they differ from the unsplit form's only by
+ * fp32 reassociation).  Without a given delta the delta sweep runs first, on
+ * its own.  A call splits when the maps' branch ranges do not overlap and
+ * `workspace_bytes` is at least this size; with less (but at least
+ * da_attn_bwd_workspace_size) it runs unsplit.  A split call takes a given
+ * delta as the exact row sums (as this entry's own sweep writes them) and
+ * does not correct d gamma towards its own. */
+DA_API int64_t da_attn_bwd_split_workspace_size(int B, int T, int R, int D, int maps, int group);
 DA_API int da_attn_bwd_mixed(const void* q, int64_t q_rows, int64_t q_base, int64_t q_sb, int64_t q_sbr,
                              const void* k, int64_t k_rows, int64_t k_base, int64_t k_sb, int64_t k_sbr,
                              const void* v, const void* dy, int B, int T, int R, int D, int maps, int group,

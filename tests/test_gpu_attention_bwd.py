@@ -205,3 +205,52 @@ def test_overwrite_gradients_equal_the_accumulated_ones(batch: int) -> None:
     assert ops.device_status(dev) == 0
     for name, a, b in zip(("routed", "value", "scales", "map weights"), out[False], out[True]):
         assert torch.equal(a, b), f"d {name}: overwrite and accumulate paths differ"
+
+
+@pytest.mark.parametrize(("batch", "length", "causal"), [(2, 2048, True), (1, 640, True), (1, 640, False)])
+def test_split_form_matches_the_unsplit_one(batch: int, length: int, causal: bool) -> None:
+    """With several maps on disjoint branches and few query tiles the library splits every pair's long row
+    over two CTA pairs (da_attn_bwd_split_workspace_size > 0) and adds the shares' fp32 partial rows in
+    share order.  Against the unsplit form on the same inputs the gradients differ by fp32 reassociation
+    only (a bf16 rounding step at most per element), the split form repeats bit for bit, and its delta
+    is the unsplit sweep's.  B2 T2048 is the config-3 shape at eight GPUs; T640 has a ragged last tile
+    and, causal, first query tiles whose second key share is empty."""
+    dev, dtype = torch.device("cuda"), torch.bfloat16
+    h = maps = 4
+    r, d = 128, 512
+    routed, value, dy, scales, mix = _inputs(h, maps, batch, length, r, d, 16.0, dtype, seed=9)
+    routed, value, dy = routed.to(dev), value.to(dev).to(dtype), dy.to(dev).to(dtype)
+    scales, mix = scales.to(dev).float(), mix.to(dev).float()
+    flat = routed.view(-1, r)
+    group, branch0 = ops._map_layout(h, maps)
+    lib = ops._lib.lib()
+    assert lib.da_attn_bwd_split_workspace_size(batch, length, r, d, maps, group) > 0
+    assert lib.da_attn_bwd_split_workspace_size(batch, length, r, d, 1, group) == 0  # one map never splits
+    qmap = ops.RowMap(flat, 0, length, batch * length)
+    kmap = ops.RowMap(flat, h * batch * length, length, batch * length)
+    _y, lse = ops._attention_forward(qmap, kmap, value, batch, length, r, maps, group, branch0, causal, scales, mix,
+                                     None, 1.0, dtype)
+
+    def run(split: bool):
+        droute = torch.empty(flat.shape, dtype=dtype, device=dev)
+        dv = torch.empty(batch * length, d, dtype=dtype, device=dev)
+        dscale = torch.zeros(maps, dtype=torch.float32, device=dev)
+        dweight = torch.zeros(maps, dtype=torch.float32, device=dev)
+        delta = torch.empty(batch, maps, length, dtype=torch.float32, device=dev)
+        ops._attention_backward(qmap, kmap, value, dy, batch, length, r, maps, group, branch0, causal, scales, mix,
+                                lse, delta, False, droute, droute, dv, dscale, dweight, overwrite=True, split=split)
+        return droute, dv, dscale, dweight, delta
+
+    whole, first, again = run(False), run(True), run(True)
+    torch.cuda.synchronize()
+    assert ops.device_status(dev) == 0
+    names = ("routed", "value", "scales", "map weights", "delta")
+    for name, a, b in zip(names, first, again):
+        assert torch.equal(a, b), f"d {name}: two split passes differ"
+    for name, a, b in zip(names, first, whole):
+        a, b = a.float(), b.float()
+        scale = max(b.abs().max().item(), 1e-30)
+        tol = 1e-5 if name in ("scales", "map weights", "delta") else 2 ** -7
+        err = (a - b).abs().max().item() / scale
+        assert err <= tol, f"d {name}: split vs unsplit max error {err:.2e} of max |g| (bound {tol:.1e})"
+        assert _cos(a, b) >= 0.99999, name
