@@ -42,6 +42,8 @@ SIGNATURES: dict[str, list] = {
     "da_temperatures": [_p, _i32, _f32, _f32, _p, _i32, _i32, _f32, _f32, _p, _p, _p],
     "da_gemm_segments": [_p, _i64, _i64, _i64, _i32, _i32, _p, _p, _p, _p, _p, _p, _p, _p, _p],
     "da_dict_norm_bwd": [_p, _p, _p, _p, _i64, _i64, _f32, _p, _i32, _p],
+    "da_dict_norm_bwd_typed": [_p, _i32, _p, _p, _p, _i64, _i64, _f32, _p, _i32, _i32, _p],
+    "da_temperatures_bwd": [_p, _i32, _f32, _f32, _p, _p, _p, _p, _i32, _i32, _f32, _f32, _p, _p, _p, _p],
     "da_col_norm_max": [_p, _i64, _i64, _i32, _p, _p],
     "da_set_debug_trace": [_p],
     "da_route_fwd_static": [_p, _i64, _i64, _i64, _i32, _i64, _i64, _i64, _i32, _p, _p, _p, _p, _f32, _i32, _i32,

@@ -160,11 +160,14 @@ __global__ void __launch_bounds__(256) dict_norm_pair_kernel(const TR* __restric
 
 // grad (and grad_t, the same gradient given in [M, R] layout) are summed.
 // One CTA per 32 columns, both operands staged in shared memory.
-__global__ void __launch_bounds__(256) dict_norm_bwd_kernel(const float* __restrict__ raw,
+// raw banks of type TR (fp32, or the half type of a module cast to it; read exactly as fp32), the gradient
+// stored as TG (fp32, added to when `accumulate`, else rounded once to TG)
+template <typename TR, typename TG>
+__global__ void __launch_bounds__(256) dict_norm_bwd_kernel(const TR* __restrict__ raw,
                                                             const float* __restrict__ denom,
                                                             const float* __restrict__ grad,
                                                             const float* __restrict__ grad_t, int R, int M, float eps,
-                                                            float* __restrict__ grad_raw, int accumulate) {
+                                                            TG* __restrict__ grad_raw, int accumulate) {
   extern __shared__ float smem_f[];
   grid_dependency_wait();
   grid_launch_dependents();
@@ -174,7 +177,7 @@ __global__ void __launch_bounds__(256) dict_norm_bwd_kernel(const float* __restr
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
   const int j0 = blockIdx.x * 32, j = j0 + tx;
   for (int r = ty; r < R; r += 8) {
-    tx_[r * 33 + tx] = j < M ? raw[(size_t)r * M + j] : 0.f;
+    tx_[r * 33 + tx] = j < M ? static_cast<float>(raw[(size_t)r * M + j]) : 0.f;
     tg[r * 33 + tx] = (grad && j < M) ? grad[(size_t)r * M + j] : 0.f;
   }
   __syncthreads();
@@ -213,8 +216,9 @@ __global__ void __launch_bounds__(256) dict_norm_bwd_kernel(const float* __restr
     for (int r = ty; r < R; r += 8) {
       const float x = tx_[r * 33 + tx], g = tg[r * 33 + tx];
       const float dx = clamped ? g / eps : (g - (x / d) * cdot) / d;
-      float* dst = grad_raw + (size_t)r * M + j;
-      *dst = accumulate ? *dst + dx : dx;
+      TG* dst = grad_raw + (size_t)r * M + j;
+      if constexpr (std::is_same<TG, float>::value) *dst = accumulate ? *dst + dx : dx;
+      else *dst = static_cast<TG>(dx);
     }
   }
 }
@@ -253,20 +257,55 @@ extern "C" int da_dict_norm_fwd(const float* raw, int64_t R, int64_t M, float ep
   return DA_OK;
 }
 
-extern "C" int da_dict_norm_bwd(const float* raw, const float* denom, const float* grad, const float* grad_t,
-                                int64_t R, int64_t M, float eps, float* grad_raw, int accumulate, void* stream) {
+namespace {
+
+template <typename TR, typename TG>
+int launch_norm_bwd(const void* raw, const float* denom, const float* grad, const float* grad_t, int64_t R, int64_t M,
+                    float eps, void* grad_raw, int accumulate, cudaStream_t st) {
+  using namespace da;
+  const size_t smem = 2 * (size_t)R * 33 * sizeof(float);
+  auto k = dict_norm_bwd_kernel<TR, TG>;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return record_cuda_error();
+  return launch_kernel(k, dim3((unsigned)((M + 31) / 32)), dim3(256), smem, st, false, static_cast<const TR*>(raw),
+                       denom, grad, grad_t, (int)R, (int)M, eps, static_cast<TG*>(grad_raw), accumulate);
+}
+
+template <typename TR>
+int launch_norm_bwd_to(int grad_dtype, const void* raw, const float* denom, const float* grad, const float* grad_t,
+                       int64_t R, int64_t M, float eps, void* grad_raw, int accumulate, cudaStream_t st) {
+  if (grad_dtype == DA_F32)
+    return launch_norm_bwd<TR, float>(raw, denom, grad, grad_t, R, M, eps, grad_raw, accumulate, st);
+  if (grad_dtype == DA_BF16)
+    return launch_norm_bwd<TR, __nv_bfloat16>(raw, denom, grad, grad_t, R, M, eps, grad_raw, 0, st);
+  return launch_norm_bwd<TR, __half>(raw, denom, grad, grad_t, R, M, eps, grad_raw, 0, st);
+}
+
+}  // namespace
+
+extern "C" int da_dict_norm_bwd_typed(const void* raw, int raw_dtype, const float* denom, const float* grad,
+                                      const float* grad_t, int64_t R, int64_t M, float eps, void* grad_raw,
+                                      int grad_dtype, int accumulate, void* stream) {
   using namespace da;
   if (!raw || !denom || !grad_raw || (!grad && !grad_t)) return DA_ERR_NULL;
   if (int rc = bind_device(raw)) return rc;
   if (R <= 0 || M <= 0 || R > (1 << 16) || M > (1 << 24)) return DA_ERR_SHAPE;
+  for (int d : {raw_dtype, grad_dtype})
+    if (d != DA_F32 && d != DA_BF16 && d != DA_F16) return DA_ERR_DTYPE;
+  if (accumulate && grad_dtype != DA_F32) return DA_ERR_UNSUPPORTED;
+  if (2 * (size_t)R * 33 * sizeof(float) > 200 * 1024) return DA_ERR_SHAPE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const size_t smem = 2 * (size_t)R * 33 * sizeof(float);
-  if (smem > 200 * 1024) return DA_ERR_SHAPE;
-  if (cudaFuncSetAttribute(dict_norm_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-      cudaSuccess)
-    return record_cuda_error();
-  return launch_kernel(dict_norm_bwd_kernel, dim3((unsigned)((M + 31) / 32)), dim3(256), smem, st, false, raw, denom,
-                       grad, grad_t, (int)R, (int)M, eps, grad_raw, accumulate);
+  if (raw_dtype == DA_F32)
+    return launch_norm_bwd_to<float>(grad_dtype, raw, denom, grad, grad_t, R, M, eps, grad_raw, accumulate, st);
+  if (raw_dtype == DA_BF16)
+    return launch_norm_bwd_to<__nv_bfloat16>(grad_dtype, raw, denom, grad, grad_t, R, M, eps, grad_raw, accumulate,
+                                             st);
+  return launch_norm_bwd_to<__half>(grad_dtype, raw, denom, grad, grad_t, R, M, eps, grad_raw, accumulate, st);
+}
+
+extern "C" int da_dict_norm_bwd(const float* raw, const float* denom, const float* grad, const float* grad_t,
+                                int64_t R, int64_t M, float eps, float* grad_raw, int accumulate, void* stream) {
+  return da_dict_norm_bwd_typed(raw, DA_F32, denom, grad, grad_t, R, M, eps, grad_raw, DA_F32, accumulate, stream);
 }
 
 // Largest column 2-norm of a [R, M] dictionary in fp16/bf16 (for callers that
@@ -363,8 +402,50 @@ __global__ void temperatures_kernel(const void* log_beta, int beta_dtype, float 
   if (i < maps && log_scales)
     scales_out[i] = expf(fminf(fmaxf(load_any(log_scales, scales_dtype, i), scale_lo), scale_hi));
 }
+// Backward of exp(clamp(log, lo, hi)): g * value where lo <= log <= hi, else 0, in fp32, rounded once to
+// the log's dtype.
+DA_DEV void store_any(void* p, int dtype, int i, float v) {
+  if (dtype == DA_F32) static_cast<float*>(p)[i] = v;
+  else if (dtype == DA_BF16) static_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+  else static_cast<__half*>(p)[i] = __float2half_rn(v);
+}
+__global__ void temperatures_bwd_kernel(const void* log_beta, int beta_dtype, float beta_lo, float beta_hi,
+                                        const float* beta, const float* g_beta, void* grad_log_beta,
+                                        const void* log_scales, int scales_dtype, int maps, float scale_lo,
+                                        float scale_hi, const float* scales, const float* g_scales,
+                                        void* grad_log_scales) {
+  grid_dependency_wait();
+  grid_launch_dependents();
+  const int i = threadIdx.x;
+  if (i == 0 && g_beta) {
+    const float x = load_any(log_beta, beta_dtype, 0);
+    store_any(grad_log_beta, beta_dtype, 0, g_beta[0] * beta[0] * ((x >= beta_lo && x <= beta_hi) ? 1.f : 0.f));
+  }
+  if (i < maps && g_scales) {
+    const float x = load_any(log_scales, scales_dtype, i);
+    store_any(grad_log_scales, scales_dtype, i,
+              g_scales[i] * scales[i] * ((x >= scale_lo && x <= scale_hi) ? 1.f : 0.f));
+  }
+}
 }  // namespace
 }  // namespace da
+
+extern "C" int da_temperatures_bwd(const void* log_beta, int beta_dtype, float beta_lo, float beta_hi,
+                                   const float* beta, const float* g_beta, void* grad_log_beta,
+                                   const void* log_scales, int scales_dtype, int maps, float scale_lo, float scale_hi,
+                                   const float* scales, const float* g_scales, void* grad_log_scales, void* stream) {
+  using namespace da;
+  if (!g_beta && !g_scales) return DA_ERR_NULL;
+  if (g_beta && (!log_beta || !beta || !grad_log_beta)) return DA_ERR_NULL;
+  if (g_scales && (!log_scales || !scales || !grad_log_scales)) return DA_ERR_NULL;
+  if (int rc = bind_device(g_beta ? (const void*)g_beta : (const void*)g_scales)) return rc;
+  if (maps < 0 || maps > 32) return DA_ERR_SHAPE;
+  for (int d : {beta_dtype, scales_dtype})
+    if (d != DA_F32 && d != DA_BF16 && d != DA_F16) return DA_ERR_DTYPE;
+  return launch_kernel(temperatures_bwd_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), false,
+                       log_beta, beta_dtype, beta_lo, beta_hi, beta, g_beta, grad_log_beta, log_scales, scales_dtype,
+                       maps, scale_lo, scale_hi, scales, g_scales, grad_log_scales);
+}
 
 extern "C" int da_temperatures(const void* log_beta, int beta_dtype, float beta_lo, float beta_hi,
                                const void* log_scales, int scales_dtype, int maps, float scale_lo, float scale_hi,

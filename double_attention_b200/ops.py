@@ -195,6 +195,7 @@ class _DictNorm(torch.autograd.Function):
         ctx.save_for_backward(raw, denom)
         ctx.eps = eps
         ctx.mark_non_differentiable(mx)
+        ctx.set_materialize_grads(False)  # views nothing differentiates stay None (no zero fills)
         anchor = torch.empty(r, m, dtype=torch.float32, device=raw.device)  # fp32 gradient entry, never read
         return out, out_t, mx, anchor
 
@@ -242,16 +243,19 @@ class _DictNormPair(torch.autograd.Function):
         ctx.eps = eps
         ctx.tied = raw_value is None
         ctx.mark_non_differentiable(kmax)
+        # the route's backward gives the fp32 anchors their gradients and the bf16 views none: those stay
+        # None instead of zero-filled tensors that the backward would convert and add
+        ctx.set_materialize_grads(False)
         key_anchor = torch.empty(r, m, dtype=torch.float32, device=dev)  # fp32 gradient entries, never read
         value_anchor = torch.empty(r, m, dtype=torch.float32, device=dev)
         return key, key_t, kmax, key_anchor, value, value_t, value_anchor
 
     @staticmethod
     def backward(ctx, g_key, g_key_t, _g_kmax, g_key_anchor, g_value, g_value_t, g_value_anchor):  # type: ignore[override]
-        rk, rv, kden, vden = ctx.saved_tensors
-        rk, rv = rk.float(), rv.float()  # the normalisation backward works on fp32 banks
+        rk, rv, kden, vden = ctx.saved_tensors  # the banks in their own dtype, read exactly by the kernel
         r, m = rk.shape
         dev = rk.device
+        rdt = dtype_code(rk.dtype)
 
         def merged(g, anchor):
             if anchor is None:
@@ -261,25 +265,27 @@ class _DictNormPair(torch.autograd.Function):
         gk, gv = merged(g_key, g_key_anchor), merged(g_value, g_value_anchor)
         gkt = None if g_key_t is None else g_key_t.float().contiguous()
         gvt = None if g_value_t is None else g_value_t.float().contiguous()
+        want_key = gk is not None or gkt is not None
+        want_value = gv is not None or gvt is not None
+
+        def norm_bwd(raw, den, g, gt, out, accumulate):
+            call("da_dict_norm_bwd_typed", raw.data_ptr(), rdt, den.data_ptr(), ptr(g), ptr(gt), r, m, ctx.eps,
+                 out.data_ptr(), dtype_code(out.dtype), accumulate, stream_ptr(dev))
+
         grad_key = grad_value = None
-        if gk is not None or gkt is not None:
-            grad_key = torch.empty_like(rk)
-            call("da_dict_norm_bwd", rk.data_ptr(), kden.data_ptr(), ptr(gk), ptr(gkt), r, m, ctx.eps,
-                 grad_key.data_ptr(), 0, stream_ptr(dev))
-        if gv is not None or gvt is not None:
-            if ctx.tied:  # the value bank is the key bank: both gradients land on raw_key
-                if grad_key is None:
-                    grad_key = torch.zeros_like(rk)
-                call("da_dict_norm_bwd", rk.data_ptr(), vden.data_ptr(), ptr(gv), ptr(gvt), r, m, ctx.eps,
-                     grad_key.data_ptr(), 1, stream_ptr(dev))
-            else:
-                grad_value = torch.empty_like(rv)
-                call("da_dict_norm_bwd", rv.data_ptr(), vden.data_ptr(), ptr(gv), ptr(gvt), r, m, ctx.eps,
-                     grad_value.data_ptr(), 0, stream_ptr(dev))
-        if grad_key is not None:
+        if ctx.tied and want_value:  # the value bank is the key bank: both gradients added in fp32 on raw_key
+            grad_key = (torch.empty if want_key else torch.zeros)(r, m, dtype=torch.float32, device=dev)
+            if want_key:
+                norm_bwd(rk, kden, gk, gkt, grad_key, 0)
+            norm_bwd(rk, vden, gv, gvt, grad_key, 1)
             grad_key = grad_key.to(ctx.raw_dtype)
-        if grad_value is not None:
-            grad_value = grad_value.to(ctx.raw_dtype)
+        else:  # each gradient stored once in its bank's dtype
+            if want_key:
+                grad_key = torch.empty(r, m, dtype=ctx.raw_dtype, device=dev)
+                norm_bwd(rk, kden, gk, gkt, grad_key, 0)
+            if want_value:
+                grad_value = torch.empty(r, m, dtype=ctx.raw_dtype, device=dev)
+                norm_bwd(rv, vden, gv, gvt, grad_value, 0)
         return grad_key, grad_value, None, None
 
 
@@ -310,16 +316,20 @@ class _Temperatures(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, g_beta, g_scales):  # type: ignore[override]
+        # d log = g * value inside the clamp range (inclusive), else 0; both in one launch, each rounded
+        # once to its log's dtype
         log_beta, log_scales, beta, scales = ctx.saved_tensors
-
-        def through_clamp(log_v, value, g, bounds):
-            if g is None:
-                return None
-            inside = (log_v.detach().float() >= bounds[0]) & (log_v.detach().float() <= bounds[1])
-            return (g * value * inside.float().reshape(value.shape)).reshape(log_v.shape).to(log_v.dtype)
-
-        return (through_clamp(log_beta, beta, g_beta, BETA_LOG_RANGE),
-                through_clamp(log_scales, scales, g_scales, SCALE_LOG_RANGE))
+        if g_beta is None and g_scales is None:
+            return None, None
+        lb, ls = log_beta.detach().contiguous(), log_scales.detach().contiguous()
+        gb = None if g_beta is None else g_beta.float().contiguous()
+        gs = None if g_scales is None else g_scales.float().contiguous()
+        grad_lb = None if gb is None else torch.empty_like(lb)
+        grad_ls = None if gs is None else torch.empty_like(ls)
+        call("da_temperatures_bwd", lb.data_ptr(), dtype_code(lb.dtype), BETA_LOG_RANGE[0], BETA_LOG_RANGE[1],
+             beta.data_ptr(), ptr(gb), ptr(grad_lb), ls.data_ptr(), dtype_code(ls.dtype), ls.numel(),
+             SCALE_LOG_RANGE[0], SCALE_LOG_RANGE[1], scales.data_ptr(), ptr(gs), ptr(grad_ls), stream_ptr(lb.device))
+        return grad_lb, grad_ls
 
 
 def temperatures(log_beta: Tensor, log_scales: Tensor) -> tuple[Tensor, Tensor]:

@@ -84,11 +84,31 @@ DA_API int da_temperatures(const void* log_beta, int beta_dtype, float beta_lo, 
                            const void* log_scales, int scales_dtype, int maps, float scale_lo, float scale_hi,
                            float* beta_out, float* scales_out, void* stream);
 
+/* Backward of da_temperatures (autograd of exp(clamp(log, lo, hi))):
+ * grad_log = g * value where lo <= log <= hi (inclusive), else 0, formed in
+ * fp32 and stored once in the log's dtype, for beta and the `maps` scales in
+ * one launch.  Either half is skipped when its g pointer is null (not both).
+ * beta / scales are da_temperatures' outputs. */
+DA_API int da_temperatures_bwd(const void* log_beta, int beta_dtype, float beta_lo, float beta_hi, const float* beta,
+                               const float* g_beta, void* grad_log_beta, const void* log_scales, int scales_dtype,
+                               int maps, float scale_lo, float scale_hi, const float* scales, const float* g_scales,
+                               void* grad_log_scales, void* stream);
+
 /* Backward of da_dict_norm_fwd (autograd of F.normalize, modules.py:46-47).
  * grad: [R, M] fp32 and/or grad_t: [M, R] fp32 (summed when both are given).
  * grad_raw: [R, M] fp32, overwritten (accumulate = 0) or added to. */
 DA_API int da_dict_norm_bwd(const float* raw, const float* denom, const float* grad, const float* grad_t, int64_t R,
                      int64_t M, float eps, float* grad_raw, int accumulate, void* stream);
+
+/* da_dict_norm_bwd for banks held in any dtype: raw [R, M] in raw_dtype
+ * (DA_F32, or the half type of a module cast to it, read exactly), grad_raw
+ * [R, M] in grad_dtype, rounded once from the fp32 result (accumulate, which
+ * adds to it, needs DA_F32; DA_ERR_UNSUPPORTED otherwise).  The same fp32
+ * arithmetic as converting the bank to fp32, calling da_dict_norm_bwd and
+ * casting its result: bit-identical, without the two conversion launches. */
+DA_API int da_dict_norm_bwd_typed(const void* raw, int raw_dtype, const float* denom, const float* grad,
+                                  const float* grad_t, int64_t R, int64_t M, float eps, void* grad_raw, int grad_dtype,
+                                  int accumulate, void* stream);
 
 /* Largest column 2-norm of a [R, M] fp16/bf16 dictionary, into out[0]. */
 DA_API int da_col_norm_max(const void* dict, int64_t R, int64_t M, int dtype, float* out, void* stream);

@@ -105,3 +105,72 @@ def test_dict_norm_pair_matches_single_bank_calls(dtype: torch.dtype, r: int, m:
     torch.testing.assert_close(kden, raw_k.norm(dim=0).clamp_min(eps), atol=1e-6, rtol=1e-5)
     torch.testing.assert_close(vden, raw_v.norm(dim=0).clamp_min(eps), atol=1e-6, rtol=1e-5)
     torch.testing.assert_close(kmax[0], key.float().norm(dim=0).max(), atol=1e-6, rtol=1e-5)
+
+
+@pytest.mark.parametrize("raw_dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_dict_norm_bwd_typed_equals_convert_call_cast(raw_dtype: torch.dtype) -> None:
+    """da_dict_norm_bwd_typed on a bank in its own dtype, gradient stored in that dtype, against the
+    fp32 call on the bank converted to fp32 and its result cast: the same arithmetic, so bit for bit
+    equal; accumulate into fp32 likewise, and accumulate into a half type is refused."""
+    torch.manual_seed(11)
+    dev = torch.device("cuda")
+    r, m, eps = 128, 320, 1e-6
+    raw = torch.randn(r, m, device=dev).to(raw_dtype)
+    raw[:, 7] = 0  # a clamped column
+    raw32 = raw.float().contiguous()
+    denom = raw32.norm(dim=0).clamp_min(eps).contiguous()
+    grad = torch.randn(r, m, device=dev)
+    grad_t = torch.randn(m, r, device=dev)
+    want = torch.empty(r, m, device=dev)
+    _lib.call("da_dict_norm_bwd", raw32.data_ptr(), denom.data_ptr(), grad.data_ptr(), grad_t.data_ptr(), r, m, eps,
+              want.data_ptr(), 0, 0)
+    got = torch.empty(r, m, dtype=raw_dtype, device=dev)
+    _lib.call("da_dict_norm_bwd_typed", raw.data_ptr(), _lib.dtype_code(raw_dtype), denom.data_ptr(), grad.data_ptr(),
+              grad_t.data_ptr(), r, m, eps, got.data_ptr(), _lib.dtype_code(raw_dtype), 0, 0)
+    acc = torch.ones(r, m, device=dev)
+    _lib.call("da_dict_norm_bwd_typed", raw.data_ptr(), _lib.dtype_code(raw_dtype), denom.data_ptr(), grad.data_ptr(),
+              None, r, m, eps, acc.data_ptr(), _lib.DA_F32, 1, 0)
+    want_acc = torch.ones(r, m, device=dev)
+    _lib.call("da_dict_norm_bwd", raw32.data_ptr(), denom.data_ptr(), grad.data_ptr(), None, r, m, eps,
+              want_acc.data_ptr(), 1, 0)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want.to(raw_dtype))
+    assert torch.equal(acc, want_acc)
+    if raw_dtype != torch.float32:
+        with pytest.raises(NotImplementedError):
+            _lib.call("da_dict_norm_bwd_typed", raw.data_ptr(), _lib.dtype_code(raw_dtype), denom.data_ptr(),
+                      grad.data_ptr(), None, r, m, eps, got.data_ptr(), _lib.dtype_code(raw_dtype), 1, 0)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_temperatures_backward_equals_autograd(dtype: torch.dtype) -> None:
+    """da_temperatures_bwd against torch autograd of exp(clamp(log, lo, hi)) (modules.py:130-132,
+    ops.py:160-161) in the log's dtype, with logs inside, outside and exactly on both bounds: the
+    gradient passes where lo <= log <= hi, bit for bit."""
+    from double_attention_b200 import ops
+
+    dev = torch.device("cuda")
+    lo_b, hi_b = ops.BETA_LOG_RANGE
+    lo_s, hi_s = ops.SCALE_LOG_RANGE
+    # bounds as the kernel compares them: rounded to fp32 (then to the log's dtype, which may move them)
+    log_beta = torch.tensor([0.7], dtype=dtype, device=dev)
+    log_scales = torch.tensor([lo_s - 1.0, float(torch.tensor(lo_s, dtype=torch.float32)), 2.5, hi_s + 0.5,
+                               float(torch.tensor(hi_s, dtype=torch.float32)), 0.0], dtype=dtype, device=dev)
+    for lb_value in (0.7, lo_b - 0.3, hi_b + 0.1):
+        log_beta.fill_(lb_value)
+        lb = log_beta.clone().requires_grad_()
+        ls = log_scales.clone().requires_grad_()
+        beta, scales = ops._Temperatures.apply(lb, ls)
+        g_beta = torch.tensor([1.75], device=dev)
+        g_scales = torch.linspace(-2.0, 3.0, log_scales.numel(), device=dev)
+        torch.autograd.backward((beta, scales), (g_beta, g_scales))
+        lb_ref = log_beta.clone().requires_grad_()
+        ls_ref = log_scales.clone().requires_grad_()
+        beta_ref = lb_ref.float().clamp(lo_b, hi_b).exp()
+        scales_ref = ls_ref.float().clamp(lo_s, hi_s).exp()
+        torch.autograd.backward((beta_ref, scales_ref), (g_beta, g_scales))
+        torch.cuda.synchronize()
+        assert lb.grad.dtype == dtype and ls.grad.dtype == dtype
+        assert torch.equal(beta, beta_ref) and torch.equal(scales, scales_ref)
+        assert torch.equal(lb.grad, lb_ref.grad), (lb_value, lb.grad, lb_ref.grad)
+        assert torch.equal(ls.grad, ls_ref.grad), (ls.grad, ls_ref.grad)
