@@ -61,6 +61,8 @@ SIGNATURES: dict[str, list] = {
     "da_col_sum_workspace_elems": [_i64, _i64],  # returns int64 (set below)
     "da_col_sum": [_p, _i64, _i64, _i64, _i32, _p, _p, _i64, _p],
     "da_gemm_splitk": [_p, _i64, _i32, _p, _i64, _i32, _p, _i64, _i64, _i64, _i64, _i32, _i32, _p, _i64, _p, _p],
+    "da_gemm_splitk_store": [_p, _i64, _i32, _p, _i64, _i32, _p, _i64, _i32, _i64, _i64, _i64, _i32, _i32, _p, _i64,
+                             _p, _p],
     "da_gemm_splitk_grouped": [_p, _i64, _i64, _p, _i64, _p, _i64, _i64, _i64, _i64, _i32, _i32, _i32, _p, _i64, _p,
                                _p],
     "da_route_bwd": [_p, _i64, _i64, _i64, _i32, _i64, _i64, _i64, _i32, _p, _p, _p, _f32, _i32, _i32, _p, _p, _p,

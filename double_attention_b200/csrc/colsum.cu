@@ -5,8 +5,8 @@
 // An HBM-bound pass.  First kernel: CTAs tile the matrix by 256-column strips and row chunks; each of
 // a CTA's 8 warps walks every 8th row of the chunk with a lane owning 8 consecutive columns (16-byte
 // loads), and the 8 warp sums are added in warp order into one fp32 partial row per chunk.  Second
-// kernel: each column's partials are added in chunk order.  The partition depends only on the shape,
-// so the result is bit-reproducible.
+// kernel: each column's partials are added in a fixed order (below).  The partition depends only on the
+// shape, so the result is bit-reproducible.
 #include "common.cuh"
 #include "host_util.h"
 
@@ -54,15 +54,26 @@ __global__ void __launch_bounds__(kWarps * 32) colsum_partial_kernel(const T* __
   }
 }
 
-__global__ void __launch_bounds__(256) colsum_final_kernel(const float* __restrict__ partial, int chunks,
-                                                           int64_t cols, float* __restrict__ out) {
+// Second kernel: a CTA takes 32 columns; warp w adds chunks w, w + 8, ... of its lane's column in chunk
+// order and the 8 warp sums are added in warp order (coalesced 128-byte rows, 16 CTAs for 512 columns).
+__global__ void __launch_bounds__(kWarps * 32) colsum_final_kernel(const float* __restrict__ partial, int chunks,
+                                                                   int64_t cols, float* __restrict__ out) {
+  __shared__ float red[kWarps][32];
   grid_dependency_wait();
   grid_launch_dependents();
-  const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= cols) return;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int64_t c = (int64_t)blockIdx.x * 32 + lane;
   float t = 0.f;
-  for (int k = 0; k < chunks; ++k) t += partial[(int64_t)k * cols + c];
-  out[c] = t;
+  if (c < cols)
+    for (int k = w; k < chunks; k += kWarps) t += partial[(int64_t)k * cols + c];
+  red[w][lane] = t;
+  __syncthreads();
+  if (w == 0 && c < cols) {
+    float a = 0.f;
+#pragma unroll
+    for (int k = 0; k < kWarps; ++k) a += red[k][lane];
+    out[c] = a;
+  }
 }
 
 // Row chunks: enough CTAs for about two per SM, each chunk a multiple of the 8 warps' row stride.
@@ -110,6 +121,6 @@ extern "C" int da_col_sum(const void* d, int64_t rows, int64_t cols, int64_t ld,
                : launch_kernel(colsum_partial_kernel<__half>, grid, dim3(kWarps * 32), 0, st, false,
                                static_cast<const __half*>(d), rows, cols, ld, per, workspace);
   if (rc) return rc;
-  return launch_kernel(colsum_final_kernel, dim3((unsigned)((cols + 255) / 256)), dim3(256), 0, st, false,
+  return launch_kernel(colsum_final_kernel, dim3((unsigned)((cols + 31) / 32)), dim3(kWarps * 32), 0, st, false,
                        (const float*)workspace, chunks, cols, out);
 }

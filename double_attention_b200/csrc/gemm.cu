@@ -669,8 +669,11 @@ int launch_pk(const void* A, int64_t lda, const void* B, int64_t ldb, const void
 }
 
 // C[m, n] += sum over splits z, in index order, of partial[z, m, n] (four columns per thread).
-__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* partial, int splits, int M, int N, float* c,
-                                                            int64_t ldc) {
+// C (+)= the splits' partial sums, added in split order: fp32 C added to (accumulate) or overwritten, or
+// C in a 16-bit type TO, stored once.
+template <typename TO>
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* partial, int splits, int M, int N, void* c,
+                                                            int64_t ldc, int accumulate) {
   grid_dependency_wait();
   grid_launch_dependents();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // float4 index
@@ -682,10 +685,17 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* partial
     const float4 v = *reinterpret_cast<const float4*>(partial + ((size_t)z * M + row) * N + col);
     acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
   }
-  float4* dst = reinterpret_cast<float4*>(c + row * ldc + col);
-  float4 o = *dst;
-  o.x += acc.x; o.y += acc.y; o.z += acc.z; o.w += acc.w;
-  *dst = o;
+  if constexpr (std::is_same<TO, float>::value) {
+    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(c) + row * ldc + col);
+    if (accumulate) {
+      const float4 o = *dst;
+      acc.x += o.x; acc.y += o.y; acc.z += o.z; acc.w += o.w;
+    }
+    *dst = acc;
+  } else {
+    *reinterpret_cast<uint2*>(static_cast<TO*>(c) + row * ldc + col) =
+        make_uint2(pack2<TO>(acc.x, acc.y), pack2<TO>(acc.z, acc.w));
+  }
 }
 
 // Split count and K stages per split of a split-K product (the same plan for the workspace query and the
@@ -702,10 +712,18 @@ inline void splitk_plan(int64_t M, int64_t N, int64_t K, int splits, int* out_sp
   *out_kps = kps;
 }
 
-inline int splitk_reduce(const Params& p, int splits, cudaStream_t st) {
+// out_dtype: DA_F32 (p.accumulate: added to C, else overwritten), or the 16-bit type C is stored in
+inline int splitk_reduce(const Params& p, int splits, cudaStream_t st, int out_dtype = DA_F32) {
   const int64_t n4 = (int64_t)p.M * (p.N / 4);
-  return launch_kernel(splitk_reduce_kernel, dim3((unsigned)((n4 + 255) / 256)), dim3(256), 0, st, false,
-                       (const float*)p.partial, splits, p.M, p.N, reinterpret_cast<float*>(p.c), p.ldc);
+  const dim3 grid((unsigned)((n4 + 255) / 256));
+  if (out_dtype == DA_BF16)
+    return launch_kernel(splitk_reduce_kernel<__nv_bfloat16>, grid, dim3(256), 0, st, false, (const float*)p.partial,
+                         splits, p.M, p.N, p.c, p.ldc, 0);
+  if (out_dtype == DA_F16)
+    return launch_kernel(splitk_reduce_kernel<__half>, grid, dim3(256), 0, st, false, (const float*)p.partial, splits,
+                         p.M, p.N, p.c, p.ldc, 0);
+  return launch_kernel(splitk_reduce_kernel<float>, grid, dim3(256), 0, st, false, (const float*)p.partial, splits,
+                       p.M, p.N, p.c, p.ldc, p.accumulate);
 }
 
 template <typename T, int kN, bool kAmn, bool kBmn>
@@ -855,20 +873,25 @@ extern "C" int64_t da_gemm_splitk_workspace_elems(int64_t M, int64_t N, int64_t 
   return (int64_t)s * M * N;
 }
 
-extern "C" int da_gemm_splitk(const void* A, int64_t lda, int a_mn_major, const void* B, int64_t ldb, int b_mn_major,
-                              float* C, int64_t ldc, int64_t M, int64_t N, int64_t K, int dtype, int splits,
-                              float* workspace, int64_t workspace_elems, int* status, void* stream) {
+namespace {
+
+// C (fp32, += when accumulate, else =; or c_dtype = the operand dtype, stored once) = A.B^T over a K split
+// across CTAs; with a workspace the splits' partials are added in split order.
+int splitk_entry(const void* A, int64_t lda, int a_mn_major, const void* B, int64_t ldb, int b_mn_major, void* C,
+                 int64_t ldc, int c_dtype, int accumulate, int64_t M, int64_t N, int64_t K, int dtype, int splits,
+                 float* workspace, int64_t workspace_elems, int* status, void* stream) {
   using namespace da;
   if (!A || !B || !C || !status) return DA_ERR_NULL;
   if (int rc = bind_device(A)) return rc;
   if (dtype != DA_BF16 && dtype != DA_F16) return DA_ERR_DTYPE;
+  if (c_dtype != DA_F32 && c_dtype != dtype) return DA_ERR_DTYPE;
   if (M <= 0 || N <= 0 || K <= 0 || N % 128 || M % 128) return DA_ERR_SHAPE;
   if ((lda % 8) || (ldb % 8)) return DA_ERR_ALIGN;
   if ((reinterpret_cast<uintptr_t>(C) & 15) || (ldc % 4)) return DA_ERR_ALIGN;
   const int n_tile = 128;
   int kps = 0;
   gemm::splitk_plan(M, N, K, splits, &splits, &kps);
-  gemm::Params p{(int)M, (int)N, (int)K, C, ldc, 1, 1, status, kps};
+  gemm::Params p{(int)M, (int)N, (int)K, C, ldc, c_dtype == DA_F32 ? 1 : 0, accumulate, status, kps};
   if (workspace) {
     if (workspace_elems < (int64_t)splits * M * N) return DA_ERR_WORKSPACE;
     if (reinterpret_cast<uintptr_t>(workspace) & 15) return DA_ERR_ALIGN;
@@ -881,14 +904,32 @@ extern "C" int da_gemm_splitk(const void* A, int64_t lda, int a_mn_major, const 
                        ? gemm::launch_pk<__nv_bfloat16, true, true>(A, lda, B, ldb, nullptr, 0, nullptr, 0, 0, p, st)
                        : gemm::launch_pk<__half, true, true>(A, lda, B, ldb, nullptr, 0, nullptr, 0, 0, p, st);
     if (rc) return rc;
-    return gemm::splitk_reduce(p, splits, st);
+    return gemm::splitk_reduce(p, splits, st, c_dtype);
   }
   int rc = dtype == DA_BF16
                ? gemm::dispatch<__nv_bfloat16>(a_mn_major, b_mn_major, n_tile, A, lda, B, ldb, p, splits, st)
                : gemm::dispatch<__half>(a_mn_major, b_mn_major, n_tile, A, lda, B, ldb, p, splits, st);
-  // one split accumulates straight into C (the kernel's non-split epilogue)
+  // one split writes C itself (the kernel's non-split epilogue)
   if (rc || !p.partial || splits == 1) return rc;
-  return gemm::splitk_reduce(p, splits, st);
+  return gemm::splitk_reduce(p, splits, st, c_dtype);
+}
+
+}  // namespace
+
+extern "C" int da_gemm_splitk(const void* A, int64_t lda, int a_mn_major, const void* B, int64_t ldb, int b_mn_major,
+                              float* C, int64_t ldc, int64_t M, int64_t N, int64_t K, int dtype, int splits,
+                              float* workspace, int64_t workspace_elems, int* status, void* stream) {
+  return splitk_entry(A, lda, a_mn_major, B, ldb, b_mn_major, C, ldc, DA_F32, 1, M, N, K, dtype, splits, workspace,
+                      workspace_elems, status, stream);
+}
+
+extern "C" int da_gemm_splitk_store(const void* A, int64_t lda, int a_mn_major, const void* B, int64_t ldb,
+                                    int b_mn_major, void* C, int64_t ldc, int c_dtype, int64_t M, int64_t N, int64_t K,
+                                    int dtype, int splits, float* workspace, int64_t workspace_elems, int* status,
+                                    void* stream) {
+  if (!workspace) return DA_ERR_WORKSPACE;
+  return splitk_entry(A, lda, a_mn_major, B, ldb, b_mn_major, C, ldc, c_dtype, 0, M, N, K, dtype, splits, workspace,
+                      workspace_elems, status, stream);
 }
 
 extern "C" int da_gemm_segments(const void* A, int64_t lda, int64_t M, int64_t K, int dtype, int nseg,

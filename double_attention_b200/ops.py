@@ -447,6 +447,20 @@ def gemm_splitk(a: Tensor, lda: int, a_mn: bool, b: Tensor, ldb: int, b_mn: bool
     return out
 
 
+def weight_grad(a: Tensor, b: Tensor, m: int, n: int, k: int, dtype: torch.dtype) -> Tensor:
+    """A new [m, n] tensor = sum over the k rows of a [k, m]^T . b [k, n] (a weight gradient dY^T . X),
+    the rows split over CTAs and the partial sums added in a fixed order, stored once in ``dtype`` (fp32,
+    or the operands' dtype; another dtype goes through fp32 and a cast)."""
+    store = dtype if dtype in (torch.float32, a.dtype) else torch.float32
+    out = torch.empty(m, n, dtype=store, device=a.device)
+    elems = int(_lib.lib().da_gemm_splitk_workspace_elems(m, n, k, 0))
+    part = torch.empty(max(elems, 4), dtype=torch.float32, device=a.device)
+    call("da_gemm_splitk_store", a.data_ptr(), a.stride(0), 1, b.data_ptr(), b.stride(0), 1, out.data_ptr(),
+         out.stride(0), dtype_code(store), m, n, k, dtype_code(a.dtype), 0, part.data_ptr(), part.numel(),
+         workspace(a.device).status.data_ptr(), stream_ptr(a.device))
+    return out if store == dtype else out.to(dtype)
+
+
 def key_dictionary_grad(q: Tensor, col_stride: int, dl: Tensor, out: Tensor) -> Tensor:
     """out [R, M] fp32 += sum_g q_g^T dl[g]: q_g the g-th column block (width R, stride col_stride) of
     the routed matrix q [rows, cols], dl [groups, rows, M] -- one split-K launch over every group
@@ -1161,9 +1175,7 @@ class _Linear(torch.autograd.Function):
             dx = torch.empty(m, k, dtype=w.dtype, device=x2d.device)
             gemm_ex(dout, w, True, dx)  # dX = dY . W
         if need[1]:
-            dw = torch.zeros(n, k, dtype=torch.float32, device=x2d.device)
-            gemm_splitk(dout, dout.stride(0), True, x2d, x2d.stride(0), True, n, k, m, dw)  # dW = dY^T . X
-            dw = dw.to(ctx.param_dtypes[0])
+            dw = weight_grad(dout, x2d, n, k, m, ctx.param_dtypes[0])  # dW = dY^T . X
         if need[2]:
             db = _bias_grad(dout).to(ctx.param_dtypes[1])
         return dx, dw, db, None
@@ -1236,17 +1248,13 @@ class _FeedForward(torch.autograd.Function):
         pd = ctx.param_dtypes
         dx = dw1 = db1 = dw2 = db2 = None
         if need[3]:
-            dw2 = torch.zeros(n, hidden, dtype=torch.float32, device=x2d.device)
-            gemm_splitk(dout, dout.stride(0), True, h, h.stride(0), True, n, hidden, m, dw2)  # dW2 = dOut^T . h
-            dw2 = dw2.to(pd[2])
+            dw2 = weight_grad(dout, h, n, hidden, m, pd[2])  # dW2 = dOut^T . h
         if need[4]:
             db2 = _bias_grad(dout).to(pd[3])
         dz = torch.empty(m, hidden, dtype=dt, device=x2d.device)
         gemm_ex(dout, w2c, True, dz, act=2, aux=z)  # dZ = (dOut . W2) * GELU'(z)
         if need[1]:
-            dw1 = torch.zeros(hidden, k, dtype=torch.float32, device=x2d.device)
-            gemm_splitk(dz, dz.stride(0), True, x2d, x2d.stride(0), True, hidden, k, m, dw1)  # dW1 = dZ^T . x
-            dw1 = dw1.to(pd[0])
+            dw1 = weight_grad(dz, x2d, hidden, k, m, pd[0])  # dW1 = dZ^T . x
         if need[2]:
             db1 = _bias_grad(dz).to(pd[1])
         if need[0]:
@@ -1292,9 +1300,7 @@ class _Projection(torch.autograd.Function):
             dx = torch.empty(m, k, dtype=x2d.dtype, device=x2d.device)
             gemm(dout, False, weight, True, m, k, n, dx)          # dX = dC . W
         if ctx.needs_input_grad[1]:
-            dw = torch.zeros(n, k, dtype=torch.float32, device=x2d.device)
-            gemm_splitk(dout, dout.stride(0), True, x2d, x2d.stride(0), True, n, k, m, dw)  # dW = dC^T . X, rows split
-            dw = dw.to(weight.dtype)
+            dw = weight_grad(dout, x2d, n, k, m, weight.dtype)  # dW = dC^T . X, rows split
         return dx, dw
 
 
@@ -1354,14 +1360,15 @@ class _QKVProjection(torch.autograd.Function):
         if dproj is not None and (need[1] or need[2]):
             # dW = dC^T . X (fp32): a [2HR, K] output of a few tiles over all B*T rows, so the row
             # dimension is split over CTAs (partial sums added in a fixed order)
-            dw = torch.zeros(2 * hr, k, dtype=torch.float32, device=x2d.device)
-            gemm_splitk(dproj, dproj.stride(0), True, x2d, x2d.stride(0), True, 2 * hr, k, m, dw)
-            dwq, dwk = dw[:hr].to(wq.dtype), dw[hr:].to(wk.dtype)
+            if wq.dtype == wk.dtype:  # one [2HR, K] gradient, its two row blocks handed out as views
+                dw = weight_grad(dproj, x2d, 2 * hr, k, m, wq.dtype)
+                dwq, dwk = dw[:hr], dw[hr:]
+            else:
+                dw = weight_grad(dproj, x2d, 2 * hr, k, m, torch.float32)
+                dwq, dwk = dw[:hr].to(wq.dtype), dw[hr:].to(wk.dtype)
         if dv is not None:
             if need[3]:  # dWv = dV^T . X, rows split over CTAs as above
-                dwv32 = torch.zeros(wv.shape[0], k, dtype=torch.float32, device=x2d.device)
-                gemm_splitk(dv, dv.stride(0), True, x2d, x2d.stride(0), True, wv.shape[0], k, m, dwv32)
-                dwv = dwv32.to(wv.dtype)
+                dwv = weight_grad(dv, x2d, wv.shape[0], k, m, wv.dtype)
             if ctx.has_bias and need[4]:
                 dbv = _bias_grad(dv).to(wv.dtype)
         return dx, dwq, dwk, dwv, dbv

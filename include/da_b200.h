@@ -426,6 +426,16 @@ DA_API int da_gemm_splitk(const void* A, int64_t lda, int a_mn_major, const void
                           float* C, int64_t ldc, int64_t M, int64_t N, int64_t K, int dtype, int splits,
                           float* workspace, int64_t workspace_elems, int* status, void* stream);
 
+/* da_gemm_splitk storing C once instead of adding to it: C = A.B^T in fp32
+ * (c_dtype DA_F32) or in the operand dtype (c_dtype = dtype; DA_ERR_DTYPE
+ * otherwise), the splits' partial sums (workspace required, else
+ * DA_ERR_WORKSPACE) added in split order and rounded once.  For weight
+ * gradients stored in the parameters' dtype without a zero-filled fp32 buffer
+ * and a cast. */
+DA_API int da_gemm_splitk_store(const void* A, int64_t lda, int a_mn_major, const void* B, int64_t ldb, int b_mn_major,
+                                void* C, int64_t ldc, int c_dtype, int64_t M, int64_t N, int64_t K, int dtype,
+                                int splits, float* workspace, int64_t workspace_elems, int* status, void* stream);
+
 /* The same sum over several groups at once: C [M, N] fp32 += sum over g < groups and k < K_group of
  * A(m, g, k) B(n, g, k) with A MN-major, its group g starting a_group_cols columns to the right
  * (A(m, g, k) = A[k * lda + g * a_group_cols + m]), and B MN-major with the groups stacked along K

@@ -93,3 +93,24 @@ def test_splitk_rejects_a_short_workspace() -> None:
                                    _lib.DA_BF16, 0, part.data_ptr(), part.numel(),
                                    ops.workspace(dev).status.data_ptr(), ops.stream_ptr(dev))
     assert rc == _lib.DA_ERR_WORKSPACE
+
+
+@pytest.mark.parametrize(("m", "n", "k"), [(1024, 512, 32768), (512, 512, 4096), (256, 256, 64)])
+@pytest.mark.parametrize("store", [torch.bfloat16, torch.float32])
+def test_splitk_store_equals_accumulate_into_zeros(m, n, k, store) -> None:
+    """da_gemm_splitk_store (C = A^T B stored once, in fp32 or the operand dtype) against da_gemm_splitk
+    into a zero-filled fp32 C then cast: the same fixed-order split sums, so bit for bit equal -- at the
+    weight-gradient shapes of the config-3 projections (B16 and B2 rows) and at a one-split size."""
+    torch.manual_seed(m + n + k)
+    dev = torch.device("cuda")
+    a = torch.randn(k, m, device=dev).to(torch.bfloat16)
+    b = torch.randn(k, n, device=dev).to(torch.bfloat16)
+    want = torch.zeros(m, n, device=dev)
+    ops.gemm_splitk(a, m, True, b, n, True, m, n, k, want)
+    got = ops.weight_grad(a, b, m, n, k, store)
+    torch.cuda.synchronize()
+    assert got.dtype == store
+    assert torch.equal(got, want.to(store))
+    assert ops.device_status(dev) == 0
+    ref = a.float().t() @ b.float()
+    assert (want - ref).abs().max().item() <= 1e-3 * ref.abs().max().item()
