@@ -1309,10 +1309,11 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_mixed_kernel(const __grid_con
   if (warp == 1) tmem_dealloc<2>(tmem, L.tmem_cols);
 }
 
-// d alpha_s (kind 0) and d gamma_s (kind 1) += the sum of the dQ kernel's n per-(CTA, warp) partials of
-// map s: every thread adds a strided subset in index order, then a fixed-shape tree over the block.
+// d alpha_s (kind 0) and d gamma_s (kind 1) += (store: =) the sum of the dQ kernel's n per-(CTA, warp)
+// partials of map s: every thread adds a strided subset in index order, then a fixed-shape tree over the
+// block.
 __global__ void __launch_bounds__(256) scalar_reduce_kernel(const float* part, int n, int maps, float* dweight,
-                                                            float* dscale) {
+                                                            float* dscale, int store) {
   __shared__ float red[256];
   grid_dependency_wait();
   grid_launch_dependents();
@@ -1328,7 +1329,7 @@ __global__ void __launch_bounds__(256) scalar_reduce_kernel(const float* part, i
     if (threadIdx.x < w) red[threadIdx.x] += red[threadIdx.x + w];
     __syncthreads();
   }
-  if (threadIdx.x == 0) out[m] += red[0];
+  if (threadIdx.x == 0) out[m] = store ? red[0] : out[m] + red[0];
 }
 
 // Destination rows of a split launch's compact partial rows: c = ((b * maps + s) * group + gi) * T + t
@@ -1563,7 +1564,7 @@ int attn_bwd_entry(const void* q, int64_t q_rows, int64_t q_base, int64_t q_sb, 
     float* dw = pp.delta_given ? nullptr : pp.dweight;
     if (r || !pp.scalar_part || (!dw && !pp.dscale)) return r;
     return launch_kernel(scalar_reduce_kernel, dim3((unsigned)maps, 2, 1), dim3(256, 1, 1), 0, st, false,
-                         (const float*)pp.scalar_part, (int)(2 * cpairs * 4), maps, dw, pp.dscale);
+                         (const float*)pp.scalar_part, (int)(2 * cpairs * 4), maps, dw, pp.dscale, pp.overwrite);
   };
   auto run_dkv = [&](const Params& pp, bool dkk) -> int {
     const Layout L = make_layout(dkk ? 1 : 2, maps, group, R, D);

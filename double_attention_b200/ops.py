@@ -104,16 +104,28 @@ class _Workspace:
 
 _ws_lock = threading.Lock()
 _workspaces: dict[tuple[int, int], _Workspace] = {}
+# Zero-filled workspaces made outside any graph capture, for streams first seen while one is captured:
+# a workspace made during the capture would put its zero fills into the graph, replayed every step.
+_spare_workspaces: dict[int, list[_Workspace]] = {}
+_SPARES = 4
 
 
 def workspace(device: torch.device) -> _Workspace:
-    key = (device.index if device.index is not None else torch.cuda.current_device(), stream_ptr(device))
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    key = (idx, stream_ptr(device))
     ws = _workspaces.get(key)
     if ws is None:
         with _ws_lock:
             ws = _workspaces.get(key)
             if ws is None:
-                ws = _Workspace(device)
+                spares = _spare_workspaces.setdefault(idx, [])
+                capturing = torch.cuda.is_current_stream_capturing()
+                if capturing and spares:
+                    ws = spares.pop()
+                else:
+                    ws = _Workspace(device)
+                    while not capturing and len(spares) < _SPARES:
+                        spares.append(_Workspace(device))
                 _workspaces[key] = ws
     return ws
 
@@ -954,10 +966,11 @@ class _MixedAttention(torch.autograd.Function):
         alloc = torch.empty if overwrite else torch.zeros
         droute = alloc(flat.shape, dtype=gdt, device=flat.device) if need[0] else None
         dv = alloc(batch * length, d, dtype=gdt, device=flat.device) if need[1] else None
-        dscale = torch.zeros(maps, dtype=torch.float32, device=flat.device)
+        # (with overwrite the library also stores d gamma and d alpha once instead of adding to them)
+        dscale = alloc(maps, dtype=torch.float32, device=flat.device)
         sc = scales.detach().float().contiguous()
         wt = weights.detach().float().contiguous() if has_weights and maps > 1 else None
-        dweight = torch.zeros(maps, dtype=torch.float32, device=flat.device) if wt is not None else None
+        dweight = alloc(maps, dtype=torch.float32, device=flat.device) if wt is not None else None
         if maps == 1:  # delta from the saved output
             delta, given = _attention_delta(dy16, y).view(batch, 1, length), True
         else:  # computed exactly by the kernel's first sweep (the per-map outputs are never stored)

@@ -357,8 +357,9 @@ DA_API int da_attn_bwd_mixed(const void* q, int64_t q_rows, int64_t q_base, int6
 /* da_attn_bwd_mixed writing dq, dk and dv once each instead of adding to fp32
  * buffers: every gradient row the op produces is stored in the input dtype
  * (dq, dk: [rows, R]; dv: [B*T, D]), rows it does not produce are left as they
- * are.  Needs maps whose branch ranges do not overlap (each row then has one
- * writer; DA_ERR_UNSUPPORTED otherwise).  Same reference interface as
+ * are; dscale and dweight are stored (=) rather than added to.  Needs maps
+ * whose branch ranges do not overlap (each row then has one writer;
+ * DA_ERR_UNSUPPORTED otherwise).  Same reference interface as
  * da_attn_bwd_mixed, without the zero-filled fp32 buffers and the casts the
  * module path otherwise runs around it. */
 DA_API int da_attn_bwd_mixed_ow(const void* q, int64_t q_rows, int64_t q_base, int64_t q_sb, int64_t q_sbr,

@@ -195,8 +195,10 @@ def test_overwrite_gradients_equal_the_accumulated_ones(batch: int) -> None:
         gdt, alloc = (dtype, torch.empty) if overwrite else (torch.float32, torch.zeros)
         droute = alloc(flat.shape, dtype=gdt, device=dev)
         dv = alloc(batch * length, d, dtype=gdt, device=dev)
-        dscale = torch.zeros(maps, dtype=torch.float32, device=dev)
-        dweight = torch.zeros(maps, dtype=torch.float32, device=dev)
+        # the overwrite entry stores d gamma and d alpha (=): NaN-filled outputs must come back finite
+        fill = float("nan") if overwrite else 0.0
+        dscale = torch.full((maps,), fill, dtype=torch.float32, device=dev)
+        dweight = torch.full((maps,), fill, dtype=torch.float32, device=dev)
         delta = torch.empty(batch, maps, length, dtype=torch.float32, device=dev)
         ops._attention_backward(qmap, kmap, value, dy, batch, length, r, maps, group, branch0, True, scales, mix,
                                 lse, delta, False, droute, droute, dv, dscale, dweight, overwrite=overwrite)
