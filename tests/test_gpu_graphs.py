@@ -68,3 +68,25 @@ def test_graphed_step_rejects_cpu_module() -> None:
     module = SharedDictionaryAttention(experiment_config("a1"))
     with pytest.raises(RuntimeError, match="CUDA device"):
         GraphedModuleStep(module, (1, 4, 512), torch.float32)
+
+
+def test_capture_takes_a_prezeroed_workspace() -> None:
+    """A stream first seen while a graph is being captured gets one of the zero-filled workspaces made
+    beforehand outside any capture, so the graph records no workspace fills (which every replay would
+    otherwise repeat)."""
+    dev = torch.device("cuda")
+    idx = torch.cuda.current_device()
+    ops.workspace(dev)  # the current stream's workspace; the device's spares are made with it
+    spares = list(ops._spare_workspaces[idx])
+    assert spares
+    graph = torch.cuda.CUDAGraph()
+    capture_stream = torch.cuda.Stream(dev)  # never used before, so it has no workspace yet
+    scratch = torch.zeros(4, device=dev)
+    with torch.cuda.graph(graph, stream=capture_stream):
+        ws = ops.workspace(dev)
+        scratch.add_(1.0)
+    assert any(ws is s for s in spares)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert int(ws.route_work.abs().sum()) == 0 and int(ws.status.abs().sum()) == 0
+    assert torch.equal(scratch, torch.ones(4, device=dev))
